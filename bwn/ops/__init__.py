@@ -1,0 +1,140 @@
+"""Public op API.  CUDA tensors run the hand-written sm_100a kernels registered
+as ``torch.ops.bwn.*``; CPU tensors run the fp32 PyTorch references in
+:mod:`bwn.ops.reference` (the CPU test tier and numerics oracle).
+
+Weight layouts the kernels expect (produced by :mod:`bwn.io.loader`):
+
+* linear weights are ``[N_out, K]`` row-major bf16 (``nn.Linear`` layout);
+* SwiGLU gate/up weights are interleaved in blocks of 16 rows
+  (``[g0..g15, u0..u15, g16..g31, u16..u31, ...]``) so the GEMM epilogue finds
+  each gate next to its up partner (:func:`interleave_gate_up`).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import reference as ref
+from ._ext import available, check_status, ops, require, status, status_clear  # noqa: F401
+
+EPI_BF16, EPI_RESID, EPI_SWIGLU, EPI_F32 = 0, 1, 2, 3
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 16) -> torch.Tensor:
+    """Pack ``gate [I, K]`` and ``up [I, K]`` into the block-16 interleaved ``[2I, K]``."""
+    I, K = gate.shape
+    assert I % block == 0, f"intermediate {I} must be a multiple of {block}"
+    g = gate.reshape(I // block, block, K)
+    u = up.reshape(I // block, block, K)
+    return torch.stack([g, u], dim=1).reshape(2 * I, K)
+
+
+def deinterleave_gate_up(w: torch.Tensor, block: int = 16):
+    n2, K = w.shape
+    x = w.reshape(n2 // (2 * block), 2, block, K)
+    return x[:, 0].reshape(n2 // 2, K), x[:, 1].reshape(n2 // 2, K)
+
+
+# --------------------------------------------------------------------------
+# GEMMs
+# --------------------------------------------------------------------------
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T`` (bf16 in/out, fp32 accumulate) on the tcgen05 GEMM."""
+    if x.is_cuda:
+        return ops().linear(x, w)
+    return ref.linear(x, w)
+
+
+def linear_f32(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    if x.is_cuda:
+        return ops().linear_f32(x, w)
+    return x.float() @ w.float().t()
+
+
+def linear_swiglu(x: torch.Tensor, w_il: torch.Tensor) -> torch.Tensor:
+    """``silu(x @ Wg.T) * (x @ Wu.T)`` with the block-16 interleaved weight."""
+    if x.is_cuda:
+        return ops().linear_swiglu(x, w_il)
+    y = x.float() @ w_il.float().t()
+    n2 = y.shape[-1]
+    y = y.reshape(*y.shape[:-1], n2 // 32, 2, 16)
+    return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*y.shape[:-3], n2 // 2).to(x.dtype)
+
+
+def linear_residual(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
+    """``resid + x @ w.T`` with the add fused into the GEMM epilogue."""
+    if x.is_cuda:
+        return ops().linear_residual(x, w, resid)
+    return (x.float() @ w.float().t() + resid.float()).to(x.dtype)
+
+
+# --------------------------------------------------------------------------
+# norms / embedding / greedy
+# --------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, one_plus: bool = True) -> torch.Tensor:
+    if x.is_cuda:
+        return ops().rms_norm(x, w, eps, one_plus)
+    return ref.rms_norm(x, w, eps, one_plus)
+
+
+def add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """``residual += x`` (in place) and return ``rmsnorm(residual) * (1+w)``."""
+    if x.is_cuda:
+        return ops().add_rms_norm(x, residual, w, eps)
+    r, n = ref.add_rms_norm(x, residual, w, eps)
+    residual.copy_(r)
+    return n
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, offset: int = 0) -> torch.Tensor:
+    """Rows ``table[ids - offset]``; ids outside the local shard give zero rows."""
+    if table.is_cuda:
+        return ops().embedding(ids.int(), table, offset)
+    local = ids.long() - offset
+    ok = (local >= 0) & (local < table.shape[0])
+    rows = table[local.clamp(0, table.shape[0] - 1)]
+    return rows * ok[..., None].to(rows.dtype)
+
+
+def argmax_packed(logits: torch.Tensor, id_offset: int = 0) -> torch.Tensor:
+    """Per row int64 key ``(orderable(max) << 32) | (2^32-1 - id)``: an int64 max
+    over shards selects the largest logit and, on ties, the lowest global id."""
+    if logits.is_cuda:
+        return ops().argmax_packed(logits, id_offset)
+    lf = logits.float()
+    m, _ = lf.max(-1)
+    ids = torch.arange(lf.shape[-1])
+    first = torch.where(lf == m[:, None], ids, torch.full_like(ids, lf.shape[-1])).min(-1).values + id_offset
+    u = m.view(torch.int32).long() & 0xFFFFFFFF
+    neg = (u & 0x80000000) != 0
+    ordv = torch.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
+    return (ordv << 32) | (0xFFFFFFFF - first)
+
+
+def unpack_argmax(packed: torch.Tensor) -> torch.Tensor:
+    if packed.is_cuda:
+        return ops().unpack_argmax(packed)
+    return (0xFFFFFFFF - (packed & 0xFFFFFFFF)).int()
+
+
+# --------------------------------------------------------------------------
+# DeltaNet / GQA decode
+# --------------------------------------------------------------------------
+def deltanet_decode(qkv, z, a, b, conv_ring, state, positions, conv_w, A_log, dt_bias, norm_w,
+                    k_heads: int, eps: float = 1e-6) -> torch.Tensor:
+    """One fused gated-DeltaNet decode step; updates ``conv_ring`` and ``state``
+    in place and returns the RMSNormGated output ``[B, VH*128]``."""
+    if qkv.is_cuda:
+        return ops().deltanet_decode(qkv, z, a, b, conv_ring, state, positions, conv_w, A_log, dt_bias, norm_w,
+                                     k_heads, eps)
+    VH = state.shape[1]
+    return ref.deltanet_decode(qkv, a, b, z, conv_ring, state, positions, conv_w, A_log, dt_bias, norm_w,
+                               k_heads, state.shape[2], state.shape[3], eps)[:, : VH * state.shape[3]]
+
+
+def gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions,
+               eps: float = 1e-6, splits: int = 0) -> torch.Tensor:
+    """Fused gated GQA decode step (appends K/V at ``positions``)."""
+    if qg.is_cuda:
+        return ops().gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions,
+                                eps, splits)
+    return ref.gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions, eps)

@@ -1,0 +1,466 @@
+// Persistent tcgen05 GEMM for sm_100a:  D[M, N] = A[M, K] * B[N, K]^T
+//
+// Both operands are K-major bf16 (row-major activations and nn.Linear weights),
+// fed by TMA with the 128-byte swizzle into a multi-stage shared-memory ring.
+// Warp roles (192 threads):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      MMA issuer (one elected lane), TMEM allocator
+//   warps 2..5  epilogue: tcgen05.ld from TMEM lanes 32*(warp%4).., fused
+//               post-processing, global stores
+// Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps
+// the main loop of tile i+1.  Split-K (for decode shapes where M/128 tiles
+// cannot fill 148 SMs) writes fp32 partials to a workspace; the last CTA to
+// finish a tile (atomic ticket) sums them and runs the epilogue, then re-arms
+// the ticket so the same launch can be replayed from a CUDA graph.
+//
+// For decode ("swap-AB") the host passes the weight matrix as A (so the 128-row
+// MMA M dimension spans output features) and the few token rows as B, and asks
+// for a transposed store.  Epilogues: bf16 store, bf16 store + residual,
+// SwiGLU over gate/up rows interleaved in blocks of 16, fp32 store.
+#include "common/host.h"
+#include "common/sm100.cuh"
+
+namespace bwn {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_m, tiles_n, splits, kb_per_split, num_kb;
+  void* out;
+  long ldo;
+  const __nv_bfloat16* resid;  // optional, same indexing as out (bf16 modes)
+  long ldr;
+  float* workspace;            // splits>1: [tiles * splits * BM * BN] fp32
+  int* tickets;                // splits>1: [tiles]
+  int* status;
+};
+
+template <int BN, int EPI, bool TRANS>
+__device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, const float (&v)[32], int ncols, int m, int n0) {
+  // m: global row (A row), n0: global column of v[0]; ncols valid in v (16 or 32)
+  if (EPI == kEpiF32) {
+    float* out = reinterpret_cast<float*>(a.out);
+    if (!TRANS) {
+      if (m >= a.M) return;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols && n0 + j < a.N) out[(long)m * a.ldo + n0 + j] = v[j];
+    } else {
+      if (m >= a.M) return;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols && n0 + j < a.N) out[(long)(n0 + j) * a.ldo + m] = v[j];
+    }
+    return;
+  }
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  if (EPI == kEpiSwiGLU) {
+    if (!TRANS) {
+      // columns [n0, n0+32) = 16 gate then 16 up features of output block n0/32
+      if (m >= a.M) return;
+      const int f0 = (n0 >> 5) * 16;
+      if (n0 + 32 > a.N) return;
+      alignas(16) __nv_bfloat16 o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = __float2bfloat16(silu_f(v[j]) * v[j + 16]);
+      uint4* dst = reinterpret_cast<uint4*>(out + (long)m * a.ldo + f0);
+      dst[0] = reinterpret_cast<uint4*>(o)[0];
+      dst[1] = reinterpret_cast<uint4*>(o)[1];
+    } else {
+      // rows: lanes 0-15 gate, 16-31 up (m block of 32 aligned)
+      const int lane = threadIdx.x & 31;
+      const int f = (m >> 5) * 16 + (lane & 15);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float up = __shfl_down_sync(0xffffffffu, v[j], 16);
+        if (lane < 16 && j < ncols && n0 + j < a.N && m < a.M)
+          out[(long)(n0 + j) * a.ldo + f] = __float2bfloat16(silu_f(v[j]) * up);
+      }
+    }
+    return;
+  }
+  // bf16 store (optionally + residual)
+  if (!TRANS) {
+    if (m >= a.M) return;
+    const bool full = (n0 + 32 <= a.N) && ncols == 32 && ((a.ldo & 7) == 0);
+    if (full) {
+      alignas(16) __nv_bfloat16 o[32];
+      if (EPI == kEpiResid) {
+        const uint4* rs = reinterpret_cast<const uint4*>(a.resid + (long)m * a.ldr + n0);
+        alignas(16) __nv_bfloat16 r[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(r)[q] = rs[q];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = __float2bfloat16(v[j] + __bfloat162float(r[j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = __float2bfloat16(v[j]);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + (long)m * a.ldo + n0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<uint4*>(o)[q];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < ncols && n0 + j < a.N) {
+          float x = v[j];
+          if (EPI == kEpiResid) x += __bfloat162float(a.resid[(long)m * a.ldr + n0 + j]);
+          out[(long)m * a.ldo + n0 + j] = __float2bfloat16(x);
+        }
+      }
+    }
+  } else {
+    if (m >= a.M) return;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < ncols && n0 + j < a.N) {
+        float x = v[j];
+        if (EPI == kEpiResid) x += __bfloat162float(a.resid[(long)(n0 + j) * a.ldr + m]);
+        out[(long)(n0 + j) * a.ldo + m] = __float2bfloat16(x);
+      }
+    }
+  }
+}
+
+template <int BN, int EPI, bool TRANS>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmArgs args) {
+  using C = GemmCfg<BN>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * C::kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* ticket_bcast = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int units = tiles * args.splits;
+  const uint32_t idesc = idesc_bf16_f32(kBM, BN);
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (elect_one()) {
+      const uint64_t polA = l2_policy_evict_first();
+      const uint64_t polB = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_mask = 0, issued_ph = 0;  // per stage: issued at least once / parity of last issue
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const int tile = u / args.splits, sp = u % args.splits;
+        const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+        const int kb0 = sp * args.kb_per_split;
+        const int kb1 = min(args.num_kb, kb0 + args.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1)) {
+            set_status(args.status, kStatusMbarTimeout);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
+          tma_load_2d_hint(&tmA, &full_bar[s], sA + s * C::kABytes, kb * kBK, tm * kBM, polA);
+          tma_load_2d_hint(&tmB, &full_bar[s], sB + s * C::kBBytes, kb * kBK, tn * BN, polB);
+          issued_mask |= 1u << s;
+          issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // bounded wait for this CTA's own copies still in flight
+        for (int j = 0; j < S; ++j)
+          if (issued_mask & (1u << j)) mbar_wait(&full_bar[j], (issued_ph >> j) & 1u, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (elect_one()) {
+      int s = 0;
+      uint32_t ph = 0;
+      int i = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++i) {
+        const int sp = u % args.splits;
+        const int kb0 = sp * args.kb_per_split;
+        const int kb1 = min(args.num_kb, kb0 + args.kb_per_split);
+        const int ab = i & 1;
+        const uint32_t use = (uint32_t)(i >> 1);
+        if (!mbar_wait(&tempty_bar[ab], (use & 1) ^ 1)) {
+          set_status(args.status, kStatusMbarTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + ab * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[s], ph)) {
+            set_status(args.status, kStatusMbarTimeout);
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + s * C::kABytes));
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + s * C::kBBytes));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // +32 bytes per K step of 16 bf16 -> +2 in the encoded start address
+            umma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        umma_commit(&tfull_bar[ab]);
+      }
+    }
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    int i = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+      const int tile = u / args.splits, sp = u % args.splits;
+      const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+      const int ab = i & 1;
+      const uint32_t use = (uint32_t)(i >> 1);
+      if (!mbar_wait(&tfull_bar[ab], use & 1)) {
+        set_status(args.status, kStatusMbarTimeout);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
+      const int m = tm * kBM + row;
+      if (args.splits == 1) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          if (BN >= 32) {
+            tmem_ld32(tbase + c, v);
+          } else {
+            float h[16];
+            tmem_ld16(tbase + c, h);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = h[j];
+#pragma unroll
+            for (int j = 16; j < 32; ++j) v[j] = 0.f;
+          }
+          epi_store_chunk<BN, EPI, TRANS>(args, v, BN >= 32 ? 32 : 16, m, tn * BN + c);
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[ab]);
+      } else {
+        float* ws = args.workspace + ((long)tile * args.splits + sp) * (kBM * BN);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          if (BN >= 32) {
+            tmem_ld32(tbase + c, v);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(ws + (long)row * BN + c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            float h[16];
+            tmem_ld16(tbase + c, h);
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(ws + (long)row * BN + c + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[ab]);
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const int t = atomicAdd(&args.tickets[tile], 1);
+          *ticket_bcast = t;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int t = *ticket_bcast;
+        if (t == args.splits - 1) {
+          __threadfence();
+          const float* base = args.workspace + (long)tile * args.splits * (kBM * BN);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            const int w = BN >= 32 ? 32 : 16;
+            for (int s2 = 0; s2 < args.splits; ++s2) {
+              const float* p = base + (long)s2 * (kBM * BN) + (long)row * BN + c;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                if (j < w) {
+                  const float4 x = __ldcg(reinterpret_cast<const float4*>(p + j));
+                  v[j] += x.x;
+                  v[j + 1] += x.y;
+                  v[j + 2] += x.z;
+                  v[j + 3] += x.w;
+                }
+              }
+            }
+            epi_store_chunk<BN, EPI, TRANS>(args, v, w, m, tn * BN + c);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (threadIdx.x == 64) args.tickets[tile] = 0;  // re-arm for the next launch
+        }
+      }
+    }
+  }
+
+  // Teardown (the producer already drained its in-flight copies on abort).
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host launcher
+// ---------------------------------------------------------------------------
+template <int BN, int EPI, bool TRANS>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
+                        cudaStream_t stream) {
+  using C = GemmCfg<BN>;
+  auto k = gemm_bf16_tc_kernel<BN, EPI, TRANS>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    BWN_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    attr_set[dev & 63] = true;
+  }
+  k<<<grid, kGemmThreads, C::kSmemBytes, stream>>>(ta, tb, a);
+  BWN_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int EPI, bool TRANS>
+static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
+                        cudaStream_t st) {
+  switch (bn) {
+    case 16: launch_gemm<16, EPI, TRANS>(ta, tb, a, grid, st); break;
+    case 32: launch_gemm<32, EPI, TRANS>(ta, tb, a, grid, st); break;
+    case 64: launch_gemm<64, EPI, TRANS>(ta, tb, a, grid, st); break;
+    case 128: launch_gemm<128, EPI, TRANS>(ta, tb, a, grid, st); break;
+    case 256: launch_gemm<256, EPI, TRANS>(ta, tb, a, grid, st); break;
+    default: BWN_FAIL("gemm: unsupported BN %d", bn);
+  }
+}
+
+int gemm_pick_bn(int n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
+  BWN_CHECK(p.K % 8 == 0, "gemm: K must be a multiple of 8 (TMA 16-byte stride rule)");
+  BWN_CHECK(p.lda % 8 == 0 && p.ldb % 8 == 0, "gemm: lda/ldb must be multiples of 8");
+  BWN_CHECK((reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.B) & 15) == 0,
+            "gemm: A/B must be 16-byte aligned");
+  const int bn = p.bn > 0 ? p.bn : gemm_pick_bn(p.N);
+  CUtensorMap ta, tb;
+  make_tmap_2d_bf16(&ta, p.A, p.M, p.K, p.lda, kBM, kBK);
+  make_tmap_2d_bf16(&tb, p.B, p.N, p.K, p.ldb, bn, kBK);
+  GemmArgs a{};
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.tiles_m = (p.M + kBM - 1) / kBM;
+  a.tiles_n = (p.N + bn - 1) / bn;
+  a.num_kb = (p.K + kBK - 1) / kBK;
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int sms = num_sms();
+  int splits = 1;
+  if (p.allow_split && p.workspace && p.tickets && tiles < sms) {
+    splits = sms / tiles;
+    if (splits > a.num_kb / 2) splits = a.num_kb / 2 > 0 ? a.num_kb / 2 : 1;
+    if (splits > 16) splits = 16;
+    const long need = (long)tiles * splits * kBM * bn;
+    if (need > p.workspace_floats) splits = 1;
+    if (tiles > p.tickets_len) splits = 1;
+  }
+  a.splits = splits;
+  a.kb_per_split = (a.num_kb + splits - 1) / splits;
+  a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;  // drop empty splits
+  a.out = p.out;
+  a.ldo = p.ldo;
+  a.resid = p.resid;
+  a.ldr = p.ldr;
+  a.workspace = p.workspace;
+  a.tickets = p.tickets;
+  a.status = p.status;
+  const int units = tiles * a.splits;
+  const int grid = units < sms ? units : sms;
+  const bool tr = p.trans_out;
+  switch (p.epi) {
+    case kEpiBF16:
+      tr ? dispatch_bn<kEpiBF16, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiBF16, false>(bn, ta, tb, a, grid, stream);
+      break;
+    case kEpiResid:
+      tr ? dispatch_bn<kEpiResid, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiResid, false>(bn, ta, tb, a, grid, stream);
+      break;
+    case kEpiSwiGLU:
+      tr ? dispatch_bn<kEpiSwiGLU, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiSwiGLU, false>(bn, ta, tb, a, grid, stream);
+      break;
+    case kEpiF32:
+      tr ? dispatch_bn<kEpiF32, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiF32, false>(bn, ta, tb, a, grid, stream);
+      break;
+    default: BWN_FAIL("gemm: bad epilogue %d", p.epi);
+  }
+}
+
+}  // namespace bwn

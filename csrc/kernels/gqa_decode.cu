@@ -1,0 +1,333 @@
+// Gated GQA decode step (one query token per sequence), fused end to end:
+// per-head q RMSNorm(1+w) and partial RoPE, the new K row's RMSNorm + RoPE,
+// append of the new K/V rows to the cache, softmax(q k^T / sqrt(D)) V over the
+// used prefix [0, pos] (the current row included), and the sigmoid output gate.
+// Reference: the GQA tail / stateful tail kernels
+// (contrib/qwen3.6-27b/kernels/gqa_tail.py:48-203,
+//  contrib/qwen3.6-35b-a3b/kernels/gqa_tail_35b.py:52-394); unlike the
+// reference, only the used prefix is read (not the whole max_seq_len).
+//
+// B200 mapping: flash-decoding.  Grid (splits, KV heads, batch); each CTA takes
+// a contiguous key range of its sequence, sized on the device from the
+// sequence's own position (so a CUDA graph stays valid as positions advance),
+// and streams it in 64-key tiles that TMA loads with the 128-byte swizzle into
+// a double-buffered shared-memory ring.  The G query heads of a KV head share
+// every K/V byte read.  Scores: 4 threads per key (one 64-dim swizzled box
+// each); P.V: one thread per head dimension.  Per-split (max, sum, acc)
+// partials go to a workspace; the last CTA of a (sequence, KV head) to finish
+// (atomic ticket, re-armed afterwards) merges them and applies the gate.  Only
+// the CTA whose range holds `pos` touches cache row `pos`: it writes the new
+// row and substitutes it into its smem tile, so no CTA reads a row being written.
+#include "common/host.h"
+#include "common/sm100.cuh"
+#include "kernels/launch.h"
+
+namespace bwn {
+
+constexpr int kGD = 256;        // head dim
+constexpr int kGTile = 64;      // keys per tile
+constexpr int kGThreads = 256;
+constexpr int kGBoxBytes = kGTile * 128;           // one [64 keys x 64 dims] swizzled box
+constexpr int kGTileBytes = 4 * kGBoxBytes;        // 256 dims = 4 boxes (32 KB)
+
+// byte offset of element (row r, dim d) inside a tile of 4 swizzled boxes
+__device__ __forceinline__ int swz_off(int r, int d) {
+  return (d >> 6) * kGBoxBytes + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + ((d & 7) << 1);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kGThreads, 1)
+    gqa_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      GqaDecodeArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sK = sm;                         // [2][kGTileBytes]
+  uint8_t* sV = sm + 2 * kGTileBytes;       // [2][kGTileBytes]
+  float* sQ = reinterpret_cast<float*>(sm + 4 * kGTileBytes);  // [G][256]
+  float* sP = sQ + G * kGD;                 // [G][64]
+  float* sNew = sP + G * kGTile;            // [2][256] new k (normed+roped), new v
+  float* sRed = sNew + 2 * kGD;             // [8][G+1]
+  float* sM = sRed + 8 * (G + 1);           // running max [G]
+  float* sL = sM + G;                       // running sum [G]
+  float* sAlpha = sL + G;                   // [G]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sAlpha + G + (G & 1 ? 1 : 2));  // [2]
+  int* sTicket = reinterpret_cast<int*>(bar + 2);
+
+  const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int pos = p.positions[b];
+  const int L = pos + 1;  // keys 0..pos
+  int chunk = (L + p.splits - 1) / p.splits;
+  chunk = (chunk + kGTile - 1) / kGTile * kGTile;
+  const int k0 = sp * chunk;
+  const int k1 = min(L, k0 + chunk);
+  const bool has_pos = (pos >= k0 && pos < k1);
+  const long row_base = ((long)b * p.kv_heads + kvh) * p.s_max;
+
+  if (t == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  // ---- prologue: q heads (RMSNorm(1+w) -> RoPE -> * 1/sqrt(D)) ----
+  const float qscale = rsqrtf((float)kGD);
+  {
+    float x[G];
+    float ss[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int qh = kvh * G + g;
+      x[g] = pos >= 0 ? __bfloat162float(p.qg[(long)b * p.qg_stride + (long)qh * 2 * kGD + t]) : 0.f;
+      ss[g] = warp_sum(x[g] * x[g]);
+    }
+    float kx = 0.f, kss = 0.f;
+    if (has_pos) {
+      kx = __bfloat162float(p.k_new[(long)b * p.kv_new_stride + (long)kvh * kGD + t]);
+      kss = warp_sum(kx * kx);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) sRed[warp * (G + 1) + g] = ss[g];
+      sRed[warp * (G + 1) + G] = kss;
+    }
+    __syncthreads();
+    const float qw = 1.f + p.q_norm_w[t];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float tot = 0.f;
+      for (int w = 0; w < 8; ++w) tot += sRed[w * (G + 1) + g];
+      sQ[g * kGD + t] = x[g] * rsqrtf(tot / kGD + p.eps) * qw;
+    }
+    if (has_pos) {
+      float tot = 0.f;
+      for (int w = 0; w < 8; ++w) tot += sRed[w * (G + 1) + G];
+      sNew[t] = kx * rsqrtf(tot / kGD + p.eps) * (1.f + p.k_norm_w[t]);
+      sNew[kGD + t] = __bfloat162float(p.v_new[(long)b * p.kv_new_stride + (long)kvh * kGD + t]);
+    }
+    __syncthreads();
+    // partial RoPE on dims [0, R): rotate-half pairing within R
+    const int R = p.rope_dim, hr = R >> 1;
+    float qr[G];
+    float kr = 0.f;
+    if (t < R && pos >= 0) {
+      const float c = p.cos[(long)pos * R + t], s = p.sin[(long)pos * R + t];
+      const int pt = t < hr ? t + hr : t - hr;
+      const float sg = t < hr ? -1.f : 1.f;
+#pragma unroll
+      for (int g = 0; g < G; ++g) qr[g] = sQ[g * kGD + t] * c + sg * sQ[g * kGD + pt] * s;
+      if (has_pos) kr = sNew[t] * c + sg * sNew[pt] * s;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (t < R) sQ[g * kGD + t] = qr[g];
+      sQ[g * kGD + t] *= qscale;
+    }
+    if (has_pos && t < R) sNew[t] = kr;
+    if (t < G) {
+      sM[t] = -INFINITY;
+      sL[t] = 0.f;
+    }
+    __syncthreads();
+    if (has_pos) {  // append the new row to the cache (only this CTA touches row pos)
+      p.k_cache[(row_base + pos) * kGD + t] = __float2bfloat16(sNew[t]);
+      p.v_cache[(row_base + pos) * kGD + t] = __float2bfloat16(sNew[kGD + t]);
+    }
+  }
+
+  // ---- main loop over 64-key tiles ----
+  float acc[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) acc[g] = 0.f;
+  const int ntiles = k1 > k0 ? (k1 - k0 + kGTile - 1) / kGTile : 0;
+  auto issue = [&](int i) {
+    const int buf = i & 1;
+    const int r0 = (int)(row_base + k0 + i * kGTile);
+    mbar_arrive_expect_tx(&bar[buf], 2 * kGTileBytes);
+#pragma unroll
+    for (int bx = 0; bx < 4; ++bx) {
+      tma_load_2d(&tmK, &bar[buf], sK + buf * kGTileBytes + bx * kGBoxBytes, bx * 64, r0);
+      tma_load_2d(&tmV, &bar[buf], sV + buf * kGTileBytes + bx * kGBoxBytes, bx * 64, r0);
+    }
+  };
+  if (t == 0 && ntiles > 0) issue(0);
+  bool ok = true;
+  for (int i = 0; i < ntiles; ++i) {
+    const int buf = i & 1;
+    if (t == 0 && i + 1 < ntiles) issue(i + 1);
+    if (!mbar_wait(&bar[buf], (i >> 1) & 1)) {
+      set_status(p.status, kStatusMbarTimeout);
+      ok = false;
+    }
+    if (!__syncthreads_and(ok)) {
+      // drain whatever may still be in flight, then leave
+      if (t == 0)
+        for (int j = 0; j < 2; ++j) mbar_wait(&bar[j], ((i + j) >> 1) & 1, 100000000ull);
+      __syncthreads();
+      return;
+    }
+    uint8_t* tk = sK + buf * kGTileBytes;
+    uint8_t* tv = sV + buf * kGTileBytes;
+    const int kbase = k0 + i * kGTile;
+    if (has_pos && pos >= kbase && pos < kbase + kGTile) {
+      const int r = pos - kbase;
+      *reinterpret_cast<__nv_bfloat16*>(tk + swz_off(r, t)) = __float2bfloat16(sNew[t]);
+      *reinterpret_cast<__nv_bfloat16*>(tv + swz_off(r, t)) = __float2bfloat16(sNew[kGD + t]);
+      __syncthreads();
+    }
+    // scores: thread -> (key r, box qt)
+    {
+      const int r = t >> 2, qt = t & 3;
+      float sc[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[g] = 0.f;
+      const uint8_t* rowp = tk + qt * kGBoxBytes + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 raw4 = *reinterpret_cast<const uint4*>(rowp + ((c ^ (r & 7)) << 4));
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw4);
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h2[e]);
+          kf[2 * e] = f.x;
+          kf[2 * e + 1] = f.y;
+        }
+        const int d0 = qt * 64 + c * 8;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(sQ + g * kGD + d0);
+          const float4 qb = *reinterpret_cast<const float4*>(sQ + g * kGD + d0 + 4);
+          sc[g] += kf[0] * qa.x + kf[1] * qa.y + kf[2] * qa.z + kf[3] * qa.w + kf[4] * qb.x + kf[5] * qb.y +
+                   kf[6] * qb.z + kf[7] * qb.w;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 1);
+        sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], 2);
+      }
+      if (qt == 0) {
+        const bool valid = (kbase + r) < k1;
+#pragma unroll
+        for (int g = 0; g < G; ++g) sP[g * kGTile + r] = valid ? sc[g] : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // online softmax: warp g handles head g
+    if (warp < G) {
+      const int g = warp;
+      const float s0 = sP[g * kGTile + lane], s1 = sP[g * kGTile + 32 + lane];
+      const float mt = warp_max(fmaxf(s0, s1));
+      const float mold = sM[g];
+      const float mnew = fmaxf(mold, mt);
+      const float p0 = s0 == -INFINITY ? 0.f : __expf(s0 - mnew);
+      const float p1 = s1 == -INFINITY ? 0.f : __expf(s1 - mnew);
+      const float ls = warp_sum(p0 + p1);
+      sP[g * kGTile + lane] = p0;
+      sP[g * kGTile + 32 + lane] = p1;
+      if (lane == 0) {
+        const float al = mold == -INFINITY ? 0.f : __expf(mold - mnew);
+        sAlpha[g] = al;
+        sL[g] = sL[g] * al + ls;
+        sM[g] = mnew;
+      }
+    }
+    __syncthreads();
+    // P.V: thread -> head dimension d = t
+    {
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] *= sAlpha[g];
+      const int nk = min(kGTile, k1 - kbase);
+      for (int r = 0; r < nk; ++r) {
+        const float v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tv + swz_off(r, t)));
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] += sP[g * kGTile + r] * v;
+      }
+    }
+    __syncthreads();  // tile buffer free for the TMA issued next iteration
+  }
+
+  // ---- write partials, last CTA merges ----
+  const int G2 = 2 + kGD;
+  float* ws = p.workspace + ((((long)b * p.kv_heads + kvh) * p.splits + sp) * G) * G2;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    ws[g * G2 + 2 + t] = acc[g];
+    if (t == 0) {
+      ws[g * G2 + 0] = sM[g];
+      ws[g * G2 + 1] = sL[g];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (t == 0) *sTicket = atomicAdd(&p.tickets[b * p.kv_heads + kvh], 1);
+  __syncthreads();
+  if (*sTicket != p.splits - 1) return;
+  __threadfence();
+  const float* wsb = p.workspace + (((long)b * p.kv_heads + kvh) * p.splits) * G * G2;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(wsb + ((long)s * G + g) * G2));
+    float Lsum = 0.f, o = 0.f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float* e = wsb + ((long)s * G + g) * G2;
+      const float m = __ldcg(e);
+      if (m == -INFINITY) continue;
+      const float w = __expf(m - M);
+      Lsum += __ldcg(e + 1) * w;
+      o += __ldcg(e + 2 + t) * w;
+    }
+    const int qh = kvh * G + g;
+    const float gate = __bfloat162float(p.qg[(long)b * p.qg_stride + (long)qh * 2 * kGD + kGD + t]);
+    const float y = (Lsum > 0.f ? o / Lsum : 0.f) * sigmoid_f(gate);
+    p.out[(long)b * p.out_stride + (long)qh * kGD + t] = __float2bfloat16(y);
+  }
+  if (t == 0) p.tickets[b * p.kv_heads + kvh] = 0;
+}
+
+int gqa_decode_workspace_floats(int batch, int q_heads, int kv_heads, int splits) {
+  return batch * q_heads * splits * (2 + kGD);
+}
+
+static int gqa_smem_bytes(int G) {
+  return 1024 + 4 * kGTileBytes + (G * kGD + G * kGTile + 2 * kGD + 8 * (G + 1) + 3 * G + 2) * 4 + 64;
+}
+
+template <int G>
+static void launch_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const GqaDecodeArgs& p, cudaStream_t st) {
+  const int smem = gqa_smem_bytes(G);
+  static bool set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    BWN_CUDA_CHECK(cudaFuncSetAttribute(gqa_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    set[dev & 63] = true;
+  }
+  dim3 grid(p.splits, p.kv_heads, p.batch);
+  gqa_decode_kernel<G><<<grid, kGThreads, smem, st>>>(tk, tv, p);
+  BWN_CUDA_CHECK(cudaGetLastError());
+}
+
+void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
+  BWN_CHECK(p.q_heads % p.kv_heads == 0, "gqa_decode: q_heads %% kv_heads");
+  BWN_CHECK(p.rope_dim <= kGD && p.rope_dim % 2 == 0, "gqa_decode: bad rope_dim");
+  const int G = p.q_heads / p.kv_heads;
+  CUtensorMap tk, tv;
+  const long rows = (long)p.batch * p.kv_heads * p.s_max;
+  make_tmap_2d_bf16(&tk, p.k_cache, rows, kGD, kGD, kGTile, 64);
+  make_tmap_2d_bf16(&tv, p.v_cache, rows, kGD, kGD, kGTile, 64);
+  switch (G) {
+    case 1: launch_gqa<1>(tk, tv, p, stream); break;
+    case 2: launch_gqa<2>(tk, tv, p, stream); break;
+    case 3: launch_gqa<3>(tk, tv, p, stream); break;
+    case 4: launch_gqa<4>(tk, tv, p, stream); break;
+    case 6: launch_gqa<6>(tk, tv, p, stream); break;
+    case 8: launch_gqa<8>(tk, tv, p, stream); break;
+    default: BWN_FAIL("gqa_decode: unsupported group size %d", G);
+  }
+}
+
+}  // namespace bwn

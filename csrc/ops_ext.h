@@ -1,0 +1,17 @@
+// Registration hooks for op groups that live outside csrc/ops.cpp (prefill,
+// MoE, communication).  Each group adds its schemas, CUDA impls and pybind
+// helpers through these three functions.
+#pragma once
+#include <torch/extension.h>
+#include <torch/library.h>
+
+namespace bwn {
+void register_ext_defs(torch::Library& m);
+void register_ext_impls(torch::Library& m);
+void register_ext_pybind(pybind11::module& mod);
+
+// shared validation helpers (defined in ops.cpp)
+void check_cuda(const at::Tensor& t, const char* name);
+void check_bf16(const at::Tensor& t, const char* name);
+void check_f32(const at::Tensor& t, const char* name);
+}  // namespace bwn
