@@ -150,9 +150,9 @@ def tiny_qwen36(moe: bool = False, layers: int = 4) -> Qwen36Config:
         dn_v_heads=4,
         q_heads=4,
         kv_heads=2,
-        head_dim=64,
-        dn_k_dim=32,
-        dn_v_dim=32,
+        head_dim=256,
+        dn_k_dim=128,
+        dn_v_dim=128,
     )
     if moe:
         kw.update(num_experts=16, top_k=4, moe_inter=64, shared_inter=64)

@@ -1,0 +1,52 @@
+"""Qwen3.6 sparse MoE block: softmax router -> top-k -> renormalise, routed
+SwiGLU experts, sigmoid-gated shared expert (HF ``Qwen3_5MoeSparseMoeBlock``;
+reference ``moe_forward`` ``contrib/qwen3.6-35b-a3b/static_decode_35b.py:701-833``
+and ``_moe`` ``:1110-1185``).
+
+Expert parallelism: each rank holds ``E/ep`` experts and the ``1/tp`` slice of
+the shared expert.  The function returns this rank's partial output; the
+caller's reduction (the reference's EP combine by all-reduce, or the fused
+all-to-all path of :mod:`bwn.parallel.ep`) sums the partials.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops as O
+from ..ops import reference as R
+
+
+def route(model, L, h: torch.Tensor):
+    """Router logits (fp32) -> (weights [T,k] fp32, ids [T,k] int32)."""
+    cfg = model.cfg
+    if h.is_cuda:
+        logits = O.linear_f32(h, L["router"])
+        return O.moe_topk_softmax(logits, cfg.top_k, cfg.norm_topk_prob)
+    logits = h.float() @ L["router"].float().t()
+    return R.moe_route_softmax(logits, cfg.top_k, cfg.norm_topk_prob)
+
+
+def shared_expert(model, L, h: torch.Tensor) -> torch.Tensor:
+    act = O.linear_swiglu(h, L["shared_gate_up"])
+    y = O.linear(act, L["shared_down"])
+    g = torch.sigmoid(O.linear_f32(h, L["shared_gate"]) if h.is_cuda else h.float() @ L["shared_gate"].float().t())
+    return y, g
+
+
+def qwen_moe_forward(model, L, h: torch.Tensor) -> torch.Tensor:
+    """This rank's partial MoE output ``[T, H]`` (bf16)."""
+    d = model.d
+    w, ids = route(model, L, h)
+    if h.is_cuda:
+        return O.moe_experts(h, w, ids, L["experts_gate_up"], L["experts_down"], d.expert_offset,
+                             shared=(L["shared_gate_up"], L["shared_down"], L["shared_gate"]))
+    out = R.moe_experts(h, w, ids, L["experts_gate_up_plain"] if "experts_gate_up_plain" in L else
+                        _deinterleave_experts(L["experts_gate_up"]), L["experts_down"], d.expert_offset)
+    y, g = shared_expert(model, L, h)
+    return (out + g * y.float()).to(h.dtype)
+
+
+def _deinterleave_experts(gu_il: torch.Tensor) -> torch.Tensor:
+    E, n2, H = gu_il.shape
+    x = gu_il.reshape(E, n2 // 32, 2, 16, H)
+    return torch.cat([x[:, :, 0].reshape(E, n2 // 2, H), x[:, :, 1].reshape(E, n2 // 2, H)], dim=1)

@@ -1,0 +1,261 @@
+"""Qwen3.6 hybrid model (gated DeltaNet + gated GQA; dense SwiGLU or routed MoE).
+
+One implementation serves Qwen3.6-27B (dense, ``StaticDecodeModule``,
+``contrib/qwen3.6-27b/static_decode.py:374-963``) and Qwen3.6-35B-A3B (MoE,
+``StaticDecode35B``, ``contrib/qwen3.6-35b-a3b/static_decode_35b.py:836-2449``).
+
+Execution model (B200): one process per GPU, tensor-parallel over a process
+group.  The decode step is a fixed-shape function of static buffers
+(:class:`Qwen36State`) so it can be captured once as a CUDA graph
+(:mod:`bwn.runtime.static_decode`), the analogue of the reference's
+``torch.compile(backend="neuron", fullgraph=True)`` NEFF.  Every hot op is a
+``torch.ops.bwn`` kernel:
+
+* per DeltaNet layer: 1 fused in-projection GEMM ``[qkv|z|b|a]``, the fused
+  recurrent kernel, the out-projection GEMM;
+* per GQA layer: 1 fused ``[q/gate|k|v]`` GEMM, the fused decode-attention
+  kernel (norms, RoPE, KV append, softmax, gate), ``o_proj``;
+* SwiGLU MLP: gate/up GEMM with the SwiGLU epilogue, ``down`` GEMM;
+* between sub-blocks: all-reduce (NCCL baseline or the fused NVLink kernels of
+  :mod:`bwn.parallel.fused`), then the fused residual add + RMSNorm.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.nn as nn
+
+from .. import ops as O
+from ..config import Qwen36Config, tp_dims
+from ..io import qwen36_weights as W
+from ..ops import reference as R
+from ..parallel.comm import Comm
+
+
+@dataclass
+class Qwen36State:
+    """Static per-sequence decode state (one writer per buffer per step)."""
+
+    conv: torch.Tensor       # [L_dn, B, 4, C]  conv ring (slot = position % 4)
+    ssm: torch.Tensor        # [L_dn, B, VH, 128, 128]  recurrent state
+    k_cache: torch.Tensor    # [L_gqa, B, KVH, S_max, D]
+    v_cache: torch.Tensor
+    positions: torch.Tensor  # [B] int32: position of the next token
+
+    @property
+    def batch(self) -> int:
+        return self.positions.shape[0]
+
+    def reset(self, rows=None) -> None:
+        if rows is None:
+            self.conv.zero_()
+            self.ssm.zero_()
+            self.positions.zero_()
+        else:
+            self.conv[:, rows] = 0
+            self.ssm[:, rows] = 0
+            self.positions[rows] = 0
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.conv, self.ssm, self.k_cache, self.v_cache))
+
+
+class Qwen36Model(nn.Module):
+    """Rank-local Qwen3.6 model.  Parameters hold this rank's shards only."""
+
+    def __init__(self, cfg: Qwen36Config, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16):
+        super().__init__()
+        self.cfg = cfg
+        self.comm = comm or Comm.single()
+        self.tp = self.comm.size
+        self.rank = self.comm.rank
+        self.d = tp_dims(cfg, self.tp, self.rank)
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.layers: list[dict[str, torch.Tensor]] = []
+        self.g: dict[str, torch.Tensor] = {}
+        cos, sin = R.rope_table(1, cfg.rope_dim, cfg.rope_theta, device=self.device)
+        self.rope_cos, self.rope_sin = cos, sin
+        self.fused_comm = None  # set by parallel.fused when the NVLink kernels are enabled
+
+    # ------------------------------------------------------------------ load
+    def load_hf(self, get: Callable[[str], torch.Tensor]) -> "Qwen36Model":
+        cfg = self.cfg
+        self.layers = []
+        for i in range(cfg.num_layers):
+            t = W.fuse_layer(cfg, i, get, self.tp, self.rank, self.dtype)
+            self.layers.append({k: v.to(self.device) for k, v in t.items()})
+        self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, get, self.tp, self.rank, self.dtype).items()}
+        return self
+
+    def init_random(self, seed: int = 0, gen_device=None) -> "Qwen36Model":
+        """Random-init weights from a seed (same model for every TP degree)."""
+        cfg = self.cfg
+        gd = gen_device or self.device
+        self.layers = []
+        for i in range(cfg.num_layers):
+            hf = W.synthetic_hf_layer(cfg, i, seed, gd)
+            t = W.fuse_layer(cfg, i, hf.__getitem__, self.tp, self.rank, self.dtype)
+            self.layers.append({k: v.to(self.device) for k, v in t.items()})
+            del hf
+        glob = W.synthetic_hf_globals(cfg, seed, gd)
+        self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, glob.__getitem__, self.tp, self.rank,
+                                                                   self.dtype).items()}
+        return self
+
+    def weight_bytes(self) -> int:
+        n = sum(v.numel() * v.element_size() for L in self.layers for v in L.values())
+        return n + sum(v.numel() * v.element_size() for v in self.g.values())
+
+    # ----------------------------------------------------------------- state
+    def new_state(self, batch: int, max_seq: int, ssm_dtype=torch.float32) -> Qwen36State:
+        cfg, d = self.cfg, self.d
+        dev = self.device
+        st = Qwen36State(
+            conv=torch.zeros(cfg.num_deltanet, batch, cfg.conv_kernel, d.dn_qkv_dim, dtype=self.dtype, device=dev),
+            ssm=torch.zeros(cfg.num_deltanet, batch, d.dn_v_heads, cfg.dn_k_dim, cfg.dn_v_dim, dtype=ssm_dtype,
+                            device=dev),
+            k_cache=torch.zeros(cfg.num_gqa, batch, d.kv_heads, max_seq, cfg.head_dim, dtype=self.dtype, device=dev),
+            v_cache=torch.zeros(cfg.num_gqa, batch, d.kv_heads, max_seq, cfg.head_dim, dtype=self.dtype, device=dev),
+            positions=torch.zeros(batch, dtype=torch.int32, device=dev),
+        )
+        self.ensure_rope(max_seq)
+        return st
+
+    def ensure_rope(self, max_seq: int) -> None:
+        if self.rope_cos.shape[0] < max_seq:
+            self.rope_cos, self.rope_sin = R.rope_table(max_seq, self.cfg.rope_dim, self.cfg.rope_theta,
+                                                        device=self.device)
+
+    # ---------------------------------------------------------------- decode
+    def _reduce_add_norm(self, part: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``x += all_reduce(part)``; return ``rmsnorm(x) * (1+w)``."""
+        if self.tp > 1:
+            self.comm.all_reduce_(part)
+        return O.add_rms_norm(part, x, w, self.cfg.rms_eps)
+
+    def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
+        """Row-parallel projection + all-reduce + residual add + RMSNorm.  With the
+        fused NVLink path this is one kernel (GEMM epilogue -> peer reduce)."""
+        if self.fused_comm is not None:
+            return self.fused_comm.gemm_allreduce_add_norm(a, w, x, norm_w, self.cfg.rms_eps)
+        return self._reduce_add_norm(O.linear(a, w), x, norm_w)
+
+    def _deltanet_decode(self, i: int, h: torch.Tensor, st: Qwen36State, di: int) -> torch.Tensor:
+        L, d = self.layers[i], self.d
+        C, Z, VH = d.dn_qkv_dim, d.dn_value_dim, d.dn_v_heads
+        proj = O.linear(h, L["in_proj"])  # [B, C + Z + 2VH]
+        qkv, z = proj[:, :C], proj[:, C:C + Z]
+        b, a = proj[:, C + Z:C + Z + VH], proj[:, C + Z + VH:]
+        return O.deltanet_decode(qkv, z, a, b, st.conv[di], st.ssm[di], st.positions, L["conv_w"], L["A_log"],
+                                 L["dt_bias"], L["norm_w"], d.dn_k_heads, self.cfg.rms_eps)
+
+    def _gqa_decode(self, i: int, h: torch.Tensor, st: Qwen36State, gi: int) -> torch.Tensor:
+        L, d, cfg = self.layers[i], self.d, self.cfg
+        B = h.shape[0]
+        D, QH, KVH = cfg.head_dim, d.q_heads, d.kv_heads
+        proj = O.linear(h, L["qkv_proj"])  # [B, QH*2D + 2*KVH*D]
+        qg = proj[:, :QH * 2 * D].view(B, QH, 2 * D)
+        k = proj[:, QH * 2 * D:QH * 2 * D + KVH * D].view(B, KVH, D)
+        v = proj[:, QH * 2 * D + KVH * D:].view(B, KVH, D)
+        return O.gqa_decode(qg, k, v, L["q_norm"], L["k_norm"], self.rope_cos, self.rope_sin, st.k_cache[gi],
+                            st.v_cache[gi], st.positions, cfg.rms_eps)
+
+    def _mlp(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        """Returns the (TP-partial) MLP / MoE output before the reduction."""
+        L = self.layers[i]
+        if self.cfg.is_moe:
+            from .moe import qwen_moe_forward
+            return qwen_moe_forward(self, L, h)
+        return O.linear_swiglu(h, L["gate_up"])
+
+    def decode_hidden(self, tokens: torch.Tensor, st: Qwen36State) -> torch.Tensor:
+        """One decode step for ``tokens [B]`` at ``st.positions``; advances the
+        positions and returns the final-normed hidden ``[B, H]``."""
+        cfg = self.cfg
+        x = O.embedding(tokens.int(), self.g["embed"], 0)  # residual stream [B, H]
+        h = O.rms_norm(x, self.layers[0]["in_norm"], cfg.rms_eps)
+        di = gi = 0
+        for i in range(cfg.num_layers):
+            L = self.layers[i]
+            if cfg.layer_type(i) == "deltanet":
+                o = self._deltanet_decode(i, h, st, di)
+                h = self._row_parallel(o, L["out_proj"], x, L["post_norm"])
+                di += 1
+            else:
+                o = self._gqa_decode(i, h, st, gi)
+                h = self._row_parallel(o, L["o_proj"], x, L["post_norm"])
+                gi += 1
+            nxt = self.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else self.g["final_norm"]
+            if cfg.is_moe:
+                part = self._mlp(i, h)
+                h = self._reduce_add_norm(part, x, nxt)
+            else:
+                act = self._mlp(i, h)
+                h = self._row_parallel(act, L["down"], x, nxt)
+        st.positions.add_(1)
+        return h
+
+    def greedy(self, h: torch.Tensor) -> torch.Tensor:
+        """Vocab-sharded LM head + greedy with the lowest-id tie break
+        (``static_decode_35b.py:1534-1564``) as a single int64 max all-reduce."""
+        logits = O.linear(h, self.g["lm_head"])
+        key = O.argmax_packed(logits, self.d.vocab_offset)
+        if self.tp > 1:
+            self.comm.all_reduce_max_(key)
+        return O.unpack_argmax(key)
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Full-vocab logits (gathered across vocab shards)."""
+        local = O.linear_f32(h, self.g["lm_head"]) if h.is_cuda else h.float() @ self.g["lm_head"].float().t()
+        return self.comm.all_gather_last(local)
+
+    def decode_step(self, tokens: torch.Tensor, st: Qwen36State) -> torch.Tensor:
+        return self.greedy(self.decode_hidden(tokens, st))
+
+    # --------------------------------------------------------------- prefill
+    def prefill_hidden(self, tokens: torch.Tensor, st: Qwen36State, valid_len: torch.Tensor | None = None,
+                       chunk: int = 64) -> torch.Tensor:
+        """Process a prompt chunk ``tokens [B, S]`` starting at ``st.positions``
+        (all rows share the start position, as in the reference's bucketed
+        prefill, ``static_decode_35b.py:2497-2678``).  ``valid_len [B]`` marks
+        real rows; pad rows leave every state untouched.  Returns the final-normed
+        hidden of each row's last valid token ``[B, H]``."""
+        from . import qwen36_prefill as P
+        return P.prefill_hidden(self, tokens, st, valid_len, chunk)
+
+    def prefill(self, tokens: torch.Tensor, st: Qwen36State, valid_len=None, bucket: int = 0) -> torch.Tensor:
+        """Bucketed prefill (``prefill_bucketed``): chunks of ``bucket`` tokens
+        (whole prompt if 0); returns the greedy next token ids ``[B]``."""
+        B, S = tokens.shape
+        bucket = bucket or S
+        vl = valid_len if valid_len is not None else torch.full((B,), S, dtype=torch.int32, device=tokens.device)
+        h = None
+        for c0 in range(0, S, bucket):
+            c1 = min(S, c0 + bucket)
+            chunk_valid = (vl.to(tokens.device) - c0).clamp(0, c1 - c0).int()
+            hc = self.prefill_hidden(tokens[:, c0:c1], st, chunk_valid)
+            # keep the hidden of the last valid row seen so far per sequence
+            h = hc if h is None else torch.where((chunk_valid > 0)[:, None], hc, h)
+        return self.greedy(h)
+
+
+def build_qwen36(cfg: Qwen36Config, comm: Comm | None = None, device="cpu", seed: int | None = 0,
+                 hf_state: dict | None = None, dtype=torch.bfloat16) -> Qwen36Model:
+    m = Qwen36Model(cfg, comm, device, dtype)
+    if hf_state is not None:
+        m.load_hf(W.hf_getter(hf_state))
+    elif seed is not None:
+        m.init_random(seed)
+    return m
+
+
+def param_gb(cfg: Qwen36Config) -> float:
+    return cfg.param_count() * 2 / 1e9
+
+
+def attn_scale(cfg: Qwen36Config) -> float:
+    return 1.0 / math.sqrt(cfg.head_dim)

@@ -1,0 +1,64 @@
+"""Prompt processing for :class:`~bwn.models.qwen36.Qwen36Model`.
+
+One chunk of ``S`` tokens per sequence at a shared start position (the
+reference's bucketed chunked prefill, ``static_decode_35b.py:2497-2678``,
+``_deltanet_prefill`` ``:2137-2258``, ``_gqa_prefill_chunk`` ``:2316-2449``):
+
+* all projections run on the flattened ``[B*S, H]`` token matrix (tcgen05 GEMMs
+  in the normal orientation, 128x256 tiles);
+* DeltaNet: causal conv with the ring as history, then the chunked gated delta
+  rule carrying the recurrent state in and out (pad rows get ``g = beta = 0``);
+* GQA: q/k norm + partial RoPE at the runtime offset, K/V written into the
+  cache, prefix-aware causal attention over ``[0, start+S)``, sigmoid gate.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops as O
+
+
+def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64) -> torch.Tensor:
+    cfg, d = model.cfg, model.d
+    B, S = tokens.shape
+    dev = tokens.device
+    start = int(st.positions[0].item())
+    model.ensure_rope(start + S)
+    if valid_len is None:
+        valid_len = torch.full((B,), S, dtype=torch.int32, device=dev)
+    valid_len = valid_len.to(dev).int()
+    T = B * S
+    x = O.embedding(tokens.reshape(T).int(), model.g["embed"], 0)  # [T, H]
+    h = O.rms_norm(x, model.layers[0]["in_norm"], cfg.rms_eps)
+    di = gi = 0
+    for i in range(cfg.num_layers):
+        L = model.layers[i]
+        if cfg.layer_type(i) == "deltanet":
+            C, Z, VH = d.dn_qkv_dim, d.dn_value_dim, d.dn_v_heads
+            proj = O.linear(h, L["in_proj"]).view(B, S, -1)
+            o = O.deltanet_prefill(proj[..., :C], proj[..., C:C + Z], proj[..., C + Z + VH:],
+                                   proj[..., C + Z:C + Z + VH], st.conv[di], st.ssm[di], start, valid_len,
+                                   L["conv_w"], L["A_log"], L["dt_bias"], L["norm_w"], d.dn_k_heads, cfg.rms_eps,
+                                   chunk)
+            h = model._row_parallel(o.reshape(T, -1), L["out_proj"], x, L["post_norm"])
+            di += 1
+        else:
+            D, QH, KVH = cfg.head_dim, d.q_heads, d.kv_heads
+            proj = O.linear(h, L["qkv_proj"]).view(B, S, -1)
+            qg = proj[..., :QH * 2 * D].reshape(B, S, QH, 2 * D)
+            k = proj[..., QH * 2 * D:QH * 2 * D + KVH * D].reshape(B, S, KVH, D)
+            v = proj[..., QH * 2 * D + KVH * D:].reshape(B, S, KVH, D)
+            o = O.gqa_prefill(qg, k, v, L["q_norm"], L["k_norm"], model.rope_cos, model.rope_sin,
+                              st.k_cache[gi], st.v_cache[gi], start, cfg.rms_eps)
+            h = model._row_parallel(o.reshape(T, -1), L["o_proj"], x, L["post_norm"])
+            gi += 1
+        nxt = model.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else model.g["final_norm"]
+        if cfg.is_moe:
+            part = model._mlp(i, h)
+            h = model._reduce_add_norm(part, x, nxt)
+        else:
+            act = model._mlp(i, h)
+            h = model._row_parallel(act, L["down"], x, nxt)
+    st.positions.add_(valid_len)
+    last = (valid_len.long() - 1).clamp(min=0) + torch.arange(B, device=dev) * S
+    return h[last]

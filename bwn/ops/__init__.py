@@ -138,3 +138,43 @@ def gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache,
         return ops().gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions,
                                 eps, splits)
     return ref.gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions, eps)
+
+
+# --------------------------------------------------------------------------
+# prefill
+# --------------------------------------------------------------------------
+def deltanet_prefill(qkv, z, a, b, conv_ring, state, start_pos: int, valid_len, conv_w, A_log, dt_bias, norm_w,
+                     k_heads: int, eps: float = 1e-6, chunk: int = 64) -> torch.Tensor:
+    """Gated-DeltaNet over a prompt chunk ``qkv [B,S,C]`` (conv ring + recurrent
+    state carried in and out).  Returns ``[B, S, VH*128]``."""
+    if qkv.is_cuda:
+        return _prefill_cuda().deltanet_prefill(qkv, z, a, b, conv_ring, state, start_pos, valid_len, conv_w, A_log,
+                                                dt_bias, norm_w, k_heads, eps)
+    return ref.deltanet_prefill(qkv, a, b, z, conv_ring, state, start_pos, valid_len, conv_w, A_log, dt_bias,
+                                norm_w, k_heads, state.shape[2], state.shape[3], eps, chunk)
+
+
+def gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_pos: int,
+                eps: float = 1e-6) -> torch.Tensor:
+    """Gated GQA over a prompt chunk: q/k norm + RoPE at ``start_pos``, K/V
+    written to cache rows ``[start, start+S)``, causal attention over the used
+    prefix, sigmoid gate.  ``qg [B,S,QH,2D]``, ``k/v [B,S,KVH,D]`` -> ``[B,S,QH*D]``."""
+    if qg.is_cuda:
+        return _prefill_cuda().gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_pos, eps)
+    B, S, QH, D2 = qg.shape
+    D = D2 // 2
+    q, gate = qg.float().split(D, dim=-1)
+    c = cos[start_pos:start_pos + S][None, :, None]
+    s = sin[start_pos:start_pos + S][None, :, None]
+    q = ref.apply_partial_rope(ref.rms_norm(q, q_norm_w, eps), c, s)
+    kk = ref.apply_partial_rope(ref.rms_norm(k.float(), k_norm_w, eps), c, s)
+    k_cache[:, :, start_pos:start_pos + S] = kk.transpose(1, 2).to(k_cache.dtype)
+    v_cache[:, :, start_pos:start_pos + S] = v.transpose(1, 2).to(v_cache.dtype)
+    o = ref.attention_prefill(q.transpose(1, 2), k_cache, v_cache, start_pos)  # [B, QH, S, D]
+    o = o.transpose(1, 2) * torch.sigmoid(gate)
+    return o.reshape(B, S, QH * D).to(qg.dtype)
+
+
+def _prefill_cuda():
+    from . import prefill_cuda
+    return prefill_cuda

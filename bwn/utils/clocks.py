@@ -1,0 +1,65 @@
+"""Sample SM clocks and throttle reasons with ``nvidia-smi`` while a timed
+region runs (read-only queries; no GPU setting is changed)."""
+from __future__ import annotations
+
+import shutil
+import statistics
+import subprocess
+import threading
+
+_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+_REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpu_index: int = 0, period_ms: int = 200):
+        self.idx = gpu_index
+        self.period = period_ms
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi") is None:
+            return self
+        self.proc = subprocess.Popen(
+            ["nvidia-smi", f"--query-gpu={_FIELDS}", "--format=csv,noheader,nounits", f"-lms={self.period}",
+             f"-i={self.idx}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self._t is not None:
+                self._t.join(timeout=2)
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(_REASONS, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}

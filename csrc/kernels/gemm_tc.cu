@@ -424,14 +424,24 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   a.num_kb = (p.K + kBK - 1) / kBK;
   const int tiles = a.tiles_m * a.tiles_n;
   const int sms = num_sms();
+  // Split-K when the output tiles cannot fill the SMs.  Cost model in units of
+  // k-blocks per CTA: waves(tiles*s) * ceil(kb/s), plus a small charge for the
+  // fp32 partial round trip of the last-arriver reduction.
   int splits = 1;
-  if (p.allow_split && p.workspace && p.tickets && tiles < sms) {
-    splits = sms / tiles;
-    if (splits > a.num_kb / 2) splits = a.num_kb / 2 > 0 ? a.num_kb / 2 : 1;
-    if (splits > 16) splits = 16;
-    const long need = (long)tiles * splits * kBM * bn;
-    if (need > p.workspace_floats) splits = 1;
-    if (tiles > p.tickets_len) splits = 1;
+  if (p.allow_split && p.workspace && p.tickets && tiles < 2 * sms && tiles <= p.tickets_len) {
+    long best = -1;
+    for (int s = 1; s <= 16; ++s) {
+      const int kbps = (a.num_kb + s - 1) / s;
+      if (s > 1 && kbps < 4) break;
+      const long units = (long)tiles * s;
+      if (units > 4L * sms) break;
+      if (s > 1 && units * kBM * bn > p.workspace_floats) break;
+      const long cost = ((units + sms - 1) / sms) * kbps + (s > 1 ? 2 : 0);
+      if (best < 0 || cost < best) {
+        best = cost;
+        splits = s;
+      }
+    }
   }
   a.splits = splits;
   a.kb_per_split = (a.num_kb + splits - 1) / splits;

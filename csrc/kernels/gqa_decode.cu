@@ -13,7 +13,9 @@
 // and streams it in 64-key tiles that TMA loads with the 128-byte swizzle into
 // a double-buffered shared-memory ring.  The G query heads of a KV head share
 // every K/V byte read.  Scores: 4 threads per key (one 64-dim swizzled box
-// each); P.V: one thread per head dimension.  Per-split (max, sum, acc)
+// each, q quarters padded 4 banks apart so the four boxes' q reads do not
+// conflict); P.V: each thread owns 2 head dims over half of the tile's keys and
+// reads the probabilities 4 keys at a time.  Per-split (max, sum, acc)
 // partials go to a workspace; the last CTA of a (sequence, KV head) to finish
 // (atomic ticket, re-armed afterwards) merges them and applies the gate.  Only
 // the CTA whose range holds `pos` touches cache row `pos`: it writes the new
@@ -30,6 +32,10 @@ constexpr int kGThreads = 256;
 constexpr int kGBoxBytes = kGTile * 128;           // one [64 keys x 64 dims] swizzled box
 constexpr int kGTileBytes = 4 * kGBoxBytes;        // 256 dims = 4 boxes (32 KB)
 
+constexpr int kQStride = 4 * (64 + 4);  // padded q row: each 64-dim quarter starts 4 banks later
+
+__device__ __forceinline__ int qidx(int g, int d) { return g * kQStride + (d >> 6) * 68 + (d & 63); }
+
 // byte offset of element (row r, dim d) inside a tile of 4 swizzled boxes
 __device__ __forceinline__ int swz_off(int r, int d) {
   return (d >> 6) * kGBoxBytes + r * 128 + ((((d & 63) >> 3) ^ (r & 7)) << 4) + ((d & 7) << 1);
@@ -44,14 +50,16 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sK = sm;                         // [2][kGTileBytes]
   uint8_t* sV = sm + 2 * kGTileBytes;       // [2][kGTileBytes]
-  float* sQ = reinterpret_cast<float*>(sm + 4 * kGTileBytes);  // [G][256]
-  float* sP = sQ + G * kGD;                 // [G][64]
+  float* sQ = reinterpret_cast<float*>(sm + 4 * kGTileBytes);  // [G][kQStride] (padded)
+  float* sP = sQ + G * kQStride;            // [G][64]
   float* sNew = sP + G * kGTile;            // [2][256] new k (normed+roped), new v
   float* sRed = sNew + 2 * kGD;             // [8][G+1]
   float* sM = sRed + 8 * (G + 1);           // running max [G]
   float* sL = sM + G;                       // running sum [G]
   float* sAlpha = sL + G;                   // [G]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sAlpha + G + (G & 1 ? 1 : 2));  // [2]
+  // 8-byte align the barriers (float offset of sAlpha+G from the 1024-aligned base)
+  const int used = G * kQStride + G * kGTile + 2 * kGD + 8 * (G + 1) + 3 * G;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sAlpha + G + ((used & 1) ? 1 : 2));  // [2]
   int* sTicket = reinterpret_cast<int*>(bar + 2);
 
   const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -97,7 +105,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     for (int g = 0; g < G; ++g) {
       float tot = 0.f;
       for (int w = 0; w < 8; ++w) tot += sRed[w * (G + 1) + g];
-      sQ[g * kGD + t] = x[g] * rsqrtf(tot / kGD + p.eps) * qw;
+      sQ[qidx(g, t)] = x[g] * rsqrtf(tot / kGD + p.eps) * qw;
     }
     if (has_pos) {
       float tot = 0.f;
@@ -115,14 +123,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const int pt = t < hr ? t + hr : t - hr;
       const float sg = t < hr ? -1.f : 1.f;
 #pragma unroll
-      for (int g = 0; g < G; ++g) qr[g] = sQ[g * kGD + t] * c + sg * sQ[g * kGD + pt] * s;
+      for (int g = 0; g < G; ++g) qr[g] = sQ[qidx(g, t)] * c + sg * sQ[qidx(g, pt)] * s;
       if (has_pos) kr = sNew[t] * c + sg * sNew[pt] * s;
     }
     __syncthreads();
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      if (t < R) sQ[g * kGD + t] = qr[g];
-      sQ[g * kGD + t] *= qscale;
+      if (t < R) sQ[qidx(g, t)] = qr[g];
+      sQ[qidx(g, t)] *= qscale;
     }
     if (has_pos && t < R) sNew[t] = kr;
     if (t < G) {
@@ -137,9 +145,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
   }
 
   // ---- main loop over 64-key tiles ----
-  float acc[G];
+  float acc[G], acc2[G];  // dims 2*dp and 2*dp+1 over this thread's key half
 #pragma unroll
-  for (int g = 0; g < G; ++g) acc[g] = 0.f;
+  for (int g = 0; g < G; ++g) acc[g] = acc2[g] = 0.f;
   const int ntiles = k1 > k0 ? (k1 - k0 + kGTile - 1) / kGTile : 0;
   auto issue = [&](int i) {
     const int buf = i & 1;
@@ -197,8 +205,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
         const int d0 = qt * 64 + c * 8;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          const float4 qa = *reinterpret_cast<const float4*>(sQ + g * kGD + d0);
-          const float4 qb = *reinterpret_cast<const float4*>(sQ + g * kGD + d0 + 4);
+          const float4 qa = *reinterpret_cast<const float4*>(sQ + qidx(g, d0));
+          const float4 qb = *reinterpret_cast<const float4*>(sQ + qidx(g, d0) + 4);
           sc[g] += kf[0] * qa.x + kf[1] * qa.y + kf[2] * qa.z + kf[3] * qa.w + kf[4] * qb.x + kf[5] * qb.y +
                    kf[6] * qb.z + kf[7] * qb.w;
         }
@@ -235,30 +243,59 @@ __global__ void __launch_bounds__(kGThreads, 1)
       }
     }
     __syncthreads();
-    // P.V: thread -> head dimension d = t
+    // P.V: thread -> (key half hf, dim pair dp); probabilities read 4 keys at a time
     {
+      const int hf = t >> 7, dp = t & 127;
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] *= sAlpha[g];
+      for (int g = 0; g < G; ++g) {
+        acc[g] *= sAlpha[g];
+        acc2[g] *= sAlpha[g];
+      }
       const int nk = min(kGTile, k1 - kbase);
-      for (int r = 0; r < nk; ++r) {
-        const float v = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(tv + swz_off(r, t)));
+      const int r0 = hf * 32;
+      const int r1 = min(r0 + 32, nk);
+      for (int r = r0; r < r1; r += 4) {
+        float4 pp[G];
 #pragma unroll
-        for (int g = 0; g < G; ++g) acc[g] += sP[g * kGTile + r] * v;
+        for (int g = 0; g < G; ++g) pp[g] = *reinterpret_cast<const float4*>(sP + g * kGTile + r);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(tv + swz_off(r + j, 2 * dp));
+          const float2 v = __bfloat1622float2(v2);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float pj = j == 0 ? pp[g].x : j == 1 ? pp[g].y : j == 2 ? pp[g].z : pp[g].w;
+            acc[g] += pj * v.x;
+            acc2[g] += pj * v.y;
+          }
+        }
       }
     }
     __syncthreads();  // tile buffer free for the TMA issued next iteration
   }
 
-  // ---- write partials, last CTA merges ----
+  // ---- fold the two key halves, write partials, last CTA merges ----
+  float* sAcc = reinterpret_cast<float*>(sK);  // tile buffers are idle now: [G][256]
+  if (t >= 128) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      sAcc[g * kGD + 2 * (t - 128)] = acc[g];
+      sAcc[g * kGD + 2 * (t - 128) + 1] = acc2[g];
+    }
+  }
+  __syncthreads();
   const int G2 = 2 + kGD;
   float* ws = p.workspace + ((((long)b * p.kv_heads + kvh) * p.splits + sp) * G) * G2;
+  if (t < 128) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    ws[g * G2 + 2 + t] = acc[g];
-    if (t == 0) {
-      ws[g * G2 + 0] = sM[g];
-      ws[g * G2 + 1] = sL[g];
+    for (int g = 0; g < G; ++g) {
+      ws[g * G2 + 2 + 2 * t] = acc[g] + sAcc[g * kGD + 2 * t];
+      ws[g * G2 + 3 + 2 * t] = acc2[g] + sAcc[g * kGD + 2 * t + 1];
     }
+  }
+  if (t < G) {
+    ws[t * G2 + 0] = sM[t];
+    ws[t * G2 + 1] = sL[t];
   }
   __threadfence();
   __syncthreads();
@@ -293,7 +330,7 @@ int gqa_decode_workspace_floats(int batch, int q_heads, int kv_heads, int splits
 }
 
 static int gqa_smem_bytes(int G) {
-  return 1024 + 4 * kGTileBytes + (G * kGD + G * kGTile + 2 * kGD + 8 * (G + 1) + 3 * G + 2) * 4 + 64;
+  return 1024 + 4 * kGTileBytes + (G * kQStride + G * kGTile + 2 * kGD + 8 * (G + 1) + 3 * G + 2) * 4 + 64;
 }
 
 template <int G>

@@ -124,8 +124,8 @@ void linear_into(const Tensor& x, const Tensor& w, const Tensor& out, int64_t ep
   p.bn = (epi == kEpiSwiGLU && !swap && bn < 32) ? 32 : bn;
   const int tiles = ((p.M + 127) / 128) * ((p.N + p.bn - 1) / p.bn);
   const int sms = num_sms();
-  if (tiles < sms) {
-    Scratch& s = scratch_for(x, (long)sms * 128 * p.bn, sms);
+  if (tiles < 2 * sms) {
+    Scratch& s = scratch_for(x, 4L * sms * 128 * p.bn, 2 * sms);
     p.workspace = s.ws.data_ptr<float>();
     p.workspace_floats = s.ws.numel();
     p.tickets = s.tickets.data_ptr<int>();
