@@ -1,0 +1,82 @@
+#!/usr/bin/env python
+"""Run one bwn kernel on a fixed small case a few times (for ncu captures and
+quick timing).  Each op here is one kernel launch per iteration.
+
+    python bench/kernel_case.py --op linear --M 32 --N 5120 --K 6144
+    python bench/kernel_case.py --op gqa --B 32 --QH 24 --KVH 4 --ctx 2048
+    python bench/kernel_case.py --op deltanet --B 32 --KH 16 --VH 48
+"""
+import argparse
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import bwn.ops as O  # noqa: E402
+from bwn.ops import reference as R  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", required=True, choices=["linear", "swiglu", "gqa", "deltanet"])
+    ap.add_argument("--M", type=int, default=32)
+    ap.add_argument("--N", type=int, default=5120)
+    ap.add_argument("--K", type=int, default=6144)
+    ap.add_argument("--B", type=int, default=32)
+    ap.add_argument("--QH", type=int, default=24)
+    ap.add_argument("--KVH", type=int, default=4)
+    ap.add_argument("--KH", type=int, default=16)
+    ap.add_argument("--VH", type=int, default=48)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--iters", type=int, default=5)
+    a = ap.parse_args()
+    dev = "cuda"
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    if a.op in ("linear", "swiglu"):
+        x = torch.randn(a.M, a.K, device=dev).bfloat16()
+        w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
+        fn = (lambda: O.linear(x, w)) if a.op == "linear" else (lambda: O.linear_swiglu(x, w))
+        nbytes = a.N * a.K * 2
+    elif a.op == "gqa":
+        D = 256
+        qg = torch.randn(a.B, a.QH, 2 * D, device=dev).bfloat16()
+        kv = torch.randn(a.B, 2, a.KVH, D, device=dev).bfloat16()
+        qn = torch.zeros(D, device=dev)
+        cos, sin = R.rope_table(a.ctx + 64, 64, 1e7, device=dev)
+        kc = torch.randn(a.B, a.KVH, a.ctx + 64, D, device=dev).bfloat16()
+        vc = torch.randn_like(kc)
+        pos = torch.full((a.B,), a.ctx, dtype=torch.int32, device=dev)
+        fn = lambda: O.gqa_decode(qg, kv[:, 0], kv[:, 1], qn, qn, cos, sin, kc, vc, pos)  # noqa: E731
+        nbytes = a.B * a.KVH * (a.ctx + 1) * D * 2 * 2
+    else:
+        C = 2 * a.KH * 128 + a.VH * 128
+        fused = torch.randn(a.B, C + a.VH * 128 + 2 * a.VH, device=dev).bfloat16()
+        qkv, z = fused[:, :C], fused[:, C:C + a.VH * 128]
+        bb, aa = fused[:, C + a.VH * 128:C + a.VH * 129], fused[:, C + a.VH * 129:]
+        ring = torch.randn(a.B, 4, C, device=dev).bfloat16()
+        st = torch.randn(a.B, a.VH, 128, 128, device=dev) * 0.05
+        pos = torch.full((a.B,), 100, dtype=torch.int32, device=dev)
+        cw = torch.randn(C, 4, device=dev)
+        hv = torch.zeros(a.VH, device=dev)
+        nw = torch.ones(128, device=dev)
+        fn = lambda: O.deltanet_decode(qkv, z, aa, bb, ring, st, pos, cw, hv, hv, nw, a.KH)  # noqa: E731
+        nbytes = a.B * a.VH * 128 * 128 * 4 * 2
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.iters):
+        ev[0].record()
+        fn()
+        ev[1].record()
+        torch.cuda.synchronize()
+        ts.append(ev[0].elapsed_time(ev[1]))
+    t = sorted(ts)[len(ts) // 2]
+    O.check_status(a.op)
+    print(f"{a.op}: median {t * 1e3:.1f} us, {nbytes / t / 1e6:.1f} GB/s (algorithmic bytes {nbytes / 1e6:.1f} MB)")
+
+
+if __name__ == "__main__":
+    main()

@@ -424,24 +424,16 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   a.num_kb = (p.K + kBK - 1) / kBK;
   const int tiles = a.tiles_m * a.tiles_n;
   const int sms = num_sms();
-  // Split-K when the output tiles cannot fill the SMs.  Cost model in units of
-  // k-blocks per CTA: waves(tiles*s) * ceil(kb/s), plus a small charge for the
-  // fp32 partial round trip of the last-arriver reduction.
+  // Split-K when the output tiles cannot fill the SMs: one wave of
+  // tiles*splits <= #SM CTAs, each with >= 4 k-blocks.  (Several split units
+  // per persistent CTA measured ~2x slower on decode shapes: each unit's
+  // partial round trip and fence serialises the CTA.)
   int splits = 1;
-  if (p.allow_split && p.workspace && p.tickets && tiles < 2 * sms && tiles <= p.tickets_len) {
-    long best = -1;
-    for (int s = 1; s <= 16; ++s) {
-      const int kbps = (a.num_kb + s - 1) / s;
-      if (s > 1 && kbps < 4) break;
-      const long units = (long)tiles * s;
-      if (units > 4L * sms) break;
-      if (s > 1 && units * kBM * bn > p.workspace_floats) break;
-      const long cost = ((units + sms - 1) / sms) * kbps + (s > 1 ? 2 : 0);
-      if (best < 0 || cost < best) {
-        best = cost;
-        splits = s;
-      }
-    }
+  if (p.allow_split && p.workspace && p.tickets && tiles < sms && tiles <= p.tickets_len) {
+    splits = sms / tiles;
+    if (splits > a.num_kb / 4) splits = a.num_kb / 4 > 0 ? a.num_kb / 4 : 1;
+    if (splits > 16) splits = 16;
+    if ((long)tiles * splits * kBM * bn > p.workspace_floats) splits = 1;
   }
   a.splits = splits;
   a.kb_per_split = (a.num_kb + splits - 1) / splits;
