@@ -20,6 +20,8 @@
 // (atomic ticket, re-armed afterwards) merges them and applies the gate.  Only
 // the CTA whose range holds `pos` touches cache row `pos`: it writes the new
 // row and substitutes it into its smem tile, so no CTA reads a row being written.
+#include <exception>
+
 #include "common/host.h"
 #include "common/sm100.cuh"
 #include "kernels/launch.h"
@@ -367,4 +369,116 @@ void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
   }
 }
 
+
+// ===========================================================================
+// Allocation-free entry point (C ABI).  This has no counterpart in the
+// reference; it exists for callers that cannot allocate device memory: host
+// runtimes that reserve all GPU memory for their own pool at start-up
+// (serving engines, embedded runtimes), plugin interfaces whose contract
+// forbids allocation after initialisation, and latency-critical paths that
+// must not risk the implicit device synchronisation of cudaMalloc/cudaFree.
+// Such a caller passes every input and output; the split-KV partials and the
+// merge tickets live in the fixed-size device array below instead.
+//
+// Limits and sharing rules:
+//  * kNoAllocScratchFloats (1 Mi floats = 4 MiB) holds the partials,
+//    batch * q_heads * splits * (2 + 256) floats; kNoAllocTickets (4096)
+//    bounds batch * kv_heads.  The split count is lowered to fit; a problem
+//    that does not fit even with one split is rejected (return code 2).
+//  * The array exists once per GPU that loads this library and is held until
+//    the process exits.  Every call on a device shares it and it keeps the last
+//    call's contents; the tickets that must start at zero are cleared at the
+//    start of every call.  Calls that overlap on the GPU (different streams,
+//    no ordering between them) race on the array and give wrong results.
+//  * The first call on a device, with that device current, resolves the
+//    array's device address with cudaGetSymbolAddress (host code cannot use
+//    the symbol itself as a device pointer).  Make that first call before any
+//    stream capture that includes this entry point.
+// Return codes: 0 ok, 1 bad argument, 2 scratch too small, 3 CUDA error
+// (symbol lookup, memset or launch), 4 internal error.
+// ===========================================================================
+namespace {
+constexpr long kNoAllocScratchFloats = 1L << 20;
+constexpr int kNoAllocTickets = 4096;
+constexpr int kNoAllocMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+static __device__ __align__(256) int g_noalloc_tickets[kNoAllocTickets];
+static __device__ __align__(256) int g_noalloc_status[64];
+
+static float* g_noalloc_partials_ptr[kNoAllocMaxDevices] = {nullptr};
+static int* g_noalloc_tickets_ptr[kNoAllocMaxDevices] = {nullptr};
+static int* g_noalloc_status_ptr[kNoAllocMaxDevices] = {nullptr};
+
 }  // namespace bwn
+
+extern "C" int bwn_gqa_decode_noalloc(const void* qg, long qg_stride, const void* k_new, const void* v_new,
+                                      long kv_new_stride, const float* q_norm_w, const float* k_norm_w,
+                                      const float* cos, const float* sin, void* k_cache, void* v_cache,
+                                      const int* positions, void* out, long out_stride, int batch, int q_heads,
+                                      int kv_heads, int s_max, int rope_dim, float eps, int splits,
+                                      cudaStream_t stream) {
+  using namespace bwn;
+  if (!qg || !k_new || !v_new || !q_norm_w || !k_norm_w || !cos || !sin || !k_cache || !v_cache || !positions ||
+      !out || batch <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || s_max <= 0 ||
+      rope_dim <= 0 || rope_dim > 256 || (rope_dim & 1))
+    return 1;
+  const int G = q_heads / kv_heads;
+  if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8)) return 1;
+  if ((long)batch * kv_heads > kNoAllocTickets) return 2;
+  const long per_split = (long)batch * q_heads * (2 + 256);
+  if (per_split > kNoAllocScratchFloats) return 2;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return 3;
+  if (!g_noalloc_partials_ptr[dev]) {  // once per device, with that device current
+    void* p0 = nullptr;
+    void* p1 = nullptr;
+    void* p2 = nullptr;
+    if (cudaGetSymbolAddress(&p0, g_noalloc_partials) != cudaSuccess) return 3;
+    if (cudaGetSymbolAddress(&p1, g_noalloc_tickets) != cudaSuccess) return 3;
+    if (cudaGetSymbolAddress(&p2, g_noalloc_status) != cudaSuccess) return 3;
+    g_noalloc_tickets_ptr[dev] = static_cast<int*>(p1);
+    g_noalloc_status_ptr[dev] = static_cast<int*>(p2);
+    g_noalloc_partials_ptr[dev] = static_cast<float*>(p0);
+  }
+  if (splits <= 0) splits = 8;
+  const long max_splits = kNoAllocScratchFloats / per_split;
+  if (splits > max_splits) splits = (int)max_splits;
+  if (splits > (s_max + 63) / 64) splits = (s_max + 63) / 64;
+  if (splits < 1) splits = 1;
+  // tickets must start at zero (a call that gave up a bounded wait may leave them set)
+  if (cudaMemsetAsync(g_noalloc_tickets_ptr[dev], 0, sizeof(int) * (size_t)batch * kv_heads, stream) != cudaSuccess)
+    return 3;
+  GqaDecodeArgs p{};
+  p.qg = static_cast<const __nv_bfloat16*>(qg);
+  p.qg_stride = qg_stride;
+  p.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  p.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  p.kv_new_stride = kv_new_stride;
+  p.q_norm_w = q_norm_w;
+  p.k_norm_w = k_norm_w;
+  p.cos = cos;
+  p.sin = sin;
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  p.positions = positions;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = out_stride;
+  p.workspace = g_noalloc_partials_ptr[dev];
+  p.tickets = g_noalloc_tickets_ptr[dev];
+  p.status = g_noalloc_status_ptr[dev];
+  p.batch = batch;
+  p.q_heads = q_heads;
+  p.kv_heads = kv_heads;
+  p.s_max = s_max;
+  p.rope_dim = rope_dim;
+  p.splits = splits;
+  p.eps = eps;
+  try {
+    gqa_decode(p, stream);
+  } catch (const std::exception&) {
+    return cudaPeekAtLastError() != cudaSuccess ? 3 : 4;
+  }
+  return 0;
+}
