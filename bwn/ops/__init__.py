@@ -67,6 +67,23 @@ def linear_residual(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor) -> to
     return (x.float() @ w.float().t() + resid.float()).to(x.dtype)
 
 
+def linear_kn(x: torch.Tensor, w_kn: torch.Tensor) -> torch.Tensor:
+    """``x @ w`` with ``w`` stored ``[K, N]`` (MN-major B operand); used for
+    input gradients ``dX = dY @ W``."""
+    if x.is_cuda:
+        return ops().linear_kn(x, w_kn)
+    return (x.float() @ w_kn.float()).to(x.dtype)
+
+
+def matmul_tn(a_km: torch.Tensor, b_kn: torch.Tensor, f32_out: bool = False) -> torch.Tensor:
+    """``a.T @ b`` for ``a [K, M]``, ``b [K, N]`` (both MN-major); used for weight
+    gradients ``dW = dY.T @ X``."""
+    if a_km.is_cuda:
+        return ops().matmul_tn(a_km, b_kn, f32_out)
+    y = a_km.float().t() @ b_kn.float()
+    return y if f32_out else y.to(a_km.dtype)
+
+
 # --------------------------------------------------------------------------
 # norms / embedding / greedy
 # --------------------------------------------------------------------------

@@ -291,11 +291,12 @@ def deltanet_prefill(
         beta = beta * live[:, None]
     o, st = chunk_gated_delta_rule(q, k, v, g, beta, state, chunk)
     state.copy_(st.to(state.dtype))
-    # conv ring: store the last (ks-1) *valid* rows of each sequence + this row set
+    # conv ring: store the last (ks-1) valid rows of each sequence (the only
+    # history the next decode step reads)
     ks = conv_w.shape[1]
     for bi in range(B):
         n = S if valid_len is None else int(valid_len[bi])
-        for t in range(max(0, n - ks), n):
+        for t in range(max(0, n - (ks - 1)), n):
             conv_ring[bi, (start_pos + t) % ks] = qkv[bi, t].to(conv_ring.dtype)
     o = o.transpose(1, 2)  # [B, S, VH, Dv]
     out = rms_norm_gated(o, z.reshape(B, S, VH, v_dim), norm_w, eps)

@@ -65,6 +65,8 @@ struct GemmProblem {
   void* out = nullptr;
   long ldo = 0;
   bool trans_out = false;  // store D^T (out[n, m]); used for swap-AB decode GEMMs
+  bool a_mn = false;       // A stored [K, M] (MN-major) instead of [M, K]
+  bool b_mn = false;       // B stored [K, N] (MN-major) instead of [N, K]
   int epi = kEpiBF16;
   const __nv_bfloat16* resid = nullptr;
   long ldr = 0;

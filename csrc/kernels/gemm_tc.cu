@@ -136,7 +136,8 @@ __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, const float (
   }
 }
 
-template <int BN, int EPI, bool TRANS>
+// MAJ bit 0: A is MN-major (stored [K, M]); bit 1: B is MN-major (stored [K, N]).
+template <int BN, int EPI, bool TRANS, int MAJ>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmArgs args) {
@@ -183,7 +184,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int tiles = args.tiles_m * args.tiles_n;
   const int units = tiles * args.splits;
-  const uint32_t idesc = idesc_bf16_f32(kBM, BN);
+  constexpr bool A_MN = (MAJ & 1) != 0, B_MN = (MAJ & 2) != 0;
+  const uint32_t idesc = idesc_bf16_f32_major(kBM, BN, A_MN, B_MN);
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -205,8 +207,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full_bar[s], C::kStageBytes);
-          tma_load_2d_hint(&tmA, &full_bar[s], sA + s * C::kABytes, kb * kBK, tm * kBM, polA);
-          tma_load_2d_hint(&tmB, &full_bar[s], sB + s * C::kBBytes, kb * kBK, tn * BN, polB);
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j)
+              tma_load_2d_hint(&tmA, &full_bar[s], sA + s * C::kABytes + j * 8192, tm * kBM + j * 64, kb * kBK, polA);
+          } else {
+            tma_load_2d_hint(&tmA, &full_bar[s], sA + s * C::kABytes, kb * kBK, tm * kBM, polA);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d_hint(&tmB, &full_bar[s], sB + s * C::kBBytes + j * 8192, tn * BN + j * 64, kb * kBK, polB);
+          } else {
+            tma_load_2d_hint(&tmB, &full_bar[s], sB + s * C::kBBytes, kb * kBK, tn * BN, polB);
+          }
           issued_mask |= 1u << s;
           issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
           if (++s == S) {
@@ -247,12 +261,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t da = smem_desc_sw128(smem_u32(sA + s * C::kABytes));
-          const uint64_t db = smem_desc_sw128(smem_u32(sB + s * C::kBBytes));
+          const uint64_t da = A_MN ? smem_desc_sw128_mn(smem_u32(sA + s * C::kABytes), 8192)
+                                   : smem_desc_sw128(smem_u32(sA + s * C::kABytes));
+          const uint64_t db = B_MN ? smem_desc_sw128_mn(smem_u32(sB + s * C::kBBytes), 8192)
+                                   : smem_desc_sw128(smem_u32(sB + s * C::kBBytes));
+          // K step of 16: K-major +32 bytes (encoded +2); MN-major +16 rows x 128 B (encoded +128)
+          constexpr uint64_t kStepA = A_MN ? 128 : 2, kStepB = B_MN ? 128 : 2;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            // +32 bytes per K step of 16 bf16 -> +2 in the encoded start address
-            umma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            umma_f16(d, da + kStepA * kk, db + kStepB * kk, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);
           if (++s == S) {
@@ -369,11 +386,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------
 // host launcher
 // ---------------------------------------------------------------------------
-template <int BN, int EPI, bool TRANS>
+template <int BN, int EPI, bool TRANS, int MAJ>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
                         cudaStream_t stream) {
   using C = GemmCfg<BN>;
-  auto k = gemm_bf16_tc_kernel<BN, EPI, TRANS>;
+  auto k = gemm_bf16_tc_kernel<BN, EPI, TRANS, MAJ>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -389,12 +406,23 @@ template <int EPI, bool TRANS>
 static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
                         cudaStream_t st) {
   switch (bn) {
-    case 16: launch_gemm<16, EPI, TRANS>(ta, tb, a, grid, st); break;
-    case 32: launch_gemm<32, EPI, TRANS>(ta, tb, a, grid, st); break;
-    case 64: launch_gemm<64, EPI, TRANS>(ta, tb, a, grid, st); break;
-    case 128: launch_gemm<128, EPI, TRANS>(ta, tb, a, grid, st); break;
-    case 256: launch_gemm<256, EPI, TRANS>(ta, tb, a, grid, st); break;
+    case 16: launch_gemm<16, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
+    case 32: launch_gemm<32, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
+    case 64: launch_gemm<64, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
+    case 128: launch_gemm<128, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
+    case 256: launch_gemm<256, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
     default: BWN_FAIL("gemm: unsupported BN %d", bn);
+  }
+}
+
+template <int EPI, int MAJ>
+static void dispatch_mn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
+                        cudaStream_t st) {
+  switch (bn) {
+    case 64: launch_gemm<64, EPI, false, MAJ>(ta, tb, a, grid, st); break;
+    case 128: launch_gemm<128, EPI, false, MAJ>(ta, tb, a, grid, st); break;
+    case 256: launch_gemm<256, EPI, false, MAJ>(ta, tb, a, grid, st); break;
+    default: BWN_FAIL("gemm: MN-major operands need BN in {64,128,256}, got %d", bn);
   }
 }
 
@@ -411,10 +439,18 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   BWN_CHECK(p.lda % 8 == 0 && p.ldb % 8 == 0, "gemm: lda/ldb must be multiples of 8");
   BWN_CHECK((reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.B) & 15) == 0,
             "gemm: A/B must be 16-byte aligned");
-  const int bn = p.bn > 0 ? p.bn : gemm_pick_bn(p.N);
+  const int maj = (p.a_mn ? 1 : 0) | (p.b_mn ? 2 : 0);
+  int bn = p.bn > 0 ? p.bn : gemm_pick_bn(p.N);
+  if (maj && bn < 64) bn = 64;
   CUtensorMap ta, tb;
-  make_tmap_2d_bf16(&ta, p.A, p.M, p.K, p.lda, kBM, kBK);
-  make_tmap_2d_bf16(&tb, p.B, p.N, p.K, p.ldb, bn, kBK);
+  if (p.a_mn)
+    make_tmap_2d_bf16(&ta, p.A, p.K, p.M, p.lda, kBK, 64);  // stored [K, M]
+  else
+    make_tmap_2d_bf16(&ta, p.A, p.M, p.K, p.lda, kBM, kBK);
+  if (p.b_mn)
+    make_tmap_2d_bf16(&tb, p.B, p.K, p.N, p.ldb, kBK, 64);  // stored [K, N]
+  else
+    make_tmap_2d_bf16(&tb, p.B, p.N, p.K, p.ldb, bn, kBK);
   GemmArgs a{};
   a.M = p.M;
   a.N = p.N;
@@ -448,6 +484,16 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   const int units = tiles * a.splits;
   const int grid = units < sms ? units : sms;
   const bool tr = p.trans_out;
+  if (maj) {
+    BWN_CHECK(!tr && (p.epi == kEpiBF16 || p.epi == kEpiF32), "gemm: MN-major operands support bf16/f32 epilogues");
+    const bool f32 = p.epi == kEpiF32;
+    switch (maj) {
+      case 1: f32 ? dispatch_mn<kEpiF32, 1>(bn, ta, tb, a, grid, stream) : dispatch_mn<kEpiBF16, 1>(bn, ta, tb, a, grid, stream); break;
+      case 2: f32 ? dispatch_mn<kEpiF32, 2>(bn, ta, tb, a, grid, stream) : dispatch_mn<kEpiBF16, 2>(bn, ta, tb, a, grid, stream); break;
+      default: f32 ? dispatch_mn<kEpiF32, 3>(bn, ta, tb, a, grid, stream) : dispatch_mn<kEpiBF16, 3>(bn, ta, tb, a, grid, stream); break;
+    }
+    return;
+  }
   switch (p.epi) {
     case kEpiBF16:
       tr ? dispatch_bn<kEpiBF16, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiBF16, false>(bn, ta, tb, a, grid, stream);

@@ -1,0 +1,58 @@
+// Launch descriptors for the prefill kernels (csrc/kernels/prefill.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace bwn {
+
+struct GqaPrefillArgs {
+  const __nv_bfloat16* qg;   // [B, S, QH, 512] rows of stride qg_row (query || gate per head)
+  long qg_row;
+  const __nv_bfloat16* k;    // [B, S, KVH, 256] rows of stride kv_row
+  const __nv_bfloat16* v;
+  long kv_row;
+  const float* q_norm_w;
+  const float* k_norm_w;
+  const float* cos;          // [S_max, rope_dim]
+  const float* sin;
+  __nv_bfloat16* k_cache;    // [B, KVH, s_max, 256]
+  __nv_bfloat16* v_cache;
+  __nv_bfloat16* q_rot;      // scratch [B, QH, S_pad, 256]
+  __nv_bfloat16* out;        // [B, S, QH*256] rows of stride out_row
+  long out_row;
+  int* status;
+  int batch, S, S_pad, start, q_heads, kv_heads, s_max, rope_dim;
+  float eps, scale;
+};
+void gqa_prefill(const GqaPrefillArgs& p, cudaStream_t stream);
+
+struct DnPrefillArgs {
+  const __nv_bfloat16* qkv;  // [B, S, C] rows of stride qkv_row
+  long qkv_row;
+  const __nv_bfloat16* z;    // [B, S, VH*128] rows of stride z_row
+  long z_row;
+  const __nv_bfloat16* a;    // [B, S, VH] rows of stride ab_row
+  const __nv_bfloat16* b;
+  long ab_row;
+  __nv_bfloat16* conv_ring;  // [B, 4, C]
+  void* state;               // [B, VH, 128, 128]
+  bool state_bf16;
+  const int* valid_len;      // [B]
+  const float* conv_w;       // [C, 4]
+  const float* A_log;
+  const float* dt_bias;
+  const float* norm_w;       // [128]
+  // scratch
+  __nv_bfloat16* q_out;      // [B, KH, S_pad, 128]
+  __nv_bfloat16* k_out;
+  __nv_bfloat16* v_out;      // [B, VH, S_pad, 128]
+  float* g_out;              // [B, VH, S_pad]
+  float* beta_out;
+  __nv_bfloat16* out;        // [B, S, VH*128] rows of stride out_row
+  long out_row;
+  int batch, S, S_pad, start, k_heads, v_heads;
+  float l2_eps, norm_eps;
+};
+void deltanet_prefill(const DnPrefillArgs& p, cudaStream_t stream);
+
+}  // namespace bwn

@@ -136,6 +136,72 @@ void linear_into(const Tensor& x, const Tensor& w, const Tensor& out, int64_t ep
   gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
 }
 
+// General (non-swapped) GEMM with optional MN-major operands:
+//   a_mn=false: A is [M, K]; a_mn=true: A is stored [K, M]
+//   b_mn=false: B is [N, K]; b_mn=true: B is stored [K, N]
+// out[M, N] (bf16 or fp32 by out's dtype).
+void gemm_into(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const Tensor& out) {
+  check_bf16(A, "A");
+  check_bf16(B, "B");
+  check_rowmajor(A, "A");
+  check_rowmajor(B, "B");
+  check_rowmajor(out, "out");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int M = (int)(a_mn ? A.size(1) : A.size(0));
+  const int K = (int)(a_mn ? A.size(0) : A.size(1));
+  const int N = (int)(b_mn ? B.size(1) : B.size(0));
+  const int Kb = (int)(b_mn ? B.size(0) : B.size(1));
+  TORCH_CHECK(K == Kb, "bwn.gemm: K mismatch");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "bwn.gemm: out shape");
+  if (M == 0 || N == 0) return;
+  GemmProblem p;
+  p.A = A.data_ptr();
+  p.lda = A.stride(0);
+  p.B = B.data_ptr();
+  p.ldb = B.stride(0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.status = status_dev_ptr();
+  if (out.scalar_type() == at::kFloat) {
+    p.epi = kEpiF32;
+  } else {
+    check_bf16(out, "out");
+    p.epi = kEpiBF16;
+  }
+  int bn = gemm_pick_bn(N);
+  if ((a_mn || b_mn) && bn < 64) bn = 64;
+  p.bn = bn;
+  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int sms = num_sms();
+  if (tiles < 2 * sms) {
+    Scratch& s = scratch_for(A, 4L * sms * 128 * bn, 2 * sms);
+    p.workspace = s.ws.data_ptr<float>();
+    p.workspace_floats = s.ws.numel();
+    p.tickets = s.tickets.data_ptr<int>();
+    p.tickets_len = (int)s.tickets.numel();
+  } else {
+    p.allow_split = false;
+  }
+  gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
+}
+
+Tensor linear_kn(const Tensor& x, const Tensor& w_kn) {
+  auto out = at::empty({x.size(0), w_kn.size(1)}, x.options());
+  gemm_into(x, false, w_kn, true, out);
+  return out;
+}
+
+Tensor matmul_tn(const Tensor& a_km, const Tensor& b_kn, bool f32_out) {
+  auto out = at::empty({a_km.size(1), b_kn.size(1)}, a_km.options().dtype(f32_out ? at::kFloat : at::kBFloat16));
+  gemm_into(a_km, true, b_kn, true, out);
+  return out;
+}
+
 Tensor linear(const Tensor& x, const Tensor& w) {
   auto out = at::empty({x.size(0), w.size(0)}, x.options());
   linear_into(x, w, out, kEpiBF16, c10::nullopt);
@@ -354,6 +420,8 @@ TORCH_LIBRARY(bwn, m) {
   m.def("linear_swiglu(Tensor x, Tensor w_il) -> Tensor");
   m.def("linear_residual(Tensor x, Tensor w, Tensor resid) -> Tensor");
   m.def("linear_out(Tensor x, Tensor w, Tensor(a!) out, int epi, Tensor? resid) -> ()");
+  m.def("linear_kn(Tensor x, Tensor w_kn) -> Tensor");
+  m.def("matmul_tn(Tensor a_km, Tensor b_kn, bool f32_out) -> Tensor");
   m.def("rms_norm(Tensor x, Tensor w, float eps, bool one_plus) -> Tensor");
   m.def("add_rms_norm(Tensor x, Tensor(a!) residual, Tensor w, float eps) -> Tensor");
   m.def("embedding(Tensor ids, Tensor table, int offset) -> Tensor");
@@ -374,6 +442,8 @@ TORCH_LIBRARY_IMPL(bwn, CUDA, m) {
   m.impl("linear_swiglu", &bwn::linear_swiglu);
   m.impl("linear_residual", &bwn::linear_residual);
   m.impl("linear_out", &bwn::linear_out);
+  m.impl("linear_kn", &bwn::linear_kn);
+  m.impl("matmul_tn", &bwn::matmul_tn);
   m.impl("rms_norm", &bwn::rms_norm_op);
   m.impl("add_rms_norm", &bwn::add_rms_norm_op);
   m.impl("embedding", &bwn::embedding_op);

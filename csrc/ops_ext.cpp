@@ -1,7 +1,142 @@
+// Prefill op registrations (torch.ops.bwn.deltanet_prefill / gqa_prefill).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common/host.h"
+#include "kernels/prefill.h"
 #include "ops_ext.h"
 
 namespace bwn {
-void register_ext_defs(torch::Library& m) {}
-void register_ext_impls(torch::Library& m) {}
+using at::Tensor;
+
+static inline const __nv_bfloat16* cbf(const Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+static inline __nv_bfloat16* mbf(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+// qkv/z/a/b are [B, S, *] views of one projection output: inner stride 1, a
+// common row stride between tokens (stride(1)), and stride(0) == S*stride(1).
+static long row_stride(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 3 && t.stride(2) == 1, "bwn: ", name, " must be [B, S, *] with inner stride 1");
+  TORCH_CHECK(t.size(0) == 1 || t.stride(0) == t.size(1) * t.stride(1), "bwn: ", name, " rows must be uniform");
+  return t.stride(1);
+}
+
+Tensor deltanet_prefill_op(const Tensor& qkv, const Tensor& z, const Tensor& a, const Tensor& b, Tensor conv_ring,
+                           Tensor state, int64_t start, const Tensor& valid_len, const Tensor& conv_w,
+                           const Tensor& A_log, const Tensor& dt_bias, const Tensor& norm_w, int64_t k_heads,
+                           double eps) {
+  check_bf16(qkv, "qkv");
+  check_bf16(z, "z");
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_bf16(conv_ring, "conv_ring");
+  check_f32(conv_w, "conv_w");
+  TORCH_CHECK(valid_len.scalar_type() == at::kInt && valid_len.is_contiguous(), "valid_len int32");
+  TORCH_CHECK(state.is_contiguous() && state.size(2) == 128 && state.size(3) == 128, "state [B,VH,128,128]");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const int B = (int)qkv.size(0), S = (int)qkv.size(1), VH = (int)state.size(1);
+  const int S_pad = ((S + 63) / 64) * 64;
+  auto opt = qkv.options();
+  auto qn = at::empty({B, k_heads, S_pad, 128}, opt);
+  auto kn = at::empty({B, k_heads, S_pad, 128}, opt);
+  auto vn = at::empty({B, VH, S_pad, 128}, opt);
+  auto g = at::empty({B, VH, S_pad}, opt.dtype(at::kFloat));
+  auto be = at::empty({B, VH, S_pad}, opt.dtype(at::kFloat));
+  auto out = at::empty({B, S, VH * 128}, opt);
+  DnPrefillArgs p{};
+  p.qkv = cbf(qkv);
+  p.qkv_row = row_stride(qkv, "qkv");
+  p.z = cbf(z);
+  p.z_row = row_stride(z, "z");
+  p.a = cbf(a);
+  p.b = cbf(b);
+  p.ab_row = row_stride(a, "a");
+  TORCH_CHECK(row_stride(b, "b") == p.ab_row, "a and b share a row stride");
+  p.conv_ring = mbf(conv_ring);
+  p.state = state.data_ptr();
+  p.state_bf16 = state.scalar_type() == at::kBFloat16;
+  p.valid_len = valid_len.data_ptr<int>();
+  p.conv_w = conv_w.data_ptr<float>();
+  p.A_log = A_log.data_ptr<float>();
+  p.dt_bias = dt_bias.data_ptr<float>();
+  p.norm_w = norm_w.data_ptr<float>();
+  p.q_out = mbf(qn);
+  p.k_out = mbf(kn);
+  p.v_out = mbf(vn);
+  p.g_out = g.data_ptr<float>();
+  p.beta_out = be.data_ptr<float>();
+  p.out = mbf(out);
+  p.out_row = out.stride(1);
+  p.batch = B;
+  p.S = S;
+  p.S_pad = S_pad;
+  p.start = (int)start;
+  p.k_heads = (int)k_heads;
+  p.v_heads = VH;
+  p.l2_eps = 1e-6f;
+  p.norm_eps = (float)eps;
+  if (S > 0) deltanet_prefill(p, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
+Tensor gqa_prefill_op(const Tensor& qg, const Tensor& k, const Tensor& v, const Tensor& q_norm_w,
+                      const Tensor& k_norm_w, const Tensor& cos, const Tensor& sin, Tensor k_cache, Tensor v_cache,
+                      int64_t start, double eps) {
+  check_bf16(qg, "qg");
+  check_bf16(k, "k");
+  check_bf16(v, "v");
+  check_bf16(k_cache, "k_cache");
+  TORCH_CHECK(qg.dim() == 4 && qg.size(3) == 512 && qg.stride(3) == 1 && qg.stride(2) == 512, "qg [B,S,QH,512]");
+  TORCH_CHECK(k.dim() == 4 && k.size(3) == 256 && k.stride(3) == 1 && k.stride(2) == 256, "k [B,S,KVH,256]");
+  TORCH_CHECK(v.stride(1) == k.stride(1) && v.stride(2) == 256, "v shares k's layout");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.size(3) == 256, "caches contiguous");
+  const c10::cuda::CUDAGuard guard(qg.device());
+  const int B = (int)qg.size(0), S = (int)qg.size(1), QH = (int)qg.size(2), KVH = (int)k.size(2);
+  TORCH_CHECK(qg.size(0) == 1 || qg.stride(0) == S * qg.stride(1), "qg rows uniform");
+  TORCH_CHECK(start + S <= k_cache.size(2), "gqa_prefill: chunk exceeds the cache");
+  const int S_pad = ((S + 127) / 128) * 128;
+  auto q_rot = at::empty({B, QH, S_pad, 256}, qg.options());
+  auto out = at::empty({B, S, QH * 256}, qg.options());
+  GqaPrefillArgs p{};
+  p.qg = cbf(qg);
+  p.qg_row = qg.stride(1);
+  p.k = cbf(k);
+  p.v = cbf(v);
+  p.kv_row = k.stride(1);
+  p.q_norm_w = q_norm_w.data_ptr<float>();
+  p.k_norm_w = k_norm_w.data_ptr<float>();
+  p.cos = cos.data_ptr<float>();
+  p.sin = sin.data_ptr<float>();
+  p.k_cache = mbf(k_cache);
+  p.v_cache = mbf(v_cache);
+  p.q_rot = mbf(q_rot);
+  p.out = mbf(out);
+  p.out_row = out.stride(1);
+  p.status = status_dev_ptr();
+  p.batch = B;
+  p.S = S;
+  p.S_pad = S_pad;
+  p.start = (int)start;
+  p.q_heads = QH;
+  p.kv_heads = KVH;
+  p.s_max = (int)k_cache.size(2);
+  p.rope_dim = (int)cos.size(1);
+  p.eps = (float)eps;
+  p.scale = 1.f / 16.f;  // 1/sqrt(256)
+  if (S > 0) gqa_prefill(p, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
+void register_ext_defs(torch::Library& m) {
+  m.def(
+      "deltanet_prefill(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) conv_ring, Tensor(b!) state, int start, "
+      "Tensor valid_len, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, float eps) -> Tensor");
+  m.def(
+      "gqa_prefill(Tensor qg, Tensor k, Tensor v, Tensor q_norm_w, Tensor k_norm_w, Tensor cos, Tensor sin, "
+      "Tensor(a!) k_cache, Tensor(b!) v_cache, int start, float eps) -> Tensor");
+}
+void register_ext_impls(torch::Library& m) {
+  m.impl("deltanet_prefill", &deltanet_prefill_op);
+  m.impl("gqa_prefill", &gqa_prefill_op);
+}
 void register_ext_pybind(pybind11::module& mod) {}
 }  // namespace bwn

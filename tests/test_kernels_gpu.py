@@ -43,6 +43,22 @@ def test_linear(M, N, K):
     assert _rel(y, ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (104, 320, 192), (4096, 2560, 2560), (8, 64, 128)])
+def test_mn_major_gemms(M, N, K):
+    """MN-major B (dX = dY @ W) and MN-major A+B (dW = dY^T @ X) descriptors."""
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w_kn = (torch.randn(K, N, device=dev) / math.sqrt(K)).bfloat16()
+    y = O.linear_kn(x, w_kn)
+    assert _rel(y, x.float() @ w_kn.float()) < 1e-2
+    a = torch.randn(K, M, device=dev).bfloat16()
+    b = torch.randn(K, N, device=dev).bfloat16()
+    for f32 in (False, True):
+        z = O.matmul_tn(a, b, f32)
+        assert z.dtype == (torch.float32 if f32 else torch.bfloat16)
+        assert _rel(z, a.float().t() @ b.float()) < 1e-2
+    O.check_status("mn-major gemm")
+
+
 @pytest.mark.parametrize("M", [1, 32, 200])
 def test_linear_swiglu_and_resid(M):
     K, I = 1024, 512
