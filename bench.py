@@ -71,6 +71,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="bwn", choices=["bwn", "reference"])
+    ap.add_argument("--model", default="27b", choices=["27b", "35b"])
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (result marked invalid)")
@@ -81,7 +82,7 @@ def main() -> None:
         reference_arm(args)
         return
 
-    from bwn.config import QWEN36_27B
+    from bwn.config import QWEN36_27B, QWEN36_35B_A3B
     from bwn.models.qwen36 import Qwen36Model
     from bwn.ops import check_status
     from bwn.parallel.comm import init_distributed
@@ -93,7 +94,8 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    cfg = QWEN36_27B if not args.layers else QWEN36_27B.scaled(num_layers=args.layers)
+    base = QWEN36_27B if args.model == "27b" else QWEN36_35B_A3B
+    cfg = base if not args.layers else base.scaled(num_layers=args.layers)
     B, S = args.batch, args.prompt_len
     max_seq = S + args.warmup + args.steps * 2 + 64
 
@@ -192,7 +194,7 @@ def main() -> None:
                 "model": cfg.name if not args.layers else f"{cfg.name}-{args.layers}L (INVALID: debug layer count)",
                 "global_batch": B,
                 "seq_len": S,
-                "parallelism": f"tp{args.gpus}",
+                "parallelism": f"tp{args.gpus}" + (f"+ep{args.gpus}" if cfg.is_moe else ""),
                 "decode": "CUDA-graph replay, on-device greedy",
                 "l2": "inputs larger than L2 (every step streams %.1f GB of weights per GPU)" % (
                     model.weight_bytes() / 1e9),

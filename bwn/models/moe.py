@@ -26,27 +26,12 @@ def route(model, L, h: torch.Tensor):
     return R.moe_route_softmax(logits, cfg.top_k, cfg.norm_topk_prob)
 
 
-def shared_expert(model, L, h: torch.Tensor) -> torch.Tensor:
-    act = O.linear_swiglu(h, L["shared_gate_up"])
-    y = O.linear(act, L["shared_down"])
-    g = torch.sigmoid(O.linear_f32(h, L["shared_gate"]) if h.is_cuda else h.float() @ L["shared_gate"].float().t())
-    return y, g
-
-
 def qwen_moe_forward(model, L, h: torch.Tensor) -> torch.Tensor:
-    """This rank's partial MoE output ``[T, H]`` (bf16)."""
+    """This rank's partial MoE output ``[T, H]`` (bf16): routed experts held
+    locally plus this rank's tensor-parallel slice of the gated shared expert."""
     d = model.d
     w, ids = route(model, L, h)
-    if h.is_cuda:
-        return O.moe_experts(h, w, ids, L["experts_gate_up"], L["experts_down"], d.expert_offset,
-                             shared=(L["shared_gate_up"], L["shared_down"], L["shared_gate"]))
-    out = R.moe_experts(h, w, ids, L["experts_gate_up_plain"] if "experts_gate_up_plain" in L else
-                        _deinterleave_experts(L["experts_gate_up"]), L["experts_down"], d.expert_offset)
-    y, g = shared_expert(model, L, h)
-    return (out + g * y.float()).to(h.dtype)
-
-
-def _deinterleave_experts(gu_il: torch.Tensor) -> torch.Tensor:
-    E, n2, H = gu_il.shape
-    x = gu_il.reshape(E, n2 // 32, 2, 16, H)
-    return torch.cat([x[:, :, 0].reshape(E, n2 // 2, H), x[:, :, 1].reshape(E, n2 // 2, H)], dim=1)
+    act = O.linear_swiglu(h, L["shared_gate_up"])
+    sy = O.linear(act, L["shared_down"])
+    sg = O.linear_f32(h, L["shared_gate"]) if h.is_cuda else h.float() @ L["shared_gate"].float().t()
+    return O.moe_experts(h, w, ids, L["experts_gate_up"], L["experts_down"], d.expert_offset, shared=(sy, sg))

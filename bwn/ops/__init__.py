@@ -195,3 +195,39 @@ def gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_
 def _prefill_cuda():
     from . import prefill_cuda
     return prefill_cuda
+
+
+# --------------------------------------------------------------------------
+# MoE
+# --------------------------------------------------------------------------
+def moe_topk_softmax(logits: torch.Tensor, k: int, renorm: bool = True):
+    """softmax -> top-k -> (renormalise); returns ``(w [T,k] fp32, ids [T,k] int32)``."""
+    if logits.is_cuda:
+        return ops().moe_topk(logits.float().contiguous(), k, renorm, None, 0, 1.0)
+    return ref.moe_route_softmax(logits, k, renorm)
+
+
+def moe_topk_deepseek(logits: torch.Tensor, bias, k: int, score_func: str = "sqrtsoftplus",
+                      route_scale: float = 1.5):
+    if logits.is_cuda:
+        mode = 1 if score_func == "sqrtsoftplus" else 2
+        b = bias.float().contiguous() if bias is not None else None
+        return ops().moe_topk(logits.float().contiguous(), k, True, b, mode, route_scale)
+    return ref.moe_route_deepseek(logits, bias, k, score_func, route_scale)
+
+
+def moe_experts(x, w, ids, gate_up_il, down, expert_offset: int = 0, shared=None):
+    """This rank's routed-expert partial (plus, when ``shared=(y, gate_logit)``
+    is given, ``sigmoid(gate_logit) * y``)."""
+    if x.is_cuda:
+        sy, sg = (shared if shared is not None else (None, None))
+        return ops().moe_experts(x, w.float().contiguous(), ids.int().contiguous(), gate_up_il, down, expert_offset,
+                                 sy, sg.float().reshape(-1).contiguous() if sg is not None else None)
+    E, n2, H = gate_up_il.shape
+    xg = gate_up_il.reshape(E, n2 // 32, 2, 16, H)
+    gu = torch.cat([xg[:, :, 0].reshape(E, n2 // 2, H), xg[:, :, 1].reshape(E, n2 // 2, H)], dim=1)
+    out = ref.moe_experts(x, w, ids, gu, down, expert_offset)
+    if shared is not None:
+        sy, sg = shared
+        out = out + torch.sigmoid(sg.float().reshape(-1, 1)) * sy.float()
+    return out.to(x.dtype)

@@ -2,7 +2,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <tuple>
+
 #include "common/host.h"
+#include "kernels/moe.h"
 #include "kernels/prefill.h"
 #include "ops_ext.h"
 
@@ -126,7 +129,119 @@ Tensor gqa_prefill_op(const Tensor& qg, const Tensor& k, const Tensor& v, const 
   return out;
 }
 
+// ---------------------------------------------------------------------------
+// MoE
+// ---------------------------------------------------------------------------
+std::tuple<Tensor, Tensor> moe_topk_op(const Tensor& logits, int64_t k, bool renorm, const c10::optional<Tensor>& bias,
+                                       int64_t mode, double route_scale) {
+  check_f32(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.is_contiguous(), "logits [T, E] contiguous");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int T = (int)logits.size(0), E = (int)logits.size(1);
+  auto w = at::empty({T, k}, logits.options());
+  auto ids = at::empty({T, k}, logits.options().dtype(at::kInt));
+  MoeTopkArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.bias = bias.has_value() ? bias->data_ptr<float>() : nullptr;
+  a.T = T;
+  a.E = E;
+  a.k = (int)k;
+  a.renorm = renorm;
+  a.deepseek = mode != 0;
+  a.sqrt_softplus = mode == 1;
+  a.route_scale = (float)route_scale;
+  a.w = w.data_ptr<float>();
+  a.ids = ids.data_ptr<int>();
+  moe_topk(a, at::cuda::getCurrentCUDAStream().stream());
+  return {w, ids};
+}
+
+// Routed experts of this rank: pack -> grouped gate/up (SwiGLU) -> grouped down
+// -> weighted combine (+ gated shared expert).  Returns this rank's partial [T, H].
+Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const Tensor& gate_up, const Tensor& down,
+                      int64_t e0, const c10::optional<Tensor>& shared_y, const c10::optional<Tensor>& shared_gate) {
+  check_bf16(x, "x");
+  check_bf16(gate_up, "gate_up");
+  check_bf16(down, "down");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, H]");
+  TORCH_CHECK(gate_up.is_contiguous() && down.is_contiguous(), "expert weights contiguous");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0), H = (int)x.size(1), k = (int)ids.size(1);
+  const int El = (int)gate_up.size(0), I2 = (int)gate_up.size(1), I = I2 / 2;
+  TORCH_CHECK(down.size(0) == El && down.size(1) == H && down.size(2) == I, "down [E, H, I]");
+  auto opt = x.options();
+  auto iopt = opt.dtype(at::kInt);
+  const int n = T * k;
+  auto counts = at::empty({El}, iopt);
+  auto offsets = at::empty({El + 1}, iopt);
+  auto pos_of = at::empty({n}, iopt);
+  auto row_src = at::empty({std::max(n, 1)}, iopt);
+  auto xp = at::empty({std::max(n, 1), H}, opt);
+  auto y1 = at::empty({std::max(n, 1), I}, opt);
+  auto y2 = at::empty({std::max(n, 1), H}, opt);
+  auto out = at::empty({T, H}, opt);
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  MoeRouteArgs r{};
+  r.ids = ids.data_ptr<int>();
+  r.T = T;
+  r.k = k;
+  r.e0 = (int)e0;
+  r.E_local = El;
+  r.counts = counts.data_ptr<int>();
+  r.offsets = offsets.data_ptr<int>();
+  r.pos_of = pos_of.data_ptr<int>();
+  r.row_src = row_src.data_ptr<int>();
+  r.x = cbf(x);
+  r.ldx = x.stride(0);
+  r.H = H;
+  r.x_perm = mbf(xp);
+  moe_route(r, st);
+  GroupedProblem g{};
+  g.W = gate_up.data_ptr();
+  g.X = xp.data_ptr();
+  g.rows_total = n;
+  g.counts = r.counts;
+  g.offsets = r.offsets;
+  g.groups = El;
+  g.N = I2;
+  g.K = H;
+  g.max_rows_per_group = T;
+  g.swiglu = true;
+  g.out = mbf(y1);
+  g.ldo = I;
+  g.status = status_dev_ptr();
+  grouped_gemm(g, st);
+  g.W = down.data_ptr();
+  g.X = y1.data_ptr();
+  g.N = H;
+  g.K = I;
+  g.swiglu = false;
+  g.out = mbf(y2);
+  g.ldo = H;
+  grouped_gemm(g, st);
+  MoeCombineArgs c{};
+  c.y = cbf(y2);
+  c.w = w.data_ptr<float>();
+  c.pos_of = r.pos_of;
+  c.T = T;
+  c.k = k;
+  c.H = H;
+  if (shared_y.has_value()) {
+    c.shared_y = cbf(*shared_y);
+    c.ld_shared = shared_y->stride(0);
+    c.shared_gate = shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr;
+  }
+  c.out = mbf(out);
+  c.ldo = out.stride(0);
+  moe_combine(c, st);
+  return out;
+}
+
 void register_ext_defs(torch::Library& m) {
+  m.def("moe_topk(Tensor logits, int k, bool renorm, Tensor? bias, int mode, float route_scale) -> (Tensor, Tensor)");
+  m.def(
+      "moe_experts(Tensor x, Tensor w, Tensor ids, Tensor gate_up, Tensor down, int e0, Tensor? shared_y, "
+      "Tensor? shared_gate) -> Tensor");
   m.def(
       "deltanet_prefill(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) conv_ring, Tensor(b!) state, int start, "
       "Tensor valid_len, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, float eps) -> Tensor");
@@ -135,6 +250,8 @@ void register_ext_defs(torch::Library& m) {
       "Tensor(a!) k_cache, Tensor(b!) v_cache, int start, float eps) -> Tensor");
 }
 void register_ext_impls(torch::Library& m) {
+  m.impl("moe_topk", &moe_topk_op);
+  m.impl("moe_experts", &moe_experts_op);
   m.impl("deltanet_prefill", &deltanet_prefill_op);
   m.impl("gqa_prefill", &gqa_prefill_op);
 }
