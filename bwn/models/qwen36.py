@@ -133,6 +133,9 @@ class Qwen36Model(nn.Module):
     # ---------------------------------------------------------------- decode
     def _reduce_add_norm(self, part: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """``x += all_reduce(part)``; return ``rmsnorm(x) * (1+w)``."""
+        fc = self.fused_comm
+        if fc is not None and fc.fits(part.shape[0]):
+            return fc.allreduce_add_norm(part, x, w, self.cfg.rms_eps)
         if self.tp > 1:
             self.comm.all_reduce_(part)
         return O.add_rms_norm(part, x, w, self.cfg.rms_eps)
@@ -140,8 +143,9 @@ class Qwen36Model(nn.Module):
     def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
         """Row-parallel projection + all-reduce + residual add + RMSNorm.  With the
         fused NVLink path this is one kernel (GEMM epilogue -> peer reduce)."""
-        if self.fused_comm is not None:
-            return self.fused_comm.gemm_allreduce_add_norm(a, w, x, norm_w, self.cfg.rms_eps)
+        fc = self.fused_comm
+        if fc is not None and fc.fits(a.shape[0]):
+            return fc.gemm_allreduce_add_norm(a, w, x, norm_w, self.cfg.rms_eps)
         return self._reduce_add_norm(O.linear(a, w), x, norm_w)
 
     def _deltanet_decode(self, i: int, h: torch.Tensor, st: Qwen36State, di: int) -> torch.Tensor:
@@ -204,6 +208,9 @@ class Qwen36Model(nn.Module):
         (``static_decode_35b.py:1534-1564``) as a single int64 max all-reduce."""
         logits = O.linear(h, self.g["lm_head"])
         key = O.argmax_packed(logits, self.d.vocab_offset)
+        fc = self.fused_comm
+        if fc is not None and fc.fits(key.shape[0]):
+            return fc.greedy(key)
         if self.tp > 1:
             self.comm.all_reduce_max_(key)
         return O.unpack_argmax(key)

@@ -1,0 +1,97 @@
+"""Fused compute + collective paths over NVLink 5 / NVSwitch.
+
+* Row-parallel GEMM -> all-reduce -> residual add -> RMSNorm (the reference's
+  ``o_proj/out_proj/down_proj`` + ``functional_all_reduce`` + next norm,
+  ``contrib/qwen3.6-27b/static_decode.py:798-961``): the tcgen05 GEMM epilogue
+  reduces fp32 partial tiles into an NVLS multicast buffer with
+  ``multimem.red`` (the switch adds every rank's contribution into every
+  rank's copy), the last CTA publishes an epoch flag to all ranks, and one small
+  kernel per rank waits for the flags, adds the residual and normalises.
+* Sharded greedy (``static_decode_35b.py:1534-1564``): packed (logit, id) keys
+  exchanged by peer stores, max taken on every rank, one launch.
+
+Buffers are symmetric allocations (``torch.distributed._symmetric_memory`` is
+used only to map them: peer pointers and the multicast address); all device
+code is in ``csrc/comm/fused_ar.cu`` and ``csrc/kernels/gemm_tc.cu``.  Every
+device-side wait is bounded (``timeout_s``) and reports through the status
+word instead of hanging.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import ops
+
+
+class FusedComm:
+    FLAGS_AR = 0
+    FLAGS_GREEDY = 128
+    SLOTS = 256
+
+    def __init__(self, comm, hidden: int, max_rows: int = 256, device=None, timeout_s: float = 5.0):
+        import torch.distributed._symmetric_memory as symm
+
+        self.comm = comm
+        self.world, self.rank = comm.size, comm.rank
+        self.hidden = hidden
+        self.max_rows = max_rows
+        self.timeout_s = timeout_s
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        group = comm.group or dist.group.WORLD
+        try:  # older torch releases want symmetric memory enabled per group first
+            symm.enable_symm_mem_for_group(group.group_name)
+        except Exception:  # noqa: BLE001
+            pass
+        slots_bytes = 8 * max_rows * 8
+        self.ar_off = ((self.SLOTS + slots_bytes + 255) // 256) * 256
+        self.buf_floats = max_rows * hidden
+        total = self.ar_off + 2 * self.buf_floats * 4
+        self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        torch.cuda.synchronize(dev)
+        self.hdl = symm.rendezvous(self.buf, group)
+        if not self.hdl.has_multicast_support:
+            raise RuntimeError("NVLS multicast is not available on this system")
+        ptrs = [int(p) for p in self.hdl.buffer_ptrs]
+        mc = int(self.hdl.multicast_ptr)
+        self.peer_flags_ar = [p + self.FLAGS_AR for p in ptrs]
+        self.peer_flags_g = [p + self.FLAGS_GREEDY for p in ptrs]
+        self.peer_slots = [p + self.SLOTS for p in ptrs]
+        self.mc_ar = mc + self.ar_off
+        self.local_ar = ptrs[self.rank] + self.ar_off
+        self.state = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.hdl.barrier()
+        torch.cuda.synchronize(dev)
+
+    def fits(self, rows: int) -> bool:
+        return rows <= self.max_rows
+
+    def gemm_allreduce_add_norm(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor, norm_w: torch.Tensor,
+                                eps: float) -> torch.Tensor:
+        """``x += all_reduce(a @ w.T)`` across ranks; returns ``rmsnorm(x)*(1+norm_w)``."""
+        o = ops()
+        o.gemm_mcred(a, w, self.mc_ar, self.buf_floats, w.shape[0], self.peer_flags_ar, self.state, self.rank)
+        return o.ar_add_norm(self.local_ar, self.buf_floats, self.peer_flags_ar[self.rank], self.world, self.state,
+                             x, norm_w, eps, self.timeout_s)
+
+    def allreduce_add_norm(self, part: torch.Tensor, x: torch.Tensor, norm_w: torch.Tensor,
+                           eps: float) -> torch.Tensor:
+        o = ops()
+        o.mc_red_signal(part, self.mc_ar, self.buf_floats, self.peer_flags_ar, self.state, self.rank)
+        return o.ar_add_norm(self.local_ar, self.buf_floats, self.peer_flags_ar[self.rank], self.world, self.state,
+                             x, norm_w, eps, self.timeout_s)
+
+    def greedy(self, keys: torch.Tensor) -> torch.Tensor:
+        return ops().greedy_allmax(keys.contiguous(), self.peer_slots, self.peer_flags_g,
+                                   self.peer_flags_g[self.rank], self.state, self.rank, self.timeout_s)
+
+
+def enable_fused_comm(model, max_rows: int = 256) -> FusedComm:
+    """Route the model's row-parallel reductions and greedy through the fused
+    NVLink kernels (decode-sized batches); larger batches keep NCCL."""
+    if model.comm.size <= 1:
+        raise RuntimeError("fused comm needs more than one rank")
+    fc = FusedComm(model.comm, model.cfg.hidden, max_rows, model.device)
+    model.fused_comm = fc
+    return fc

@@ -1,0 +1,47 @@
+// Host entry points of the fused NVLink collective kernels (csrc/comm/fused_ar.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common/host.h"
+
+namespace bwn {
+
+void mc_red_signal(const __nv_bfloat16* x, long ldx, int rows, int cols, float* mc_base, const CommSignal& sig,
+                   cudaStream_t st);
+
+struct ArNormArgs {
+  float* local_base;       // this rank's unicast view of the two fp32 reduce buffers
+  long buf_stride;
+  int* sel;                // [2]: selector, CTA ticket
+  const unsigned* flags;   // this rank's flag array (slot r written by rank r)
+  int world;
+  const int* epoch;
+  __nv_bfloat16* resid;
+  long ldr;
+  const float* w;
+  __nv_bfloat16* out;
+  long ldo;
+  int rows, cols;
+  float eps;
+  int* status;
+  unsigned long long limit_ns;
+};
+void ar_add_norm(const ArNormArgs& a, cudaStream_t st);
+
+struct GreedyArgs {
+  const int64_t* keys;     // [rows] local packed argmax keys
+  int rows;
+  int64_t* peer_slots[8];       // each rank's slot base ([world][rows] int64)
+  unsigned* peer_flags[8];      // each rank's flag array
+  const unsigned* flags;
+  int world, rank;
+  int* epoch;
+  int* ids_out;
+  int* status;
+  unsigned long long limit_ns;
+};
+void greedy_allmax(const GreedyArgs& a, cudaStream_t st);
+
+}  // namespace bwn

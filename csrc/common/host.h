@@ -53,6 +53,18 @@ enum GemmEpilogue : int {
   kEpiResid = 1,   // out = bf16(acc + resid)
   kEpiSwiGLU = 2,  // out = bf16(silu(gate) * up), gate/up interleaved in blocks of 16
   kEpiF32 = 3,     // out = acc (fp32)
+  kEpiMcRed = 4,   // multimem.red.add.f32 of acc into an NVLS multicast buffer, then signal peers
+};
+
+// Completion signalling of a fused compute + collective launch: the last CTA to
+// finish bumps *epoch and release-stores it into every rank's flag slot.
+struct CommSignal {
+  unsigned* peer_flags[8] = {nullptr};  // flag array of each rank (slot = this rank)
+  int world = 1, rank = 0;
+  int* epoch = nullptr;                  // local epoch counter
+  int* done_ticket = nullptr;            // grid completion ticket (re-armed)
+  const int* sel = nullptr;              // device buffer selector: buffer (*sel & 1)
+  long buf_stride = 0;                   // elements between the two alternating buffers
 };
 
 struct GemmProblem {
@@ -77,6 +89,7 @@ struct GemmProblem {
   int* tickets = nullptr;
   int tickets_len = 0;
   int* status = nullptr;
+  CommSignal sig;  // kEpiMcRed only
 };
 
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);

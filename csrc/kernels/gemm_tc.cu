@@ -47,11 +47,26 @@ struct GemmArgs {
   float* workspace;            // splits>1: [tiles * splits * BM * BN] fp32
   int* tickets;                // splits>1: [tiles]
   int* status;
+  CommSignal sig;              // kEpiMcRed: completion signal to peers
 };
 
 template <int BN, int EPI, bool TRANS>
 __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, const float (&v)[32], int ncols, int m, int n0) {
   // m: global row (A row), n0: global column of v[0]; ncols valid in v (16 or 32)
+  if (EPI == kEpiMcRed) {
+    // out is the multicast address of an fp32 [tokens, ldo] buffer; the switch
+    // adds every rank's (and every split's) partial into all ranks' copies
+    float* out = reinterpret_cast<float*>(a.out) + (long)((*a.sig.sel) & 1) * a.sig.buf_stride;
+    if (m >= a.M) return;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < ncols && n0 + j < a.N) {
+        const long idx = TRANS ? (long)(n0 + j) * a.ldo + m : (long)m * a.ldo + n0 + j;
+        mc_red_add_f32(out + idx, v[j]);
+      }
+    }
+    return;
+  }
   if (EPI == kEpiF32) {
     float* out = reinterpret_cast<float*>(a.out);
     if (!TRANS) {
@@ -298,7 +313,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
       const int m = tm * kBM + row;
-      if (args.splits == 1) {
+      if (args.splits == 1 || EPI == kEpiMcRed) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
@@ -375,6 +390,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  if (EPI == kEpiMcRed && warp >= 2) {
+    // publish completion: every red of this CTA is performed system-wide before
+    // the ticket; the last CTA bumps the epoch and release-stores it to all ranks
+    fence_acq_rel_sys();
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (threadIdx.x == 64) {
+      const int t = atomicAdd(args.sig.done_ticket, 1);
+      if (t == (int)gridDim.x - 1) {
+        *args.sig.done_ticket = 0;
+        fence_acq_rel_sys();
+        const unsigned e = (unsigned)(*args.sig.epoch) + 1u;
+        *args.sig.epoch = (int)e;
+        for (int r = 0; r < args.sig.world; ++r) st_release_sys(args.sig.peer_flags[r] + args.sig.rank, e);
+      }
+    }
+  }
   // Teardown (the producer already drained its in-flight copies on abort).
   __syncthreads();
   if (warp == 1) {
@@ -465,11 +496,12 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   // per persistent CTA measured ~2x slower on decode shapes: each unit's
   // partial round trip and fence serialises the CTA.)
   int splits = 1;
-  if (p.allow_split && p.workspace && p.tickets && tiles < sms && tiles <= p.tickets_len) {
+  const bool mcred = p.epi == kEpiMcRed;  // partials reduce in the switch: no workspace
+  if (p.allow_split && tiles < sms && (mcred || (p.workspace && p.tickets && tiles <= p.tickets_len))) {
     splits = sms / tiles;
     if (splits > a.num_kb / 4) splits = a.num_kb / 4 > 0 ? a.num_kb / 4 : 1;
     if (splits > 16) splits = 16;
-    if ((long)tiles * splits * kBM * bn > p.workspace_floats) splits = 1;
+    if (!mcred && (long)tiles * splits * kBM * bn > p.workspace_floats) splits = 1;
   }
   a.splits = splits;
   a.kb_per_split = (a.num_kb + splits - 1) / splits;
@@ -481,6 +513,7 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   a.workspace = p.workspace;
   a.tickets = p.tickets;
   a.status = p.status;
+  a.sig = p.sig;
   const int units = tiles * a.splits;
   const int grid = units < sms ? units : sms;
   const bool tr = p.trans_out;
@@ -506,6 +539,10 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
       break;
     case kEpiF32:
       tr ? dispatch_bn<kEpiF32, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiF32, false>(bn, ta, tb, a, grid, stream);
+      break;
+    case kEpiMcRed:
+      BWN_CHECK(p.sig.epoch && p.sig.done_ticket && p.sig.world >= 1 && p.sig.world <= 8, "gemm: bad comm signal");
+      tr ? dispatch_bn<kEpiMcRed, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiMcRed, false>(bn, ta, tb, a, grid, stream);
       break;
     default: BWN_FAIL("gemm: bad epilogue %d", p.epi);
   }

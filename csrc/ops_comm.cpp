@@ -1,0 +1,150 @@
+// torch.ops.bwn registrations of the fused NVLink collectives.  Buffer
+// addresses (symmetric peer pointers, the NVLS multicast address) come from the
+// Python side as integers; this file only validates and launches.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+#include <torch/library.h>
+
+#include "comm/fused.h"
+#include "common/host.h"
+#include "ops_ext.h"
+
+namespace bwn {
+using at::Tensor;
+
+// local_state int32 layout: [0] AR epoch, [1] AR grid ticket, [2] buffer selector,
+// [3] norm-kernel ticket, [4] greedy epoch
+static CommSignal make_sig(const std::vector<int64_t>& peer_flags, const Tensor& local_state, int64_t rank,
+                           int64_t buf_stride) {
+  TORCH_CHECK(local_state.scalar_type() == at::kInt && local_state.numel() >= 8, "local_state int32[8+]");
+  TORCH_CHECK(peer_flags.size() >= 1 && peer_flags.size() <= 8, "1..8 ranks");
+  CommSignal s;
+  s.world = (int)peer_flags.size();
+  s.rank = (int)rank;
+  for (size_t i = 0; i < peer_flags.size(); ++i) s.peer_flags[i] = reinterpret_cast<unsigned*>(peer_flags[i]);
+  int* ls = local_state.data_ptr<int>();
+  s.epoch = ls + 0;
+  s.done_ticket = ls + 1;
+  s.sel = ls + 2;
+  s.buf_stride = buf_stride;
+  return s;
+}
+
+void gemm_mcred_op(const Tensor& x, const Tensor& w, int64_t mc_base, int64_t buf_stride, int64_t ldo,
+                   std::vector<int64_t> peer_flags, const Tensor& local_state, int64_t rank) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w.dim() == 2 && w.stride(1) == 1, "row-major x, w");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int M = (int)x.size(0), Nw = (int)w.size(0), K = (int)x.size(1);
+  GemmProblem p;
+  p.epi = kEpiMcRed;
+  p.status = status_dev_ptr();
+  const bool swap = M <= 128;
+  if (swap) {
+    p.A = w.data_ptr();
+    p.lda = w.stride(0);
+    p.B = x.data_ptr();
+    p.ldb = x.stride(0);
+    p.M = Nw;
+    p.N = M;
+    p.trans_out = true;
+  } else {
+    p.A = x.data_ptr();
+    p.lda = x.stride(0);
+    p.B = w.data_ptr();
+    p.ldb = w.stride(0);
+    p.M = M;
+    p.N = Nw;
+  }
+  p.K = K;
+  p.out = reinterpret_cast<void*>(mc_base);
+  p.ldo = ldo;
+  p.sig = make_sig(peer_flags, local_state, rank, buf_stride);
+  gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
+}
+
+void mc_red_signal_op(const Tensor& x, int64_t mc_base, int64_t buf_stride, std::vector<int64_t> peer_flags,
+                      const Tensor& local_state, int64_t rank) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [rows, cols]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  mc_red_signal(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)x.size(0), (int)x.size(1),
+                reinterpret_cast<float*>(mc_base), make_sig(peer_flags, local_state, rank, buf_stride),
+                at::cuda::getCurrentCUDAStream().stream());
+}
+
+Tensor ar_add_norm_op(int64_t local_base, int64_t buf_stride, int64_t flags_local, int64_t world,
+                      const Tensor& local_state, Tensor residual, const Tensor& w, double eps, double timeout_s) {
+  check_bf16(residual, "residual");
+  check_f32(w, "w");
+  TORCH_CHECK(residual.dim() == 2 && residual.stride(1) == 1, "residual [rows, H]");
+  const c10::cuda::CUDAGuard guard(residual.device());
+  auto out = at::empty_like(residual, residual.options().memory_format(at::MemoryFormat::Contiguous));
+  ArNormArgs a{};
+  a.local_base = reinterpret_cast<float*>(local_base);
+  a.buf_stride = buf_stride;
+  int* ls = local_state.data_ptr<int>();
+  a.sel = ls + 2;
+  a.flags = reinterpret_cast<const unsigned*>(flags_local);
+  a.world = (int)world;
+  a.epoch = ls + 0;
+  a.resid = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  a.ldr = residual.stride(0);
+  a.w = w.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ldo = out.stride(0);
+  a.rows = (int)residual.size(0);
+  a.cols = (int)residual.size(1);
+  a.eps = (float)eps;
+  a.status = status_dev_ptr();
+  a.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  if (a.rows > 0) ar_add_norm(a, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
+Tensor greedy_allmax_op(const Tensor& keys, std::vector<int64_t> peer_slots, std::vector<int64_t> peer_flags,
+                        int64_t flags_local, const Tensor& local_state, int64_t rank, double timeout_s) {
+  check_cuda(keys, "keys");
+  TORCH_CHECK(keys.scalar_type() == at::kLong && keys.is_contiguous(), "keys int64");
+  TORCH_CHECK(peer_slots.size() == peer_flags.size() && peer_slots.size() <= 8, "peer arrays");
+  const c10::cuda::CUDAGuard guard(keys.device());
+  auto ids = at::empty({keys.numel()}, keys.options().dtype(at::kInt));
+  GreedyArgs a{};
+  a.keys = keys.data_ptr<int64_t>();
+  a.rows = (int)keys.numel();
+  for (size_t i = 0; i < peer_slots.size(); ++i) {
+    a.peer_slots[i] = reinterpret_cast<int64_t*>(peer_slots[i]);
+    a.peer_flags[i] = reinterpret_cast<unsigned*>(peer_flags[i]);
+  }
+  a.flags = reinterpret_cast<const unsigned*>(flags_local);
+  a.world = (int)peer_slots.size();
+  a.rank = (int)rank;
+  a.epoch = local_state.data_ptr<int>() + 4;
+  a.ids_out = ids.data_ptr<int>();
+  a.status = status_dev_ptr();
+  a.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  greedy_allmax(a, at::cuda::getCurrentCUDAStream().stream());
+  return ids;
+}
+
+void register_comm_defs(torch::Library& m) {
+  m.def(
+      "gemm_mcred(Tensor x, Tensor w, int mc_base, int buf_stride, int ldo, int[] peer_flags, Tensor(a!) local_state, "
+      "int rank) -> ()");
+  m.def("mc_red_signal(Tensor x, int mc_base, int buf_stride, int[] peer_flags, Tensor(a!) local_state, int rank) -> ()");
+  m.def(
+      "ar_add_norm(int local_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
+      "Tensor(b!) residual, Tensor w, float eps, float timeout_s) -> Tensor");
+  m.def(
+      "greedy_allmax(Tensor keys, int[] peer_slots, int[] peer_flags, int flags_local, Tensor(a!) local_state, "
+      "int rank, float timeout_s) -> Tensor");
+}
+void register_comm_impls(torch::Library& m) {
+  m.impl("gemm_mcred", &gemm_mcred_op);
+  m.impl("mc_red_signal", &mc_red_signal_op);
+  m.impl("ar_add_norm", &ar_add_norm_op);
+  m.impl("greedy_allmax", &greedy_allmax_op);
+}
+}  // namespace bwn

@@ -238,6 +238,7 @@ Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const
 }
 
 void register_ext_defs(torch::Library& m) {
+  register_comm_defs(m);
   m.def("moe_topk(Tensor logits, int k, bool renorm, Tensor? bias, int mode, float route_scale) -> (Tensor, Tensor)");
   m.def(
       "moe_experts(Tensor x, Tensor w, Tensor ids, Tensor gate_up, Tensor down, int e0, Tensor? shared_y, "
@@ -250,6 +251,7 @@ void register_ext_defs(torch::Library& m) {
       "Tensor(a!) k_cache, Tensor(b!) v_cache, int start, float eps) -> Tensor");
 }
 void register_ext_impls(torch::Library& m) {
+  register_comm_impls(m);
   m.impl("moe_topk", &moe_topk_op);
   m.impl("moe_experts", &moe_experts_op);
   m.impl("deltanet_prefill", &deltanet_prefill_op);

@@ -9,6 +9,8 @@ namespace bwn {
 void register_ext_defs(torch::Library& m);
 void register_ext_impls(torch::Library& m);
 void register_ext_pybind(pybind11::module& mod);
+void register_comm_defs(torch::Library& m);
+void register_comm_impls(torch::Library& m);
 
 // shared validation helpers (defined in ops.cpp)
 void check_cuda(const at::Tensor& t, const char* name);
