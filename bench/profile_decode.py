@@ -28,12 +28,28 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--tp-shapes", type=int, default=1,
+                    help="emulate rank 0 of a TP group of this size on one GPU (collectives become no-ops)")
     args = ap.parse_args()
     cfg = QWEN36_27B if args.model == "27b" else QWEN36_35B_A3B
     if args.layers:
         cfg = cfg.scaled(num_layers=args.layers)
     dev = torch.device("cuda", 0)
-    m = Qwen36Model(cfg, device=dev).init_random(0)
+    comm = None
+    if args.tp_shapes > 1:
+        from bwn.parallel.comm import Comm
+
+        class ShapeOnlyComm(Comm):
+            """Rank 0 of an N-way group whose collectives do nothing (profiling only)."""
+
+            def all_reduce_(self, x):
+                return x
+
+            def all_reduce_max_(self, x):
+                return x
+
+        comm = ShapeOnlyComm(None, 0, args.tp_shapes)
+    m = Qwen36Model(cfg, comm, device=dev).init_random(0)
     st = m.new_state(args.batch, args.ctx + 64)
     st.k_cache.normal_()
     st.v_cache.normal_()
