@@ -1,0 +1,237 @@
+"""DeepSeek V4 Flash (MLA-style single-KV-head attention, Hyper-Connections,
+256-expert MoE) -- the reference's TP/EP model
+(``contrib/deepseek-v4-flash/run_deepseek_v4_tp.py:261-650``).
+
+Parameter names follow the reference module (its state dict is the checkpoint
+layout the pre-sharding script writes, ``preprocess_weights.py:80-121``).
+Per rank:
+
+* attention: ``wq_a``/``q_norm``/``wkv``/``kv_norm`` replicated, ``wq_b``
+  column-parallel by heads, ``wo_a`` restricted to this rank's head groups,
+  ``wo_b`` row-parallel over the matching o_lora slices -> all-reduce;
+* MoE: gate (+ selection bias after the hash layers) replicated, experts
+  partitioned (EP), shared expert tensor-parallel; partials all-reduced;
+* Hyper-Connections: ``hc_mult`` residual streams, fused pre-mix (GEMV +
+  Sinkhorn + contraction) and post-mix kernels.
+
+On CUDA every op is a bwn kernel (tcgen05 GEMMs, grouped MoE GEMMs, hc_pre /
+hc_post, interleaved RoPE, single-KV-head attention); on CPU the same code runs
+the fp32 references.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops as O
+from ..config import DeepSeekV4Config
+from ..io.qwen36_weights import seeded_tensor
+from ..parallel.comm import Comm
+
+
+class DeepSeekV4State:
+    def __init__(self, cfg: DeepSeekV4Config, batch: int, max_seq: int, device, dtype=torch.bfloat16):
+        self.kv = torch.zeros(cfg.num_layers, batch, max_seq, cfg.head_dim, dtype=dtype, device=device)
+        self.positions = torch.zeros(batch, dtype=torch.int32, device=device)
+
+
+def synthetic_checkpoint(cfg: DeepSeekV4Config, seed: int, device="cpu") -> dict:
+    """Random-init weights in the reference's state-dict layout."""
+    sd = {}
+    d, hd, E, I = cfg.dim, cfg.head_dim, cfg.n_routed_experts, cfg.moe_inter
+    mix = (2 + cfg.hc_mult) * cfg.hc_mult
+
+    def t(name, shape, kind="normal", std=0.02, dtype=torch.bfloat16):
+        sd[name] = seeded_tensor(name, shape, seed, device, kind, std, dtype)
+
+    t("embed.weight", (cfg.vocab, d), std=1.0)
+    t("head.weight", (cfg.vocab, d))
+    t("norm.weight", (d,), "ones", dtype=torch.float32)
+    t("hc_head_fn", (cfg.hc_mult, cfg.hc_mult * d), std=0.02, dtype=torch.float32)
+    t("hc_head_base", (cfg.hc_mult,), "zeros", dtype=torch.float32)
+    t("hc_head_scale", (1,), "ones", dtype=torch.float32)
+    for i in range(cfg.num_layers):
+        p = f"layers.{i}."
+        t(p + "attn_norm.weight", (d,), "ones", dtype=torch.float32)
+        t(p + "ffn_norm.weight", (d,), "ones", dtype=torch.float32)
+        for w in ("attn", "ffn"):
+            t(p + f"hc_{w}_fn", (mix, cfg.hc_mult * d), std=0.02, dtype=torch.float32)
+            t(p + f"hc_{w}_base", (mix,), "normal", 0.1, dtype=torch.float32)
+            t(p + f"hc_{w}_scale", (3,), "ones", dtype=torch.float32)
+        a = p + "attn."
+        t(a + "wq_a.weight", (cfg.q_lora_rank, d))
+        t(a + "q_norm.weight", (cfg.q_lora_rank,), "ones", dtype=torch.float32)
+        t(a + "wq_b.weight", (cfg.n_heads * hd, cfg.q_lora_rank))
+        t(a + "wkv.weight", (hd, d))
+        t(a + "kv_norm.weight", (hd,), "ones", dtype=torch.float32)
+        t(a + "wo_a.weight", (cfg.o_groups * cfg.o_lora_rank, cfg.n_heads * hd // cfg.o_groups))
+        t(a + "wo_b.weight", (d, cfg.o_groups * cfg.o_lora_rank))
+        f = p + "ffn."
+        t(f + "gate.weight", (E, d))
+        if i >= cfg.n_hash_layers:
+            t(f + "gate.bias", (E,), "normal", 0.01, dtype=torch.float32)
+        t(f + "experts_w1", (E, I, d))
+        t(f + "experts_w3", (E, I, d))
+        t(f + "experts_w2", (E, d, I))
+        t(f + "shared_experts.w1.weight", (I, d))
+        t(f + "shared_experts.w3.weight", (I, d))
+        t(f + "shared_experts.w2.weight", (d, I))
+    return sd
+
+
+def _expert_stack(sd, f, name, E):
+    """Experts as one ``[E, ...]`` tensor, from either the stacked or the
+    per-expert (``experts.{e}.wN.weight``) layout."""
+    if f + f"experts_{name}" in sd:
+        return sd[f + f"experts_{name}"]
+    return torch.stack([sd[f + f"experts.{e}.{name}.weight"] for e in range(E)])
+
+
+class DeepSeekV4Model:
+    def __init__(self, cfg: DeepSeekV4Config, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16):
+        self.cfg = cfg
+        self.comm = comm or Comm.single()
+        self.tp, self.rank = self.comm.size, self.comm.rank
+        if cfg.n_heads % self.tp or cfg.o_groups % self.tp or cfg.n_routed_experts % self.tp:
+            raise ValueError("tp must divide n_heads, o_groups and n_routed_experts")
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.heads = cfg.n_heads // self.tp
+        self.groups = cfg.o_groups // self.tp
+        self.e_local = cfg.n_routed_experts // self.tp
+        self.e0 = self.rank * self.e_local
+        half = cfg.rope_head_dim // 2
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.rope_head_dim, 2, dtype=torch.float32) / cfg.rope_head_dim))
+        f = torch.outer(torch.arange(cfg.max_seq_len, dtype=torch.float32), inv)
+        self.cos, self.sin = f.cos().to(self.device), f.sin().to(self.device)
+        assert self.cos.shape[1] == half
+        self.L: list[dict] = []
+        self.g: dict = {}
+        self.ones_hd = torch.ones(cfg.head_dim, device=self.device)
+
+    # ------------------------------------------------------------------ load
+    def load(self, sd: dict) -> "DeepSeekV4Model":
+        cfg, dt, dev = self.cfg, self.dtype, self.device
+        hd, r = cfg.head_dim, self.rank
+        h0, h1 = r * self.heads, (r + 1) * self.heads
+        g0, g1 = r * self.groups, (r + 1) * self.groups
+        olr = cfg.o_lora_rank
+        E, I = cfg.n_routed_experts, cfg.moe_inter
+        Is = I // self.tp
+        self.L = []
+        for i in range(cfg.num_layers):
+            p, a, f = f"layers.{i}.", f"layers.{i}.attn.", f"layers.{i}.ffn."
+            L = {
+                "attn_norm": sd[p + "attn_norm.weight"].float(),
+                "ffn_norm": sd[p + "ffn_norm.weight"].float(),
+                "hc_attn": (sd[p + "hc_attn_fn"].float(), sd[p + "hc_attn_scale"].float(), sd[p + "hc_attn_base"].float()),
+                "hc_ffn": (sd[p + "hc_ffn_fn"].float(), sd[p + "hc_ffn_scale"].float(), sd[p + "hc_ffn_base"].float()),
+                "wq_a": sd[a + "wq_a.weight"].to(dt),
+                "q_norm": sd[a + "q_norm.weight"].float(),
+                "wq_b": sd[a + "wq_b.weight"][h0 * hd:h1 * hd].to(dt),
+                "wkv": sd[a + "wkv.weight"].to(dt),
+                "kv_norm": sd[a + "kv_norm.weight"].float(),
+                "wo_a": sd[a + "wo_a.weight"].view(cfg.o_groups, olr, -1)[g0:g1].to(dt),
+                "wo_b": sd[a + "wo_b.weight"][:, g0 * olr:g1 * olr].to(dt),
+                "gate": sd[f + "gate.weight"].to(dt),
+                "gate_bias": sd[f + "gate.bias"].float() if (f + "gate.bias") in sd else None,
+            }
+            w1 = _expert_stack(sd, f, "w1", E)[self.e0:self.e0 + self.e_local]
+            w3 = _expert_stack(sd, f, "w3", E)[self.e0:self.e0 + self.e_local]
+            L["experts_gate_up"] = torch.stack([O.interleave_gate_up(w1[e], w3[e]) for e in range(self.e_local)]).to(dt)
+            L["experts_down"] = _expert_stack(sd, f, "w2", E)[self.e0:self.e0 + self.e_local].to(dt)
+            L["shared_gate_up"] = O.interleave_gate_up(sd[f + "shared_experts.w1.weight"][r * Is:(r + 1) * Is],
+                                                       sd[f + "shared_experts.w3.weight"][r * Is:(r + 1) * Is]).to(dt)
+            L["shared_down"] = sd[f + "shared_experts.w2.weight"][:, r * Is:(r + 1) * Is].to(dt)
+            self.L.append({k: (tuple(x.to(dev) for x in v) if isinstance(v, tuple) else
+                               (v.to(dev).contiguous() if v is not None else None)) for k, v in L.items()})
+        self.g = {
+            "embed": sd["embed.weight"].to(dt).to(dev),
+            "head": sd["head.weight"].to(dt).to(dev),
+            "norm": sd["norm.weight"].float().to(dev),
+            "hc_head": tuple(sd[k].float().to(dev) for k in ("hc_head_fn", "hc_head_scale", "hc_head_base")),
+        }
+        return self
+
+    def init_random(self, seed: int = 0) -> "DeepSeekV4Model":
+        return self.load(synthetic_checkpoint(self.cfg, seed, "cpu"))
+
+    def new_state(self, batch: int, max_seq: int) -> DeepSeekV4State:
+        return DeepSeekV4State(self.cfg, batch, max_seq, self.device, self.dtype)
+
+    # --------------------------------------------------------------- blocks
+    def _allreduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp > 1:
+            self.comm.all_reduce_(x)
+        return x
+
+    def _attn(self, L, x, st: DeepSeekV4State, li: int, pos: torch.Tensor, bidx: torch.Tensor, q_per_seq: int):
+        cfg = self.cfg
+        T, hd, rd = x.shape[0], cfg.head_dim, cfg.rope_head_dim
+        eps = cfg.norm_eps
+        q = O.linear(O.rms_norm(O.linear(x, L["wq_a"]), L["q_norm"], eps, one_plus=False), L["wq_b"])
+        q = O.rms_norm(q.view(T * self.heads, hd), self.ones_hd, 1e-6, one_plus=False).view(T, self.heads, hd)
+        kv = O.rms_norm(O.linear(x, L["wkv"]), L["kv_norm"], eps, one_plus=False).view(T, 1, hd)
+        if rd > 0:
+            O.rope_interleaved_(q, self.cos, self.sin, pos)
+            O.rope_interleaved_(kv, self.cos, self.sin, pos)
+        cache = st.kv[li]  # [B, S, hd]
+        S = cache.shape[1]
+        cache.view(-1, hd).index_copy_(0, (bidx.long() * S + pos.long()), kv.view(T, hd))
+        o = O.mqa_attn(q, cache, pos + 1, q_per_seq, 1.0 / math.sqrt(hd))  # [T, H, hd]
+        hpg = cfg.n_heads // cfg.o_groups
+        og = o.view(T, self.groups, hpg * hd)
+        lora = torch.cat([O.linear(og[:, g].contiguous(), L["wo_a"][g]) for g in range(self.groups)], dim=-1)
+        return self._allreduce(O.linear(lora, L["wo_b"]))
+
+    def _moe(self, L, x, li: int):
+        cfg = self.cfg
+        logits = O.linear_f32(x, L["gate"])
+        w, ids = O.moe_topk_deepseek(logits, L["gate_bias"], cfg.n_activated_experts, cfg.score_func, cfg.route_scale)
+        routed = O.moe_experts(x, w, ids, L["experts_gate_up"], L["experts_down"], self.e0,
+                               swiglu_limit=cfg.swiglu_limit)
+        shared = O.linear(O.linear_swiglu(x, L["shared_gate_up"]), L["shared_down"])
+        return self._allreduce((routed.float() + shared.float()).to(x.dtype))
+
+    def forward_tokens(self, tokens: torch.Tensor, pos: torch.Tensor, bidx: torch.Tensor, st: DeepSeekV4State,
+                       q_per_seq: int) -> torch.Tensor:
+        """Run flattened tokens ``[T]`` (positions ``pos``, sequence ``bidx``)
+        through every layer, writing their K/V rows; returns final hidden ``[T, dim]``."""
+        cfg = self.cfg
+        hc = cfg.hc_mult
+        x0 = O.embedding(tokens.int(), self.g["embed"], 0)
+        h = x0.unsqueeze(1).expand(-1, hc, -1).contiguous()  # [T, hc, dim]
+        for li, L in enumerate(self.L):
+            fn, sc, bs = L["hc_attn"]
+            x, post, comb = O.hc_pre(h, fn, sc, bs, cfg.hc_sinkhorn_iters, cfg.hc_eps, cfg.norm_eps)
+            a = self._attn(L, O.rms_norm(x, L["attn_norm"], cfg.norm_eps, one_plus=False), st, li, pos, bidx, q_per_seq)
+            h = O.hc_post(a, h, post, comb)
+            fn, sc, bs = L["hc_ffn"]
+            x, post, comb = O.hc_pre(h, fn, sc, bs, cfg.hc_sinkhorn_iters, cfg.hc_eps, cfg.norm_eps)
+            m = self._moe(L, O.rms_norm(x, L["ffn_norm"], cfg.norm_eps, one_plus=False), li)
+            h = O.hc_post(m, h, post, comb)
+        fn, sc, bs = self.g["hc_head"]
+        y, _, _ = O.hc_pre(h, fn, sc, bs, cfg.hc_sinkhorn_iters, cfg.hc_eps, cfg.norm_eps)
+        return O.rms_norm(y, self.g["norm"], cfg.norm_eps, one_plus=False)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        return O.linear_f32(hidden, self.g["head"]) if hidden.is_cuda else hidden.float() @ self.g["head"].float().t()
+
+    def prefill(self, tokens: torch.Tensor, st: DeepSeekV4State) -> torch.Tensor:
+        """``tokens [B, S]`` from position 0; returns next ids ``[B]``."""
+        B, S = tokens.shape
+        dev = self.device
+        pos = torch.arange(S, device=dev, dtype=torch.int32).repeat(B)
+        bidx = torch.arange(B, device=dev, dtype=torch.int32).repeat_interleave(S)
+        h = self.forward_tokens(tokens.reshape(-1).to(dev), pos, bidx, st, S)
+        st.positions.fill_(S)
+        last = h.view(B, S, -1)[:, -1]
+        return self.logits(last).argmax(-1).int()
+
+    def decode_step(self, tokens: torch.Tensor, st: DeepSeekV4State) -> torch.Tensor:
+        B = tokens.shape[0]
+        bidx = torch.arange(B, device=self.device, dtype=torch.int32)
+        h = self.forward_tokens(tokens.to(self.device), st.positions, bidx, st, 1)
+        st.positions.add_(1)
+        return self.logits(h).argmax(-1).int()

@@ -216,18 +216,59 @@ def moe_topk_deepseek(logits: torch.Tensor, bias, k: int, score_func: str = "sqr
     return ref.moe_route_deepseek(logits, bias, k, score_func, route_scale)
 
 
-def moe_experts(x, w, ids, gate_up_il, down, expert_offset: int = 0, shared=None):
+def moe_experts(x, w, ids, gate_up_il, down, expert_offset: int = 0, shared=None, swiglu_limit: float = 0.0):
     """This rank's routed-expert partial (plus, when ``shared=(y, gate_logit)``
     is given, ``sigmoid(gate_logit) * y``)."""
     if x.is_cuda:
         sy, sg = (shared if shared is not None else (None, None))
         return ops().moe_experts(x, w.float().contiguous(), ids.int().contiguous(), gate_up_il, down, expert_offset,
-                                 sy, sg.float().reshape(-1).contiguous() if sg is not None else None)
+                                 sy, sg.float().reshape(-1).contiguous() if sg is not None else None, swiglu_limit)
     E, n2, H = gate_up_il.shape
     xg = gate_up_il.reshape(E, n2 // 32, 2, 16, H)
     gu = torch.cat([xg[:, :, 0].reshape(E, n2 // 2, H), xg[:, :, 1].reshape(E, n2 // 2, H)], dim=1)
-    out = ref.moe_experts(x, w, ids, gu, down, expert_offset)
+    out = ref.moe_experts(x, w, ids, gu, down, expert_offset, swiglu_limit)
     if shared is not None:
         sy, sg = shared
         out = out + torch.sigmoid(sg.float().reshape(-1, 1)) * sy.float()
     return out.to(x.dtype)
+
+
+# --------------------------------------------------------------------------
+# DeepSeek V4: hyper-connections, single-KV-head attention
+# --------------------------------------------------------------------------
+def hc_pre(x, fn, scale, base, iters: int = 20, eps: float = 1e-6, norm_eps: float = 1e-6):
+    """Hyper-Connection pre-mix of ``x [T, hc, dim]``.  With ``fn [(2+hc)*hc, hc*dim]``
+    returns ``(y [T,dim], post [T,hc], comb [T,hc,hc])``; with ``fn [hc, hc*dim]``
+    (the head) returns ``(y, None, None)``."""
+    if x.is_cuda:
+        y, post, comb = ops().hc_pre(x.contiguous(), fn.float().contiguous(), scale.float().contiguous(),
+                                     base.float().contiguous(), iters, eps, norm_eps)
+        return (y, None, None) if fn.shape[0] == x.shape[1] else (y, post, comb)
+    return ref.hc_pre(x, fn, scale, base, iters, eps, norm_eps)
+
+
+def hc_post(x, resid, post, comb):
+    if x.is_cuda:
+        return ops().hc_post(x.contiguous(), resid.contiguous(), post.contiguous(), comb.contiguous())
+    return ref.hc_post(x, resid, post, comb)
+
+
+def mqa_attn(q, kv, visible, q_per_seq: int, scale: float, splits: int = 0):
+    """Attention of ``q [rows, H, D]`` over one shared K/V head per sequence
+    ``kv [B, T, D]``; row ``r`` (sequence ``r // q_per_seq``) sees keys
+    ``[0, visible[r])``."""
+    if q.is_cuda:
+        return ops().mqa_attn(q.contiguous(), kv, visible.int().contiguous(), q_per_seq, scale, splits)
+    return ref.mqa_attn(q, kv, visible, q_per_seq, scale)
+
+
+def rope_interleaved_(x, cos, sin, pos):
+    """In place: interleaved-pair RoPE on the trailing ``2*cos.shape[1]`` dims of
+    ``x [rows, H, D]`` at ``pos [rows]``."""
+    if x.is_cuda:
+        ops().rope_interleaved_(x, cos, sin, pos.int().contiguous())
+        return x
+    c = cos[pos.long()][:, None]
+    s = sin[pos.long()][:, None]
+    x.copy_(ref.apply_interleaved_rope(x, c, s))
+    return x

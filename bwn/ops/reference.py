@@ -430,3 +430,46 @@ def sharded_greedy(local_logits: list[torch.Tensor]) -> torch.Tensor:
     ids = torch.arange(full.shape[-1], device=full.device)
     cand = torch.where(full == m, ids, torch.full_like(ids, full.shape[-1]))
     return cand.min(-1).values
+
+
+# --------------------------------------------------------------------------
+# DeepSeek V4: hyper-connections and single-KV-head attention
+# --------------------------------------------------------------------------
+def hc_pre(x, fn, scale, base, iters: int = 20, eps: float = 1e-6, norm_eps: float = 1e-6):
+    """Hyper-Connection pre-mix (``run_deepseek_v4_tp.py:179-217``) on
+    ``x [T, hc, dim]``; ``fn.shape[0] == hc`` selects the head variant (``:230-243``)."""
+    T, hc, dim = x.shape
+    xf = x.reshape(T, hc * dim).float()
+    rs = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + norm_eps)
+    mixes = (xf @ fn.float().t()) * rs
+    if fn.shape[0] == hc:
+        pre = torch.sigmoid(mixes * scale.float()[0] + base.float()) + eps
+        y = (pre.unsqueeze(-1) * x.float()).sum(1)
+        return y.to(x.dtype), None, None
+    s, b = scale.float(), base.float()
+    pre = torch.sigmoid(mixes[:, :hc] * s[0] + b[:hc]) + eps
+    post = torch.sigmoid(mixes[:, hc:2 * hc] * s[1] + b[hc:2 * hc]) + eps
+    m = torch.exp((mixes[:, 2 * hc:] * s[2] + b[2 * hc:]).view(T, hc, hc))
+    for _ in range(iters):
+        m = m / (m.sum(-1, keepdim=True) + eps)
+        m = m / (m.sum(-2, keepdim=True) + eps)
+    y = (pre.unsqueeze(-1) * x.float()).sum(1)
+    return y.to(x.dtype), post, m
+
+
+def hc_post(x, resid, post, comb):
+    """``out[j] = post[j] x + sum_i comb[i][j] resid[i]`` (``:221-227``)."""
+    out = post.unsqueeze(-1) * x.float().unsqueeze(-2) + (comb.unsqueeze(-1) * resid.float().unsqueeze(-2)).sum(1)
+    return out.to(x.dtype)
+
+
+def mqa_attn(q, kv, visible, q_per_seq: int, scale: float):
+    rows, H, D = q.shape
+    out = torch.empty(rows, H, D, dtype=torch.float32, device=q.device)
+    for r in range(rows):
+        b = r // q_per_seq
+        L = int(visible[r])
+        k = kv[b, :L].float()
+        sc = (q[r].float() @ k.t()) * scale
+        out[r] = sc.softmax(-1) @ k
+    return out.to(q.dtype)

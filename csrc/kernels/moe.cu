@@ -462,9 +462,14 @@ __global__ void __launch_bounds__(kGThreadsG, 1)
           const int fo = (f >> 5) * 16 + (lane & 15);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float up = __shfl_down_sync(0xffffffffu, v[j], 16);
+            float up = __shfl_down_sync(0xffffffffu, v[j], 16);
+            float gt = v[j];
+            if (a.swiglu_limit > 0.f) {
+              gt = fminf(gt, a.swiglu_limit);
+              up = fminf(fmaxf(up, -a.swiglu_limit), a.swiglu_limit);
+            }
             if (lane < 16 && c + j < nr)
-              a.out[(long)(n0 + c + j) * a.ldo + fo] = __float2bfloat16(silu_f(v[j]) * up);
+              a.out[(long)(n0 + c + j) * a.ldo + fo] = __float2bfloat16(silu_f(gt) * up);
           }
         } else {
 #pragma unroll
@@ -522,6 +527,7 @@ void grouped_gemm(const GroupedProblem& p, cudaStream_t st) {
   a.out = p.out;
   a.ldo = p.ldo;
   a.status = p.status;
+  a.swiglu_limit = p.swiglu_limit;
   if (a.max_tiles_n == 0) return;
   switch (bn) {
     case 16: p.swiglu ? launch_grouped<16, true>(tw, tx, a, st) : launch_grouped<16, false>(tw, tx, a, st); break;

@@ -52,6 +52,7 @@ struct GroupedArgs {
   __nv_bfloat16* out;
   long ldo;
   int* status;
+  float swiglu_limit;  // > 0: gate <= limit, |up| <= limit before silu(gate) * up
 };
 struct GroupedProblem {
   const void* W;    // [groups * N, K] bf16 (expert-major)
@@ -64,6 +65,7 @@ struct GroupedProblem {
   __nv_bfloat16* out;
   long ldo;
   int* status;
+  float swiglu_limit = 0.f;
 };
 void grouped_gemm(const GroupedProblem& p, cudaStream_t st);
 

@@ -5,6 +5,7 @@
 #include <tuple>
 
 #include "common/host.h"
+#include "kernels/deepseek.h"
 #include "kernels/moe.h"
 #include "kernels/prefill.h"
 #include "ops_ext.h"
@@ -159,7 +160,8 @@ std::tuple<Tensor, Tensor> moe_topk_op(const Tensor& logits, int64_t k, bool ren
 // Routed experts of this rank: pack -> grouped gate/up (SwiGLU) -> grouped down
 // -> weighted combine (+ gated shared expert).  Returns this rank's partial [T, H].
 Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const Tensor& gate_up, const Tensor& down,
-                      int64_t e0, const c10::optional<Tensor>& shared_y, const c10::optional<Tensor>& shared_gate) {
+                      int64_t e0, const c10::optional<Tensor>& shared_y, const c10::optional<Tensor>& shared_gate,
+                      double swiglu_limit) {
   check_bf16(x, "x");
   check_bf16(gate_up, "gate_up");
   check_bf16(down, "down");
@@ -207,6 +209,7 @@ Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const
   g.K = H;
   g.max_rows_per_group = T;
   g.swiglu = true;
+  g.swiglu_limit = (float)swiglu_limit;
   g.out = mbf(y1);
   g.ldo = I;
   g.status = status_dev_ptr();
@@ -216,6 +219,7 @@ Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const
   g.N = H;
   g.K = I;
   g.swiglu = false;
+  g.swiglu_limit = 0.f;
   g.out = mbf(y2);
   g.ldo = H;
   grouped_gemm(g, st);
@@ -237,12 +241,101 @@ Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const
   return out;
 }
 
+// ---------------------------------------------------------------------------
+// DeepSeek V4
+// ---------------------------------------------------------------------------
+std::tuple<Tensor, Tensor, Tensor> hc_pre_op(const Tensor& x, const Tensor& fn, const Tensor& scale, const Tensor& base,
+                                             int64_t iters, double eps, double norm_eps) {
+  check_bf16(x, "x");
+  check_f32(fn, "fn");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x [T, hc, dim] contiguous");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0), hc = (int)x.size(1), dim = (int)x.size(2), mix = (int)fn.size(0);
+  auto y = at::empty({T, dim}, x.options());
+  auto post = at::empty({T, hc}, x.options().dtype(at::kFloat));
+  auto comb = at::empty({T, hc, hc}, x.options().dtype(at::kFloat));
+  HcPreArgs a{};
+  a.x = cbf(x);
+  a.fn = fn.data_ptr<float>();
+  a.scale = scale.data_ptr<float>();
+  a.base = base.data_ptr<float>();
+  a.tokens = T;
+  a.hc = hc;
+  a.dim = dim;
+  a.mix_out = mix;
+  a.sinkhorn_iters = (int)iters;
+  a.eps = (float)eps;
+  a.norm_eps = (float)norm_eps;
+  a.y = mbf(y);
+  a.post = post.data_ptr<float>();
+  a.comb = comb.data_ptr<float>();
+  hc_pre(a, at::cuda::getCurrentCUDAStream().stream());
+  return {y, post, comb};
+}
+
+Tensor hc_post_op(const Tensor& x, const Tensor& resid, const Tensor& post, const Tensor& comb) {
+  check_bf16(x, "x");
+  check_bf16(resid, "resid");
+  TORCH_CHECK(x.is_contiguous() && resid.is_contiguous() && post.is_contiguous() && comb.is_contiguous(), "contig");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto out = at::empty_like(resid);
+  hc_post(cbf(x), cbf(resid), post.data_ptr<float>(), comb.data_ptr<float>(), (int)resid.size(0), (int)resid.size(1),
+          (int)resid.size(2), mbf(out), at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
+Tensor mqa_attn_op(const Tensor& q, const Tensor& kv, const Tensor& visible, int64_t q_per_seq, double scale,
+                   int64_t splits) {
+  check_bf16(q, "q");
+  check_bf16(kv, "kv");
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous(), "q [rows, H, D]");
+  TORCH_CHECK(kv.dim() == 3 && kv.stride(2) == 1 && kv.stride(1) == kv.size(2), "kv [B, T, D]");
+  TORCH_CHECK(visible.scalar_type() == at::kInt && visible.is_contiguous(), "visible int32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int rows = (int)q.size(0), H = (int)q.size(1), D = (int)q.size(2);
+  if (splits <= 0) splits = std::max<int64_t>(1, std::min<int64_t>(32, (2 * num_sms() + rows - 1) / std::max(rows, 1)));
+  auto ws = at::empty({(long)rows * splits * H * (2 + D)}, q.options().dtype(at::kFloat));
+  auto tickets = at::zeros({rows}, q.options().dtype(at::kInt));
+  auto out = at::empty_like(q);
+  MqaArgs a{};
+  a.q = cbf(q);
+  a.kv = cbf(kv);
+  a.kv_seq_stride = kv.stride(0);
+  a.visible = visible.data_ptr<int>();
+  a.rows = rows;
+  a.q_per_seq = (int)q_per_seq;
+  a.H = H;
+  a.D = D;
+  a.splits = (int)splits;
+  a.scale = (float)scale;
+  a.workspace = ws.data_ptr<float>();
+  a.tickets = tickets.data_ptr<int>();
+  a.out = mbf(out);
+  mqa_attn(a, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
+void rope_interleaved_op(Tensor x, const Tensor& cos, const Tensor& sin, const Tensor& pos) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x [rows, H, D] contiguous");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous(), "pos int32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  rope_interleaved(mbf(x), (int)x.size(0), (int)x.size(1), (int)x.size(2), (int)cos.size(1), cos.data_ptr<float>(),
+                   sin.data_ptr<float>(), pos.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
+}
+
 void register_ext_defs(torch::Library& m) {
+  m.def("rope_interleaved_(Tensor(a!) x, Tensor cos, Tensor sin, Tensor pos) -> ()");
   register_comm_defs(m);
   m.def("moe_topk(Tensor logits, int k, bool renorm, Tensor? bias, int mode, float route_scale) -> (Tensor, Tensor)");
   m.def(
       "moe_experts(Tensor x, Tensor w, Tensor ids, Tensor gate_up, Tensor down, int e0, Tensor? shared_y, "
-      "Tensor? shared_gate) -> Tensor");
+      "Tensor? shared_gate, float swiglu_limit) -> Tensor");
+  m.def(
+      "hc_pre(Tensor x, Tensor fn, Tensor scale, Tensor base, int sinkhorn_iters, float eps, float norm_eps) "
+      "-> (Tensor, Tensor, Tensor)");
+  m.def("hc_post(Tensor x, Tensor resid, Tensor post, Tensor comb) -> Tensor");
+  m.def("mqa_attn(Tensor q, Tensor kv, Tensor visible, int q_per_seq, float scale, int splits) -> Tensor");
   m.def(
       "deltanet_prefill(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) conv_ring, Tensor(b!) state, int start, "
       "Tensor valid_len, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, float eps) -> Tensor");
@@ -254,6 +347,10 @@ void register_ext_impls(torch::Library& m) {
   register_comm_impls(m);
   m.impl("moe_topk", &moe_topk_op);
   m.impl("moe_experts", &moe_experts_op);
+  m.impl("hc_pre", &hc_pre_op);
+  m.impl("hc_post", &hc_post_op);
+  m.impl("mqa_attn", &mqa_attn_op);
+  m.impl("rope_interleaved_", &rope_interleaved_op);
   m.impl("deltanet_prefill", &deltanet_prefill_op);
   m.impl("gqa_prefill", &gqa_prefill_op);
 }
