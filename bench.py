@@ -76,6 +76,7 @@ def main() -> None:
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (result marked invalid)")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--fp8", action="store_true", help="W8A16: 128x128 block-scaled E4M3 projection weights")
     ap.add_argument("--fused-comm", default="auto", choices=["auto", "on", "off"])
     args = ap.parse_args()
     if args.impl == "reference":
@@ -100,6 +101,9 @@ def main() -> None:
     max_seq = S + args.warmup + args.steps * 2 + 64
 
     model = Qwen36Model(cfg, comm, dev).init_random(seed=0)
+    if args.fp8:
+        model.quantize_fp8()
+        torch.cuda.empty_cache()
     if comm.size > 1 and args.fused_comm != "off":
         try:
             from bwn.parallel.fused import enable_fused_comm
@@ -188,7 +192,7 @@ def main() -> None:
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": round(value / BASELINE_TOK_S, 3),
-            "dtype": "bf16",
+            "dtype": "bf16 activations, fp8 e4m3 weights (128x128 block scales)" if args.fp8 else "bf16",
             "data": "synthetic (uniform-random prompt ids, random-init weights seed 0)",
             "config": {
                 "model": cfg.name if not args.layers else f"{cfg.name}-{args.layers}L (INVALID: debug layer count)",

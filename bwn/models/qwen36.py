@@ -106,9 +106,26 @@ class Qwen36Model(nn.Module):
                                                                    self.dtype).items()}
         return self
 
+    FP8_KEYS = ("in_proj", "out_proj", "qkv_proj", "o_proj", "gate_up", "down", "shared_gate_up", "shared_down")
+
+    def quantize_fp8(self, include_head: bool = True) -> "Qwen36Model":
+        """Convert the projection weights to 128x128 block-scaled E4M3 (W8A16):
+        the fp8 variant of the reference's ``--fp8-weights``
+        (``contrib/qwen3.6-27b/static_decode.py:283-319``)."""
+        from ..io.fp8 import FP8Weight
+        for L in self.layers:
+            for k in self.FP8_KEYS:
+                if k in L and torch.is_tensor(L[k]) and L[k].dim() == 2 and L[k].shape[1] % 16 == 0:
+                    L[k] = FP8Weight.from_dense(L[k])
+        if include_head:
+            self.g["lm_head"] = FP8Weight.from_dense(self.g["lm_head"])
+        return self
+
     def weight_bytes(self) -> int:
-        n = sum(v.numel() * v.element_size() for L in self.layers for v in L.values())
-        return n + sum(v.numel() * v.element_size() for v in self.g.values())
+        def nb(v):
+            return v.nbytes() if hasattr(v, "nbytes") and not torch.is_tensor(v) else v.numel() * v.element_size()
+        n = sum(nb(v) for L in self.layers for v in L.values())
+        return n + sum(nb(v) for v in self.g.values())
 
     # ----------------------------------------------------------------- state
     def new_state(self, batch: int, max_seq: int, ssm_dtype=torch.float32) -> Qwen36State:
@@ -217,7 +234,7 @@ class Qwen36Model(nn.Module):
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         """Full-vocab logits (gathered across vocab shards)."""
-        local = O.linear_f32(h, self.g["lm_head"]) if h.is_cuda else h.float() @ self.g["lm_head"].float().t()
+        local = O.linear_f32(h, self.g["lm_head"])
         return self.comm.all_gather_last(local)
 
     def decode_step(self, tokens: torch.Tensor, st: Qwen36State) -> torch.Tensor:

@@ -35,36 +35,53 @@ def deinterleave_gate_up(w: torch.Tensor, block: int = 16):
 
 
 # --------------------------------------------------------------------------
-# GEMMs
+# GEMMs (a weight is a bf16 [N, K] tensor or an FP8Weight: W8A16, 128x128 blocks)
 # --------------------------------------------------------------------------
-def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def _is_fp8(w) -> bool:
+    return hasattr(w, "w8") and hasattr(w, "scales")
+
+
+def _dense(w):
+    return w.dequant() if _is_fp8(w) else w
+
+
+def linear(x: torch.Tensor, w) -> torch.Tensor:
     """``x @ w.T`` (bf16 in/out, fp32 accumulate) on the tcgen05 GEMM."""
     if x.is_cuda:
+        if _is_fp8(w):
+            return ops().linear_w8(x, w.w8, w.scales, EPI_BF16, None)
         return ops().linear(x, w)
-    return ref.linear(x, w)
+    return ref.linear(x, _dense(w).to(x.dtype))
 
 
-def linear_f32(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def linear_f32(x: torch.Tensor, w) -> torch.Tensor:
     if x.is_cuda:
+        if _is_fp8(w):
+            return ops().linear_w8(x, w.w8, w.scales, EPI_F32, None)
         return ops().linear_f32(x, w)
-    return x.float() @ w.float().t()
+    return x.float() @ _dense(w).float().t()
 
 
-def linear_swiglu(x: torch.Tensor, w_il: torch.Tensor) -> torch.Tensor:
+def linear_swiglu(x: torch.Tensor, w_il) -> torch.Tensor:
     """``silu(x @ Wg.T) * (x @ Wu.T)`` with the block-16 interleaved weight."""
     if x.is_cuda:
+        if _is_fp8(w_il):
+            return ops().linear_w8(x, w_il.w8, w_il.scales, EPI_SWIGLU, None)
         return ops().linear_swiglu(x, w_il)
+    w_il = _dense(w_il)
     y = x.float() @ w_il.float().t()
     n2 = y.shape[-1]
     y = y.reshape(*y.shape[:-1], n2 // 32, 2, 16)
     return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*y.shape[:-3], n2 // 2).to(x.dtype)
 
 
-def linear_residual(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
+def linear_residual(x: torch.Tensor, w, resid: torch.Tensor) -> torch.Tensor:
     """``resid + x @ w.T`` with the add fused into the GEMM epilogue."""
     if x.is_cuda:
+        if _is_fp8(w):
+            return ops().linear_w8(x, w.w8, w.scales, EPI_RESID, resid)
         return ops().linear_residual(x, w, resid)
-    return (x.float() @ w.float().t() + resid.float()).to(x.dtype)
+    return (x.float() @ _dense(w).float().t() + resid.float()).to(x.dtype)
 
 
 def linear_kn(x: torch.Tensor, w_kn: torch.Tensor) -> torch.Tensor:

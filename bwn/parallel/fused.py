@@ -71,6 +71,9 @@ class FusedComm:
                                 eps: float) -> torch.Tensor:
         """``x += all_reduce(a @ w.T)`` across ranks; returns ``rmsnorm(x)*(1+norm_w)``."""
         o = ops()
+        if hasattr(w, "w8"):  # FP8 weight: W8A16 GEMM, then the multicast reduction
+            from .. import ops as O
+            return self.allreduce_add_norm(O.linear(a, w), x, norm_w, eps)
         o.gemm_mcred(a, w, self.mc_ar, self.buf_floats, w.shape[0], self.peer_flags_ar, self.state, self.rank)
         return o.ar_add_norm(self.local_ar, self.buf_floats, self.peer_flags_ar[self.rank], self.world, self.state,
                              x, norm_w, eps, self.timeout_s)

@@ -12,6 +12,7 @@
 #include <utility>
 
 #include "common/host.h"
+#include "kernels/gemm_w8.h"
 #include "kernels/launch.h"
 #include "ops_ext.h"
 
@@ -199,6 +200,57 @@ Tensor linear_kn(const Tensor& x, const Tensor& w_kn) {
 Tensor matmul_tn(const Tensor& a_km, const Tensor& b_kn, bool f32_out) {
   auto out = at::empty({a_km.size(1), b_kn.size(1)}, a_km.options().dtype(f32_out ? at::kFloat : at::kBFloat16));
   gemm_into(a_km, true, b_kn, true, out);
+  return out;
+}
+
+// FP8 W8A16: out[T, N] = x[T, K] . dequant(w8[N, K], scales[N/128, K/128])^T
+void linear_w8_into(const Tensor& x, const Tensor& w8, const Tensor& scales, const Tensor& out, int64_t epi,
+                    const c10::optional<Tensor>& resid) {
+  check_bf16(x, "x");
+  check_rowmajor(x, "x");
+  check_cuda(w8, "w8");
+  TORCH_CHECK(w8.element_size() == 1 && w8.dim() == 2 && w8.stride(1) == 1, "w8 must be a [N, K] 8-bit matrix");
+  check_f32(scales, "scales");
+  TORCH_CHECK(scales.dim() == 2 && scales.is_contiguous(), "scales [N/128, K/128]");
+  TORCH_CHECK(x.size(1) == w8.size(1), "linear_w8: K mismatch");
+  TORCH_CHECK(scales.size(0) == (w8.size(0) + 127) / 128 && scales.size(1) == (w8.size(1) + 127) / 128,
+              "linear_w8: scales must be [ceil(N/128), ceil(K/128)]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0), N = (int)w8.size(0), K = (int)x.size(1);
+  if (T == 0) return;
+  GemmW8Problem p;
+  p.A = w8.data_ptr();
+  p.lda = w8.stride(0);
+  p.scales = scales.data_ptr<float>();
+  p.lds = (int)scales.size(1);
+  p.B = x.data_ptr();
+  p.ldb = x.stride(0);
+  p.M = N;
+  p.N = T;
+  p.K = K;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.epi = (int)epi;
+  p.status = status_dev_ptr();
+  if (epi == kEpiResid) {
+    TORCH_CHECK(resid.has_value(), "linear_w8: residual epilogue needs resid");
+    p.resid = bf(*resid);
+    p.ldr = resid->stride(0);
+  }
+  const int sms = num_sms();
+  Scratch& s = scratch_for(x, 4L * sms * 128 * 128, 2 * sms);
+  p.workspace = s.ws.data_ptr<float>();
+  p.workspace_floats = s.ws.numel();
+  p.tickets = s.tickets.data_ptr<int>();
+  p.tickets_len = (int)s.tickets.numel();
+  gemm_w8(p, at::cuda::getCurrentCUDAStream().stream());
+}
+
+Tensor linear_w8(const Tensor& x, const Tensor& w8, const Tensor& scales, int64_t epi,
+                 const c10::optional<Tensor>& resid) {
+  const int64_t N = epi == kEpiSwiGLU ? w8.size(0) / 2 : w8.size(0);
+  auto out = at::empty({x.size(0), N}, x.options().dtype(epi == kEpiF32 ? at::kFloat : at::kBFloat16));
+  linear_w8_into(x, w8, scales, out, epi, resid);
   return out;
 }
 
@@ -421,6 +473,7 @@ TORCH_LIBRARY(bwn, m) {
   m.def("linear_residual(Tensor x, Tensor w, Tensor resid) -> Tensor");
   m.def("linear_out(Tensor x, Tensor w, Tensor(a!) out, int epi, Tensor? resid) -> ()");
   m.def("linear_kn(Tensor x, Tensor w_kn) -> Tensor");
+  m.def("linear_w8(Tensor x, Tensor w8, Tensor scales, int epi, Tensor? resid) -> Tensor");
   m.def("matmul_tn(Tensor a_km, Tensor b_kn, bool f32_out) -> Tensor");
   m.def("rms_norm(Tensor x, Tensor w, float eps, bool one_plus) -> Tensor");
   m.def("add_rms_norm(Tensor x, Tensor(a!) residual, Tensor w, float eps) -> Tensor");
@@ -443,6 +496,7 @@ TORCH_LIBRARY_IMPL(bwn, CUDA, m) {
   m.impl("linear_residual", &bwn::linear_residual);
   m.impl("linear_out", &bwn::linear_out);
   m.impl("linear_kn", &bwn::linear_kn);
+  m.impl("linear_w8", &bwn::linear_w8);
   m.impl("matmul_tn", &bwn::matmul_tn);
   m.impl("rms_norm", &bwn::rms_norm_op);
   m.impl("add_rms_norm", &bwn::add_rms_norm_op);

@@ -179,3 +179,27 @@ def test_gqa_decode(B, QH, KVH, S, plen):
     # a second call (tickets re-armed) gives the same answer
     out2 = O.gqa_decode(qg, k_new, v_new, qn, kn, cos, sin, kc, vc, pos)
     assert _rel(out2, out) < 1e-3
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 512, 1024), (32, 5120, 6144), (32, 2176 * 2, 5120), (7, 384, 256),
+                                   (100, 1024, 2048)])
+def test_linear_w8(T, N, K):
+    """FP8 W8A16 with 128x128 block scales vs the fp32 product with dequantised weights."""
+    from bwn.io.fp8 import FP8Weight
+    x = torch.randn(T, K, device=dev).bfloat16()
+    w = torch.randn(N, K, device=dev) * 0.05
+    w[: N // 2] *= 4.0  # blocks with different scales
+    fw = FP8Weight.from_dense(w)
+    wd = fw.dequant().cuda()
+    ref = x.float() @ wd.t()
+    assert _rel(O.linear(x, fw), ref) < 1e-2
+    assert _rel(O.linear_f32(x, fw), ref) < 1e-2
+    r = torch.randn(T, N, device=dev).bfloat16()
+    assert _rel(O.linear_residual(x, fw, r), ref + r.float()) < 1e-2
+    if N % 32 == 0:
+        g, u = w[: N // 2], w[N // 2:]
+        fil = FP8Weight.from_dense(O.interleave_gate_up(g, u))
+        gd, ud = O.deinterleave_gate_up(fil.dequant().cuda())
+        want = torch.nn.functional.silu(x.float() @ gd.t()) * (x.float() @ ud.t())
+        assert _rel(O.linear_swiglu(x, fil), want) < 2e-2
+    O.check_status("linear_w8")
