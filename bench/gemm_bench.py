@@ -38,6 +38,19 @@ def bench(fn, iters=20):
 
 
 def main():
+    import sys as _s
+    if "--fp8" in _s.argv:
+        from bwn.io.fp8 import FP8Weight
+        for M, N, K in SHAPES[:10]:
+            x = torch.randn(M, K, device="cuda").bfloat16()
+            w = (torch.randn(N, K, device="cuda") * 0.02)
+            fw = FP8Weight.from_dense(w)
+            wb = w.bfloat16()
+            t8 = bench(lambda: O.linear(x, fw))
+            t16 = bench(lambda: O.linear(x, wb))
+            print(json.dumps({"M": M, "N": N, "K": K, "w8_us": round(t8 * 1e3, 1), "bf16_us": round(t16 * 1e3, 1),
+                              "w8_GBps": round(N * K / t8 / 1e6, 1), "bf16_GBps": round(2 * N * K / t16 / 1e6, 1)}))
+        return
     for M, N, K in SHAPES:
         x = torch.randn(M, K, device="cuda").bfloat16()
         w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()

@@ -20,7 +20,7 @@ from bwn.ops import reference as R  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", required=True, choices=["linear", "swiglu", "gqa", "deltanet"])
+    ap.add_argument("--op", required=True, choices=["linear", "linear_w8", "swiglu", "gqa", "deltanet"])
     ap.add_argument("--M", type=int, default=32)
     ap.add_argument("--N", type=int, default=5120)
     ap.add_argument("--K", type=int, default=6144)
@@ -34,7 +34,13 @@ def main():
     a = ap.parse_args()
     dev = "cuda"
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    if a.op in ("linear", "swiglu"):
+    if a.op == "linear_w8":
+        from bwn.io.fp8 import FP8Weight
+        x = torch.randn(a.M, a.K, device=dev).bfloat16()
+        fw = FP8Weight.from_dense(torch.randn(a.N, a.K, device=dev) * 0.02)
+        fn = lambda: O.linear(x, fw)  # noqa: E731
+        nbytes = a.N * a.K
+    elif a.op in ("linear", "swiglu"):
         x = torch.randn(a.M, a.K, device=dev).bfloat16()
         w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
         fn = (lambda: O.linear(x, w)) if a.op == "linear" else (lambda: O.linear_swiglu(x, w))

@@ -7,14 +7,19 @@
 // Orientation is swap-AB: the fp8 weight is the 128-row MMA "A" operand, the
 // bf16 token rows are "B", the store is transposed.  Per 128-deep K block:
 //   warp 0      TMA: fp8 weight tile [128 x 128 B] (SW128) + bf16 token tile
-//   warps 6-13  converters: fp8 e4m3 -> bf16 with the block scale folded in,
-//               written straight into the SW128 K-major layout the MMA reads
-//               (bits of e4m3 placed in bf16 position, times 2^120 * scale:
-//               exact for normals and subnormals), then fence.proxy.async
-//   warp 1      tcgen05.mma kind::f16 (bf16 x bf16 -> fp32 TMEM), 8 per block
+//   warps 6-13  converters: the fp8 weight tile to f16 with the hardware
+//               e4m3x2 -> f16x2 conversion (exact for every e4m3 value), and
+//               the bf16 token tile to f16 scaled by this tile's 128x128 block
+//               scale (W x^T = w8 (s x)^T: each CTA owns one scale block row),
+//               both written in the SW128 K-major layout the MMA reads, then
+//               fence.proxy.async
+//   warp 1      tcgen05.mma kind::f16 (f16 x f16 -> fp32 TMEM), 8 per block
 //   warps 2-5   epilogue (shared with the bf16 GEMM: bf16 / residual /
 //               SwiGLU / fp32 / NVLS multimem reduction)
 // Split-K and the completion signalling are the same as the bf16 GEMM.
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
 #include "common/host.h"
 #include "common/sm100.cuh"
 #include "kernels/gemm_epilogue.cuh"
@@ -28,19 +33,27 @@ constexpr int kW8Threads = 448;
 
 template <int BN>
 struct W8Cfg {
-  static constexpr int kA8 = kW8BM * kW8BK;        // 16 KB fp8
-  static constexpr int kA16 = kW8BM * kW8BK * 2;   // 32 KB bf16 (two SW128 boxes)
-  static constexpr int kB = BN * kW8BK * 2;        // bf16 tokens (two SW128 boxes)
-  static constexpr int kStage = kA8 + kA16 + kB;
-  static constexpr int kStagesRaw = (200 * 1024) / kStage;
-  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kA8 = kW8BM * kW8BK;        // 16 KB fp8 weight tile
+  static constexpr int kA16 = kW8BM * kW8BK * 2;   // 32 KB f16 weight tile (two SW128 boxes)
+  static constexpr int kB = BN * kW8BK * 2;        // token tile (two SW128 boxes), bf16 in / f16 out
+  static constexpr int kL = kA8 + kB;              // TMA ring stage
+  static constexpr int kC = kA16 + kB;             // converted ring stage
+  static constexpr int kNC = (BN <= 32) ? 4 : 2;
+  static constexpr int kNLRaw = (216 * 1024 - kNC * kC) / kL;
+  static constexpr int kNL = kNLRaw > 8 ? 8 : kNLRaw;
   static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
-  static constexpr int kSmem = kStages * kStage + 1024 + 512;
+  static constexpr int kMaxKb = 512;  // scales staged per unit
+  static constexpr int kSmem = kNL * kL + kNC * kC + 1024 + 512 + kMaxKb * 4;
 };
 
-// fp8 e4m3 byte -> fp32 value / 2^120 (bit placement only; caller rescales)
-__device__ __forceinline__ float e4m3_raw(uint32_t byte) {
-  return __uint_as_float(((byte & 0x80u) << 24) | ((byte & 0x7Fu) << 20));
+// four e4m3 bytes -> two f16x2 words (bytes 0,1 -> lo; bytes 2,3 -> hi), exactly
+__device__ __forceinline__ void e4m3x4_to_f16x4(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
 }
 
 template <int BN, int EPI>
@@ -48,25 +61,32 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args,
                    const float* __restrict__ scales, int lds) {
   using C = W8Cfg<BN>;
-  constexpr int S = C::kStages;
+  constexpr int S = C::kNL;   // TMA ring depth
+  constexpr int SC = C::kNC;  // converted ring depth
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sA8 = smem;
-  uint8_t* sA16 = sA8 + S * C::kA8;
-  uint8_t* sB = sA16 + S * C::kA16;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + S * C::kB);
-  uint64_t* cvt_bar = full_bar + S;
-  uint64_t* empty_bar = cvt_bar + S;
-  uint64_t* tfull_bar = empty_bar + S;
+  uint8_t* sA8 = smem;                    // [S][kA8]
+  uint8_t* sB = sA8 + S * C::kA8;         // [S][kB]   bf16 tokens
+  uint8_t* sA16 = sB + S * C::kB;         // [SC][kA16] f16 weights
+  uint8_t* sB16 = sA16 + SC * C::kA16;    // [SC][kB]   f16 tokens * scale
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB16 + SC * C::kB);  // [S]  TMA landed
+  uint64_t* lempty_bar = full_bar + S;    // [S]  converters done reading
+  uint64_t* cvt_bar = lempty_bar + S;     // [SC] converted slot ready
+  uint64_t* empty_bar = cvt_bar + SC;     // [SC] MMA done with the slot
+  uint64_t* tfull_bar = empty_bar + SC;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* ticket_bcast = reinterpret_cast<int*>(tmem_slot + 2);
+  float* s_scale = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full_bar) + 512);  // [kMaxKb]
   const int warp = warp_id(), lane = lane_id();
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_bar[i], 1);
+      mbar_init(&lempty_bar[i], 256);
+    }
+    for (int i = 0; i < SC; ++i) {
       mbar_init(&cvt_bar[i], 256);
       mbar_init(&empty_bar[i], 1);
     }
@@ -100,7 +120,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
         const int kb0 = sp * args.kb_per_split, kb1 = min(args.num_kb, kb0 + args.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty_bar[s], ph ^ 1)) {
+          if (!mbar_wait(&lempty_bar[s], ph ^ 1)) {
             set_status(args.status, kStatusMbarTimeout);
             *abort_flag = 1;
             break;
@@ -125,21 +145,26 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     // ------------------------------ converters ------------------------------
     const int c = threadIdx.x - 6 * 32;  // 0..255
     const int r = c >> 1, half = c & 1;
-    int s = 0;
-    uint32_t ph = 0;
+    int s = 0, sc2 = 0;
+    uint32_t ph = 0, ph2 = 0;
     for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
       const int tile = u / args.splits, sp = u % args.splits;
       const int tm = tile % args.tiles_m;
       const int kb0 = sp * args.kb_per_split, kb1 = min(args.num_kb, kb0 + args.kb_per_split);
+      // stage this unit's block scales once (a per-block global load would put
+      // an L2 round trip in front of every conversion)
+      asm volatile("bar.sync 2, 256;" ::: "memory");
+      for (int j = c; j < kb1 - kb0; j += 256) s_scale[j] = scales[(long)tm * lds + kb0 + j];
+      asm volatile("bar.sync 2, 256;" ::: "memory");
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&full_bar[s], ph)) {
+        if (!mbar_wait(&full_bar[s], ph) || !mbar_wait(&empty_bar[sc2], ph2 ^ 1)) {
           set_status(args.status, kStatusMbarTimeout);
           *abort_flag = 1;
           break;
         }
-        const float sc = scales[(long)tm * lds + kb] * 1.329227995784916e36f;  // * 2^120
+        const float sc = s_scale[kb - kb0];
         const uint8_t* a8 = sA8 + s * C::kA8 + r * 128;
-        uint8_t* a16 = sA16 + s * C::kA16;
+        uint8_t* a16 = sA16 + sc2 * C::kA16;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int cc = half * 4 + q;  // 16-byte fp8 chunk = 16 k
@@ -147,27 +172,40 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           const uint32_t w[4] = {raw8.x, raw8.y, raw8.z, raw8.w};
           uint32_t o[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            o[2 * j] = pack_bf16x2(e4m3_raw(w[j] & 0xFFu) * sc, e4m3_raw((w[j] >> 8) & 0xFFu) * sc);
-            o[2 * j + 1] = pack_bf16x2(e4m3_raw((w[j] >> 16) & 0xFFu) * sc, e4m3_raw(w[j] >> 24) * sc);
-          }
-          // k = 16*cc .. 16*cc+15 -> bf16 box t = cc/4, 16-byte chunks c8 and c8+1
+          for (int j = 0; j < 4; ++j) e4m3x4_to_f16x4(w[j], o[2 * j], o[2 * j + 1]);
+          // k = 16*cc .. 16*cc+15 -> f16 box t = cc/4, 16-byte chunks c8 and c8+1
           const int t = cc >> 2, c8 = (cc & 3) * 2;
           uint8_t* rowp = a16 + t * (kW8BM * 128) + r * 128;
           *reinterpret_cast<uint4*>(rowp + ((c8 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           *reinterpret_cast<uint4*>(rowp + (((c8 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
+        {  // token tile: bf16 -> f16 * block scale, same swizzled positions
+          const uint32_t* b32 = reinterpret_cast<const uint32_t*>(sB + s * C::kB);
+          uint32_t* o32 = reinterpret_cast<uint32_t*>(sB16 + sc2 * C::kB);
+          for (int i = c; i < C::kB / 4; i += 256) {
+            const uint32_t v = b32[i];
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+            __half2 h = __floats2half2_rn(f.x * sc, f.y * sc);
+            o32[i] = *reinterpret_cast<uint32_t*>(&h);
+          }
+        }
         fence_async_smem();
-        mbar_arrive(&cvt_bar[s]);
+        mbar_arrive(&cvt_bar[sc2]);
+        mbar_arrive(&lempty_bar[s]);
         if (++s == S) {
           s = 0;
           ph ^= 1;
+        }
+        if (++sc2 == SC) {
+          sc2 = 0;
+          ph2 ^= 1;
         }
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      const uint32_t idesc = idesc_bf16_f32(kW8BM, BN);
+      // kind::f16 with A = B = f16 (format 0), D = f32
+      const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kW8BM >> 4) << 24);
       int s = 0, i = 0;
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x, ++i) {
@@ -191,13 +229,13 @@ __global__ void __launch_bounds__(kW8Threads, 1)
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             const uint64_t da = smem_desc_sw128(smem_u32(sA16 + s * C::kA16 + t * (kW8BM * 128)));
-            const uint64_t db = smem_desc_sw128(smem_u32(sB + s * C::kB + t * (BN * 128)));
+            const uint64_t db = smem_desc_sw128(smem_u32(sB16 + s * C::kB + t * (BN * 128)));
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
               umma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (kb > kb0 || t > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);
-          if (++s == S) {
+          if (++s == SC) {
             s = 0;
             ph ^= 1;
           }
@@ -359,6 +397,7 @@ void gemm_w8(const GemmW8Problem& p, cudaStream_t stream) {
   }
   a.kb_per_split = (a.num_kb + splits - 1) / splits;
   a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
+  BWN_CHECK(a.kb_per_split <= 512, "gemm_w8: K too large for the staged scales (%d blocks)", a.kb_per_split);
   a.out = p.out;
   a.ldo = p.ldo;
   a.resid = p.resid;
