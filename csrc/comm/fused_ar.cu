@@ -21,6 +21,7 @@
 // hanging the GPU.
 #include "comm/fused.h"
 #include "common/host.h"
+#include "common/launch.cuh"
 #include "common/sm100.cuh"
 
 namespace bwn {
@@ -55,6 +56,8 @@ __device__ __forceinline__ void signal_done(const CommSignal& sig) {
 
 __global__ void __launch_bounds__(256) mc_red_signal_kernel(const __nv_bfloat16* __restrict__ x, long ldx, int rows,
                                                             int cols, float* mc_base, CommSignal sig) {
+  pdl_trigger();
+  pdl_wait();
   float* mc = mc_base + (long)((*sig.sel) & 1) * sig.buf_stride;
   const long n = (long)rows * cols;
   for (long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 2; i < n; i += (long)gridDim.x * blockDim.x * 2) {
@@ -74,6 +77,8 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(float* local_base, lon
                                                           const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                                           long ldo, int cols, float eps, int* status,
                                                           unsigned long long limit_ns) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   __shared__ float red[8];
   if (threadIdx.x == 0) wait_flags(flags, world, (unsigned)(*epoch), status, limit_ns);
@@ -113,6 +118,8 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(float* local_base, lon
 }
 
 __global__ void greedy_allmax_kernel(GreedyArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t* keys = a.keys;
   const int rows = a.rows, world = a.world, rank = a.rank;
   int64_t* const* peer_slots = a.peer_slots;
@@ -155,21 +162,18 @@ void mc_red_signal(const __nv_bfloat16* x, long ldx, int rows, int cols, float* 
   long n = (long)rows * cols / 2;
   int grid = (int)std::min<long>((n + 255) / 256, num_sms());
   if (grid < 1) grid = 1;
-  mc_red_signal_kernel<<<grid, 256, 0, st>>>(x, ldx, rows, cols, mc_base, sig);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(mc_red_signal_kernel, dim3(grid), dim3(256), 0, st, x, ldx, rows, cols, mc_base, sig);
 }
 
 void ar_add_norm(const ArNormArgs& a, cudaStream_t st) {
   BWN_CHECK(a.cols <= 256 * 32, "ar_add_norm: hidden too wide");
-  ar_add_norm_kernel<<<a.rows, 256, 0, st>>>(a.local_base, a.buf_stride, a.sel, a.flags, a.world, a.epoch, a.resid,
-                                             a.ldr, a.w, a.out, a.ldo, a.cols, a.eps, a.status, a.limit_ns);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(ar_add_norm_kernel, dim3(a.rows), dim3(256), 0, st, a.local_base, a.buf_stride, a.sel, a.flags, a.world,
+           a.epoch, a.resid, a.ldr, a.w, a.out, a.ldo, a.cols, a.eps, a.status, a.limit_ns);
 }
 
 void greedy_allmax(const GreedyArgs& a, cudaStream_t st) {
   BWN_CHECK(a.world >= 1 && a.world <= 8, "greedy_allmax: world size 1..8");
-  greedy_allmax_kernel<<<1, 256, 0, st>>>(a);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(greedy_allmax_kernel, dim3(1), dim3(256), 0, st, a);
 }
 
 }  // namespace bwn

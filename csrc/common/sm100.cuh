@@ -344,3 +344,12 @@ __device__ __forceinline__ void st_relaxed_sys_f32(float* p, float v) {
   asm volatile("st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 }  // namespace bwn
+
+namespace bwn {
+// Programmatic dependent launch: let the next kernel in the stream begin
+// launching (effective once every CTA of this grid has executed it) / wait until
+// the previous grid has completed and its memory is visible.  Both are no-ops
+// for kernels launched without the PDL attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+}  // namespace bwn

@@ -19,6 +19,7 @@
 
 #include "common/host.h"
 #include "common/sm100.cuh"
+#include "common/launch.cuh"
 #include "kernels/launch.h"
 
 namespace cg = cooperative_groups;
@@ -33,6 +34,8 @@ constexpr int kDnCols = kDnDv / kDnNJ;  // 32
 template <typename StateT>
 __global__ void __cluster_dims__(kDnNJ, 1, 1) __launch_bounds__(128)
     deltanet_decode_kernel(DeltaNetDecodeArgs p) {
+  pdl_trigger();
+  pdl_wait();
   cg::cluster_group cluster = cg::this_cluster();
   const int jb = blockIdx.x;  // column block == rank in cluster
   const int h = blockIdx.y;   // local V head
@@ -172,11 +175,10 @@ __global__ void __cluster_dims__(kDnNJ, 1, 1) __launch_bounds__(128)
 void deltanet_decode(const DeltaNetDecodeArgs& p, cudaStream_t stream) {
   dim3 grid(kDnNJ, p.v_heads, p.batch);
   if (p.state_bf16) {
-    deltanet_decode_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(p);
+    launch_k(deltanet_decode_kernel<__nv_bfloat16>, grid, dim3(128), 0, stream, p);
   } else {
-    deltanet_decode_kernel<float><<<grid, 128, 0, stream>>>(p);
+    launch_k(deltanet_decode_kernel<float>, grid, dim3(128), 0, stream, p);
   }
-  BWN_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace bwn

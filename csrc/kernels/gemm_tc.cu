@@ -19,6 +19,7 @@
 // SwiGLU over gate/up rows interleaved in blocks of 16, fp32 store.
 #include "common/host.h"
 #include "common/sm100.cuh"
+#include "common/launch.cuh"
 #include "kernels/gemm_epilogue.cuh"
 
 namespace bwn {
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -88,6 +90,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int units = tiles * args.splits;
   constexpr bool A_MN = (MAJ & 1) != 0, B_MN = (MAJ & 2) != 0;
   const uint32_t idesc = idesc_bf16_f32_major(kBM, BN, A_MN, B_MN);
+  if (warp != 0) pdl_wait();  // the producer waits after prefetching static weight tiles
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -97,12 +100,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued_mask = 0, issued_ph = 0;  // per stage: issued at least once / parity of last issue
+      // Weight prefetch: when B is the activation (swap-AB decode), the first
+      // stages' A tiles (static weights) are issued before waiting for the
+      // previous kernel, so the weight stream overlaps its tail.
+      int pre = 0, pre_n = 0, kb00 = 0, tn0 = 0;
+      if (TRANS && !A_MN && !B_MN && (int)blockIdx.x < units) {
+        const int sp0 = blockIdx.x % args.splits, tile0 = blockIdx.x / args.splits;
+        const int tm0 = tile0 % args.tiles_m;
+        tn0 = tile0 / args.tiles_m;
+        kb00 = sp0 * args.kb_per_split;
+        const int kb01 = min(args.num_kb, kb00 + args.kb_per_split);
+        pre = pre_n = min(S, kb01 - kb00);
+        for (int j = 0; j < pre; ++j) {
+          mbar_arrive_expect_tx(&full_bar[j], C::kStageBytes);
+          tma_load_2d_hint(&tmA, &full_bar[j], sA + j * C::kABytes, (kb00 + j) * kBK, tm0 * kBM, polA);
+          issued_mask |= 1u << j;
+        }
+      }
+      pdl_wait();
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         const int tile = u / args.splits, sp = u % args.splits;
         const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
         const int kb0 = sp * args.kb_per_split;
         const int kb1 = min(args.num_kb, kb0 + args.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (pre > 0) {  // A already in flight for this stage: only B remains
+            tma_load_2d_hint(&tmB, &full_bar[s], sB + s * C::kBBytes, kb * kBK, tn * BN, polB);
+            issued_mask |= 1u << s;
+            issued_ph = (issued_ph & ~(1u << s)) | (ph << s);
+            --pre;
+            if (++s == S) {
+              s = 0;
+              ph ^= 1;
+            }
+            continue;
+          }
           if (!mbar_wait(&empty_bar[s], ph ^ 1)) {
             set_status(args.status, kStatusMbarTimeout);
             *abort_flag = 1;
@@ -132,7 +164,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       if (*abort_flag) {
-        // bounded wait for this CTA's own copies still in flight
+        // complete the transaction count of prefetched stages that never got
+        // their B tile, then a bounded wait for this CTA's own copies in flight
+        for (int j = pre_n - pre; j < pre_n; ++j)
+          tma_load_2d_hint(&tmB, &full_bar[j], sB + j * C::kBBytes, (kb00 + j) * kBK, tn0 * BN, polB);
         for (int j = 0; j < S; ++j)
           if (issued_mask & (1u << j)) mbar_wait(&full_bar[j], (issued_ph >> j) & 1u, 100000000ull);
       }
@@ -316,8 +351,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
     BWN_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
     attr_set[dev & 63] = true;
   }
-  k<<<grid, kGemmThreads, C::kSmemBytes, stream>>>(ta, tb, a);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(k, dim3(grid), dim3(kGemmThreads), C::kSmemBytes, stream, ta, tb, a);
 }
 
 template <int EPI, bool TRANS>

@@ -22,6 +22,7 @@
 
 #include "common/host.h"
 #include "common/sm100.cuh"
+#include "common/launch.cuh"
 #include "kernels/gemm_epilogue.cuh"
 #include "kernels/gemm_w8.h"
 
@@ -103,9 +104,11 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
   const int tiles = args.tiles_m * args.tiles_n;
   const int units = tiles * args.splits;
@@ -356,8 +359,7 @@ static void launch_w8(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     BWN_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
     set[dev & 63] = true;
   }
-  k<<<grid, kW8Threads, C::kSmem, st>>>(ta, tb, a, scales, lds);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(k, dim3(grid), dim3(kW8Threads), C::kSmem, st, ta, tb, a, scales, lds);
 }
 
 template <int EPI>

@@ -24,6 +24,7 @@
 
 #include "common/host.h"
 #include "common/sm100.cuh"
+#include "common/launch.cuh"
 #include "kernels/launch.h"
 
 namespace bwn {
@@ -64,6 +65,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sAlpha + G + ((used & 1) ? 1 : 2));  // [2]
   int* sTicket = reinterpret_cast<int*>(bar + 2);
 
+  pdl_trigger();
+  pdl_wait();
   const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int pos = p.positions[b];
@@ -346,8 +349,7 @@ static void launch_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const GqaDe
     set[dev & 63] = true;
   }
   dim3 grid(p.splits, p.kv_heads, p.batch);
-  gqa_decode_kernel<G><<<grid, kGThreads, smem, st>>>(tk, tv, p);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(gqa_decode_kernel<G>, grid, dim3(kGThreads), smem, st, tk, tv, p);
 }
 
 void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {

@@ -6,6 +6,7 @@
 // sharded greedy a single int64 max all-reduce (static_decode_35b.py:1534-1564).
 #include "common/host.h"
 #include "common/sm100.cuh"
+#include "common/launch.cuh"
 #include "kernels/launch.h"
 
 namespace bwn {
@@ -16,6 +17,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
                                                        __nv_bfloat16* __restrict__ resid, long ldr,
                                                        const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                                        long ldo, int cols, float eps, bool one_plus) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int t = threadIdx.x;
   const int nvec = cols >> 3;
@@ -88,7 +91,8 @@ static void launch_norm(const __nv_bfloat16* x, long ldx, __nv_bfloat16* resid, 
   if (rows == 0) return;
 #define BWN_NORM_CASE(V)                                                                              \
   case V:                                                                                             \
-    rms_norm_kernel<ADD, V><<<rows, threads, 0, st>>>(x, ldx, resid, ldr, w, out, ldo, cols, eps, one_plus); \
+    launch_k(rms_norm_kernel<ADD, V>, dim3(rows), dim3(threads), 0, st, x, ldx, resid, ldr, w, out, ldo, cols, eps, \
+             one_plus);                                                                                \
     break;
   switch (vpt) {
     BWN_NORM_CASE(1)
@@ -118,6 +122,8 @@ void add_rms_norm(const __nv_bfloat16* x, long ldx, __nv_bfloat16* residual, lon
 // ---------------------------------------------------------------------------
 __global__ void embedding_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, long rows,
                                  int cols, long offset, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int tok = blockIdx.x;
   const long id = (long)ids[tok] - offset;
   const bool in = id >= 0 && id < rows;
@@ -133,7 +139,7 @@ void embedding(const int* ids, int n, const __nv_bfloat16* table, long rows, int
                __nv_bfloat16* out, cudaStream_t stream) {
   BWN_CHECK(cols % 8 == 0, "embedding: hidden must be a multiple of 8");
   if (n == 0) return;
-  embedding_kernel<<<n, 128, 0, stream>>>(ids, table, rows, cols, offset, out);
+  launch_k(embedding_kernel, dim3(n), dim3(128), 0, stream, ids, table, rows, cols, offset, out);
   BWN_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -150,6 +156,8 @@ __device__ __forceinline__ unsigned long long pack_key(float v, long id) {
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logits, long ld, int cols, long id_offset,
                                                       int64_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const T* p = logits + (long)row * ld;
   unsigned long long best = 0;
@@ -176,25 +184,27 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logi
 void argmax_packed(const float* logits, long ld, int rows, int cols, long id_offset, int64_t* out,
                    cudaStream_t stream) {
   if (rows == 0) return;
-  argmax_kernel<float><<<rows, 1024, 0, stream>>>(logits, ld, cols, id_offset, out);
+  launch_k(argmax_kernel<float>, dim3(rows), dim3(1024), 0, stream, logits, ld, cols, id_offset, out);
   BWN_CUDA_CHECK(cudaGetLastError());
 }
 
 void argmax_packed_bf16(const __nv_bfloat16* logits, long ld, int rows, int cols, long id_offset, int64_t* out,
                         cudaStream_t stream) {
   if (rows == 0) return;
-  argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, stream>>>(logits, ld, cols, id_offset, out);
+  launch_k(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(1024), 0, stream, logits, ld, cols, id_offset, out);
   BWN_CUDA_CHECK(cudaGetLastError());
 }
 
 __global__ void unpack_argmax_kernel(const int64_t* packed, int rows, int* ids) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < rows) ids[i] = (int)(0xFFFFFFFFu - (uint32_t)((unsigned long long)packed[i] & 0xFFFFFFFFull));
 }
 
 void unpack_argmax(const int64_t* packed, int rows, int* ids_out, cudaStream_t stream) {
   if (rows == 0) return;
-  unpack_argmax_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(packed, rows, ids_out);
+  launch_k(unpack_argmax_kernel, dim3((rows + 127) / 128), dim3(128), 0, stream, packed, rows, ids_out);
   BWN_CUDA_CHECK(cudaGetLastError());
 }
 
