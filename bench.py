@@ -78,6 +78,9 @@ def main() -> None:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--fp8", action="store_true", help="W8A16: 128x128 block-scaled E4M3 projection weights")
     ap.add_argument("--fused-comm", default="auto", choices=["auto", "on", "off"])
+    ap.add_argument("--profile-steps", type=int, default=int(os.environ.get("BWN_PROFILE_STEPS", "0")),
+                    help="run warm-up + N decode steps only (for a profiler), then exit")
+    ap.add_argument("--metrics", default=os.environ.get("BWN_METRICS", ""), help="JSONL metrics file")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -88,7 +91,12 @@ def main() -> None:
     from bwn.ops import check_status
     from bwn.parallel.comm import init_distributed
     from bwn.runtime.static_decode import StaticDecoder
+    from bwn.utils import fingerprint as F
     from bwn.utils.clocks import ClockSampler
+    from bwn.utils.env import validate
+    from bwn.utils.metrics import MetricsLog
+
+    validate()
 
     comm = init_distributed("nccl", timeout_s=300)
     assert comm.size == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={comm.size}"
@@ -114,6 +122,15 @@ def main() -> None:
             if comm.rank == 0:
                 print(f"[bench] fused NVLink comm unavailable, using NCCL: {e}", file=sys.stderr)
     dec = StaticDecoder(model, B, max_seq, use_graph=not args.no_graph)
+    if args.profile_steps:
+        # warm-up + N decode steps and nothing else, for a profiler's timeline
+        from bwn.utils.profiling import profile_steps
+        dec.capture()
+        ms = profile_steps(dec, args.profile_steps)
+        if comm.rank == 0:
+            print(json.dumps({"profile_steps": args.profile_steps, "ms_per_step": round(ms, 4)}))
+        dec.release()
+        return
 
     launches_per_step = count_launches(lambda: model.decode_step(dec.tokens, dec.st))
     dec.reset()
@@ -167,14 +184,18 @@ def main() -> None:
 
     # ---- end to end through the public per-step API (pinned H2D + D2H each step) ----
     host_tok = torch.randint(0, cfg.vocab, (B,), dtype=torch.int32)
+    row0 = []
     comm.barrier()
     torch.cuda.synchronize()
     e0 = time.perf_counter()
     for _ in range(args.steps):
         host_tok = dec.step(host_tok)
+        row0.append(host_tok[0])
     e_ms = (time.perf_counter() - e0) * 1e3
     e_ms = comm.max_scalar(e_ms, dev)
     check_status("e2e")
+    # occupancy gates on every rank (a lost state write leaves a layer empty)
+    occupancy = F.check_qwen36_state(dec.st, f"decode state rank={comm.rank}")
 
     ms_step = total_ms / args.steps
     value = B * args.steps / (total_ms / 1e3)
@@ -212,8 +233,16 @@ def main() -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "decode tokens/s (StaticDecoder.step, host round trip)",
                     "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
             "gpu_launches": launches_per_step * args.steps,
+            "gen_hash_row0": F.gen_hash(row0),
+            "occupancy_min_rows": {k: min(v) for k, v in occupancy.items() if v},
         }
         print(json.dumps(out))
+    if args.metrics:
+        log = MetricsLog(args.metrics, comm, run={"argv": sys.argv[1:], "model": cfg.name})
+        log.timing("decode_step", ms_step, batch=B)
+        log.timing("decode_e2e_step", e_ms / args.steps, batch=B)
+        if prefill_ms:
+            log.timing("prefill", prefill_ms, batch=B, seq=S)
     if comm.size > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

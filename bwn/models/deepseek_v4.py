@@ -80,12 +80,40 @@ def synthetic_checkpoint(cfg: DeepSeekV4Config, seed: int, device="cpu") -> dict
     return sd
 
 
-def _expert_stack(sd, f, name, E):
-    """Experts as one ``[E, ...]`` tensor, from either the stacked or the
+def _expert_stack(sd, f, name, e0, e1):
+    """Experts ``[e0, e1)`` as one tensor, from either the stacked or the
     per-expert (``experts.{e}.wN.weight``) layout."""
     if f + f"experts_{name}" in sd:
-        return sd[f + f"experts_{name}"]
-    return torch.stack([sd[f + f"experts.{e}.{name}.weight"] for e in range(E)])
+        return sd[f + f"experts_{name}"][e0:e1]
+    return torch.stack([sd[f + f"experts.{e}.{name}.weight"] for e in range(e0, e1)])
+
+
+def _unshard_view(sd: dict, cfg: DeepSeekV4Config, tp: int, rank: int) -> dict:
+    """Present a pre-sharded rank file under the full-checkpoint names the loader
+    slices: local experts move to their global ids, ``wq_b`` / ``wo_b`` /
+    shared-expert slices are placed in zero-padded full tensors at this rank's
+    offsets (only that window is read back)."""
+    out = dict(sd)
+    per = cfg.n_routed_experts // tp
+    for k in list(sd):
+        parts = k.split(".")
+        if "experts" in parts and ".shared_experts." not in k:
+            i = parts.index("experts")
+            if i + 1 < len(parts) and parts[i + 1].isdigit():
+                parts[i + 1] = str(rank * per + int(parts[i + 1]))
+                out.pop(k)
+                out[".".join(parts)] = sd[k]
+        elif k.endswith(".wq_b.weight"):
+            t = sd[k]
+            full = t.new_zeros(t.shape[0] * tp, t.shape[1])
+            full[rank * t.shape[0]:(rank + 1) * t.shape[0]] = t
+            out[k] = full
+        elif k.endswith(".wo_b.weight"):
+            t = sd[k]
+            full = t.new_zeros(t.shape[0], t.shape[1] * tp)
+            full[:, rank * t.shape[1]:(rank + 1) * t.shape[1]] = t
+            out[k] = full
+    return out
 
 
 class DeepSeekV4Model:
@@ -111,7 +139,10 @@ class DeepSeekV4Model:
         self.ones_hd = torch.ones(cfg.head_dim, device=self.device)
 
     # ------------------------------------------------------------------ load
-    def load(self, sd: dict) -> "DeepSeekV4Model":
+    def load(self, sd: dict, presharded: bool = False) -> "DeepSeekV4Model":
+        """Load a full state dict (sliced here per rank) or, with ``presharded``,
+        this rank's file from :func:`bwn.io.deepseek_weights.preprocess`
+        (experts renumbered from 0, ``wq_b``/``wo_b`` already split)."""
         cfg, dt, dev = self.cfg, self.dtype, self.device
         hd, r = cfg.head_dim, self.rank
         h0, h1 = r * self.heads, (r + 1) * self.heads
@@ -119,6 +150,8 @@ class DeepSeekV4Model:
         olr = cfg.o_lora_rank
         E, I = cfg.n_routed_experts, cfg.moe_inter
         Is = I // self.tp
+        if presharded:
+            sd = _unshard_view(sd, cfg, self.tp, r)
         self.L = []
         for i in range(cfg.num_layers):
             p, a, f = f"layers.{i}.", f"layers.{i}.attn.", f"layers.{i}.ffn."
@@ -137,10 +170,10 @@ class DeepSeekV4Model:
                 "gate": sd[f + "gate.weight"].to(dt),
                 "gate_bias": sd[f + "gate.bias"].float() if (f + "gate.bias") in sd else None,
             }
-            w1 = _expert_stack(sd, f, "w1", E)[self.e0:self.e0 + self.e_local]
-            w3 = _expert_stack(sd, f, "w3", E)[self.e0:self.e0 + self.e_local]
+            w1 = _expert_stack(sd, f, "w1", self.e0, self.e0 + self.e_local)
+            w3 = _expert_stack(sd, f, "w3", self.e0, self.e0 + self.e_local)
             L["experts_gate_up"] = torch.stack([O.interleave_gate_up(w1[e], w3[e]) for e in range(self.e_local)]).to(dt)
-            L["experts_down"] = _expert_stack(sd, f, "w2", E)[self.e0:self.e0 + self.e_local].to(dt)
+            L["experts_down"] = _expert_stack(sd, f, "w2", self.e0, self.e0 + self.e_local).to(dt)
             L["shared_gate_up"] = O.interleave_gate_up(sd[f + "shared_experts.w1.weight"][r * Is:(r + 1) * Is],
                                                        sd[f + "shared_experts.w3.weight"][r * Is:(r + 1) * Is]).to(dt)
             L["shared_down"] = sd[f + "shared_experts.w2.weight"][:, r * Is:(r + 1) * Is].to(dt)
@@ -152,6 +185,29 @@ class DeepSeekV4Model:
             "norm": sd["norm.weight"].float().to(dev),
             "hc_head": tuple(sd[k].float().to(dev) for k in ("hc_head_fn", "hc_head_scale", "hc_head_base")),
         }
+        return self
+
+    def load_checkpoint(self, path: str, presharded: bool | None = None) -> "DeepSeekV4Model":
+        """Load safetensors: a per-rank preprocessed file (``rank{r}.safetensors``
+        in ``path``) or a full checkpoint in the reference's state-dict layout.
+        FP8 pairs (``w`` + ``w_scale_inv``) are dequantized to the model dtype."""
+        import os
+        from ..io.checkpoint import Checkpoint
+        from ..io.fp8 import dequantize_block
+        rank_file = os.path.join(path, f"rank{self.rank}.safetensors")
+        if presharded is None:
+            presharded = os.path.isfile(rank_file)
+        ck = Checkpoint(rank_file if presharded else path, prefix="")
+        sd = {}
+        for k in ck.wm:
+            if k.endswith("_scale_inv"):
+                continue
+            t = ck.raw(k)
+            if (k + "_scale_inv") in ck.wm:
+                t = dequantize_block(t, ck.raw(k + "_scale_inv").float()).to(self.dtype)
+            sd[k] = t
+        self.load(sd, presharded=presharded)
+        ck.close()
         return self
 
     def init_random(self, seed: int = 0) -> "DeepSeekV4Model":

@@ -268,13 +268,27 @@ class Qwen36Model(nn.Module):
 
 
 def build_qwen36(cfg: Qwen36Config, comm: Comm | None = None, device="cpu", seed: int | None = 0,
-                 hf_state: dict | None = None, dtype=torch.bfloat16) -> Qwen36Model:
+                 hf_state: dict | None = None, dtype=torch.bfloat16, checkpoint: str | None = None) -> Qwen36Model:
+    """A rank's model from an in-memory HF state dict, a safetensors checkpoint
+    directory (HF layout, packed or per-expert MoE, official FP8 dequantized) or
+    random init from ``seed``."""
     m = Qwen36Model(cfg, comm, device, dtype)
-    if hf_state is not None:
+    if checkpoint is not None:
+        from ..io.checkpoint import Checkpoint
+        ck = Checkpoint(checkpoint)
+        m.load_hf(ck.getter())
+        ck.close()
+    elif hf_state is not None:
         m.load_hf(W.hf_getter(hf_state))
     elif seed is not None:
         m.init_random(seed)
     return m
+
+
+def from_pretrained(path: str, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16) -> Qwen36Model:
+    """Config from ``config.json`` plus weights from the safetensors beside it."""
+    from ..config import qwen36_from_hf
+    return build_qwen36(qwen36_from_hf(path), comm, device, None, None, dtype, checkpoint=path)
 
 
 def param_gb(cfg: Qwen36Config) -> float:

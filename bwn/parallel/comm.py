@@ -21,6 +21,8 @@ class Comm:
         self.group = group
         self.rank = rank
         self.size = size
+        # cost probe (the reference's NOREDUCE): sum all-reduces become no-ops
+        self.no_reduce = os.environ.get("BWN_NO_REDUCE", "0") == "1"
 
     @staticmethod
     def single() -> "Comm":
@@ -34,7 +36,7 @@ class Comm:
 
     # ---- collectives (in place) ------------------------------------------
     def all_reduce_(self, x: torch.Tensor) -> torch.Tensor:
-        if self.size > 1:
+        if self.size > 1 and not self.no_reduce:
             dist.all_reduce(x, op=dist.ReduceOp.SUM, group=self.group)
         return x
 
@@ -76,6 +78,8 @@ class Comm:
         """Max of a host scalar over ranks (used for max-over-ranks timings)."""
         if self.size == 1:
             return v
+        if device is None and dist.get_backend(self.group) == "nccl":
+            device = torch.device("cuda", torch.cuda.current_device())
         t = torch.tensor([v], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
         return float(t.item())

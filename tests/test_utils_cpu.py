@@ -1,0 +1,94 @@
+"""Fingerprints, guards, env validation, topology decisions and JSONL metrics (CPU)."""
+import hashlib
+
+import pytest
+import torch
+
+from bwn.config import tiny_qwen36
+from bwn.models.qwen36 import build_qwen36
+from bwn.parallel.topology import Topology, choose_comm_path
+from bwn.utils import env, fingerprint as F
+from bwn.utils.metrics import MetricsLog, read_jsonl
+
+
+def test_gen_hash_format_matches_reference_definition():
+    ids = [760, 6511, 314, 9338, 369]
+    assert F.gen_hash(ids) == hashlib.md5(str(ids).encode()).hexdigest()[:12]
+    assert F.gen_hash(torch.tensor(ids)) == F.gen_hash(ids)
+
+
+def test_logits_fingerprint():
+    x = torch.zeros(2, 10)
+    x[0, 7] = 3.0
+    x[0, 2] = 2.0
+    fp = F.logits_fingerprint(x)
+    assert fp["top5"][:2] == [7, 2] and fp["finite"] and fp["sum"] == 5.0
+    x[1, 1] = float("nan")
+    assert not F.logits_fingerprint(x)["finite"]
+
+
+def test_assert_disjoint_catches_overlap_allows_slices():
+    base = torch.zeros(4, 8)
+    F.assert_disjoint([base[i] for i in range(4)])           # per-layer slices: disjoint
+    with pytest.raises(RuntimeError, match="overlap"):
+        F.assert_disjoint([base[0:2], base[1:3]])             # overlapping views
+    with pytest.raises(RuntimeError, match="overlap"):
+        F.assert_disjoint([base, base.view(-1)])               # same memory, two views
+    F.assert_disjoint([base[:, :4], torch.zeros(3)])
+
+
+def test_occupancy_gate_fires_on_an_empty_layer(monkeypatch):
+    st = torch.ones(3, 2, 4)
+    assert F.assert_occupancy(st, "x") == [2, 2, 2]
+    st[1] = 0
+    with pytest.raises(RuntimeError, match=r"layers \[1\]"):
+        F.assert_occupancy(st, "x")
+    monkeypatch.setenv("BWN_OCCUPANCY_CHECK", "0")
+    assert F.assert_occupancy(st, "x") == []
+
+
+def test_qwen36_state_guards_after_decode():
+    cfg = tiny_qwen36(layers=4)
+    m = build_qwen36(cfg, device="cpu", dtype=torch.float32)
+    st = m.new_state(2, 16)
+    with pytest.raises(RuntimeError):   # nothing written yet
+        F.check_qwen36_state(st)
+    ids = torch.tensor([[3, 4, 5], [6, 7, 8]])
+    m.prefill(ids, st)
+    rows = F.check_qwen36_state(st)
+    assert all(n > 0 for n in rows["ssm"]) and all(n > 0 for n in rows["k"])
+
+
+def test_env_validation(monkeypatch):
+    assert env.validate({})["BWN_PDL"] == 1
+    with pytest.raises(ValueError, match="unknown"):
+        env.validate({"BWN_NOPE": "1"})
+    with pytest.raises(ValueError, match="expected one of"):
+        env.validate({"BWN_FUSED_COMM": "maybe"})
+    with pytest.raises(ValueError, match="cannot be combined"):
+        env.validate({"BWN_NO_REDUCE": "1", "BWN_FUSED_COMM": "on"})
+    monkeypatch.setenv("BWN_PROFILE_STEPS", "7")
+    assert env.get("BWN_PROFILE_STEPS") == 7
+    assert "BWN_PDL" in env.describe()
+
+
+def test_choose_comm_path():
+    full = Topology(8, ["B200"] * 8, [[True] * 8 for _ in range(8)], multicast=True)
+    assert choose_comm_path(full, 1) == "single"
+    assert choose_comm_path(full, 8) == "fused_nvls"
+    assert choose_comm_path(full, 8, "off") == "nccl"
+    nomc = Topology(8, ["B200"] * 8, [[True] * 8 for _ in range(8)], multicast=False)
+    assert choose_comm_path(nomc, 4) == "fused_p2p"
+    broken = Topology(2, ["B200"] * 2, [[True, False], [False, True]], multicast=True)
+    assert choose_comm_path(broken, 2) == "nccl"
+    with pytest.raises(RuntimeError):
+        choose_comm_path(broken, 2, "on")
+
+
+def test_metrics_jsonl(tmp_path):
+    p = str(tmp_path / "m" / "run.jsonl")
+    log = MetricsLog(p, None, run={"model": "tiny"})
+    log.timing("decode_step", 1.25, batch=4)
+    recs = read_jsonl(p)
+    assert [r["event"] for r in recs] == ["run", "decode_step"]
+    assert recs[1]["ms"] == 1.25 and recs[1]["batch"] == 4 and recs[0]["model"] == "tiny"
