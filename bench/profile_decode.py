@@ -28,6 +28,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--graph-time", type=int, default=0,
+                    help="capture the step as a CUDA graph and print ms/step over this many replays")
     ap.add_argument("--tp-shapes", type=int, default=1,
                     help="emulate rank 0 of a TP group of this size on one GPU (collectives become no-ops)")
     args = ap.parse_args()
@@ -57,6 +59,30 @@ def main():
     st.positions.fill_(args.ctx)
     tok = torch.randint(0, cfg.vocab, (args.batch,), dtype=torch.int32, device=dev)
     torch.cuda.synchronize()
+    if args.graph_time:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):  # eager warm-up on the capture stream sizes its scratch
+                m.decode_step(tok, st)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                m.decode_step(tok, st)
+        torch.cuda.current_stream().wait_stream(s)
+        st.positions.fill_(args.ctx)
+        for _ in range(3):
+            g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(args.graph_time):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        print(f"tp-shapes {args.tp_shapes} batch {args.batch}: {a.elapsed_time(b) / args.graph_time:.3f} ms/step "
+              f"(graph replay, collectives skipped)")
+        return
     for _ in range(args.steps):
         tok = m.decode_step(tok, st)
     torch.cuda.synchronize()

@@ -165,13 +165,27 @@ def deltanet_decode(qkv, z, a, b, conv_ring, state, positions, conv_w, A_log, dt
                                k_heads, state.shape[2], state.shape[3], eps)[:, : VH * state.shape[3]]
 
 
+def deltanet_verify(qkv, z, a, b, stash_qkv, stash_ab, vstep, conv_ring, state, positions, pending, conv_w, A_log,
+                    dt_bias, norm_w, k_heads: int, n_tok: int, eps: float = 1e-6) -> torch.Tensor:
+    """Speculative verify of ``n_tok`` tokens per sequence with deferred commit
+    (rows ``[B*n_tok, *]``): the stashed tokens the last step accepted
+    (``pending``) are committed to the state first; the new tokens only produce
+    outputs and are stashed for the next commit."""
+    if qkv.is_cuda:
+        return ops().deltanet_verify(qkv, z, a, b, stash_qkv, stash_ab, vstep, conv_ring, state, positions, pending,
+                                     conv_w, A_log, dt_bias, norm_w, k_heads, n_tok, eps)
+    return ref.deltanet_verify(qkv, z, a, b, stash_qkv, stash_ab, vstep, conv_ring, state, positions, pending, conv_w,
+                               A_log, dt_bias, norm_w, k_heads, n_tok, eps)
+
+
 def gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions,
-               eps: float = 1e-6, splits: int = 0) -> torch.Tensor:
-    """Fused gated GQA decode step (appends K/V at ``positions``)."""
+               eps: float = 1e-6, splits: int = 0, n_tok: int = 1) -> torch.Tensor:
+    """Fused gated GQA decode step (appends K/V at ``positions``); ``n_tok``
+    query rows per cache sequence for speculative verification."""
     if qg.is_cuda:
         return ops().gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions,
-                                eps, splits)
-    return ref.gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions, eps)
+                                eps, splits, n_tok)
+    return ref.gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, positions, eps, n_tok)
 
 
 # --------------------------------------------------------------------------

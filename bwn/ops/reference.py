@@ -6,9 +6,10 @@ states the reference behaviour it reproduces.
 
 Conventions shared with the CUDA kernels:
 
-* DeltaNet conv history is a 4-slot ring ``conv_ring[B, 4, C]``: the qkv row of
-  token position ``t`` lives in slot ``t % 4``.  A decode step at position ``p``
-  reads slots ``(p-3..p-1) % 4`` and writes slot ``p % 4``; no reader ever needs
+* DeltaNet conv history is an R-slot ring ``conv_ring[B, R, C]`` (R = 4, or 8
+  when multi-token verify is used): the qkv row of token position ``t`` lives in
+  slot ``t % R``.  A decode step at position ``p`` reads slots
+  ``(p-3..p-1) % R`` and writes slot ``p % R``; no reader ever needs
   the slot being written, so one launch may update the ring in place while other
   CTAs still read it.  (The reference keeps a shifted ``[QKV, 3]`` window,
   ``contrib/qwen3.6-27b/kernels/deltanet_full.py:82-134``.)
@@ -148,10 +149,11 @@ def deltanet_decode(
     pos = positions.long()
     ks = conv_w.shape[1]
     rows = torch.arange(B, device=qkv.device)
-    hist = [conv_ring[rows, (pos - (ks - 1) + j) % ks].float() for j in range(ks - 1)]
+    R = conv_ring.shape[1]  # ring slots (4, or 8 for multi-token verify)
+    hist = [conv_ring[rows, (pos - (ks - 1) + j) % R].float() for j in range(ks - 1)]
     xs = torch.stack(hist + [qkv.float()], dim=-1)  # [B, C, ks]
     y = F.silu((xs * conv_w.float().unsqueeze(0)).sum(-1))
-    conv_ring[rows, pos % ks] = qkv.to(conv_ring.dtype)
+    conv_ring[rows, pos % R] = qkv.to(conv_ring.dtype)
     q = y[:, :KD].reshape(B, k_heads, k_dim)
     k = y[:, KD:2 * KD].reshape(B, k_heads, k_dim)
     v = y[:, 2 * KD:].reshape(B, VH, v_dim)
@@ -183,7 +185,7 @@ def causal_conv1d_prefill(x: torch.Tensor, conv_w: torch.Tensor, init_ring: torc
     ks = conv_w.shape[1]
     if init_ring is not None:
         hist = torch.stack(
-            [init_ring[:, (start_pos - (ks - 1) + j) % ks] for j in range(ks - 1)], dim=1
+            [init_ring[:, (start_pos - (ks - 1) + j) % init_ring.shape[1]] for j in range(ks - 1)], dim=1
         ).float()
         if start_pos < ks - 1:
             hist[:, : (ks - 1) - start_pos] = 0
@@ -297,7 +299,7 @@ def deltanet_prefill(
     for bi in range(B):
         n = S if valid_len is None else int(valid_len[bi])
         for t in range(max(0, n - (ks - 1)), n):
-            conv_ring[bi, (start_pos + t) % ks] = qkv[bi, t].to(conv_ring.dtype)
+            conv_ring[bi, (start_pos + t) % conv_ring.shape[1]] = qkv[bi, t].to(conv_ring.dtype)
     o = o.transpose(1, 2)  # [B, S, VH, Dv]
     out = rms_norm_gated(o, z.reshape(B, S, VH, v_dim), norm_w, eps)
     return out.reshape(B, S, VH * v_dim)
@@ -316,13 +318,17 @@ def gqa_decode(
     sin: torch.Tensor,       # [S_max, R]
     k_cache: torch.Tensor,   # [B, KVH, S_max, D] (row `pos` written)
     v_cache: torch.Tensor,
-    positions: torch.Tensor, # [B]
+    positions: torch.Tensor, # [B] (one per query row)
     eps: float = 1e-6,
+    n_tok: int = 1,
 ) -> torch.Tensor:
     """Gated GQA decode step (the reference's GQA tail + stateful KV append,
     ``qwen3.6-35b-a3b/kernels/gqa_tail_35b.py:52-394``): q/k RMSNorm(1+w),
     partial RoPE, append K/V at ``pos``, softmax over ``[0, pos]``, P.V,
-    ``* sigmoid(gate)``.  Returns ``[B, QH*D]``."""
+    ``* sigmoid(gate)``.  Returns ``[B, QH*D]``.  With ``n_tok > 1`` the query
+    rows are ``n_tok`` consecutive tokens per cache sequence (speculative
+    verify): all new K/V rows are written first, then each row attends causally
+    up to its own position."""
     B, QH, D2 = qg.shape
     D = D2 // 2
     KVH = k_new.shape[1]
@@ -332,14 +338,14 @@ def gqa_decode(
     c, s = cos[pos].float()[:, None], sin[pos].float()[:, None]
     q = apply_partial_rope(rms_norm(q, q_norm_w, eps), c, s)
     k = apply_partial_rope(rms_norm(k_new.float(), k_norm_w, eps), c, s)
-    rows = torch.arange(B, device=qg.device)
-    k_cache[rows, :, pos] = k.to(k_cache.dtype)
-    v_cache[rows, :, pos] = v_new.to(v_cache.dtype)
+    seq = torch.arange(B, device=qg.device) // n_tok
+    k_cache[seq, :, pos] = k.to(k_cache.dtype)
+    v_cache[seq, :, pos] = v_new.to(v_cache.dtype)
     out = torch.empty(B, QH, D, dtype=torch.float32, device=qg.device)
     for bi in range(B):
         L = int(pos[bi]) + 1
-        kk = k_cache[bi, :, :L].float().repeat_interleave(rep, 0)  # [QH, L, D]
-        vv = v_cache[bi, :, :L].float().repeat_interleave(rep, 0)
+        kk = k_cache[bi // n_tok, :, :L].float().repeat_interleave(rep, 0)  # [QH, L, D]
+        vv = v_cache[bi // n_tok, :, :L].float().repeat_interleave(rep, 0)
         sc = torch.einsum("hd,hld->hl", q[bi], kk) / math.sqrt(D)
         p = sc.softmax(-1)
         out[bi] = torch.einsum("hl,hld->hd", p, vv)
@@ -473,3 +479,38 @@ def mqa_attn(q, kv, visible, q_per_seq: int, scale: float):
         sc = (q[r].float() @ k.t()) * scale
         out[r] = sc.softmax(-1) @ k
     return out.to(q.dtype)
+
+
+def deltanet_verify(qkv, z, a, b, stash_qkv, stash_ab, vstep, conv_ring, state, positions, pending, conv_w,
+                    A_log, dt_bias, norm_w, k_heads: int, n_tok: int, eps: float = 1e-6) -> torch.Tensor:
+    """Multi-token DeltaNet verify with deferred commit (oracle of
+    ``deltanet_verify.cu``): commit the ``pending[b]`` stashed tokens of the last
+    step into ``state``/``conv_ring``, run the ``n_tok`` new tokens per sequence
+    on copies (outputs only), stash their raw rows under the other parity.
+    Rows are ``[B*n_tok, *]``; returns ``[B*n_tok, VH*Dv]``."""
+    B, VH, Dk, Dv = state.shape
+    N = n_tok
+    assert N <= stash_qkv.shape[2]
+    par = int(vstep.reshape(-1)[0]) & 1
+    out = torch.zeros(B * N, VH * Dv, dtype=qkv.dtype, device=qkv.device)
+    for bi in range(B):
+        p = int(positions[bi])
+        if p < 0:
+            continue
+        na = int(pending[bi])
+        for j in range(na):
+            ab = stash_ab[par, bi, j]
+            deltanet_decode(stash_qkv[par, bi, j][None], ab[None, :VH], ab[None, VH:],
+                            torch.zeros(1, VH * Dv, dtype=qkv.dtype, device=qkv.device),
+                            conv_ring[bi:bi + 1], state[bi:bi + 1], torch.tensor([p - na + j]), conv_w, A_log,
+                            dt_bias, norm_w, k_heads, Dk, Dv, eps)
+        ring_c, st_c = conv_ring[bi:bi + 1].clone(), state[bi:bi + 1].clone()
+        for i in range(N):
+            r = bi * N + i
+            out[r] = deltanet_decode(qkv[r][None], a[r][None], b[r][None], z[r][None], ring_c, st_c,
+                                     torch.tensor([p + i]), conv_w, A_log, dt_bias, norm_w, k_heads, Dk, Dv,
+                                     eps)[0].to(out.dtype)
+            stash_qkv[par ^ 1, bi, i] = qkv[r].to(stash_qkv.dtype)
+            stash_ab[par ^ 1, bi, i, :VH] = a[r].to(stash_ab.dtype)
+            stash_ab[par ^ 1, bi, i, VH:] = b[r].to(stash_ab.dtype)
+    return out

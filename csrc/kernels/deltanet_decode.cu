@@ -55,8 +55,9 @@ __global__ void __cluster_dims__(kDnNJ, 1, 1) __launch_bounds__(128)
   const int pos = p.positions[b];
   const bool active = pos >= 0;
   const __nv_bfloat16* qkv = p.qkv + (long)b * p.qkv_stride;
-  __nv_bfloat16* ring = p.conv_ring + (long)b * 4 * C;
-  const int ks0 = (pos + 1) & 3, ks1 = (pos + 2) & 3, ks2 = (pos + 3) & 3, kcur = pos & 3;
+  const int rm = p.ring_slots - 1;
+  __nv_bfloat16* ring = p.conv_ring + (long)b * p.ring_slots * C;
+  const int ks0 = (pos - 3) & rm, ks1 = (pos - 2) & rm, ks2 = (pos - 1) & rm, kcur = pos & rm;
 
   // ---- conv + SiLU for q, k (128 ch each) and this block's 32 v channels ----
   auto conv = [&](int ch) -> float {
@@ -102,7 +103,7 @@ __global__ void __cluster_dims__(kDnNJ, 1, 1) __launch_bounds__(128)
   }
   __syncthreads();
   // the ring slot of this position: q/k channels written by one CTA per K head,
-  // v channels by their column block (nobody reads slot pos&3 in this step)
+  // v channels by their column block (nobody reads slot pos&(R-1) in this step)
   if (active) {
     if (jb == 0 && (h % rep) == 0) {
       ring[kcur * C + kh * kDnDk + t] = qkv[kh * kDnDk + t];

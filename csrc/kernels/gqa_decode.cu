@@ -67,16 +67,17 @@ __global__ void __launch_bounds__(kGThreads, 1)
 
   pdl_trigger();
   pdl_wait();
-  const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;  // b: query row
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int ntok = p.n_tok > 1 ? p.n_tok : 1;
   const int pos = p.positions[b];
   const int L = pos + 1;  // keys 0..pos
   int chunk = (L + p.splits - 1) / p.splits;
   chunk = (chunk + kGTile - 1) / kGTile * kGTile;
   const int k0 = sp * chunk;
   const int k1 = min(L, k0 + chunk);
-  const bool has_pos = (pos >= k0 && pos < k1);
-  const long row_base = ((long)b * p.kv_heads + kvh) * p.s_max;
+  const bool has_pos = ntok == 1 && (pos >= k0 && pos < k1);
+  const long row_base = ((long)(b / ntok) * p.kv_heads + kvh) * p.s_max;
 
   if (t == 0) {
     mbar_init(&bar[0], 1);
@@ -352,12 +353,44 @@ static void launch_gqa(const CUtensorMap& tk, const CUtensorMap& tv, const GqaDe
   launch_k(gqa_decode_kernel<G>, grid, dim3(kGThreads), smem, st, tk, tv, p);
 }
 
+// Multi-token verify: RMSNorm(1+w) + partial RoPE of every new K row, and the
+// K/V rows written at their positions, before any row's attention reads them.
+__global__ void __launch_bounds__(kGD) gqa_kv_append_kernel(GqaDecodeArgs p) {
+  pdl_trigger();
+  pdl_wait();
+  const int kvh = blockIdx.x, r = blockIdx.y, t = threadIdx.x;
+  const int pos = p.positions[r];
+  if (pos < 0 || pos >= p.s_max) return;
+  __shared__ float sk[kGD];
+  __shared__ float red[kGD / 32];
+  const float kx = __bfloat162float(p.k_new[(long)r * p.kv_new_stride + (long)kvh * kGD + t]);
+  const float ss = warp_sum(kx * kx);
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int w = 0; w < kGD / 32; ++w) tot += red[w];
+  sk[t] = kx * rsqrtf(tot / kGD + p.eps) * (1.f + p.k_norm_w[t]);
+  __syncthreads();
+  const int R = p.rope_dim, hr = R >> 1;
+  float kv = sk[t];
+  if (t < R) {
+    const float c = p.cos[(long)pos * R + t], s = p.sin[(long)pos * R + t];
+    kv = sk[t] * c + (t < hr ? -1.f : 1.f) * sk[t < hr ? t + hr : t - hr] * s;
+  }
+  const long row = ((long)(r / p.n_tok) * p.kv_heads + kvh) * p.s_max + pos;
+  p.k_cache[row * kGD + t] = __float2bfloat16(kv);
+  p.v_cache[row * kGD + t] = p.v_new[(long)r * p.kv_new_stride + (long)kvh * kGD + t];
+}
+
 void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
   BWN_CHECK(p.q_heads % p.kv_heads == 0, "gqa_decode: q_heads %% kv_heads");
   BWN_CHECK(p.rope_dim <= kGD && p.rope_dim % 2 == 0, "gqa_decode: bad rope_dim");
+  const int ntok = p.n_tok > 1 ? p.n_tok : 1;
+  BWN_CHECK(p.batch % ntok == 0, "gqa_decode: rows %% n_tok");
+  if (ntok > 1) launch_k(gqa_kv_append_kernel, dim3(p.kv_heads, p.batch), dim3(kGD), 0, stream, p);
   const int G = p.q_heads / p.kv_heads;
   CUtensorMap tk, tv;
-  const long rows = (long)p.batch * p.kv_heads * p.s_max;
+  const long rows = (long)(p.batch / ntok) * p.kv_heads * p.s_max;
   make_tmap_2d_bf16(&tk, p.k_cache, rows, kGD, kGD, kGTile, 64);
   make_tmap_2d_bf16(&tv, p.v_cache, rows, kGD, kGD, kGTile, 64);
   switch (G) {

@@ -18,7 +18,8 @@ struct DeltaNetDecodeArgs {
   const __nv_bfloat16* a;    // [B, VH]  (row stride ab_stride)
   const __nv_bfloat16* b;
   long ab_stride;
-  __nv_bfloat16* conv_ring;  // [B, 4, C]
+  __nv_bfloat16* conv_ring;  // [B, R, C], slot = position & (R - 1)
+  int ring_slots;            // R: 4, or 8 when multi-token verify is used
   void* state;               // [B, VH, 128, 128] fp32 or bf16
   bool state_bf16;
   const int* positions;      // [B]; < 0 = inactive row
@@ -32,6 +33,38 @@ struct DeltaNetDecodeArgs {
   float l2_eps, norm_eps;
 };
 void deltanet_decode(const DeltaNetDecodeArgs& p, cudaStream_t stream);
+
+// ---- DeltaNet multi-token verify with deferred commit (deltanet_verify.cu) --
+struct DnVerifyArgs {
+  const __nv_bfloat16* qkv;  // [B*N, C] new tokens, pre-conv (row stride qkv_row)
+  long qkv_row;
+  const __nv_bfloat16* z;    // [B*N, VH*128]
+  long z_row;
+  const __nv_bfloat16* a;    // [B*N, VH] (row stride ab_row)
+  const __nv_bfloat16* b;
+  long ab_row;
+  __nv_bfloat16* stash_qkv;  // [2, B, SN, C]     raw rows of the last verify, by step parity
+  __nv_bfloat16* stash_ab;   // [2, B, SN, 2*VH]  their a then b
+  int stash_n;               // SN >= n_tok (n_tok = 0: commit only)
+  const int* vstep;          // verify step counter: read parity vstep&1, write the other
+  __nv_bfloat16* conv_ring;  // [B, R, C], R >= N + 3
+  int ring_slots;
+  void* state;               // [B, VH, 128, 128] committed state
+  bool state_bf16;
+  const int* positions;      // [B] committed length = position of the first new token; < 0 inactive
+  const int* pending;        // [B] accepted tokens of the last verify not yet committed (0..N)
+  const float* conv_w;
+  const float* A_log;
+  const float* dt_bias;
+  const float* norm_w;
+  __nv_bfloat16* out;        // [B*N, VH*128]
+  long out_row;
+  int* status;
+  int batch, n_tok, k_heads, v_heads;
+  float l2_eps, norm_eps;
+};
+void deltanet_verify(const DnVerifyArgs& p, cudaStream_t stream);
+constexpr int kDnVerifyMaxTok = 8;
 
 // ---- gated GQA decode (gqa_decode.cu) ---------------------------------------
 struct GqaDecodeArgs {
@@ -54,6 +87,11 @@ struct GqaDecodeArgs {
   int* status;
   int batch, q_heads, kv_heads, s_max, rope_dim, splits;
   float eps;
+  // multi-token verify: `batch` query rows, n_tok consecutive rows per cache
+  // sequence (row r -> cache sequence r / n_tok, position positions[r]).  With
+  // n_tok > 1 the new K/V rows are appended by a separate launch first, so
+  // every row's attention reads them from the cache; 0 or 1 = decode.
+  int n_tok;
 };
 void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream);
 int gqa_decode_workspace_floats(int batch, int q_heads, int kv_heads, int splits);

@@ -363,13 +363,13 @@ __global__ void __launch_bounds__(256) dn_prefill_prep_kernel(DnPrefillArgs p) {
   const int KD = p.k_heads * 128, C = 2 * KD + p.v_heads * 128;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const __nv_bfloat16* row = p.qkv + ((long)b * p.S + t) * p.qkv_row;
-  const __nv_bfloat16* ring = p.conv_ring + (long)b * 4 * C;
+  const __nv_bfloat16* ring = p.conv_ring + (long)b * p.ring_slots * C;
   auto hist = [&](int ch, int back) -> float {  // x at position start+t-back
     const int tt = t - back;
     if (tt >= 0) return __bfloat162float(row[(long)(-back) * p.qkv_row + ch]);
     const int pos = p.start + tt;
     if (pos < 0) return 0.f;
-    return __bfloat162float(ring[(pos & 3) * C + ch]);
+    return __bfloat162float(ring[(pos & (p.ring_slots - 1)) * C + ch]);
   };
   auto conv = [&](int ch) -> float {
     const float4 w = *reinterpret_cast<const float4*>(p.conv_w + (long)ch * 4);
@@ -421,7 +421,7 @@ __global__ void dn_ring_update_kernel(DnPrefillArgs p) {
     const int t = vl - back;
     if (t < 0) continue;
     const __nv_bfloat16* row = p.qkv + ((long)b * p.S + t) * p.qkv_row;
-    __nv_bfloat16* dst = p.conv_ring + ((long)b * 4 + ((p.start + t) & 3)) * C;
+    __nv_bfloat16* dst = p.conv_ring + ((long)b * p.ring_slots + ((p.start + t) & (p.ring_slots - 1))) * C;
     for (int ch = blockIdx.x * blockDim.x + threadIdx.x; ch < C; ch += gridDim.x * blockDim.x) dst[ch] = row[ch];
   }
 }

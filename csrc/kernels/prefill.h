@@ -34,7 +34,8 @@ struct DnPrefillArgs {
   const __nv_bfloat16* a;    // [B, S, VH] rows of stride ab_row
   const __nv_bfloat16* b;
   long ab_row;
-  __nv_bfloat16* conv_ring;  // [B, 4, C]
+  __nv_bfloat16* conv_ring;  // [B, R, C], slot = position & (R - 1)
+  int ring_slots;            // R (4 or 8)
   void* state;               // [B, VH, 128, 128]
   bool state_bf16;
   const int* valid_len;      // [B]

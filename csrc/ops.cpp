@@ -370,7 +370,8 @@ Tensor deltanet_decode_op(const Tensor& qkv, const Tensor& z, const Tensor& a, c
   const int B = (int)qkv.size(0), VH = (int)state.size(1);
   const int C = (int)qkv.size(1);
   TORCH_CHECK(C == 2 * k_heads * 128 + VH * 128, "qkv width mismatch");
-  TORCH_CHECK(conv_ring.size(0) == B && conv_ring.size(1) == 4 && conv_ring.size(2) == C, "conv_ring [B,4,C]");
+  TORCH_CHECK(conv_ring.size(0) == B && (conv_ring.size(1) == 4 || conv_ring.size(1) == 8) && conv_ring.size(2) == C,
+              "conv_ring [B, 4 or 8, C]");
   TORCH_CHECK(qkv.stride(1) == 1 && z.stride(1) == 1 && a.stride(1) == 1 && b.stride(1) == 1, "inner stride 1");
   TORCH_CHECK(a.stride(0) == b.stride(0), "a and b must share a row stride");
   const c10::cuda::CUDAGuard guard(qkv.device());
@@ -384,6 +385,7 @@ Tensor deltanet_decode_op(const Tensor& qkv, const Tensor& z, const Tensor& a, c
   p.b = bf(b);
   p.ab_stride = a.stride(0);
   p.conv_ring = bfm(conv_ring);
+  p.ring_slots = (int)conv_ring.size(1);
   p.state = state.data_ptr();
   p.state_bf16 = state.scalar_type() == at::kBFloat16;
   p.positions = positions.data_ptr<int>();
@@ -404,7 +406,7 @@ Tensor deltanet_decode_op(const Tensor& qkv, const Tensor& z, const Tensor& a, c
 
 Tensor gqa_decode_op(const Tensor& qg, const Tensor& k_new, const Tensor& v_new, const Tensor& q_norm_w,
                      const Tensor& k_norm_w, const Tensor& cos, const Tensor& sin, Tensor k_cache, Tensor v_cache,
-                     const Tensor& positions, double eps, int64_t splits) {
+                     const Tensor& positions, double eps, int64_t splits, int64_t n_tok) {
   check_bf16(qg, "qg");
   check_bf16(k_new, "k_new");
   check_bf16(v_new, "v_new");
@@ -417,8 +419,12 @@ Tensor gqa_decode_op(const Tensor& qg, const Tensor& k_new, const Tensor& v_new,
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.is_contiguous(), "positions int32");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == 256 && k_cache.is_contiguous() && v_cache.is_contiguous(),
               "caches must be contiguous [B, KVH, S_max, 256]");
-  const int B = (int)k_cache.size(0), KVH = (int)k_cache.size(1), S = (int)k_cache.size(2);
-  TORCH_CHECK(qg.dim() == 3 && qg.size(2) == 512 && qg.stride(2) == 1 && qg.stride(1) == 512, "qg [B, QH, 512]");
+  TORCH_CHECK(n_tok >= 1 && n_tok <= 16, "n_tok in [1, 16]");
+  const int KVH = (int)k_cache.size(1), S = (int)k_cache.size(2);
+  const int B = (int)(k_cache.size(0) * n_tok);  // query rows
+  TORCH_CHECK(qg.dim() == 3 && qg.size(0) == B && qg.size(2) == 512 && qg.stride(2) == 1 && qg.stride(1) == 512,
+              "qg [B * n_tok, QH, 512]");
+  TORCH_CHECK(positions.numel() == B, "positions: one per query row");
   TORCH_CHECK(k_new.dim() == 3 && k_new.stride(2) == 1 && k_new.stride(1) == 256, "k_new [B, KVH, 256]");
   TORCH_CHECK(v_new.stride(0) == k_new.stride(0), "k_new and v_new must share a row stride");
   const int QH = (int)qg.size(1);
@@ -456,6 +462,7 @@ Tensor gqa_decode_op(const Tensor& qg, const Tensor& k_new, const Tensor& v_new,
   p.rope_dim = (int)cos.size(1);
   p.splits = (int)splits;
   p.eps = (float)eps;
+  p.n_tok = (int)n_tok;
   gqa_decode(p, at::cuda::getCurrentCUDAStream().stream());
   return out;
 }
@@ -485,7 +492,7 @@ TORCH_LIBRARY(bwn, m) {
       "Tensor positions, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, float eps) -> Tensor");
   m.def(
       "gqa_decode(Tensor qg, Tensor k_new, Tensor v_new, Tensor q_norm_w, Tensor k_norm_w, Tensor cos, Tensor sin, "
-      "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor positions, float eps, int splits) -> Tensor");
+      "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor positions, float eps, int splits, int n_tok=1) -> Tensor");
   bwn::register_ext_defs(m);
 }
 

@@ -6,6 +6,7 @@
 
 #include "common/host.h"
 #include "kernels/deepseek.h"
+#include "kernels/launch.h"
 #include "kernels/moe.h"
 #include "kernels/prefill.h"
 #include "ops_ext.h"
@@ -55,7 +56,10 @@ Tensor deltanet_prefill_op(const Tensor& qkv, const Tensor& z, const Tensor& a, 
   p.b = cbf(b);
   p.ab_row = row_stride(a, "a");
   TORCH_CHECK(row_stride(b, "b") == p.ab_row, "a and b share a row stride");
+  TORCH_CHECK(conv_ring.dim() == 3 && (conv_ring.size(1) == 4 || conv_ring.size(1) == 8) && conv_ring.is_contiguous(),
+              "conv_ring [B, 4 or 8, C]");
   p.conv_ring = mbf(conv_ring);
+  p.ring_slots = (int)conv_ring.size(1);
   p.state = state.data_ptr();
   p.state_bf16 = state.scalar_type() == at::kBFloat16;
   p.valid_len = valid_len.data_ptr<int>();
@@ -324,7 +328,74 @@ void rope_interleaved_op(Tensor x, const Tensor& cos, const Tensor& sin, const T
                    sin.data_ptr<float>(), pos.data_ptr<int>(), at::cuda::getCurrentCUDAStream().stream());
 }
 
+// Speculative verify of n_tok tokens per sequence with deferred commit.
+// qkv/z/a/b: [B*n_tok, *] row views of one projection output.
+Tensor deltanet_verify_op(const Tensor& qkv, const Tensor& z, const Tensor& a, const Tensor& b, Tensor stash_qkv,
+                          Tensor stash_ab, const Tensor& vstep, Tensor conv_ring, Tensor state,
+                          const Tensor& positions, const Tensor& pending, const Tensor& conv_w, const Tensor& A_log,
+                          const Tensor& dt_bias, const Tensor& norm_w, int64_t k_heads, int64_t n_tok, double eps) {
+  for (const Tensor* t : std::initializer_list<const Tensor*>{&qkv, &z, &a, &b, &stash_qkv, &stash_ab, &conv_ring})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16, "deltanet_verify: bf16 CUDA tensors expected");
+  TORCH_CHECK(state.is_contiguous() && state.dim() == 4 && state.size(2) == 128 && state.size(3) == 128,
+              "state [B, VH, 128, 128]");
+  TORCH_CHECK(state.scalar_type() == at::kFloat || state.scalar_type() == at::kBFloat16, "state fp32/bf16");
+  const int B = (int)state.size(0), VH = (int)state.size(1);
+  const long C = conv_ring.size(2);
+  TORCH_CHECK(conv_ring.is_contiguous() && conv_ring.size(0) == B, "conv_ring [B, R, C]");
+  TORCH_CHECK(stash_qkv.is_contiguous() && stash_qkv.dim() == 4 && stash_qkv.size(0) == 2 && stash_qkv.size(1) == B &&
+                  stash_qkv.size(2) >= n_tok && stash_qkv.size(3) == C,
+              "stash_qkv [2, B, SN >= n_tok, C]");
+  const long SN = stash_qkv.size(2);
+  TORCH_CHECK(stash_ab.is_contiguous() && stash_ab.numel() == 2L * B * SN * 2 * VH, "stash_ab [2, B, SN, 2*VH]");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && pending.scalar_type() == at::kInt && vstep.scalar_type() == at::kInt,
+              "positions / pending / vstep int32");
+  TORCH_CHECK(positions.numel() == B && pending.numel() == B, "positions / pending: one per sequence");
+  for (const Tensor* t : std::initializer_list<const Tensor*>{&qkv, &z, &a, &b})
+    TORCH_CHECK(t->dim() == 2 && t->size(0) == (long)B * n_tok && t->stride(1) == 1, "rows [B*n_tok, *]");
+  TORCH_CHECK(a.stride(0) == b.stride(0), "a and b share a row stride");
+  TORCH_CHECK(qkv.size(1) == C && z.size(1) == (long)VH * 128 && a.size(1) == VH, "row widths");
+  const c10::cuda::CUDAGuard guard(state.device());
+  auto out = at::empty({(long)B * n_tok, (long)VH * 128}, qkv.options());
+  DnVerifyArgs p{};
+  p.qkv = cbf(qkv);
+  p.qkv_row = qkv.stride(0);
+  p.z = cbf(z);
+  p.z_row = z.stride(0);
+  p.a = cbf(a);
+  p.b = cbf(b);
+  p.ab_row = a.stride(0);
+  p.stash_qkv = mbf(stash_qkv);
+  p.stash_ab = mbf(stash_ab);
+  p.stash_n = (int)SN;
+  p.vstep = vstep.data_ptr<int>();
+  p.conv_ring = mbf(conv_ring);
+  p.ring_slots = (int)conv_ring.size(1);
+  p.state = state.data_ptr();
+  p.state_bf16 = state.scalar_type() == at::kBFloat16;
+  p.positions = positions.data_ptr<int>();
+  p.pending = pending.data_ptr<int>();
+  p.conv_w = conv_w.data_ptr<float>();
+  p.A_log = A_log.data_ptr<float>();
+  p.dt_bias = dt_bias.data_ptr<float>();
+  p.norm_w = norm_w.data_ptr<float>();
+  p.out = mbf(out);
+  p.out_row = out.stride(0);
+  p.status = status_dev_ptr();
+  p.batch = B;
+  p.n_tok = (int)n_tok;
+  p.k_heads = (int)k_heads;
+  p.v_heads = VH;
+  p.l2_eps = 1e-6f;
+  p.norm_eps = (float)eps;
+  deltanet_verify(p, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
 void register_ext_defs(torch::Library& m) {
+  m.def(
+      "deltanet_verify(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) stash_qkv, Tensor(b!) stash_ab, "
+      "Tensor vstep, Tensor(c!) conv_ring, Tensor(d!) state, Tensor positions, Tensor pending, Tensor conv_w, "
+      "Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, int n_tok, float eps) -> Tensor");
   m.def("rope_interleaved_(Tensor(a!) x, Tensor cos, Tensor sin, Tensor pos) -> ()");
   register_comm_defs(m);
   m.def("moe_topk(Tensor logits, int k, bool renorm, Tensor? bias, int mode, float route_scale) -> (Tensor, Tensor)");
@@ -345,6 +416,7 @@ void register_ext_defs(torch::Library& m) {
 }
 void register_ext_impls(torch::Library& m) {
   register_comm_impls(m);
+  m.impl("deltanet_verify", &deltanet_verify_op);
   m.impl("moe_topk", &moe_topk_op);
   m.impl("moe_experts", &moe_experts_op);
   m.impl("hc_pre", &hc_pre_op);
