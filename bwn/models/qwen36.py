@@ -39,7 +39,7 @@ from ..parallel.comm import Comm
 class Qwen36State:
     """Static per-sequence decode state (one writer per buffer per step)."""
 
-    conv: torch.Tensor       # [L_dn, B, 4, C]  conv ring (slot = position % 4)
+    conv: torch.Tensor       # [L_dn, B, R, C]  conv ring (slot = position % R; R = 4, or 8 for verify)
     ssm: torch.Tensor        # [L_dn, B, VH, 128, 128]  recurrent state
     k_cache: torch.Tensor    # [L_gqa, B, KVH, S_max, D]
     v_cache: torch.Tensor
@@ -61,6 +61,17 @@ class Qwen36State:
 
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.conv, self.ssm, self.k_cache, self.v_cache))
+
+
+@dataclass
+class SpecBuffers:
+    """Per-sequence buffers of speculative verification (deferred DeltaNet commit)."""
+
+    n_tok: int               # tokens verified per step (drafts + 1)
+    stash_qkv: torch.Tensor  # [L_dn, 2, B, n_tok, C] raw rows of the last verify, by step parity
+    stash_ab: torch.Tensor   # [L_dn, 2, B, n_tok, 2*VH]
+    pending: torch.Tensor    # [B] accepted tokens of the last verify not yet committed
+    vstep: torch.Tensor      # [1] verify step counter (selects the stash parity)
 
 
 class Qwen36Model(nn.Module):
@@ -128,11 +139,14 @@ class Qwen36Model(nn.Module):
         return n + sum(nb(v) for v in self.g.values())
 
     # ----------------------------------------------------------------- state
-    def new_state(self, batch: int, max_seq: int, ssm_dtype=torch.float32) -> Qwen36State:
+    def new_state(self, batch: int, max_seq: int, ssm_dtype=torch.float32, ring_slots: int | None = None) -> Qwen36State:
+        """Static decode buffers.  ``ring_slots`` (default the conv kernel size) is
+        the position-addressed conv ring; speculative verify needs 8."""
         cfg, d = self.cfg, self.d
         dev = self.device
+        R = ring_slots or cfg.conv_kernel
         st = Qwen36State(
-            conv=torch.zeros(cfg.num_deltanet, batch, cfg.conv_kernel, d.dn_qkv_dim, dtype=self.dtype, device=dev),
+            conv=torch.zeros(cfg.num_deltanet, batch, R, d.dn_qkv_dim, dtype=self.dtype, device=dev),
             ssm=torch.zeros(cfg.num_deltanet, batch, d.dn_v_heads, cfg.dn_k_dim, cfg.dn_v_dim, dtype=ssm_dtype,
                             device=dev),
             k_cache=torch.zeros(cfg.num_gqa, batch, d.kv_heads, max_seq, cfg.head_dim, dtype=self.dtype, device=dev),
@@ -220,6 +234,89 @@ class Qwen36Model(nn.Module):
         st.positions.add_(1)
         return h
 
+    # ------------------------------------------------------ speculative verify
+    def new_spec_state(self, batch: int, n_tok: int) -> "SpecBuffers":
+        """Stash / pending / step-counter buffers of multi-token verification
+        (the decode state must come from ``new_state(..., ring_slots=8)``)."""
+        d = self.d
+        dev = self.device
+        return SpecBuffers(
+            n_tok=n_tok,
+            stash_qkv=torch.zeros(self.cfg.num_deltanet, 2, batch, n_tok, d.dn_qkv_dim, dtype=self.dtype, device=dev),
+            stash_ab=torch.zeros(self.cfg.num_deltanet, 2, batch, n_tok, 2 * d.dn_v_heads, dtype=self.dtype,
+                                 device=dev),
+            pending=torch.zeros(batch, dtype=torch.int32, device=dev),
+            vstep=torch.zeros(1, dtype=torch.int32, device=dev),
+        )
+
+    def verify_hidden(self, tokens: torch.Tensor, st: Qwen36State, sp: "SpecBuffers",
+                      feat_layers: tuple[int, ...] = ()) -> tuple[torch.Tensor, list[torch.Tensor]]:
+        """Target forward over ``tokens [B, N]`` at positions ``st.positions + i``
+        without committing them: DeltaNet layers first commit ``sp.pending`` tokens
+        of the previous verify and only read the new ones; GQA layers write K/V at
+        the new positions (overwritten later if rejected).  Positions are not
+        advanced (the acceptance does it).  Returns the final-normed hidden
+        ``[B*N, H]`` and the residual stream after each of ``feat_layers``."""
+        cfg, d = self.cfg, self.d
+        B, N = tokens.shape
+        T = B * N
+        pos_rows = (st.positions[:, None] + torch.arange(N, device=tokens.device, dtype=torch.int32)[None]).reshape(T)
+        x = O.embedding(tokens.reshape(T).int(), self.g["embed"], 0)
+        h = O.rms_norm(x, self.layers[0]["in_norm"], cfg.rms_eps)
+        feats = []
+        di = gi = 0
+        for i in range(cfg.num_layers):
+            L = self.layers[i]
+            if cfg.layer_type(i) == "deltanet":
+                C, Z, VH = d.dn_qkv_dim, d.dn_value_dim, d.dn_v_heads
+                proj = O.linear(h, L["in_proj"])
+                o = O.deltanet_verify(proj[:, :C], proj[:, C:C + Z], proj[:, C + Z + VH:], proj[:, C + Z:C + Z + VH],
+                                      sp.stash_qkv[di], sp.stash_ab[di], sp.vstep, st.conv[di], st.ssm[di],
+                                      st.positions, sp.pending, L["conv_w"], L["A_log"], L["dt_bias"], L["norm_w"],
+                                      d.dn_k_heads, N, cfg.rms_eps)
+                h = self._row_parallel(o, L["out_proj"], x, L["post_norm"])
+                di += 1
+            else:
+                D, QH, KVH = cfg.head_dim, d.q_heads, d.kv_heads
+                proj = O.linear(h, L["qkv_proj"])
+                qg = proj[:, :QH * 2 * D].view(T, QH, 2 * D)
+                k = proj[:, QH * 2 * D:QH * 2 * D + KVH * D].view(T, KVH, D)
+                v = proj[:, QH * 2 * D + KVH * D:].view(T, KVH, D)
+                o = O.gqa_decode(qg, k, v, L["q_norm"], L["k_norm"], self.rope_cos, self.rope_sin, st.k_cache[gi],
+                                 st.v_cache[gi], pos_rows, cfg.rms_eps, 0, N)
+                h = self._row_parallel(o, L["o_proj"], x, L["post_norm"])
+                gi += 1
+            nxt = self.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else self.g["final_norm"]
+            if cfg.is_moe:
+                h = self._reduce_add_norm(self._mlp(i, h), x, nxt)
+            else:
+                h = self._row_parallel(self._mlp(i, h), L["down"], x, nxt)
+            if i in feat_layers:
+                feats.append((i, x.clone()))
+        by_layer = dict(feats)
+        return h, [by_layer[i] for i in feat_layers]
+
+    def commit_pending(self, st: Qwen36State, sp: "SpecBuffers") -> None:
+        """Fold the last verify's accepted tokens into the DeltaNet states (a
+        verify with no new tokens); afterwards plain decode steps may follow."""
+        cfg, d = self.cfg, self.d
+        B = st.positions.shape[0]
+        dev = st.positions.device
+        C, VH = d.dn_qkv_dim, d.dn_v_heads
+        empty = torch.zeros(0, C + d.dn_value_dim + 2 * VH, dtype=self.dtype, device=dev)
+        di = 0
+        for i in range(cfg.num_layers):
+            if cfg.layer_type(i) != "deltanet":
+                continue
+            L = self.layers[i]
+            O.deltanet_verify(empty[:, :C], empty[:, C:C + d.dn_value_dim], empty[:, :VH], empty[:, :VH],
+                              sp.stash_qkv[di], sp.stash_ab[di], sp.vstep, st.conv[di], st.ssm[di], st.positions,
+                              sp.pending, L["conv_w"], L["A_log"], L["dt_bias"], L["norm_w"], d.dn_k_heads, 0,
+                              cfg.rms_eps)
+            di += 1
+        sp.pending.zero_()
+        sp.vstep.add_(1)
+
     def greedy(self, h: torch.Tensor) -> torch.Tensor:
         """Vocab-sharded LM head + greedy with the lowest-id tie break
         (``static_decode_35b.py:1534-1564``) as a single int64 max all-reduce."""
@@ -242,14 +339,14 @@ class Qwen36Model(nn.Module):
 
     # --------------------------------------------------------------- prefill
     def prefill_hidden(self, tokens: torch.Tensor, st: Qwen36State, valid_len: torch.Tensor | None = None,
-                       chunk: int = 64) -> torch.Tensor:
+                       chunk: int = 64, feat_layers: tuple[int, ...] = (), feats_out: list | None = None) -> torch.Tensor:
         """Process a prompt chunk ``tokens [B, S]`` starting at ``st.positions``
         (all rows share the start position, as in the reference's bucketed
         prefill, ``static_decode_35b.py:2497-2678``).  ``valid_len [B]`` marks
         real rows; pad rows leave every state untouched.  Returns the final-normed
         hidden of each row's last valid token ``[B, H]``."""
         from . import qwen36_prefill as P
-        return P.prefill_hidden(self, tokens, st, valid_len, chunk)
+        return P.prefill_hidden(self, tokens, st, valid_len, chunk, feat_layers, feats_out)
 
     def prefill(self, tokens: torch.Tensor, st: Qwen36State, valid_len=None, bucket: int = 0) -> torch.Tensor:
         """Bucketed prefill (``prefill_bucketed``): chunks of ``bucket`` tokens

@@ -18,7 +18,11 @@ import torch
 from .. import ops as O
 
 
-def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64) -> torch.Tensor:
+def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, feat_layers=(), feats_out=None,
+                   all_rows: bool = False) -> torch.Tensor:
+    """Returns the final-normed hidden of each sequence's last valid row ``[B, H]``
+    (every row ``[B*S, H]`` with ``all_rows``); the residual stream after each of
+    ``feat_layers`` is appended to ``feats_out`` (``[B*S, H]``, for EAGLE3)."""
     cfg, d = model.cfg, model.d
     B, S = tokens.shape
     dev = tokens.device
@@ -30,6 +34,7 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64) 
     T = B * S
     x = O.embedding(tokens.reshape(T).int(), model.g["embed"], 0)  # [T, H]
     h = O.rms_norm(x, model.layers[0]["in_norm"], cfg.rms_eps)
+    captured = {}
     di = gi = 0
     for i in range(cfg.num_layers):
         L = model.layers[i]
@@ -59,6 +64,12 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64) 
         else:
             act = model._mlp(i, h)
             h = model._row_parallel(act, L["down"], x, nxt)
+        if feats_out is not None and i in feat_layers:
+            captured[i] = x.clone()
+    if feats_out is not None:
+        feats_out.extend(captured[i] for i in feat_layers)
     st.positions.add_(valid_len)
+    if all_rows:
+        return h
     last = (valid_len.long() - 1).clamp(min=0) + torch.arange(B, device=dev) * S
     return h[last]
