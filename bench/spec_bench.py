@@ -53,14 +53,10 @@ def main():
     draft = Eagle3Draft(eagle3_config(cfg), dev).init_random(1)
     prompt = torch.randint(0, cfg.vocab, (B, S), generator=torch.Generator().manual_seed(1234))
 
-    # plain greedy decode: the continuation (for the oracle draft), then time per step
+    # plain greedy decode
     dec = StaticDecoder(target, B, max_seq + args.steps + args.warmup)
     dec.capture()
-    cont = [dec.prefill(prompt).clone()]
-    for _ in range(gen_len):
-        dec.step_device()
-        cont.append(dec.next_ids.clone())
-    truth = torch.stack(cont, 1)
+    dec.prefill(prompt)
     for _ in range(args.warmup):
         dec.step_device()
     plain_ms = _time(dec.step_device, args.steps)
@@ -70,6 +66,18 @@ def main():
     torch.cuda.empty_cache()
 
     res = {}
+    # random draft: the emitted sequence is the target's greedy continuation under
+    # the verify kernels; it is also the oracle for the all-accepted run
+    sd = SpecDecoder(target, draft, B, max_seq, num_draft=K)
+    cont = [[int(v)] for v in sd.prefill(prompt).cpu()]
+    sd.capture()
+    while min(len(c) for c in cont) < gen_len:
+        ids, cnt = sd.step()
+        for b in range(B):
+            cont[b].extend(int(v) for v in ids[b, :int(cnt[b])])
+    truth = torch.tensor([c[:gen_len] for c in cont])
+    sd.release()
+    del sd
     for mode in ("random_draft", "oracle_draft"):
         sd = SpecDecoder(target, draft, B, max_seq, num_draft=K)
         if mode == "oracle_draft":

@@ -3,10 +3,11 @@
 * Row-parallel GEMM -> all-reduce -> residual add -> RMSNorm (the reference's
   ``o_proj/out_proj/down_proj`` + ``functional_all_reduce`` + next norm,
   ``contrib/qwen3.6-27b/static_decode.py:798-961``): the tcgen05 GEMM epilogue
-  reduces fp32 partial tiles into an NVLS multicast buffer with
-  ``multimem.red`` (the switch adds every rank's contribution into every
-  rank's copy), the last CTA publishes an epoch flag to all ranks, and one small
-  kernel per rank waits for the flags, adds the residual and normalises.
+  stores its bf16 partial into this rank's slot of a symmetric buffer and the
+  last CTA publishes an epoch flag to every rank; one small kernel per rank
+  waits for the flags, reads the sum of all ranks' slots with
+  ``multimem.ld_reduce`` (the NVSwitch adds them, fp32 accumulation), adds the
+  residual and normalises.
 * Sharded greedy (``static_decode_35b.py:1534-1564``): packed (logit, id) keys
   exchanged by peer stores, max taken on every rank, one launch.
 
@@ -45,8 +46,8 @@ class FusedComm:
             pass
         slots_bytes = 8 * max_rows * 8
         self.ar_off = ((self.SLOTS + slots_bytes + 255) // 256) * 256
-        self.buf_floats = max_rows * hidden
-        total = self.ar_off + 2 * self.buf_floats * 4
+        self.buf_elems = max_rows * hidden  # bf16 elements per slot (two slots)
+        total = self.ar_off + 2 * self.buf_elems * 2
         self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
         self.buf.zero_()
         torch.cuda.synchronize(dev)
@@ -74,15 +75,16 @@ class FusedComm:
         if hasattr(w, "w8"):  # FP8 weight: W8A16 GEMM, then the multicast reduction
             from .. import ops as O
             return self.allreduce_add_norm(O.linear(a, w), x, norm_w, eps)
-        o.gemm_mcred(a, w, self.mc_ar, self.buf_floats, w.shape[0], self.peer_flags_ar, self.state, self.rank)
-        return o.ar_add_norm(self.local_ar, self.buf_floats, self.peer_flags_ar[self.rank], self.world, self.state,
+        o.gemm_symm(a, w, self.local_ar, self.buf_elems, w.shape[0], self.peer_flags_ar, self.state, self.rank)
+        return o.ar_add_norm(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
                              x, norm_w, eps, self.timeout_s)
 
     def allreduce_add_norm(self, part: torch.Tensor, x: torch.Tensor, norm_w: torch.Tensor,
                            eps: float) -> torch.Tensor:
         o = ops()
-        o.mc_red_signal(part, self.mc_ar, self.buf_floats, self.peer_flags_ar, self.state, self.rank)
-        return o.ar_add_norm(self.local_ar, self.buf_floats, self.peer_flags_ar[self.rank], self.world, self.state,
+        o.symm_put_signal(part.contiguous(), self.local_ar, self.buf_elems, self.peer_flags_ar, self.state,
+                          self.rank)
+        return o.ar_add_norm(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
                              x, norm_w, eps, self.timeout_s)
 
     def greedy(self, keys: torch.Tensor) -> torch.Tensor:

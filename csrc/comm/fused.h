@@ -8,11 +8,11 @@
 
 namespace bwn {
 
-void mc_red_signal(const __nv_bfloat16* x, long ldx, int rows, int cols, float* mc_base, const CommSignal& sig,
-                   cudaStream_t st);
+void symm_put_signal(const __nv_bfloat16* x, long ldx, int rows, int cols, __nv_bfloat16* local_base,
+                     const CommSignal& sig, cudaStream_t st);
 
 struct ArNormArgs {
-  float* local_base;       // this rank's unicast view of the two fp32 reduce buffers
+  const __nv_bfloat16* mc_base;  // multicast address of the two bf16 partial slots
   long buf_stride;
   int* sel;                // [2]: selector, CTA ticket
   const unsigned* flags;   // this rank's flag array (slot r written by rank r)

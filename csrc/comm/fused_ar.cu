@@ -3,28 +3,48 @@
 // Row-parallel projections (o_proj, out_proj, down_proj) are followed by an
 // all-reduce in the reference (functional_all_reduce after every row-parallel
 // GEMM, contrib/qwen3.6-27b/static_decode.py:798-961; static_decode_35b.py:1972,
-// 2110, 1278).  Here the tcgen05 GEMM epilogue reduces its fp32 partial tiles
-// straight into an NVLS multicast buffer (multimem.red; csrc/kernels/gemm_tc.cu,
-// kEpiMcRed) and publishes an epoch flag to every rank; the kernels below
+// 2110, 1278).  Here it is a one-shot reduction through the switch:
 //
-//  * mc_red_signal_kernel  do the same for a partial that is already in memory
-//                          (MoE output, embedding), and
-//  * ar_add_norm_kernel    wait for all ranks' flags (bounded), add the reduced
-//                          row to the residual stream, RMSNorm(1+w) it, and zero
-//                          the local copy for its next use (two buffers
-//                          alternate under a device-side selector, so a CUDA
-//                          graph replays the same launches), and
-//  * greedy_allmax_kernel  exchange per-rank packed (logit, id) argmax keys by
-//                          peer stores and take the max: the sharded greedy of
-//                          static_decode_35b.py:1534-1564 in one launch.
-// Every wait gives up after a bounded time and sets a status bit instead of
-// hanging the GPU.
+//  * the tcgen05 GEMM epilogue (csrc/kernels/gemm_tc.cu, kEpiSymm) stores its
+//    bf16 partial into this rank's slot of a symmetric buffer pair -- plain
+//    local stores -- and its last CTA release-stores an epoch flag into every
+//    rank's flag array; symm_put_signal_kernel does the same for a partial
+//    already in memory (MoE output);
+//  * ar_add_norm_kernel waits (bounded) for every rank's flag, reads the sum of
+//    all ranks' partials with multimem.ld_reduce on the multicast address (the
+//    NVSwitch adds the eight copies with fp32 accumulation, 16 bytes per
+//    request), adds the residual, RMSNorm(1+w)s the row, and flips the slot
+//    selector once all its CTAs have read;
+//  * greedy_allmax_kernel exchanges per-rank packed (logit, id) argmax keys by
+//    peer stores and takes the max: the sharded greedy of
+//    static_decode_35b.py:1534-1564 in one launch.
+// Two slots alternate under a device-side selector so a CUDA graph replays the
+// same launches; a slot is rewritten only after every rank has passed the next
+// flag barrier, i.e. after every rank finished reading it.  Every wait gives up
+// after a bounded time and sets a status bit instead of hanging the GPU.
 #include "comm/fused.h"
 #include "common/host.h"
 #include "common/launch.cuh"
 #include "common/sm100.cuh"
 
 namespace bwn {
+
+// Thread r (< world) waits for rank r's flag to reach `epoch`; all ranks' flags
+// are polled in parallel.  Callers follow with a CTA barrier.
+__device__ __forceinline__ bool wait_flag_lane(const unsigned* flags, int world, unsigned epoch, int* status,
+                                               uint64_t limit_ns) {
+  const int r = threadIdx.x;
+  if (r >= world) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while ((int)(ld_acquire_sys(flags + r) - epoch) < 0) {
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
+      set_status(status, kStatusPeerTimeout);
+      return false;
+    }
+  }
+  return true;
+}
 
 __device__ __forceinline__ bool wait_flags(const unsigned* flags, int world, unsigned epoch, int* status,
                                            uint64_t limit_ns) {
@@ -41,37 +61,37 @@ __device__ __forceinline__ bool wait_flags(const unsigned* flags, int world, uns
   return true;
 }
 
+// Completion of a producer grid: each CTA (one thread, after a CTA barrier)
+// orders its stores before a ticket; the last CTA publishes the new epoch to
+// every rank's flag array (one system fence, then relaxed stores).
 __device__ __forceinline__ void signal_done(const CommSignal& sig) {
-  // caller: one thread per CTA, after a CTA-wide barrier
-  fence_acq_rel_sys();
+  __threadfence();
   const int t = atomicAdd(sig.done_ticket, 1);
   if (t == (int)gridDim.x - 1) {
     *sig.done_ticket = 0;
     fence_acq_rel_sys();
     const unsigned e = (unsigned)(*sig.epoch) + 1u;
     *sig.epoch = (int)e;
-    for (int r = 0; r < sig.world; ++r) st_release_sys(sig.peer_flags[r] + sig.rank, e);
+    for (int r = 0; r < sig.world; ++r) st_relaxed_sys_u32(sig.peer_flags[r] + sig.rank, e);
   }
 }
 
-__global__ void __launch_bounds__(256) mc_red_signal_kernel(const __nv_bfloat16* __restrict__ x, long ldx, int rows,
-                                                            int cols, float* mc_base, CommSignal sig) {
+__global__ void __launch_bounds__(256) symm_put_signal_kernel(const __nv_bfloat16* __restrict__ x, long ldx, int rows,
+                                                              int cols, __nv_bfloat16* local_base, CommSignal sig) {
   pdl_trigger();
   pdl_wait();
-  float* mc = mc_base + (long)((*sig.sel) & 1) * sig.buf_stride;
-  const long n = (long)rows * cols;
-  for (long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 2; i < n; i += (long)gridDim.x * blockDim.x * 2) {
-    const long r = i / cols, c = i % cols;
-    const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + r * ldx + c));
-    mc_red_add_f32(mc + r * cols + c, v.x);
-    mc_red_add_f32(mc + r * cols + c + 1, v.y);
+  __nv_bfloat16* dst = local_base + (long)((*sig.sel) & 1) * sig.buf_stride;
+  const int c8 = cols >> 3;
+  const long n = (long)rows * c8;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / c8, c = (i % c8) * 8;
+    *reinterpret_cast<uint4*>(dst + r * cols + c) = *reinterpret_cast<const uint4*>(x + r * ldx + c);
   }
-  fence_acq_rel_sys();
-  __syncthreads();
+  __syncthreads();  // the CTA's stores precede thread 0's system-scope fence in signal_done
   if (threadIdx.x == 0) signal_done(sig);
 }
 
-__global__ void __launch_bounds__(256) ar_add_norm_kernel(float* local_base, long buf_stride, int* sel,
+__global__ void __launch_bounds__(256) ar_add_norm_kernel(const __nv_bfloat16* mc_base, long buf_stride, int* sel,
                                                           const unsigned* flags, int world, const int* epoch,
                                                           __nv_bfloat16* __restrict__ resid, long ldr,
                                                           const float* __restrict__ w, __nv_bfloat16* __restrict__ out,
@@ -81,20 +101,37 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(float* local_base, lon
   pdl_wait();
   const int row = blockIdx.x;
   __shared__ float red[8];
-  if (threadIdx.x == 0) wait_flags(flags, world, (unsigned)(*epoch), status, limit_ns);
+  wait_flag_lane(flags, world, (unsigned)(*epoch), status, limit_ns);
   __syncthreads();
-  float* buf = local_base + (long)((*sel) & 1) * buf_stride + (long)row * cols;
+  const __nv_bfloat16* buf = mc_base + (long)((*sel) & 1) * buf_stride + (long)row * cols;
+  constexpr int kMaxVec = 4;  // 8 columns per vector, 256 threads: cols <= 8192
+  float v[kMaxVec][8];
   float ss = 0.f;
-  constexpr int kMaxPerThread = 32;
-  float v[kMaxPerThread];
-  int n = 0;
-  for (int c = threadIdx.x; c < cols && n < kMaxPerThread; c += blockDim.x, ++n) {
-    const float x = __ldcg(buf + c);
-    const float r = __bfloat162float(__float2bfloat16(__bfloat162float(resid[(long)row * ldr + c]) + x));
-    resid[(long)row * ldr + c] = __float2bfloat16(r);
-    buf[c] = 0.f;  // ready for this buffer's next use
-    v[n] = r;
-    ss += r * r;
+  // issue every reduction load first so their switch round trips overlap
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c < cols) mc_ld_reduce_bf16x8(buf + c, v[n]);
+  }
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c >= cols) continue;
+    const uint4 rr = *reinterpret_cast<const uint4*>(resid + (long)row * ldr + c);
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 rf = __bfloat1622float2(r2[e]);
+      const __nv_bfloat162 nb = __floats2bfloat162_rn(rf.x + v[n][2 * e], rf.y + v[n][2 * e + 1]);
+      o2[e] = nb;
+      const float2 nf = __bfloat1622float2(nb);
+      v[n][2 * e] = nf.x;
+      v[n][2 * e + 1] = nf.y;
+      ss += nf.x * nf.x + nf.y * nf.y;
+    }
+    *reinterpret_cast<uint4*>(resid + (long)row * ldr + c) = o;
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -102,10 +139,18 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(float* local_base, lon
   float tot = 0.f;
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
   const float inv = rsqrtf(tot / cols + eps);
-  n = 0;
-  for (int c = threadIdx.x; c < cols && n < kMaxPerThread; c += blockDim.x, ++n)
-    out[(long)row * ldo + c] = __float2bfloat16(v[n] * inv * (1.f + w[c]));
-  // flip the buffer selector once every CTA has read it: last CTA (ticket)
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c >= cols) continue;
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o2[e] = __floats2bfloat162_rn(v[n][2 * e] * inv * (1.f + w[c + 2 * e]), v[n][2 * e + 1] * inv * (1.f + w[c + 2 * e + 1]));
+    *reinterpret_cast<uint4*>(out + (long)row * ldo + c) = o;
+  }
+  // flip the slot selector once every CTA has read it: last CTA (ticket)
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -135,9 +180,9 @@ __global__ void greedy_allmax_kernel(GreedyArgs a) {
       unsigned long long* dst = reinterpret_cast<unsigned long long*>(peer_slots[r]) + (long)rank * rows + i;
       asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"((unsigned long long)keys[i]) : "memory");
     }
-  fence_acq_rel_sys();
   __syncthreads();
   if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
     const unsigned e = (unsigned)(*epoch) + 1u;
     *epoch = (int)e;
     for (int r = 0; r < world; ++r) st_release_sys(peer_flags[r] + rank, e);
@@ -156,18 +201,20 @@ __global__ void greedy_allmax_kernel(GreedyArgs a) {
   }
 }
 
-void mc_red_signal(const __nv_bfloat16* x, long ldx, int rows, int cols, float* mc_base, const CommSignal& sig,
-                   cudaStream_t st) {
-  BWN_CHECK(cols % 2 == 0 && ldx % 2 == 0, "mc_red_signal: even columns");
-  long n = (long)rows * cols / 2;
+void symm_put_signal(const __nv_bfloat16* x, long ldx, int rows, int cols, __nv_bfloat16* local_base,
+                     const CommSignal& sig, cudaStream_t st) {
+  BWN_CHECK(cols % 8 == 0 && ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+            "symm_put_signal: 16-byte aligned rows");
+  const long n = (long)rows * cols / 8;
   int grid = (int)std::min<long>((n + 255) / 256, num_sms());
   if (grid < 1) grid = 1;
-  launch_k(mc_red_signal_kernel, dim3(grid), dim3(256), 0, st, x, ldx, rows, cols, mc_base, sig);
+  launch_k(symm_put_signal_kernel, dim3(grid), dim3(256), 0, st, x, ldx, rows, cols, local_base, sig);
 }
 
 void ar_add_norm(const ArNormArgs& a, cudaStream_t st) {
-  BWN_CHECK(a.cols <= 256 * 32, "ar_add_norm: hidden too wide");
-  launch_k(ar_add_norm_kernel, dim3(a.rows), dim3(256), 0, st, a.local_base, a.buf_stride, a.sel, a.flags, a.world,
+  BWN_CHECK(a.cols % 8 == 0 && a.cols <= 256 * 8 * 4, "ar_add_norm: hidden must be a multiple of 8, at most 8192");
+  BWN_CHECK(a.ldr % 8 == 0 && a.ldo % 8 == 0, "ar_add_norm: 16-byte aligned rows");
+  launch_k(ar_add_norm_kernel, dim3(a.rows), dim3(256), 0, st, a.mc_base, a.buf_stride, a.sel, a.flags, a.world,
            a.epoch, a.resid, a.ldr, a.w, a.out, a.ldo, a.cols, a.eps, a.status, a.limit_ns);
 }
 

@@ -53,7 +53,7 @@ enum GemmEpilogue : int {
   kEpiResid = 1,   // out = bf16(acc + resid)
   kEpiSwiGLU = 2,  // out = bf16(silu(gate) * up), gate/up interleaved in blocks of 16
   kEpiF32 = 3,     // out = acc (fp32)
-  kEpiMcRed = 4,   // multimem.red.add.f32 of acc into an NVLS multicast buffer, then signal peers
+  kEpiSymm = 4,    // bf16 partial into this rank's symmetric buffer slot, then signal every peer
 };
 
 // Completion signalling of a fused compute + collective launch: the last CTA to
@@ -89,7 +89,7 @@ struct GemmProblem {
   int* tickets = nullptr;
   int tickets_len = 0;
   int* status = nullptr;
-  CommSignal sig;  // kEpiMcRed only
+  CommSignal sig;  // kEpiSymm only
 };
 
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);

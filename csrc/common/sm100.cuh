@@ -328,12 +328,27 @@ __device__ __forceinline__ void fence_async_smem() {
 
 namespace bwn {
 // ---- system-scope memory ops for NVLink peers / NVLS multicast ---------------
-__device__ __forceinline__ void mc_red_add_f32(float* mc_addr, float v) {
-  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc_addr), "f"(v) : "memory");
+// 8 bf16 lanes summed over every rank's copy by the NVSwitch (fp32
+// accumulation in the switch, bf16 result), through the multicast address.
+__device__ __forceinline__ void mc_ld_reduce_bf16x8(const void* mc_addr, float (&v)[8]) {
+  uint32_t r[4];
+  // no memory clobber: independent loads stay in flight together; ordering
+  // after the flag acquire comes from the CTA barrier that precedes them
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "l"(mc_addr));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(r[i] << 16);
+    v[2 * i + 1] = __uint_as_float(r[i] & 0xFFFF0000u);
+  }
 }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   unsigned v;

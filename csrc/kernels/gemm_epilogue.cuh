@@ -18,24 +18,19 @@ struct GemmArgs {
   float* workspace;            // splits>1: [tiles * splits * BM * BN] fp32
   int* tickets;                // splits>1: [tiles]
   int* status;
-  CommSignal sig;              // kEpiMcRed: completion signal to peers
+  CommSignal sig;              // kEpiSymm: completion signal to peers
 };
 
 template <int BN, int EPI, bool TRANS>
 __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, const float (&v)[32], int ncols, int m, int n0) {
   // m: global row (A row), n0: global column of v[0]; ncols valid in v (16 or 32)
-  if (EPI == kEpiMcRed) {
-    // out is the multicast address of an fp32 [tokens, ldo] buffer; the switch
-    // adds every rank's (and every split's) partial into all ranks' copies
-    float* out = reinterpret_cast<float*>(a.out) + (long)((*a.sig.sel) & 1) * a.sig.buf_stride;
-    if (m >= a.M) return;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < ncols && n0 + j < a.N) {
-        const long idx = TRANS ? (long)(n0 + j) * a.ldo + m : (long)m * a.ldo + n0 + j;
-        mc_red_add_f32(out + idx, v[j]);
-      }
-    }
+  if (EPI == kEpiSymm) {
+    // out is this rank's bf16 [tokens, ldo] symmetric buffer pair; the slot in
+    // use alternates under the device-side selector.  Peers read it through the
+    // multicast address once the completion flag is published.
+    GemmArgs b = a;
+    b.out = reinterpret_cast<__nv_bfloat16*>(a.out) + (long)((*a.sig.sel) & 1) * a.sig.buf_stride;
+    epi_store_chunk<BN, kEpiBF16, TRANS>(b, v, ncols, m, n0);
     return;
   }
   if (EPI == kEpiF32) {

@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
       const int m = tm * kBM + row;
-      if (args.splits == 1 || EPI == kEpiMcRed) {
+      if (args.splits == 1) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
@@ -312,19 +312,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
-  if (EPI == kEpiMcRed && warp >= 2) {
-    // publish completion: every red of this CTA is performed system-wide before
-    // the ticket; the last CTA bumps the epoch and release-stores it to all ranks
-    fence_acq_rel_sys();
+  if (EPI == kEpiSymm && warp >= 2) {
+    // publish completion: the epilogue warps' stores precede one thread's
+    // system-scope fence (named barrier), then the ticket; the last CTA bumps
+    // the epoch and release-stores it to all ranks
     asm volatile("bar.sync 1, 128;" ::: "memory");
     if (threadIdx.x == 64) {
+      __threadfence();
       const int t = atomicAdd(args.sig.done_ticket, 1);
       if (t == (int)gridDim.x - 1) {
         *args.sig.done_ticket = 0;
         fence_acq_rel_sys();
         const unsigned e = (unsigned)(*args.sig.epoch) + 1u;
         *args.sig.epoch = (int)e;
-        for (int r = 0; r < args.sig.world; ++r) st_release_sys(args.sig.peer_flags[r] + args.sig.rank, e);
+        for (int r = 0; r < args.sig.world; ++r) st_relaxed_sys_u32(args.sig.peer_flags[r] + args.sig.rank, e);
       }
     }
   }
@@ -417,12 +418,11 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   // per persistent CTA measured ~2x slower on decode shapes: each unit's
   // partial round trip and fence serialises the CTA.)
   int splits = 1;
-  const bool mcred = p.epi == kEpiMcRed;  // partials reduce in the switch: no workspace
-  if (p.allow_split && tiles < sms && (mcred || (p.workspace && p.tickets && tiles <= p.tickets_len))) {
+  if (p.allow_split && tiles < sms && p.workspace && p.tickets && tiles <= p.tickets_len) {
     splits = sms / tiles;
     if (splits > a.num_kb / 4) splits = a.num_kb / 4 > 0 ? a.num_kb / 4 : 1;
     if (splits > 16) splits = 16;
-    if (!mcred && (long)tiles * splits * kBM * bn > p.workspace_floats) splits = 1;
+    if ((long)tiles * splits * kBM * bn > p.workspace_floats) splits = 1;
   }
   a.splits = splits;
   a.kb_per_split = (a.num_kb + splits - 1) / splits;
@@ -461,9 +461,9 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
     case kEpiF32:
       tr ? dispatch_bn<kEpiF32, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiF32, false>(bn, ta, tb, a, grid, stream);
       break;
-    case kEpiMcRed:
+    case kEpiSymm:
       BWN_CHECK(p.sig.epoch && p.sig.done_ticket && p.sig.world >= 1 && p.sig.world <= 8, "gemm: bad comm signal");
-      tr ? dispatch_bn<kEpiMcRed, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiMcRed, false>(bn, ta, tb, a, grid, stream);
+      tr ? dispatch_bn<kEpiSymm, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiSymm, false>(bn, ta, tb, a, grid, stream);
       break;
     default: BWN_FAIL("gemm: bad epilogue %d", p.epi);
   }

@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + ab * BN;
       const int m = tm * kW8BM + row;
-      if (args.splits == 1 || EPI == kEpiMcRed) {
+      if (args.splits == 1) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           float v[32];
@@ -325,17 +325,17 @@ __global__ void __launch_bounds__(kW8Threads, 1)
         }
       }
     }
-    if (EPI == kEpiMcRed) {
-      fence_acq_rel_sys();
+    if (EPI == kEpiSymm) {
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
+        __threadfence();
         const int t = atomicAdd(args.sig.done_ticket, 1);
         if (t == (int)gridDim.x - 1) {
           *args.sig.done_ticket = 0;
           fence_acq_rel_sys();
           const unsigned e = (unsigned)(*args.sig.epoch) + 1u;
           *args.sig.epoch = (int)e;
-          for (int r2 = 0; r2 < args.sig.world; ++r2) st_release_sys(args.sig.peer_flags[r2] + args.sig.rank, e);
+          for (int r2 = 0; r2 < args.sig.world; ++r2) st_relaxed_sys_u32(args.sig.peer_flags[r2] + args.sig.rank, e);
         }
       }
     }
@@ -389,13 +389,12 @@ void gemm_w8(const GemmW8Problem& p, cudaStream_t stream) {
   a.tiles_n = (p.N + bn - 1) / bn;
   a.num_kb = (p.K + kW8BK - 1) / kW8BK;
   const int tiles = a.tiles_m * a.tiles_n, sms = num_sms();
-  const bool mcred = p.epi == kEpiMcRed;
   int splits = 1;
-  if (tiles < sms && (mcred || (p.workspace && p.tickets && tiles <= p.tickets_len))) {
+  if (tiles < sms && p.workspace && p.tickets && tiles <= p.tickets_len) {
     splits = sms / tiles;
     if (splits > a.num_kb / 2) splits = a.num_kb / 2 > 0 ? a.num_kb / 2 : 1;
     if (splits > 16) splits = 16;
-    if (!mcred && (long)tiles * splits * kW8BM * bn > p.workspace_floats) splits = 1;
+    if ((long)tiles * splits * kW8BM * bn > p.workspace_floats) splits = 1;
   }
   a.kb_per_split = (a.num_kb + splits - 1) / splits;
   a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
@@ -415,7 +414,7 @@ void gemm_w8(const GemmW8Problem& p, cudaStream_t stream) {
     case kEpiResid: w8_bn<kEpiResid>(bn, ta, tb, a, p.scales, p.lds, grid, stream); break;
     case kEpiSwiGLU: w8_bn<kEpiSwiGLU>(bn, ta, tb, a, p.scales, p.lds, grid, stream); break;
     case kEpiF32: w8_bn<kEpiF32>(bn, ta, tb, a, p.scales, p.lds, grid, stream); break;
-    case kEpiMcRed: w8_bn<kEpiMcRed>(bn, ta, tb, a, p.scales, p.lds, grid, stream); break;
+    case kEpiSymm: w8_bn<kEpiSymm>(bn, ta, tb, a, p.scales, p.lds, grid, stream); break;
     default: BWN_FAIL("gemm_w8: bad epilogue");
   }
 }

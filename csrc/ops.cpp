@@ -41,10 +41,6 @@ static void check_rowmajor(const Tensor& t, const char* name) {
 }
 
 // ---- per (device, stream) scratch for split-K / split-KV ------------------
-struct Scratch {
-  Tensor ws;
-  Tensor tickets;
-};
 static std::mutex g_scratch_mu;
 static std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 
@@ -69,7 +65,7 @@ Scratch& scratch_for(const Tensor& like, long floats, long tickets) {
 // ---------------------------------------------------------------------------
 // GEMM
 // ---------------------------------------------------------------------------
-static constexpr int kSwapMaxTokens = 128;
+static constexpr int kSwapMaxTokens = 256;  // tokens up to one 256-wide N tile: weights stream once
 
 // out[M_tok, N_out] (+)= x[M_tok, K] . w[N_w, K]^T with the chosen epilogue.
 void linear_into(const Tensor& x, const Tensor& w, const Tensor& out, int64_t epi, const c10::optional<Tensor>& resid) {

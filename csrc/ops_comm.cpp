@@ -31,17 +31,19 @@ static CommSignal make_sig(const std::vector<int64_t>& peer_flags, const Tensor&
   return s;
 }
 
-void gemm_mcred_op(const Tensor& x, const Tensor& w, int64_t mc_base, int64_t buf_stride, int64_t ldo,
-                   std::vector<int64_t> peer_flags, const Tensor& local_state, int64_t rank) {
+// Row-parallel GEMM whose epilogue stores the bf16 partial into this rank's
+// symmetric slot and publishes the completion flag to every rank.
+void gemm_symm_op(const Tensor& x, const Tensor& w, int64_t local_base, int64_t buf_stride, int64_t ldo,
+                  std::vector<int64_t> peer_flags, const Tensor& local_state, int64_t rank) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w.dim() == 2 && w.stride(1) == 1, "row-major x, w");
   const c10::cuda::CUDAGuard guard(x.device());
   const int M = (int)x.size(0), Nw = (int)w.size(0), K = (int)x.size(1);
   GemmProblem p;
-  p.epi = kEpiMcRed;
+  p.epi = kEpiSymm;
   p.status = status_dev_ptr();
-  const bool swap = M <= 128;
+  const bool swap = M <= 256;
   if (swap) {
     p.A = w.data_ptr();
     p.lda = w.stride(0);
@@ -59,23 +61,33 @@ void gemm_mcred_op(const Tensor& x, const Tensor& w, int64_t mc_base, int64_t bu
     p.N = Nw;
   }
   p.K = K;
-  p.out = reinterpret_cast<void*>(mc_base);
+  p.out = reinterpret_cast<void*>(local_base);
   p.ldo = ldo;
   p.sig = make_sig(peer_flags, local_state, rank, buf_stride);
+  const int bn = gemm_pick_bn(p.N);
+  const int tiles = ((p.M + 127) / 128) * ((p.N + bn - 1) / bn);
+  const int sms = num_sms();
+  if (tiles < 2 * sms) {
+    Scratch& s = scratch_for(x, 4L * sms * 128 * bn, 2 * sms);
+    p.workspace = s.ws.data_ptr<float>();
+    p.workspace_floats = s.ws.numel();
+    p.tickets = s.tickets.data_ptr<int>();
+    p.tickets_len = (int)s.tickets.numel();
+  }
   gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
 }
 
-void mc_red_signal_op(const Tensor& x, int64_t mc_base, int64_t buf_stride, std::vector<int64_t> peer_flags,
-                      const Tensor& local_state, int64_t rank) {
+void symm_put_signal_op(const Tensor& x, int64_t local_base, int64_t buf_stride, std::vector<int64_t> peer_flags,
+                        const Tensor& local_state, int64_t rank) {
   check_bf16(x, "x");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [rows, cols]");
   const c10::cuda::CUDAGuard guard(x.device());
-  mc_red_signal(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)x.size(0), (int)x.size(1),
-                reinterpret_cast<float*>(mc_base), make_sig(peer_flags, local_state, rank, buf_stride),
-                at::cuda::getCurrentCUDAStream().stream());
+  symm_put_signal(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)x.size(0), (int)x.size(1),
+                  reinterpret_cast<__nv_bfloat16*>(local_base), make_sig(peer_flags, local_state, rank, buf_stride),
+                  at::cuda::getCurrentCUDAStream().stream());
 }
 
-Tensor ar_add_norm_op(int64_t local_base, int64_t buf_stride, int64_t flags_local, int64_t world,
+Tensor ar_add_norm_op(int64_t mc_base, int64_t buf_stride, int64_t flags_local, int64_t world,
                       const Tensor& local_state, Tensor residual, const Tensor& w, double eps, double timeout_s) {
   check_bf16(residual, "residual");
   check_f32(w, "w");
@@ -83,7 +95,7 @@ Tensor ar_add_norm_op(int64_t local_base, int64_t buf_stride, int64_t flags_loca
   const c10::cuda::CUDAGuard guard(residual.device());
   auto out = at::empty_like(residual, residual.options().memory_format(at::MemoryFormat::Contiguous));
   ArNormArgs a{};
-  a.local_base = reinterpret_cast<float*>(local_base);
+  a.mc_base = reinterpret_cast<const __nv_bfloat16*>(mc_base);
   a.buf_stride = buf_stride;
   int* ls = local_state.data_ptr<int>();
   a.sel = ls + 2;
@@ -131,19 +143,21 @@ Tensor greedy_allmax_op(const Tensor& keys, std::vector<int64_t> peer_slots, std
 
 void register_comm_defs(torch::Library& m) {
   m.def(
-      "gemm_mcred(Tensor x, Tensor w, int mc_base, int buf_stride, int ldo, int[] peer_flags, Tensor(a!) local_state, "
-      "int rank) -> ()");
-  m.def("mc_red_signal(Tensor x, int mc_base, int buf_stride, int[] peer_flags, Tensor(a!) local_state, int rank) -> ()");
+      "gemm_symm(Tensor x, Tensor w, int local_base, int buf_stride, int ldo, int[] peer_flags, "
+      "Tensor(a!) local_state, int rank) -> ()");
   m.def(
-      "ar_add_norm(int local_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
+      "symm_put_signal(Tensor x, int local_base, int buf_stride, int[] peer_flags, Tensor(a!) local_state, "
+      "int rank) -> ()");
+  m.def(
+      "ar_add_norm(int mc_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
       "Tensor(b!) residual, Tensor w, float eps, float timeout_s) -> Tensor");
   m.def(
       "greedy_allmax(Tensor keys, int[] peer_slots, int[] peer_flags, int flags_local, Tensor(a!) local_state, "
       "int rank, float timeout_s) -> Tensor");
 }
 void register_comm_impls(torch::Library& m) {
-  m.impl("gemm_mcred", &gemm_mcred_op);
-  m.impl("mc_red_signal", &mc_red_signal_op);
+  m.impl("gemm_symm", &gemm_symm_op);
+  m.impl("symm_put_signal", &symm_put_signal_op);
   m.impl("ar_add_norm", &ar_add_norm_op);
   m.impl("greedy_allmax", &greedy_allmax_op);
 }

@@ -12,6 +12,13 @@ void register_ext_pybind(pybind11::module& mod);
 void register_comm_defs(torch::Library& m);
 void register_comm_impls(torch::Library& m);
 
+// per (device, stream) split-K / split-KV scratch (defined in ops.cpp)
+struct Scratch {
+  at::Tensor ws;
+  at::Tensor tickets;
+};
+Scratch& scratch_for(const at::Tensor& like, long floats, long tickets);
+
 // shared validation helpers (defined in ops.cpp)
 void check_cuda(const at::Tensor& t, const char* name);
 void check_bf16(const at::Tensor& t, const char* name);
