@@ -14,7 +14,7 @@ _REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_pow
 
 
 class ClockSampler:
-    def __init__(self, gpu_index: int = 0, period_ms: int = 200):
+    def __init__(self, gpu_index: int = 0, period_ms: int = 50):
         self.idx = gpu_index
         self.period = period_ms
         self.proc = None
@@ -29,6 +29,13 @@ class ClockSampler:
              f"-i={self.idx}"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         self._t = threading.Thread(target=self._read, daemon=True)
         self._t.start()
+        # nvidia-smi takes a while to start: return once sampling is live, so a
+        # short timed region is still covered
+        import time
+        t0 = time.monotonic()
+        while not self.lines and time.monotonic() - t0 < 10 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.lines.clear()
         return self
 
     def _read(self):
