@@ -318,15 +318,30 @@ struct GCfg {
   static constexpr int kSmem = kStages * kStage + 1024 + 256;
 };
 
-__device__ __forceinline__ bool gunit(const GroupedArgs& a, int u, int& e, int& tm, int& tn, int& n0, int& nrows,
-                                      int BN) {
-  const int per_e = a.tiles_m * a.max_tiles_n;
-  e = u / per_e;
-  const int rem = u % per_e;
+constexpr int kGMaxGroups = 256;
+
+// Work units are compacted over the groups' actual row counts (cached in
+// shared memory at kernel start): unit u -> group e by binary search over the
+// per-group unit prefix, so empty groups and empty row tiles cost nothing.
+struct GUnits {
+  int pref[kGMaxGroups + 1];  // units before group e
+  int cnt[kGMaxGroups];
+  int off[kGMaxGroups];
+};
+
+__device__ __forceinline__ bool gunit(const GroupedArgs& a, const GUnits& g, int u, int& e, int& tm, int& tn, int& n0,
+                                      int& nrows, int BN) {
+  int lo = 0, hi = a.groups;  // largest e with pref[e] <= u
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (g.pref[mid] <= u) lo = mid; else hi = mid;
+  }
+  e = lo;
+  const int rem = u - g.pref[e];
   tm = rem % a.tiles_m;
   tn = rem / a.tiles_m;
-  const int cnt = a.counts[e];
-  n0 = a.offsets[e] + tn * BN;
+  const int cnt = g.cnt[e];
+  n0 = g.off[e] + tn * BN;
   nrows = min(BN, cnt - tn * BN);
   return nrows > 0;
 }
@@ -365,11 +380,23 @@ __global__ void __launch_bounds__(kGThreadsG, 1)
     tmem_alloc(tmem_slot, C::kTmem);
     tmem_relinquish();
   }
+  __shared__ GUnits gu;
+  for (int e = threadIdx.x; e < a.groups; e += blockDim.x) {
+    const int c = min(a.counts[e], a.max_tiles_n * BN);
+    gu.cnt[e] = c;
+    gu.off[e] = a.offsets[e];
+    gu.pref[e + 1] = a.tiles_m * ((c + BN - 1) / BN);
+  }
   tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    gu.pref[0] = 0;
+    for (int e = 0; e < a.groups; ++e) gu.pref[e + 1] += gu.pref[e];
+  }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int units = a.groups * a.tiles_m * a.max_tiles_n;
+  const int units = gu.pref[a.groups];
   const int num_kb = (a.K + kGBK - 1) / kGBK;
   if (warp == 0) {
     if (elect_one()) {
@@ -380,7 +407,7 @@ __global__ void __launch_bounds__(kGThreadsG, 1)
       uint32_t issued_mask = 0, issued_ph = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int e, tm, tn, n0, nr;
-        if (!gunit(a, u, e, tm, tn, n0, nr, BN)) continue;
+        if (!gunit(a, gu, u, e, tm, tn, n0, nr, BN)) continue;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1)) {
             set_status(a.status, kStatusMbarTimeout);
@@ -409,7 +436,7 @@ __global__ void __launch_bounds__(kGThreadsG, 1)
       uint32_t ph = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int e, tm, tn, n0, nr;
-        if (!gunit(a, u, e, tm, tn, n0, nr, BN)) continue;
+        if (!gunit(a, gu, u, e, tm, tn, n0, nr, BN)) continue;
         const int ab = i & 1;
         if (!mbar_wait(&tempty[ab], ((i >> 1) & 1) ^ 1)) {
           set_status(a.status, kStatusMbarTimeout);
@@ -444,7 +471,7 @@ __global__ void __launch_bounds__(kGThreadsG, 1)
     int i = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       int e, tm, tn, n0, nr;
-      if (!gunit(a, u, e, tm, tn, n0, nr, BN)) continue;
+      if (!gunit(a, gu, u, e, tm, tn, n0, nr, BN)) continue;
       const int ab = i & 1;
       if (!mbar_wait(&tfull[ab], (i >> 1) & 1)) {
         set_status(a.status, kStatusMbarTimeout);
@@ -508,6 +535,7 @@ static void launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const G
 
 void grouped_gemm(const GroupedProblem& p, cudaStream_t st) {
   BWN_CHECK(p.N % kGBM == 0, "grouped_gemm: N_out must be a multiple of 128");
+  BWN_CHECK(p.groups <= kGMaxGroups, "grouped_gemm: at most %d groups", kGMaxGroups);
   BWN_CHECK(p.K % 8 == 0, "grouped_gemm: K multiple of 8");
   if (p.swiglu) BWN_CHECK(p.N % 32 == 0, "grouped_gemm: swiglu rows multiple of 32");
   int bn = 16;

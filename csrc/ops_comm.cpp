@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 #include <torch/library.h>
 
+#include "comm/ep.h"
 #include "comm/fused.h"
 #include "common/host.h"
 #include "ops_ext.h"
@@ -141,7 +142,110 @@ Tensor greedy_allmax_op(const Tensor& keys, std::vector<int64_t> peer_slots, std
   return ids;
 }
 
+// ---- expert-parallel all-to-all -------------------------------------------
+// Symmetric buffer layout (byte offsets, identical on every rank):
+//   [flags 3*8 u32][table W*W*E_l i32][recv tags max_recv*4 i32][recv rows max_recv*H bf16][comb T_max*k*H bf16]
+static std::vector<int64_t> ep_layout(int64_t world, int64_t e_local, int64_t H, int64_t k, int64_t T_max,
+                                      int64_t max_recv) {
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  std::vector<int64_t> off(6);
+  off[0] = 0;
+  off[1] = up(3 * kEpMaxRanks * 4);
+  off[2] = off[1] + up(world * world * e_local * 4);
+  off[3] = off[2] + up(max_recv * 16);
+  off[4] = off[3] + up(max_recv * H * 2);
+  off[5] = off[4] + up(T_max * k * H * 2);  // total bytes
+  return off;
+}
+std::vector<int64_t> ep_layout_op(int64_t world, int64_t e_local, int64_t H, int64_t k, int64_t T_max,
+                                  int64_t max_recv) {
+  return ep_layout(world, e_local, H, k, T_max, max_recv);
+}
+
+// ep_state int32 layout: [0..15] epochs/tickets, then recv counts [E_l], recv offsets [E_l+1], send slots [W*E_l]
+static EpArgs make_ep(const std::vector<int64_t>& peer_base, int64_t rank, int64_t e_local, int64_t H, int64_t k,
+                      int64_t T_max, int64_t max_recv, const Tensor& state, double timeout_s) {
+  const int W = (int)peer_base.size();
+  TORCH_CHECK(W >= 1 && W <= kEpMaxRanks, "ep: 1..8 ranks");
+  TORCH_CHECK(state.scalar_type() == at::kInt && state.is_contiguous() &&
+                  state.numel() >= 16 + 2 * e_local + 1 + W * e_local,
+              "ep: state int32[16 + 2*E_l + 1 + W*E_l]");
+  const auto off = ep_layout(W, e_local, H, k, T_max, max_recv);
+  EpArgs a{};
+  a.world = W;
+  a.rank = (int)rank;
+  a.e_local = (int)e_local;
+  a.H = (int)H;
+  a.k = (int)k;
+  a.T_max = (int)T_max;
+  a.max_recv = (int)max_recv;
+  for (int r = 0; r < W; ++r) {
+    char* b = reinterpret_cast<char*>(peer_base[r]);
+    a.peer_flags[r] = reinterpret_cast<unsigned*>(b + off[0]);
+    a.peer_table[r] = reinterpret_cast<int*>(b + off[1]);
+    a.peer_recv_tag[r] = reinterpret_cast<int*>(b + off[2]);
+    a.peer_recv_x[r] = reinterpret_cast<__nv_bfloat16*>(b + off[3]);
+    a.peer_comb[r] = reinterpret_cast<__nv_bfloat16*>(b + off[4]);
+  }
+  a.flags = a.peer_flags[rank];
+  a.table = a.peer_table[rank];
+  a.recv_tag = a.peer_recv_tag[rank];
+  int* s = state.data_ptr<int>();
+  a.epoch_a = s + 0;
+  a.epoch_b = s + 1;
+  a.epoch_c = s + 2;
+  a.ticket_b = s + 3;
+  a.ticket_c = s + 4;
+  a.recv_counts = s + 16;
+  a.recv_offsets = s + 16 + e_local;
+  a.send_ctr = s + 16 + 2 * e_local + 1;
+  a.status = status_dev_ptr();
+  a.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  return a;
+}
+
+// Dispatch: counts all-gather, row sends, wait for every source's rows.
+void ep_dispatch_op(const Tensor& x, const Tensor& ids, std::vector<int64_t> peer_base, int64_t rank, int64_t e_local,
+                    int64_t T_max, int64_t max_recv, Tensor state, double timeout_s) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0, "x [T, H] with 16-byte rows");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
+              "ids int32 [T, k]");
+  TORCH_CHECK(x.size(0) <= T_max, "ep_dispatch: more tokens than T_max");
+  const c10::cuda::CUDAGuard guard(x.device());
+  EpArgs a = make_ep(peer_base, rank, e_local, x.size(1), ids.size(1), T_max, max_recv, state, timeout_s);
+  a.T = (int)x.size(0);
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.ids = ids.data_ptr<int>();
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  ep_count(a, st);
+  ep_send(a, st);
+  ep_wait(a, 0, st);
+}
+
+// Return: every received row's expert output back to its source; wait for ours.
+void ep_return_op(const Tensor& y, std::vector<int64_t> peer_base, int64_t rank, int64_t e_local, int64_t k,
+                  int64_t T, int64_t T_max, int64_t max_recv, Tensor state, double timeout_s) {
+  check_bf16(y, "y");
+  TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(0) >= max_recv && y.stride(0) % 8 == 0, "y [max_recv, H]");
+  const c10::cuda::CUDAGuard guard(y.device());
+  EpArgs a = make_ep(peer_base, rank, e_local, y.size(1), k, T_max, max_recv, state, timeout_s);
+  a.T = (int)T;
+  a.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr());
+  a.ldy = y.stride(0);
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  ep_return(a, st);
+  ep_wait(a, 1, st);
+}
+
 void register_comm_defs(torch::Library& m) {
+  m.def(
+      "ep_dispatch(Tensor x, Tensor ids, int[] peer_base, int rank, int e_local, int T_max, int max_recv, "
+      "Tensor(a!) state, float timeout_s) -> ()");
+  m.def(
+      "ep_return(Tensor y, int[] peer_base, int rank, int e_local, int k, int T, int T_max, int max_recv, "
+      "Tensor(a!) state, float timeout_s) -> ()");
   m.def(
       "gemm_symm(Tensor x, Tensor w, int local_base, int buf_stride, int ldo, int[] peer_flags, "
       "Tensor(a!) local_state, int rank) -> ()");
@@ -155,7 +259,13 @@ void register_comm_defs(torch::Library& m) {
       "greedy_allmax(Tensor keys, int[] peer_slots, int[] peer_flags, int flags_local, Tensor(a!) local_state, "
       "int rank, float timeout_s) -> Tensor");
 }
+void register_comm_pybind(pybind11::module& mod) {
+  mod.def("ep_layout", &ep_layout_op, "EP all-to-all symmetric buffer offsets: flags, table, tags, rows, comb, total");
+}
+
 void register_comm_impls(torch::Library& m) {
+  m.impl("ep_dispatch", &ep_dispatch_op);
+  m.impl("ep_return", &ep_return_op);
   m.impl("gemm_symm", &gemm_symm_op);
   m.impl("symm_put_signal", &symm_put_signal_op);
   m.impl("ar_add_norm", &ar_add_norm_op);

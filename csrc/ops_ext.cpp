@@ -391,7 +391,86 @@ Tensor deltanet_verify_op(const Tensor& qkv, const Tensor& z, const Tensor& a, c
   return out;
 }
 
+// Routed-expert FFN on rows already grouped by expert (device counts/offsets):
+// gate/up GEMM with the SwiGLU epilogue, then the down GEMM.  Used on the
+// expert-parallel receive buffer.
+Tensor moe_grouped_ffn_op(const Tensor& x_perm, const Tensor& counts, const Tensor& offsets, const Tensor& gate_up,
+                          const Tensor& down, int64_t max_rows_per_group, double swiglu_limit) {
+  check_bf16(x_perm, "x_perm");
+  check_bf16(gate_up, "gate_up");
+  check_bf16(down, "down");
+  TORCH_CHECK(x_perm.dim() == 2 && x_perm.is_contiguous(), "x_perm [rows, H] contiguous");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && offsets.scalar_type() == at::kInt, "counts/offsets int32");
+  const c10::cuda::CUDAGuard guard(x_perm.device());
+  const int rows = (int)x_perm.size(0), H = (int)x_perm.size(1);
+  const int El = (int)gate_up.size(0), I2 = (int)gate_up.size(1), I = I2 / 2;
+  TORCH_CHECK(down.size(0) == El && down.size(1) == H && down.size(2) == I, "down [E, H, I]");
+  auto y1 = at::empty({std::max(rows, 1), I}, x_perm.options());
+  auto y2 = at::empty({std::max(rows, 1), H}, x_perm.options());
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  GroupedProblem g{};
+  g.W = gate_up.data_ptr();
+  g.X = x_perm.data_ptr();
+  g.rows_total = rows;
+  g.counts = counts.data_ptr<int>();
+  g.offsets = offsets.data_ptr<int>();
+  g.groups = El;
+  g.N = I2;
+  g.K = H;
+  g.max_rows_per_group = (int)max_rows_per_group;
+  g.swiglu = true;
+  g.swiglu_limit = (float)swiglu_limit;
+  g.out = mbf(y1);
+  g.ldo = I;
+  g.status = status_dev_ptr();
+  grouped_gemm(g, st);
+  g.W = down.data_ptr();
+  g.X = y1.data_ptr();
+  g.N = H;
+  g.K = I;
+  g.swiglu = false;
+  g.swiglu_limit = 0.f;
+  g.out = mbf(y2);
+  g.ldo = H;
+  grouped_gemm(g, st);
+  return y2;
+}
+
+// Router-weighted sum of per-(token, slot) expert outputs y[pos_of[t*k+j]]
+// (+ the sigmoid-gated shared expert).
+Tensor moe_combine_op(const Tensor& y, const Tensor& w, const Tensor& pos_of, const c10::optional<Tensor>& shared_y,
+                      const c10::optional<Tensor>& shared_gate) {
+  check_bf16(y, "y");
+  TORCH_CHECK(y.dim() == 2 && y.is_contiguous(), "y [rows, H] contiguous");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.dim() == 2, "w fp32 [T, k]");
+  TORCH_CHECK(pos_of.scalar_type() == at::kInt && pos_of.numel() == w.numel(), "pos_of int32 [T*k]");
+  const c10::cuda::CUDAGuard guard(y.device());
+  const int T = (int)w.size(0), k = (int)w.size(1), H = (int)y.size(1);
+  auto out = at::empty({T, H}, y.options());
+  MoeCombineArgs c{};
+  c.y = cbf(y);
+  c.w = w.data_ptr<float>();
+  c.pos_of = pos_of.data_ptr<int>();
+  c.T = T;
+  c.k = k;
+  c.H = H;
+  if (shared_y.has_value()) {
+    check_bf16(*shared_y, "shared_y");
+    c.shared_y = cbf(*shared_y);
+    c.ld_shared = shared_y->stride(0);
+    c.shared_gate = shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr;
+  }
+  c.out = mbf(out);
+  c.ldo = out.stride(0);
+  if (T > 0) moe_combine(c, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
 void register_ext_defs(torch::Library& m) {
+  m.def("moe_combine(Tensor y, Tensor w, Tensor pos_of, Tensor? shared_y, Tensor? shared_gate) -> Tensor");
+  m.def(
+      "moe_grouped_ffn(Tensor x_perm, Tensor counts, Tensor offsets, Tensor gate_up, Tensor down, "
+      "int max_rows_per_group, float swiglu_limit) -> Tensor");
   m.def(
       "deltanet_verify(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) stash_qkv, Tensor(b!) stash_ab, "
       "Tensor vstep, Tensor(c!) conv_ring, Tensor(d!) state, Tensor positions, Tensor pending, Tensor conv_w, "
@@ -419,6 +498,8 @@ void register_ext_impls(torch::Library& m) {
   m.impl("deltanet_verify", &deltanet_verify_op);
   m.impl("moe_topk", &moe_topk_op);
   m.impl("moe_experts", &moe_experts_op);
+  m.impl("moe_grouped_ffn", &moe_grouped_ffn_op);
+  m.impl("moe_combine", &moe_combine_op);
   m.impl("hc_pre", &hc_pre_op);
   m.impl("hc_post", &hc_post_op);
   m.impl("mqa_attn", &mqa_attn_op);
@@ -426,5 +507,5 @@ void register_ext_impls(torch::Library& m) {
   m.impl("deltanet_prefill", &deltanet_prefill_op);
   m.impl("gqa_prefill", &gqa_prefill_op);
 }
-void register_ext_pybind(pybind11::module& mod) {}
+void register_ext_pybind(pybind11::module& mod) { register_comm_pybind(mod); }
 }  // namespace bwn

@@ -11,6 +11,7 @@ void register_ext_impls(torch::Library& m);
 void register_ext_pybind(pybind11::module& mod);
 void register_comm_defs(torch::Library& m);
 void register_comm_impls(torch::Library& m);
+void register_comm_pybind(pybind11::module& mod);
 
 // per (device, stream) split-K / split-KV scratch (defined in ops.cpp)
 struct Scratch {

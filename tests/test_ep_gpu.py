@@ -1,0 +1,102 @@
+"""Expert-parallel all-to-all over NVLink peer memory (2 GPUs, one process
+each): the dispatch -> grouped expert GEMMs -> return -> combine block equals
+the MoE with every expert local, eagerly, repeatedly (buffer reuse) and
+replayed from a CUDA graph."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+
+        from bwn import ops as O
+        from bwn.ops import check_status
+        from bwn.parallel.comm import init_distributed
+        from bwn.parallel.ep import EPAllToAll, nccl_ep_moe
+
+        comm = init_distributed("nccl", timeout_s=60)
+        dev = torch.device("cuda", rank)
+        E, H, I, k, T = 16, 256, 64, 4, 24
+        El = E // world
+        g = torch.Generator().manual_seed(0)
+        gu = torch.stack([O.interleave_gate_up(torch.randn(I, H, generator=g) * 0.05,
+                                               torch.randn(I, H, generator=g) * 0.05) for _ in range(E)])
+        dn = torch.randn(E, H, I, generator=g) * 0.05
+        gu, dn = gu.bfloat16().to(dev), dn.bfloat16().to(dev)
+        loc_gu, loc_dn = gu[rank * El:(rank + 1) * El].contiguous(), dn[rank * El:(rank + 1) * El].contiguous()
+        ep = EPAllToAll(comm, H, E, k, max_tokens=T, device=dev)
+        errs = []
+        for it in range(3):
+            gt = torch.Generator().manual_seed(100 * it + rank)
+            x = torch.randn(T, H, generator=gt).bfloat16().to(dev)
+            ids = torch.stack([torch.randperm(E, generator=gt)[:k] for _ in range(T)]).int().to(dev)
+            w = torch.rand(T, k, generator=gt).to(dev)
+            sy = torch.randn(T, H, generator=gt).bfloat16().to(dev)
+            sg = torch.randn(T, 1, generator=gt).to(dev)
+            out = ep.moe(x, w, ids, loc_gu, loc_dn, shared=(sy, sg))
+            ref = O.moe_experts(x, w, ids, gu, dn, 0, shared=(sy, sg))
+            base = nccl_ep_moe(comm, x, w, ids, loc_gu, loc_dn, El, shared=(sy, sg))
+            torch.cuda.synchronize()
+            check_status("ep")
+            errs.append(float((out.float() - ref.float()).abs().max() / ref.float().abs().max()))
+            errs.append(float((base.float() - ref.float()).abs().max() / ref.float().abs().max()))
+        # CUDA graph replay of the whole block
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(7 + rank)).bfloat16().to(dev)
+        ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(9 + rank + 2 * i))[:k]
+                           for i in range(T)]).int().to(dev)
+        w = torch.rand(T, k, generator=torch.Generator().manual_seed(3)).to(dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            ep.moe(x, w, ids, loc_gu, loc_dn)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                out_g = ep.moe(x, w, ids, loc_gu, loc_dn)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        check_status("ep graph")
+        ref = O.moe_experts(x, w, ids, gu, dn, 0)
+        errs.append(float((out_g.float() - ref.float()).abs().max() / ref.float().abs().max()))
+        del graph
+        q.put((rank, errs))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001
+        import traceback
+        q.put((rank, "ERR " + traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_all_to_all_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        assert max(res[r]) < 2e-2, res[r]
