@@ -207,6 +207,26 @@ class Qwen36Model(nn.Module):
             return qwen_moe_forward(self, L, h)
         return O.linear_swiglu(h, L["gate_up"])
 
+    def moe_residual(self, i: int, h: torch.Tensor, x: torch.Tensor, nxt: torch.Tensor) -> torch.Tensor:
+        """MoE sub-block with residual add + next RMSNorm.  With the expert-parallel
+        all-to-all enabled (:func:`bwn.parallel.ep.enable_ep_all_to_all`) and enough
+        tokens per rank, each rank routes its slice of the tokens through the
+        NVLink all-to-all and the slices are all-gathered; otherwise each rank runs
+        its experts over all tokens and the partials are all-reduced."""
+        ep = getattr(self, "ep_a2a", None)
+        T = h.shape[0]
+        if ep is not None and T % self.tp == 0 and ep.min_tokens <= T // self.tp <= ep.T_max:
+            from .moe import route
+            L = self.layers[i]
+            Ts = T // self.tp
+            hs = h[self.rank * Ts:(self.rank + 1) * Ts]
+            w, ids = route(self, L, hs)
+            sy = O.linear(O.linear_swiglu(hs, L["shared_gate_up_full"]), L["shared_down_full"])
+            sg = O.linear_f32(hs, L["shared_gate"])
+            ys = ep.moe(hs, w, ids, L["experts_gate_up"], L["experts_down"], shared=(sy, sg))
+            return O.add_rms_norm(self.comm.all_gather_first(ys), x, nxt, self.cfg.rms_eps)
+        return self._reduce_add_norm(self._mlp(i, h), x, nxt)
+
     def decode_hidden(self, tokens: torch.Tensor, st: Qwen36State) -> torch.Tensor:
         """One decode step for ``tokens [B]`` at ``st.positions``; advances the
         positions and returns the final-normed hidden ``[B, H]``."""
@@ -226,8 +246,7 @@ class Qwen36Model(nn.Module):
                 gi += 1
             nxt = self.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else self.g["final_norm"]
             if cfg.is_moe:
-                part = self._mlp(i, h)
-                h = self._reduce_add_norm(part, x, nxt)
+                h = self.moe_residual(i, h, x, nxt)
             else:
                 act = self._mlp(i, h)
                 h = self._row_parallel(act, L["down"], x, nxt)
@@ -288,7 +307,7 @@ class Qwen36Model(nn.Module):
                 gi += 1
             nxt = self.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else self.g["final_norm"]
             if cfg.is_moe:
-                h = self._reduce_add_norm(self._mlp(i, h), x, nxt)
+                h = self.moe_residual(i, h, x, nxt)
             else:
                 h = self._row_parallel(self._mlp(i, h), L["down"], x, nxt)
             if i in feat_layers:

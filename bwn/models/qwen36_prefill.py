@@ -59,8 +59,7 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
             gi += 1
         nxt = model.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else model.g["final_norm"]
         if cfg.is_moe:
-            part = model._mlp(i, h)
-            h = model._reduce_add_norm(part, x, nxt)
+            h = model.moe_residual(i, h, x, nxt)
         else:
             act = model._mlp(i, h)
             h = model._row_parallel(act, L["down"], x, nxt)

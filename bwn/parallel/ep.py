@@ -91,6 +91,25 @@ class EPAllToAll:
                                    sy, sg)
 
 
+def enable_ep_all_to_all(model, max_tokens_per_rank: int = 512, min_tokens_per_rank: int = 16) -> EPAllToAll:
+    """Route a Qwen3.6 MoE model's expert layers through the NVLink all-to-all
+    when a step has at least ``min_tokens_per_rank`` tokens per rank (prefill,
+    large batches); smaller steps keep the all-reduce formulation, which needs
+    fewer cross-GPU round trips.  The shared expert is made replicated (its
+    tensor-parallel slices are all-gathered once) since each rank then runs it
+    on its own token slice."""
+    cfg, comm = model.cfg, model.comm
+    if not cfg.is_moe or comm.size <= 1:
+        raise RuntimeError("expert-parallel all-to-all needs a MoE model on more than one rank")
+    ep = EPAllToAll(comm, cfg.hidden, cfg.num_experts, cfg.top_k, max_tokens_per_rank, device=model.device)
+    ep.min_tokens = min_tokens_per_rank
+    for L in model.layers:
+        L["shared_gate_up_full"] = comm.all_gather_first(L["shared_gate_up"].contiguous())
+        L["shared_down_full"] = comm.all_gather_last(L["shared_down"].contiguous()).contiguous()
+    model.ep_a2a = ep
+    return ep
+
+
 def nccl_ep_moe(comm, x, w, ids, gate_up, down, e_local: int, shared=None, swiglu_limit: float = 0.0):
     """Baseline: the same expert-parallel block with NCCL (or gloo) all-to-all
     and host-side split sizes (one device sync per call)."""

@@ -99,12 +99,13 @@ class MLMTrainer:
     def step(self, batch=None) -> torch.Tensor:
         dev = next(self.model.parameters()).device
         ids, am, labels, lm = [t.to(dev, non_blocking=True) for t in (batch or self.next_batch())]
-        self.opt.zero_grad(set_to_none=True)
+        # a bucketed reducer owns the gradient storage: zero it in place
+        self.opt.zero_grad(set_to_none=self.grad_reducer is None)
         loss = self.loss(ids, am, labels, lm)
         loss.backward()
         if self.comm is not None and self.comm.size > 1:
             if self.grad_reducer is not None:
-                self.grad_reducer.reduce(self.model)
+                self.grad_reducer.finish()
             else:
                 for p in self.model.parameters():
                     if p.grad is not None:

@@ -8,6 +8,7 @@
 
 #include "comm/ep.h"
 #include "comm/fused.h"
+#include "comm/grad_reduce.h"
 #include "common/host.h"
 #include "ops_ext.h"
 
@@ -239,7 +240,52 @@ void ep_return_op(const Tensor& y, std::vector<int64_t> peer_base, int64_t rank,
   ep_wait(a, 1, st);
 }
 
+// ---- fused data-parallel gradient reduction --------------------------------
+static GradBucketArgs make_grad(const Tensor& grad, int64_t local, int64_t mc, int64_t flags_local,
+                                const std::vector<int64_t>& peer_flags, int64_t rank, int64_t epoch,
+                                const Tensor& ticket, double timeout_s) {
+  TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == at::kFloat && grad.is_contiguous(), "grad: fp32 contiguous");
+  TORCH_CHECK(ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "ticket int32");
+  TORCH_CHECK(peer_flags.size() >= 1 && peer_flags.size() <= 8, "1..8 ranks");
+  GradBucketArgs a{};
+  a.world = (int)peer_flags.size();
+  a.rank = (int)rank;
+  a.n = grad.numel();
+  a.grad = grad.data_ptr<float>();
+  a.local = reinterpret_cast<__nv_bfloat16*>(local);
+  a.mc = reinterpret_cast<__nv_bfloat16*>(mc);
+  a.flags = reinterpret_cast<const unsigned*>(flags_local);
+  for (size_t i = 0; i < peer_flags.size(); ++i) a.peer_flags[i] = reinterpret_cast<unsigned*>(peer_flags[i]);
+  a.epoch = (unsigned)epoch;
+  a.ticket = ticket.data_ptr<int>();
+  a.scale = 1.f / (float)a.world;
+  a.status = status_dev_ptr();
+  a.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  return a;
+}
+
+void grad_bucket_reduce_op(const Tensor& grad, int64_t local, int64_t mc, int64_t flags_local,
+                           std::vector<int64_t> peer_flags, int64_t rank, int64_t epoch, Tensor ticket,
+                           double timeout_s) {
+  const c10::cuda::CUDAGuard guard(grad.device());
+  grad_bucket_reduce(make_grad(grad, local, mc, flags_local, peer_flags, rank, epoch, ticket, timeout_s),
+                     at::cuda::getCurrentCUDAStream().stream());
+}
+
+void grad_bucket_unpack_op(Tensor grad, int64_t local, int64_t mc, int64_t flags_local, std::vector<int64_t> peer_flags,
+                           int64_t rank, int64_t epoch, Tensor ticket, double timeout_s) {
+  const c10::cuda::CUDAGuard guard(grad.device());
+  grad_bucket_unpack(make_grad(grad, local, mc, flags_local, peer_flags, rank, epoch, ticket, timeout_s),
+                     at::cuda::getCurrentCUDAStream().stream());
+}
+
 void register_comm_defs(torch::Library& m) {
+  m.def(
+      "grad_bucket_reduce(Tensor grad, int local, int mc, int flags_local, int[] peer_flags, int rank, int epoch, "
+      "Tensor(a!) ticket, float timeout_s) -> ()");
+  m.def(
+      "grad_bucket_unpack(Tensor(a!) grad, int local, int mc, int flags_local, int[] peer_flags, int rank, "
+      "int epoch, Tensor(b!) ticket, float timeout_s) -> ()");
   m.def(
       "ep_dispatch(Tensor x, Tensor ids, int[] peer_base, int rank, int e_local, int T_max, int max_recv, "
       "Tensor(a!) state, float timeout_s) -> ()");
@@ -264,6 +310,8 @@ void register_comm_pybind(pybind11::module& mod) {
 }
 
 void register_comm_impls(torch::Library& m) {
+  m.impl("grad_bucket_reduce", &grad_bucket_reduce_op);
+  m.impl("grad_bucket_unpack", &grad_bucket_unpack_op);
   m.impl("ep_dispatch", &ep_dispatch_op);
   m.impl("ep_return", &ep_return_op);
   m.impl("gemm_symm", &gemm_symm_op);

@@ -100,3 +100,58 @@ def test_ep_all_to_all_two_gpus():
     for r in range(2):
         assert not isinstance(res[r], str), res[r]
         assert max(res[r]) < 2e-2, res[r]
+
+
+def _model_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+
+        from bwn.config import tiny_qwen36
+        from bwn.io import qwen36_weights as Wt
+        from bwn.models.qwen36 import build_qwen36
+        from bwn.ops import check_status
+        from bwn.parallel.comm import init_distributed
+        from bwn.parallel.ep import enable_ep_all_to_all
+
+        comm = init_distributed("nccl", timeout_s=60)
+        dev = torch.device("cuda", rank)
+        cfg = tiny_qwen36(moe=True).scaled(q_heads=8, kv_heads=2, dn_k_heads=2, dn_v_heads=4)
+        hf = dict(Wt.synthetic_hf_globals(cfg, 3, "cpu"))
+        for i in range(cfg.num_layers):
+            hf.update(Wt.synthetic_hf_layer(cfg, i, 3, "cpu"))
+        ref = build_qwen36(cfg, device=dev, hf_state=hf)
+        ep_model = build_qwen36(cfg, comm=comm, device=dev, hf_state=hf)
+        enable_ep_all_to_all(ep_model, max_tokens_per_rank=64, min_tokens_per_rank=8)
+        B, S = 4, 24
+        toks = torch.randint(0, cfg.vocab, (B, S), generator=torch.Generator().manual_seed(0)).to(dev)
+        hs = []
+        for m in (ref, ep_model):
+            st = m.new_state(B, 64)
+            hs.append(m.prefill_hidden(toks, st).float())
+        torch.cuda.synchronize()
+        check_status("ep model")
+        rel = float((hs[0] - hs[1]).norm() / hs[0].norm())
+        q.put((rank, rel))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001
+        import traceback
+        q.put((rank, "ERR " + traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_qwen36_moe_prefill_with_ep_all_to_all():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_model_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        assert res[r] < 3e-2, res
