@@ -75,3 +75,14 @@ def test_training_reduces_loss():
     for _ in range(40):
         last = float(tr.step())
     assert last < first - 0.3, (first, last)
+
+
+def test_tokenize_and_predict_masked_middle():
+    from bwn.train.esm_infer import predict_masked_middle, tokenize
+    from bwn.train.esm_mlm import build_esm
+    m = build_esm("8M", seed=0)
+    ids, am = tokenize(["AC<mask>D", "LL"], m.cfg, 8)
+    assert ids.shape == (2, 8) and int(am[0].sum()) == 6 and int(am[1].sum()) == 4
+    assert int(ids[0, 3]) == m.cfg.mask_token_id and int(ids[0, 0]) == m.cfg.cls_token_id
+    res = predict_masked_middle(m, ["MKTVRQERLK", "KALTAR"])
+    assert [r["position"] for r in res] == [5, 3] and all(0 < r["prob"] <= 1 for r in res)
