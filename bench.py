@@ -78,6 +78,8 @@ def main() -> None:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--fp8", action="store_true", help="W8A16: 128x128 block-scaled E4M3 projection weights")
     ap.add_argument("--fused-comm", default="auto", choices=["auto", "on", "off"])
+    ap.add_argument("--ep-a2a", default="auto", choices=["auto", "on", "off"],
+                    help="MoE models on N>1: expert-parallel NVLink all-to-all for steps with >=16 tokens per rank")
     ap.add_argument("--profile-steps", type=int, default=int(os.environ.get("BWN_PROFILE_STEPS", "0")),
                     help="run warm-up + N decode steps only (for a profiler), then exit")
     ap.add_argument("--metrics", default=os.environ.get("BWN_METRICS", ""), help="JSONL metrics file")
@@ -121,6 +123,15 @@ def main() -> None:
                 raise
             if comm.rank == 0:
                 print(f"[bench] fused NVLink comm unavailable, using NCCL: {e}", file=sys.stderr)
+    if cfg.is_moe and comm.size > 1 and args.ep_a2a != "off":
+        try:
+            from bwn.parallel.ep import enable_ep_all_to_all
+            enable_ep_all_to_all(model, max_tokens_per_rank=max(16, B * S // comm.size), min_tokens_per_rank=16)
+        except Exception as e:  # noqa: BLE001
+            if args.ep_a2a == "on":
+                raise
+            if comm.rank == 0:
+                print(f"[bench] EP all-to-all unavailable: {e}", file=sys.stderr)
     dec = StaticDecoder(model, B, max_seq, use_graph=not args.no_graph)
     if args.profile_steps:
         # warm-up + N decode steps and nothing else, for a profiler's timeline
@@ -224,6 +235,7 @@ def main() -> None:
                 "l2": "inputs larger than L2 (every step streams %.1f GB of weights per GPU)" % (
                     model.weight_bytes() / 1e9),
                 "fused_comm": model.fused_comm is not None,
+                "ep_all_to_all": getattr(model, "ep_a2a", None) is not None,
             },
             "tpot_p50_ms": round(p50, 4),
             "context": context,

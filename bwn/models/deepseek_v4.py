@@ -210,6 +210,47 @@ class DeepSeekV4Model:
         ck.close()
         return self
 
+    def init_random_local(self, seed: int = 0) -> "DeepSeekV4Model":
+        """Random-init only this rank's shards, directly on the device (full-size
+        models: the whole synthetic state dict would not fit in host memory).
+        The weights differ between tensor-parallel degrees; for benchmarks."""
+        cfg, dt, dev = self.cfg, self.dtype, self.device
+        hd, olr, I = cfg.head_dim, cfg.o_lora_rank, cfg.moe_inter
+        Is = I // self.tp
+        mix = (2 + cfg.hc_mult) * cfg.hc_mult
+        g = torch.Generator(device=dev).manual_seed(seed * 1000 + self.rank)
+
+        def rn(*shape, std=0.02, dtype=dt):
+            return (torch.randn(*shape, device=dev, generator=g, dtype=torch.float32) * std).to(dtype)
+
+        def ones(n):
+            return torch.ones(n, device=dev)
+
+        self.L = []
+        for i in range(cfg.num_layers):
+            L = {
+                "attn_norm": ones(cfg.dim), "ffn_norm": ones(cfg.dim),
+                "hc_attn": (rn(mix, cfg.hc_mult * cfg.dim, dtype=torch.float32), ones(3),
+                            rn(mix, std=0.1, dtype=torch.float32)),
+                "hc_ffn": (rn(mix, cfg.hc_mult * cfg.dim, dtype=torch.float32), ones(3),
+                           rn(mix, std=0.1, dtype=torch.float32)),
+                "wq_a": rn(cfg.q_lora_rank, cfg.dim), "q_norm": ones(cfg.q_lora_rank),
+                "wq_b": rn(self.heads * hd, cfg.q_lora_rank), "wkv": rn(hd, cfg.dim), "kv_norm": ones(hd),
+                "wo_a": rn(self.groups, olr, cfg.n_heads * hd // cfg.o_groups),
+                "wo_b": rn(cfg.dim, self.groups * olr),
+                "gate": rn(cfg.n_routed_experts, cfg.dim),
+                "gate_bias": rn(cfg.n_routed_experts, std=0.01, dtype=torch.float32)
+                if i >= cfg.n_hash_layers else None,
+                "experts_gate_up": rn(self.e_local, 2 * I, cfg.dim),
+                "experts_down": rn(self.e_local, cfg.dim, I),
+                "shared_gate_up": rn(2 * Is, cfg.dim), "shared_down": rn(cfg.dim, Is),
+            }
+            self.L.append(L)
+        self.g = {"embed": rn(cfg.vocab, cfg.dim, std=1.0), "head": rn(cfg.vocab, cfg.dim), "norm": ones(cfg.dim),
+                  "hc_head": (rn(cfg.hc_mult, cfg.hc_mult * cfg.dim, dtype=torch.float32), ones(1),
+                              torch.zeros(cfg.hc_mult, device=dev))}
+        return self
+
     def init_random(self, seed: int = 0) -> "DeepSeekV4Model":
         return self.load(synthetic_checkpoint(self.cfg, seed, "cpu"))
 
