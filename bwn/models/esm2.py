@@ -48,6 +48,11 @@ class _BwnLinearFn(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             gx = O.linear_kn(gyb, wb)
         if ctx.needs_input_grad[1]:
+            rows = gyb.shape[0]
+            if rows % 8:  # dW contracts over tokens: zero rows keep the TMA 16-byte rule and the sum
+                pad = 8 - rows % 8
+                gyb = torch.nn.functional.pad(gyb, (0, 0, 0, pad))
+                xb = torch.nn.functional.pad(xb, (0, 0, 0, pad))
             gw = O.matmul_tn(gyb, xb, f32_out=True).to(ctx.w_dtype)
         if ctx.has_b and ctx.needs_input_grad[2]:
             gb = gy.float().sum(0).to(ctx.w_dtype)
