@@ -78,6 +78,8 @@ def main() -> None:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--fp8", action="store_true", help="W8A16: 128x128 block-scaled E4M3 projection weights")
     ap.add_argument("--fused-comm", default="auto", choices=["auto", "on", "off"])
+    ap.add_argument("--sp", default="auto", choices=["auto", "on", "off"],
+                    help="N>1: sequence-parallel prefill (reduce-scatter/all-gather fused into the GEMM path)")
     ap.add_argument("--ep-a2a", default="auto", choices=["auto", "on", "off"],
                     help="MoE models on N>1: expert-parallel NVLink all-to-all for steps with >=16 tokens per rank")
     ap.add_argument("--profile-steps", type=int, default=int(os.environ.get("BWN_PROFILE_STEPS", "0")),
@@ -132,6 +134,15 @@ def main() -> None:
                 raise
             if comm.rank == 0:
                 print(f"[bench] EP all-to-all unavailable: {e}", file=sys.stderr)
+    if comm.size > 1 and args.sp != "off" and (B * S) % (128 * comm.size) == 0:
+        try:
+            from bwn.parallel.sp import enable_sequence_parallel
+            enable_sequence_parallel(model, B * S)
+        except Exception as e:  # noqa: BLE001
+            if args.sp == "on":
+                raise
+            if comm.rank == 0:
+                print(f"[bench] sequence-parallel prefill unavailable: {e}", file=sys.stderr)
     dec = StaticDecoder(model, B, max_seq, use_graph=not args.no_graph)
     if args.profile_steps:
         # warm-up + N decode steps and nothing else, for a profiler's timeline
@@ -236,6 +247,7 @@ def main() -> None:
                     model.weight_bytes() / 1e9),
                 "fused_comm": model.fused_comm is not None,
                 "ep_all_to_all": getattr(model, "ep_a2a", None) is not None,
+                "prefill_sequence_parallel": getattr(model, "seq_parallel", None) is not None,
             },
             "tpot_p50_ms": round(p50, 4),
             "context": context,

@@ -371,6 +371,11 @@ class Qwen36Model(nn.Module):
         """Bucketed prefill (``prefill_bucketed``): chunks of ``bucket`` tokens
         (whole prompt if 0); returns the greedy next token ids ``[B]``."""
         B, S = tokens.shape
+        sp = getattr(self, "seq_parallel", None)
+        if sp is not None and valid_len is None and (bucket == 0 or bucket >= S) and \
+                (B * S) % (128 * self.tp) == 0 and B * S <= sp.T_max:
+            from .qwen36_prefill import prefill_hidden_sp
+            return self.greedy(prefill_hidden_sp(self, tokens, st, sp))
         bucket = bucket or S
         vl = valid_len if valid_len is not None else torch.full((B,), S, dtype=torch.int32, device=tokens.device)
         h = None

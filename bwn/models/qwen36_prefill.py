@@ -72,3 +72,79 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
         return h
     last = (valid_len.long() - 1).clamp(min=0) + torch.arange(B, device=dev) * S
     return h[last]
+
+
+def prefill_hidden_sp(model, tokens: torch.Tensor, st, sp, chunk: int = 64) -> torch.Tensor:
+    """Sequence-parallel prefill of full-length rows (``tokens [B, S]``, no
+    padding, ``B*S`` a multiple of ``128 * world``) through :class:`bwn.parallel.sp.SeqParallel`:
+    the residual stream is sharded by rows, every row-parallel output is
+    reduce-scattered + normed + all-gathered in one kernel, and each
+    column-parallel GEMM reads the gathered rows as they arrive.  MoE layers use
+    the expert-parallel all-to-all on the row shard.  Returns the final-normed
+    hidden of each sequence's last token ``[B, H]``."""
+    cfg, d = model.cfg, model.d
+    B, S = tokens.shape
+    T = B * S
+    W, r = model.tp, model.rank
+    if T % (128 * W) or T > sp.T_max:
+        raise ValueError(f"sequence-parallel prefill needs B*S a multiple of {128 * W} and <= {sp.T_max}")
+    Ts = T // W
+    dev = tokens.device
+    start = int(st.positions[0].item())
+    model.ensure_rope(start + S)
+    valid_len = torch.full((B,), S, dtype=torch.int32, device=dev)
+    x_full = O.embedding(tokens.reshape(T).int(), model.g["embed"], 0)
+    x = x_full[r * Ts:(r + 1) * Ts].contiguous()  # residual shard
+    h = O.rms_norm(x_full, model.layers[0]["in_norm"], cfg.rms_eps)
+    del x_full
+    eps = cfg.rms_eps
+    di = gi = 0
+
+    def col(w, first, swiglu=False):
+        if first:
+            return O.linear_swiglu(h, w) if swiglu else O.linear(h, w)
+        return sp.column(w, T, swiglu)
+
+    for i in range(cfg.num_layers):
+        L = model.layers[i]
+        first = i == 0
+        if cfg.layer_type(i) == "deltanet":
+            C, Z, VH = d.dn_qkv_dim, d.dn_value_dim, d.dn_v_heads
+            proj = col(L["in_proj"], first).view(B, S, -1)
+            o = O.deltanet_prefill(proj[..., :C], proj[..., C:C + Z], proj[..., C + Z + VH:],
+                                   proj[..., C + Z:C + Z + VH], st.conv[di], st.ssm[di], start, valid_len,
+                                   L["conv_w"], L["A_log"], L["dt_bias"], L["norm_w"], d.dn_k_heads, eps, chunk)
+            sp.row_parallel(o.reshape(T, -1), L["out_proj"])
+            di += 1
+        else:
+            D, QH, KVH = cfg.head_dim, d.q_heads, d.kv_heads
+            proj = col(L["qkv_proj"], first).view(B, S, -1)
+            qg = proj[..., :QH * 2 * D].reshape(B, S, QH, 2 * D)
+            k = proj[..., QH * 2 * D:QH * 2 * D + KVH * D].reshape(B, S, KVH, D)
+            v = proj[..., QH * 2 * D + KVH * D:].reshape(B, S, KVH, D)
+            o = O.gqa_prefill(qg, k, v, L["q_norm"], L["k_norm"], model.rope_cos, model.rope_sin,
+                              st.k_cache[gi], st.v_cache[gi], start, eps)
+            sp.row_parallel(o.reshape(T, -1), L["o_proj"])
+            gi += 1
+        sp.norm_gather(x, L["post_norm"], eps)
+        nxt = model.layers[i + 1]["in_norm"] if i + 1 < cfg.num_layers else model.g["final_norm"]
+        if cfg.is_moe:
+            ep = getattr(model, "ep_a2a", None)
+            if ep is None or Ts > ep.T_max:
+                raise RuntimeError("sequence-parallel MoE layers need the expert-parallel all-to-all sized for the shard")
+            from .moe import route
+            hs = sp.gathered(T)[r * Ts:(r + 1) * Ts]
+            w, ids = route(model, L, hs)
+            sy = O.linear(O.linear_swiglu(hs, L["shared_gate_up_full"]), L["shared_down_full"])
+            sg = O.linear_f32(hs, L["shared_gate"])
+            ys = ep.moe(hs, w, ids, L["experts_gate_up"], L["experts_down"], shared=(sy, sg))
+            sp.norm_gather(x, nxt, eps, addend=ys)
+        else:
+            act = sp.column(L["gate_up"], T, swiglu=True)
+            sp.row_parallel(act, L["down"])
+            sp.norm_gather(x, nxt, eps)
+        h = None
+    st.positions.add_(valid_len)
+    hf = sp.gathered(T)
+    last = torch.arange(B, device=dev) * S + (S - 1)
+    return hf[last].clone()

@@ -30,6 +30,31 @@ struct ArNormArgs {
 };
 void ar_add_norm(const ArNormArgs& a, cudaStream_t st);
 
+// Sequence-parallel reduce-scatter + residual add + RMSNorm + all-gather of
+// one shard of rows (F1 in reduce-scatter mode feeding F2).
+struct SpNormArgs {
+  const __nv_bfloat16* mc_partial;     // multicast base of the partial slots, or null
+  const __nv_bfloat16* local_partial;  // [rows, cols] local addend when mc_partial is null
+  long ldp;
+  long buf_stride;
+  int* sel;                  // slot selector of the partial slots
+  const unsigned* flags;     // partial completion flags (this rank's array)
+  const int* epoch;          // partial epoch
+  int world, rank;
+  __nv_bfloat16* x;          // residual shard [rows, cols] (updated)
+  long ldx;
+  const float* w;            // RMSNorm(1+w)
+  __nv_bfloat16* h_mc;       // multicast base of the gathered normed rows [world*rows, cols]
+  int rows, cols;
+  float eps;
+  unsigned* ag_peer_flags[8];
+  int* ag_epoch;
+  int* ticket;
+  int* status;
+  unsigned long long limit_ns;
+};
+void sp_norm_gather(const SpNormArgs& a, cudaStream_t st);
+
 struct GreedyArgs {
   const int64_t* keys;     // [rows] local packed argmax keys
   int rows;

@@ -162,6 +162,97 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(const __nv_bfloat16* m
   }
 }
 
+// One CTA per shard row: (sum of every rank's partial row through the switch |
+// a local addend) + residual -> RMSNorm(1+w) -> multicast store of the normed
+// row into every rank's gathered buffer; the last CTA flips the partial slot
+// and publishes the gather flag.  The next column-parallel GEMM waits for that
+// flag per owner before reading the owner's rows (gemm_tc.cu, AgWait).
+__global__ void __launch_bounds__(256) sp_norm_gather_kernel(SpNormArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x;
+  const int cols = a.cols;
+  const long grow = (long)a.rank * a.rows + i;
+  __shared__ float red[8];
+  if (a.mc_partial) wait_flag_lane(a.flags, a.world, (unsigned)(*a.epoch), a.status, a.limit_ns);
+  __syncthreads();
+  constexpr int kMaxVec = 4;
+  float v[kMaxVec][8];
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c >= cols) continue;
+    if (a.mc_partial) {
+      mc_ld_reduce_bf16x8(a.mc_partial + (long)((*a.sel) & 1) * a.buf_stride + grow * cols + c, v[n]);
+    } else {
+      const uint4 p = *reinterpret_cast<const uint4*>(a.local_partial + (long)i * a.ldp + c);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(p2[e]);
+        v[n][2 * e] = f.x;
+        v[n][2 * e + 1] = f.y;
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c >= cols) continue;
+    __nv_bfloat16* xr = a.x + (long)i * a.ldx + c;
+    const uint4 rr = *reinterpret_cast<const uint4*>(xr);
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 rf = __bfloat1622float2(r2[e]);
+      const __nv_bfloat162 nb = __floats2bfloat162_rn(rf.x + v[n][2 * e], rf.y + v[n][2 * e + 1]);
+      o2[e] = nb;
+      const float2 nf = __bfloat1622float2(nb);
+      v[n][2 * e] = nf.x;
+      v[n][2 * e + 1] = nf.y;
+      ss += nf.x * nf.x + nf.y * nf.y;
+    }
+    *reinterpret_cast<uint4*>(xr) = o;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int k = 0; k < (int)(blockDim.x >> 5); ++k) tot += red[k];
+  const float inv = rsqrtf(tot / cols + a.eps);
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c >= cols) continue;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = v[n][e] * inv * (1.f + a.w[c + e]);
+    mc_st_bf16x8(a.h_mc + grow * cols + c, o);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int t = atomicAdd(a.ticket, 1);
+    if (t == (int)gridDim.x - 1) {
+      *a.ticket = 0;
+      if (a.mc_partial) a.sel[0] = a.sel[0] + 1;
+      fence_acq_rel_sys();
+      const unsigned e = (unsigned)(*a.ag_epoch) + 1u;
+      *a.ag_epoch = (int)e;
+      for (int r = 0; r < a.world; ++r) st_relaxed_sys_u32(a.ag_peer_flags[r] + a.rank, e);
+    }
+  }
+}
+
+void sp_norm_gather(const SpNormArgs& a, cudaStream_t st) {
+  BWN_CHECK(a.cols % 8 == 0 && a.cols <= 256 * 8 * 4, "sp_norm_gather: hidden must be a multiple of 8, at most 8192");
+  BWN_CHECK(a.world >= 1 && a.world <= 8 && a.rows > 0, "sp_norm_gather: bad shape");
+  launch_k(sp_norm_gather_kernel, dim3(a.rows), dim3(256), 0, st, a);
+}
+
 __global__ void greedy_allmax_kernel(GreedyArgs a) {
   pdl_trigger();
   pdl_wait();

@@ -67,6 +67,18 @@ struct CommSignal {
   long buf_stride = 0;                   // elements between the two alternating buffers
 };
 
+// All-gathered A operand: rows [r*rows, (r+1)*rows) of A are written by rank r
+// into this rank's copy; the producer waits for flags[r] >= *epoch before
+// loading them, and visits this rank's own rows first.
+struct AgWait {
+  const unsigned* flags = nullptr;
+  const int* epoch = nullptr;
+  int rows = 0;  // rows per rank, a multiple of 128
+  int rank = 0;
+  int world = 0;
+  unsigned long long limit_ns = 0;
+};
+
 struct GemmProblem {
   // D[M, N] = A[M, K] . B[N, K]^T ; A, B bf16 K-major
   const void* A = nullptr;
@@ -90,6 +102,7 @@ struct GemmProblem {
   int tickets_len = 0;
   int* status = nullptr;
   CommSignal sig;  // kEpiSymm only
+  AgWait ag;       // A all-gathered by peers (normal orientation only)
 };
 
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);

@@ -347,6 +347,18 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// 8 values rounded to bf16 and stored into every rank's copy (multicast address).
+__device__ __forceinline__ void mc_st_bf16x8(void* mc_addr, const float (&v)[8]) {
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    r[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
 __device__ __forceinline__ void st_relaxed_sys_u32(unsigned* p, unsigned v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

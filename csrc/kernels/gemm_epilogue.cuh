@@ -1,7 +1,8 @@
 // Shared epilogue of the tcgen05 GEMM kernels (gemm_tc.cu, gemm_w8.cu): the
 // argument block and the per-thread store of one 32-column accumulator chunk
-// (bf16, bf16 + residual, SwiGLU over 16-interleaved gate/up, fp32, or NVLS
-// multimem reduction), in normal or transposed (swap-AB) orientation.
+// (bf16, bf16 + residual, SwiGLU over 16-interleaved gate/up, fp32, or the
+// bf16 partial into a symmetric slot), in normal or transposed (swap-AB)
+// orientation.
 #pragma once
 #include "common/host.h"
 #include "common/sm100.cuh"
@@ -19,7 +20,15 @@ struct GemmArgs {
   int* tickets;                // splits>1: [tiles]
   int* status;
   CommSignal sig;              // kEpiSymm: completion signal to peers
+  AgWait ag;                   // A rows all-gathered by peers: wait per owner
 };
+
+// Row tile of a work tile; with an all-gathered A this rank's own rows come first.
+__device__ __forceinline__ int gemm_tile_m(const GemmArgs& a, int tile, int bm) {
+  int tm = tile % a.tiles_m;
+  if (a.ag.flags) tm = (tm + a.ag.rank * (a.ag.rows / bm)) % a.tiles_m;
+  return tm;
+}
 
 template <int BN, int EPI, bool TRANS>
 __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, const float (&v)[32], int ncols, int m, int n0) {

@@ -118,11 +118,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       pdl_wait();
+      // all-gathered A: owners whose rows have arrived (this rank's are local)
+      uint32_t ag_ready = args.ag.flags ? (1u << args.ag.rank) : 0xFFFFFFFFu;
+      const unsigned ag_epoch = args.ag.flags ? (unsigned)(*args.ag.epoch) : 0u;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         const int tile = u / args.splits, sp = u % args.splits;
-        const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+        const int tm = gemm_tile_m(args, tile, kBM), tn = tile / args.tiles_m;
         const int kb0 = sp * args.kb_per_split;
         const int kb1 = min(args.num_kb, kb0 + args.kb_per_split);
+        if (!TRANS && !A_MN && args.ag.flags) {
+          const int owner = (tm * kBM) / args.ag.rows;
+          if (owner < args.ag.world && !((ag_ready >> owner) & 1u)) {
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while ((int)(ld_acquire_sys(args.ag.flags + owner) - ag_epoch) < 0) {
+              if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > args.ag.limit_ns) {
+                set_status(args.status, kStatusPeerTimeout);
+                *abort_flag = 1;
+                break;
+              }
+            }
+            if (*abort_flag) break;
+            ag_ready |= 1u << owner;
+          }
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (pre > 0) {  // A already in flight for this stage: only B remains
             tma_load_2d_hint(&tmB, &full_bar[s], sB + s * C::kBBytes, kb * kBK, tn * BN, polB);
@@ -224,7 +243,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int i = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
       const int tile = u / args.splits, sp = u % args.splits;
-      const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+      const int tm = gemm_tile_m(args, tile, kBM), tn = tile / args.tiles_m;
       const int ab = i & 1;
       const uint32_t use = (uint32_t)(i >> 1);
       if (!mbar_wait(&tfull_bar[ab], use & 1)) {
@@ -408,6 +427,12 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   a.M = p.M;
   a.N = p.N;
   a.K = p.K;
+  if (p.ag.flags) {
+    BWN_CHECK(!p.trans_out && !p.a_mn && p.ag.rows % kBM == 0 && p.ag.world >= 1 && p.ag.world <= 32 &&
+                  (long)p.ag.rows * p.ag.world == p.M,
+              "gemm: all-gathered A needs the normal orientation and 128-row shards covering M");
+    a.ag = p.ag;
+  }
   a.tiles_m = (p.M + kBM - 1) / kBM;
   a.tiles_n = (p.N + bn - 1) / bn;
   a.num_kb = (p.K + kBK - 1) / kBK;

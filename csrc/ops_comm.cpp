@@ -240,6 +240,83 @@ void ep_return_op(const Tensor& y, std::vector<int64_t> peer_base, int64_t rank,
   ep_wait(a, 1, st);
 }
 
+// ---- sequence parallelism: reduce-scatter + norm + all-gather, all-gather -> GEMM
+// sp state int32: [0] partial epoch, [1] GEMM done ticket, [2] slot selector,
+// [3] unused, [4] gather epoch, [5] gather ticket
+void sp_norm_gather_op(int64_t mc_partial, const c10::optional<Tensor>& local_partial, int64_t buf_stride,
+                       int64_t flags_local, int64_t world, int64_t rank, Tensor state, Tensor x, const Tensor& w,
+                       double eps, int64_t h_mc, std::vector<int64_t> ag_peer_flags, double timeout_s) {
+  check_bf16(x, "x");
+  check_f32(w, "w");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 8 == 0, "x [rows, H] with 16-byte rows");
+  TORCH_CHECK(state.scalar_type() == at::kInt && state.numel() >= 8, "state int32[8+]");
+  TORCH_CHECK(ag_peer_flags.size() == (size_t)world && world >= 1 && world <= 8, "ag flags: one per rank");
+  const c10::cuda::CUDAGuard guard(x.device());
+  SpNormArgs a{};
+  a.mc_partial = reinterpret_cast<const __nv_bfloat16*>(mc_partial);
+  if (!mc_partial) {
+    TORCH_CHECK(local_partial.has_value(), "sp_norm_gather: a local addend when there is no partial slot");
+    check_bf16(*local_partial, "local_partial");
+    TORCH_CHECK(local_partial->size(0) == x.size(0) && local_partial->stride(1) == 1, "local_partial [rows, H]");
+    a.local_partial = reinterpret_cast<const __nv_bfloat16*>(local_partial->data_ptr());
+    a.ldp = local_partial->stride(0);
+  }
+  int* s = state.data_ptr<int>();
+  a.buf_stride = buf_stride;
+  a.sel = s + 2;
+  a.flags = reinterpret_cast<const unsigned*>(flags_local);
+  a.epoch = s + 0;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.x = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr<float>();
+  a.h_mc = reinterpret_cast<__nv_bfloat16*>(h_mc);
+  a.rows = (int)x.size(0);
+  a.cols = (int)x.size(1);
+  a.eps = (float)eps;
+  for (int r = 0; r < world; ++r) a.ag_peer_flags[r] = reinterpret_cast<unsigned*>(ag_peer_flags[r]);
+  a.ag_epoch = s + 4;
+  a.ticket = s + 5;
+  a.status = status_dev_ptr();
+  a.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  if (a.rows > 0) sp_norm_gather(a, at::cuda::getCurrentCUDAStream().stream());
+}
+
+// Column-parallel GEMM on the gathered rows: waits per owner for its rows.
+Tensor linear_ag_op(const Tensor& h, const Tensor& w, int64_t epi, int64_t ag_flags_local, const Tensor& state,
+                    int64_t rows_per_rank, int64_t rank, int64_t world, double timeout_s) {
+  check_bf16(h, "h");
+  check_bf16(w, "w");
+  TORCH_CHECK(h.dim() == 2 && h.stride(1) == 1 && w.dim() == 2 && w.is_contiguous(), "row-major h, w");
+  TORCH_CHECK(epi == kEpiBF16 || epi == kEpiSwiGLU, "linear_ag: bf16 or SwiGLU epilogue");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int M = (int)h.size(0), Nw = (int)w.size(0), K = (int)h.size(1);
+  auto out = at::empty({M, epi == kEpiSwiGLU ? Nw / 2 : Nw}, h.options());
+  GemmProblem p;
+  p.A = h.data_ptr();
+  p.lda = h.stride(0);
+  p.B = w.data_ptr();
+  p.ldb = w.stride(0);
+  p.M = M;
+  p.N = Nw;
+  p.K = K;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.epi = (int)epi;
+  p.bn = epi == kEpiSwiGLU ? std::max(32, gemm_pick_bn(Nw)) : 0;
+  p.status = status_dev_ptr();
+  p.allow_split = false;
+  p.ag.flags = reinterpret_cast<const unsigned*>(ag_flags_local);
+  p.ag.epoch = state.data_ptr<int>() + 4;
+  p.ag.rows = (int)rows_per_rank;
+  p.ag.rank = (int)rank;
+  p.ag.world = (int)world;
+  p.ag.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
 // ---- fused data-parallel gradient reduction --------------------------------
 static GradBucketArgs make_grad(const Tensor& grad, int64_t local, int64_t mc, int64_t flags_local,
                                 const std::vector<int64_t>& peer_flags, int64_t rank, int64_t epoch,
@@ -281,6 +358,12 @@ void grad_bucket_unpack_op(Tensor grad, int64_t local, int64_t mc, int64_t flags
 
 void register_comm_defs(torch::Library& m) {
   m.def(
+      "sp_norm_gather(int mc_partial, Tensor? local_partial, int buf_stride, int flags_local, int world, int rank, "
+      "Tensor(a!) state, Tensor(b!) x, Tensor w, float eps, int h_mc, int[] ag_peer_flags, float timeout_s) -> ()");
+  m.def(
+      "linear_ag(Tensor h, Tensor w, int epi, int ag_flags_local, Tensor state, int rows_per_rank, int rank, "
+      "int world, float timeout_s) -> Tensor");
+  m.def(
       "grad_bucket_reduce(Tensor grad, int local, int mc, int flags_local, int[] peer_flags, int rank, int epoch, "
       "Tensor(a!) ticket, float timeout_s) -> ()");
   m.def(
@@ -310,6 +393,8 @@ void register_comm_pybind(pybind11::module& mod) {
 }
 
 void register_comm_impls(torch::Library& m) {
+  m.impl("sp_norm_gather", &sp_norm_gather_op);
+  m.impl("linear_ag", &linear_ag_op);
   m.impl("grad_bucket_reduce", &grad_bucket_reduce_op);
   m.impl("grad_bucket_unpack", &grad_bucket_unpack_op);
   m.impl("ep_dispatch", &ep_dispatch_op);

@@ -155,3 +155,70 @@ def test_qwen36_moe_prefill_with_ep_all_to_all():
     for r in range(2):
         assert not isinstance(res[r], str), res[r]
         assert res[r] < 3e-2, res
+
+
+def _sp_worker(rank, world, port, moe, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+
+        from bwn.config import tiny_qwen36
+        from bwn.io import qwen36_weights as Wt
+        from bwn.models.qwen36 import build_qwen36
+        from bwn.models.qwen36_prefill import prefill_hidden_sp
+        from bwn.ops import check_status
+        from bwn.parallel.comm import init_distributed
+        from bwn.parallel.ep import enable_ep_all_to_all
+        from bwn.parallel.sp import SeqParallel
+
+        comm = init_distributed("nccl", timeout_s=60)
+        dev = torch.device("cuda", rank)
+        cfg = tiny_qwen36(moe=moe).scaled(q_heads=8, kv_heads=2, dn_k_heads=2, dn_v_heads=4)
+        hf = dict(Wt.synthetic_hf_globals(cfg, 3, "cpu"))
+        for i in range(cfg.num_layers):
+            hf.update(Wt.synthetic_hf_layer(cfg, i, 3, "cpu"))
+        ref = build_qwen36(cfg, device=dev, hf_state=hf)
+        m = build_qwen36(cfg, comm=comm, device=dev, hf_state=hf)
+        B, S = 4, 128
+        if moe:
+            enable_ep_all_to_all(m, max_tokens_per_rank=B * S // world, min_tokens_per_rank=8)
+        sp = SeqParallel(comm, cfg.hidden, B * S, device=dev)
+        toks = torch.randint(0, cfg.vocab, (B, S), generator=torch.Generator().manual_seed(0)).to(dev)
+        st0, st1 = ref.new_state(B, 160), m.new_state(B, 160)
+        h0 = ref.prefill_hidden(toks, st0).float()
+        errs = []
+        for _ in range(2):  # twice: buffers and epochs reused
+            st1 = m.new_state(B, 160)
+            h1 = prefill_hidden_sp(m, toks, st1, sp).float()
+            torch.cuda.synchronize()
+            check_status("sp prefill")
+            errs.append(float((h0 - h1).norm() / h0.norm()))
+        # decode after the sequence-parallel prefill continues correctly
+        t0 = ref.greedy(h0.bfloat16())
+        d0 = ref.decode_step(t0, st0).float()
+        d1 = m.decode_step(t0, st1).float()
+        errs.append(float((d0 != d1).float().mean()))
+        q.put((rank, errs))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001
+        import traceback
+        q.put((rank, "ERR " + traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("moe", [False, True])
+def test_sequence_parallel_prefill(moe):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_sp_worker, args=(r, 2, port, moe, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(60)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        assert max(res[r][:2]) < 3e-2 and res[r][2] <= 0.25, res
