@@ -55,6 +55,14 @@ __global__ void __cluster_dims__(kDnNJ, 1, 1) __launch_bounds__(128)
   const int pos = p.positions[b];
   const bool active = pos >= 0;
   const __nv_bfloat16* qkv = p.qkv + (long)b * p.qkv_stride;
+  // the state columns go into registers first: their HBM latency overlaps the
+  // conv / norm / gate prologue below
+  StateT* S = reinterpret_cast<StateT*>(p.state) + (((long)b * p.v_heads + h) * kDnDk) * kDnDv + jb * kDnCols + lane;
+  float st[32];
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) st[i] = to_f(S[(long)(warp * 32 + i) * kDnDv]);
+  }
   const int rm = p.ring_slots - 1;
   __nv_bfloat16* ring = p.conv_ring + (long)b * p.ring_slots * C;
   const int ks0 = (pos - 3) & rm, ks1 = (pos - 2) & rm, ks2 = (pos - 1) & rm, kcur = pos & rm;
@@ -121,14 +129,11 @@ __global__ void __cluster_dims__(kDnNJ, 1, 1) __launch_bounds__(128)
   __syncthreads();
 
   // ---- state pass: rows [32*warp, 32*warp+32), column = lane ----
-  StateT* S = reinterpret_cast<StateT*>(p.state) + (((long)b * p.v_heads + h) * kDnDk) * kDnDv + jb * kDnCols + lane;
-  float st[32];
   float pk = 0.f, pq = 0.f;
   if (active) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int r = warp * 32 + i;
-      st[i] = to_f(S[(long)r * kDnDv]);
       pk += st[i] * s_k[r];
       pq += st[i] * s_q[r];
     }

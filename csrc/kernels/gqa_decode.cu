@@ -20,6 +20,7 @@
 // (atomic ticket, re-armed afterwards) merges them and applies the gate.  Only
 // the CTA whose range holds `pos` touches cache row `pos`: it writes the new
 // row and substitutes it into its smem tile, so no CTA reads a row being written.
+#include <cstdlib>
 #include <exception>
 
 #include "common/host.h"
@@ -332,7 +333,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
 }
 
 int gqa_decode_workspace_floats(int batch, int q_heads, int kv_heads, int splits) {
-  return batch * q_heads * splits * (2 + kGD);
+  // per (row, head, split): the larger of the two kernels' partial records
+  // (CUDA-core: max, sum, O[256]; tensor-core: 16-byte aligned, 4 + 256)
+  return batch * q_heads * splits * (4 + kGD);
 }
 
 static int gqa_smem_bytes(int G) {
@@ -382,11 +385,38 @@ __global__ void __launch_bounds__(kGD) gqa_kv_append_kernel(GqaDecodeArgs p) {
   p.v_cache[row * kGD + t] = p.v_new[(long)r * p.kv_new_stride + (long)kvh * kGD + t];
 }
 
+bool gqa_decode_tc_supported(const GqaDecodeArgs& p);
+void gqa_decode_tc(const CUtensorMap& tk, const CUtensorMap& tv, const GqaDecodeArgs& p, cudaStream_t st);
+
+static bool tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("BWN_GQA_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
   BWN_CHECK(p.q_heads % p.kv_heads == 0, "gqa_decode: q_heads %% kv_heads");
   BWN_CHECK(p.rope_dim <= kGD && p.rope_dim % 2 == 0, "gqa_decode: bad rope_dim");
   const int ntok = p.n_tok > 1 ? p.n_tok : 1;
   BWN_CHECK(p.batch % ntok == 0, "gqa_decode: rows %% n_tok");
+  if (tc_enabled() && gqa_decode_tc_supported(p)) {
+    // tensor-core path: append the new K/V rows, then attention over the cache
+    GqaDecodeArgs q = p;
+    q.n_tok = ntok;
+    launch_k(gqa_kv_append_kernel, dim3(q.kv_heads, q.batch), dim3(kGD), 0, stream, q);
+    const int pairs = (q.batch / ntok) * q.kv_heads;
+    int splits = std::max(1, std::min(p.splits, num_sms() / std::max(1, pairs)));
+    splits = std::min(splits, (q.s_max + 127) / 128);
+    q.splits = splits;
+    CUtensorMap tk, tv;
+    const long rows = (long)(q.batch / ntok) * q.kv_heads * q.s_max;
+    make_tmap_2d_bf16(&tk, q.k_cache, rows, kGD, kGD, 128, 64);
+    make_tmap_2d_bf16(&tv, q.v_cache, rows, kGD, kGD, 128, 64);
+    gqa_decode_tc(tk, tv, q, stream);
+    return;
+  }
   if (ntok > 1) launch_k(gqa_kv_append_kernel, dim3(p.kv_heads, p.batch), dim3(kGD), 0, stream, p);
   const int G = p.q_heads / p.kv_heads;
   CUtensorMap tk, tv;
@@ -417,7 +447,7 @@ void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
 //
 // Limits and sharing rules:
 //  * kNoAllocScratchFloats (1 Mi floats = 4 MiB) holds the partials,
-//    batch * q_heads * splits * (2 + 256) floats; kNoAllocTickets (4096)
+//    batch * q_heads * splits * (4 + 256) floats; kNoAllocTickets (4096)
 //    bounds batch * kv_heads.  The split count is lowered to fit; a problem
 //    that does not fit even with one split is rejected (return code 2).
 //  * The array exists once per GPU that loads this library and is held until
@@ -462,7 +492,7 @@ extern "C" int bwn_gqa_decode_noalloc(const void* qg, long qg_stride, const void
   const int G = q_heads / kv_heads;
   if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8)) return 1;
   if ((long)batch * kv_heads > kNoAllocTickets) return 2;
-  const long per_split = (long)batch * q_heads * (2 + 256);
+  const long per_split = (long)batch * q_heads * (4 + 256);
   if (per_split > kNoAllocScratchFloats) return 2;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return 3;

@@ -1,0 +1,369 @@
+// Gated GQA decode attention on the tcgen05 tensor cores (one or a few query
+// tokens per sequence).  Reference: the GQA tail kernels
+// (contrib/qwen3.6-27b/kernels/gqa_tail.py:48-203,
+//  contrib/qwen3.6-35b-a3b/kernels/gqa_tail_35b.py:52-394).
+//
+// The G query heads of a KV head (times the tokens of a multi-token verify)
+// are the MMA rows of one CTA: Q [128 rows x 256] is normalised (RMSNorm(1+w)),
+// rotated (partial RoPE) and scaled by the softmax warps straight into shared
+// memory, then every 128-key tile of the CTA's split of the cache runs
+//   S = Q K^T   (tcgen05, fp32 in TMEM, double-buffered)
+//   P = exp2(S - m)  -> bf16 in shared memory (one thread per query row)
+//   O += P V    (tcgen05, V MN-major, O rescaled lazily in TMEM)
+// with K/V tiles streamed by TMA in the 128-byte swizzle.  The new K/V rows
+// are appended by gqa_kv_append_kernel before this kernel runs, so every CTA
+// only reads the cache.  Each split writes (max, sum, O) partials; the last
+// CTA of a (sequence, KV head) merges them and applies the sigmoid gate.
+#include "common/host.h"
+#include "common/launch.cuh"
+#include "common/sm100.cuh"
+#include "kernels/launch.h"
+
+namespace bwn {
+
+namespace {
+constexpr int kTM = 128;             // query rows per CTA (G * n_tok, padded)
+constexpr int kTN = 128;             // keys per tile
+constexpr int kTBox = 128 * 128;     // [128 rows x 64 dims] SW128 box, 16 KB
+constexpr int kTThreads = 192;
+constexpr int kTSmem = 1024 + 4 * kTBox /*Q*/ + 4 * kTBox /*K*/ + 4 * kTBox /*V*/ + 2 * kTBox /*P*/ + 256;
+constexpr int kTW = 4 + 256;         // partial record: max (log2 units), sum, 2 pad, O[256] (16-byte aligned)
+}  // namespace
+
+__global__ void __launch_bounds__(kTThreads, 1)
+    gqa_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                         GqaDecodeArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sQ = sm;
+  uint8_t* sK = sQ + 4 * kTBox;
+  uint8_t* sV = sK + 4 * kTBox;
+  uint8_t* sP = sV + 4 * kTBox;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTBox);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;   // [2]
+  uint64_t* s_empty = bars + 7;  // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_ready = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_ticket = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+
+  const int sp = blockIdx.x, kvh = blockIdx.y, cb = blockIdx.z;
+  const int warp = warp_id(), lane = lane_id();
+  const int ntok = p.n_tok > 1 ? p.n_tok : 1;
+  const int G = p.q_heads / p.kv_heads;
+  const int nrows = ntok * G;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], (i == 0 || i == 7 || i == 8 || i == 9) ? 128 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S0 @0, S1 @128, O @256
+  pdl_wait();
+
+  int Lmax = 0;
+  for (int i = 0; i < ntok; ++i) Lmax = max(Lmax, p.positions[cb * ntok + i] + 1);
+  int chunk = (Lmax + p.splits - 1) / p.splits;
+  chunk = (chunk + kTN - 1) / kTN * kTN;
+  const int k0 = sp * chunk;
+  const int k1 = min(Lmax, k0 + chunk);
+  const int ntiles = k1 > k0 ? (k1 - k0 + kTN - 1) / kTN : 0;
+  const long krow0 = ((long)cb * p.kv_heads + kvh) * p.s_max + k0;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (elect_one()) {
+      for (int j = 0; j < ntiles && !*abort_flag; ++j) {
+        if (!mbar_wait(k_empty, (j & 1) ^ 1)) {
+          set_status(p.status, kStatusMbarTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(k_full, 4 * kTBox);
+        for (int bx = 0; bx < 4; ++bx) tma_load_2d(&tmK, k_full, sK + bx * kTBox, bx * 64, (int)(krow0 + j * kTN));
+        if (!mbar_wait(v_empty, (j & 1) ^ 1)) {
+          set_status(p.status, kStatusMbarTimeout);
+          *abort_flag = 1;
+          mbar_wait(k_full, j & 1, 100000000ull);
+          break;
+        }
+        mbar_arrive_expect_tx(v_full, 4 * kTBox);
+        for (int bx = 0; bx < 4; ++bx) tma_load_2d(&tmV, v_full, sV + bx * kTBox, bx * 64, (int)(krow0 + j * kTN));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (elect_one()) {
+      const uint32_t id_qk = idesc_bf16_f32_major(kTM, kTN, false, false);
+      const uint32_t id_pv = idesc_bf16_f32_major(kTM, 256, false, true);
+      bool ok = ntiles == 0 || mbar_wait(q_full, 0);
+      auto issue_qk = [&](int j) -> bool {
+        if (!mbar_wait(k_full, j & 1)) return false;
+        if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + (j & 1) * kTN;
+        for (int bx = 0; bx < 4; ++bx) {
+          const uint64_t da = smem_desc_sw128(smem_u32(sQ + bx * kTBox));
+          const uint64_t db = smem_desc_sw128(smem_u32(sK + bx * kTBox));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) umma_f16(d, da + 2 * kk, db + 2 * kk, id_qk, (bx | kk) ? 1u : 0u);
+        }
+        umma_commit(&s_full[j & 1]);
+        umma_commit(k_empty);
+        return true;
+      };
+      if (ok && ntiles > 0) ok = issue_qk(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (j + 1 < ntiles && !issue_qk(j + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(v_full, j & 1) || !mbar_wait(p_full, j & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < 2; ++kb) {
+          const uint64_t da = smem_desc_sw128(smem_u32(sP + kb * kTBox));
+          const uint64_t db = smem_desc_sw128_mn(smem_u32(sV + kb * 8192), kTBox);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + 256, da + 2 * kk, db + 128 * kk, id_pv, (j | kb | kk) ? 1u : 0u);
+        }
+        umma_commit(o_ready);
+        umma_commit(v_empty);
+      }
+      if (!ok) {
+        set_status(p.status, kStatusMbarTimeout);
+        *abort_flag = 1;
+      }
+    }
+  } else {
+    // ------------------------- Q prologue + softmax warps ---------------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // query row == TMEM lane
+    const bool real = r < nrows;
+    const int i_tok = real ? r / G : 0, g = real ? r % G : 0;
+    const int vrow = cb * ntok + i_tok, qh = kvh * G + g;
+    const int pos = real ? p.positions[vrow] : -1;
+    const __nv_bfloat16* qrow = p.qg + (long)vrow * p.qg_stride + (long)qh * 512;
+    // q row: RMSNorm(1+w), partial RoPE (rotate-half within rope_dim), 1/sqrt(256)
+    float ss = 0.f;
+    if (real) {
+      for (int c = 0; c < 256; c += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(qrow + c);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h2[e]);
+          ss += f.x * f.x + f.y * f.y;
+        }
+      }
+    }
+    const float inv = rsqrtf(ss / 256.f + p.eps);
+    const int R = p.rope_dim, hr = R >> 1;
+    const float qscale = rsqrtf(256.f);
+    for (int c = 0; c < 256; c += 8) {
+      alignas(16) __nv_bfloat16 o8[8];
+      if (real) {
+        float x[8], y[8];
+        const uint4 u = *reinterpret_cast<const uint4*>(qrow + c);
+        const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(hb[e]) * inv * (1.f + p.q_norm_w[c + e]);
+        if (c < R) {
+          const int pc = c < hr ? c + hr : c - hr;
+          const float sg = c < hr ? -1.f : 1.f;
+          const uint4 up = *reinterpret_cast<const uint4*>(qrow + pc);
+          const __nv_bfloat16* hp = reinterpret_cast<const __nv_bfloat16*>(&up);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float xp = __bfloat162float(hp[e]) * inv * (1.f + p.q_norm_w[pc + e]);
+            const float cs = p.cos[(long)pos * R + c + e], sn = p.sin[(long)pos * R + c + e];
+            y[e] = x[e] * cs + sg * xp * sn;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) y[e] = x[e];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16(y[e] * qscale);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16(0.f);
+      }
+      const int box = c >> 6, chk = ((c & 63) >> 3) ^ (r & 7);
+      *reinterpret_cast<uint4*>(sQ + box * kTBox + r * 128 + chk * 16) = *reinterpret_cast<uint4*>(o8);
+    }
+    fence_async_smem();
+    mbar_arrive(q_full);
+
+    const float sl2 = 1.4426950408889634f;  // log2(e); 1/sqrt(D) is folded into q
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kTN];
+#pragma unroll
+      for (int c = 0; c < kTN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + (j & 1) * kTN + c, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[c + e] = v[e];
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[j & 1]);
+      const int kbase = k0 + j * kTN;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTN; ++c) {
+        const int key = kbase + c;
+        const bool vis = key <= pos && key < k1;
+        s[c] = vis ? s[c] * sl2 : -INFINITY;
+        mt = fmaxf(mt, s[c]);
+      }
+      const float mn = fmaxf(m, mt);
+      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - mn);
+      if (j > 0) {
+        if (!mbar_wait(o_ready, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, mn > m)) {
+#pragma unroll 1
+          for (int c = 0; c < 256; c += 32) {
+            float v[32];
+            tmem_ld32(tmem + lane_base + 256 + c, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= alpha;
+            tmem_st32(tmem + lane_base + 256 + c, v);
+          }
+        }
+      }
+      float ls = 0.f;
+      const float msafe = mn == -INFINITY ? 0.f : mn;
+#pragma unroll
+      for (int c = 0; c < kTN; c += 8) {
+        alignas(16) __nv_bfloat16 pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float pe = exp2f(s[c + e] - msafe);
+          ls += pe;
+          pv[e] = __float2bfloat16(pe);
+        }
+        const int box = c >> 6;
+        const int chk = ((c & 63) >> 3) ^ (r & 7);
+        *reinterpret_cast<uint4*>(sP + box * kTBox + r * 128 + chk * 16) = *reinterpret_cast<uint4*>(pv);
+      }
+      l = l * alpha + ls;
+      m = mn;
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- this split's partial (max, sum, O) ----
+    float* ws = p.workspace + ((((long)cb * p.kv_heads + kvh) * p.splits + sp) * nrows) * kTW;
+    if (ok && ntiles > 0 && mbar_wait(o_ready, (ntiles - 1) & 1)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 256; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + 256 + c, v);
+        if (real) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(ws + (long)r * kTW + 4 + c + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        }
+      }
+      if (real) {
+        ws[(long)r * kTW + 0] = m;
+        ws[(long)r * kTW + 1] = l;
+      }
+    } else {
+      if (!ok) {
+        set_status(p.status, kStatusMbarTimeout);
+        *abort_flag = 1;
+      }
+      if (real) {
+        ws[(long)r * kTW + 0] = -INFINITY;
+        ws[(long)r * kTW + 1] = 0.f;
+      }
+    }
+  }
+  // ---- last CTA of (sequence, KV head) merges the splits, applies the gate ----
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) *s_ticket = atomicAdd(&p.tickets[cb * p.kv_heads + kvh], 1);
+  __syncthreads();
+  if (*s_ticket == p.splits - 1) {
+    __threadfence();
+    const float* wsb = p.workspace + (((long)cb * p.kv_heads + kvh) * p.splits) * nrows * kTW;
+    for (int rr = 0; rr < nrows; ++rr) {
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(wsb + ((long)s2 * nrows + rr) * kTW));
+      const int vr = cb * ntok + rr / G, qh2 = kvh * G + rr % G;
+      for (int d = threadIdx.x; d < 256; d += blockDim.x) {
+        float Ls = 0.f, o = 0.f;
+        for (int s2 = 0; s2 < p.splits; ++s2) {
+          const float* e = wsb + ((long)s2 * nrows + rr) * kTW;
+          const float mm = __ldcg(e);
+          if (mm == -INFINITY) continue;
+          const float w = exp2f(mm - M);
+          Ls += __ldcg(e + 1) * w;
+          o += __ldcg(e + 4 + d) * w;
+        }
+        const float gate = __bfloat162float(p.qg[(long)vr * p.qg_stride + (long)qh2 * 512 + 256 + d]);
+        p.out[(long)vr * p.out_stride + (long)qh2 * 256 + d] =
+            __float2bfloat16((Ls > 0.f ? o / Ls : 0.f) * sigmoid_f(gate));
+      }
+    }
+    if (threadIdx.x == 0) p.tickets[cb * p.kv_heads + kvh] = 0;
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+bool gqa_decode_tc_supported(const GqaDecodeArgs& p) {
+  const int ntok = p.n_tok > 1 ? p.n_tok : 1;
+  const int G = p.q_heads / p.kv_heads;
+  return G * ntok <= kTM && p.rope_dim % 16 == 0;  // rope halves on 16-byte chunks
+}
+
+void gqa_decode_tc(const CUtensorMap& tk, const CUtensorMap& tv, const GqaDecodeArgs& p, cudaStream_t st) {
+  static bool set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!set[dev & 63]) {
+    BWN_CUDA_CHECK(cudaFuncSetAttribute(gqa_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTSmem));
+    set[dev & 63] = true;
+  }
+  const int ntok = p.n_tok > 1 ? p.n_tok : 1;
+  launch_k(gqa_decode_tc_kernel, dim3(p.splits, p.kv_heads, p.batch / ntok), dim3(kTThreads), kTSmem, st, tk, tv,
+           p);
+}
+
+}  // namespace bwn
