@@ -117,18 +117,28 @@ def _unshard_view(sd: dict, cfg: DeepSeekV4Config, tp: int, rank: int) -> dict:
 
 
 class DeepSeekV4Model:
-    def __init__(self, cfg: DeepSeekV4Config, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16):
+    """``comm`` is the tensor-parallel group of the attention.  ``ep_comm``
+    (optional) is a separate expert-parallel group: the hybrid layout of the
+    reference (``run_deepseek_v4_hybrid.py:36-37, 437-460, 516-585, 760-763``),
+    where TP groups are consecutive ranks and EP groups are strided by the TP
+    size; routed experts and the shared expert are then split over the EP group
+    and the MoE partials all-reduced there.  Without it, one group does both."""
+
+    def __init__(self, cfg: DeepSeekV4Config, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16,
+                 ep_comm: Comm | None = None):
         self.cfg = cfg
         self.comm = comm or Comm.single()
+        self.ep_comm = ep_comm or self.comm
         self.tp, self.rank = self.comm.size, self.comm.rank
-        if cfg.n_heads % self.tp or cfg.o_groups % self.tp or cfg.n_routed_experts % self.tp:
-            raise ValueError("tp must divide n_heads, o_groups and n_routed_experts")
+        self.ep, self.ep_rank = self.ep_comm.size, self.ep_comm.rank
+        if cfg.n_heads % self.tp or cfg.o_groups % self.tp or cfg.n_routed_experts % self.ep:
+            raise ValueError("tp must divide n_heads and o_groups, ep must divide n_routed_experts")
         self.device = torch.device(device)
         self.dtype = dtype
         self.heads = cfg.n_heads // self.tp
         self.groups = cfg.o_groups // self.tp
-        self.e_local = cfg.n_routed_experts // self.tp
-        self.e0 = self.rank * self.e_local
+        self.e_local = cfg.n_routed_experts // self.ep
+        self.e0 = self.ep_rank * self.e_local
         half = cfg.rope_head_dim // 2
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.rope_head_dim, 2, dtype=torch.float32) / cfg.rope_head_dim))
         f = torch.outer(torch.arange(cfg.max_seq_len, dtype=torch.float32), inv)
@@ -149,7 +159,8 @@ class DeepSeekV4Model:
         g0, g1 = r * self.groups, (r + 1) * self.groups
         olr = cfg.o_lora_rank
         E, I = cfg.n_routed_experts, cfg.moe_inter
-        Is = I // self.tp
+        Is = I // self.ep
+        re = self.ep_rank
         if presharded:
             sd = _unshard_view(sd, cfg, self.tp, r)
         self.L = []
@@ -174,9 +185,9 @@ class DeepSeekV4Model:
             w3 = _expert_stack(sd, f, "w3", self.e0, self.e0 + self.e_local)
             L["experts_gate_up"] = torch.stack([O.interleave_gate_up(w1[e], w3[e]) for e in range(self.e_local)]).to(dt)
             L["experts_down"] = _expert_stack(sd, f, "w2", self.e0, self.e0 + self.e_local).to(dt)
-            L["shared_gate_up"] = O.interleave_gate_up(sd[f + "shared_experts.w1.weight"][r * Is:(r + 1) * Is],
-                                                       sd[f + "shared_experts.w3.weight"][r * Is:(r + 1) * Is]).to(dt)
-            L["shared_down"] = sd[f + "shared_experts.w2.weight"][:, r * Is:(r + 1) * Is].to(dt)
+            L["shared_gate_up"] = O.interleave_gate_up(sd[f + "shared_experts.w1.weight"][re * Is:(re + 1) * Is],
+                                                       sd[f + "shared_experts.w3.weight"][re * Is:(re + 1) * Is]).to(dt)
+            L["shared_down"] = sd[f + "shared_experts.w2.weight"][:, re * Is:(re + 1) * Is].to(dt)
             self.L.append({k: (tuple(x.to(dev) for x in v) if isinstance(v, tuple) else
                                (v.to(dev).contiguous() if v is not None else None)) for k, v in L.items()})
         self.g = {
@@ -216,7 +227,7 @@ class DeepSeekV4Model:
         The weights differ between tensor-parallel degrees; for benchmarks."""
         cfg, dt, dev = self.cfg, self.dtype, self.device
         hd, olr, I = cfg.head_dim, cfg.o_lora_rank, cfg.moe_inter
-        Is = I // self.tp
+        Is = I // self.ep
         mix = (2 + cfg.hc_mult) * cfg.hc_mult
         g = torch.Generator(device=dev).manual_seed(seed * 1000 + self.rank)
 
@@ -289,7 +300,10 @@ class DeepSeekV4Model:
         routed = O.moe_experts(x, w, ids, L["experts_gate_up"], L["experts_down"], self.e0,
                                swiglu_limit=cfg.swiglu_limit)
         shared = O.linear(O.linear_swiglu(x, L["shared_gate_up"]), L["shared_down"])
-        return self._allreduce((routed.float() + shared.float()).to(x.dtype))
+        y = (routed.float() + shared.float()).to(x.dtype)
+        if self.ep > 1:
+            self.ep_comm.all_reduce_(y)
+        return y
 
     def forward_tokens(self, tokens: torch.Tensor, pos: torch.Tensor, bidx: torch.Tensor, st: DeepSeekV4State,
                        q_per_seq: int) -> torch.Tensor:

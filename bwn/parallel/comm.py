@@ -103,3 +103,27 @@ def init_distributed(backend: str | None = None, timeout_s: float = 120.0) -> Co
     else:
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s))
     return Comm.from_group(None)
+
+
+def hybrid_groups(tp: int, timeout_s: float = 120.0) -> tuple[Comm, Comm]:
+    """Split the world into tensor-parallel groups of ``tp`` consecutive ranks
+    and expert-parallel groups of the ranks with the same TP index (strided by
+    ``tp``), as the reference's hybrid runner does
+    (``contrib/deepseek-v4-flash/run_deepseek_v4_hybrid.py:760-763``).  Every
+    rank creates every group, in the same order."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if world % tp:
+        raise ValueError(f"tp={tp} must divide the world size {world}")
+    ep = world // tp
+    tp_group = ep_group = None
+    for g in range(ep):
+        ranks = list(range(g * tp, (g + 1) * tp))
+        grp = dist.new_group(ranks, timeout=datetime.timedelta(seconds=timeout_s))
+        if rank in ranks:
+            tp_group = grp
+    for i in range(tp):
+        ranks = list(range(i, world, tp))
+        grp = dist.new_group(ranks, timeout=datetime.timedelta(seconds=timeout_s))
+        if rank in ranks:
+            ep_group = grp
+    return (Comm(tp_group, dist.get_rank(tp_group), tp), Comm(ep_group, dist.get_rank(ep_group), ep))
