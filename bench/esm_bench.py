@@ -64,7 +64,9 @@ def main():
     tp = args.tp if W > 1 else 1
     dp = W // tp
     assert args.batch % dp == 0, "global batch must split over the data-parallel ranks"
-    model = init_on_device(EsmForMaskedLM(cfg).to(dev), 0, dev)
+    with torch.device(dev):  # build directly on the device (a 15B fp32 model does not fit host RAM x ranks)
+        model = EsmForMaskedLM(cfg)
+    model = init_on_device(model, 0, dev)
     reducer = None
     if tp > 1:
         from bwn.parallel.tensor_parallel import apply_esm_tp

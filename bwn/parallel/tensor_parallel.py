@@ -58,12 +58,12 @@ class ColumnParallelLinear(nn.Module):
             raise ValueError(f"{out} output features do not split over {tp} ranks")
         n = out // tp
         self.comm = comm
-        self.lin = BwnLinear(full.in_features, n, bias=full.bias is not None)
+        with torch.device(full.weight.device):
+            self.lin = BwnLinear(full.in_features, n, bias=full.bias is not None)
         with torch.no_grad():
             self.lin.weight.copy_(full.weight[r * n:(r + 1) * n])
             if full.bias is not None:
                 self.lin.bias.copy_(full.bias[r * n:(r + 1) * n])
-        self.lin.to(full.weight.device)
 
     @property
     def weight(self):
@@ -82,11 +82,11 @@ class RowParallelLinear(nn.Module):
             raise ValueError(f"{inp} input features do not split over {tp} ranks")
         n = inp // tp
         self.comm = comm
-        self.lin = BwnLinear(n, full.out_features, bias=False)
+        with torch.device(full.weight.device):
+            self.lin = BwnLinear(n, full.out_features, bias=False)
         with torch.no_grad():
             self.lin.weight.copy_(full.weight[:, r * n:(r + 1) * n])
         self.bias = nn.Parameter(full.bias.detach().clone()) if full.bias is not None else None
-        self.lin.to(full.weight.device)
 
     @property
     def weight(self):
