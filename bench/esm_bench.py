@@ -52,6 +52,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cpu", action="store_true")
+    ap.add_argument("--act-ckpt", action="store_true", help="recompute each layer's activations in backward")
     args = ap.parse_args()
     cfg = ESM2_SIZES[args.size]
     if args.cpu:
@@ -67,6 +68,7 @@ def main():
     with torch.device(dev):  # build directly on the device (a 15B fp32 model does not fit host RAM x ranks)
         model = EsmForMaskedLM(cfg)
     model = init_on_device(model, 0, dev)
+    model.activation_checkpointing = args.act_ckpt
     reducer = None
     if tp > 1:
         from bwn.parallel.tensor_parallel import apply_esm_tp
@@ -109,6 +111,7 @@ def main():
             "samples_per_s": round(args.batch / ms * 1e3, 2), "tokens_per_s": round(tokens / ms * 1e3, 1),
             "model_tflops_per_gpu": round(flops / (ms / 1e3) / 1e12 / max(W, 1), 1) if not args.cpu else None,
             "dtype": "fp32" if args.cpu else "bf16 GEMMs, fp32 master weights", "loss": round(float(loss), 4),
+            "activation_checkpointing": args.act_ckpt,
             "data": "synthetic (uniform amino acids, 15% masking 80/10/10), random-init weights"}))
     if W > 1:
         import torch.distributed as dist

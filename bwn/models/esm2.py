@@ -184,8 +184,13 @@ class EsmForMaskedLM(nn.Module):
         x = self.embed(input_ids, attention_mask).to(compute_dtype)
         bias = torch.zeros(attention_mask.shape, dtype=compute_dtype, device=x.device)
         bias = bias.masked_fill(attention_mask == 0, torch.finfo(compute_dtype).min)[:, None, None, :]
+        ckpt = getattr(self, "activation_checkpointing", False) and torch.is_grad_enabled()
         for layer in self.esm.encoder.layer:
-            x = layer(x, bias)
+            if ckpt:  # keep only each layer's input; recompute its activations in backward
+                from torch.utils.checkpoint import checkpoint
+                x = checkpoint(layer, x, bias, use_reentrant=False)
+            else:
+                x = layer(x, bias)
         x = self.esm.encoder.emb_layer_norm_after(x)
         h = self.lm_head.layer_norm(esm_gelu(self.lm_head.dense(x)))
         w = self.esm.embeddings.word_embeddings.weight
