@@ -104,9 +104,13 @@ class EsmSelfAttention(nn.Module):
         cos, sin = emb.cos().to(q.dtype), emb.sin().to(q.dtype)
         q = q * cos + _rotate_half(q) * sin
         k = k * cos + _rotate_half(k) * sin
-        q, k, v = q.to(v.dtype), k.to(v.dtype), v
+        out_dtype = v.dtype
+        if x.is_cuda:  # bf16 attention (flash path) on the GPU, like the bf16 GEMMs
+            q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+        else:
+            q, k = q.to(v.dtype), k.to(v.dtype)
         o = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_bias.to(v.dtype), scale=1.0)
-        return o.transpose(1, 2).reshape(B, S, -1)
+        return o.transpose(1, 2).reshape(B, S, -1).to(out_dtype)
 
 
 class EsmLayer(nn.Module):

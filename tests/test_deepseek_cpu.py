@@ -12,7 +12,10 @@ import torch
 from bwn.config import tiny_deepseek_v4
 from bwn.models.deepseek_v4 import DeepSeekV4Model
 
-REF = "/root/reference/contrib/deepseek-v4-flash/run_deepseek_v4_tp.py"
+# the reference checkout: BWN_REFERENCE_ROOT, else a "reference" directory beside this repository
+_REF_ROOT = os.environ.get("BWN_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
+REF = os.path.join(_REF_ROOT, "contrib", "deepseek-v4-flash", "run_deepseek_v4_tp.py")
 
 
 def _load_reference():
