@@ -45,7 +45,25 @@ def main():
     g = torch.Generator(device=dev).manual_seed(0)
     R, H, K = a.rows, a.hidden, a.k
     paths = a.paths.split(",")
-    if "ar" in paths:
+
+    def run(name, setup):
+        """``setup`` builds the path's buffers (errors there, e.g. no multicast
+        object on a one-GPU group, skip the path) and returns one iteration;
+        kernel errors are not caught."""
+        if name not in paths:
+            return
+        try:
+            step = setup()
+        except RuntimeError as e:
+            print(f"{name}: skipped ({str(e).splitlines()[0][:160]})")
+            return
+        for _ in range(a.iters):
+            step()
+        torch.cuda.synchronize()
+        check_status(name)
+        print(f"{name}: ok")
+
+    def ar():
         from bwn.parallel.fused import FusedComm
         fc = FusedComm(comm, H, max_rows=max(R, 32), device=dev)
         x = torch.randn(R, K, device=dev, generator=g).bfloat16()
@@ -53,12 +71,13 @@ def main():
         resid = torch.randn(R, H, device=dev, generator=g).bfloat16()
         nw = torch.zeros(H, device=dev)
         part = torch.randn(R, H, device=dev, generator=g).bfloat16()
-        for _ in range(a.iters):
+
+        def step():
             fc.gemm_allreduce_add_norm(x, w, resid, nw, 1e-6)
             fc.allreduce_add_norm(part, resid, nw, 1e-6)
-        torch.cuda.synchronize()
-        print("ar: ok")
-    if "sp" in paths:
+        return step
+
+    def sp_path():
         from bwn.parallel.sp import SeqParallel
         T = a.sp_tokens
         sp = SeqParallel(comm, H, T, device=dev)
@@ -67,13 +86,14 @@ def main():
         w_row = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
         w_col = (torch.randn(4096, H, device=dev, generator=g) * 0.02).bfloat16()
         nw = torch.zeros(H, device=dev)
-        for _ in range(a.iters):
+
+        def step():
             sp.row_parallel(a_in, w_row)
             sp.norm_gather(xs, nw, 1e-6)
             sp.column(w_col, T)
-        torch.cuda.synchronize()
-        print("sp: ok")
-    if "ep" in paths:
+        return step
+
+    def ep_path():
         from bwn.parallel.ep import EPAllToAll
         E, Hm, I, k, T = 256, 2048, 512, 8, a.ep_tokens
         ep = EPAllToAll(comm, Hm, E, k, max_tokens=T, device=dev)
@@ -81,21 +101,21 @@ def main():
         dn = (torch.randn(E, Hm, I, device=dev, generator=g) * 0.02).bfloat16()
         xe = torch.randn(T, Hm, device=dev, generator=g).bfloat16()
         wt, ids = O.moe_topk_softmax(torch.randn(T, E, device=dev, generator=g), k, True)
-        for _ in range(a.iters):
-            ep.moe(xe, wt, ids, gu, dn)
-        torch.cuda.synchronize()
-        print("ep: ok")
-    if "grad" in paths:
+        return lambda: ep.moe(xe, wt, ids, gu, dn)
+
+    def grad_path():
         from bwn.parallel.grad_reduce import GradReducer
         from bwn.train.esm_mlm import build_esm
         m = build_esm("650M", device=dev, seed=0)
         red = GradReducer(m, comm, bucket_mb=64)
         for p in m.parameters():
             p.grad.normal_(generator=g)
-        for _ in range(a.iters):
-            red.finish()
-        torch.cuda.synchronize()
-        print("grad: ok")
+        return red.finish
+
+    run("ar", ar)
+    run("sp", sp_path)
+    run("ep", ep_path)
+    run("grad", grad_path)
     check_status("profile_fused")
     dist.destroy_process_group()
 
