@@ -32,6 +32,8 @@ FLAGS = {f.name: f for f in (
     Flag("BWN_DEBUG", int, 0, "build kernels with device-side bounds checks (build-time)", (0, 1)),
     Flag("BWN_METRICS", str, "", "path of a JSONL metrics file"),
     Flag("BWN_WAIT_LIMIT_MS", int, 2000, "bound on every device-side wait before it reports a timeout"),
+    Flag("BWN_GQA_TC", int, 1, "GQA decode on the tcgen05 kernel (0: CUDA-core kernel)", (0, 1)),
+    Flag("BWN_GEMM_MAX_SPLITS", int, 16, "upper bound of the decode GEMMs' split-K factor (1..16)"),
 )}
 
 

@@ -19,6 +19,8 @@
 // SwiGLU over gate/up rows interleaved in blocks of 16, fp32 store.
 #include "common/host.h"
 #include "common/sm100.cuh"
+#include <cstdlib>
+
 #include "common/launch.cuh"
 #include "kernels/gemm_epilogue.cuh"
 
@@ -446,7 +448,12 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   if (p.allow_split && tiles < sms && p.workspace && p.tickets && tiles <= p.tickets_len) {
     splits = sms / tiles;
     if (splits > a.num_kb / 4) splits = a.num_kb / 4 > 0 ? a.num_kb / 4 : 1;
-    if (splits > 16) splits = 16;
+    static const int max_splits = [] {
+      const char* e = getenv("BWN_GEMM_MAX_SPLITS");
+      const int v = e ? atoi(e) : 16;
+      return v >= 1 && v <= 16 ? v : 16;
+    }();
+    if (splits > max_splits) splits = max_splits;
     if ((long)tiles * splits * kBM * bn > p.workspace_floats) splits = 1;
   }
   a.splits = splits;
