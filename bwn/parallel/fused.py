@@ -52,10 +52,9 @@ class FusedComm:
         self.buf.zero_()
         torch.cuda.synchronize(dev)
         self.hdl = symm.rendezvous(self.buf, group)
-        if not self.hdl.has_multicast_support:
-            raise RuntimeError("NVLS multicast is not available on this system")
+        from .symm import multicast_address
+        mc = multicast_address(self.hdl)
         ptrs = [int(p) for p in self.hdl.buffer_ptrs]
-        mc = int(self.hdl.multicast_ptr)
         self.peer_flags_ar = [p + self.FLAGS_AR for p in ptrs]
         self.peer_flags_g = [p + self.FLAGS_GREEDY for p in ptrs]
         self.peer_slots = [p + self.SLOTS for p in ptrs]

@@ -154,9 +154,8 @@ class GradReducer(_HookedReducer):
         torch.cuda.synchronize(dev)
         self.hdl = symm.rendezvous(self.buf, group)
         ptrs = [int(p) for p in self.hdl.buffer_ptrs]
-        mc = int(self.hdl.multicast_ptr)
-        if not self.hdl.has_multicast_support:
-            raise RuntimeError("NVLS multicast is not available on this system")
+        from .symm import multicast_address
+        mc = multicast_address(self.hdl)
         for i, b in enumerate(self.buckets):
             b.local = ptrs[self.rank] + offs[i]
             b.mc = mc + offs[i]

@@ -46,10 +46,9 @@ class SeqParallel:
         self.buf.zero_()
         torch.cuda.synchronize(dev)
         self.hdl = symm.rendezvous(self.buf, group)
-        if not self.hdl.has_multicast_support:
-            raise RuntimeError("NVLS multicast is not available on this system")
+        from .symm import multicast_address
+        mc = multicast_address(self.hdl)
         ptrs = [int(p) for p in self.hdl.buffer_ptrs]
-        mc = int(self.hdl.multicast_ptr)
         self.partial_flags = list(ptrs)
         self.gather_flags = [p + 128 for p in ptrs]
         self.local_partial = ptrs[self.rank] + self.off_partial
