@@ -26,6 +26,7 @@ import time
 import torch
 
 BASELINE_TOK_S = 63.1  # reference Qwen3.6-27B decode, BS=16, trn2.3xl TP=4 (contrib/qwen3.6-27b/README.md:96)
+BASELINE_BS1_TOK_S = 28.2  # reference Qwen3.6-27B decode, BS=1, same box (contrib/qwen3.6-27b/README.md:94)
 METRIC = "decode tok/s/box + p50 TPOT & prefill TTFT, Qwen3.6 TP/EP at 1/2/4/8 B200"
 
 
@@ -85,6 +86,8 @@ def main() -> None:
     ap.add_argument("--profile-steps", type=int, default=int(os.environ.get("BWN_PROFILE_STEPS", "0")),
                     help="run warm-up + N decode steps only (for a profiler), then exit")
     ap.add_argument("--metrics", default=os.environ.get("BWN_METRICS", ""), help="JSONL metrics file")
+    ap.add_argument("--batch1-steps", type=int, default=32,
+                    help="also time batch-1 decode (latency) for this many steps; 0 skips")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -223,6 +226,32 @@ def main() -> None:
     value = B * args.steps / (total_ms / 1e3)
     e2e_value = B * args.steps / (e_ms / 1e3)
     dec.release()
+    del dec
+    torch.cuda.empty_cache()
+
+    # ---- batch-1 decode latency (same prompt length), its own CUDA graph ----
+    batch1 = None
+    if args.batch1_steps > 0:
+        n1 = args.batch1_steps
+        d1 = StaticDecoder(model, 1, S + n1 + 64, use_graph=not args.no_graph)
+        d1.capture()
+        d1.prefill(prompt[:1])
+        for _ in range(3):
+            d1.step_device()
+        torch.cuda.synchronize()
+        comm.barrier()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        for _ in range(n1):
+            d1.step_device()
+        b1.record()
+        torch.cuda.synchronize()
+        ms1 = comm.max_scalar(b0.elapsed_time(b1) / n1, dev)
+        check_status("batch-1 decode")
+        batch1 = {"tpot_ms": round(ms1, 4), "tok_s": round(1e3 / ms1, 1), "steps": n1,
+                  "vs_baseline_bs1": round((1e3 / ms1) / BASELINE_BS1_TOK_S, 2)}
+        d1.release()
+        del d1
     if comm.rank == 0:
         out = {
             "metric": METRIC,
@@ -258,6 +287,7 @@ def main() -> None:
                     "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
             "gpu_launches": launches_per_step * args.steps,
             "gen_hash_row0": F.gen_hash(row0),
+            "batch1_decode": batch1,
             "occupancy_min_rows": {k: min(v) for k, v in occupancy.items() if v},
         }
         print(json.dumps(out))
