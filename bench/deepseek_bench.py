@@ -12,6 +12,7 @@ import argparse
 import json
 import os
 import sys
+import time
 
 import torch
 
@@ -41,6 +42,8 @@ def main():
     ap.add_argument("--batch", type=int, nargs="+", default=[1, 32])
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (marked in the output)")
+    ap.add_argument("--fp8", action="store_true", help="dense projections and LM head as 128x128 block-scaled E4M3")
+    ap.add_argument("--skip-prefill", action="store_true")
     args = ap.parse_args()
     comm = init_distributed("nccl", timeout_s=600)
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -49,21 +52,33 @@ def main():
         cfg = cfg.scaled(num_layers=args.layers)
     S = args.prompt_len
     cfg = cfg.scaled(max_seq_len=S + 64)
+    t_start = time.perf_counter()
+
+    def note(msg):
+        if comm.rank == 0:
+            print(f"[deepseek_bench +{time.perf_counter() - t_start:.1f}s] {msg}", file=sys.stderr, flush=True)
+
     model = DeepSeekV4Model(cfg, comm, dev).init_random_local(0)
+    if args.fp8:
+        model.quantize_fp8()
     torch.cuda.synchronize()
+    note("weights ready")
     res = {"model": cfg.name + (f"-{args.layers}L (debug)" if args.layers else ""), "n_gpus": comm.size,
-           "parallelism": f"tp{comm.size}+ep{comm.size}", "dtype": "bf16",
+           "parallelism": f"tp{comm.size}+ep{comm.size}",
+           "dtype": "bf16 activations, fp8 dense weights" if args.fp8 else "bf16",
            "data": "synthetic (uniform-random prompt ids, random-init weights)",
            "weights_gb_per_gpu": round(sum(v.numel() * v.element_size() for L in model.L for v in L.values()
                                            if torch.is_tensor(v)) / 1e9, 1)}
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (1, S), generator=g).to(dev)
-    st = model.new_state(1, S + 64)
-    model.prefill(prompt[:, :128], st)  # warm-up
-    st = model.new_state(1, S + 64)
-    res["prefill_ttft_ms"] = round(ev_ms(lambda: model.prefill(prompt, st), comm), 1)
-    res["prefill_tok_s"] = round(S / res["prefill_ttft_ms"] * 1e3, 1)
-    check_status("prefill")
+    if not args.skip_prefill:
+        st = model.new_state(1, S + 64)
+        model.prefill(prompt[:, :128], st)  # warm-up
+        st = model.new_state(1, S + 64)
+        res["prefill_ttft_ms"] = round(ev_ms(lambda: model.prefill(prompt, st), comm), 1)
+        res["prefill_tok_s"] = round(S / res["prefill_ttft_ms"] * 1e3, 1)
+        check_status("prefill")
+        note("prefill done")
     for B in args.batch:
         st = model.new_state(B, S + args.steps * 4 + 64)
         st.positions.fill_(S)
@@ -98,6 +113,7 @@ def main():
         check_status("decode")
         res[f"decode_b{B}"] = {"ms_per_step": round(ms, 3), "tok_s": round(B / ms * 1e3, 1),
                                "graph": graph is not None}
+        note(f"decode batch {B} done")
         del graph
     if comm.rank == 0:
         print(json.dumps({"metric": "DeepSeek V4 Flash prefill TTFT + decode tok/s", **res}))

@@ -221,6 +221,22 @@ class DeepSeekV4Model:
         ck.close()
         return self
 
+    FP8_KEYS = ("wq_a", "wq_b", "wkv", "wo_b", "shared_gate_up", "shared_down")
+
+    def quantize_fp8(self, include_head: bool = True) -> "DeepSeekV4Model":
+        """Dense projections (and the LM head) as 128x128 block-scaled E4M3
+        (W8A16), the layout of the checkpoint's FP8 dense weights; routed experts
+        stay bf16 (grouped GEMM)."""
+        from ..io.fp8 import FP8Weight
+        for L in self.L:
+            for k in self.FP8_KEYS:
+                w = L.get(k)
+                if torch.is_tensor(w) and w.dim() == 2 and w.shape[1] % 16 == 0:
+                    L[k] = FP8Weight.from_dense(w)
+        if include_head:
+            self.g["head"] = FP8Weight.from_dense(self.g["head"])
+        return self
+
     def init_random_local(self, seed: int = 0) -> "DeepSeekV4Model":
         """Random-init only this rank's shards, directly on the device (full-size
         models: the whole synthetic state dict would not fit in host memory).
@@ -327,7 +343,7 @@ class DeepSeekV4Model:
         return O.rms_norm(y, self.g["norm"], cfg.norm_eps, one_plus=False)
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        return O.linear_f32(hidden, self.g["head"]) if hidden.is_cuda else hidden.float() @ self.g["head"].float().t()
+        return O.linear_f32(hidden, self.g["head"])
 
     def prefill(self, tokens: torch.Tensor, st: DeepSeekV4State) -> torch.Tensor:
         """``tokens [B, S]`` from position 0; returns next ids ``[B]``."""
