@@ -161,7 +161,7 @@ class GradReducer(_HookedReducer):
             b.mc = mc + offs[i]
             b.flags_local = ptrs[self.rank] + i * self.FLAG_BYTES
             b.peer_flags = [p + i * self.FLAG_BYTES for p in ptrs]
-            b.ticket = torch.zeros(1, dtype=torch.int32, device=dev)
+            b.ticket = torch.zeros(2, dtype=torch.int32, device=dev)  # CTA ticket, last wait's outcome
         self.steps = 0  # flags of step s reach s + 1
         self.hdl.barrier()
         torch.cuda.synchronize(dev)

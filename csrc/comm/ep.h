@@ -40,6 +40,7 @@ struct EpArgs {
   int* epoch_c;
   int* ticket_b;
   int* ticket_c;
+  int* ok;            // [3] outcome of the count / row / return waits (0 after a timeout)
   int* status;
   unsigned long long limit_ns;
 };

@@ -91,8 +91,15 @@ __global__ void __launch_bounds__(256) ep_count_kernel(EpArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) publish(a, kEpFlagA, a.epoch_a);
   __syncthreads();
-  wait_lane(a.flags + kEpFlagA, W, (unsigned)(*a.epoch_a), a.status, a.limit_ns);
-  __syncthreads();
+  const bool ok = __syncthreads_and(wait_lane(a.flags + kEpFlagA, W, (unsigned)(*a.epoch_a), a.status, a.limit_ns));
+  if (threadIdx.x == 0) a.ok[0] = ok ? 1 : 0;
+  if (!ok) {  // a rank never published its counts: receive nothing, send nothing
+    for (int e = threadIdx.x; e <= El; e += blockDim.x) {
+      if (e < El) a.recv_counts[e] = 0;
+      a.recv_offsets[e] = 0;
+    }
+    return;
+  }
   // receive counts / offsets of this rank's experts (expert-major rows):
   // per-expert sums in parallel, then one scan out of shared memory
   int* s_rc = s_cnt;  // reuse: [E_l]
@@ -117,6 +124,7 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpArgs a) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ int s_off[];  // [W * E_l] base offset of this rank's rows in (dst, e); then [W * E_l] totals
+  if (!a.ok[0]) return;  // the count exchange timed out: no peer stores
   const int W = a.world, El = a.e_local, H = a.H;
   int* s_tot = s_off + W * El;
   for (int i = threadIdx.x; i < W * El; i += blockDim.x) {
@@ -165,15 +173,17 @@ __global__ void __launch_bounds__(256) ep_send_kernel(EpArgs a) {
   grid_publish(a, a.ticket_b, kEpFlagB, a.epoch_b);
 }
 
-__global__ void __launch_bounds__(64) ep_wait_kernel(EpArgs a, int flag_off, const int* epoch) {
+__global__ void __launch_bounds__(64) ep_wait_kernel(EpArgs a, int flag_off, const int* epoch, int which) {
   pdl_trigger();
   pdl_wait();
-  wait_lane(a.flags + flag_off, a.world, (unsigned)(*epoch), a.status, a.limit_ns);
+  const bool ok = __syncthreads_and(wait_lane(a.flags + flag_off, a.world, (unsigned)(*epoch), a.status, a.limit_ns));
+  if (threadIdx.x == 0) a.ok[1 + which] = ok ? 1 : 0;
 }
 
 __global__ void __launch_bounds__(256) ep_return_kernel(EpArgs a) {
   pdl_trigger();
   pdl_wait();
+  if (!a.ok[1]) return;  // rows did not all arrive: return nothing
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int rows = a.recv_offsets[a.e_local];
   const int H = a.H;
@@ -208,7 +218,8 @@ void ep_send(const EpArgs& a, cudaStream_t st) {
 
 void ep_wait(const EpArgs& a, int which, cudaStream_t st) {
   const int off = which == 0 ? kEpFlagB : kEpFlagC;
-  launch_k(ep_wait_kernel, dim3(1), dim3(64), 0, st, a, off, which == 0 ? (const int*)a.epoch_b : (const int*)a.epoch_c);
+  launch_k(ep_wait_kernel, dim3(1), dim3(64), 0, st, a, off, which == 0 ? (const int*)a.epoch_b : (const int*)a.epoch_c,
+           which);
 }
 
 void ep_return(const EpArgs& a, cudaStream_t st) {

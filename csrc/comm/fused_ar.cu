@@ -101,8 +101,10 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(const __nv_bfloat16* m
   pdl_wait();
   const int row = blockIdx.x;
   __shared__ float red[8];
-  wait_flag_lane(flags, world, (unsigned)(*epoch), status, limit_ns);
-  __syncthreads();
+  const bool arrived = wait_flag_lane(flags, world, (unsigned)(*epoch), status, limit_ns);
+  // a peer that never signalled: its partial may not exist, so nothing is read
+  // or written (the status word carries the timeout to the host)
+  if (!__syncthreads_and(arrived)) return;
   const __nv_bfloat16* buf = mc_base + (long)((*sel) & 1) * buf_stride + (long)row * cols;
   constexpr int kMaxVec = 4;  // 8 columns per vector, 256 threads: cols <= 8192
   float v[kMaxVec][8];
@@ -174,8 +176,8 @@ __global__ void __launch_bounds__(256) sp_norm_gather_kernel(SpNormArgs a) {
   const int cols = a.cols;
   const long grow = (long)a.rank * a.rows + i;
   __shared__ float red[8];
-  if (a.mc_partial) wait_flag_lane(a.flags, a.world, (unsigned)(*a.epoch), a.status, a.limit_ns);
-  __syncthreads();
+  const bool arrived = !a.mc_partial || wait_flag_lane(a.flags, a.world, (unsigned)(*a.epoch), a.status, a.limit_ns);
+  if (!__syncthreads_and(arrived)) return;  // timed out: read and write nothing
   constexpr int kMaxVec = 4;
   float v[kMaxVec][8];
 #pragma unroll

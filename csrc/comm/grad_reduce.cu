@@ -26,20 +26,23 @@ namespace bwn {
 
 namespace {
 
-__device__ __forceinline__ void wait_all(const unsigned* flags, int world, unsigned epoch, int* status,
+// true when every rank's flag reached `epoch` within the limit
+__device__ __forceinline__ bool wait_all(const unsigned* flags, int world, unsigned epoch, int* status,
                                          uint64_t limit_ns) {
   const int r = threadIdx.x;
+  bool ok = true;
   if (r < world) {
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
     while ((int)(ld_acquire_sys(flags + r) - epoch) < 0) {
       if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) {
         set_status(status, kStatusPeerTimeout);
+        ok = false;
         break;
       }
     }
   }
-  __syncthreads();
+  return __syncthreads_and(ok);
 }
 
 __device__ __forceinline__ void grid_signal(const GradBucketArgs& a, int* ticket, int flag_slot) {
@@ -75,14 +78,18 @@ __global__ void __launch_bounds__(256) grad_pack_kernel(GradBucketArgs a) {
   grid_signal(a, a.ticket, 0);
 }
 
-// One CTA waits for a phase of every rank.  The kernels that follow are
-// launched without programmatic overlap, so no CTA of theirs holds an SM while
-// the peers are still behind (backward keeps running on the main stream).
+// One CTA waits for a phase of every rank and records the outcome in
+// ticket[1]; the kernels that follow are launched without programmatic
+// overlap, so no CTA of theirs holds an SM while the peers are still behind
+// (backward keeps running on the main stream), and after a timeout they touch
+// no peer memory.
 __global__ void __launch_bounds__(32) grad_wait_kernel(GradBucketArgs a, int slot) {
-  wait_all(a.flags + slot, a.world, a.epoch, a.status, a.limit_ns);
+  const bool ok = wait_all(a.flags + slot, a.world, a.epoch, a.status, a.limit_ns);
+  if (threadIdx.x == 0) a.ticket[1] = ok ? 1 : 0;
 }
 
 __global__ void __launch_bounds__(256) grad_rs_ag_kernel(GradBucketArgs a) {
+  if (!a.ticket[1]) return;
   const long slice = a.n / a.world;  // multiple of 8
   const long base = (long)a.rank * slice;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < slice / 8; i += (long)gridDim.x * blockDim.x) {
@@ -94,6 +101,7 @@ __global__ void __launch_bounds__(256) grad_rs_ag_kernel(GradBucketArgs a) {
 }
 
 __global__ void __launch_bounds__(256) grad_unpack_kernel(GradBucketArgs a) {
+  if (!a.ticket[1]) return;
   const long n8 = a.n / 8;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
     const uint4 v = __ldcg(reinterpret_cast<const uint4*>(a.local) + i);

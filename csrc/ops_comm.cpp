@@ -163,7 +163,8 @@ std::vector<int64_t> ep_layout_op(int64_t world, int64_t e_local, int64_t H, int
   return ep_layout(world, e_local, H, k, T_max, max_recv);
 }
 
-// ep_state int32 layout: [0..15] epochs/tickets, then recv counts [E_l], recv offsets [E_l+1], send slots [W*E_l]
+// ep_state int32 layout: [0..2] epochs, [3..4] tickets, [5..7] wait outcomes, then recv counts [E_l],
+// recv offsets [E_l+1], send slots [W*E_l]
 static EpArgs make_ep(const std::vector<int64_t>& peer_base, int64_t rank, int64_t e_local, int64_t H, int64_t k,
                       int64_t T_max, int64_t max_recv, const Tensor& state, double timeout_s) {
   const int W = (int)peer_base.size();
@@ -197,6 +198,7 @@ static EpArgs make_ep(const std::vector<int64_t>& peer_base, int64_t rank, int64
   a.epoch_c = s + 2;
   a.ticket_b = s + 3;
   a.ticket_c = s + 4;
+  a.ok = s + 5;  // [5..7]
   a.recv_counts = s + 16;
   a.recv_offsets = s + 16 + e_local;
   a.send_ctr = s + 16 + 2 * e_local + 1;
@@ -322,7 +324,7 @@ static GradBucketArgs make_grad(const Tensor& grad, int64_t local, int64_t mc, i
                                 const std::vector<int64_t>& peer_flags, int64_t rank, int64_t epoch,
                                 const Tensor& ticket, double timeout_s) {
   TORCH_CHECK(grad.is_cuda() && grad.scalar_type() == at::kFloat && grad.is_contiguous(), "grad: fp32 contiguous");
-  TORCH_CHECK(ticket.scalar_type() == at::kInt && ticket.numel() >= 1, "ticket int32");
+  TORCH_CHECK(ticket.scalar_type() == at::kInt && ticket.numel() >= 2, "ticket int32[2]: CTA ticket, wait outcome");
   TORCH_CHECK(peer_flags.size() >= 1 && peer_flags.size() <= 8, "1..8 ranks");
   GradBucketArgs a{};
   a.world = (int)peer_flags.size();
