@@ -130,8 +130,9 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, offset: int = 0) -> torch.
 
 
 def argmax_packed(logits: torch.Tensor, id_offset: int = 0) -> torch.Tensor:
-    """Per row int64 key ``(orderable(max) << 32) | (2^32-1 - id)``: an int64 max
-    over shards selects the largest logit and, on ties, the lowest global id."""
+    """Per row int64 key ``((orderable(max) ^ 2^31) << 32) | (2^32-1 - id)``: a
+    signed int64 max over shards (NCCL MAX all-reduce, the fused greedy) selects
+    the largest logit and, on ties, the lowest global id."""
     if logits.is_cuda:
         return ops().argmax_packed(logits, id_offset)
     lf = logits.float()
@@ -141,7 +142,8 @@ def argmax_packed(logits: torch.Tensor, id_offset: int = 0) -> torch.Tensor:
     u = m.view(torch.int32).long() & 0xFFFFFFFF
     neg = (u & 0x80000000) != 0
     ordv = torch.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
-    return (ordv << 32) | (0xFFFFFFFF - first)
+    hi = (ordv ^ 0x80000000) - ((ordv ^ 0x80000000) >= 0x80000000).long() * (1 << 32)  # as signed 32-bit
+    return (hi << 32) | (0xFFFFFFFF - first)
 
 
 def unpack_argmax(packed: torch.Tensor) -> torch.Tensor:

@@ -22,6 +22,8 @@
 // same launches; a slot is rewritten only after every rank has passed the next
 // flag barrier, i.e. after every rank finished reading it.  Every wait gives up
 // after a bounded time and sets a status bit instead of hanging the GPU.
+#include <climits>
+
 #include "comm/fused.h"
 #include "common/host.h"
 #include "common/launch.cuh"
@@ -284,11 +286,11 @@ __global__ void greedy_allmax_kernel(GreedyArgs a) {
   __syncthreads();
   const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(peer_slots[rank]);
   for (int i = threadIdx.x; i < rows; i += blockDim.x) {
-    unsigned long long best = 0;
+    long long best = LLONG_MIN;  // keys order as signed int64 (argmax_packed)
     for (int r = 0; r < world; ++r) {
       unsigned long long k;
       asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(mine + (long)r * rows + i) : "memory");
-      best = k > best ? k : best;
+      best = (long long)k > best ? (long long)k : best;
     }
     ids_out[i] = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
   }

@@ -177,7 +177,9 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logi
   if (threadIdx.x == 0) {
     for (int i = 1; i < (int)(blockDim.x >> 5); ++i) best = red[i] > best ? red[i] : best;
     best = red[0] > best ? red[0] : best;
-    out[row] = (int64_t)best;
+    // stored with the top bit flipped: a signed int64 max over shards (NCCL MAX
+    // all-reduce, the fused greedy) then orders keys as the unsigned max does
+    out[row] = (int64_t)(best ^ 0x8000000000000000ull);
   }
 }
 
