@@ -22,7 +22,8 @@ DEFAULT_SEQUENCES = [
 
 def tokenize(seqs: list[str], cfg: ESM2Config, max_len: int | None = None):
     """ESM alphabet ids with ``<cls>``/``<eos>``, right-padded with ``<pad>``;
-    ``<mask>`` in a sequence string is one token."""
+    ``<mask>`` in a sequence string is one token, letters outside the alphabet
+    are ``<unk>`` (as the HF ESM tokenizer maps them)."""
     idx = {t: i for i, t in enumerate(ESM_ALPHABET)}
     rows = []
     for s in seqs:
@@ -32,7 +33,7 @@ def tokenize(seqs: list[str], cfg: ESM2Config, max_len: int | None = None):
                 toks.append(cfg.mask_token_id)
                 i += 6
             else:
-                toks.append(idx.get(s[i], idx.get("X", cfg.pad_token_id)))
+                toks.append(idx.get(s[i], idx["<unk>"]))
                 i += 1
         toks.append(cfg.eos_token_id)
         rows.append(toks)

@@ -1,7 +1,8 @@
 """ESM-2 masked-language-model fine-tuning (``contrib/esm2/train_esm.py``).
 
-* synthetic protein batches (uniform over the 20 standard amino acids, with
-  ``<cls>``/``<eos>``), BERT masking 15% with the 80/10/10 mask/random/keep split
+* FASTA data with a held-out eval split (:mod:`bwn.train.esm_data`) or
+  synthetic protein batches (uniform over the 20 standard amino acids, with
+  ``<cls>``/``<eos>``); BERT masking 15% with the 80/10/10 mask/random/keep split
   (``mask_tokens``, ``train_esm.py:93-116``);
 * AdamW (wd 0.01) on fp32 master weights, bf16 GEMMs, cosine LR with warmup
   (``get_cosine_schedule_with_warmup``, ``:136-143``);
@@ -10,7 +11,12 @@
 * data parallelism: gradients averaged across ranks (NCCL baseline, or the
   fused NVLink reduce of :mod:`bwn.parallel.grad_reduce`);
 * checkpoint / resume of model, optimizer, schedule, step and RNG
-  (``save_checkpoint`` / ``load_checkpoint``, ``:148-178``).
+  (``save_checkpoint`` / ``load_checkpoint``, ``:148-178``);
+* :func:`main`: the training command (``run_training`` ``:250-370``):
+  periodic evaluation with perplexity, periodic and final checkpoints, resume.
+
+    python -m bwn.train.esm_mlm --model-size 8M --fasta seqs.fasta --num-steps 100
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m bwn.train.esm_mlm --model-size 15B --parallel tp
 """
 from __future__ import annotations
 
@@ -72,11 +78,18 @@ def cosine_with_warmup(step: int, warmup: int, total: int) -> float:
 
 
 class MLMTrainer:
-    def __init__(self, model: EsmForMaskedLM, tcfg: MLMConfig, comm=None, grad_reducer=None):
+    """One optimizer step per :meth:`step`.  ``data`` / ``eval_data``
+    (:class:`~bwn.train.esm_data.SequenceBatches`) supply real sequences;
+    without them the batches are synthetic."""
+
+    def __init__(self, model: EsmForMaskedLM, tcfg: MLMConfig, comm=None, grad_reducer=None, data=None,
+                 eval_data=None):
         self.model = model
         self.cfg = tcfg
         self.comm = comm
         self.grad_reducer = grad_reducer
+        self.data = data
+        self.eval_data = eval_data
         self.step_idx = 0
         self.opt = torch.optim.AdamW(model.parameters(), lr=tcfg.lr, weight_decay=tcfg.weight_decay,
                                      betas=(0.9, 0.999), eps=1e-8)
@@ -86,7 +99,10 @@ class MLMTrainer:
 
     def next_batch(self):
         mcfg = self.model.cfg
-        ids, am = synthetic_batch(mcfg, self.cfg.batch, self.cfg.seq_len, self.gen)
+        if self.data is not None:
+            ids, am = self.data.sample()
+        else:
+            ids, am = synthetic_batch(mcfg, self.cfg.batch, self.cfg.seq_len, self.gen)
         ids, labels, lm = mask_tokens(ids, mcfg, self.gen, self.cfg.mask_prob)
         return ids, am, labels, lm
 
@@ -118,14 +134,23 @@ class MLMTrainer:
 
     @torch.no_grad()
     def evaluate(self, batches: int = 2) -> dict:
+        """Mean masked-LM loss and perplexity over the held-out sequences (in
+        order, fixed masking seed) or ``batches`` synthetic batches."""
         gen = torch.Generator().manual_seed(12345)
         dev = next(self.model.parameters()).device
-        tot = 0.0
-        for _ in range(batches):
-            ids, am = synthetic_batch(self.model.cfg, self.cfg.batch, self.cfg.seq_len, gen)
+        if self.eval_data is not None:
+            src = self.eval_data.sequential()
+        else:
+            src = (synthetic_batch(self.model.cfg, self.cfg.batch, self.cfg.seq_len, gen) for _ in range(batches))
+        was_training = self.model.training
+        self.model.eval()
+        tot, n = 0.0, 0
+        for ids, am in src:
             ids, labels, lm = mask_tokens(ids, self.model.cfg, gen, self.cfg.mask_prob)
             tot += float(self.loss(ids.to(dev), am.to(dev), labels.to(dev), lm.to(dev)))
-        loss = tot / batches
+            n += 1
+        self.model.train(was_training)
+        loss = tot / max(1, n)
         return {"loss": loss, "perplexity": math.exp(min(loss, 50.0))}
 
     # ------------------------------------------------------------ checkpoint
@@ -137,6 +162,7 @@ class MLMTrainer:
             "step": self.step_idx,
             "rng": self.gen.get_state(),
             "torch_rng": torch.get_rng_state(),
+            "data": self.data.state_dict() if self.data is not None else None,
             "config": asdict(self.cfg),
         }
 
@@ -155,7 +181,114 @@ class MLMTrainer:
         self.step_idx = ck["step"]
         self.gen.set_state(ck["rng"])
         torch.set_rng_state(ck["torch_rng"])
+        if self.data is not None and ck.get("data") is not None:
+            self.data.load_state_dict(ck["data"])
 
 
 def build_esm(size: str = "8M", device="cpu", seed: int = 0) -> EsmForMaskedLM:
     return EsmForMaskedLM(ESM2_SIZES[size]).init_weights(seed).to(device)
+
+
+def _checkpoint_path(ck_dir: str, rank: int, sharded: bool) -> str:
+    """``checkpoint.pt`` (replicated weights, rank 0 writes) or one file per
+    rank when the weights are tensor-parallel shards."""
+    return os.path.join(ck_dir, f"checkpoint_rank{rank}.pt" if sharded else "checkpoint.pt")
+
+
+def main(argv=None):
+    import argparse
+    import json
+    import time
+
+    from ..parallel.comm import init_distributed
+    from .esm_data import SequenceBatches, load_fasta, split_dataset
+    from .esm_infer import DEFAULT_SEQUENCES
+
+    ap = argparse.ArgumentParser(description="ESM-2 masked-LM fine-tuning")
+    ap.add_argument("--model-size", default="8M", choices=sorted(ESM2_SIZES))
+    ap.add_argument("--max-seq-len", type=int, default=128, help="tokens per sequence incl. <cls>/<eos>")
+    ap.add_argument("--batch-size", type=int, default=4, help="sequences per data-parallel rank")
+    ap.add_argument("--num-steps", type=int, default=100)
+    ap.add_argument("--lr", type=float, default=5e-5)
+    ap.add_argument("--warmup-steps", type=int, default=10)
+    ap.add_argument("--fasta", default=None, help="FASTA file (train/eval split automatically)")
+    ap.add_argument("--eval-fraction", type=float, default=0.1)
+    ap.add_argument("--eval-every", type=int, default=25, help="0 disables")
+    ap.add_argument("--save-every", type=int, default=50, help="0 disables")
+    ap.add_argument("--checkpoint-dir", default="./checkpoints")
+    ap.add_argument("--resume", default=None, help="checkpoint directory to resume from")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "tp"],
+                    help="auto: tensor-parallel for 3B/15B, data-parallel otherwise")
+    ap.add_argument("--reducer", default="nccl", choices=["nccl", "fused"], help="data-parallel gradient reduction")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu", action="store_true")
+    a = ap.parse_args(argv)
+
+    comm = init_distributed("gloo" if a.cpu or not torch.cuda.is_available() else None)
+    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() and not a.cpu \
+        else torch.device("cpu")
+    mode = a.parallel if a.parallel != "auto" else ("tp" if a.model_size in ("3B", "15B") else "dp")
+    tp = comm.size > 1 and mode == "tp"
+    model = build_esm(a.model_size, device=dev, seed=a.seed)
+    reducer = None
+    if tp:
+        from ..parallel.tensor_parallel import apply_esm_tp
+        model = apply_esm_tp(model, comm)
+    elif comm.size > 1 and a.reducer == "fused":
+        from ..parallel.grad_reduce import GradReducer
+        reducer = GradReducer(model, comm, bucket_mb=64)
+    seqs = load_fasta(a.fasta) if a.fasta else list(DEFAULT_SEQUENCES)
+    train, held = split_dataset(seqs, a.eval_fraction)
+    mcfg = model.cfg
+    # tensor-parallel ranks must see the same batch; data-parallel ranks draw their own
+    data_seed = a.seed if tp else a.seed + comm.rank
+    data = SequenceBatches(train, mcfg, a.batch_size, a.max_seq_len, seed=data_seed)
+    eval_data = SequenceBatches(held, mcfg, a.batch_size, a.max_seq_len)
+    tcfg = MLMConfig(model=a.model_size, batch=a.batch_size, seq_len=a.max_seq_len - 2, lr=a.lr,
+                     warmup=a.warmup_steps, total_steps=a.num_steps, seed=a.seed)
+    trainer = MLMTrainer(model, tcfg, None if tp else comm, grad_reducer=reducer, data=data, eval_data=eval_data)
+    if tp:
+        trainer.gen.manual_seed(a.seed)  # identical masking on every tensor-parallel rank
+    log = (lambda **kv: print(json.dumps(kv), flush=True)) if comm.rank == 0 else (lambda **kv: None)
+    if a.resume:
+        path = _checkpoint_path(a.resume, comm.rank, tp)
+        if os.path.exists(path):
+            trainer.load(path)
+            log(event="resumed", step=trainer.step_idx, path=path)
+        else:
+            log(event="no_checkpoint", path=path)
+    log(event="start", model=a.model_size, parallel=f"tp{comm.size}" if tp else f"dp{comm.size}",
+        train_sequences=len(train), eval_sequences=len(held), steps=a.num_steps, start=trainer.step_idx)
+
+    def save():
+        if tp or comm.rank == 0:
+            trainer.save(_checkpoint_path(a.checkpoint_dir, comm.rank, tp))
+
+    t0 = time.perf_counter()
+    start = trainer.step_idx
+    total = 0.0
+    for step in range(start, a.num_steps):
+        loss = float(trainer.step())
+        total += loss
+        if step % 5 == 0 or step == a.num_steps - 1:
+            log(event="step", step=step, loss=round(loss, 4), lr=trainer.sched.get_last_lr()[0],
+                elapsed_s=round(time.perf_counter() - t0, 2))
+        if a.eval_every > 0 and (step + 1) % a.eval_every == 0:
+            ev = trainer.evaluate()  # every rank: tensor-parallel forward passes are collective
+            log(event="eval", step=step + 1, **ev)
+        if a.save_every > 0 and (step + 1) % a.save_every == 0:
+            save()
+    dt = time.perf_counter() - t0
+    n = max(1, a.num_steps - start)
+    ev = trainer.evaluate()
+    save()
+    log(event="done", steps=n, seconds=round(dt, 2), avg_loss=round(total / n, 4),
+        samples_per_s=round(n * a.batch_size * (1 if tp else comm.size) / max(dt, 1e-9), 2), final_eval=ev)
+    if comm.size > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
