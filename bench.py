@@ -83,6 +83,8 @@ def main() -> None:
                     help="N>1: sequence-parallel prefill (reduce-scatter/all-gather fused into the GEMM path)")
     ap.add_argument("--ep-a2a", default="auto", choices=["auto", "on", "off"],
                     help="MoE models on N>1: expert-parallel NVLink all-to-all for steps with >=16 tokens per rank")
+    ap.add_argument("--moe-sharding", default="ep", choices=["ep", "tp"],
+                    help="MoE models on N>1: partition experts across ranks (ep) or slice every expert (tp)")
     ap.add_argument("--profile-steps", type=int, default=int(os.environ.get("BWN_PROFILE_STEPS", "0")),
                     help="run warm-up + N decode steps only (for a profiler), then exit")
     ap.add_argument("--metrics", default=os.environ.get("BWN_METRICS", ""), help="JSONL metrics file")
@@ -115,7 +117,7 @@ def main() -> None:
     B, S = args.batch, args.prompt_len
     max_seq = S + args.warmup + args.steps * 2 + 64
 
-    model = Qwen36Model(cfg, comm, dev).init_random(seed=0)
+    model = Qwen36Model(cfg, comm, dev, moe_sharding=args.moe_sharding).init_random(seed=0)
     if args.fp8:
         model.quantize_fp8()
         torch.cuda.empty_cache()
@@ -128,7 +130,7 @@ def main() -> None:
                 raise
             if comm.rank == 0:
                 print(f"[bench] fused NVLink comm unavailable, using NCCL: {e}", file=sys.stderr)
-    if cfg.is_moe and comm.size > 1 and args.ep_a2a != "off":
+    if cfg.is_moe and comm.size > 1 and args.ep_a2a != "off" and args.moe_sharding == "ep":
         try:
             from bwn.parallel.ep import enable_ep_all_to_all
             enable_ep_all_to_all(model, max_tokens_per_rank=max(16, B * S // comm.size), min_tokens_per_rank=16)

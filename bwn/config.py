@@ -167,7 +167,11 @@ class TPDims:
 
     Mirrors ``model_dims.tp_dims`` (``contrib/qwen3.6-35b-a3b/model_dims.py:99-127``):
     DeltaNet K/V heads and attention Q heads split evenly; KV heads are
-    replicated when ``tp > kv_heads``; experts are partitioned ``E/tp`` per rank.
+    replicated when ``tp > kv_heads``; experts are partitioned ``E/tp`` per rank
+    (``moe_sharding="ep"``), or every rank holds every expert with a ``1/tp``
+    slice of its intermediate width (``"tp"``, the reference's MOE_DECODE_TP,
+    ``static_decode_35b.py:746-768``: the routed work is balanced across ranks
+    whatever the routing).
     """
 
     tp: int
@@ -185,15 +189,25 @@ class TPDims:
     expert_offset: int
     vocab: int
     vocab_offset: int
+    moe_sharding: str = "ep"
+    moe_inter: int = 0  # intermediate width of each held expert
 
 
-def tp_dims(cfg: Qwen36Config, tp: int, rank: int = 0) -> TPDims:
+MOE_SHARDINGS = ("ep", "tp")
+
+
+def tp_dims(cfg: Qwen36Config, tp: int, rank: int = 0, moe_sharding: str = "ep") -> TPDims:
     if cfg.dn_k_heads % tp or cfg.dn_v_heads % tp:
         raise ValueError(f"DeltaNet heads ({cfg.dn_k_heads}/{cfg.dn_v_heads}) must divide tp={tp}")
     if cfg.q_heads % tp:
         raise ValueError(f"q_heads={cfg.q_heads} must divide tp={tp}")
-    if cfg.is_moe and cfg.num_experts % tp:
+    if moe_sharding not in MOE_SHARDINGS:
+        raise ValueError(f"moe_sharding={moe_sharding!r}: expected one of {MOE_SHARDINGS}")
+    expert_tp = cfg.is_moe and moe_sharding == "tp"
+    if cfg.is_moe and not expert_tp and cfg.num_experts % tp:
         raise ValueError(f"num_experts={cfg.num_experts} must divide tp={tp}")
+    if expert_tp and (cfg.moe_inter % tp or (cfg.moe_inter // tp) % 16):
+        raise ValueError(f"moe_inter={cfg.moe_inter} must split over tp={tp} into multiples of 16")
     if not cfg.is_moe and cfg.intermediate % tp:
         raise ValueError(f"intermediate={cfg.intermediate} must divide tp={tp}")
     if cfg.vocab % tp:
@@ -223,10 +237,12 @@ def tp_dims(cfg: Qwen36Config, tp: int, rank: int = 0) -> TPDims:
         kv_head_offset=kv_off,
         kv_replication=rep,
         intermediate=(cfg.intermediate // tp) if not cfg.is_moe else 0,
-        experts=(cfg.num_experts // tp) if cfg.is_moe else 0,
-        expert_offset=(rank * (cfg.num_experts // tp)) if cfg.is_moe else 0,
+        experts=(cfg.num_experts if expert_tp else cfg.num_experts // tp) if cfg.is_moe else 0,
+        expert_offset=(0 if expert_tp else rank * (cfg.num_experts // tp)) if cfg.is_moe else 0,
         vocab=cfg.vocab // tp,
         vocab_offset=rank * (cfg.vocab // tp),
+        moe_sharding=moe_sharding if cfg.is_moe else "ep",
+        moe_inter=(cfg.moe_inter // tp if expert_tp else cfg.moe_inter) if cfg.is_moe else 0,
     )
 
 

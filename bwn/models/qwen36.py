@@ -77,13 +77,17 @@ class SpecBuffers:
 class Qwen36Model(nn.Module):
     """Rank-local Qwen3.6 model.  Parameters hold this rank's shards only."""
 
-    def __init__(self, cfg: Qwen36Config, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16):
+    def __init__(self, cfg: Qwen36Config, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16,
+                 moe_sharding: str | None = None):
         super().__init__()
+        from ..utils import env
         self.cfg = cfg
         self.comm = comm or Comm.single()
         self.tp = self.comm.size
         self.rank = self.comm.rank
-        self.d = tp_dims(cfg, self.tp, self.rank)
+        self.moe_sharding = moe_sharding or env.get("BWN_MOE_SHARDING")
+        self.moe_shared_only = bool(env.get("BWN_MOE_SHARED_ONLY"))
+        self.d = tp_dims(cfg, self.tp, self.rank, self.moe_sharding)
         self.device = torch.device(device)
         self.dtype = dtype
         self.layers: list[dict[str, torch.Tensor]] = []
@@ -97,7 +101,7 @@ class Qwen36Model(nn.Module):
         cfg = self.cfg
         self.layers = []
         for i in range(cfg.num_layers):
-            t = W.fuse_layer(cfg, i, get, self.tp, self.rank, self.dtype)
+            t = W.fuse_layer(cfg, i, get, self.tp, self.rank, self.dtype, self.moe_sharding)
             self.layers.append({k: v.to(self.device) for k, v in t.items()})
         self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, get, self.tp, self.rank, self.dtype).items()}
         return self
@@ -109,7 +113,7 @@ class Qwen36Model(nn.Module):
         self.layers = []
         for i in range(cfg.num_layers):
             hf = W.synthetic_hf_layer(cfg, i, seed, gd)
-            t = W.fuse_layer(cfg, i, hf.__getitem__, self.tp, self.rank, self.dtype)
+            t = W.fuse_layer(cfg, i, hf.__getitem__, self.tp, self.rank, self.dtype, self.moe_sharding)
             self.layers.append({k: v.to(self.device) for k, v in t.items()})
             del hf
         glob = W.synthetic_hf_globals(cfg, seed, gd)
@@ -389,11 +393,14 @@ class Qwen36Model(nn.Module):
 
 
 def build_qwen36(cfg: Qwen36Config, comm: Comm | None = None, device="cpu", seed: int | None = 0,
-                 hf_state: dict | None = None, dtype=torch.bfloat16, checkpoint: str | None = None) -> Qwen36Model:
+                 hf_state: dict | None = None, dtype=torch.bfloat16, checkpoint: str | None = None,
+                 moe_sharding: str | None = None) -> Qwen36Model:
     """A rank's model from an in-memory HF state dict, a safetensors checkpoint
     directory (HF layout, packed or per-expert MoE, official FP8 dequantized) or
-    random init from ``seed``."""
-    m = Qwen36Model(cfg, comm, device, dtype)
+    random init from ``seed``.  ``moe_sharding``: ``"ep"`` (experts partitioned
+    across ranks) or ``"tp"`` (every expert sliced across ranks); default from
+    ``BWN_MOE_SHARDING``."""
+    m = Qwen36Model(cfg, comm, device, dtype, moe_sharding)
     if checkpoint is not None:
         from ..io.checkpoint import Checkpoint
         ck = Checkpoint(checkpoint)

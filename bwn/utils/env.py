@@ -34,6 +34,10 @@ FLAGS = {f.name: f for f in (
     Flag("BWN_WAIT_LIMIT_MS", int, 2000, "bound on every device-side wait before it reports a timeout"),
     Flag("BWN_GQA_TC", int, 1, "GQA decode on the tcgen05 kernel (0: CUDA-core kernel)", (0, 1)),
     Flag("BWN_GEMM_MAX_SPLITS", int, 16, "upper bound of the decode GEMMs' split-K factor (1..16)"),
+    Flag("BWN_MOE_SHARDING", str, "ep", "MoE expert layout across TP ranks: partition experts (ep) or slice each "
+         "expert's intermediate width (tp)", ("ep", "tp")),
+    Flag("BWN_MOE_SHARED_ONLY", int, 0, "cost probe: skip the routed experts, keep the shared expert (wrong results)",
+         (0, 1)),
 )}
 
 

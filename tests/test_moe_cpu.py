@@ -141,3 +141,52 @@ def test_swiglu_limit_clamps_both_halves():
     u = torch.tensor([7.0, -7.0])
     assert torch.allclose(out[0], F.silu(g) * u)
     assert torch.allclose(R.swiglu(gu), F.silu(gu[0, :2]) * gu[0, 2:])
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel_experts_sum_to_block(world):
+    """``moe_sharding="tp"``: every simulated rank holds all experts with a
+    ``1/world`` slice of their intermediate width; the partials sum to HF's block."""
+    from bwn.io import qwen36_weights as W
+    from bwn.models.moe import qwen_moe_forward
+    from bwn.models.qwen36 import Qwen36Model
+    from bwn.parallel.comm import Comm
+    cfg = replace(tiny_qwen36(moe=True), dn_k_heads=4, dn_v_heads=8, moe_inter=128, shared_inter=128)
+    blk = _hf_block(cfg, seed=2)
+    sd = _layer_state(blk, cfg)
+    x = torch.randn(5, cfg.hidden)
+    with torch.no_grad():
+        ref = blk(x[None])[0]
+    total = torch.zeros_like(ref)
+    for r in range(world):
+        m = Qwen36Model(cfg, Comm(None, r, world), "cpu", torch.float32, moe_sharding="tp")
+        L = W.fuse_layer(cfg, 0, W.hf_getter(sd), world, r, torch.float32, "tp")
+        assert m.d.expert_offset == 0 and L["experts_gate_up"].shape == (cfg.num_experts, 2 * 128 // world, cfg.hidden)
+        assert L["experts_down"].shape == (cfg.num_experts, cfg.hidden, 128 // world)
+        total += qwen_moe_forward(m, L, x).float()
+    assert torch.allclose(total, ref, atol=1e-5), (total - ref).abs().max()
+
+
+def test_tensor_parallel_experts_dims():
+    """Per-rank dims of the tensor-parallel expert layout and its checks."""
+    from bwn.config import tp_dims
+    cfg = tiny_qwen36(moe=True)
+    with pytest.raises(ValueError):
+        tp_dims(cfg, 8, 0, "tp")  # 64 / 8 = 8 columns: below a 16-row gate/up block
+    with pytest.raises(ValueError):
+        tp_dims(cfg, 2, 0, "xx")
+    d = tp_dims(cfg, 2, 1, "tp")
+    assert (d.experts, d.expert_offset, d.moe_inter) == (cfg.num_experts, 0, cfg.moe_inter // 2)
+
+
+def test_shared_only_probe(monkeypatch):
+    from bwn.models.moe import qwen_moe_forward
+    from bwn.models.qwen36 import build_qwen36
+    cfg = tiny_qwen36(moe=True)
+    monkeypatch.setenv("BWN_MOE_SHARED_ONLY", "1")
+    m = build_qwen36(cfg, seed=1, dtype=torch.float32)
+    x = torch.randn(3, cfg.hidden)
+    L = m.layers[0]
+    got = qwen_moe_forward(m, L, x)
+    sy = O.linear(O.linear_swiglu(x, L["shared_gate_up"]), L["shared_down"])
+    assert torch.allclose(got, torch.sigmoid(x @ L["shared_gate"].t()) * sy, atol=1e-6)

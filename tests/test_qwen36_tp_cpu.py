@@ -3,7 +3,8 @@ sharding math of ``tp_dims`` (DeltaNet and attention heads split, KV heads
 replicated when ``tp > kv_heads``, experts partitioned ``E/tp``), the
 row-parallel all-reduces, the vocab-sharded LM head and the int64-max greedy
 (the reference's ``model_dims.py:99-127`` plan and ``test_moe_decode_model_device.py``
-tier, run here as real ranks over gloo)."""
+tier, run here as real ranks over gloo); the MoE runs with experts
+partitioned across ranks and with every expert sliced across ranks."""
 import os
 import socket
 
@@ -21,7 +22,7 @@ def _port():
     return p
 
 
-def _rank(rank, world, port, moe, q):
+def _rank(rank, world, port, moe, sharding, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -33,7 +34,7 @@ def _rank(rank, world, port, moe, q):
         torch.set_num_threads(2)  # ranks share the host's cores
         cfg = replace(tiny_qwen36(moe=moe), dn_k_heads=4, dn_v_heads=8)  # DeltaNet heads split over 4
         comm = Comm(None, rank, world)
-        tp = build_qwen36(cfg, comm, seed=3, dtype=torch.float32)
+        tp = build_qwen36(cfg, comm, seed=3, dtype=torch.float32, moe_sharding=sharding)
         one = build_qwen36(cfg, Comm.single(), seed=3, dtype=torch.float32)
         B, S = 3, 9
         toks = torch.randint(0, cfg.vocab, (B, S), generator=torch.Generator().manual_seed(5))
@@ -55,12 +56,13 @@ def _rank(rank, world, port, moe, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,moe", [(2, False), (4, False), (2, True), (4, True)])
-def test_tp_ranks_match_single_rank(world, moe):
+@pytest.mark.parametrize("world,moe,sharding", [(2, False, "ep"), (4, False, "ep"), (2, True, "ep"), (4, True, "ep"),
+                                                (4, True, "tp")])
+def test_tp_ranks_match_single_rank(world, moe, sharding):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_rank, args=(r, world, port, moe, q)) for r in range(world)]
+    ps = [ctx.Process(target=_rank, args=(r, world, port, moe, sharding, q)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=240) for _ in range(world)]
