@@ -107,32 +107,18 @@ ESM_TP_PLAN = {
 }
 
 
-def _get(mod, path):
-    for p in path.split("."):
-        mod = getattr(mod, p)
-    return mod
-
-
-def _set(mod, path, new):
-    parts = path.split(".")
-    for p in parts[:-1]:
-        mod = getattr(mod, p)
-    setattr(mod, parts[-1], new)
-
-
 def apply_esm_tp(model, comm, plan: dict | None = None):
     """Shard every encoder layer of an :class:`~bwn.models.esm2.EsmForMaskedLM`
-    in place (embeddings, final norms and LM head stay replicated)."""
+    in place (embeddings, final norms and LM head stay replicated), through
+    :func:`bwn.parallel.plan.parallelize_module` with the reference's layer plan."""
     if comm.size <= 1:
         return model
-    plan = plan or ESM_TP_PLAN
+    from .plan import parallelize_module
     heads = model.cfg.heads
     if heads % comm.size:
         raise ValueError(f"{heads} heads do not split over {comm.size} ranks")
     for layer in model.esm.encoder.layer:
-        for path, kind in plan.items():
-            full = _get(layer, path)
-            _set(layer, path, ColumnParallelLinear(full, comm) if kind == "colwise" else RowParallelLinear(full, comm))
+        parallelize_module(layer, comm, plan or ESM_TP_PLAN)
         layer.attention.self.heads = heads // comm.size
     model.tp_comm = comm
     return model
