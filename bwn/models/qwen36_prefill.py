@@ -18,6 +18,23 @@ import torch
 from .. import ops as O
 
 
+def _trace_layer(model, mode: int, start: int, i: int, kind: str, x: torch.Tensor, state: torch.Tensor) -> None:
+    """Per-layer numeric trace of a prefill chunk (``BWN_PREFILL_TRACE``; the
+    reference's PREFILL_TRACE_LAYER / _FINITE, ``static_decode_35b.py:2457-2470``):
+    finiteness and max-abs of the residual stream and of the layer's carried
+    state, printed on rank 0; mode 2 also raises at the first non-finite layer."""
+    def stat(t):
+        f = t.float()
+        fin = torch.isfinite(f)
+        return bool(fin.all()), float(f[fin].abs().max()) if bool(fin.any()) else float("nan")
+    (xf, xm), (sf, sm) = stat(x), stat(state)
+    if model.rank == 0:
+        print(f"[prefill-trace] start={start} layer={i} type={kind} residual finite={xf} max={xm:.4e} "
+              f"state finite={sf} max={sm:.4e}", flush=True)
+    if mode >= 2 and not (xf and sf):
+        raise FloatingPointError(f"prefill: non-finite values after layer {i} ({kind}) at start={start}")
+
+
 def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, feat_layers=(), feats_out=None,
                    all_rows: bool = False) -> torch.Tensor:
     """Returns the final-normed hidden of each sequence's last valid row ``[B, H]``
@@ -35,6 +52,8 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
     x = O.embedding(tokens.reshape(T).int(), model.g["embed"], 0)  # [T, H]
     h = O.rms_norm(x, model.layers[0]["in_norm"], cfg.rms_eps)
     captured = {}
+    from ..utils import env
+    trace = env.get("BWN_PREFILL_TRACE")
     di = gi = 0
     for i in range(cfg.num_layers):
         L = model.layers[i]
@@ -65,6 +84,9 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
             h = model._row_parallel(act, L["down"], x, nxt)
         if feats_out is not None and i in feat_layers:
             captured[i] = x.clone()
+        if trace:
+            dn = cfg.layer_type(i) == "deltanet"
+            _trace_layer(model, trace, start, i, cfg.layer_type(i), x, st.ssm[di - 1] if dn else st.k_cache[gi - 1])
     if feats_out is not None:
         feats_out.extend(captured[i] for i in feat_layers)
     st.positions.add_(valid_len)

@@ -36,6 +36,8 @@ FLAGS = {f.name: f for f in (
     Flag("BWN_GEMM_MAX_SPLITS", int, 16, "upper bound of the decode GEMMs' split-K factor (1..16)"),
     Flag("BWN_MOE_SHARDING", str, "ep", "MoE expert layout across TP ranks: partition experts (ep) or slice each "
          "expert's intermediate width (tp)", ("ep", "tp")),
+    Flag("BWN_PREFILL_TRACE", int, 0, "per-layer finite / max-abs trace of prefill (1: print, 2: also raise at the "
+         "first non-finite layer)", (0, 1, 2)),
     Flag("BWN_MOE_SHARED_ONLY", int, 0, "cost probe: skip the routed experts, keep the shared expert (wrong results)",
          (0, 1)),
 )}

@@ -98,3 +98,18 @@ def test_global_logits_concatenates_vocab_shards():
     caps = [{"logits": torch.ones(2, 3)}, {"logits": torch.zeros(2, 3)}]
     assert D.global_logits(caps).shape == (2, 6)
     assert D.global_logits(caps, width=3).shape == (2, 3)
+
+
+def test_prefill_trace(monkeypatch, capsys):
+    cfg = tiny_qwen36()
+    m = build_qwen36(cfg, seed=4, dtype=torch.float32)
+    monkeypatch.setenv("BWN_PREFILL_TRACE", "1")
+    st = m.new_state(1, 32)
+    m.prefill_hidden(torch.randint(0, cfg.vocab, (1, 5)), st)
+    lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.startswith("[prefill-trace]")]
+    assert len(lines) == cfg.num_layers and all("finite=True" in ln for ln in lines)
+    assert f"layer=3 type={cfg.layer_type(3)}" in lines[3]
+    monkeypatch.setenv("BWN_PREFILL_TRACE", "2")
+    m.layers[1]["post_norm"][0] = float("nan")
+    with pytest.raises(FloatingPointError, match="layer 1"):
+        m.prefill_hidden(torch.randint(0, cfg.vocab, (1, 5)), m.new_state(1, 32))
