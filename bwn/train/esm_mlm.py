@@ -154,45 +154,81 @@ class MLMTrainer:
         return {"loss": loss, "perplexity": math.exp(min(loss, 50.0))}
 
     # ------------------------------------------------------------ checkpoint
+    def _job_comm(self):
+        """The job's ranks: the data-parallel group, or the tensor-parallel one."""
+        if self.comm is not None and self.comm.size > 1:
+            return self.comm
+        return getattr(self.model, "tp_comm", None)
+
     def state_dict(self) -> dict:
+        """Portable checkpoint (:mod:`bwn.train.esm_ckpt`): the unsharded model
+        and AdamW moments by parameter name, scheduler, step, and every rank's
+        generator states.  Collective on multi-rank jobs."""
+        from .esm_ckpt import full_state, gather_objects
+        msd, moments = full_state(self.model, self.opt, getattr(self.model, "tp_comm", None))
+        mine = {"gen": self.gen.get_state(), "data": self.data.state_dict() if self.data is not None else None}
         return {
-            "model": {k: v.detach().cpu() for k, v in self.model.state_dict().items()},
-            "optim": self.opt.state_dict(),
+            "format": CKPT_FORMAT,
+            "model": msd,
+            "moments": moments,
+            "optim_groups": [{k: v for k, v in g.items() if k != "params"} for g in self.opt.param_groups],
             "sched": self.sched.state_dict(),
             "step": self.step_idx,
-            "rng": self.gen.get_state(),
+            "rngs": gather_objects(mine, self._job_comm()),
+            # tensor-parallel ranks (and a single process) draw one shared sample stream
+            "shared_stream": self.comm is None or self.comm.size <= 1,
             "torch_rng": torch.get_rng_state(),
-            "data": self.data.state_dict() if self.data is not None else None,
             "config": asdict(self.cfg),
         }
 
     def save(self, path: str) -> None:
-        """Atomic save (write to a temp file, then rename)."""
+        """Every rank calls it; the job's rank 0 writes atomically (temp file, rename)."""
+        sd = self.state_dict()
+        jc = self._job_comm()
+        if jc is not None and jc.rank != 0:
+            return
         os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
         tmp = path + ".tmp"
-        torch.save(self.state_dict(), tmp)
+        torch.save(sd, tmp)
         os.replace(tmp, path)
 
     def load(self, path: str) -> None:
+        """Resume from a portable checkpoint at any tensor/data-parallel degree.
+        A shared sample stream (single process or tensor-parallel ranks)
+        continues on any number of tensor-parallel ranks; data-parallel ranks
+        continue their own streams at the saved world size; otherwise the
+        generators are re-seeded from (seed, rank, step)."""
+        from .esm_ckpt import load_full_state
         ck = torch.load(path, map_location="cpu", weights_only=False)
-        self.model.load_state_dict(ck["model"])
-        self.opt.load_state_dict(ck["optim"])
+        if ck.get("format") != CKPT_FORMAT:
+            raise ValueError(f"{path}: not a {CKPT_FORMAT} checkpoint")
+        load_full_state(self.model, self.opt, getattr(self.model, "tp_comm", None), ck["model"], ck["moments"])
+        for g, saved in zip(self.opt.param_groups, ck["optim_groups"]):
+            g.update(saved)
         self.sched.load_state_dict(ck["sched"])
         self.step_idx = ck["step"]
-        self.gen.set_state(ck["rng"])
         torch.set_rng_state(ck["torch_rng"])
-        if self.data is not None and ck.get("data") is not None:
-            self.data.load_state_dict(ck["data"])
+        jc = self._job_comm()
+        world, rank = (jc.size, jc.rank) if jc is not None else (1, 0)
+        rngs = ck["rngs"]
+        shared_now = self.comm is None or self.comm.size <= 1
+        mine = rngs[0] if (ck.get("shared_stream") and shared_now) else rngs[rank] if len(rngs) == world else None
+        if mine is not None:
+            self.gen.set_state(mine["gen"])
+            if self.data is not None and mine["data"] is not None:
+                self.data.load_state_dict(mine["data"])
+        else:
+            s = self.cfg.seed * 1_000_003 + self.step_idx
+            self.gen.manual_seed(s + (rank if self.comm is not None else 0))
+            if self.data is not None:
+                self.data.rng.seed(s + rank)
+
+
+CKPT_FORMAT = "bwn-esm-portable-1"
 
 
 def build_esm(size: str = "8M", device="cpu", seed: int = 0) -> EsmForMaskedLM:
     return EsmForMaskedLM(ESM2_SIZES[size]).init_weights(seed).to(device)
-
-
-def _checkpoint_path(ck_dir: str, rank: int, sharded: bool) -> str:
-    """``checkpoint.pt`` (replicated weights, rank 0 writes) or one file per
-    rank when the weights are tensor-parallel shards."""
-    return os.path.join(ck_dir, f"checkpoint_rank{rank}.pt" if sharded else "checkpoint.pt")
 
 
 def main(argv=None):
@@ -214,9 +250,13 @@ def main(argv=None):
     ap.add_argument("--fasta", default=None, help="FASTA file (train/eval split automatically)")
     ap.add_argument("--eval-fraction", type=float, default=0.1)
     ap.add_argument("--eval-every", type=int, default=25, help="0 disables")
+    ap.add_argument("--log-every", type=int, default=5)
     ap.add_argument("--save-every", type=int, default=50, help="0 disables")
     ap.add_argument("--checkpoint-dir", default="./checkpoints")
     ap.add_argument("--resume", default=None, help="checkpoint directory to resume from")
+    ap.add_argument("--stop-after", type=int, default=0,
+                    help="end this invocation after N steps with a checkpoint (a preempted job; the schedule "
+                         "still spans --num-steps); 0 runs to --num-steps")
     ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "tp"],
                     help="auto: tensor-parallel for 3B/15B, data-parallel otherwise")
     ap.add_argument("--reducer", default="nccl", choices=["nccl", "fused"], help="data-parallel gradient reduction")
@@ -251,7 +291,7 @@ def main(argv=None):
         trainer.gen.manual_seed(a.seed)  # identical masking on every tensor-parallel rank
     log = (lambda **kv: print(json.dumps(kv), flush=True)) if comm.rank == 0 else (lambda **kv: None)
     if a.resume:
-        path = _checkpoint_path(a.resume, comm.rank, tp)
+        path = os.path.join(a.resume, "checkpoint.pt")
         if os.path.exists(path):
             trainer.load(path)
             log(event="resumed", step=trainer.step_idx, path=path)
@@ -260,17 +300,17 @@ def main(argv=None):
     log(event="start", model=a.model_size, parallel=f"tp{comm.size}" if tp else f"dp{comm.size}",
         train_sequences=len(train), eval_sequences=len(held), steps=a.num_steps, start=trainer.step_idx)
 
-    def save():
-        if tp or comm.rank == 0:
-            trainer.save(_checkpoint_path(a.checkpoint_dir, comm.rank, tp))
+    def save():  # collective: shards are gathered, rank 0 writes
+        trainer.save(os.path.join(a.checkpoint_dir, "checkpoint.pt"))
 
     t0 = time.perf_counter()
     start = trainer.step_idx
+    end = min(a.num_steps, start + a.stop_after) if a.stop_after > 0 else a.num_steps
     total = 0.0
-    for step in range(start, a.num_steps):
+    for step in range(start, end):
         loss = float(trainer.step())
         total += loss
-        if step % 5 == 0 or step == a.num_steps - 1:
+        if step % max(1, a.log_every) == 0 or step == end - 1:
             log(event="step", step=step, loss=round(loss, 4), lr=trainer.sched.get_last_lr()[0],
                 elapsed_s=round(time.perf_counter() - t0, 2))
         if a.eval_every > 0 and (step + 1) % a.eval_every == 0:
@@ -279,7 +319,15 @@ def main(argv=None):
         if a.save_every > 0 and (step + 1) % a.save_every == 0:
             save()
     dt = time.perf_counter() - t0
-    n = max(1, a.num_steps - start)
+    n = max(1, end - start)
+    if end < a.num_steps:
+        save()
+        log(event="stopped", step=end, seconds=round(dt, 2))
+        if comm.size > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     ev = trainer.evaluate()
     save()
     log(event="done", steps=n, seconds=round(dt, 2), avg_loss=round(total / n, 4),

@@ -91,25 +91,76 @@ def test_training_command_evaluates_saves_and_resumes(tmp_path):
     assert sum(k == "eval" for k in kinds) == 2
     assert all(e["perplexity"] > 1.0 for e in ev if e["event"] == "eval")
     saved = torch.load(os.path.join(ck, "checkpoint.pt"), weights_only=False)
-    assert saved["step"] == 4 and saved["data"] is not None
+    assert saved["step"] == 4 and saved["rngs"][0]["data"] is not None
     ev2 = _run(base + ["--num-steps", "6", "--resume", ck])
     assert ev2[0]["event"] == "resumed" and ev2[0]["step"] == 4
     assert ev2[-1]["steps"] == 2
     assert torch.load(os.path.join(ck, "checkpoint.pt"), weights_only=False)["step"] == 6
 
 
-def test_training_command_two_ranks(tmp_path):
+def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
+    return port
+
+
+def _torchrun(n, port):
+    return [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", str(n),
+            "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "bwn.train.esm_mlm", "--cpu"]
+
+
+def test_training_command_two_ranks(tmp_path):
+    port = _free_port()
     for mode in ("dp", "tp"):
         ck = str(tmp_path / mode)
-        ev = _run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-                   "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "bwn.train.esm_mlm", "--cpu",
-                   "--model-size", "8M", "--max-seq-len", "32", "--batch-size", "2", "--num-steps", "3",
-                   "--eval-every", "0", "--save-every", "0", "--checkpoint-dir", ck, "--parallel", mode])
+        ev = _run(_torchrun(2, port) + ["--model-size", "8M", "--max-seq-len", "32", "--batch-size", "2",
+                                        "--num-steps", "3", "--eval-every", "0", "--save-every", "0",
+                                        "--checkpoint-dir", ck, "--parallel", mode])
         assert ev[0]["parallel"] == f"{mode}2"
         assert ev[-1]["event"] == "done"
-        files = sorted(os.listdir(ck))
-        assert files == (["checkpoint.pt"] if mode == "dp" else ["checkpoint_rank0.pt", "checkpoint_rank1.pt"])
+        assert sorted(os.listdir(ck)) == ["checkpoint.pt"]  # one portable file in both modes
+
+
+def _losses(events):
+    return {e["step"]: e["loss"] for e in events if e["event"] == "step"}
+
+
+def test_resume_continues_the_loss_trajectory(tmp_path):
+    """A run stopped after 3 steps and resumed in a new process reproduces the
+    uninterrupted run's losses exactly (same world size: model, AdamW moments,
+    schedule and every generator restored)."""
+    fasta = _fasta(tmp_path, 20)
+    base = [sys.executable, "-m", "bwn.train.esm_mlm", "--cpu", "--model-size", "8M", "--fasta", fasta,
+            "--max-seq-len", "40", "--batch-size", "2", "--eval-every", "0", "--log-every", "1",
+            "--warmup-steps", "2"]
+    full = _losses(_run(base + ["--num-steps", "6", "--save-every", "0", "--checkpoint-dir", str(tmp_path / "x")]))
+    ck = str(tmp_path / "ck")
+    first = _losses(_run(base + ["--num-steps", "6", "--stop-after", "3", "--save-every", "0", "--checkpoint-dir", ck]))
+    rest = _losses(_run(base + ["--num-steps", "6", "--save-every", "0", "--checkpoint-dir", ck, "--resume", ck]))
+    assert sorted(first) == [0, 1, 2] and sorted(rest) == [3, 4, 5]
+    assert {**first, **rest} == full
+
+
+def test_checkpoint_reshards_from_tp2_to_one_rank(tmp_path):
+    """Saved by two tensor-parallel ranks, resumed by a single process: the
+    losses continue the two-rank run's trajectory up to reduction-order rounding."""
+    common = ["--model-size", "8M", "--max-seq-len", "32", "--batch-size", "2", "--eval-every", "0",
+              "--log-every", "1", "--warmup-steps", "2"]
+    ref = _losses(_run(_torchrun(2, _free_port()) + common + ["--parallel", "tp", "--num-steps", "4",
+                                                            "--save-every", "0", "--checkpoint-dir",
+                                                            str(tmp_path / "r")]))
+    ck = str(tmp_path / "ck")
+    _run(_torchrun(2, _free_port()) + common + ["--parallel", "tp", "--num-steps", "4", "--stop-after", "2",
+                                              "--save-every", "0", "--checkpoint-dir", ck])
+    saved = torch.load(os.path.join(ck, "checkpoint.pt"), weights_only=False)
+    q = saved["model"]["esm.encoder.layer.0.attention.self.query.weight"]
+    assert q.shape == (CFG.hidden, CFG.hidden)  # stored unsharded
+    assert "esm.encoder.layer.0.attention.self.query.weight" in saved["moments"]
+    rest = _losses(_run([sys.executable, "-m", "bwn.train.esm_mlm", "--cpu"] + common +
+                        ["--parallel", "tp", "--num-steps", "4", "--save-every", "0", "--checkpoint-dir", ck,
+                         "--resume", ck]))
+    assert sorted(rest) == [2, 3]
+    for s in (2, 3):
+        assert abs(rest[s] - ref[s]) < 2e-3, (s, rest[s], ref[s])
