@@ -221,6 +221,10 @@ def main() -> None:
     e_ms = (time.perf_counter() - e0) * 1e3
     e_ms = comm.max_scalar(e_ms, dev)
     check_status("e2e")
+    from bwn.parallel.symm import check_canaries
+    bad = check_canaries()  # outside the timed regions
+    if bad:
+        raise RuntimeError(f"symmetric buffers written past their end: {bad}")
     # occupancy gates on every rank (a lost state write leaves a layer empty)
     occupancy = F.check_qwen36_state(dec.st, f"decode state rank={comm.rank}")
 

@@ -31,8 +31,6 @@ from ..ops import _ext
 class EPAllToAll:
     def __init__(self, comm, hidden: int, n_experts: int, top_k: int, max_tokens: int,
                  max_recv: int | None = None, device=None, timeout_s: float = 5.0):
-        import torch.distributed._symmetric_memory as symm
-
         self.comm = comm
         self.W, self.rank = comm.size, comm.rank
         if n_experts % self.W:
@@ -47,14 +45,8 @@ class EPAllToAll:
         C = _ext.require()
         self.off = list(C.ep_layout(self.W, self.e_local, hidden, top_k, self.T_max, self.max_recv))
         group = comm.group or dist.group.WORLD
-        try:
-            symm.enable_symm_mem_for_group(group.group_name)
-        except Exception:  # noqa: BLE001
-            pass
-        self.buf = symm.empty(self.off[5], dtype=torch.uint8, device=dev)
-        self.buf.zero_()
-        torch.cuda.synchronize(dev)
-        self.hdl = symm.rendezvous(self.buf, group)
+        from .symm import allocate
+        self.buf, self.hdl = allocate(self.off[5], group, dev, "ep_all_to_all")
         self.peer_base = [int(p) for p in self.hdl.buffer_ptrs]
         self.state = torch.zeros(16 + 2 * self.e_local + 1 + self.W * self.e_local, dtype=torch.int32, device=dev)
         self.recv_x = self.buf[self.off[3]:self.off[3] + self.max_recv * hidden * 2].view(torch.bfloat16).view(

@@ -31,8 +31,6 @@ class FusedComm:
     SLOTS = 256
 
     def __init__(self, comm, hidden: int, max_rows: int = 256, device=None, timeout_s: float = 5.0):
-        import torch.distributed._symmetric_memory as symm
-
         self.comm = comm
         self.world, self.rank = comm.size, comm.rank
         self.hidden = hidden
@@ -40,19 +38,12 @@ class FusedComm:
         self.timeout_s = timeout_s
         dev = device or torch.device("cuda", torch.cuda.current_device())
         group = comm.group or dist.group.WORLD
-        try:  # older torch releases want symmetric memory enabled per group first
-            symm.enable_symm_mem_for_group(group.group_name)
-        except Exception:  # noqa: BLE001
-            pass
         slots_bytes = 8 * max_rows * 8
         self.ar_off = ((self.SLOTS + slots_bytes + 255) // 256) * 256
         self.buf_elems = max_rows * hidden  # bf16 elements per slot (two slots)
         total = self.ar_off + 2 * self.buf_elems * 2
-        self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
-        self.buf.zero_()
-        torch.cuda.synchronize(dev)
-        self.hdl = symm.rendezvous(self.buf, group)
-        from .symm import multicast_address
+        from .symm import allocate, multicast_address
+        self.buf, self.hdl = allocate(total, group, dev, "fused_ar")
         mc = multicast_address(self.hdl)
         ptrs = [int(p) for p in self.hdl.buffer_ptrs]
         self.peer_flags_ar = [p + self.FLAGS_AR for p in ptrs]

@@ -132,29 +132,20 @@ class GradReducer(_HookedReducer):
     FLAG_BYTES = 256  # per bucket: 2 phases x 8 ranks x 4 bytes, padded
 
     def __init__(self, model, comm, bucket_mb: float = 32.0, timeout_s: float = 30.0):
-        import torch.distributed._symmetric_memory as symm
-
         super().__init__(model, comm, bucket_mb, align=8 * comm.size)
         self.timeout_s = timeout_s
         self.rank = comm.rank
         dev = self.buckets[0].flat.device
         group = comm.group or dist.group.WORLD
-        try:
-            symm.enable_symm_mem_for_group(group.group_name)
-        except Exception:  # noqa: BLE001
-            pass
         nb = len(self.buckets)
         data_off = (nb * self.FLAG_BYTES + 255) // 256 * 256
         offs, total = [], data_off
         for b in self.buckets:
             offs.append(total)
             total += (b.n * 2 + 255) // 256 * 256
-        self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
-        self.buf.zero_()
-        torch.cuda.synchronize(dev)
-        self.hdl = symm.rendezvous(self.buf, group)
+        from .symm import allocate, multicast_address
+        self.buf, self.hdl = allocate(total, group, dev, "grad_reduce")
         ptrs = [int(p) for p in self.hdl.buffer_ptrs]
-        from .symm import multicast_address
         mc = multicast_address(self.hdl)
         for i, b in enumerate(self.buckets):
             b.local = ptrs[self.rank] + offs[i]

@@ -28,8 +28,6 @@ class SeqParallel:
     FLAGS = 256  # partial flags at 0, gather flags at 128 (bytes)
 
     def __init__(self, comm, hidden: int, max_tokens: int, device=None, timeout_s: float = 10.0):
-        import torch.distributed._symmetric_memory as symm
-
         self.comm, self.W, self.rank = comm, comm.size, comm.rank
         self.H, self.T_max, self.timeout_s = hidden, max_tokens, timeout_s
         dev = device or torch.device("cuda", torch.cuda.current_device())
@@ -38,15 +36,8 @@ class SeqParallel:
         self.off_h = self.off_partial + 2 * self.buf_elems * 2
         total = self.off_h + self.buf_elems * 2
         group = comm.group or dist.group.WORLD
-        try:
-            symm.enable_symm_mem_for_group(group.group_name)
-        except Exception:  # noqa: BLE001
-            pass
-        self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
-        self.buf.zero_()
-        torch.cuda.synchronize(dev)
-        self.hdl = symm.rendezvous(self.buf, group)
-        from .symm import multicast_address
+        from .symm import allocate, multicast_address
+        self.buf, self.hdl = allocate(total, group, dev, "seq_parallel")
         mc = multicast_address(self.hdl)
         ptrs = [int(p) for p in self.hdl.buffer_ptrs]
         self.partial_flags = list(ptrs)

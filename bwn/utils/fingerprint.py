@@ -6,6 +6,11 @@
 * :func:`logits_fingerprint` -- sum, norm, top-5 and finiteness of prefill
   logits (``static_decode_35b.py:3222-3246``).
 * :func:`state_stats` -- sum / norm / non-zero count of carried state tensors.
+* :func:`snapshot_state` / :func:`assert_state_advanced`: every per-layer
+  state buffer must change on every decode step (each DeltaNet layer's
+  recurrent state and conv ring slot, each attention layer's K/V row at the
+  step's position) -- the static-buffer form of the reference's in-place
+  mutation lesson.
 * Guards (``static_decode_35b.py:549-659``): :func:`assert_disjoint` rejects two
   in-place-mutated buffers whose bytes overlap; :func:`assert_occupancy` rejects
   a per-layer state slice with no non-zero row after a step (a dropped write
@@ -92,3 +97,32 @@ def check_qwen36_state(st, what: str = "decode state", kv_rows_used: bool = True
         out["k"] = assert_occupancy(st.k_cache, what + " k_cache")
         out["v"] = assert_occupancy(st.v_cache, what + " v_cache")
     return out
+
+
+def snapshot_state(st) -> dict:
+    """Copies of the state slices one decode step must write (taken before the step)."""
+    pos = st.positions.long()
+    b = torch.arange(pos.shape[0], device=pos.device)
+    R = st.conv.shape[2]
+    return {"pos": pos.clone(), "ssm": st.ssm.clone(), "conv": st.conv[:, b, pos % R].clone(),
+            "k": st.k_cache[:, b, :, pos].clone(), "v": st.v_cache[:, b, :, pos].clone()}
+
+
+def assert_state_advanced(before: dict, st, what: str = "decode step") -> None:
+    """Postcondition of one decode step: the positions moved by one, and for
+    every sequence each DeltaNet layer's recurrent state and conv-ring slot and
+    each attention layer's K/V row at the step's position changed."""
+    pos = before["pos"]
+    if not torch.equal(st.positions.long(), pos + 1):
+        raise RuntimeError(f"{what}: positions did not advance by one")
+    b = torch.arange(pos.shape[0], device=pos.device)
+    R = st.conv.shape[2]
+    now = {"ssm": st.ssm, "conv": st.conv[:, b, pos % R], "k": st.k_cache[:, b, :, pos],
+           "v": st.v_cache[:, b, :, pos]}
+    for name, cur in now.items():
+        old = before[name]
+        # [L, B, ...]: per layer and sequence, did anything change
+        same = (cur == old).reshape(cur.shape[0], cur.shape[1], -1).all(-1)
+        if bool(same.any()):
+            lay, seq = [int(v) for v in same.nonzero()[0]]
+            raise RuntimeError(f"{what}: {name} of layer {lay} (sequence {seq}) was not written")

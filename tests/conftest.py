@@ -27,3 +27,14 @@ def pytest_collection_modifyitems(config, items):
 def _seed():
     torch.manual_seed(0)
     yield
+
+
+@pytest.fixture(autouse=True)
+def _symm_canaries(request):
+    """After a GPU test, no symmetric buffer may have been written past its end
+    (each one carries a guard tail; :mod:`bwn.parallel.symm`)."""
+    yield
+    mod = sys.modules.get("bwn.parallel.symm")
+    if mod is not None and "gpu" in request.keywords and torch.cuda.is_available():
+        bad = mod.check_canaries()
+        assert not bad, f"symmetric buffers written past their end: {bad}"

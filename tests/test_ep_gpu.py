@@ -78,6 +78,8 @@ def _worker(rank, world, port, q):
         ref = O.moe_experts(x, w, ids, gu, dn, 0)
         errs.append(float((out_g.float() - ref.float()).abs().max() / ref.float().abs().max()))
         del graph
+        from bwn.parallel.symm import check_canaries
+        assert not check_canaries(), "a symmetric buffer was written past its end"
         q.put((rank, errs))
         dist.barrier()
         dist.destroy_process_group()
@@ -133,6 +135,8 @@ def _model_worker(rank, world, port, q):
         torch.cuda.synchronize()
         check_status("ep model")
         rel = float((hs[0] - hs[1]).norm() / hs[0].norm())
+        from bwn.parallel.symm import check_canaries
+        assert not check_canaries(), "a symmetric buffer was written past its end"
         q.put((rank, rel))
         dist.barrier()
         dist.destroy_process_group()
@@ -199,6 +203,8 @@ def _sp_worker(rank, world, port, moe, q):
         d0 = ref.decode_step(t0, st0).float()
         d1 = m.decode_step(t0, st1).float()
         errs.append(float((d0 != d1).float().mean()))
+        from bwn.parallel.symm import check_canaries
+        assert not check_canaries(), "a symmetric buffer was written past its end"
         q.put((rank, errs))
         dist.barrier()
         dist.destroy_process_group()

@@ -54,6 +54,8 @@ def _worker(rank, world, port, q):
             num = max(float((a.grad - b.grad).abs().max()) for a, b in zip(ref.parameters(), dp.parameters()))
             den = max(float(a.grad.abs().max()) for a in ref.parameters())
             errs[name] = num / den
+        from bwn.parallel.symm import check_canaries
+        assert not check_canaries(), "a symmetric buffer was written past its end"
         q.put((rank, errs))
         dist.barrier()
         dist.destroy_process_group()

@@ -68,3 +68,19 @@ def test_graph_replay_equals_eager():
     # host API: H2D of the tokens, D2H of the ids
     out = d1.step(torch.tensor([7, 8], dtype=torch.int32))
     assert out.shape == (2,) and out.dtype == torch.int32
+
+
+def test_every_layer_state_changes_every_step_on_gpu():
+    """The kernels' decode step writes every per-layer state slice each step
+    (DeltaNet recurrent state and conv-ring slot, K/V row at the position)."""
+    from bwn.utils import fingerprint as F
+    cfg = tiny_qwen36()
+    m = build_qwen36(cfg, device="cuda", seed=5)
+    st = m.new_state(4, 32)
+    tok = torch.tensor([1, 5, 9, 11], dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        snap = F.snapshot_state(st)
+        tok = m.decode_step(tok, st).int()
+        torch.cuda.synchronize()
+        check_status("decode")
+        F.assert_state_advanced(snap, st)

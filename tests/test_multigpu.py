@@ -52,6 +52,8 @@ def _worker(rank, world, port, moe, q):
             torch.cuda.synchronize()
             check_status("tp decode")
             outs.append(torch.stack(ids, 1).cpu())
+        from bwn.parallel.symm import check_canaries
+        assert not check_canaries(), "a symmetric buffer was written past its end"
         q.put((rank, [o.tolist() for o in outs]))
         dist.barrier()
         dist.destroy_process_group()

@@ -92,3 +92,41 @@ def test_metrics_jsonl(tmp_path):
     recs = read_jsonl(p)
     assert [r["event"] for r in recs] == ["run", "decode_step"]
     assert recs[1]["ms"] == 1.25 and recs[1]["batch"] == 4 and recs[0]["model"] == "tiny"
+
+
+def test_symm_canary_registry_reports_a_changed_tail():
+    """The guard-tail registry without symmetric memory: a stand-in buffer
+    registered as an allocation is reported once its tail changes, and dropped
+    once it is freed."""
+    import weakref
+
+    from bwn.parallel import symm
+    full = torch.empty(100 + symm.CANARY_BYTES, dtype=torch.uint8)
+    full[:100].zero_()
+    full[100:].fill_(symm.CANARY)
+    symm._guarded.append((weakref.ref(full), 100, "standin"))
+    full[:100].fill_(7)  # writes inside the region are fine
+    assert "standin" not in symm.check_canaries()
+    full[100 + 5] = 0    # one byte past the end
+    assert "standin" in symm.check_canaries()
+    del full
+    assert "standin" not in symm.check_canaries()
+    assert all(name != "standin" for _, _, name in symm._guarded)
+
+
+def test_every_layer_state_changes_every_step():
+    from bwn.config import tiny_qwen36
+    from bwn.models.qwen36 import build_qwen36
+    from bwn.utils import fingerprint as F
+    cfg = tiny_qwen36()
+    m = build_qwen36(cfg, seed=2, dtype=torch.float32)
+    st = m.new_state(2, 16)
+    tok = torch.tensor([3, 7], dtype=torch.int32)
+    for _ in range(3):
+        snap = F.snapshot_state(st)
+        tok = m.decode_step(tok, st).int()
+        F.assert_state_advanced(snap, st)
+    snap = F.snapshot_state(st)
+    st.positions.add_(1)  # a step that wrote nothing
+    with pytest.raises(RuntimeError, match="was not written"):
+        F.assert_state_advanced(snap, st)
