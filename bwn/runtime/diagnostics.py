@@ -22,6 +22,7 @@ only when both runs see a near tie (``kernels/tests/test_decode_fullgraph_device
 * :func:`compare_captures` reports per-layer, per-tap cosine / relative L2 /
   max-abs and applies the logits and near-tie gates.
 
+    python -m bwn.runtime.diagnostics capture --model 35b --layers 0,3,39 --out RUN_A   # per rank (torchrun)
     python -m bwn.runtime.diagnostics compare RUN_A RUN_B
 """
 from __future__ import annotations
@@ -198,10 +199,51 @@ def compare_captures(ref: list[dict], cand: list[dict], cos_min: float = 0.999, 
             "first_diverging_tap": first_bad, "taps": taps}
 
 
+def capture_run(a) -> str:
+    """Build the model (random init from ``--seed``; one rank per process under
+    torchrun), prefill a seeded prompt, run one tapped decode step and save
+    this rank's capture."""
+    from ..config import QWEN36_27B, QWEN36_35B_A3B, tiny_qwen36
+    from ..models.qwen36 import build_qwen36
+    from ..parallel.comm import init_distributed
+    cpu = a.cpu or not torch.cuda.is_available()
+    comm = init_distributed("gloo" if cpu else "nccl")
+    dev = torch.device("cpu") if cpu else torch.device("cuda", torch.cuda.current_device())
+    cfg = {"27b": QWEN36_27B, "35b": QWEN36_35B_A3B, "tiny": tiny_qwen36(), "tiny-moe": tiny_qwen36(moe=True)}[a.model]
+    if a.layers_total:
+        cfg = cfg.scaled(num_layers=a.layers_total)
+    model = build_qwen36(cfg, comm, dev, seed=a.seed, dtype=torch.float32 if cpu else torch.bfloat16,
+                         moe_sharding=a.moe_sharding)
+    gen = torch.Generator().manual_seed(a.seed + 1)
+    prompt = torch.randint(0, cfg.vocab, (a.batch, a.prompt_len), generator=gen).to(dev)
+    st = model.new_state(a.batch, a.prompt_len + 8)
+    ids = model.greedy(model.prefill_hidden(prompt, st))
+    layers = [int(v) for v in a.layers.split(",")] if a.layers else None
+    cap = decode_diagnostics(model, ids.int(), st, layers)
+    meta = {"model": cfg.name, "world": comm.size, "rank": comm.rank, "seed": a.seed, "batch": a.batch,
+            "prompt_len": a.prompt_len, "moe_sharding": a.moe_sharding, "device": str(dev)}
+    path = save_capture(cap, a.out, comm.rank, meta)
+    if comm.size > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return path
+
+
 def main(argv=None):
     import argparse
-    ap = argparse.ArgumentParser(description="compare two runs' per-rank decode captures")
+    ap = argparse.ArgumentParser(description="per-rank decode captures and their comparison")
     sub = ap.add_subparsers(dest="cmd", required=True)
+    k = sub.add_parser("capture")
+    k.add_argument("--model", default="tiny", choices=["27b", "35b", "tiny", "tiny-moe"])
+    k.add_argument("--layers-total", type=int, default=0, help="truncate the model to this many layers")
+    k.add_argument("--layers", default="", help="comma-separated layers to tap (all when empty)")
+    k.add_argument("--batch", type=int, default=2)
+    k.add_argument("--prompt-len", type=int, default=16)
+    k.add_argument("--seed", type=int, default=0)
+    k.add_argument("--moe-sharding", default="ep", choices=["ep", "tp"])
+    k.add_argument("--cpu", action="store_true")
+    k.add_argument("--out", required=True)
     c = sub.add_parser("compare")
     c.add_argument("reference")
     c.add_argument("candidate")
@@ -210,6 +252,9 @@ def main(argv=None):
     c.add_argument("--tie-tol", type=float, default=0.125)
     c.add_argument("--report-only", action="store_true")
     a = ap.parse_args(argv)
+    if a.cmd == "capture":
+        print(json.dumps({"saved": capture_run(a)}))
+        return 0
     rep = compare_captures(load_captures(a.reference), load_captures(a.candidate), a.cos_min, a.rel_l2_max,
                            a.tie_tol)
     print(json.dumps({k: v for k, v in rep.items() if k != "taps"}))

@@ -113,3 +113,32 @@ def test_prefill_trace(monkeypatch, capsys):
     m.layers[1]["post_norm"][0] = float("nan")
     with pytest.raises(FloatingPointError, match="layer 1"):
         m.prefill_hidden(torch.randint(0, cfg.vocab, (1, 5)), m.new_state(1, 32))
+
+
+def test_capture_command_tp2_against_single_rank(tmp_path):
+    """Captures taken by the command under two gloo ranks (experts sliced
+    across ranks) and by one process compare as equal (replicated taps)."""
+    import os
+    import socket
+    import subprocess
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PYTHONPATH=repo, OMP_NUM_THREADS="2")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    args = ["-m", "bwn.runtime.diagnostics", "capture", "--model", "tiny-moe", "--cpu", "--moe-sharding", "tp"]
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port)] + args + ["--out", str(tmp_path / "tp2")],
+                       env=env, capture_output=True, text=True, timeout=300, cwd=repo)
+    assert r.returncode == 0, r.stderr[-3000:]
+    r = subprocess.run([sys.executable] + args + ["--out", str(tmp_path / "one")], env=env, capture_output=True,
+                       text=True, timeout=300, cwd=repo)
+    assert r.returncode == 0, r.stderr[-3000:]
+    one, tp2 = D.load_captures(str(tmp_path / "one")), D.load_captures(str(tmp_path / "tp2"))
+    assert len(one) == 1 and len(tp2) == 2 and tp2[1]["meta"]["world"] == 2
+    rep = D.compare_captures(one, tp2)
+    assert rep["ok"], rep["logits"]
+    assert rep["first_diverging_tap"] is None
+    assert all("mixer" not in k for k in rep["taps"])  # shard-local taps skipped across world sizes
