@@ -78,6 +78,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (result marked invalid)")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--fp8", action="store_true", help="W8A16: 128x128 block-scaled E4M3 projection weights")
+    ap.add_argument("--fp8-experts", action="store_true",
+                    help="MoE: block-scaled E4M3 routed experts on the fp8 grouped GEMM")
     ap.add_argument("--fused-comm", default="auto", choices=["auto", "on", "off"])
     ap.add_argument("--sp", default="auto", choices=["auto", "on", "off"],
                     help="N>1: sequence-parallel prefill (reduce-scatter/all-gather fused into the GEMM path)")
@@ -118,8 +120,8 @@ def main() -> None:
     max_seq = S + args.warmup + args.steps * 2 + 64
 
     model = Qwen36Model(cfg, comm, dev, moe_sharding=args.moe_sharding).init_random(seed=0)
-    if args.fp8:
-        model.quantize_fp8()
+    if args.fp8 or args.fp8_experts:
+        model.quantize_fp8(include_head=args.fp8, experts=args.fp8_experts and cfg.is_moe, dense=args.fp8)
         torch.cuda.empty_cache()
     if comm.size > 1 and args.fused_comm != "off":
         try:
@@ -270,7 +272,8 @@ def main() -> None:
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": round(value / BASELINE_TOK_S, 3),
-            "dtype": "bf16 activations, fp8 e4m3 weights (128x128 block scales)" if args.fp8 else "bf16",
+            "dtype": ("bf16 activations, fp8 e4m3 weights (128x128 block scales)" if args.fp8 else
+                      "bf16, fp8 e4m3 routed experts (128x128 block scales)" if args.fp8_experts else "bf16"),
             "data": "synthetic (uniform-random prompt ids, random-init weights seed 0)",
             "config": {
                 "model": cfg.name if not args.layers else f"{cfg.name}-{args.layers}L (INVALID: debug layer count)",

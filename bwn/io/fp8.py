@@ -149,3 +149,73 @@ class FP8Weight:
 
     def nbytes(self) -> int:
         return self.w8.numel() + self.scales.numel() * 4
+
+
+ROW_GROUP = 16  # rows per expert-weight scale (the gate/up interleave block)
+
+
+def _scales16(scales: torch.Tensor, rows: int, block: int = BLOCK) -> torch.Tensor:
+    """128-row block scales ``[.., ceil(rows/128), KB]`` repeated over their
+    16-row groups: ``[.., rows/16, KB]``."""
+    rep = scales.repeat_interleave(block // ROW_GROUP, dim=-2)
+    return rep[..., : rows // ROW_GROUP, :].contiguous()
+
+
+class FP8Experts:
+    """Stacked expert weights ``[E, N, K]`` in E4M3FN with one fp32 scale per
+    16 rows x 128 columns (``scales16 [E, N/16, ceil(K/128)]``, value = fp8 *
+    scale): the operand of the fp8 grouped expert GEMM.  Built from 128x128
+    block quantization of each original matrix (the official checkpoints'
+    blocks); the 16-row granularity lets the block-16 gate/up interleave keep
+    each row's own scale."""
+
+    __slots__ = ("w8", "scales16")
+
+    def __init__(self, w8: torch.Tensor, scales16: torch.Tensor):
+        if w8.dim() != 3 or w8.shape[1] % ROW_GROUP:
+            raise ValueError(f"expert weights [E, N, K] with N a multiple of {ROW_GROUP}, got {tuple(w8.shape)}")
+        want = (w8.shape[0], w8.shape[1] // ROW_GROUP, math.ceil(w8.shape[2] / BLOCK))
+        if tuple(scales16.shape) != want:
+            raise ValueError(f"scales16 {tuple(scales16.shape)} != {want}")
+        self.w8 = w8.contiguous()
+        self.scales16 = scales16.float().contiguous()
+
+    @staticmethod
+    def quantize(w: torch.Tensor) -> "FP8Experts":
+        """``w [E, N, K]`` with 128x128 blocks per expert (a down projection)."""
+        w8, s = quantize_block(w)
+        return FP8Experts(w8, _scales16(s, w.shape[1]))
+
+    @staticmethod
+    def quantize_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = ROW_GROUP) -> "FP8Experts":
+        """``gate, up [E, I, K]``, each quantized in its own 128x128 blocks, rows
+        interleaved in 16s (the layout of the fused SwiGLU epilogue)."""
+        E, I, K = gate.shape
+        g8, gs = quantize_block(gate)
+        u8, us = quantize_block(up)
+        w8 = torch.stack([g8.reshape(E, I // block, block, K), u8.reshape(E, I // block, block, K)], dim=2)
+        s16 = torch.stack([_scales16(gs, I), _scales16(us, I)], dim=2)
+        return FP8Experts(w8.reshape(E, 2 * I, K), s16.reshape(E, 2 * I // ROW_GROUP, -1))
+
+    @staticmethod
+    def from_interleaved(w_il: torch.Tensor, block: int = ROW_GROUP) -> "FP8Experts":
+        """Quantize already-interleaved bf16 gate/up weights ``[E, 2I, K]``."""
+        E, n2, K = w_il.shape
+        x = w_il.reshape(E, n2 // (2 * block), 2, block, K)
+        return FP8Experts.quantize_gate_up(x[:, :, 0].reshape(E, n2 // 2, K), x[:, :, 1].reshape(E, n2 // 2, K))
+
+    @property
+    def shape(self):
+        return self.w8.shape
+
+    def dequant(self) -> torch.Tensor:
+        """fp32 ``[E, N, K]``."""
+        v = decode_e4m3fn(self.w8, reject_nan=False)
+        s = self.scales16.repeat_interleave(ROW_GROUP, dim=1).repeat_interleave(BLOCK, dim=2)
+        return v * s[..., : v.shape[2]]
+
+    def to(self, device) -> "FP8Experts":
+        return FP8Experts(self.w8.to(device), self.scales16.to(device))
+
+    def nbytes(self) -> int:
+        return self.w8.numel() + self.scales16.numel() * 4

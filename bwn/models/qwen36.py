@@ -123,15 +123,20 @@ class Qwen36Model(nn.Module):
 
     FP8_KEYS = ("in_proj", "out_proj", "qkv_proj", "o_proj", "gate_up", "down", "shared_gate_up", "shared_down")
 
-    def quantize_fp8(self, include_head: bool = True) -> "Qwen36Model":
+    def quantize_fp8(self, include_head: bool = True, experts: bool = False, dense: bool = True) -> "Qwen36Model":
         """Convert the projection weights to 128x128 block-scaled E4M3 (W8A16):
         the fp8 variant of the reference's ``--fp8-weights``
-        (``contrib/qwen3.6-27b/static_decode.py:283-319``)."""
-        from ..io.fp8 import FP8Weight
+        (``contrib/qwen3.6-27b/static_decode.py:283-319``).  ``experts``: the
+        routed experts too (:class:`~bwn.io.fp8.FP8Experts`, fp8 grouped GEMM;
+        the reference's block-scaled FP8 MoE, ``moe_fused_w8_35b.py``)."""
+        from ..io.fp8 import FP8Experts, FP8Weight
         for L in self.layers:
-            for k in self.FP8_KEYS:
+            for k in self.FP8_KEYS if dense else ():
                 if k in L and torch.is_tensor(L[k]) and L[k].dim() == 2 and L[k].shape[1] % 16 == 0:
                     L[k] = FP8Weight.from_dense(L[k])
+            if experts and torch.is_tensor(L.get("experts_gate_up")):
+                L["experts_gate_up"] = FP8Experts.from_interleaved(L["experts_gate_up"])
+                L["experts_down"] = FP8Experts.quantize(L["experts_down"])
         if include_head:
             self.g["lm_head"] = FP8Weight.from_dense(self.g["lm_head"])
         return self

@@ -251,7 +251,18 @@ def moe_topk_deepseek(logits: torch.Tensor, bias, k: int, score_func: str = "sqr
 
 def moe_experts(x, w, ids, gate_up_il, down, expert_offset: int = 0, shared=None, swiglu_limit: float = 0.0):
     """This rank's routed-expert partial (plus, when ``shared=(y, gate_logit)``
-    is given, ``sigmoid(gate_logit) * y``)."""
+    is given, ``sigmoid(gate_logit) * y``).  The experts are bf16 tensors or
+    :class:`~bwn.io.fp8.FP8Experts` (fp8 grouped GEMM on the GPU)."""
+    if hasattr(gate_up_il, "scales16"):
+        if x.is_cuda:
+            sy, sg = (shared if shared is not None else (None, None))
+            return ops().moe_experts_w8(x, w.float().contiguous(), ids.int().contiguous(), gate_up_il.w8,
+                                        gate_up_il.scales16, down.w8, down.scales16, expert_offset, sy,
+                                        sg.float().reshape(-1).contiguous() if sg is not None else None,
+                                        swiglu_limit)
+        # the GPU kernel rounds each dequantized weight to bf16
+        gate_up_il = gate_up_il.dequant().to(torch.bfloat16).to(x.dtype)
+        down = down.dequant().to(torch.bfloat16).to(x.dtype)
     if x.is_cuda:
         sy, sg = (shared if shared is not None else (None, None))
         return ops().moe_experts(x, w.float().contiguous(), ids.int().contiguous(), gate_up_il, down, expert_offset,

@@ -93,6 +93,8 @@ def enable_ep_all_to_all(model, max_tokens_per_rank: int = 512, min_tokens_per_r
     cfg, comm = model.cfg, model.comm
     if not cfg.is_moe or comm.size <= 1:
         raise RuntimeError("expert-parallel all-to-all needs a MoE model on more than one rank")
+    if any(hasattr(L.get("experts_gate_up"), "scales16") for L in model.layers):
+        raise RuntimeError("the expert-parallel all-to-all runs bf16 experts; fp8 experts use the all-reduce path")
     if model.d.moe_sharding != "ep":
         raise RuntimeError("the expert-parallel all-to-all needs experts partitioned across ranks (moe_sharding='ep')")
     ep = EPAllToAll(comm, cfg.hidden, cfg.num_experts, cfg.top_k, max_tokens_per_rank, device=model.device)

@@ -21,6 +21,7 @@
 #include "common/host.h"
 #include "common/sm100.cuh"
 #include "kernels/moe.h"
+#include "kernels/grouped_units.cuh"
 
 namespace bwn {
 
@@ -317,34 +318,6 @@ struct GCfg {
   static constexpr int kTmem = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kSmem = kStages * kStage + 1024 + 256;
 };
-
-constexpr int kGMaxGroups = 256;
-
-// Work units are compacted over the groups' actual row counts (cached in
-// shared memory at kernel start): unit u -> group e by binary search over the
-// per-group unit prefix, so empty groups and empty row tiles cost nothing.
-struct GUnits {
-  int pref[kGMaxGroups + 1];  // units before group e
-  int cnt[kGMaxGroups];
-  int off[kGMaxGroups];
-};
-
-__device__ __forceinline__ bool gunit(const GroupedArgs& a, const GUnits& g, int u, int& e, int& tm, int& tn, int& n0,
-                                      int& nrows, int BN) {
-  int lo = 0, hi = a.groups;  // largest e with pref[e] <= u
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (g.pref[mid] <= u) lo = mid; else hi = mid;
-  }
-  e = lo;
-  const int rem = u - g.pref[e];
-  tm = rem % a.tiles_m;
-  tn = rem / a.tiles_m;
-  const int cnt = g.cnt[e];
-  n0 = g.off[e] + tn * BN;
-  nrows = min(BN, cnt - tn * BN);
-  return nrows > 0;
-}
 
 template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(kGThreadsG, 1)

@@ -1,5 +1,6 @@
 // Launch descriptors for the MoE kernels (csrc/kernels/moe.cu).
 #pragma once
+#include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -68,5 +69,25 @@ struct GroupedProblem {
   float swiglu_limit = 0.f;
 };
 void grouped_gemm(const GroupedProblem& p, cudaStream_t st);
+
+// Grouped GEMM with block-scaled E4M3FN expert weights (csrc/kernels/moe_w8.cu).
+// ``scales16[e][r / 16][k / 128]``: one fp32 scale per 16 weight rows and 128
+// columns (a 128x128 checkpoint block repeats over its 8 row groups; 16-row
+// granularity keeps the gate/up interleave exact), value = fp8 * scale.
+struct GroupedW8Problem {
+  const uint8_t* W;       // [groups * N, K] E4M3FN bytes (expert-major)
+  const float* scales16;  // [groups, N / 16, ceil(K / 128)]
+  const void* X;          // [rows_total, K] bf16, expert-major rows
+  int rows_total;
+  const int* counts;
+  const int* offsets;
+  int groups, N, K, max_rows_per_group;
+  bool swiglu;
+  __nv_bfloat16* out;
+  long ldo;
+  int* status;
+  float swiglu_limit = 0.f;
+};
+void grouped_gemm_w8(const GroupedW8Problem& p, cudaStream_t st);
 
 }  // namespace bwn

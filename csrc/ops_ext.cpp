@@ -245,6 +245,102 @@ Tensor moe_experts_op(const Tensor& x, const Tensor& w, const Tensor& ids, const
   return out;
 }
 
+// Routed experts with block-scaled E4M3FN weights (scales per 16 rows x 128
+// columns, csrc/kernels/moe.h): the same pack -> gate/up (SwiGLU) -> down ->
+// combine pipeline as moe_experts, the two GEMMs on the fp8 grouped kernel.
+Tensor moe_experts_w8_op(const Tensor& x, const Tensor& w, const Tensor& ids, const Tensor& gate_up8,
+                         const Tensor& gate_up_s16, const Tensor& down8, const Tensor& down_s16, int64_t e0,
+                         const c10::optional<Tensor>& shared_y, const c10::optional<Tensor>& shared_gate,
+                         double swiglu_limit) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, H]");
+  TORCH_CHECK(gate_up8.is_cuda() && gate_up8.scalar_type() == at::kByte && gate_up8.is_contiguous() &&
+                  gate_up8.dim() == 3, "gate_up8: uint8 [E, 2I, H] contiguous");
+  TORCH_CHECK(down8.is_cuda() && down8.scalar_type() == at::kByte && down8.is_contiguous() && down8.dim() == 3,
+              "down8: uint8 [E, H, I] contiguous");
+  check_f32(gate_up_s16, "gate_up_scales16");
+  check_f32(down_s16, "down_scales16");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0), H = (int)x.size(1), k = (int)ids.size(1);
+  const int El = (int)gate_up8.size(0), I2 = (int)gate_up8.size(1), I = I2 / 2;
+  TORCH_CHECK(gate_up8.size(2) == H && down8.size(0) == El && down8.size(1) == H && down8.size(2) == I,
+              "expert shapes: gate_up8 [E, 2I, H], down8 [E, H, I]");
+  TORCH_CHECK(gate_up_s16.is_contiguous() && gate_up_s16.numel() == (long)El * (I2 / 16) * ((H + 127) / 128),
+              "gate_up_scales16 [E, 2I/16, ceil(H/128)]");
+  TORCH_CHECK(down_s16.is_contiguous() && down_s16.numel() == (long)El * (H / 16) * ((I + 127) / 128),
+              "down_scales16 [E, H/16, ceil(I/128)]");
+  auto opt = x.options();
+  auto iopt = opt.dtype(at::kInt);
+  const int n = T * k;
+  auto counts = at::empty({El}, iopt);
+  auto offsets = at::empty({El + 1}, iopt);
+  auto pos_of = at::empty({n}, iopt);
+  auto row_src = at::empty({std::max(n, 1)}, iopt);
+  auto xp = at::empty({std::max(n, 1), H}, opt);
+  auto y1 = at::empty({std::max(n, 1), I}, opt);
+  auto y2 = at::empty({std::max(n, 1), H}, opt);
+  auto out = at::empty({T, H}, opt);
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  MoeRouteArgs r{};
+  r.ids = ids.data_ptr<int>();
+  r.T = T;
+  r.k = k;
+  r.e0 = (int)e0;
+  r.E_local = El;
+  r.counts = counts.data_ptr<int>();
+  r.offsets = offsets.data_ptr<int>();
+  r.pos_of = pos_of.data_ptr<int>();
+  r.row_src = row_src.data_ptr<int>();
+  r.x = cbf(x);
+  r.ldx = x.stride(0);
+  r.H = H;
+  r.x_perm = mbf(xp);
+  moe_route(r, st);
+  GroupedW8Problem g{};
+  g.W = gate_up8.data_ptr<uint8_t>();
+  g.scales16 = gate_up_s16.data_ptr<float>();
+  g.X = xp.data_ptr();
+  g.rows_total = n;
+  g.counts = r.counts;
+  g.offsets = r.offsets;
+  g.groups = El;
+  g.N = I2;
+  g.K = H;
+  g.max_rows_per_group = T;
+  g.swiglu = true;
+  g.swiglu_limit = (float)swiglu_limit;
+  g.out = mbf(y1);
+  g.ldo = I;
+  g.status = status_dev_ptr();
+  grouped_gemm_w8(g, st);
+  g.W = down8.data_ptr<uint8_t>();
+  g.scales16 = down_s16.data_ptr<float>();
+  g.X = y1.data_ptr();
+  g.N = H;
+  g.K = I;
+  g.swiglu = false;
+  g.swiglu_limit = 0.f;
+  g.out = mbf(y2);
+  g.ldo = H;
+  grouped_gemm_w8(g, st);
+  MoeCombineArgs c{};
+  c.y = cbf(y2);
+  c.w = w.data_ptr<float>();
+  c.pos_of = r.pos_of;
+  c.T = T;
+  c.k = k;
+  c.H = H;
+  if (shared_y.has_value()) {
+    c.shared_y = cbf(*shared_y);
+    c.ld_shared = shared_y->stride(0);
+    c.shared_gate = shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr;
+  }
+  c.out = mbf(out);
+  c.ldo = out.stride(0);
+  moe_combine(c, st);
+  return out;
+}
+
 // ---------------------------------------------------------------------------
 // DeepSeek V4
 // ---------------------------------------------------------------------------
@@ -482,6 +578,9 @@ void register_ext_defs(torch::Library& m) {
       "moe_experts(Tensor x, Tensor w, Tensor ids, Tensor gate_up, Tensor down, int e0, Tensor? shared_y, "
       "Tensor? shared_gate, float swiglu_limit) -> Tensor");
   m.def(
+      "moe_experts_w8(Tensor x, Tensor w, Tensor ids, Tensor gate_up8, Tensor gate_up_scales16, Tensor down8, "
+      "Tensor down_scales16, int e0, Tensor? shared_y, Tensor? shared_gate, float swiglu_limit) -> Tensor");
+  m.def(
       "hc_pre(Tensor x, Tensor fn, Tensor scale, Tensor base, int sinkhorn_iters, float eps, float norm_eps) "
       "-> (Tensor, Tensor, Tensor)");
   m.def("hc_post(Tensor x, Tensor resid, Tensor post, Tensor comb) -> Tensor");
@@ -498,6 +597,7 @@ void register_ext_impls(torch::Library& m) {
   m.impl("deltanet_verify", &deltanet_verify_op);
   m.impl("moe_topk", &moe_topk_op);
   m.impl("moe_experts", &moe_experts_op);
+  m.impl("moe_experts_w8", &moe_experts_w8_op);
   m.impl("moe_grouped_ffn", &moe_grouped_ffn_op);
   m.impl("moe_combine", &moe_combine_op);
   m.impl("hc_pre", &hc_pre_op);
