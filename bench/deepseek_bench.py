@@ -43,6 +43,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (marked in the output)")
     ap.add_argument("--fp8", action="store_true", help="dense projections and LM head as 128x128 block-scaled E4M3")
+    ap.add_argument("--fp8-experts", action="store_true", help="routed experts as block-scaled E4M3 (fp8 grouped GEMM)")
     ap.add_argument("--skip-prefill", action="store_true")
     args = ap.parse_args()
     comm = init_distributed("nccl", timeout_s=600)
@@ -59,16 +60,18 @@ def main():
             print(f"[deepseek_bench +{time.perf_counter() - t_start:.1f}s] {msg}", file=sys.stderr, flush=True)
 
     model = DeepSeekV4Model(cfg, comm, dev).init_random_local(0)
-    if args.fp8:
-        model.quantize_fp8()
+    if args.fp8 or args.fp8_experts:
+        model.quantize_fp8(include_head=args.fp8, experts=args.fp8_experts)
     torch.cuda.synchronize()
     note("weights ready")
     res = {"model": cfg.name + (f"-{args.layers}L (debug)" if args.layers else ""), "n_gpus": comm.size,
            "parallelism": f"tp{comm.size}+ep{comm.size}",
-           "dtype": "bf16 activations, fp8 dense weights" if args.fp8 else "bf16",
+           "dtype": "bf16 activations" + (", fp8 dense weights" if args.fp8 else "") +
+                    (", fp8 routed experts" if args.fp8_experts else ""),
            "data": "synthetic (uniform-random prompt ids, random-init weights)",
-           "weights_gb_per_gpu": round(sum(v.numel() * v.element_size() for L in model.L for v in L.values()
-                                           if torch.is_tensor(v)) / 1e9, 1)}
+           "weights_gb_per_gpu": round(sum(v.numel() * v.element_size() if torch.is_tensor(v) else v.nbytes()
+                                           for L in model.L for v in L.values()
+                                           if torch.is_tensor(v) or hasattr(v, "nbytes")) / 1e9, 1)}
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (1, S), generator=g).to(dev)
     if not args.skip_prefill:

@@ -223,16 +223,20 @@ class DeepSeekV4Model:
 
     FP8_KEYS = ("wq_a", "wq_b", "wkv", "wo_b", "shared_gate_up", "shared_down")
 
-    def quantize_fp8(self, include_head: bool = True) -> "DeepSeekV4Model":
+    def quantize_fp8(self, include_head: bool = True, experts: bool = False) -> "DeepSeekV4Model":
         """Dense projections (and the LM head) as 128x128 block-scaled E4M3
-        (W8A16), the layout of the checkpoint's FP8 dense weights; routed experts
-        stay bf16 (grouped GEMM)."""
-        from ..io.fp8 import FP8Weight
+        (W8A16), the layout of the checkpoint's FP8 dense weights; with
+        ``experts`` the routed experts too (:class:`~bwn.io.fp8.FP8Experts` on
+        the fp8 grouped GEMM, clamped SwiGLU in its epilogue)."""
+        from ..io.fp8 import FP8Experts, FP8Weight
         for L in self.L:
             for k in self.FP8_KEYS:
                 w = L.get(k)
                 if torch.is_tensor(w) and w.dim() == 2 and w.shape[1] % 16 == 0:
                     L[k] = FP8Weight.from_dense(w)
+            if experts and torch.is_tensor(L.get("experts_gate_up")):
+                L["experts_gate_up"] = FP8Experts.from_interleaved(L["experts_gate_up"])
+                L["experts_down"] = FP8Experts.quantize(L["experts_down"])
         if include_head:
             self.g["head"] = FP8Weight.from_dense(self.g["head"])
         return self

@@ -103,3 +103,21 @@ def test_fp8_dense_weights_close_to_bf16():
         hs.append(m.logits(m.forward_tokens(toks.reshape(-1), pos, bidx, st, 8)))
     rel = float((hs[0] - hs[1]).norm() / hs[0].norm())
     assert 0 < rel < 0.1
+
+
+def test_fp8_experts_close_to_bf16():
+    from bwn.models.deepseek_v4 import synthetic_checkpoint
+    cfg = tiny_deepseek_v4()
+    sd = synthetic_checkpoint(cfg, 0)
+    a = DeepSeekV4Model(cfg, None, "cpu", torch.float32).load(sd)
+    b = DeepSeekV4Model(cfg, None, "cpu", torch.float32).load(sd).quantize_fp8(include_head=False, experts=True)
+    assert hasattr(b.L[-1]["experts_gate_up"], "scales16")
+    toks = torch.randint(0, cfg.vocab, (2, 8), generator=torch.Generator().manual_seed(2))
+    hs = []
+    for m in (a, b):
+        st = m.new_state(2, 16)
+        pos = torch.arange(8, dtype=torch.int32).repeat(2)
+        bidx = torch.arange(2, dtype=torch.int32).repeat_interleave(8)
+        hs.append(m.logits(m.forward_tokens(toks.reshape(-1), pos, bidx, st, 8)))
+    rel = float((hs[0] - hs[1]).norm() / hs[0].norm())
+    assert 0 < rel < 0.1
