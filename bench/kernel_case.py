@@ -1,10 +1,12 @@
 #!/usr/bin/env python
 """Run one bwn kernel on a fixed small case a few times (for ncu captures and
-quick timing).  Each op here is one kernel launch per iteration.
+quick timing).  Each op here is one kernel launch per iteration, except the
+MoE blocks (route, gather, two grouped GEMMs, combine: five launches).
 
     python bench/kernel_case.py --op linear --M 32 --N 5120 --K 6144
     python bench/kernel_case.py --op gqa --B 32 --QH 24 --KVH 4 --ctx 2048
     python bench/kernel_case.py --op deltanet --B 32 --KH 16 --VH 48
+    python bench/kernel_case.py --op moe_w8 --T 32 --E 256 --k 8 --H 2048 --I 512
 """
 import argparse
 import os
@@ -20,7 +22,7 @@ from bwn.ops import reference as R  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", required=True, choices=["linear", "linear_w8", "swiglu", "gqa", "deltanet"])
+    ap.add_argument("--op", required=True, choices=["linear", "linear_w8", "swiglu", "gqa", "deltanet", "moe", "moe_w8"])
     ap.add_argument("--M", type=int, default=32)
     ap.add_argument("--N", type=int, default=5120)
     ap.add_argument("--K", type=int, default=6144)
@@ -30,6 +32,11 @@ def main():
     ap.add_argument("--KH", type=int, default=16)
     ap.add_argument("--VH", type=int, default=48)
     ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--T", type=int, default=32, help="MoE tokens")
+    ap.add_argument("--E", type=int, default=256, help="MoE experts (all local)")
+    ap.add_argument("--k", type=int, default=8, help="MoE experts per token")
+    ap.add_argument("--H", type=int, default=2048)
+    ap.add_argument("--I", type=int, default=512)
     ap.add_argument("--iters", type=int, default=5)
     a = ap.parse_args()
     dev = "cuda"
@@ -45,6 +52,22 @@ def main():
         w = (torch.randn(a.N, a.K, device=dev) * 0.02).bfloat16()
         fn = (lambda: O.linear(x, w)) if a.op == "linear" else (lambda: O.linear_swiglu(x, w))
         nbytes = a.N * a.K * 2
+    elif a.op in ("moe", "moe_w8"):
+        from bwn.io.fp8 import FP8Experts
+        x = torch.randn(a.T, a.H, device=dev).bfloat16()
+        w, ids = O.moe_topk_softmax(torch.randn(a.T, a.E, device=dev), a.k)
+        g = torch.randn(a.E, a.I, a.H, device=dev) * 0.02
+        u = torch.randn(a.E, a.I, a.H, device=dev) * 0.02
+        dn = torch.randn(a.E, a.H, a.I, device=dev) * 0.02
+        if a.op == "moe_w8":
+            gu, dw = FP8Experts.quantize_gate_up(g, u), FP8Experts.quantize(dn)
+        else:
+            gu = torch.stack([O.interleave_gate_up(g[e], u[e]) for e in range(a.E)]).bfloat16()
+            dw = dn.bfloat16()
+        del g, u, dn
+        fn = lambda: O.moe_experts(x, w, ids, gu, dw, 0)  # noqa: E731
+        active = int(torch.unique(ids).numel())
+        nbytes = active * 3 * a.I * a.H * (1 if a.op == "moe_w8" else 2)
     elif a.op == "gqa":
         D = 256
         qg = torch.randn(a.B, a.QH, 2 * D, device=dev).bfloat16()
