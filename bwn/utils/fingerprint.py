@@ -105,7 +105,12 @@ def snapshot_state(st) -> dict:
     b = torch.arange(pos.shape[0], device=pos.device)
     R = st.conv.shape[2]
     return {"pos": pos.clone(), "ssm": st.ssm.clone(), "conv": st.conv[:, b, pos % R].clone(),
-            "k": st.k_cache[:, b, :, pos].clone(), "v": st.v_cache[:, b, :, pos].clone()}
+            "k": _kv_rows(st.k_cache, b, pos).clone(), "v": _kv_rows(st.v_cache, b, pos).clone()}
+
+
+def _kv_rows(cache: torch.Tensor, b: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    """``cache [L, B, KVH, S, D]`` -> the row at each sequence's position, ``[L, B, KVH, D]``."""
+    return cache.transpose(2, 3)[:, b, pos]
 
 
 def assert_state_advanced(before: dict, st, what: str = "decode step") -> None:
@@ -117,8 +122,8 @@ def assert_state_advanced(before: dict, st, what: str = "decode step") -> None:
         raise RuntimeError(f"{what}: positions did not advance by one")
     b = torch.arange(pos.shape[0], device=pos.device)
     R = st.conv.shape[2]
-    now = {"ssm": st.ssm, "conv": st.conv[:, b, pos % R], "k": st.k_cache[:, b, :, pos],
-           "v": st.v_cache[:, b, :, pos]}
+    now = {"ssm": st.ssm, "conv": st.conv[:, b, pos % R], "k": _kv_rows(st.k_cache, b, pos),
+           "v": _kv_rows(st.v_cache, b, pos)}
     for name, cur in now.items():
         old = before[name]
         # [L, B, ...]: per layer and sequence, did anything change
