@@ -1,11 +1,16 @@
 """HTTP completion server (``/v1/completions``, ``/health``, ``/metrics``).
 
 Requests carry token ids (``prompt``: list of ints; a tokenizer is outside the
-framework).  A worker thread drains the queue into batches of at most
-``max_batch`` requests (waiting up to ``batch_window_ms`` for a batch to fill)
-and runs them through :class:`~bwn.serve.engine.GenerationEngine`.
+framework).  Two schedulers:
 
-    python -m bwn.serve.server --model tiny --port 8000
+* ``static`` (:class:`BatchingWorker`): a worker thread drains the queue into
+  batches of at most ``max_batch`` requests (waiting up to ``batch_window_ms``
+  for a batch to fill) and runs each batch to completion through
+  :class:`~bwn.serve.engine.GenerationEngine`;
+* ``continuous`` (:class:`ContinuousWorker`): requests join and leave the
+  running batch between decode steps (:class:`~bwn.serve.continuous.ContinuousEngine`).
+
+    python -m bwn.serve.server --model tiny --port 8000 --scheduler continuous
 """
 from __future__ import annotations
 
@@ -73,7 +78,69 @@ class BatchingWorker:
         self.thread.join(timeout=5)
 
 
-def build_app(worker: BatchingWorker, model_name: str = "bwn"):
+class ContinuousWorker:
+    """One thread owns the engine: it admits queued requests, runs decode steps
+    while any slot is busy, and completes each request's future when it finishes."""
+
+    def __init__(self, engine, idle_poll_s: float = 0.05):
+        self.engine = engine
+        self.poll = idle_poll_s
+        self.q: queue.Queue = queue.Queue()
+        self.futs: dict[int, Future] = {}
+        self.stats = {"requests": 0, "steps": 0, "tokens": 0}
+        self._stop = False
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
+
+    def submit(self, req: Request) -> Future:
+        fut: Future = Future()
+        self.q.put((req, fut))
+        return fut
+
+    def _drain(self, block: bool):
+        try:
+            item = self.q.get(timeout=self.poll) if block else self.q.get_nowait()
+        except queue.Empty:
+            return False
+        while item is not None:
+            req, fut = item
+            try:
+                self.futs[self.engine.add(req)] = fut
+            except ValueError as e:
+                fut.set_exception(e)
+            try:
+                item = self.q.get_nowait()
+            except queue.Empty:
+                item = None
+        return True
+
+    def _loop(self):
+        while not self._stop:
+            if self.engine.idle():
+                self._drain(block=True)
+                continue
+            self._drain(block=False)
+            try:
+                finished = self.engine.step()
+            except Exception as e:  # noqa: BLE001 - fail every request in flight, keep serving
+                for fut in self.futs.values():
+                    fut.set_exception(e)
+                self.futs.clear()
+                self.engine.slots = [None] * self.engine.max_batch
+                self.engine.waiting.clear()
+                continue
+            self.stats["steps"] += 1
+            for rid, res in finished:
+                self.stats["requests"] += 1
+                self.stats["tokens"] += len(res.tokens)
+                self.futs.pop(rid).set_result(res)
+
+    def stop(self):
+        self._stop = True
+        self.thread.join(timeout=5)
+
+
+def build_app(worker, model_name: str = "bwn"):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import PlainTextResponse
 
@@ -112,6 +179,7 @@ def main():
     ap.add_argument("--max-seq", type=int, default=4096)
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--scheduler", default="continuous", choices=["continuous", "static"])
     a = ap.parse_args()
     import torch
     import uvicorn
@@ -124,7 +192,11 @@ def main():
     else:
         cfg = {"tiny": tiny_qwen36(), "27b": QWEN36_27B, "35b": QWEN36_35B_A3B}[a.model]
         model = Qwen36Model(cfg, None, dev).init_random(0)
-    worker = BatchingWorker(GenerationEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda"))
+    if a.scheduler == "continuous":
+        from .continuous import ContinuousEngine
+        worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda"))
+    else:
+        worker = BatchingWorker(GenerationEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda"))
     uvicorn.run(build_app(worker, a.model), host=a.host, port=a.port)
 
 

@@ -1,5 +1,6 @@
 """Generation engine (static batches, right-padded prompts, stop ids) and the
 HTTP completion server, on the tiny Qwen3.6 model on the CPU."""
+import pytest
 import torch
 
 from bwn.config import tiny_qwen36
@@ -47,4 +48,66 @@ def test_http_server():
     assert body["choices"][0]["tokens"] == _greedy(model, [5, 9, 13], 4)
     assert client.post("/v1/completions", json={"prompt": [], "max_tokens": 4}).status_code == 400
     assert "bwn_requests_total 1" in client.get("/metrics").text
+    worker.stop()
+
+
+def test_continuous_batching_matches_solo_generation():
+    """Five requests of different lengths through two slots: requests join and
+    leave the running batch between steps, and each one's tokens equal its
+    generation alone; idle slots stay inside their caches although the run is
+    longer than max_seq."""
+    from bwn.config import tiny_qwen36
+    from bwn.models.qwen36 import build_qwen36
+    from bwn.runtime.static_decode import StaticDecoder
+    from bwn.serve.continuous import ContinuousEngine
+    from bwn.serve.engine import Request
+    cfg = tiny_qwen36()
+    m = build_qwen36(cfg, seed=11, dtype=torch.float32)
+    g = torch.Generator().manual_seed(4)
+    reqs = [Request(torch.randint(0, cfg.vocab, (n,), generator=g).tolist(), max_tokens=t)
+            for n, t in [(5, 6), (9, 3), (3, 8), (7, 1), (4, 5)]]
+    solo = []
+    for q in reqs:
+        d = StaticDecoder(m, 1, 32, use_graph=False)
+        solo.append(d.generate(torch.tensor([q.prompt]), q.max_tokens)[0].tolist())
+    eng = ContinuousEngine(m, max_batch=2, max_seq=24, use_graph=False)
+    res = eng.run(reqs)
+    assert [r.tokens for r in res] == solo
+    assert all(r.finish_reason == "length" for r in res)
+    assert eng.stats["admitted"] == 5 and eng.stats["finished"] == 5
+    # a stop id ends a request early and frees its slot
+    stop_at = solo[2][2]
+    res2 = eng.run([Request(reqs[2].prompt, max_tokens=8, stop=[stop_at])])
+    assert res2[0].tokens == solo[2][:solo[2].index(stop_at) + 1] and res2[0].finish_reason == "stop"
+    # one long request beside an idle slot: more steps than max_seq rows would allow an idle row
+    eng2 = ContinuousEngine(m, max_batch=2, max_seq=24, use_graph=False)
+    long = Request(reqs[0].prompt, max_tokens=18)
+    ref = StaticDecoder(m, 1, 32, use_graph=False).generate(torch.tensor([long.prompt]), 18)[0].tolist()
+    assert eng2.run([long])[0].tokens == ref
+    assert int(eng2.dec.st.positions[1]) <= 1  # pinned to 0 before every step
+    with pytest.raises(ValueError):
+        eng2.add(Request([1] * 20, max_tokens=10))
+
+
+def test_http_server_continuous_scheduler():
+    """Concurrent HTTP requests through the continuous scheduler: each answer
+    equals the request's solo greedy tokens; a request that cannot fit is a 400."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from fastapi.testclient import TestClient
+
+    from bwn.serve.continuous import ContinuousEngine
+    from bwn.serve.server import ContinuousWorker, build_app
+    model = build_qwen36(tiny_qwen36(layers=4), device="cpu", dtype=torch.float32)
+    worker = ContinuousWorker(ContinuousEngine(model, 2, 64, use_graph=False))
+    client = TestClient(build_app(worker, "tiny"))
+    prompts = [([5, 9, 13], 4), ([7, 7, 2, 1, 30], 6), ([100], 3), ([3, 4], 5)]
+    with ThreadPoolExecutor(4) as ex:
+        rs = list(ex.map(lambda pt: client.post("/v1/completions", json={"prompt": pt[0], "max_tokens": pt[1]}),
+                         prompts))
+    for (p, t), r in zip(prompts, rs):
+        assert r.status_code == 200
+        assert r.json()["choices"][0]["tokens"] == _greedy(model, p, t)
+    assert client.post("/v1/completions", json={"prompt": [1] * 60, "max_tokens": 10}).status_code == 400
+    assert "bwn_requests_total 4" in client.get("/metrics").text
     worker.stop()
