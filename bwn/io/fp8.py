@@ -217,5 +217,9 @@ class FP8Experts:
     def to(self, device) -> "FP8Experts":
         return FP8Experts(self.w8.to(device), self.scales16.to(device))
 
+    def select(self, e0: int, e1: int) -> "FP8Experts":
+        """Experts ``[e0, e1)`` (an expert-parallel rank's slice)."""
+        return FP8Experts(self.w8[e0:e1], self.scales16[e0:e1])
+
     def nbytes(self) -> int:
         return self.w8.numel() + self.scales16.numel() * 4

@@ -74,8 +74,12 @@ class EPAllToAll:
         ``down``; ``shared = (shared_y [T, H], shared_gate_logit [T, 1])``."""
         T = x.shape[0]
         self.dispatch(x, ids)
-        y = O.ops().moe_grouped_ffn(self.recv_x, self.counts, self.offsets, gate_up, down, self.max_recv,
-                                    swiglu_limit)
+        if hasattr(gate_up, "scales16"):  # block-scaled fp8 experts (bwn.io.fp8.FP8Experts)
+            y = O.ops().moe_grouped_ffn_w8(self.recv_x, self.counts, self.offsets, gate_up.w8, gate_up.scales16,
+                                           down.w8, down.scales16, self.max_recv, swiglu_limit)
+        else:
+            y = O.ops().moe_grouped_ffn(self.recv_x, self.counts, self.offsets, gate_up, down, self.max_recv,
+                                        swiglu_limit)
         self.give_back(y, T)
         sy, sg = shared if shared is not None else (None, None)
         sg = sg.float().reshape(-1).contiguous() if sg is not None else None
@@ -93,8 +97,6 @@ def enable_ep_all_to_all(model, max_tokens_per_rank: int = 512, min_tokens_per_r
     cfg, comm = model.cfg, model.comm
     if not cfg.is_moe or comm.size <= 1:
         raise RuntimeError("expert-parallel all-to-all needs a MoE model on more than one rank")
-    if any(hasattr(L.get("experts_gate_up"), "scales16") for L in model.layers):
-        raise RuntimeError("the expert-parallel all-to-all runs bf16 experts; fp8 experts use the all-reduce path")
     if model.d.moe_sharding != "ep":
         raise RuntimeError("the expert-parallel all-to-all needs experts partitioned across ranks (moe_sharding='ep')")
     ep = EPAllToAll(comm, cfg.hidden, cfg.num_experts, cfg.top_k, max_tokens_per_rank, device=model.device)

@@ -532,6 +532,62 @@ Tensor moe_grouped_ffn_op(const Tensor& x_perm, const Tensor& counts, const Tens
   return y2;
 }
 
+// moe_grouped_ffn with block-scaled E4M3FN experts (scales per 16 rows x 128
+// columns): the expert-parallel receive buffer through the fp8 grouped GEMM.
+Tensor moe_grouped_ffn_w8_op(const Tensor& x_perm, const Tensor& counts, const Tensor& offsets,
+                             const Tensor& gate_up8, const Tensor& gate_up_s16, const Tensor& down8,
+                             const Tensor& down_s16, int64_t max_rows_per_group, double swiglu_limit) {
+  check_bf16(x_perm, "x_perm");
+  TORCH_CHECK(x_perm.dim() == 2 && x_perm.is_contiguous(), "x_perm [rows, H] contiguous");
+  TORCH_CHECK(counts.scalar_type() == at::kInt && offsets.scalar_type() == at::kInt, "counts/offsets int32");
+  TORCH_CHECK(gate_up8.is_cuda() && gate_up8.scalar_type() == at::kByte && gate_up8.is_contiguous() &&
+                  gate_up8.dim() == 3, "gate_up8: uint8 [E, 2I, H] contiguous");
+  TORCH_CHECK(down8.is_cuda() && down8.scalar_type() == at::kByte && down8.is_contiguous() && down8.dim() == 3,
+              "down8: uint8 [E, H, I] contiguous");
+  check_f32(gate_up_s16, "gate_up_scales16");
+  check_f32(down_s16, "down_scales16");
+  const c10::cuda::CUDAGuard guard(x_perm.device());
+  const int rows = (int)x_perm.size(0), H = (int)x_perm.size(1);
+  const int El = (int)gate_up8.size(0), I2 = (int)gate_up8.size(1), I = I2 / 2;
+  TORCH_CHECK(gate_up8.size(2) == H && down8.size(0) == El && down8.size(1) == H && down8.size(2) == I,
+              "expert shapes: gate_up8 [E, 2I, H], down8 [E, H, I]");
+  TORCH_CHECK(gate_up_s16.is_contiguous() && gate_up_s16.numel() == (long)El * (I2 / 16) * ((H + 127) / 128),
+              "gate_up_scales16 [E, 2I/16, ceil(H/128)]");
+  TORCH_CHECK(down_s16.is_contiguous() && down_s16.numel() == (long)El * (H / 16) * ((I + 127) / 128),
+              "down_scales16 [E, H/16, ceil(I/128)]");
+  auto y1 = at::empty({std::max(rows, 1), I}, x_perm.options());
+  auto y2 = at::empty({std::max(rows, 1), H}, x_perm.options());
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  GroupedW8Problem g{};
+  g.W = gate_up8.data_ptr<uint8_t>();
+  g.scales16 = gate_up_s16.data_ptr<float>();
+  g.X = x_perm.data_ptr();
+  g.rows_total = rows;
+  g.counts = counts.data_ptr<int>();
+  g.offsets = offsets.data_ptr<int>();
+  g.groups = El;
+  g.N = I2;
+  g.K = H;
+  g.max_rows_per_group = (int)max_rows_per_group;
+  g.swiglu = true;
+  g.swiglu_limit = (float)swiglu_limit;
+  g.out = mbf(y1);
+  g.ldo = I;
+  g.status = status_dev_ptr();
+  grouped_gemm_w8(g, st);
+  g.W = down8.data_ptr<uint8_t>();
+  g.scales16 = down_s16.data_ptr<float>();
+  g.X = y1.data_ptr();
+  g.N = H;
+  g.K = I;
+  g.swiglu = false;
+  g.swiglu_limit = 0.f;
+  g.out = mbf(y2);
+  g.ldo = H;
+  grouped_gemm_w8(g, st);
+  return y2;
+}
+
 // Router-weighted sum of per-(token, slot) expert outputs y[pos_of[t*k+j]]
 // (+ the sigmoid-gated shared expert).
 Tensor moe_combine_op(const Tensor& y, const Tensor& w, const Tensor& pos_of, const c10::optional<Tensor>& shared_y,
@@ -578,6 +634,9 @@ void register_ext_defs(torch::Library& m) {
       "moe_experts(Tensor x, Tensor w, Tensor ids, Tensor gate_up, Tensor down, int e0, Tensor? shared_y, "
       "Tensor? shared_gate, float swiglu_limit) -> Tensor");
   m.def(
+      "moe_grouped_ffn_w8(Tensor x_perm, Tensor counts, Tensor offsets, Tensor gate_up8, Tensor gate_up_scales16, "
+      "Tensor down8, Tensor down_scales16, int max_rows_per_group, float swiglu_limit) -> Tensor");
+  m.def(
       "moe_experts_w8(Tensor x, Tensor w, Tensor ids, Tensor gate_up8, Tensor gate_up_scales16, Tensor down8, "
       "Tensor down_scales16, int e0, Tensor? shared_y, Tensor? shared_gate, float swiglu_limit) -> Tensor");
   m.def(
@@ -599,6 +658,7 @@ void register_ext_impls(torch::Library& m) {
   m.impl("moe_experts", &moe_experts_op);
   m.impl("moe_experts_w8", &moe_experts_w8_op);
   m.impl("moe_grouped_ffn", &moe_grouped_ffn_op);
+  m.impl("moe_grouped_ffn_w8", &moe_grouped_ffn_w8_op);
   m.impl("moe_combine", &moe_combine_op);
   m.impl("hc_pre", &hc_pre_op);
   m.impl("hc_post", &hc_post_op);

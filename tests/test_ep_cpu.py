@@ -1,5 +1,6 @@
 """Expert-parallel MoE baseline (host all-to-all with split sizes) on two gloo
-ranks equals the single-process MoE with every expert local."""
+ranks equals the single-process MoE with every expert local, with bf16 and
+with block-scaled fp8 experts."""
 import os
 import socket
 
@@ -47,7 +48,17 @@ def _rank(rank, port, q):
     local_gu, local_dn = gu_i[rank * El:(rank + 1) * El], dn[rank * El:(rank + 1) * El]
     out = nccl_ep_moe(Comm(None, rank, 2), x, w, ids, local_gu, local_dn, El)
     ref = R.moe_experts(x, w, ids, gu_i, dn, 0)
-    q.put((rank, float((out.float() - ref.float()).abs().max())))
+    err = float((out.float() - ref.float()).abs().max())
+    # block-scaled fp8 experts: each rank holds its slice of the quantized set
+    from bwn.io.fp8 import FP8Experts
+    gate, up = gu[:, :I].contiguous(), gu[:, I:].contiguous()
+    f_gu, f_dn = FP8Experts.quantize_gate_up(gate, up), FP8Experts.quantize(dn)
+    out8 = nccl_ep_moe(Comm(None, rank, 2), x, w, ids, f_gu.select(rank * El, (rank + 1) * El),
+                       f_dn.select(rank * El, (rank + 1) * El), El)
+    gq = f_gu.dequant().to(torch.bfloat16).float().reshape(E, I // 16, 2, 16, H)
+    ref8 = R.moe_experts(x, w, ids, torch.cat([gq[:, :, 0].reshape(E, I, H), gq[:, :, 1].reshape(E, I, H)], 1),
+                         f_dn.dequant().to(torch.bfloat16).float(), 0)
+    q.put((rank, max(err, float((out8.float() - ref8.float()).abs().max()))))
     dist.destroy_process_group()
 
 
