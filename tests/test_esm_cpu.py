@@ -2,7 +2,6 @@
 checkpoint/resume (config 1: ESM-2 8M on CPU fp32, b8 x s256)."""
 import os
 
-import pytest
 import torch
 
 from bwn.config import ESM2Config

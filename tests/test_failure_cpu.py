@@ -7,7 +7,6 @@ import subprocess
 import sys
 import time
 
-import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
