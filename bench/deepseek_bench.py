@@ -45,6 +45,8 @@ def main():
     ap.add_argument("--fp8", action="store_true", help="dense projections and LM head as 128x128 block-scaled E4M3")
     ap.add_argument("--fp8-experts", action="store_true", help="routed experts as block-scaled E4M3 (fp8 grouped GEMM)")
     ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--fused-comm", default="off", choices=["on", "off"],
+                    help="N>1: row-parallel wo_b GEMM and MoE partials reduced through the fused NVLS kernels")
     args = ap.parse_args()
     comm = init_distributed("nccl", timeout_s=600)
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -62,10 +64,13 @@ def main():
     model = DeepSeekV4Model(cfg, comm, dev).init_random_local(0)
     if args.fp8 or args.fp8_experts:
         model.quantize_fp8(include_head=args.fp8, experts=args.fp8_experts)
+    if args.fused_comm == "on" and comm.size > 1:
+        from bwn.parallel.fused import enable_fused_comm
+        enable_fused_comm(model)
     torch.cuda.synchronize()
     note("weights ready")
     res = {"model": cfg.name + (f"-{args.layers}L (debug)" if args.layers else ""), "n_gpus": comm.size,
-           "parallelism": f"tp{comm.size}+ep{comm.size}",
+           "parallelism": f"tp{comm.size}+ep{comm.size}", "comm": "fused NVLS" if model.fused_comm else "NCCL",
            "dtype": "bf16 activations" + (", fp8 dense weights" if args.fp8 else "") +
                     (", fp8 routed experts" if args.fp8_experts else ""),
            "data": "synthetic (uniform-random prompt ids, random-init weights)",

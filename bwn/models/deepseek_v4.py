@@ -147,6 +147,7 @@ class DeepSeekV4Model:
         self.L: list[dict] = []
         self.g: dict = {}
         self.ones_hd = torch.ones(cfg.head_dim, device=self.device)
+        self.fused_comm = None  # set by bwn.parallel.fused.enable_fused_comm
 
     # ------------------------------------------------------------------ load
     def load(self, sd: dict, presharded: bool = False) -> "DeepSeekV4Model":
@@ -311,6 +312,9 @@ class DeepSeekV4Model:
         hpg = cfg.n_heads // cfg.o_groups
         og = o.view(T, self.groups, hpg * hd)
         lora = torch.cat([O.linear(og[:, g].contiguous(), L["wo_a"][g]) for g in range(self.groups)], dim=-1)
+        fc = self.fused_comm
+        if fc is not None and fc.fits(T):  # row-parallel GEMM -> NVLS all-reduce (fused path F1)
+            return fc.gemm_allreduce(lora, L["wo_b"])
         return self._allreduce(O.linear(lora, L["wo_b"]))
 
     def _moe(self, L, x, li: int):
@@ -322,6 +326,9 @@ class DeepSeekV4Model:
         shared = O.linear(O.linear_swiglu(x, L["shared_gate_up"]), L["shared_down"])
         y = (routed.float() + shared.float()).to(x.dtype)
         if self.ep > 1:
+            fc = self.fused_comm
+            if fc is not None and self.ep_comm is self.comm and fc.fits(y.shape[0]):
+                return fc.allreduce(y)
             self.ep_comm.all_reduce_(y)
         return y
 

@@ -77,6 +77,27 @@ class FusedComm:
         return o.ar_add_norm(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
                              x, norm_w, eps, self.timeout_s)
 
+    def _zero_norm(self, cols: int, dev) -> torch.Tensor:
+        w = getattr(self, "_nw0", None)
+        if w is None or w.numel() != cols:
+            w = self._nw0 = torch.zeros(cols, dtype=torch.float32, device=dev)
+        return w
+
+    def allreduce(self, part: torch.Tensor) -> torch.Tensor:
+        """Sum of every rank's ``part [rows, hidden]`` through the one-shot NVLS
+        reduction (the fused add-norm kernel accumulating into a zeroed residual;
+        its normed output is not used)."""
+        acc = torch.zeros_like(part)
+        self.allreduce_add_norm(part, acc, self._zero_norm(part.shape[1], part.device), 1e-6)
+        return acc
+
+    def gemm_allreduce(self, a: torch.Tensor, w) -> torch.Tensor:
+        """``all_reduce(a @ w.T)``: the row-parallel GEMM writes its partial into
+        this rank's symmetric slot and the reduction reads it through NVLS."""
+        acc = torch.zeros(a.shape[0], w.shape[0], dtype=torch.bfloat16, device=a.device)
+        self.gemm_allreduce_add_norm(a, w, acc, self._zero_norm(w.shape[0], a.device), 1e-6)
+        return acc
+
     def greedy(self, keys: torch.Tensor) -> torch.Tensor:
         return ops().greedy_allmax(keys.contiguous(), self.peer_slots, self.peer_flags_g,
                                    self.peer_flags_g[self.rank], self.state, self.rank, self.timeout_s)
@@ -84,9 +105,12 @@ class FusedComm:
 
 def enable_fused_comm(model, max_rows: int = 256) -> FusedComm:
     """Route the model's row-parallel reductions and greedy through the fused
-    NVLink kernels (decode-sized batches); larger batches keep NCCL."""
+    NVLink kernels (decode-sized batches); larger batches keep NCCL.  Works for
+    :class:`~bwn.models.qwen36.Qwen36Model` (``cfg.hidden``) and
+    :class:`~bwn.models.deepseek_v4.DeepSeekV4Model` (``cfg.dim``)."""
     if model.comm.size <= 1:
         raise RuntimeError("fused comm needs more than one rank")
-    fc = FusedComm(model.comm, model.cfg.hidden, max_rows, model.device)
+    hidden = getattr(model.cfg, "hidden", None) or model.cfg.dim
+    fc = FusedComm(model.comm, hidden, max_rows, model.device)
     model.fused_comm = fc
     return fc

@@ -58,3 +58,68 @@ def test_deepseek_hybrid_tp2_ep2():
     for r in range(4):
         assert isinstance(res[r], float), res[r]
         assert res[r] < 1e-4, res
+
+
+class _FakeFused:
+    """Stands in for bwn.parallel.fused.FusedComm on gloo: same interface, the
+    reduction through the process group; counts the calls."""
+
+    def __init__(self, comm):
+        self.comm, self.calls = comm, {"gemm_allreduce": 0, "allreduce": 0}
+
+    def fits(self, rows):
+        return rows <= 256
+
+    def gemm_allreduce(self, a, w):
+        self.calls["gemm_allreduce"] += 1
+        return self.comm.all_reduce_(a.float() @ w.float().t())
+
+    def allreduce(self, part):
+        self.calls["allreduce"] += 1
+        return self.comm.all_reduce_(part.clone())
+
+
+def _fused_rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.set_num_threads(2)
+        from bwn.config import tiny_deepseek_v4
+        from bwn.models.deepseek_v4 import DeepSeekV4Model, synthetic_checkpoint
+        from bwn.parallel.comm import Comm
+        cfg = tiny_deepseek_v4()
+        sd = synthetic_checkpoint(cfg, 0)
+        comm = Comm(None, rank, world)
+        plain = DeepSeekV4Model(cfg, comm, "cpu", torch.float32).load(sd)
+        fused = DeepSeekV4Model(cfg, comm, "cpu", torch.float32).load(sd)
+        fused.fused_comm = _FakeFused(comm)
+        toks = torch.randint(0, cfg.vocab, (2, 6), generator=torch.Generator().manual_seed(5))
+        outs = []
+        for m in (plain, fused):
+            st = m.new_state(2, 16)
+            pos = torch.arange(6, dtype=torch.int32).repeat(2)
+            bidx = torch.arange(2, dtype=torch.int32).repeat_interleave(6)
+            outs.append(m.forward_tokens(toks.reshape(-1), pos, bidx, st, 6))
+        q.put((rank, float((outs[0] - outs[1]).abs().max()), fused.fused_comm.calls, cfg.num_layers))
+    except Exception:  # noqa: BLE001
+        import traceback
+        q.put((rank, traceback.format_exc(), None, 0))
+    dist.destroy_process_group()
+
+
+def test_deepseek_fused_comm_hooks_two_ranks():
+    """With a fused communicator attached, each layer reduces its attention
+    output projection and its MoE partial through it, with the same result."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_fused_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=240) for _ in range(2)]
+    for p in ps:
+        p.join(30)
+    for rank, err, calls, layers in res:
+        assert not isinstance(err, str), err
+        assert err < 1e-4, (rank, err)
+        assert calls == {"gemm_allreduce": layers, "allreduce": layers}, calls
