@@ -150,17 +150,19 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     const int r = c >> 1, half = c & 1;
     int s = 0, sc2 = 0;
     uint32_t ph = 0, ph2 = 0;
-    for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      // all 256 converter threads leave together after an abort (the named
+      // barrier below needs every one of them)
+      if (bar_any(2, 256, *abort_flag != 0)) break;
       const int tile = u / args.splits, sp = u % args.splits;
       const int tm = tile % args.tiles_m;
       const int kb0 = sp * args.kb_per_split, kb1 = min(args.num_kb, kb0 + args.kb_per_split);
       // stage this unit's block scales once (a per-block global load would put
       // an L2 round trip in front of every conversion)
-      asm volatile("bar.sync 2, 256;" ::: "memory");
       for (int j = c; j < kb1 - kb0; j += 256) s_scale[j] = scales[(long)tm * lds + kb0 + j];
       asm volatile("bar.sync 2, 256;" ::: "memory");
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&full_bar[s], ph) || !mbar_wait(&empty_bar[sc2], ph2 ^ 1)) {
+        if (*abort_flag || !mbar_wait(&full_bar[s], ph) || !mbar_wait(&empty_bar[sc2], ph2 ^ 1)) {
           set_status(args.status, kStatusMbarTimeout);
           *abort_flag = 1;
           break;

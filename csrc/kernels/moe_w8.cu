@@ -66,21 +66,6 @@ __device__ __forceinline__ void e4m3x4_to_f16x4_g(uint32_t v, uint32_t& lo, uint
       : "r"(v));
 }
 
-// OR of a predicate over the threads of named barrier ``id`` (``n`` threads):
-// a decision every converter thread takes the same way
-__device__ __forceinline__ bool bar_any(int id, int n, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(n)
-      : "memory");
-  return r != 0;
-}
-
 // f16x2 (exact fp8 values) * scale -> bf16x2
 __device__ __forceinline__ uint32_t scale_to_bf16x2(uint32_t h2, float s) {
   const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
