@@ -286,6 +286,28 @@ def qwen36_from_hf(path_or_dict: str | dict) -> Qwen36Config:
     return Qwen36Config(**kw)
 
 
+def qwen36_to_hf(cfg: Qwen36Config) -> dict:
+    """The HF ``config.json`` fields :func:`qwen36_from_hf` reads (for writing
+    checkpoints this framework can load back)."""
+    d = {
+        "model_type": cfg.name, "num_hidden_layers": cfg.num_layers, "hidden_size": cfg.hidden,
+        "vocab_size": cfg.vocab, "rms_norm_eps": cfg.rms_eps, "full_attention_interval": cfg.full_attn_interval,
+        "linear_num_key_heads": cfg.dn_k_heads, "linear_num_value_heads": cfg.dn_v_heads,
+        "linear_key_head_dim": cfg.dn_k_dim, "linear_value_head_dim": cfg.dn_v_dim,
+        "linear_conv_kernel_dim": cfg.conv_kernel, "num_attention_heads": cfg.q_heads,
+        "num_key_value_heads": cfg.kv_heads, "head_dim": cfg.head_dim,
+        "rope_parameters": {"rope_type": "default", "rope_theta": cfg.rope_theta,
+                            "partial_rotary_factor": cfg.partial_rotary},
+        "tie_word_embeddings": cfg.tie_embeddings, "norm_topk_prob": cfg.norm_topk_prob,
+    }
+    if cfg.num_experts:
+        d.update(num_experts=cfg.num_experts, num_experts_per_tok=cfg.top_k, moe_intermediate_size=cfg.moe_inter,
+                 shared_expert_intermediate_size=cfg.shared_inter)
+    else:
+        d["intermediate_size"] = cfg.intermediate
+    return d
+
+
 @dataclass(frozen=True)
 class DeepSeekV4Config:
     """DeepSeek V4 Flash dims (``run_deepseek_v4_tp.py:40-81``).

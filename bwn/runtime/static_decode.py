@@ -104,3 +104,107 @@ class StaticDecoder:
             out.append(self.next_ids.clone())
         check_status("generate")
         return torch.stack(out, 1)
+
+
+def main(argv=None) -> None:
+    """Greedy generation from the command line (the reference harness's
+    ``main``: ``--prompt-ids`` coherence runs, ``--tiny`` random models, gen
+    hash, prefill fingerprint and occupancy gates; ``contrib/qwen3.6-35b-a3b/
+    static_decode_35b.py:2967-3530``, ``contrib/qwen3.6-27b/static_decode.py:1060-1479``).
+    One process per GPU under torchrun for tensor parallelism.
+
+        python -m bwn.runtime.static_decode --checkpoint HF_DIR --prompt-ids 760,6511,314,9338,369 --max-new 32
+        python -m bwn.runtime.static_decode --model tiny --cpu --batch 2 --prompt-len 16
+    """
+    import argparse
+    import json
+    import time
+
+    from ..config import QWEN36_27B, QWEN36_35B_A3B, tiny_qwen36
+    from ..models.qwen36 import build_qwen36, from_pretrained
+    from ..parallel.comm import init_distributed
+    from ..utils import fingerprint as F
+
+    ap = argparse.ArgumentParser(description="static greedy decode")
+    ap.add_argument("--model", default="tiny", choices=["27b", "35b", "tiny", "tiny-moe"])
+    ap.add_argument("--checkpoint", default="", help="HF safetensors directory (config.json beside it)")
+    ap.add_argument("--layers", type=int, default=0, help="truncate to this many layers (random models)")
+    ap.add_argument("--prompt-ids", default="", help="comma-separated prompt token ids (every row)")
+    ap.add_argument("--prompt-len", type=int, default=16, help="uniform-random prompt length without --prompt-ids")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--max-new", type=int, default=16)
+    ap.add_argument("--bucket", type=int, default=0, help="prefill chunk length (0: whole prompt)")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--fp8", action="store_true", help="W8A16 projection weights")
+    ap.add_argument("--fused-comm", action="store_true", help="N>1: fused NVLink reductions")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--cpu", action="store_true")
+    a = ap.parse_args(argv)
+
+    cpu = a.cpu or not torch.cuda.is_available()
+    comm = init_distributed("gloo" if cpu else "nccl")
+    dev = torch.device("cpu") if cpu else torch.device("cuda", torch.cuda.current_device())
+    dtype = torch.float32 if cpu else torch.bfloat16
+    if a.checkpoint:
+        model = from_pretrained(a.checkpoint, comm, dev, dtype)
+    else:
+        cfg = {"27b": QWEN36_27B, "35b": QWEN36_35B_A3B, "tiny": tiny_qwen36(),
+               "tiny-moe": tiny_qwen36(moe=True)}[a.model]
+        if a.layers:
+            cfg = cfg.scaled(num_layers=a.layers)
+        model = build_qwen36(cfg, comm, dev, seed=a.seed, dtype=dtype)
+    if a.fp8:
+        model.quantize_fp8()
+    if a.fused_comm and comm.size > 1:
+        from ..parallel.fused import enable_fused_comm
+        enable_fused_comm(model)
+    cfg = model.cfg
+    if a.prompt_ids:
+        ids = [int(t) for t in a.prompt_ids.split(",") if t.strip()]
+        prompt = torch.tensor([ids] * a.batch, dtype=torch.long)
+    else:
+        prompt = torch.randint(0, cfg.vocab, (a.batch, a.prompt_len), generator=torch.Generator().manual_seed(a.seed))
+    S = prompt.shape[1]
+    dec = StaticDecoder(model, a.batch, S + a.max_new + 8, use_graph=not a.no_graph)
+    dec.capture()
+
+    def sync():
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+
+    sync()
+    t0 = time.perf_counter()
+    bucket = a.bucket or S
+    for c0 in range(0, S, bucket):  # bucketed prefill; the last chunk's hidden gives the logits
+        last = model.prefill_hidden(prompt[:, c0:c0 + bucket].to(dev), dec.st, None)
+    logits = model.logits(last)
+    first = model.greedy(last)
+    dec.tokens.copy_(first.to(dec.tokens.dtype))
+    sync()
+    ttft = (time.perf_counter() - t0) * 1e3
+    out = [first.cpu()]
+    t1 = time.perf_counter()
+    for _ in range(a.max_new - 1):
+        dec.step_device()
+        out.append(dec.next_ids.clone().cpu())
+    sync()
+    tpot = (time.perf_counter() - t1) * 1e3 / max(1, a.max_new - 1)
+    check_status("static_decode")
+    gen = torch.stack(out, 1)
+    occupancy = F.check_qwen36_state(dec.st, f"decode state rank={comm.rank}")
+    if comm.rank == 0:
+        print(json.dumps({
+            "model": cfg.name, "tp": comm.size, "batch": a.batch, "prompt_len": S,
+            "generated_row0": gen[0].tolist(), "gen_hash_row0": F.gen_hash(gen[0]),
+            "prefill_fingerprint": F.logits_fingerprint(logits.float().cpu()),
+            "ttft_ms": round(ttft, 2), "tpot_ms": round(tpot, 3),
+            "occupied_ssm_layers": len(occupancy["ssm"]), "graph": dec.graph is not None}))
+    dec.release()
+    if comm.size > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,54 @@
+"""The static-decode command (the reference harness's main): generated ids,
+gen hash and prefill fingerprint are the same for whole and bucketed prefill
+and for one process and two tensor-parallel gloo ranks; a checkpoint
+directory with --prompt-ids runs the same path."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ENV = dict(os.environ, PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
+BASE = ["-m", "bwn.runtime.static_decode", "--model", "tiny", "--cpu", "--batch", "2", "--prompt-len", "12",
+        "--max-new", "6"]
+
+
+def _run(args):
+    r = subprocess.run([sys.executable] + args, env=ENV, cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1])
+
+
+def test_whole_bucketed_and_two_ranks_agree():
+    one = _run(BASE)
+    assert one["prefill_fingerprint"]["finite"] and len(one["generated_row0"]) == 6
+    assert _run(BASE + ["--bucket", "5"])["gen_hash_row0"] == one["gen_hash_row0"]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    two = _run(["-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                "--master-port", str(port)] + BASE)
+    assert two["tp"] == 2 and two["gen_hash_row0"] == one["gen_hash_row0"]
+    assert two["prefill_fingerprint"]["top5"] == one["prefill_fingerprint"]["top5"]
+
+
+def test_checkpoint_with_prompt_ids(tmp_path):
+    from bwn.config import qwen36_from_hf, qwen36_to_hf, tiny_qwen36
+    from bwn.io import qwen36_weights as W
+    from bwn.io.safetensors import save_file
+    cfg = tiny_qwen36()
+    sd = dict(W.synthetic_hf_globals(cfg, 2, "cpu"))
+    for i in range(cfg.num_layers):
+        sd.update(W.synthetic_hf_layer(cfg, i, 2, "cpu"))
+    save_file({"model." + k if k != "lm_head.weight" else k: v.contiguous() for k, v in sd.items()},
+              str(tmp_path / "model.safetensors"))
+    (tmp_path / "config.json").write_text(json.dumps(qwen36_to_hf(cfg)))
+    assert qwen36_from_hf(str(tmp_path)) == cfg
+    out = _run(["-m", "bwn.runtime.static_decode", "--checkpoint", str(tmp_path), "--cpu", "--prompt-ids",
+                "7,11,13,17,19", "--max-new", "4"])
+    assert out["prompt_len"] == 5 and len(out["generated_row0"]) == 4
+    assert torch.tensor(out["generated_row0"]).max() < cfg.vocab
