@@ -373,3 +373,97 @@ class DeepSeekV4Model:
         h = self.forward_tokens(tokens.to(self.device), st.positions, bidx, st, 1)
         st.positions.add_(1)
         return self.logits(h).argmax(-1).int()
+
+
+def main(argv=None) -> None:
+    """The runner command (``contrib/deepseek-v4-flash/run_deepseek_v4_tp.py:730-907``
+    and its hybrid / tiny twins): load a checkpoint (HF-layout safetensors, or
+    the per-rank files of :func:`bwn.io.deepseek_weights.preprocess`) or a
+    random tiny model, prefill a prompt, greedy-decode ``--max-new`` tokens;
+    prints TTFT, decode tok/s, the ids and a NaN check.  One process per GPU
+    under torchrun; ``--hybrid-tp N`` splits the world into TP groups of N and
+    EP groups strided by N.
+
+        torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m bwn.models.deepseek_v4 --checkpoint DIR
+        python -m bwn.models.deepseek_v4 --tiny --cpu --max-new 8
+    """
+    import argparse
+    import json
+    import time
+
+    import torch.distributed as dist
+
+    from ..config import deepseek_v4_from_hf, tiny_deepseek_v4
+    from ..ops import check_status
+    from ..parallel.comm import hybrid_groups, init_distributed
+
+    ap = argparse.ArgumentParser(description="DeepSeek V4 greedy generation")
+    ap.add_argument("--checkpoint", default="", help="checkpoint directory (config.json beside the weights)")
+    ap.add_argument("--presharded", action="store_true", help="per-rank files from bwn.io.deepseek_weights")
+    ap.add_argument("--tiny", action="store_true", help="random tiny model instead of a checkpoint")
+    ap.add_argument("--prompt-ids", default="", help="comma-separated prompt ids (random when empty)")
+    ap.add_argument("--prompt-len", type=int, default=32)
+    ap.add_argument("--max-new", type=int, default=8)
+    ap.add_argument("--max-cache", type=int, default=128)
+    ap.add_argument("--hybrid-tp", type=int, default=0)
+    ap.add_argument("--fp8", action="store_true")
+    ap.add_argument("--cpu", action="store_true")
+    a = ap.parse_args(argv)
+
+    cpu = a.cpu or not torch.cuda.is_available()
+    comm = init_distributed("gloo" if cpu else "nccl")
+    dev = torch.device("cpu") if cpu else torch.device("cuda", torch.cuda.current_device())
+    dtype = torch.float32 if cpu else torch.bfloat16
+    ep_comm = None
+    if a.hybrid_tp and comm.size > 1:
+        comm, ep_comm = hybrid_groups(a.hybrid_tp)
+    if a.checkpoint and not a.tiny:
+        cfg = deepseek_v4_from_hf(a.checkpoint)
+        model = DeepSeekV4Model(cfg, comm, dev, dtype, ep_comm=ep_comm)
+        model.load_checkpoint(a.checkpoint, a.presharded or None)
+    else:
+        cfg = tiny_deepseek_v4()
+        model = DeepSeekV4Model(cfg, comm, dev, dtype, ep_comm=ep_comm).init_random(0)
+    if a.fp8:
+        model.quantize_fp8()
+    if a.prompt_ids:
+        prompt = torch.tensor([[int(t) for t in a.prompt_ids.split(",") if t.strip()]])
+    else:
+        prompt = torch.randint(0, cfg.vocab, (1, a.prompt_len), generator=torch.Generator().manual_seed(0))
+    S = prompt.shape[1]
+    max_gen = min(a.max_new, a.max_cache - S)
+    st = model.new_state(1, a.max_cache)
+
+    def sync():
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+
+    sync()
+    t0 = time.perf_counter()
+    nxt = model.prefill(prompt.to(dev), st)
+    sync()
+    ttft = time.perf_counter() - t0
+    ids = [int(nxt[0])]
+    t1 = time.perf_counter()
+    for _ in range(max_gen - 1):
+        nxt = model.decode_step(nxt, st)
+        ids.append(int(nxt[0]))
+    sync()
+    dt = time.perf_counter() - t1
+    check_status("deepseek generate")
+    h = model.forward_tokens(nxt.to(dev), st.positions, torch.zeros(1, dtype=torch.int32, device=dev), st, 1)
+    finite = bool(torch.isfinite(model.logits(h)).all())
+    multi = dist.is_available() and dist.is_initialized()
+    if (dist.get_rank() if multi else 0) == 0:
+        print(json.dumps({"model": cfg.name, "world": dist.get_world_size() if multi else 1,
+                          "tp": model.tp, "ep": model.ep, "prompt_len": S, "generated": ids,
+                          "ttft_s": round(ttft, 3),
+                          "decode_tok_s": round((len(ids) - 1) / dt, 2) if len(ids) > 1 and dt > 0 else None,
+                          "finite": finite}))
+    if multi:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -121,3 +121,38 @@ def test_fp8_experts_close_to_bf16():
         hs.append(m.logits(m.forward_tokens(toks.reshape(-1), pos, bidx, st, 8)))
     rel = float((hs[0] - hs[1]).norm() / hs[0].norm())
     assert 0 < rel < 0.1
+
+
+def test_runner_command_single_tp2_and_hybrid():
+    """The runner command generates the same ids on one process, two
+    tensor-parallel gloo ranks and two ranks in the hybrid layout (TP 1 x EP 2)."""
+    import json
+    import socket
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PYTHONPATH=root, OMP_NUM_THREADS="2")
+    args = ["-m", "bwn.models.deepseek_v4", "--tiny", "--cpu", "--max-new", "5", "--prompt-len", "9"]
+
+    def run(pre):
+        r = subprocess.run([sys.executable] + pre + args + extra, env=env, cwd=root, capture_output=True,
+                           text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-3000:]
+        return json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1])
+
+    def torchrun():
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+        s.close()
+        return ["-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                "--master-port", str(port)]
+
+    extra = []
+    one = run([])
+    assert one["finite"] and len(one["generated"]) == 5
+    tp2 = run(torchrun())
+    extra = ["--hybrid-tp", "1"]
+    hyb = run(torchrun())
+    assert (tp2["tp"], tp2["ep"], hyb["tp"], hyb["ep"]) == (2, 2, 1, 2)
+    assert tp2["generated"] == one["generated"] == hyb["generated"]
