@@ -59,3 +59,25 @@ def test_esm_fsdp_two_ranks():
     for r in (0, 1):
         assert isinstance(res[r], float), res[r]
         assert res[r] < 1e-5, res
+
+
+def test_fsdp_command_two_ranks(tmp_path):
+    """The FSDP training command on two gloo ranks under torchrun."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(port), "-m", "bwn.train.esm_fsdp",
+                        "--model-size", "8M", "--cpu", "--num-steps", "3", "--max-seq-len", "32"],
+                       env=dict(os.environ, PYTHONPATH=root, OMP_NUM_THREADS="2"), cwd=root, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    ev = [json.loads(ln) for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert ev[0]["world"] == 2 and ev[-1]["event"] == "done" and ev[-1]["steps"] == 3
+    assert all(e["loss"] > 0 for e in ev if e["event"] == "step")
