@@ -97,6 +97,8 @@ def enable_ep_all_to_all(model, max_tokens_per_rank: int = 512, min_tokens_per_r
     cfg, comm = model.cfg, model.comm
     if not cfg.is_moe or comm.size <= 1:
         raise RuntimeError("expert-parallel all-to-all needs a MoE model on more than one rank")
+    from .topology import require_single_domain
+    require_single_domain(comm, "expert-parallel all-to-all")
     if model.d.moe_sharding != "ep":
         raise RuntimeError("the expert-parallel all-to-all needs experts partitioned across ranks (moe_sharding='ep')")
     ep = EPAllToAll(comm, cfg.hidden, cfg.num_experts, cfg.top_k, max_tokens_per_rank, device=model.device)

@@ -110,6 +110,8 @@ def enable_fused_comm(model, max_rows: int = 256) -> FusedComm:
     :class:`~bwn.models.deepseek_v4.DeepSeekV4Model` (``cfg.dim``)."""
     if model.comm.size <= 1:
         raise RuntimeError("fused comm needs more than one rank")
+    from .topology import require_single_domain
+    require_single_domain(model.comm, "fused comm")
     hidden = getattr(model.cfg, "hidden", None) or model.cfg.dim
     fc = FusedComm(model.comm, hidden, max_rows, model.device)
     model.fused_comm = fc

@@ -132,6 +132,8 @@ class GradReducer(_HookedReducer):
     FLAG_BYTES = 256  # per bucket: 2 phases x 8 ranks x 4 bytes, padded
 
     def __init__(self, model, comm, bucket_mb: float = 32.0, timeout_s: float = 30.0):
+        from .topology import require_single_domain
+        require_single_domain(comm, "fused gradient reduction")
         super().__init__(model, comm, bucket_mb, align=8 * comm.size)
         self.timeout_s = timeout_s
         self.rank = comm.rank

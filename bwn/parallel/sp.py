@@ -74,6 +74,8 @@ def enable_sequence_parallel(model, max_tokens: int) -> SeqParallel:
     ``128 * world``) prefill sequence-parallel; other calls keep the replicated path."""
     if model.comm.size <= 1:
         raise RuntimeError("sequence parallelism needs more than one rank")
+    from .topology import require_single_domain
+    require_single_domain(model.comm, "sequence-parallel prefill")
     sp = SeqParallel(model.comm, model.cfg.hidden, max_tokens, model.device)
     model.seq_parallel = sp
     return sp

@@ -6,7 +6,8 @@ the question is which data paths the comm layer may use: peer access between
 every pair (NVLink through NVSwitch), and NVLink multicast (NVLS) for
 ``multimem`` reductions.  :func:`probe` answers from the CUDA runtime; the
 decision function :func:`choose_comm_path` is pure so it is tested on CPU with
-fake topologies.
+fake topologies.  :func:`require_single_domain` is the check every fused path
+runs when it is enabled: a group spanning hosts (a multi-node job) keeps NCCL.
 """
 from __future__ import annotations
 
@@ -57,3 +58,26 @@ def choose_comm_path(topo: Topology, world: int, requested: str = "auto") -> str
             raise RuntimeError("fused comm requested but the ranks' GPUs lack peer access to one another")
         return "nccl"
     return "fused_nvls" if topo.multicast else "fused_p2p"
+
+
+def hosts_of(comm) -> list[str]:
+    """Host name of every rank of ``comm`` (collective over the group)."""
+    import socket
+
+    import torch.distributed as dist
+    name = socket.gethostname()
+    if comm.size <= 1 or not dist.is_initialized():
+        return [name]
+    out = [None] * comm.size
+    dist.all_gather_object(out, name, group=comm.group)
+    return out
+
+
+def require_single_domain(comm, what: str) -> None:
+    """The fused kernels address peers' memory directly, so every rank of the
+    group must sit in one NVLink / NVSwitch domain (one host here).  Raises
+    otherwise (callers fall back to NCCL)."""
+    hosts = hosts_of(comm)
+    if len(set(hosts)) > 1:
+        raise RuntimeError(f"{what}: the group spans hosts {sorted(set(hosts))}; peer-memory kernels need one "
+                           "NVLink domain (NCCL is used instead)")

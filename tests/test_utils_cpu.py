@@ -130,3 +130,15 @@ def test_every_layer_state_changes_every_step():
     st.positions.add_(1)  # a step that wrote nothing
     with pytest.raises(RuntimeError, match="was not written"):
         F.assert_state_advanced(snap, st)
+
+
+def test_single_domain_check(monkeypatch):
+    """Fused peer-memory paths refuse a group whose ranks sit on different hosts."""
+    from bwn.parallel import topology as T
+    from bwn.parallel.comm import Comm
+    assert len(T.hosts_of(Comm.single())) == 1
+    monkeypatch.setattr(T, "hosts_of", lambda comm: ["node-a", "node-a"])
+    T.require_single_domain(Comm(None, 0, 2), "x")  # one host: fine
+    monkeypatch.setattr(T, "hosts_of", lambda comm: ["node-a", "node-b"])
+    with pytest.raises(RuntimeError, match="spans hosts"):
+        T.require_single_domain(Comm(None, 0, 2), "fused comm")
