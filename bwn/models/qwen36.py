@@ -357,6 +357,27 @@ class Qwen36Model(nn.Module):
             self.comm.all_reduce_max_(key)
         return O.unpack_argmax(key)
 
+    def sample(self, h: torch.Tensor, temperature: torch.Tensor, generator: torch.Generator | None = None
+               ) -> torch.Tensor:
+        """Temperature sampling on the vocab-sharded head by the Gumbel-max
+        trick: ``argmax(logits / T + G)`` with iid standard Gumbel noise ``G`` is
+        an exact sample of ``softmax(logits / T)``, so each rank perturbs only
+        its own vocab shard and the same packed int64 max all-reduce as
+        :meth:`greedy` picks the token.  ``temperature [B]`` (fp32, on the
+        device; rows with T = 0 get exactly :meth:`greedy`'s token: the same
+        head output, lowest id on ties)."""
+        logits = O.linear(h, self.g["lm_head"]).float()
+        t = temperature.float().reshape(-1, 1)
+        u = torch.rand(logits.shape, device=logits.device, generator=generator).clamp_(1e-20, 1.0)
+        noisy = torch.where(t > 0, logits / t.clamp_min(1e-6) - torch.log(-torch.log(u)), logits)
+        key = O.argmax_packed(noisy, self.d.vocab_offset)
+        fc = self.fused_comm
+        if fc is not None and fc.fits(key.shape[0]):
+            return fc.greedy(key)
+        if self.tp > 1:
+            self.comm.all_reduce_max_(key)
+        return O.unpack_argmax(key)
+
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         """Full-vocab logits (gathered across vocab shards)."""
         local = O.linear_f32(h, self.g["lm_head"])

@@ -21,7 +21,12 @@ from ..ops import check_status
 
 
 class StaticDecoder:
-    def __init__(self, model, batch: int, max_seq: int, use_graph: bool = True, ssm_dtype=torch.float32):
+    """``sampling=True`` captures a step that samples each row at its entry of
+    ``self.temperature`` (Gumbel-max over the sharded head; rows at 0 are
+    greedy); the default step is greedy."""
+
+    def __init__(self, model, batch: int, max_seq: int, use_graph: bool = True, ssm_dtype=torch.float32,
+                 sampling: bool = False, seed: int = 0):
         self.model = model
         self.batch = batch
         self.max_seq = max_seq
@@ -29,6 +34,13 @@ class StaticDecoder:
         dev = model.device
         self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.next_ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.sampling = sampling
+        self.temperature = torch.zeros(batch, dtype=torch.float32, device=dev)
+        # the default generator of the device (graph-safe under capture); a
+        # separate one on the CPU keeps host runs reproducible
+        self.gen = torch.Generator().manual_seed(seed) if dev.type == "cpu" else None
+        if dev.type == "cuda" and sampling:
+            torch.cuda.manual_seed(seed + getattr(model, "rank", 0))
         self.use_graph = use_graph and dev.type == "cuda"
         self.graph: torch.cuda.CUDAGraph | None = None
         self._host_in = torch.zeros(batch, dtype=torch.int32, pin_memory=dev.type == "cuda")
@@ -47,7 +59,10 @@ class StaticDecoder:
 
     # ----------------------------------------------------------------- step
     def _step_body(self) -> None:
-        ids = self.model.decode_step(self.tokens, self.st)
+        if self.sampling:
+            ids = self.model.sample(self.model.decode_hidden(self.tokens, self.st), self.temperature, self.gen)
+        else:
+            ids = self.model.decode_step(self.tokens, self.st)
         self.next_ids.copy_(ids)
         self.tokens.copy_(ids)
 

@@ -13,7 +13,10 @@ graph over ``max_batch`` static rows ("slots"):
   request reaches ``max_tokens`` or a stop id, and the next request can take
   it on the following step;
 * idle slots still ride in the fixed-shape step; their positions are pinned to
-  0 before each step so they never write past their cache rows.
+  0 before each step so they never write past their cache rows;
+* with ``sampling=True`` each slot samples at its request's temperature
+  (Gumbel-max on the sharded head, :meth:`~bwn.models.qwen36.Qwen36Model.sample`);
+  temperature 0 stays greedy.
 
 Greedy outputs are those of the request run alone (tested on CPU).
 """
@@ -46,12 +49,14 @@ def _row_view(st, r: int):
 
 
 class ContinuousEngine:
-    def __init__(self, model, max_batch: int, max_seq: int, use_graph: bool = True, bucket: int = 0):
+    def __init__(self, model, max_batch: int, max_seq: int, use_graph: bool = True, bucket: int = 0,
+                 sampling: bool = False, seed: int = 0):
         self.model = model
         self.max_batch = max_batch
         self.max_seq = max_seq
         self.bucket = bucket
-        self.dec = StaticDecoder(model, max_batch, max_seq, use_graph=use_graph)
+        self.sampling = sampling
+        self.dec = StaticDecoder(model, max_batch, max_seq, use_graph=use_graph, sampling=sampling, seed=seed)
         self.dec.capture()
         self.dev = model.device
         self.slots: list[_Slot | None] = [None] * max_batch
@@ -64,6 +69,8 @@ class ContinuousEngine:
         """Queue a request; returns its id."""
         if not req.prompt:
             raise ValueError("empty prompt")
+        if req.temperature > 0 and not self.sampling:
+            raise ValueError("temperature > 0 needs an engine built with sampling=True")
         if len(req.prompt) + req.max_tokens > self.max_seq:
             raise ValueError(f"prompt ({len(req.prompt)}) + {req.max_tokens} new tokens exceed max_seq {self.max_seq}")
         rid = next(self._ids)
@@ -116,7 +123,16 @@ class ContinuousEngine:
         st.reset(rows=[r])
         t0 = time.perf_counter()
         prompt = torch.tensor([req.prompt], dtype=torch.long, device=self.dev)
-        first = self.model.prefill(prompt, _row_view(st, r), None, self.bucket)
+        if self.sampling:
+            self.dec.temperature[r] = float(req.temperature)
+        if req.temperature > 0:  # the first token is sampled as well
+            view = _row_view(st, r)
+            S, bucket = prompt.shape[1], self.bucket or prompt.shape[1]
+            for c0 in range(0, S, bucket):
+                h = self.model.prefill_hidden(prompt[:, c0:c0 + bucket], view, None)
+            first = self.model.sample(h, self.dec.temperature[r:r + 1], self.dec.gen)
+        else:
+            first = self.model.prefill(prompt, _row_view(st, r), None, self.bucket)
         self.dec.tokens[r:r + 1].copy_(first.to(self.dec.tokens.dtype))
         tok = int(first[0])
         ms = (time.perf_counter() - t0) * 1e3

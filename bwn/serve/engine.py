@@ -23,6 +23,7 @@ class Request:
     prompt: list[int]
     max_tokens: int = 16
     stop: list[int] = field(default_factory=list)
+    temperature: float = 0.0  # 0: greedy; > 0: sampled (engines built with sampling=True)
 
 
 @dataclass
@@ -50,6 +51,8 @@ class GenerationEngine:
     def generate(self, reqs: list[Request]) -> list[Result]:
         if not reqs:
             return []
+        if any(r.temperature > 0 for r in reqs):
+            raise ValueError("the static-batch engine is greedy; sampling runs on the continuous scheduler")
         if len(reqs) > self.max_batch:
             out = []
             for i in range(0, len(reqs), self.max_batch):

@@ -29,6 +29,7 @@ class CompletionIn(BaseModel):
     prompt: list[int]
     max_tokens: int = 16
     stop: list[int] = []
+    temperature: float = 0.0
 
 
 class BatchingWorker:
@@ -155,7 +156,7 @@ def build_app(worker, model_name: str = "bwn"):
         if not body.prompt:
             raise HTTPException(400, "prompt must hold at least one token id")
         try:
-            out = worker.submit(Request(body.prompt, body.max_tokens, body.stop)).result(timeout=600)
+            out = worker.submit(Request(body.prompt, body.max_tokens, body.stop, body.temperature)).result(timeout=600)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
         return {"object": "text_completion", "model": model_name,
@@ -180,6 +181,7 @@ def main():
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--scheduler", default="continuous", choices=["continuous", "static"])
+    ap.add_argument("--sampling", action="store_true", help="continuous scheduler: honour request temperatures")
     a = ap.parse_args()
     import torch
     import uvicorn
@@ -194,7 +196,8 @@ def main():
         model = Qwen36Model(cfg, None, dev).init_random(0)
     if a.scheduler == "continuous":
         from .continuous import ContinuousEngine
-        worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda"))
+        worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda",
+                                                   sampling=a.sampling))
     else:
         worker = BatchingWorker(GenerationEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda"))
     uvicorn.run(build_app(worker, a.model), host=a.host, port=a.port)

@@ -111,3 +111,26 @@ def test_http_server_continuous_scheduler():
     assert client.post("/v1/completions", json={"prompt": [1] * 60, "max_tokens": 10}).status_code == 400
     assert "bwn_requests_total 4" in client.get("/metrics").text
     worker.stop()
+
+
+def test_continuous_sampling_engine():
+    """With sampling on, temperature-0 requests still equal solo greedy
+    generation and sampled requests are reproducible from the engine seed."""
+    from bwn.runtime.static_decode import StaticDecoder
+    from bwn.serve.continuous import ContinuousEngine
+    from bwn.serve.engine import Request
+    cfg = tiny_qwen36()
+    m = build_qwen36(cfg, seed=11, dtype=torch.float32)
+    p0, p1 = [5, 9, 13, 2], [7, 7, 1]
+    solo = StaticDecoder(m, 1, 32, use_graph=False).generate(torch.tensor([p0]), 5)[0].tolist()
+
+    def run(seed):
+        eng = ContinuousEngine(m, max_batch=2, max_seq=24, use_graph=False, sampling=True, seed=seed)
+        return eng.run([Request(p0, 5), Request(p1, 6, temperature=1.5)])
+
+    a, b = run(3), run(3)
+    assert a[0].tokens == solo
+    assert a[1].tokens == b[1].tokens and len(a[1].tokens) == 6
+    assert all(0 <= t < cfg.vocab for t in a[1].tokens)
+    with pytest.raises(ValueError):
+        ContinuousEngine(m, 2, 24, use_graph=False).add(Request(p0, 3, temperature=1.0))
