@@ -145,6 +145,18 @@ class SpecDecoder:
             x.copy_(y)
         torch.cuda.synchronize()
 
+    def reset(self) -> None:
+        """Back to the state of a fresh decoder (a new batch of prompts); the
+        captured graph stays valid (same buffers)."""
+        self.st.reset()
+        self.sp.pending.zero_()
+        self.sp.vstep.zero_()
+        self.tok.zero_()
+        self.out.fill_(-1)
+        self.n_out.zero_()
+        self.accepted_total.zero_()
+        self.steps = 0
+
     def _mutable(self):
         st, sp, ds = self.st, self.sp, self.dst
         return [st.conv, st.ssm, st.k_cache, st.v_cache, st.positions, sp.stash_qkv, sp.stash_ab, sp.pending,

@@ -8,7 +8,9 @@ framework).  Two schedulers:
   for a batch to fill) and runs each batch to completion through
   :class:`~bwn.serve.engine.GenerationEngine`;
 * ``continuous`` (:class:`ContinuousWorker`): requests join and leave the
-  running batch between decode steps (:class:`~bwn.serve.continuous.ContinuousEngine`).
+  running batch between decode steps (:class:`~bwn.serve.continuous.ContinuousEngine`);
+* ``spec``: EAGLE3 speculative decoding on batches of equal-length prompts
+  (:class:`~bwn.serve.spec.SpecEngine` behind the batching worker).
 
     python -m bwn.serve.server --model tiny --port 8000 --scheduler continuous
 """
@@ -180,7 +182,9 @@ def main():
     ap.add_argument("--max-seq", type=int, default=4096)
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
-    ap.add_argument("--scheduler", default="continuous", choices=["continuous", "static"])
+    ap.add_argument("--scheduler", default="continuous", choices=["continuous", "static", "spec"])
+    ap.add_argument("--draft", default="", help="spec: EAGLE3 draft safetensors directory (random 1-layer when empty)")
+    ap.add_argument("--num-draft", type=int, default=3, help="spec: draft tokens per step")
     ap.add_argument("--sampling", action="store_true", help="continuous scheduler: honour request temperatures")
     a = ap.parse_args()
     import torch
@@ -194,7 +198,19 @@ def main():
     else:
         cfg = {"tiny": tiny_qwen36(), "27b": QWEN36_27B, "35b": QWEN36_35B_A3B}[a.model]
         model = Qwen36Model(cfg, None, dev).init_random(0)
-    if a.scheduler == "continuous":
+    if a.scheduler == "spec":
+        from ..models.eagle3 import Eagle3Draft, eagle3_config
+        from .spec import SpecEngine
+        draft = Eagle3Draft(eagle3_config(model.cfg), dev, model.dtype)
+        if a.draft:
+            from ..io.checkpoint import Checkpoint
+            ck = Checkpoint(a.draft, prefix="")
+            draft.load({k: ck.raw(k) for k in ck.wm})
+        else:
+            draft.init_random(0)
+        worker = BatchingWorker(SpecEngine(model, draft, a.max_batch, a.max_seq, a.num_draft,
+                                           use_graph=dev == "cuda"))
+    elif a.scheduler == "continuous":
         from .continuous import ContinuousEngine
         worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda",
                                                    sampling=a.sampling))

@@ -134,3 +134,42 @@ def test_continuous_sampling_engine():
     assert all(0 <= t < cfg.vocab for t in a[1].tokens)
     with pytest.raises(ValueError):
         ContinuousEngine(m, 2, 24, use_graph=False).add(Request(p0, 3, temperature=1.0))
+
+
+def test_speculative_engine_matches_greedy():
+    """EAGLE3 speculative serving (random 1-layer draft, 4 drafts per step):
+    requests of mixed prompt lengths are grouped, and every request's tokens
+    equal its plain greedy generation, also when the decoder is reused."""
+    from bwn.models.eagle3 import Eagle3Draft, eagle3_config
+    from bwn.runtime.static_decode import StaticDecoder
+    from bwn.serve.engine import Request
+    from bwn.serve.spec import SpecEngine
+    cfg = tiny_qwen36()
+    m = build_qwen36(cfg, seed=11, dtype=torch.float32)
+    draft = Eagle3Draft(eagle3_config(cfg), "cpu", torch.float32).init_random(1)
+    g = torch.Generator().manual_seed(9)
+    reqs = [Request(torch.randint(0, cfg.vocab, (n,), generator=g).tolist(), max_tokens=t)
+            for n, t in [(6, 7), (6, 4), (9, 5), (6, 9)]]
+    solo = [StaticDecoder(m, 1, 48, use_graph=False).generate(torch.tensor([q.prompt]), q.max_tokens)[0].tolist()
+            for q in reqs]
+    eng = SpecEngine(m, draft, max_batch=2, max_seq=48, num_draft=4, use_graph=False)
+    assert [r.tokens for r in eng.generate(reqs)] == solo
+    assert [r.tokens for r in eng.generate(reqs[:2])] == solo[:2]  # decoder reuse after reset
+    assert eng.stats["batches"] == 4 and eng.stats["steps"] > 0  # (6,6) (6) (9), then (6,6)
+
+
+def test_http_server_spec_scheduler():
+    from fastapi.testclient import TestClient
+
+    from bwn.models.eagle3 import Eagle3Draft, eagle3_config
+    from bwn.serve.server import BatchingWorker, build_app
+    from bwn.serve.spec import SpecEngine
+    cfg = tiny_qwen36(layers=4)
+    model = build_qwen36(cfg, device="cpu", dtype=torch.float32)
+    draft = Eagle3Draft(eagle3_config(cfg), "cpu", torch.float32).init_random(0)
+    worker = BatchingWorker(SpecEngine(model, draft, 2, 64, 3, use_graph=False), batch_window_ms=2)
+    client = TestClient(build_app(worker, "tiny-eagle3"))
+    r = client.post("/v1/completions", json={"prompt": [5, 9, 13], "max_tokens": 6})
+    assert r.status_code == 200 and r.json()["choices"][0]["tokens"] == _greedy(model, [5, 9, 13], 6)
+    assert client.post("/v1/completions", json={"prompt": [5], "max_tokens": 3, "temperature": 1.0}).status_code == 400
+    worker.stop()
