@@ -173,3 +173,17 @@ def test_http_server_spec_scheduler():
     assert r.status_code == 200 and r.json()["choices"][0]["tokens"] == _greedy(model, [5, 9, 13], 6)
     assert client.post("/v1/completions", json={"prompt": [5], "max_tokens": 3, "temperature": 1.0}).status_code == 400
     worker.stop()
+
+
+def test_serve_bench_runs(capsys):
+    import importlib.util
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench", "serve_bench.py")
+    spec = importlib.util.spec_from_file_location("serve_bench", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.main(["--model", "tiny", "--cpu", "--concurrency", "1", "2", "--prompt-len", "8", "--max-tokens", "4"])
+    lines = [json.loads(ln) for ln in capsys.readouterr().out.splitlines() if ln.startswith("{")]
+    assert [x["concurrency"] for x in lines] == [1, 2]
+    assert all(x["output_tok_s"] > 0 and x["requests"] == 4 for x in lines)
