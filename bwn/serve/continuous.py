@@ -63,6 +63,8 @@ class ContinuousEngine:
         self.waiting: deque[tuple[int, Request]] = deque()
         self._ids = itertools.count()
         self.stats = {"admitted": 0, "finished": 0, "steps": 0}
+        self._idle_key: tuple = ()
+        self._idle_idx = None
 
     # ----------------------------------------------------------------- API
     def add(self, req: Request) -> int:
@@ -93,9 +95,11 @@ class ContinuousEngine:
         active = [r for r, s in enumerate(self.slots) if s is not None]
         if not active:
             return done
-        idle = [r for r in range(self.max_batch) if self.slots[r] is None]
+        idle = tuple(r for r in range(self.max_batch) if self.slots[r] is None)
         if idle:  # keep idle rows inside their caches
-            self.dec.st.positions[torch.tensor(idle, device=self.dev)] = 0
+            if idle != self._idle_key:  # the index tensor changes only when a slot fills or frees
+                self._idle_key, self._idle_idx = idle, torch.tensor(idle, device=self.dev)
+            self.dec.st.positions.index_fill_(0, self._idle_idx, 0)
         t0 = time.perf_counter()
         nxt = self.dec.step()  # device tokens already hold every slot's last id
         self.stats["steps"] += 1
