@@ -117,6 +117,45 @@ class Checkpoint:
             dns.append(self.get(p + "down_proj.weight"))
         return torch.stack(gus), torch.stack(dns)
 
+    def fp8_experts(self, layer_prefix: str, e0: int, e1: int, c0: int = 0, width: int | None = None):
+        """Official FP8 per-expert weights of experts ``[e0, e1)`` kept in fp8:
+        ``(gate_up, down)`` as :class:`~bwn.io.fp8.FP8Experts` (gate/up rows
+        interleaved in 16s with their own 128x128 block scales), no dequantize /
+        requantize round trip.  ``c0`` / ``width`` select a slice of every
+        expert's intermediate width (tensor parallelism within experts); a
+        slice must not straddle two 128-column scale blocks of ``down``."""
+        from .fp8 import FP8Experts, _scales16
+        m = layer_prefix + "mlp.experts."
+        g8s, u8s, g16, u16, d8s, d16 = [], [], [], [], [], []
+        for e in range(e0, e1):
+            p = f"{m}{e}."
+            parts = []
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                key = self.resolve(p + name + ".weight")
+                if self.tag(key) != "F8_E4M3":
+                    raise ValueError(f"{key} is not an FP8 weight")
+                parts.append((self.raw(key), self.raw(key + "_scale_inv").float()))
+            (g, gs), (u, us), (d, ds) = parts
+            I = g.shape[0]
+            w = I if width is None else width
+            if c0 % 16 or w % 16 or c0 + w > I:
+                raise ValueError(f"intermediate slice [{c0}, {c0 + w}) of {I} must follow 16-row groups")
+            if width is not None and c0 % 128 and (c0 % 128) + w > 128:
+                raise ValueError("the slice straddles two 128-column scale blocks of down_proj")
+            g8s.append(g[c0:c0 + w])
+            u8s.append(u[c0:c0 + w])
+            g16.append(_scales16(gs, I)[c0 // 16:(c0 + w) // 16])
+            u16.append(_scales16(us, I)[c0 // 16:(c0 + w) // 16])
+            d8s.append(d[:, c0:c0 + w])
+            k0 = c0 // 128
+            d16.append(_scales16(ds, d.shape[0])[:, k0:k0 + -(-w // 128)])
+        E, H = len(g8s), g8s[0].shape[1]
+        w = g8s[0].shape[0]
+        w8 = torch.stack([torch.stack(g8s).reshape(E, w // 16, 16, H), torch.stack(u8s).reshape(E, w // 16, 16, H)],
+                         dim=2).reshape(E, 2 * w, H)
+        s16 = torch.stack([torch.stack(g16), torch.stack(u16)], dim=2).reshape(E, 2 * w // 16, -1)
+        return FP8Experts(w8.contiguous(), s16), FP8Experts(torch.stack(d8s).contiguous(), torch.stack(d16))
+
     def getter(self):
         """``get(name)`` callable for the model loaders (stacked expert names are
         synthesised from per-expert layouts on demand)."""

@@ -121,9 +121,11 @@ def synthetic_hf_globals(cfg: Qwen36Config, seed: int, device) -> dict[str, torc
 # per-rank slicing + fusion
 # --------------------------------------------------------------------------
 def fuse_layer(cfg: Qwen36Config, i: int, get: Callable[[str], torch.Tensor], tp: int, rank: int,
-               dtype=torch.bfloat16, moe_sharding: str = "ep") -> dict[str, torch.Tensor]:
+               dtype=torch.bfloat16, moe_sharding: str = "ep", experts: tuple | None = None) -> dict[str, torch.Tensor]:
     """Build the rank-local fused tensors of layer ``i``; ``get(name)`` returns an
-    HF-layout tensor (name without the ``model.`` prefix)."""
+    HF-layout tensor (name without the ``model.`` prefix).  ``experts``: this
+    rank's routed experts already built (e.g. fp8 ``(gate_up, down)`` straight
+    from an official FP8 checkpoint); they are not read through ``get``."""
     d = tp_dims(cfg, tp, rank, moe_sharding)
     p = f"layers.{i}."
     out: dict[str, torch.Tensor] = {
@@ -168,15 +170,18 @@ def fuse_layer(cfg: Qwen36Config, i: int, get: Callable[[str], torch.Tensor], tp
     if cfg.is_moe:
         e0, e1 = d.expert_offset, d.expert_offset + d.experts
         out["router"] = get(m + "gate.weight").to(dtype).contiguous()
-        gu = get(m + "experts.gate_up_proj")[e0:e1]
-        # intermediate columns held: all of them (expert parallel) or this
-        # rank's slice of every expert (tensor parallel within the expert)
-        I, Il = cfg.moe_inter, d.moe_inter
-        c0 = rank * Il if d.moe_sharding == "tp" else 0
-        out["experts_gate_up"] = torch.stack(
-            [interleave_gate_up(gu[e, c0:c0 + Il], gu[e, I + c0:I + c0 + Il]) for e in range(gu.shape[0])]
-        ).to(dtype).contiguous()
-        out["experts_down"] = get(m + "experts.down_proj")[e0:e1, :, c0:c0 + Il].to(dtype).contiguous()
+        if experts is not None:
+            out["experts_gate_up"], out["experts_down"] = experts
+        else:
+            gu = get(m + "experts.gate_up_proj")[e0:e1]
+            # intermediate columns held: all of them (expert parallel) or this
+            # rank's slice of every expert (tensor parallel within the expert)
+            I, Il = cfg.moe_inter, d.moe_inter
+            c0 = rank * Il if d.moe_sharding == "tp" else 0
+            out["experts_gate_up"] = torch.stack(
+                [interleave_gate_up(gu[e, c0:c0 + Il], gu[e, I + c0:I + c0 + Il]) for e in range(gu.shape[0])]
+            ).to(dtype).contiguous()
+            out["experts_down"] = get(m + "experts.down_proj")[e0:e1, :, c0:c0 + Il].to(dtype).contiguous()
         # shared expert: tensor-parallel (colwise gate/up, rowwise down); each rank
         # scales its partial by the replicated sigmoid gate, so the EP/TP sum
         # reconstructs gate * shared(x) without a redundant copy per rank

@@ -97,11 +97,18 @@ class Qwen36Model(nn.Module):
         self.fused_comm = None  # set by parallel.fused when the NVLink kernels are enabled
 
     # ------------------------------------------------------------------ load
-    def load_hf(self, get: Callable[[str], torch.Tensor]) -> "Qwen36Model":
-        cfg = self.cfg
+    def load_hf(self, get: Callable[[str], torch.Tensor], fp8_experts: Callable | None = None) -> "Qwen36Model":
+        """``fp8_experts(layer, e0, e1, c0, width)``, when given, supplies each MoE
+        layer's routed experts as fp8 (see :meth:`bwn.io.checkpoint.Checkpoint.fp8_experts`)."""
+        cfg, d = self.cfg, self.d
         self.layers = []
         for i in range(cfg.num_layers):
-            t = W.fuse_layer(cfg, i, get, self.tp, self.rank, self.dtype, self.moe_sharding)
+            ex = None
+            if fp8_experts is not None and cfg.is_moe:
+                tp_slice = d.moe_sharding == "tp"
+                ex = fp8_experts(i, d.expert_offset, d.expert_offset + d.experts,
+                                 self.rank * d.moe_inter if tp_slice else 0, d.moe_inter if tp_slice else None)
+            t = W.fuse_layer(cfg, i, get, self.tp, self.rank, self.dtype, self.moe_sharding, experts=ex)
             self.layers.append({k: v.to(self.device) for k, v in t.items()})
         self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, get, self.tp, self.rank, self.dtype).items()}
         return self
@@ -420,17 +427,19 @@ class Qwen36Model(nn.Module):
 
 def build_qwen36(cfg: Qwen36Config, comm: Comm | None = None, device="cpu", seed: int | None = 0,
                  hf_state: dict | None = None, dtype=torch.bfloat16, checkpoint: str | None = None,
-                 moe_sharding: str | None = None) -> Qwen36Model:
+                 moe_sharding: str | None = None, fp8_experts: bool = False) -> Qwen36Model:
     """A rank's model from an in-memory HF state dict, a safetensors checkpoint
     directory (HF layout, packed or per-expert MoE, official FP8 dequantized) or
     random init from ``seed``.  ``moe_sharding``: ``"ep"`` (experts partitioned
     across ranks) or ``"tp"`` (every expert sliced across ranks); default from
-    ``BWN_MOE_SHARDING``."""
+    ``BWN_MOE_SHARDING``.  ``fp8_experts``: an official FP8 checkpoint's routed
+    experts stay fp8 (the fp8 grouped GEMM) instead of being dequantized."""
     m = Qwen36Model(cfg, comm, device, dtype, moe_sharding)
     if checkpoint is not None:
         from ..io.checkpoint import Checkpoint
         ck = Checkpoint(checkpoint)
-        m.load_hf(ck.getter())
+        src = (lambda i, e0, e1, c0, w: ck.fp8_experts(f"layers.{i}.", e0, e1, c0, w)) if fp8_experts else None
+        m.load_hf(ck.getter(), fp8_experts=src)
         ck.close()
     elif hf_state is not None:
         m.load_hf(W.hf_getter(hf_state))
@@ -439,10 +448,12 @@ def build_qwen36(cfg: Qwen36Config, comm: Comm | None = None, device="cpu", seed
     return m
 
 
-def from_pretrained(path: str, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16) -> Qwen36Model:
+def from_pretrained(path: str, comm: Comm | None = None, device="cpu", dtype=torch.bfloat16,
+                    fp8_experts: bool = False) -> Qwen36Model:
     """Config from ``config.json`` plus weights from the safetensors beside it."""
     from ..config import qwen36_from_hf
-    return build_qwen36(qwen36_from_hf(path), comm, device, None, None, dtype, checkpoint=path)
+    return build_qwen36(qwen36_from_hf(path), comm, device, None, None, dtype, checkpoint=path,
+                        fp8_experts=fp8_experts)
 
 
 def param_gb(cfg: Qwen36Config) -> float:

@@ -151,6 +151,8 @@ def main(argv=None) -> None:
     ap.add_argument("--bucket", type=int, default=0, help="prefill chunk length (0: whole prompt)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--fp8", action="store_true", help="W8A16 projection weights")
+    ap.add_argument("--fp8-experts", action="store_true",
+                    help="MoE: routed experts in fp8 (an official FP8 checkpoint's stay fp8; random ones are quantized)")
     ap.add_argument("--fused-comm", action="store_true", help="N>1: fused NVLink reductions")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu", action="store_true")
@@ -161,7 +163,7 @@ def main(argv=None) -> None:
     dev = torch.device("cpu") if cpu else torch.device("cuda", torch.cuda.current_device())
     dtype = torch.float32 if cpu else torch.bfloat16
     if a.checkpoint:
-        model = from_pretrained(a.checkpoint, comm, dev, dtype)
+        model = from_pretrained(a.checkpoint, comm, dev, dtype, fp8_experts=a.fp8_experts)
     else:
         cfg = {"27b": QWEN36_27B, "35b": QWEN36_35B_A3B, "tiny": tiny_qwen36(),
                "tiny-moe": tiny_qwen36(moe=True)}[a.model]
@@ -170,6 +172,8 @@ def main(argv=None) -> None:
         model = build_qwen36(cfg, comm, dev, seed=a.seed, dtype=dtype)
     if a.fp8:
         model.quantize_fp8()
+    if a.fp8_experts and not a.checkpoint and model.cfg.is_moe:
+        model.quantize_fp8(include_head=False, experts=True, dense=False)
     if a.fused_comm and comm.size > 1:
         from ..parallel.fused import enable_fused_comm
         enable_fused_comm(model)

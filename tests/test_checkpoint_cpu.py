@@ -136,6 +136,25 @@ def test_qwen36_official_fp8_experts(tmp_path):
     for La, Lb in zip(a.layers, b.layers):
         for k in ("experts_gate_up", "experts_down"):
             assert torch.equal(La[k], Lb[k])
+    # kept fp8 (no dequantize / requantize): the same weights once dequantized
+    c = build_qwen36(cfg, checkpoint=str(tmp_path), device="cpu", fp8_experts=True)
+    for Lb, Lc in zip(b.layers, c.layers):
+        for k in ("experts_gate_up", "experts_down"):
+            assert hasattr(Lc[k], "scales16")
+            assert torch.equal(Lc[k].dequant().to(torch.bfloat16), Lb[k])
+    # experts sliced across two simulated ranks (tensor parallelism within experts)
+    from bwn.models.qwen36 import Qwen36Model
+    from bwn.io.checkpoint import Checkpoint
+    from bwn.parallel.comm import Comm
+    ck = Checkpoint(str(tmp_path))
+    for r in range(2):
+        m = Qwen36Model(cfg, Comm(None, r, 2), "cpu", torch.bfloat16, moe_sharding="tp")
+        m.load_hf(ck.getter(), fp8_experts=lambda i, e0, e1, c0, w: ck.fp8_experts(f"layers.{i}.", e0, e1, c0, w))
+        ref = Qwen36Model(cfg, Comm(None, r, 2), "cpu", torch.bfloat16, moe_sharding="tp").load_hf(ck.getter())
+        for Lm, Lr in zip(m.layers, ref.layers):
+            for k in ("experts_gate_up", "experts_down"):
+                assert torch.equal(Lm[k].dequant().to(torch.bfloat16), Lr[k]), (r, k)
+    ck.close()
 
 
 def test_fp4_e2m1_decode_table():
