@@ -33,8 +33,27 @@ def _value_of(exponent: torch.Tensor, mantissa: torch.Tensor) -> torch.Tensor:
     return torch.where(exponent == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * torch.exp2(e - 7.0))
 
 
+_E4M3FN_LUT: dict = {}
+
+
+def _e4m3fn_lut(device) -> torch.Tensor:
+    """The 256 E4M3FN values (NaN at 0x7F / 0xFF), built once per device from the bit layout."""
+    key = str(device)
+    if key not in _E4M3FN_LUT:
+        _E4M3FN_LUT[key] = _decode_bits(torch.arange(256, dtype=torch.uint8), False).to(device)
+    return _E4M3FN_LUT[key]
+
+
 def decode_e4m3fn(raw: torch.Tensor, reject_nan: bool = True) -> torch.Tensor:
-    """OCP E4M3FN bytes -> float32 (from the bit layout, no float8 dtype needed)."""
+    """OCP E4M3FN bytes -> float32 (a 256-entry table built from the bit layout;
+    no float8 dtype needed)."""
+    b = _bytes(raw)
+    if reject_nan and bool(((b & 0x7F) == 0x7F).any()):
+        raise ValueError(f"E4M3FN tensor holds {int(((b & 0x7F) == 0x7F).sum())} NaN encodings")
+    return _e4m3fn_lut(b.device)[b.long()]
+
+
+def _decode_bits(raw: torch.Tensor, reject_nan: bool = True) -> torch.Tensor:
     b = _bytes(raw)
     sign = (b >> 7).bool()
     exp = ((b >> 3) & 0xF).to(torch.int32)
