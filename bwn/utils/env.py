@@ -82,3 +82,8 @@ def validate(environ=None) -> dict:
 
 def describe() -> str:
     return "\n".join(f"{f.name:22s} default={f.default!r:8} {f.help}" for f in FLAGS.values())
+
+
+if __name__ == "__main__":  # python -m bwn.utils.env: list the flags, then validate the current environment
+    print(describe())
+    validate()
