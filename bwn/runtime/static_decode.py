@@ -38,7 +38,8 @@ class StaticDecoder:
         self.temperature = torch.zeros(batch, dtype=torch.float32, device=dev)
         # the default generator of the device (graph-safe under capture); a
         # separate one on the CPU keeps host runs reproducible
-        self.gen = torch.Generator().manual_seed(seed) if dev.type == "cpu" else None
+        # (one stream per rank: each vocab shard draws its own noise)
+        self.gen = torch.Generator().manual_seed(seed + getattr(model, "rank", 0)) if dev.type == "cpu" else None
         if dev.type == "cuda" and sampling:
             torch.cuda.manual_seed(seed + getattr(model, "rank", 0))
         self.use_graph = use_graph and dev.type == "cuda"

@@ -112,6 +112,11 @@ class ContinuousEngine:
                 done.append(fin)
         return done
 
+    def abort_all(self) -> None:
+        """Drop every waiting and running request (after an error)."""
+        self.slots = [None] * self.max_batch
+        self.waiting.clear()
+
     def run(self, reqs: list[Request]) -> list[Result]:
         """Convenience: serve ``reqs`` to completion, results in input order."""
         ids = [self.add(q) for q in reqs]

@@ -13,6 +13,7 @@ framework).  Two schedulers:
   (:class:`~bwn.serve.spec.SpecEngine` behind the batching worker).
 
     python -m bwn.serve.server --model tiny --port 8000 --scheduler continuous
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m bwn.serve.server --model 27b   # rank 0 serves HTTP
 """
 from __future__ import annotations
 
@@ -129,8 +130,7 @@ class ContinuousWorker:
                 for fut in self.futs.values():
                     fut.set_exception(e)
                 self.futs.clear()
-                self.engine.slots = [None] * self.engine.max_batch
-                self.engine.waiting.clear()
+                self.engine.abort_all()
                 continue
             self.stats["steps"] += 1
             for rid, res in finished:
@@ -141,6 +141,8 @@ class ContinuousWorker:
     def stop(self):
         self._stop = True
         self.thread.join(timeout=5)
+        if hasattr(self.engine, "stop"):  # followers of a multi-rank engine leave their loop
+            self.engine.stop()
 
 
 def build_app(worker, model_name: str = "bwn"):
@@ -192,13 +194,33 @@ def main():
 
     from ..config import QWEN36_27B, QWEN36_35B_A3B, tiny_qwen36
     from ..models.qwen36 import Qwen36Model, from_pretrained
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    from ..parallel.comm import init_distributed
+    comm = init_distributed()  # torchrun: one rank per GPU, the model sharded over them
+    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
     if a.checkpoint:
-        model = from_pretrained(a.checkpoint, None, dev)
+        model = from_pretrained(a.checkpoint, comm, dev)
     else:
         cfg = {"tiny": tiny_qwen36(), "27b": QWEN36_27B, "35b": QWEN36_35B_A3B}[a.model]
-        model = Qwen36Model(cfg, None, dev).init_random(0)
-    if a.scheduler == "spec":
+        model = Qwen36Model(cfg, comm, dev).init_random(0)
+    if comm.size > 1 and dev.type == "cuda":
+        from ..parallel.fused import enable_fused_comm
+        try:
+            enable_fused_comm(model)
+        except RuntimeError as e:
+            print(f"[server] fused NVLink comm unavailable, using NCCL: {e}")
+    use_graph = dev.type == "cuda"
+    if comm.size > 1:
+        if a.scheduler != "continuous":
+            raise SystemExit("multi-rank serving runs the continuous scheduler")
+        from .continuous import ContinuousEngine
+        from .lockstep import LockstepEngine, control_group, follow
+        engine = ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=use_graph, sampling=a.sampling)
+        ctrl = control_group()
+        if comm.rank != 0:
+            follow(engine, ctrl)
+            return
+        worker = ContinuousWorker(LockstepEngine(engine, ctrl))
+    elif a.scheduler == "spec":
         from ..models.eagle3 import Eagle3Draft, eagle3_config
         from .spec import SpecEngine
         draft = Eagle3Draft(eagle3_config(model.cfg), dev, model.dtype)
@@ -208,15 +230,17 @@ def main():
             draft.load({k: ck.raw(k) for k in ck.wm})
         else:
             draft.init_random(0)
-        worker = BatchingWorker(SpecEngine(model, draft, a.max_batch, a.max_seq, a.num_draft,
-                                           use_graph=dev == "cuda"))
+        worker = BatchingWorker(SpecEngine(model, draft, a.max_batch, a.max_seq, a.num_draft, use_graph=use_graph))
     elif a.scheduler == "continuous":
         from .continuous import ContinuousEngine
-        worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda",
+        worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=use_graph,
                                                    sampling=a.sampling))
     else:
-        worker = BatchingWorker(GenerationEngine(model, a.max_batch, a.max_seq, use_graph=dev == "cuda"))
-    uvicorn.run(build_app(worker, a.model), host=a.host, port=a.port)
+        worker = BatchingWorker(GenerationEngine(model, a.max_batch, a.max_seq, use_graph=use_graph))
+    try:
+        uvicorn.run(build_app(worker, a.model), host=a.host, port=a.port)
+    finally:
+        worker.stop()
 
 
 if __name__ == "__main__":
