@@ -60,8 +60,25 @@ class LockstepEngine:
         self._send("stop")
 
 
+class LockstepBatchEngine:
+    """Rank 0's handle of a batch engine (static or speculative): each batch is
+    broadcast, then generated on every rank."""
+
+    def __init__(self, engine, group):
+        self.e, self.group = engine, group
+        self.max_batch = engine.max_batch
+
+    def generate(self, reqs):
+        dist.broadcast_object_list([("generate", list(reqs))], src=0, group=self.group)
+        return self.e.generate(reqs)
+
+    def stop(self) -> None:
+        dist.broadcast_object_list([("stop", [])], src=0, group=self.group)
+
+
 def follow(engine, group) -> None:
-    """A follower rank: replay rank 0's requests and steps until it stops."""
+    """A follower rank: replay rank 0's requests and steps (or batches) until
+    it stops.  A batch the engine rejects is rejected on every rank alike."""
     while True:
         msg = [None]
         dist.broadcast_object_list(msg, src=0, group=group)
@@ -70,7 +87,12 @@ def follow(engine, group) -> None:
             return
         if kind == "abort":
             engine.abort_all()
-            continue
-        for r in reqs:
-            engine.add(r)
-        engine.step()
+        elif kind == "generate":
+            try:
+                engine.generate(reqs)
+            except ValueError:
+                pass
+        else:
+            for r in reqs:
+                engine.add(r)
+            engine.step()

@@ -80,6 +80,8 @@ class BatchingWorker:
     def stop(self):
         self._stop = True
         self.thread.join(timeout=5)
+        if hasattr(self.engine, "stop"):  # followers of a multi-rank engine leave their loop
+            self.engine.stop()
 
 
 class ContinuousWorker:
@@ -209,18 +211,7 @@ def main():
         except RuntimeError as e:
             print(f"[server] fused NVLink comm unavailable, using NCCL: {e}")
     use_graph = dev.type == "cuda"
-    if comm.size > 1:
-        if a.scheduler != "continuous":
-            raise SystemExit("multi-rank serving runs the continuous scheduler")
-        from .continuous import ContinuousEngine
-        from .lockstep import LockstepEngine, control_group, follow
-        engine = ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=use_graph, sampling=a.sampling)
-        ctrl = control_group()
-        if comm.rank != 0:
-            follow(engine, ctrl)
-            return
-        worker = ContinuousWorker(LockstepEngine(engine, ctrl))
-    elif a.scheduler == "spec":
+    if a.scheduler == "spec":
         from ..models.eagle3 import Eagle3Draft, eagle3_config
         from .spec import SpecEngine
         draft = Eagle3Draft(eagle3_config(model.cfg), dev, model.dtype)
@@ -230,13 +221,20 @@ def main():
             draft.load({k: ck.raw(k) for k in ck.wm})
         else:
             draft.init_random(0)
-        worker = BatchingWorker(SpecEngine(model, draft, a.max_batch, a.max_seq, a.num_draft, use_graph=use_graph))
+        engine = SpecEngine(model, draft, a.max_batch, a.max_seq, a.num_draft, use_graph=use_graph)
     elif a.scheduler == "continuous":
         from .continuous import ContinuousEngine
-        worker = ContinuousWorker(ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=use_graph,
-                                                   sampling=a.sampling))
+        engine = ContinuousEngine(model, a.max_batch, a.max_seq, use_graph=use_graph, sampling=a.sampling)
     else:
-        worker = BatchingWorker(GenerationEngine(model, a.max_batch, a.max_seq, use_graph=use_graph))
+        engine = GenerationEngine(model, a.max_batch, a.max_seq, use_graph=use_graph)
+    if comm.size > 1:  # every rank runs the engine; rank 0 serves HTTP and leads
+        from .lockstep import LockstepBatchEngine, LockstepEngine, control_group, follow
+        ctrl = control_group()
+        if comm.rank != 0:
+            follow(engine, ctrl)
+            return
+        engine = (LockstepEngine if a.scheduler == "continuous" else LockstepBatchEngine)(engine, ctrl)
+    worker = ContinuousWorker(engine) if a.scheduler == "continuous" else BatchingWorker(engine)
     try:
         uvicorn.run(build_app(worker, a.model), host=a.host, port=a.port)
     finally:
