@@ -139,7 +139,7 @@ def argmax_packed(logits: torch.Tensor, id_offset: int = 0) -> torch.Tensor:
     m, _ = lf.max(-1)
     ids = torch.arange(lf.shape[-1])
     first = torch.where(lf == m[:, None], ids, torch.full_like(ids, lf.shape[-1])).min(-1).values + id_offset
-    u = m.view(torch.int32).long() & 0xFFFFFFFF
+    u = (m + 0.0).view(torch.int32).long() & 0xFFFFFFFF  # + 0.0: -0.0 keys like +0.0 (ties, lowest id)
     neg = (u & 0x80000000) != 0
     ordv = torch.where(neg, (~u) & 0xFFFFFFFF, u | 0x80000000)
     hi = (ordv ^ 0x80000000) - ((ordv ^ 0x80000000) >= 0x80000000).long() * (1 << 32)  # as signed 32-bit

@@ -144,8 +144,11 @@ void embedding(const int* ids, int n, const __nv_bfloat16* table, long rows, int
 }
 
 // ---------------------------------------------------------------------------
+// monotone map float -> uint32 (unsigned order = float order); -0.0 maps like
+// +0.0 so equal logits of either zero sign tie and the lowest id wins
 __device__ __forceinline__ uint32_t orderable(float f) {
-  const uint32_t u = __float_as_uint(f);
+  uint32_t u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 

@@ -1,0 +1,77 @@
+"""Property tests (hypothesis) of the numeric invariants the kernels' CPU twins
+rely on:
+
+* packed greedy keys: for any logits (signs, ties, infinities) and any split
+  into vocab shards, the int64 max over the shards' keys decodes to the
+  largest logit with the lowest global id;
+* fp8 block codec: dequantize(quantize(w)) stays within E4M3's relative step
+  of each 128x128 block's scale, zeros stay zero, and FP8Experts keeps every
+  row's own block scale through the gate/up interleave.
+"""
+import math
+
+import torch
+from hypothesis import given, settings
+from hypothesis import strategies as st
+
+from bwn import ops as O
+from bwn.io.fp8 import FP8Experts, dequantize_block, quantize_block
+
+finite = st.floats(min_value=-2.0 ** 100, max_value=2.0 ** 100, allow_nan=False, allow_infinity=False, width=32)
+
+
+@settings(max_examples=60, deadline=None)
+@given(vals=st.lists(st.one_of(finite, st.sampled_from([0.0, -0.0, 1.5, -1.5, float("inf"), -float("inf")])),
+                     min_size=2, max_size=64),
+       shards=st.integers(min_value=1, max_value=8))
+def test_packed_greedy_any_split(vals, shards):
+    v = torch.tensor(vals, dtype=torch.float32)[None]
+    V = v.shape[1]
+    bounds = sorted({0, V, *[(V * i) // shards for i in range(1, shards)]})
+    keys = [O.argmax_packed(v[:, a:b], a) for a, b in zip(bounds, bounds[1:]) if b > a]
+    got = int(O.unpack_argmax(torch.stack(keys).max(0).values)[0])
+    best = v[0].max()
+    want = int(torch.nonzero(v[0] == best)[0, 0])
+    assert got == want, (vals, shards, got, want)
+
+
+@settings(max_examples=40, deadline=None)
+@given(rows=st.integers(1, 300), cols=st.integers(1, 300), scale=st.floats(1e-4, 1e3), seed=st.integers(0, 10_000))
+def test_fp8_block_roundtrip_bound(rows, cols, scale, seed):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(rows, cols, generator=g) * scale
+    w[0, 0] = 0.0
+    w8, s = quantize_block(w)
+    d = dequantize_block(w8, s)
+    assert d[0, 0] == 0.0
+    # E4M3: 3 mantissa bits -> |error| <= 2^-4 * |value| for normals, plus the
+    # subnormal spacing 2^-9 of the block scale
+    se = s.repeat_interleave(128, 0).repeat_interleave(128, 1)[:rows, :cols]
+    assert bool(((d - w).abs() <= w.abs() * 2 ** -4 + se * 2 ** -9 + 1e-30).all())
+
+
+@settings(max_examples=25, deadline=None)
+@given(E=st.integers(1, 3), I16=st.integers(1, 12), K=st.integers(1, 260), seed=st.integers(0, 10_000))
+def test_fp8_experts_interleave_keeps_row_scales(E, I16, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    I = 16 * I16
+    gate = torch.randn(E, I, K, generator=g) * torch.rand(E, I, 1, generator=g) * 10
+    up = torch.randn(E, I, K, generator=g)
+    fx = FP8Experts.quantize_gate_up(gate, up)
+    d = fx.dequant()
+    x = d.reshape(E, I // 16, 2, 16, K)
+    dg, du = x[:, :, 0].reshape(E, I, K), x[:, :, 1].reshape(E, I, K)
+    for e in range(E):
+        g8, gs = quantize_block(gate[e])
+        u8, us = quantize_block(up[e])
+        assert torch.equal(dg[e], dequantize_block(g8, gs))
+        assert torch.equal(du[e], dequantize_block(u8, us))
+    assert fx.scales16.shape == (E, 2 * I // 16, math.ceil(K / 128))
+
+
+def test_signed_zero_maxima_tie_across_shards():
+    """-0.0 and +0.0 are equal logits: the lowest id wins, whichever shard holds it."""
+    ka = O.argmax_packed(torch.tensor([[-0.0, -1.0]]), 0)
+    kb = O.argmax_packed(torch.tensor([[0.0, -2.0]]), 5)
+    assert int(O.unpack_argmax(torch.stack([ka, kb]).max(0).values)[0]) == 0
+    assert int(O.unpack_argmax(O.argmax_packed(torch.tensor([[-1.0, -0.0, 0.0]]), 0))[0]) == 1
