@@ -75,3 +75,41 @@ def test_signed_zero_maxima_tie_across_shards():
     kb = O.argmax_packed(torch.tensor([[0.0, -2.0]]), 5)
     assert int(O.unpack_argmax(torch.stack([ka, kb]).max(0).values)[0]) == 0
     assert int(O.unpack_argmax(O.argmax_packed(torch.tensor([[-1.0, -0.0, 0.0]]), 0))[0]) == 1
+
+
+@settings(max_examples=20, deadline=None)
+@given(S=st.integers(1, 40), chunk=st.sampled_from([4, 8, 16]), g_scale=st.sampled_from([1e-4, 0.3, 3.0]),
+       seed=st.integers(0, 10_000))
+def test_chunked_delta_rule_equals_recurrent(S, chunk, g_scale, seed):
+    import torch.nn.functional as F
+
+    from bwn.ops import reference as R
+    gen = torch.Generator().manual_seed(seed)
+    q = F.normalize(torch.randn(1, 2, S, 16, generator=gen, dtype=torch.float64), dim=-1).float() * 0.25
+    k = F.normalize(torch.randn(1, 2, S, 16, generator=gen, dtype=torch.float64), dim=-1).float()
+    v = torch.randn(1, 2, S, 8, generator=gen)
+    g = -torch.rand(1, 2, S, generator=gen) * g_scale
+    beta = torch.rand(1, 2, S, generator=gen)
+    s0 = torch.randn(1, 2, 16, 8, generator=gen) * 0.1
+    o1, s1 = R.chunk_gated_delta_rule(q, k, v, g, beta, s0, chunk)
+    o2, s2 = R.recurrent_gated_delta_rule(q, k, v, g, beta, s0)
+    assert torch.allclose(o1, o2, atol=2e-4, rtol=1e-3) and torch.allclose(s1, s2, atol=2e-4, rtol=1e-3)
+
+
+@settings(max_examples=20, deadline=None)
+@given(T=st.integers(1, 12), E=st.integers(2, 12), k=st.integers(1, 4), seed=st.integers(0, 10_000))
+def test_sparse_moe_equals_masked_dense(T, E, k, seed):
+    import torch.nn.functional as F
+
+    from bwn.ops import reference as R
+    k = min(k, E)
+    gen = torch.Generator().manual_seed(seed)
+    H, I = 16, 8
+    x = torch.randn(T, H, generator=gen)
+    w, ids = R.moe_route_softmax(torch.randn(T, E, generator=gen), k)
+    gu = torch.randn(E, 2 * I, H, generator=gen) * 0.2
+    dn = torch.randn(E, H, I, generator=gen) * 0.2
+    dense = torch.zeros(T, E).scatter_add_(1, ids.long(), w)
+    gg, uu = torch.einsum("th,eih->eti", x, gu).chunk(2, dim=-1)
+    ref = torch.einsum("te,eth->th", dense, torch.einsum("eti,ehi->eth", F.silu(gg) * uu, dn))
+    assert torch.allclose(R.moe_experts(x, w, ids, gu, dn), ref, atol=1e-5)
