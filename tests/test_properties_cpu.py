@@ -113,3 +113,22 @@ def test_sparse_moe_equals_masked_dense(T, E, k, seed):
     gg, uu = torch.einsum("th,eih->eti", x, gu).chunk(2, dim=-1)
     ref = torch.einsum("te,eth->th", dense, torch.einsum("eti,ehi->eth", F.silu(gg) * uu, dn))
     assert torch.allclose(R.moe_experts(x, w, ids, gu, dn), ref, atol=1e-5)
+
+
+@settings(max_examples=50, deadline=None)
+@given(B=st.integers(1, 4), N=st.integers(2, 6), vocab=st.integers(2, 5), seed=st.integers(0, 10_000))
+def test_accept_greedy_matches_a_plain_loop(B, N, vocab, seed):
+    """Accepted drafts = the longest prefix of drafts equal to the target's
+    greedy ids; emitted = those drafts then the target's next id."""
+    from bwn.runtime.spec_decode import accept_greedy
+    gen = torch.Generator().manual_seed(seed)
+    tok = torch.randint(0, vocab, (B, N), generator=gen)
+    tgt = torch.randint(0, vocab, (B, N), generator=gen)
+    m, bonus, out = accept_greedy(tok, tgt)
+    for b in range(B):
+        mm = 0
+        while mm < N - 1 and int(tok[b, mm + 1]) == int(tgt[b, mm]):
+            mm += 1
+        emitted = [int(t) for t in tok[b, 1:mm + 1]] + [int(tgt[b, mm])]
+        assert int(m[b]) == mm and int(bonus[b]) == int(tgt[b, mm])
+        assert out[b, :mm + 1].tolist() == emitted and (out[b, mm + 1:] == -1).all()
