@@ -156,6 +156,9 @@ def main(argv=None) -> None:
                     help="MoE: routed experts in fp8 (an official FP8 checkpoint's stay fp8; random ones are quantized)")
     ap.add_argument("--fused-comm", action="store_true", help="N>1: fused NVLink reductions")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--prefill-gen", action="store_true",
+                    help="also generate by re-prefilling the growing sequence each step (the reference's PREFILL_GEN "
+                         "coherence check) and report whether it matches the decode path")
     ap.add_argument("--cpu", action="store_true")
     a = ap.parse_args(argv)
 
@@ -212,13 +215,25 @@ def main(argv=None) -> None:
     check_status("static_decode")
     gen = torch.stack(out, 1)
     occupancy = F.check_qwen36_state(dec.st, f"decode state rank={comm.rank}")
+    pgen = None
+    if a.prefill_gen:  # every token from a fresh prefill of prompt + tokens so far
+        seq = prompt.clone()
+        toks = []
+        for _ in range(a.max_new):
+            st = model.new_state(a.batch, S + a.max_new + 8)
+            nxt = model.greedy(model.prefill_hidden(seq.to(dev), st, None)).cpu()
+            toks.append(nxt)
+            seq = torch.cat([seq, nxt[:, None].long()], 1)
+        pgen = torch.stack(toks, 1)
     if comm.rank == 0:
         print(json.dumps({
             "model": cfg.name, "tp": comm.size, "batch": a.batch, "prompt_len": S,
             "generated_row0": gen[0].tolist(), "gen_hash_row0": F.gen_hash(gen[0]),
             "prefill_fingerprint": F.logits_fingerprint(logits.float().cpu()),
             "ttft_ms": round(ttft, 2), "tpot_ms": round(tpot, 3),
-            "occupied_ssm_layers": len(occupancy["ssm"]), "graph": dec.graph is not None}))
+            "occupied_ssm_layers": len(occupancy["ssm"]), "graph": dec.graph is not None,
+            **({"prefill_gen_hash_row0": F.gen_hash(pgen[0]), "prefill_gen_matches": bool(torch.equal(pgen, gen))}
+               if pgen is not None else {})}))
     dec.release()
     if comm.size > 1:
         import torch.distributed as dist

@@ -23,7 +23,8 @@ def _run(args):
 
 
 def test_whole_bucketed_and_two_ranks_agree():
-    one = _run(BASE)
+    one = _run(BASE + ["--prefill-gen"])
+    assert one["prefill_gen_matches"] and one["prefill_gen_hash_row0"] == one["gen_hash_row0"]
     assert one["prefill_fingerprint"]["finite"] and len(one["generated_row0"]) == 6
     assert _run(BASE + ["--bucket", "5"])["gen_hash_row0"] == one["gen_hash_row0"]
     s = socket.socket()
