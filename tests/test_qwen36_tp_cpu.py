@@ -34,6 +34,9 @@ def _rank(rank, world, port, moe, sharding, q):
         torch.set_num_threads(2)  # ranks share the host's cores
         cfg = replace(tiny_qwen36(moe=moe), dn_k_heads=4, dn_v_heads=8)  # DeltaNet heads split over 4
         comm = Comm(None, rank, world)
+        from bwn.parallel.topology import hosts_of, require_single_domain
+        require_single_domain(comm, "test")  # every rank on this host: the collective check passes
+        assert len(hosts_of(comm)) == world
         tp = build_qwen36(cfg, comm, seed=3, dtype=torch.float32, moe_sharding=sharding)
         one = build_qwen36(cfg, Comm.single(), seed=3, dtype=torch.float32)
         B, S = 3, 9
