@@ -55,6 +55,30 @@ class FusedComm:
         self.hdl.barrier()
         torch.cuda.synchronize(dev)
 
+    @classmethod
+    def on_local_multicast(cls, hidden: int, max_rows: int = 256, device=None, timeout_s: float = 5.0):
+        """The same buffer layout on a one-GPU multicast object
+        (:class:`~bwn.parallel.mc_local.LocalMulticastBuffer`): a world of one that
+        still runs the ``multimem`` code path, for single-process profiling."""
+        from .comm import Comm
+        from .mc_local import LocalMulticastBuffer
+        self = cls.__new__(cls)
+        self.comm, self.world, self.rank = Comm.single(), 1, 0
+        self.hidden, self.max_rows, self.timeout_s = hidden, max_rows, timeout_s
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        slots_bytes = 8 * max_rows * 8
+        self.ar_off = ((self.SLOTS + slots_bytes + 255) // 256) * 256
+        self.buf_elems = max_rows * hidden
+        self.mcbuf = LocalMulticastBuffer(self.ar_off + 2 * self.buf_elems * 2, dev)
+        self.buf, self.hdl = self.mcbuf.tensor, None
+        base = self.mcbuf.uc_ptr
+        self.peer_flags_ar, self.peer_flags_g, self.peer_slots = [base + self.FLAGS_AR], [base + self.FLAGS_GREEDY], \
+            [base + self.SLOTS]
+        self.mc_ar = self.mcbuf.mc_ptr + self.ar_off
+        self.local_ar = base + self.ar_off
+        self.state = torch.zeros(8, dtype=torch.int32, device=dev)
+        return self
+
     def fits(self, rows: int) -> bool:
         return rows <= self.max_rows
 
