@@ -69,4 +69,13 @@ class ClockSampler:
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        med = statistics.median(sm)
+        out = {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        # the run is not trustworthy under thermal / hardware slowdown, or with the
+        # clock held well below its maximum for no listed reason (a leftover lock)
+        bad = sorted(reasons & {"hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown"})
+        if bad:
+            out["suspect"] = "throttled: " + ",".join(bad)
+        elif mx and med < 0.8 * mx and not reasons:
+            out["suspect"] = "SM clock held below max with no throttle reason"
+        return out

@@ -142,3 +142,20 @@ def test_single_domain_check(monkeypatch):
     monkeypatch.setattr(T, "hosts_of", lambda comm: ["node-a", "node-b"])
     with pytest.raises(RuntimeError, match="spans hosts"):
         T.require_single_domain(Comm(None, 0, 2), "fused comm")
+
+
+def test_clock_summary_parsing():
+    from bwn.utils.clocks import ClockSampler
+    c = ClockSampler()
+    c.lines = ["0, 1860, 1965, 900.1, 0x0, Not Active, Not Active, Not Active, Not Active",
+               "0, 1320, 1965, 999.9, 0x4, Not Active, Not Active, Not Active, Active",
+               "garbage", "0, N/A, 1965, 1, 0, a, b, c, d"]
+    s = c.summary()
+    assert s["samples"] == 2 and s["sm_mhz"] == (1860 + 1320) / 2 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"] and "suspect" not in s  # power cap: kept and noted
+    c.lines = ["0, 1500, 1965, 700, 0x40, Not Active, Active, Not Active, Not Active"]
+    assert c.summary()["suspect"].startswith("throttled: hw_thermal_slowdown")
+    c.lines = ["0, 1000, 1965, 400, 0x0, Not Active, Not Active, Not Active, Not Active"]
+    assert "held below max" in c.summary()["suspect"]
+    c.lines = []
+    assert c.summary()["samples"] == 0
