@@ -78,7 +78,9 @@ class LockstepBatchEngine:
 
 def follow(engine, group) -> None:
     """A follower rank: replay rank 0's requests and steps (or batches) until
-    it stops.  A batch the engine rejects is rejected on every rank alike."""
+    it stops.  A batch the engine rejects is rejected on every rank alike; a
+    step that fails here fails on rank 0 too, which then broadcasts an abort,
+    so the follower stays in its loop instead of leaving rank 0 waiting."""
     while True:
         msg = [None]
         dist.broadcast_object_list(msg, src=0, group=group)
@@ -93,6 +95,9 @@ def follow(engine, group) -> None:
             except ValueError:
                 pass
         else:
-            for r in reqs:
-                engine.add(r)
-            engine.step()
+            try:
+                for r in reqs:
+                    engine.add(r)
+                engine.step()
+            except Exception:  # noqa: BLE001 - rank 0 fails the same step and broadcasts "abort"
+                engine.abort_all()
