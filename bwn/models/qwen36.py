@@ -87,6 +87,9 @@ class Qwen36Model(nn.Module):
         self.rank = self.comm.rank
         self.moe_sharding = moe_sharding or env.get("BWN_MOE_SHARDING")
         self.moe_shared_only = bool(env.get("BWN_MOE_SHARED_ONLY"))
+        # vocab-parallel embedding (the reference's PREFILL_SHARDED_EMBED): each rank
+        # keeps vocab/tp rows, ids outside its range read zeros, one sum all-reduce
+        self.shard_embed = bool(env.get("BWN_SHARD_EMBED")) and self.comm.size > 1
         self.d = tp_dims(cfg, self.tp, self.rank, self.moe_sharding)
         self.device = torch.device(device)
         self.dtype = dtype
@@ -111,7 +114,15 @@ class Qwen36Model(nn.Module):
             t = W.fuse_layer(cfg, i, get, self.tp, self.rank, self.dtype, self.moe_sharding, experts=ex)
             self.layers.append({k: v.to(self.device) for k, v in t.items()})
         self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, get, self.tp, self.rank, self.dtype).items()}
+        self._shard_embed_table()
         return self
+
+    def embed(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Token embeddings ``[T, H]`` (the residual stream's start)."""
+        if not self.shard_embed:
+            return O.embedding(tokens.int(), self.g["embed"], 0)
+        e = O.embedding(tokens.int(), self.g["embed"], self.d.vocab_offset)
+        return self.comm.all_reduce_(e)
 
     def init_random(self, seed: int = 0, gen_device=None) -> "Qwen36Model":
         """Random-init weights from a seed (same model for every TP degree)."""
@@ -126,7 +137,13 @@ class Qwen36Model(nn.Module):
         glob = W.synthetic_hf_globals(cfg, seed, gd)
         self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, glob.__getitem__, self.tp, self.rank,
                                                                    self.dtype).items()}
+        self._shard_embed_table()
         return self
+
+    def _shard_embed_table(self) -> None:
+        if self.shard_embed:
+            d = self.d
+            self.g["embed"] = self.g["embed"][d.vocab_offset:d.vocab_offset + d.vocab].contiguous()
 
     FP8_KEYS = ("in_proj", "out_proj", "qkv_proj", "o_proj", "gate_up", "down", "shared_gate_up", "shared_down")
 
@@ -247,7 +264,7 @@ class Qwen36Model(nn.Module):
         """One decode step for ``tokens [B]`` at ``st.positions``; advances the
         positions and returns the final-normed hidden ``[B, H]``."""
         cfg = self.cfg
-        x = O.embedding(tokens.int(), self.g["embed"], 0)  # residual stream [B, H]
+        x = self.embed(tokens)  # residual stream [B, H]
         h = O.rms_norm(x, self.layers[0]["in_norm"], cfg.rms_eps)
         di = gi = 0
         for i in range(cfg.num_layers):
@@ -296,7 +313,7 @@ class Qwen36Model(nn.Module):
         B, N = tokens.shape
         T = B * N
         pos_rows = (st.positions[:, None] + torch.arange(N, device=tokens.device, dtype=torch.int32)[None]).reshape(T)
-        x = O.embedding(tokens.reshape(T).int(), self.g["embed"], 0)
+        x = self.embed(tokens.reshape(T))
         h = O.rms_norm(x, self.layers[0]["in_norm"], cfg.rms_eps)
         feats = []
         di = gi = 0

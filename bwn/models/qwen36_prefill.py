@@ -49,7 +49,7 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
         valid_len = torch.full((B,), S, dtype=torch.int32, device=dev)
     valid_len = valid_len.to(dev).int()
     T = B * S
-    x = O.embedding(tokens.reshape(T).int(), model.g["embed"], 0)  # [T, H]
+    x = model.embed(tokens.reshape(T))  # [T, H]
     h = O.rms_norm(x, model.layers[0]["in_norm"], cfg.rms_eps)
     captured = {}
     from ..utils import env
@@ -115,7 +115,7 @@ def prefill_hidden_sp(model, tokens: torch.Tensor, st, sp, chunk: int = 64) -> t
     start = int(st.positions[0].item())
     model.ensure_rope(start + S)
     valid_len = torch.full((B,), S, dtype=torch.int32, device=dev)
-    x_full = O.embedding(tokens.reshape(T).int(), model.g["embed"], 0)
+    x_full = model.embed(tokens.reshape(T))
     x = x_full[r * Ts:(r + 1) * Ts].contiguous()  # residual shard
     h = O.rms_norm(x_full, model.layers[0]["in_norm"], cfg.rms_eps)
     del x_full

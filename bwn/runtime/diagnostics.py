@@ -50,7 +50,7 @@ def decode_diagnostics(model, tokens: torch.Tensor, st, layers=None) -> dict:
     cfg, d = model.cfg, model.d
     sel = set(range(cfg.num_layers) if layers is None else layers)
     out: dict = {"layers": {}}
-    x = O.embedding(tokens.int(), model.g["embed"], 0)
+    x = model.embed(tokens)
     h = O.rms_norm(x, model.layers[0]["in_norm"], cfg.rms_eps)
     di = gi = 0
     for i in range(cfg.num_layers):

@@ -49,6 +49,8 @@ class SpecDecoder:
         self.sp = target.new_spec_state(batch, self.N)
         self.dst = draft.new_state(batch, max_seq)
         target.ensure_rope(max_seq)
+        if getattr(target, "shard_embed", False):
+            raise ValueError("the EAGLE3 draft reads the full embedding table; run the target with BWN_SHARD_EMBED=0")
         draft.bind_embedding(target.g["embed"])
         self.tok = torch.zeros(batch, self.N, dtype=torch.int32, device=dev)    # next verify input
         self.out = torch.full((batch, self.N), -1, dtype=torch.int32, device=dev)  # emitted this step

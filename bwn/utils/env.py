@@ -38,6 +38,8 @@ FLAGS = {f.name: f for f in (
          "expert's intermediate width (tp)", ("ep", "tp")),
     Flag("BWN_PREFILL_TRACE", int, 0, "per-layer finite / max-abs trace of prefill (1: print, 2: also raise at the "
          "first non-finite layer)", (0, 1, 2)),
+    Flag("BWN_SHARD_EMBED", int, 0, "vocab-parallel token embedding (vocab/tp rows per rank, one all-reduce per "
+         "lookup) instead of a replicated table", (0, 1)),
     Flag("BWN_MOE_SHARED_ONLY", int, 0, "cost probe: skip the routed experts, keep the shared expert (wrong results)",
          (0, 1)),
 )}

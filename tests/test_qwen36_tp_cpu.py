@@ -22,8 +22,8 @@ def _port():
     return p
 
 
-def _rank(rank, world, port, moe, sharding, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _rank(rank, world, port, moe, sharding, q, shard_embed=False):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), BWN_SHARD_EMBED="1" if shard_embed else "0")
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from dataclasses import replace
@@ -51,6 +51,9 @@ def _rank(rank, world, port, moe, sharding, q):
             err = max(err, float((tp.logits(h_tp) - one.logits(h_one)).abs().max()))
             ids_tp, ids_one = tp.greedy(h_tp), one.greedy(h_one)
             same = same and torch.equal(ids_tp, ids_one)
+        assert tp.shard_embed == shard_embed
+        if shard_embed:
+            assert tp.g["embed"].shape[0] == cfg.vocab // world
         q.put((rank, err, same, tp.d.kv_heads, tp.d.q_heads))
     except Exception:
         import traceback
@@ -59,13 +62,14 @@ def _rank(rank, world, port, moe, sharding, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,moe,sharding", [(2, False, "ep"), (4, False, "ep"), (2, True, "ep"), (4, True, "ep"),
-                                                (4, True, "tp")])
-def test_tp_ranks_match_single_rank(world, moe, sharding):
+@pytest.mark.parametrize("world,moe,sharding,shard_embed", [(2, False, "ep", False), (4, False, "ep", False),
+                                                            (2, True, "ep", False), (4, True, "ep", False),
+                                                            (4, True, "tp", False), (2, False, "ep", True)])
+def test_tp_ranks_match_single_rank(world, moe, sharding, shard_embed):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_rank, args=(r, world, port, moe, sharding, q)) for r in range(world)]
+    ps = [ctx.Process(target=_rank, args=(r, world, port, moe, sharding, q, shard_embed)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=240) for _ in range(world)]
