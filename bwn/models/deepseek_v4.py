@@ -295,7 +295,10 @@ class DeepSeekV4Model:
             self.comm.all_reduce_(x)
         return x
 
-    def _attn(self, L, x, st: DeepSeekV4State, li: int, pos: torch.Tensor, bidx: torch.Tensor, q_per_seq: int):
+    def _attn(self, L, x, st: DeepSeekV4State, li: int, pos: torch.Tensor, bidx: torch.Tensor, q_per_seq: int,
+              mix):
+        """Attention sub-block; returns the new residual streams
+        ``hc_post(all_reduce(out), *mix)`` with ``mix = (h, post, comb)``."""
         cfg = self.cfg
         T, hd, rd = x.shape[0], cfg.head_dim, cfg.rope_head_dim
         eps = cfg.norm_eps
@@ -313,11 +316,12 @@ class DeepSeekV4Model:
         og = o.view(T, self.groups, hpg * hd)
         lora = torch.cat([O.linear(og[:, g].contiguous(), L["wo_a"][g]) for g in range(self.groups)], dim=-1)
         fc = self.fused_comm
-        if fc is not None and fc.fits(T):  # row-parallel GEMM -> NVLS all-reduce (fused path F1)
-            return fc.gemm_allreduce(lora, L["wo_b"])
-        return self._allreduce(O.linear(lora, L["wo_b"]))
+        if fc is not None and fc.fits(T):  # row-parallel GEMM -> NVLS all-reduce + hc_post (fused path F1)
+            return fc.gemm_allreduce_hc_post(lora, L["wo_b"], *mix)
+        return O.hc_post(self._allreduce(O.linear(lora, L["wo_b"])), *mix)
 
-    def _moe(self, L, x, li: int):
+    def _moe(self, L, x, li: int, mix):
+        """MoE sub-block (routed + shared experts); returns ``hc_post(y, *mix)``."""
         cfg = self.cfg
         logits = O.linear_f32(x, L["gate"])
         w, ids = O.moe_topk_deepseek(logits, L["gate_bias"], cfg.n_activated_experts, cfg.score_func, cfg.route_scale)
@@ -328,9 +332,9 @@ class DeepSeekV4Model:
         if self.ep > 1:
             fc = self.fused_comm
             if fc is not None and self.ep_comm is self.comm and fc.fits(y.shape[0]):
-                return fc.allreduce(y)
+                return fc.allreduce_hc_post(y, *mix)
             self.ep_comm.all_reduce_(y)
-        return y
+        return O.hc_post(y, *mix)
 
     def forward_tokens(self, tokens: torch.Tensor, pos: torch.Tensor, bidx: torch.Tensor, st: DeepSeekV4State,
                        q_per_seq: int) -> torch.Tensor:
@@ -343,12 +347,11 @@ class DeepSeekV4Model:
         for li, L in enumerate(self.L):
             fn, sc, bs = L["hc_attn"]
             x, post, comb = O.hc_pre(h, fn, sc, bs, cfg.hc_sinkhorn_iters, cfg.hc_eps, cfg.norm_eps)
-            a = self._attn(L, O.rms_norm(x, L["attn_norm"], cfg.norm_eps, one_plus=False), st, li, pos, bidx, q_per_seq)
-            h = O.hc_post(a, h, post, comb)
+            h = self._attn(L, O.rms_norm(x, L["attn_norm"], cfg.norm_eps, one_plus=False), st, li, pos, bidx,
+                           q_per_seq, (h, post, comb))
             fn, sc, bs = L["hc_ffn"]
             x, post, comb = O.hc_pre(h, fn, sc, bs, cfg.hc_sinkhorn_iters, cfg.hc_eps, cfg.norm_eps)
-            m = self._moe(L, O.rms_norm(x, L["ffn_norm"], cfg.norm_eps, one_plus=False), li)
-            h = O.hc_post(m, h, post, comb)
+            h = self._moe(L, O.rms_norm(x, L["ffn_norm"], cfg.norm_eps, one_plus=False), li, (h, post, comb))
         fn, sc, bs = self.g["hc_head"]
         y, _, _ = O.hc_pre(h, fn, sc, bs, cfg.hc_sinkhorn_iters, cfg.hc_eps, cfg.norm_eps)
         return O.rms_norm(y, self.g["norm"], cfg.norm_eps, one_plus=False)

@@ -122,6 +122,31 @@ class FusedComm:
         self.gemm_allreduce_add_norm(a, w, acc, self._zero_norm(w.shape[0], a.device), 1e-6)
         return acc
 
+    def allreduce_hc_post(self, part: torch.Tensor, resid: torch.Tensor, post: torch.Tensor,
+                          comb: torch.Tensor) -> torch.Tensor:
+        """DeepSeek V4's hyper-connection post-mix of the all-reduced ``part
+        [rows, dim]``: ``out[t, j] = post[t, j] * sum_ranks(part)[t] + sum_i
+        comb[t, i, j] * resid[t, i]`` in one kernel after the partial's store
+        (``resid [rows, hc, dim]``)."""
+        o = ops()
+        o.symm_put_signal(part.contiguous(), self.local_ar, self.buf_elems, self.peer_flags_ar, self.state,
+                          self.rank)
+        return o.ar_hc_post(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
+                            resid.contiguous(), post.contiguous(), comb.contiguous(), self.timeout_s)
+
+    def gemm_allreduce_hc_post(self, a: torch.Tensor, w, resid: torch.Tensor, post: torch.Tensor,
+                               comb: torch.Tensor) -> torch.Tensor:
+        """``hc_post(all_reduce(a @ w.T), resid, post, comb)``: the row-parallel
+        GEMM's epilogue stores its partial into this rank's symmetric slot, and
+        one kernel reduces it through NVLS and applies the post-mix."""
+        o = ops()
+        if hasattr(w, "w8"):
+            from .. import ops as O
+            return self.allreduce_hc_post(O.linear(a, w), resid, post, comb)
+        o.gemm_symm(a, w, self.local_ar, self.buf_elems, w.shape[0], self.peer_flags_ar, self.state, self.rank)
+        return o.ar_hc_post(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
+                            resid.contiguous(), post.contiguous(), comb.contiguous(), self.timeout_s)
+
     def greedy(self, keys: torch.Tensor) -> torch.Tensor:
         return ops().greedy_allmax(keys.contiguous(), self.peer_slots, self.peer_flags_g,
                                    self.peer_flags_g[self.rank], self.state, self.rank, self.timeout_s)

@@ -30,6 +30,27 @@ struct ArNormArgs {
 };
 void ar_add_norm(const ArNormArgs& a, cudaStream_t st);
 
+// The all-reduce of a row-parallel partial [rows, cols] fused with DeepSeek V4's
+// hyper-connection post-mix: out[t, j, :] = post[t, j] * x[t, :] +
+// sum_i comb[t, i, j] * resid[t, i, :], x = the bf16-rounded sum over ranks.
+// Same slots, flags and selector protocol as ar_add_norm.
+struct ArHcArgs {
+  const __nv_bfloat16* mc_base;
+  long buf_stride;
+  int* sel;
+  const unsigned* flags;
+  int world;
+  const int* epoch;
+  const __nv_bfloat16* resid;  // [rows, hc, cols]
+  const float* post;           // [rows, hc]
+  const float* comb;           // [rows, hc, hc]
+  __nv_bfloat16* out;          // [rows, hc, cols]
+  int rows, cols, hc;
+  int* status;
+  unsigned long long limit_ns;
+};
+void ar_hc_post(const ArHcArgs& a, cudaStream_t st);
+
 // Sequence-parallel reduce-scatter + residual add + RMSNorm + all-gather of
 // one shard of rows (F1 in reduce-scatter mode feeding F2).
 struct SpNormArgs {

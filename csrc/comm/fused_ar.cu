@@ -166,6 +166,79 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(const __nv_bfloat16* m
   }
 }
 
+// One CTA per token: the partial rows of every rank summed through the switch
+// (multimem.ld_reduce, fp32), rounded to bf16 as the unfused all-reduce output
+// is, then DeepSeek V4's hyper-connection post-mix of the residual streams
+// (hc_post of csrc/kernels/deepseek.cu; the reference's all-reduce followed by
+// hc_post, contrib/deepseek-v4-flash/run_deepseek_v4_tp.py:541-556, 564-583).
+template <int HC>
+__global__ void __launch_bounds__(256) ar_hc_post_kernel(ArHcArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int cols = a.cols;
+  __shared__ float s_post[HC], s_comb[HC * HC];
+  if (threadIdx.x < HC) s_post[threadIdx.x] = a.post[(long)t * HC + threadIdx.x];
+  if (threadIdx.x < HC * HC) s_comb[threadIdx.x] = a.comb[(long)t * HC * HC + threadIdx.x];
+  const bool arrived = wait_flag_lane(a.flags, a.world, (unsigned)(*a.epoch), a.status, a.limit_ns);
+  // (the barrier also publishes s_post / s_comb)  a timed-out wait reads and writes nothing
+  if (!__syncthreads_and(arrived)) return;
+  const __nv_bfloat16* buf = a.mc_base + (long)((*a.sel) & 1) * a.buf_stride + (long)t * cols;
+  constexpr int kMaxVec = 4;  // 8 columns per vector, 256 threads: cols <= 8192
+  float v[kMaxVec][8];
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c < cols) mc_ld_reduce_bf16x8(buf + c, v[n]);
+  }
+#pragma unroll
+  for (int n = 0; n < kMaxVec; ++n) {
+    const int c = (threadIdx.x + n * blockDim.x) * 8;
+    if (c >= cols) continue;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16(v[n][e]));
+    float r[HC][8];
+#pragma unroll
+    for (int i = 0; i < HC; ++i) {
+      const uint4 rr = *reinterpret_cast<const uint4*>(a.resid + ((long)t * HC + i) * cols + c);
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(r2[e]);
+        r[i][2 * e] = f.x;
+        r[i][2 * e + 1] = f.y;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < HC; ++j) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float acc = s_post[j] * x[e];
+#pragma unroll
+        for (int i = 0; i < HC; ++i) acc += s_comb[i * HC + j] * r[i][e];
+        o[e] = acc;
+      }
+      uint4 w;
+      __nv_bfloat162* w2 = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w2[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+      *reinterpret_cast<uint4*>(a.out + ((long)t * HC + j) * cols + c) = w;
+    }
+  }
+  // flip the slot selector once every CTA has read it: last CTA (ticket)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int tk = atomicAdd(a.sel + 1, 1);
+    if (tk == (int)gridDim.x - 1) {
+      a.sel[1] = 0;
+      a.sel[0] = a.sel[0] + 1;
+    }
+  }
+}
+
 // One CTA per shard row: (sum of every rank's partial row through the switch |
 // a local addend) + residual -> RMSNorm(1+w) -> multicast store of the normed
 // row into every rank's gathered buffer; the last CTA flips the partial slot
@@ -311,6 +384,12 @@ void ar_add_norm(const ArNormArgs& a, cudaStream_t st) {
   BWN_CHECK(a.ldr % 8 == 0 && a.ldo % 8 == 0, "ar_add_norm: 16-byte aligned rows");
   launch_k(ar_add_norm_kernel, dim3(a.rows), dim3(256), 0, st, a.mc_base, a.buf_stride, a.sel, a.flags, a.world,
            a.epoch, a.resid, a.ldr, a.w, a.out, a.ldo, a.cols, a.eps, a.status, a.limit_ns);
+}
+
+void ar_hc_post(const ArHcArgs& a, cudaStream_t st) {
+  BWN_CHECK(a.hc == 4, "ar_hc_post: hc_mult 4 supported");
+  BWN_CHECK(a.cols % 8 == 0 && a.cols <= 256 * 8 * 4, "ar_hc_post: dim must be a multiple of 8, at most 8192");
+  launch_k(ar_hc_post_kernel<4>, dim3(a.rows), dim3(256), 0, st, a);
 }
 
 void greedy_allmax(const GreedyArgs& a, cudaStream_t st) {

@@ -118,6 +118,39 @@ Tensor ar_add_norm_op(int64_t mc_base, int64_t buf_stride, int64_t flags_local, 
   return out;
 }
 
+Tensor ar_hc_post_op(int64_t mc_base, int64_t buf_stride, int64_t flags_local, int64_t world,
+                     const Tensor& local_state, const Tensor& resid, const Tensor& post, const Tensor& comb,
+                     double timeout_s) {
+  check_bf16(resid, "resid");
+  check_f32(post, "post");
+  check_f32(comb, "comb");
+  TORCH_CHECK(resid.dim() == 3 && resid.is_contiguous(), "resid [rows, hc, cols] contiguous");
+  const int64_t rows = resid.size(0), hc = resid.size(1);
+  TORCH_CHECK(post.is_contiguous() && post.numel() == rows * hc, "post [rows, hc]");
+  TORCH_CHECK(comb.is_contiguous() && comb.numel() == rows * hc * hc, "comb [rows, hc, hc]");
+  const c10::cuda::CUDAGuard guard(resid.device());
+  auto out = at::empty_like(resid);
+  ArHcArgs a{};
+  a.mc_base = reinterpret_cast<const __nv_bfloat16*>(mc_base);
+  a.buf_stride = buf_stride;
+  int* ls = local_state.data_ptr<int>();
+  a.sel = ls + 2;
+  a.flags = reinterpret_cast<const unsigned*>(flags_local);
+  a.world = (int)world;
+  a.epoch = ls + 0;
+  a.resid = reinterpret_cast<const __nv_bfloat16*>(resid.data_ptr());
+  a.post = post.data_ptr<float>();
+  a.comb = comb.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.rows = (int)rows;
+  a.cols = (int)resid.size(2);
+  a.hc = (int)hc;
+  a.status = status_dev_ptr();
+  a.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  if (a.rows > 0) ar_hc_post(a, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
 Tensor greedy_allmax_op(const Tensor& keys, std::vector<int64_t> peer_slots, std::vector<int64_t> peer_flags,
                         int64_t flags_local, const Tensor& local_state, int64_t rank, double timeout_s) {
   check_cuda(keys, "keys");
@@ -387,6 +420,9 @@ void register_comm_defs(torch::Library& m) {
       "ar_add_norm(int mc_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
       "Tensor(b!) residual, Tensor w, float eps, float timeout_s) -> Tensor");
   m.def(
+      "ar_hc_post(int mc_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
+      "Tensor resid, Tensor post, Tensor comb, float timeout_s) -> Tensor");
+  m.def(
       "greedy_allmax(Tensor keys, int[] peer_slots, int[] peer_flags, int flags_local, Tensor(a!) local_state, "
       "int rank, float timeout_s) -> Tensor");
 }
@@ -404,6 +440,7 @@ void register_comm_impls(torch::Library& m) {
   m.impl("gemm_symm", &gemm_symm_op);
   m.impl("symm_put_signal", &symm_put_signal_op);
   m.impl("ar_add_norm", &ar_add_norm_op);
+  m.impl("ar_hc_post", &ar_hc_post_op);
   m.impl("greedy_allmax", &greedy_allmax_op);
 }
 }  // namespace bwn

@@ -65,18 +65,20 @@ class _FakeFused:
     reduction through the process group; counts the calls."""
 
     def __init__(self, comm):
-        self.comm, self.calls = comm, {"gemm_allreduce": 0, "allreduce": 0}
+        self.comm, self.calls = comm, {"gemm_allreduce_hc_post": 0, "allreduce_hc_post": 0}
 
     def fits(self, rows):
         return rows <= 256
 
-    def gemm_allreduce(self, a, w):
-        self.calls["gemm_allreduce"] += 1
-        return self.comm.all_reduce_(a.float() @ w.float().t())
+    def gemm_allreduce_hc_post(self, a, w, resid, post, comb):
+        from bwn.ops import reference as R
+        self.calls["gemm_allreduce_hc_post"] += 1
+        return R.hc_post(self.comm.all_reduce_(a.float() @ w.float().t()).to(resid.dtype), resid, post, comb)
 
-    def allreduce(self, part):
-        self.calls["allreduce"] += 1
-        return self.comm.all_reduce_(part.clone())
+    def allreduce_hc_post(self, part, resid, post, comb):
+        from bwn.ops import reference as R
+        self.calls["allreduce_hc_post"] += 1
+        return R.hc_post(self.comm.all_reduce_(part.clone()), resid, post, comb)
 
 
 def _fused_rank(rank, world, port, q):
@@ -109,7 +111,8 @@ def _fused_rank(rank, world, port, q):
 
 def test_deepseek_fused_comm_hooks_two_ranks():
     """With a fused communicator attached, each layer reduces its attention
-    output projection and its MoE partial through it, with the same result."""
+    output projection and its MoE partial through it, folded with the
+    hyper-connection post-mix, with the same result."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
@@ -122,4 +125,4 @@ def test_deepseek_fused_comm_hooks_two_ranks():
     for rank, err, calls, layers in res:
         assert not isinstance(err, str), err
         assert err < 1e-4, (rank, err)
-        assert calls == {"gemm_allreduce": layers, "allreduce": layers}, calls
+        assert calls == {"gemm_allreduce_hc_post": layers, "allreduce_hc_post": layers}, calls
