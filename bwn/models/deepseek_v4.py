@@ -314,7 +314,10 @@ class DeepSeekV4Model:
         o = O.mqa_attn(q, cache, pos + 1, q_per_seq, 1.0 / math.sqrt(hd))  # [T, H, hd]
         hpg = cfg.n_heads // cfg.o_groups
         og = o.view(T, self.groups, hpg * hd)
-        lora = torch.cat([O.linear(og[:, g].contiguous(), L["wo_a"][g]) for g in range(self.groups)], dim=-1)
+        olr = cfg.o_lora_rank
+        lora = torch.empty(T, self.groups * olr, dtype=x.dtype, device=x.device)
+        for g in range(self.groups):  # grouped low-rank projection straight into its column slice
+            O.linear_into(og[:, g], L["wo_a"][g], lora[:, g * olr:(g + 1) * olr])
         fc = self.fused_comm
         if fc is not None and fc.fits(T):  # row-parallel GEMM -> NVLS all-reduce + hc_post (fused path F1)
             return fc.gemm_allreduce_hc_post(lora, L["wo_b"], *mix)

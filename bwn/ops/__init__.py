@@ -54,6 +54,20 @@ def linear(x: torch.Tensor, w) -> torch.Tensor:
     return ref.linear(x, _dense(w).to(x.dtype))
 
 
+def linear_into(x: torch.Tensor, w, out: torch.Tensor) -> torch.Tensor:
+    """``out[:] = x @ w.T`` where ``x`` and ``out`` may be row-strided views
+    (a column slice of a wider matrix): the tcgen05 GEMM reads ``x`` and writes
+    ``out`` through their row strides, so no gather or concatenation is
+    launched.  Views whose base or row stride is not 16-byte aligned (the TMA
+    rule) go through a contiguous copy instead."""
+    if x.is_cuda and not _is_fp8(w) and all(
+            t.stride(1) == 1 and t.data_ptr() % 16 == 0 and t.stride(0) % 8 == 0 for t in (x, out)):
+        ops().linear_out(x, w, out, EPI_BF16, None)
+        return out
+    out.copy_(linear(x.contiguous() if x.is_cuda else x, w))
+    return out
+
+
 def linear_f32(x: torch.Tensor, w) -> torch.Tensor:
     if x.is_cuda:
         if _is_fp8(w):

@@ -59,6 +59,27 @@ def test_mn_major_gemms(M, N, K):
     O.check_status("mn-major gemm")
 
 
+@pytest.mark.parametrize("T", [1, 16, 300])
+def test_linear_into_strided_views(T):
+    """Grouped low-rank projection (DeepSeek's wo_a): each group's GEMM reads a
+    column slice of the attention output and writes a column slice of the
+    result, through the row strides; the columns around it stay untouched."""
+    G, Kg, R = 4, 512, 256
+    og = torch.randn(T, G * Kg, device=dev).bfloat16().view(T, G, Kg)
+    w = (torch.randn(G, R, Kg, device=dev) / math.sqrt(Kg)).bfloat16()
+    out = torch.full((T, G * R), 7.0, device=dev).bfloat16()
+    for g in range(0, G, 2):  # every other group: the skipped slices must keep their fill
+        O.linear_into(og[:, g], w[g], out[:, g * R:(g + 1) * R])
+    torch.cuda.synchronize()
+    O.check_status("linear_into")
+    for g in range(G):
+        got = out[:, g * R:(g + 1) * R]
+        if g % 2:
+            assert bool((got == 7.0).all())
+        else:
+            assert _rel(got, og[:, g].float() @ w[g].float().t()) < 1e-2
+
+
 @pytest.mark.parametrize("M", [1, 32, 200])
 def test_linear_swiglu_and_resid(M):
     K, I = 1024, 512
