@@ -1,0 +1,245 @@
+"""OpenAI-compatible HTTP surface of the server.
+
+The reference serves its models through a vLLM fork, whose OpenAI API is what
+its users call (``contrib/qwen3.6-27b/deploy/serve_qwen35.sh``,
+``serve_eagle3.sh``; ``contrib/qwen3.6-35b-a3b/VLLM_NEURON_ASSESSMENT.md``).
+This module gives the same endpoints over the bwn engines:
+
+* ``POST /v1/completions``: ``prompt`` as token ids or text; ``max_tokens``,
+  ``temperature``, ``stop`` (token ids, or strings that are one token each),
+  ``stop_token_ids``, ``ignore_eos``, ``stream`` (server-sent events, one
+  chunk per token as the continuous engine produces it, then ``[DONE]``);
+* ``POST /v1/chat/completions``: ``messages`` rendered by the tokenizer's chat
+  template; the reply as ``message`` (or ``delta`` chunks when streaming);
+* ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).
+
+Text needs a tokenizer: a local HF tokenizer directory (usually the checkpoint
+directory) loaded with ``transformers`` offline.  Without one the server takes
+and returns token ids only.  Every choice carries ``tokens`` (the generated
+ids) beside ``text``.
+"""
+from __future__ import annotations
+
+import itertools
+import json
+import queue
+import time
+
+from pydantic import BaseModel
+
+from .engine import Request
+
+_ids = itertools.count()
+
+
+class CompletionIn(BaseModel):
+    prompt: list[int] | str
+    max_tokens: int = 16
+    stop: list[int] | list[str] | str | None = None
+    stop_token_ids: list[int] = []
+    temperature: float = 0.0
+    ignore_eos: bool = False
+    stream: bool = False
+    model: str | None = None
+
+
+class ChatMessage(BaseModel):
+    role: str
+    content: str
+
+
+class ChatIn(BaseModel):
+    messages: list[ChatMessage]
+    max_tokens: int = 16
+    stop: list[int] | list[str] | str | None = None
+    stop_token_ids: list[int] = []
+    temperature: float = 0.0
+    ignore_eos: bool = False
+    stream: bool = False
+    model: str | None = None
+
+
+class TextCodec:
+    """Token ids <-> text through a local HF tokenizer."""
+
+    def __init__(self, tokenizer):
+        self.tok = tokenizer
+        eos = getattr(tokenizer, "eos_token_id", None)
+        self.eos = [] if eos is None else ([int(e) for e in eos] if isinstance(eos, (list, tuple)) else [int(eos)])
+
+    def encode(self, text: str) -> list[int]:
+        return [int(i) for i in self.tok.encode(text, add_special_tokens=False)]
+
+    def decode(self, ids: list[int]) -> str:
+        return self.tok.decode(ids, skip_special_tokens=True)
+
+    def chat(self, messages: list[dict]) -> list[int]:
+        out = self.tok.apply_chat_template(messages, add_generation_prompt=True, tokenize=True)
+        if hasattr(out, "keys"):  # a BatchEncoding
+            out = out["input_ids"]
+        return [int(i) for i in out]
+
+    def stop_id(self, s: str) -> int:
+        ids = self.encode(s)
+        if len(ids) != 1:
+            raise ValueError(f"stop string {s!r} is {len(ids)} tokens; only single-token stop strings are supported")
+        return ids[0]
+
+
+def load_tokenizer(path: str) -> TextCodec | None:
+    """The HF tokenizer saved in ``path`` (``tokenizer.json`` /
+    ``tokenizer_config.json``), or None when the directory has none."""
+    import os
+    if not path or not any(os.path.exists(os.path.join(path, f))
+                           for f in ("tokenizer.json", "tokenizer_config.json", "tokenizer.model")):
+        return None
+    from transformers import AutoTokenizer
+    return TextCodec(AutoTokenizer.from_pretrained(path, local_files_only=True))
+
+
+class _Incremental:
+    """Streams text deltas: the decode of every id so far, minus what was sent
+    (a multi-token character appears once it is complete)."""
+
+    def __init__(self, codec: TextCodec | None):
+        self.codec, self.ids, self.sent = codec, [], ""
+
+    def push(self, tok: int) -> str | None:
+        self.ids.append(tok)
+        if self.codec is None:
+            return None
+        text = self.codec.decode(self.ids)
+        if text.endswith("�"):  # an incomplete byte sequence: wait for the next token
+            return ""
+        delta, self.sent = text[len(self.sent):], text
+        return delta
+
+
+def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import PlainTextResponse, StreamingResponse
+
+    app = FastAPI(title="bwn")
+
+    def stop_ids(body) -> list[int]:
+        out = list(body.stop_token_ids)
+        stops = [body.stop] if isinstance(body.stop, (str, int)) else (body.stop or [])
+        for s in stops:
+            if isinstance(s, int):
+                out.append(s)
+            elif codec is None:
+                raise HTTPException(400, "stop strings need a tokenizer (--tokenizer)")
+            else:
+                try:
+                    out.append(codec.stop_id(s))
+                except ValueError as e:
+                    raise HTTPException(400, str(e)) from e
+        if codec is not None and not body.ignore_eos:
+            out += [e for e in codec.eos if e not in out]
+        return out
+
+    def run(prompt: list[int], body, stream: bool):
+        if not prompt:
+            raise HTTPException(400, "prompt must hold at least one token id")
+        q: queue.Queue = queue.Queue()
+        req = Request(prompt, body.max_tokens, stop_ids(body), body.temperature,
+                      on_token=q.put if stream else None)
+        fut = worker.submit(req)
+        if stream:
+            return fut, q
+        try:
+            return fut.result(timeout=600), None
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+
+    def events(fut, q, chunk):
+        """SSE body: one chunk per token while the engine produces them, the
+        rest (engines that finish a request at once) after it completes, then
+        a final chunk with the finish reason and ``[DONE]``."""
+        inc = _Incremental(codec)
+        n = 0
+        while True:
+            try:
+                tok = q.get(timeout=0.05)
+            except queue.Empty:
+                if fut.done():
+                    break
+                continue
+            n += 1
+            yield "data: " + json.dumps(chunk([tok], inc.push(tok), None)) + "\n\n"
+        try:
+            res = fut.result()
+        except Exception as e:  # noqa: BLE001 - headers are sent: report in the stream
+            yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
+            yield "data: [DONE]\n\n"
+            return
+        while not q.empty():  # tokens queued after the last poll
+            q.get_nowait()
+        rest = res.tokens[n:]
+        for tok in rest:
+            yield "data: " + json.dumps(chunk([tok], inc.push(tok), None)) + "\n\n"
+        yield "data: " + json.dumps(chunk([], "" if codec else None, res.finish_reason)) + "\n\n"
+        yield "data: [DONE]\n\n"
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok", "model": model_name}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "bwn"}]}
+
+    @app.post("/v1/completions")
+    def completions(body: CompletionIn):
+        if isinstance(body.prompt, str):
+            if codec is None:
+                raise HTTPException(400, "text prompts need a tokenizer (--tokenizer); send token ids")
+            prompt = codec.encode(body.prompt)
+        else:
+            prompt = body.prompt
+        cid, created = f"cmpl-{next(_ids)}", int(time.time())
+        out, q = run(prompt, body, body.stream)
+        if body.stream:
+            def chunk(toks, text, fin):
+                return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
+                        "choices": [{"index": 0, "text": text, "tokens": toks, "finish_reason": fin}]}
+            return StreamingResponse(events(out, q, chunk), media_type="text/event-stream")
+        return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "text": codec.decode(out.tokens) if codec else None,
+                             "tokens": out.tokens, "finish_reason": out.finish_reason}],
+                "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out.tokens),
+                          "total_tokens": len(prompt) + len(out.tokens)},
+                "timing_ms": {"prefill": round(out.prefill_ms, 3), "decode": round(out.decode_ms, 3)}}
+
+    @app.post("/v1/chat/completions")
+    def chat(body: ChatIn):
+        if codec is None:
+            raise HTTPException(400, "chat needs a tokenizer with a chat template (--tokenizer)")
+        try:
+            prompt = codec.chat([m.model_dump() for m in body.messages])
+        except Exception as e:  # noqa: BLE001 - a template that cannot render these messages
+            raise HTTPException(400, f"chat template: {e}") from e
+        cid, created = f"chatcmpl-{next(_ids)}", int(time.time())
+        out, q = run(prompt, body, body.stream)
+        if body.stream:
+            first = [True]
+
+            def chunk(toks, text, fin):
+                delta = {"content": text} if text else {}
+                if first[0]:
+                    delta["role"], first[0] = "assistant", False
+                return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
+                        "choices": [{"index": 0, "delta": delta, "tokens": toks, "finish_reason": fin}]}
+            return StreamingResponse(events(out, q, chunk), media_type="text/event-stream")
+        return {"id": cid, "object": "chat.completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "message": {"role": "assistant", "content": codec.decode(out.tokens)},
+                             "tokens": out.tokens, "finish_reason": out.finish_reason}],
+                "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out.tokens),
+                          "total_tokens": len(prompt) + len(out.tokens)}}
+
+    @app.get("/metrics", response_class=PlainTextResponse)
+    def metrics():
+        s = worker.stats
+        return "".join(f"bwn_{k}_total {v}\n" for k, v in s.items())
+
+    return app

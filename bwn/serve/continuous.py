@@ -107,6 +107,8 @@ class ContinuousEngine:
         for r in active:
             s = self.slots[r]
             s.tokens.append(int(nxt[r]))
+            if s.req.on_token is not None:
+                s.req.on_token(s.tokens[-1])
             fin = self._maybe_finish(r, dt)
             if fin is not None:
                 done.append(fin)
@@ -147,6 +149,8 @@ class ContinuousEngine:
         ms = (time.perf_counter() - t0) * 1e3
         self.slots[r] = _Slot(rid, req, [tok], time.perf_counter(), ms)
         self.stats["admitted"] += 1
+        if req.on_token is not None:
+            req.on_token(tok)
         return self._maybe_finish(r, 0.0)
 
     def _maybe_finish(self, r: int, step_ms: float):

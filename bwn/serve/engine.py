@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
+from typing import Callable
 
 import torch
 
@@ -24,6 +25,9 @@ class Request:
     max_tokens: int = 16
     stop: list[int] = field(default_factory=list)
     temperature: float = 0.0  # 0: greedy; > 0: sampled (engines built with sampling=True)
+    # called with each new token id as the continuous engine produces it (streaming);
+    # engines that finish a request at once leave it to the caller
+    on_token: Callable[[int], None] | None = field(default=None, compare=False, repr=False)
 
 
 @dataclass

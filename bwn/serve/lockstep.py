@@ -12,6 +12,7 @@ timeout.  (The reference's multi-core serving runs inside its vLLM fork,
 """
 from __future__ import annotations
 
+import dataclasses
 import datetime
 
 import torch.distributed as dist
@@ -37,7 +38,7 @@ class LockstepEngine:
 
     def add(self, req) -> int:
         rid = self.e.add(req)  # a request the engine rejects is not sent
-        self.pending.append(req)
+        self.pending.append(dataclasses.replace(req, on_token=None))  # callbacks stay on rank 0
         return rid
 
     def idle(self) -> bool:
@@ -69,7 +70,8 @@ class LockstepBatchEngine:
         self.max_batch = engine.max_batch
 
     def generate(self, reqs):
-        dist.broadcast_object_list([("generate", list(reqs))], src=0, group=self.group)
+        sent = [dataclasses.replace(r, on_token=None) for r in reqs]
+        dist.broadcast_object_list([("generate", sent)], src=0, group=self.group)
         return self.e.generate(reqs)
 
     def stop(self) -> None:

@@ -1,7 +1,9 @@
-"""HTTP completion server (``/v1/completions``, ``/health``, ``/metrics``).
+"""HTTP server with the OpenAI API (``/v1/completions``,
+``/v1/chat/completions``, ``/v1/models``, streaming; :mod:`bwn.serve.api`) plus
+``/health`` and ``/metrics``.
 
-Requests carry token ids (``prompt``: list of ints; a tokenizer is outside the
-framework).  Two schedulers:
+Prompts are token ids, or text when a tokenizer is loaded (``--tokenizer``,
+by default the checkpoint directory's).  Three schedulers:
 
 * ``static`` (:class:`BatchingWorker`): a worker thread drains the queue into
   batches of at most ``max_batch`` requests (waiting up to ``batch_window_ms``
@@ -23,16 +25,8 @@ import threading
 import time
 from concurrent.futures import Future
 
-from pydantic import BaseModel
-
+from .api import build_app, load_tokenizer  # noqa: F401 - build_app is this module's app factory too
 from .engine import GenerationEngine, Request
-
-
-class CompletionIn(BaseModel):
-    prompt: list[int]
-    max_tokens: int = 16
-    stop: list[int] = []
-    temperature: float = 0.0
 
 
 class BatchingWorker:
@@ -147,37 +141,6 @@ class ContinuousWorker:
             self.engine.stop()
 
 
-def build_app(worker, model_name: str = "bwn"):
-    from fastapi import FastAPI, HTTPException
-    from fastapi.responses import PlainTextResponse
-
-    app = FastAPI(title="bwn")
-
-    @app.get("/health")
-    def health():
-        return {"status": "ok", "model": model_name}
-
-    @app.post("/v1/completions")
-    def completions(body: CompletionIn):
-        if not body.prompt:
-            raise HTTPException(400, "prompt must hold at least one token id")
-        try:
-            out = worker.submit(Request(body.prompt, body.max_tokens, body.stop, body.temperature)).result(timeout=600)
-        except ValueError as e:
-            raise HTTPException(400, str(e)) from e
-        return {"object": "text_completion", "model": model_name,
-                "choices": [{"index": 0, "tokens": out.tokens, "finish_reason": out.finish_reason}],
-                "usage": {"prompt_tokens": len(body.prompt), "completion_tokens": len(out.tokens)},
-                "timing_ms": {"prefill": round(out.prefill_ms, 3), "decode": round(out.decode_ms, 3)}}
-
-    @app.get("/metrics", response_class=PlainTextResponse)
-    def metrics():
-        s = worker.stats
-        return "".join(f"bwn_{k}_total {v}\n" for k, v in s.items())
-
-    return app
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="tiny", choices=["tiny", "27b", "35b"])
@@ -190,6 +153,8 @@ def main():
     ap.add_argument("--draft", default="", help="spec: EAGLE3 draft safetensors directory (random 1-layer when empty)")
     ap.add_argument("--num-draft", type=int, default=3, help="spec: draft tokens per step")
     ap.add_argument("--sampling", action="store_true", help="continuous scheduler: honour request temperatures")
+    ap.add_argument("--tokenizer", default="", help="HF tokenizer directory (default: the checkpoint's, if any)")
+    ap.add_argument("--served-model-name", default="", help="model id in responses (default: --model)")
     a = ap.parse_args()
     import torch
     import uvicorn
@@ -235,8 +200,11 @@ def main():
             return
         engine = (LockstepEngine if a.scheduler == "continuous" else LockstepBatchEngine)(engine, ctrl)
     worker = ContinuousWorker(engine) if a.scheduler == "continuous" else BatchingWorker(engine)
+    codec = load_tokenizer(a.tokenizer or a.checkpoint)
+    if a.tokenizer and codec is None:
+        raise SystemExit(f"no tokenizer files in {a.tokenizer}")
     try:
-        uvicorn.run(build_app(worker, a.model), host=a.host, port=a.port)
+        uvicorn.run(build_app(worker, a.served_model_name or a.model, codec), host=a.host, port=a.port)
     finally:
         worker.stop()
 
