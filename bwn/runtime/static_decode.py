@@ -141,21 +141,34 @@ def main(argv=None) -> None:
     from ..parallel.comm import init_distributed
     from ..utils import fingerprint as F
 
+    # the reference harness's flag names are accepted as aliases (--batch-size, --num-layers,
+    # --num-tokens, --model-path, --bucket-chunk, --fp8-weights, --tiny, --skip-compile)
     ap = argparse.ArgumentParser(description="static greedy decode")
     ap.add_argument("--model", default="tiny", choices=["27b", "35b", "tiny", "tiny-moe"])
-    ap.add_argument("--checkpoint", default="", help="HF safetensors directory (config.json beside it)")
-    ap.add_argument("--layers", type=int, default=0, help="truncate to this many layers (random models)")
+    ap.add_argument("--tiny", dest="model", action="store_const", const="tiny", help="= --model tiny")
+    ap.add_argument("--checkpoint", "--model-path", default="", help="HF safetensors directory (config.json beside it)")
+    ap.add_argument("--layers", "--num-layers", type=int, default=0, help="truncate to this many layers")
     ap.add_argument("--prompt-ids", default="", help="comma-separated prompt token ids (every row)")
     ap.add_argument("--prompt-len", type=int, default=16, help="uniform-random prompt length without --prompt-ids")
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--max-new", type=int, default=16)
-    ap.add_argument("--bucket", type=int, default=0, help="prefill chunk length (0: whole prompt)")
+    ap.add_argument("--batch", "--batch-size", type=int, default=1)
+    ap.add_argument("--max-new", "--num-tokens", type=int, default=16)
+    ap.add_argument("--max-seq-len", type=int, default=0, help="KV / cache length (0: prompt + new tokens + 8)")
+    ap.add_argument("--bucket", "--bucket-chunk", type=int, default=0, help="prefill chunk length (0: whole prompt)")
+    ap.add_argument("--skip-prefill", action="store_true",
+                    help="decode from the prompt's last token over an empty cache (decode-only runs)")
+    ap.add_argument("--bench", action="store_true", help="after decode, time a synced TPOT window")
+    ap.add_argument("--bench-iters", type=int, default=50, help="decode steps in the --bench window")
+    ap.add_argument("--prefill-bench", type=int, default=0,
+                    help="time the prefill of a synthetic N-token prompt (tok/s, TTFT) and exit")
+    ap.add_argument("--prefill-bench-sweep", default="", help="comma-separated further lengths after --prefill-bench")
+    ap.add_argument("--graph-splits", "--prefill-splits", type=int, default=0,
+                    help="accepted for the reference's command lines; a CUDA graph needs no compile partitioning")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--fp8", action="store_true", help="W8A16 projection weights")
+    ap.add_argument("--fp8", "--fp8-weights", action="store_true", help="W8A16 projection weights")
     ap.add_argument("--fp8-experts", action="store_true",
                     help="MoE: routed experts in fp8 (an official FP8 checkpoint's stay fp8; random ones are quantized)")
     ap.add_argument("--fused-comm", action="store_true", help="N>1: fused NVLink reductions")
-    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-graph", "--skip-compile", action="store_true", help="eager steps, no CUDA graph")
     ap.add_argument("--prefill-gen", action="store_true",
                     help="also generate by re-prefilling the growing sequence each step (the reference's PREFILL_GEN "
                          "coherence check) and report whether it matches the decode path")
@@ -182,26 +195,67 @@ def main(argv=None) -> None:
         from ..parallel.fused import enable_fused_comm
         enable_fused_comm(model)
     cfg = model.cfg
+
+    def sync():
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
+
+    def finish():
+        if comm.size > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+    if a.prefill_bench:  # prompt-ingest throughput at each length, then exit
+        lens = [a.prefill_bench] + [int(x) for x in a.prefill_bench_sweep.split(",") if x.strip()]
+        g = torch.Generator().manual_seed(a.seed)
+        for n in lens:
+            ids = torch.randint(0, cfg.vocab, (a.batch, n), generator=g).to(dev)
+            st = model.new_state(a.batch, n + 8)
+            bucket = a.bucket or n
+            times = []
+            for _ in range(2):  # the first pass warms the kernels and allocator
+                st.reset()
+                sync()
+                t0 = time.perf_counter()
+                for c0 in range(0, n, bucket):
+                    last = model.prefill_hidden(ids[:, c0:c0 + bucket], st, None)
+                model.greedy(last)
+                sync()
+                times.append(comm.max_scalar(time.perf_counter() - t0, None if cpu else dev))
+            del st
+            if comm.rank == 0:
+                print(json.dumps({"model": cfg.name, "tp": comm.size, "batch": a.batch, "prefill_tokens": n,
+                                  "bucket": bucket, "ttft_ms": round(times[-1] * 1e3, 2),
+                                  "prefill_tok_s": round(a.batch * n / times[-1], 1),
+                                  "timing": "host clock around synchronize, max over ranks"}), flush=True)
+        finish()
+        return
+
     if a.prompt_ids:
         ids = [int(t) for t in a.prompt_ids.split(",") if t.strip()]
         prompt = torch.tensor([ids] * a.batch, dtype=torch.long)
     else:
         prompt = torch.randint(0, cfg.vocab, (a.batch, a.prompt_len), generator=torch.Generator().manual_seed(a.seed))
     S = prompt.shape[1]
-    dec = StaticDecoder(model, a.batch, S + a.max_new + 8, use_graph=not a.no_graph)
+    steps_after = a.max_new + (a.bench_iters if a.bench else 0)
+    max_seq = a.max_seq_len or (S + steps_after + 8)
+    if max_seq < S + steps_after:
+        raise SystemExit(f"--max-seq-len {max_seq} < prompt {S} + {steps_after} decode steps")
+    dec = StaticDecoder(model, a.batch, max_seq, use_graph=not a.no_graph)
     dec.capture()
-
-    def sync():
-        if dev.type == "cuda":
-            torch.cuda.synchronize(dev)
 
     sync()
     t0 = time.perf_counter()
-    bucket = a.bucket or S
-    for c0 in range(0, S, bucket):  # bucketed prefill; the last chunk's hidden gives the logits
-        last = model.prefill_hidden(prompt[:, c0:c0 + bucket].to(dev), dec.st, None)
-    logits = model.logits(last)
-    first = model.greedy(last)
+    logits = None
+    if a.skip_prefill:  # decode-only: the prompt's last token at position 0 of an empty cache
+        first = prompt[:, -1].to(dev)
+    else:
+        bucket = a.bucket or S
+        for c0 in range(0, S, bucket):  # bucketed prefill; the last chunk's hidden gives the logits
+            last = model.prefill_hidden(prompt[:, c0:c0 + bucket].to(dev), dec.st, None)
+        logits = model.logits(last)
+        first = model.greedy(last)
     dec.tokens.copy_(first.to(dec.tokens.dtype))
     sync()
     ttft = (time.perf_counter() - t0) * 1e3
@@ -212,6 +266,24 @@ def main(argv=None) -> None:
         out.append(dec.next_ids.clone().cpu())
     sync()
     tpot = (time.perf_counter() - t1) * 1e3 / max(1, a.max_new - 1)
+    bench = None
+    if a.bench:  # synced TPOT window: device time of bench_iters further steps, max over ranks
+        if dev.type == "cuda":
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.bench_iters):
+                dec.step_device()
+            e1.record()
+            sync()
+            ms = e0.elapsed_time(e1)
+        else:
+            tb = time.perf_counter()
+            for _ in range(a.bench_iters):
+                dec.step_device()
+            ms = (time.perf_counter() - tb) * 1e3
+        ms = comm.max_scalar(ms, None if cpu else dev)
+        bench = {"bench_iters": a.bench_iters, "bench_tpot_ms": round(ms / a.bench_iters, 4),
+                 "bench_tok_s": round(a.batch * a.bench_iters * 1e3 / ms, 1)}
     check_status("static_decode")
     gen = torch.stack(out, 1)
     occupancy = F.check_qwen36_state(dec.st, f"decode state rank={comm.rank}")
@@ -229,16 +301,14 @@ def main(argv=None) -> None:
         print(json.dumps({
             "model": cfg.name, "tp": comm.size, "batch": a.batch, "prompt_len": S,
             "generated_row0": gen[0].tolist(), "gen_hash_row0": F.gen_hash(gen[0]),
-            "prefill_fingerprint": F.logits_fingerprint(logits.float().cpu()),
+            "prefill_fingerprint": F.logits_fingerprint(logits.float().cpu()) if logits is not None else None,
             "ttft_ms": round(ttft, 2), "tpot_ms": round(tpot, 3),
             "occupied_ssm_layers": len(occupancy["ssm"]), "graph": dec.graph is not None,
+            "skip_prefill": a.skip_prefill, **(bench or {}),
             **({"prefill_gen_hash_row0": F.gen_hash(pgen[0]), "prefill_gen_matches": bool(torch.equal(pgen, gen))}
                if pgen is not None else {})}))
     dec.release()
-    if comm.size > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
+    finish()
 
 
 if __name__ == "__main__":

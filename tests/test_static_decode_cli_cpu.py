@@ -53,3 +53,28 @@ def test_checkpoint_with_prompt_ids(tmp_path):
                 "7,11,13,17,19", "--max-new", "4"])
     assert out["prompt_len"] == 5 and len(out["generated_row0"]) == 4
     assert torch.tensor(out["generated_row0"]).max() < cfg.vocab
+
+
+def _run_all(args):
+    r = subprocess.run([sys.executable] + args, env=ENV, cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return [json.loads(ln) for ln in r.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_reference_flag_names_and_bench_modes():
+    """The reference harness's command line runs as is: --tiny, --batch-size,
+    --num-tokens, --bucket-chunk, --skip-compile name the same settings; --bench
+    adds a TPOT window after the generated tokens; --skip-prefill decodes from
+    the last prompt token; --prefill-bench (+ sweep) reports prompt-ingest
+    throughput per length and exits."""
+    ref = _run(BASE)
+    alias = _run(["-m", "bwn.runtime.static_decode", "--tiny", "--cpu", "--batch-size", "2", "--prompt-len", "12",
+                  "--num-tokens", "6", "--bucket-chunk", "5", "--skip-compile", "--bench", "--bench-iters", "3"])
+    assert alias["gen_hash_row0"] == ref["gen_hash_row0"] and alias["batch"] == 2
+    assert alias["bench_iters"] == 3 and alias["bench_tpot_ms"] > 0 and alias["bench_tok_s"] > 0
+    skip = _run(BASE + ["--skip-prefill"])
+    assert skip["skip_prefill"] and skip["prefill_fingerprint"] is None and len(skip["generated_row0"]) == 6
+    lines = _run_all(["-m", "bwn.runtime.static_decode", "--tiny", "--cpu", "--prefill-bench", "32",
+                      "--prefill-bench-sweep", "16,48", "--bucket-chunk", "16"])
+    assert [ln["prefill_tokens"] for ln in lines] == [32, 16, 48]
+    assert all(ln["prefill_tok_s"] > 0 and ln["bucket"] == 16 for ln in lines)
