@@ -404,7 +404,9 @@ def main(argv=None) -> None:
     from ..parallel.comm import hybrid_groups, init_distributed
 
     ap = argparse.ArgumentParser(description="DeepSeek V4 greedy generation")
-    ap.add_argument("--checkpoint", default="", help="checkpoint directory (config.json beside the weights)")
+    ap.add_argument("--checkpoint", "--model-path", default="",
+                    help="checkpoint directory (config.json beside the weights), or the per-rank files of "
+                         "bwn.io.deepseek_weights (detected)")
     ap.add_argument("--presharded", action="store_true", help="per-rank files from bwn.io.deepseek_weights")
     ap.add_argument("--tiny", action="store_true", help="random tiny model instead of a checkpoint")
     ap.add_argument("--prompt-ids", default="", help="comma-separated prompt ids (random when empty)")

@@ -66,12 +66,13 @@ def predict_masked_middle(model, seqs: list[str], max_len: int | None = None) ->
     return out
 
 
-def main():
+def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--size", default="8M", choices=sorted(ESM2_SIZES))
+    ap.add_argument("--size", "--model-size", default="8M", choices=sorted(ESM2_SIZES))
     ap.add_argument("--checkpoint", default="", help="HF safetensors directory (random init when empty)")
-    ap.add_argument("--max-len", type=int, default=128)
-    args = ap.parse_args()
+    ap.add_argument("--max-len", "--max-seq-len", type=int, default=128, help="padded length")
+    ap.add_argument("--sequences", nargs="+", default=None, help="protein sequences (the middle residue is masked)")
+    args = ap.parse_args(argv)
     from ..models.esm2 import EsmForMaskedLM
     from ..parallel.comm import init_distributed
     comm = init_distributed()
@@ -87,7 +88,7 @@ def main():
     if comm.size > 1:
         from ..parallel.tensor_parallel import apply_esm_tp
         model = apply_esm_tp(model, comm)
-    res = predict_masked_middle(model, DEFAULT_SEQUENCES, args.max_len)
+    res = predict_masked_middle(model, args.sequences or DEFAULT_SEQUENCES, args.max_len)
     if comm.rank == 0:
         print(json.dumps(res))
 

@@ -85,3 +85,14 @@ def test_tokenize_and_predict_masked_middle():
     assert int(ids[0, 3]) == m.cfg.mask_token_id and int(ids[0, 0]) == m.cfg.cls_token_id
     res = predict_masked_middle(m, ["MKTVRQERLK", "KALTAR"])
     assert [r["position"] for r in res] == [5, 3] and all(0 < r["prob"] <= 1 for r in res)
+
+
+def test_infer_command_with_reference_flags(capsys):
+    """``python -m bwn.train.esm_infer`` with the reference's flag names
+    (``--model-size``, ``--max-seq-len``, ``--sequences``)."""
+    import json
+
+    from bwn.train.esm_infer import main
+    main(["--model-size", "8M", "--max-seq-len", "32", "--sequences", "MKTVRQERLK", "KALTAR"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert [r["position"] for r in res] == [5, 3] and [r["true"] for r in res] == ["Q", "T"]
