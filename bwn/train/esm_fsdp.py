@@ -69,6 +69,7 @@ def main(argv=None) -> None:
     ap.add_argument("--lr", type=float, default=5e-5)
     ap.add_argument("--fasta", default=None)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-compile", action="store_true", help="accepted for the reference's command line: steps always run eagerly")
     ap.add_argument("--cpu", action="store_true")
     a = ap.parse_args(argv)
 
