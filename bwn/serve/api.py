@@ -239,7 +239,13 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
 
     @app.get("/metrics", response_class=PlainTextResponse)
     def metrics():
-        s = worker.stats
-        return "".join(f"bwn_{k}_total {v}\n" for k, v in s.items())
+        """Prometheus text: counters, request latency summaries (TTFT, TPOT),
+        and the continuous scheduler's running / waiting gauges."""
+        out = "".join(f"bwn_{k}_total {v}\n" for k, v in worker.stats.items())
+        if hasattr(worker, "latency"):
+            out += worker.latency.prometheus()
+        if hasattr(worker, "gauges"):
+            out += "".join(f"bwn_{k} {v}\n" for k, v in worker.gauges().items())
+        return out
 
     return app

@@ -29,12 +29,46 @@ from .api import build_app, load_tokenizer  # noqa: F401 - build_app is this mod
 from .engine import GenerationEngine, Request
 
 
+class LatencyStats:
+    """Per-request TTFT (prefill) and TPOT (decode time per token after the
+    first) for ``/metrics``: running sums and counts, and quantiles over the
+    last ``window`` requests."""
+
+    def __init__(self, window: int = 1000):
+        from collections import deque
+        self.lock = threading.Lock()
+        self.vals = {"ttft_ms": deque(maxlen=window), "tpot_ms": deque(maxlen=window)}
+        self.sums = {"ttft_ms": 0.0, "tpot_ms": 0.0}
+        self.count = 0
+
+    def record(self, res) -> None:
+        tpot = res.decode_ms / max(1, len(res.tokens) - 1)
+        with self.lock:
+            for k, v in (("ttft_ms", res.prefill_ms), ("tpot_ms", tpot)):
+                self.vals[k].append(v)
+                self.sums[k] += v
+            self.count += 1
+
+    def prometheus(self) -> str:
+        out = []
+        with self.lock:
+            for k, vals in self.vals.items():
+                out.append(f"# TYPE bwn_{k} summary\n")
+                srt = sorted(vals)
+                for q in (0.5, 0.9, 0.99):
+                    if srt:
+                        out.append(f'bwn_{k}{{quantile="{q}"}} {srt[min(len(srt) - 1, int(q * len(srt)))]:.4f}\n')
+                out.append(f"bwn_{k}_sum {self.sums[k]:.4f}\nbwn_{k}_count {self.count}\n")
+        return "".join(out)
+
+
 class BatchingWorker:
     def __init__(self, engine: GenerationEngine, batch_window_ms: float = 5.0):
         self.engine = engine
         self.window = batch_window_ms / 1e3
         self.q: queue.Queue = queue.Queue()
         self.stats = {"requests": 0, "batches": 0, "tokens": 0}
+        self.latency = LatencyStats()
         self._stop = False
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
@@ -63,6 +97,7 @@ class BatchingWorker:
             try:
                 res = self.engine.generate([r for r, _ in batch])
                 for (_, fut), out in zip(batch, res):
+                    self.latency.record(out)
                     fut.set_result(out)
                 self.stats["requests"] += len(batch)
                 self.stats["batches"] += 1
@@ -88,6 +123,7 @@ class ContinuousWorker:
         self.q: queue.Queue = queue.Queue()
         self.futs: dict[int, Future] = {}
         self.stats = {"requests": 0, "steps": 0, "tokens": 0}
+        self.latency = LatencyStats()
         self._stop = False
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
@@ -132,7 +168,12 @@ class ContinuousWorker:
             for rid, res in finished:
                 self.stats["requests"] += 1
                 self.stats["tokens"] += len(res.tokens)
+                self.latency.record(res)
                 self.futs.pop(rid).set_result(res)
+
+    def gauges(self) -> dict:
+        e = getattr(self.engine, "e", self.engine)  # a lockstep handle wraps the engine
+        return {"running_requests": sum(s is not None for s in e.slots), "waiting_requests": len(e.waiting)}
 
     def stop(self):
         self._stop = True

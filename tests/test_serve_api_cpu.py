@@ -141,3 +141,17 @@ def test_chat_completions(model, tmp_path):
         assert chunks[-1]["choices"][0]["finish_reason"] == "length"
     finally:
         worker.stop()
+
+
+def test_metrics_latency_summaries(model):
+    client, worker = _continuous_client(model, None)
+    try:
+        for p in ([5, 9, 13], [7, 2]):
+            assert client.post("/v1/completions", json={"prompt": p, "max_tokens": 3}).status_code == 200
+        text = client.get("/metrics").text
+        assert "bwn_requests_total 2" in text
+        assert "bwn_ttft_ms_count 2" in text and "bwn_tpot_ms_count 2" in text
+        assert 'bwn_ttft_ms{quantile="0.5"}' in text
+        assert "bwn_running_requests 0" in text and "bwn_waiting_requests 0" in text
+    finally:
+        worker.stop()
