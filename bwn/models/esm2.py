@@ -11,8 +11,6 @@ training with fp32 master weights.
 """
 from __future__ import annotations
 
-import math
-
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
@@ -32,9 +30,7 @@ class _BwnLinearFn(torch.autograd.Function):
     def forward(ctx, x2d, w, b):
         xb = x2d.to(torch.bfloat16).contiguous()
         wb = w.to(torch.bfloat16).contiguous()
-        y = O.linear(xb, wb)
-        if b is not None:
-            y = y + b.to(y.dtype)
+        y = O.linear(xb, wb) if b is None else O.linear_bias(xb, wb, b)
         ctx.save_for_backward(xb, wb)
         ctx.has_b = b is not None
         ctx.w_dtype = w.dtype
@@ -71,8 +67,10 @@ class BwnLinear(nn.Linear):
 
 
 def esm_gelu(x: torch.Tensor) -> torch.Tensor:
-    """erf GELU as in the original ESM code (HF ``esm.modeling_esm.gelu``)."""
-    return x * 0.5 * (1.0 + torch.erf(x / math.sqrt(2.0)))
+    """erf GELU as in the original ESM code (HF ``esm.modeling_esm.gelu``:
+    ``x * 0.5 * (1 + erf(x / sqrt(2)))``), as one fused elementwise op forward
+    and backward instead of five."""
+    return F.gelu(x, approximate="none")
 
 
 def _rotate_half(x):

@@ -98,6 +98,16 @@ def linear_residual(x: torch.Tensor, w, resid: torch.Tensor) -> torch.Tensor:
     return (x.float() @ _dense(w).float().t() + resid.float()).to(x.dtype)
 
 
+def linear_bias(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``x @ w.T + b`` with the bias added in the GEMM epilogue: the residual
+    epilogue reads a row stride of 0, so every output row adds the same bf16
+    bias vector (one rounding, no separate elementwise kernel)."""
+    if x.is_cuda:
+        bb = b.to(torch.bfloat16).contiguous()
+        return ops().linear_residual(x, w, bb.expand(x.shape[0], bb.shape[0]))
+    return (x.float() @ _dense(w).float().t() + b.float()).to(x.dtype)
+
+
 def linear_kn(x: torch.Tensor, w_kn: torch.Tensor) -> torch.Tensor:
     """``x @ w`` with ``w`` stored ``[K, N]`` (MN-major B operand); used for
     input gradients ``dX = dY @ W``."""

@@ -59,6 +59,20 @@ def test_mn_major_gemms(M, N, K):
     O.check_status("mn-major gemm")
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 320, 320), (24, 1280, 320), (2048, 1280, 320), (4096, 2560, 10240)])
+def test_linear_bias_epilogue(M, N, K):
+    """``x @ w.T + b`` with the bias read through a row stride of 0 by the
+    residual epilogue: token-swapped, split-K and full-tile paths."""
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(N, K, device=dev) / math.sqrt(K)).bfloat16()
+    b = torch.randn(N, device=dev)  # fp32 master bias, rounded to bf16 inside
+    y = O.linear_bias(x, w, b)
+    torch.cuda.synchronize()
+    O.check_status("linear_bias")
+    assert y.shape == (M, N) and y.dtype == torch.bfloat16
+    assert _rel(y, x.float() @ w.float().t() + b.bfloat16().float()) < 1e-2
+
+
 @pytest.mark.parametrize("T", [1, 16, 300])
 def test_linear_into_strided_views(T):
     """Grouped low-rank projection (DeepSeek's wo_a): each group's GEMM reads a
