@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256) ar_add_norm_kernel(const __nv_bfloat16* m
 // is, then DeepSeek V4's hyper-connection post-mix of the residual streams
 // (hc_post of csrc/kernels/deepseek.cu; the reference's all-reduce followed by
 // hc_post, contrib/deepseek-v4-flash/run_deepseek_v4_tp.py:541-556, 564-583).
-template <int HC>
+template <int HC, int kMaxVec>  // kMaxVec: 8-column vectors per thread, cols <= 2048 * kMaxVec
 __global__ void __launch_bounds__(256) ar_hc_post_kernel(ArHcArgs a) {
   pdl_trigger();
   pdl_wait();
@@ -184,7 +184,6 @@ __global__ void __launch_bounds__(256) ar_hc_post_kernel(ArHcArgs a) {
   // (the barrier also publishes s_post / s_comb)  a timed-out wait reads and writes nothing
   if (!__syncthreads_and(arrived)) return;
   const __nv_bfloat16* buf = a.mc_base + (long)((*a.sel) & 1) * a.buf_stride + (long)t * cols;
-  constexpr int kMaxVec = 4;  // 8 columns per vector, 256 threads: cols <= 8192
   float v[kMaxVec][8];
 #pragma unroll
   for (int n = 0; n < kMaxVec; ++n) {
@@ -198,32 +197,34 @@ __global__ void __launch_bounds__(256) ar_hc_post_kernel(ArHcArgs a) {
     float x[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16(v[n][e]));
-    float r[HC][8];
+    // acc[j] = post[j] * x + sum_i comb[i][j] * resid[i], one residual stream live at a time
+    float acc[HC][8];
+#pragma unroll
+    for (int j = 0; j < HC; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[j][e] = s_post[j] * x[e];
 #pragma unroll
     for (int i = 0; i < HC; ++i) {
       const uint4 rr = *reinterpret_cast<const uint4*>(a.resid + ((long)t * HC + i) * cols + c);
       const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+      float r[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __bfloat1622float2(r2[e]);
-        r[i][2 * e] = f.x;
-        r[i][2 * e + 1] = f.y;
+        r[2 * e] = f.x;
+        r[2 * e + 1] = f.y;
       }
+#pragma unroll
+      for (int j = 0; j < HC; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[j][e] += s_comb[i * HC + j] * r[e];
     }
 #pragma unroll
     for (int j = 0; j < HC; ++j) {
-      float o[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float acc = s_post[j] * x[e];
-#pragma unroll
-        for (int i = 0; i < HC; ++i) acc += s_comb[i * HC + j] * r[i][e];
-        o[e] = acc;
-      }
       uint4 w;
       __nv_bfloat162* w2 = reinterpret_cast<__nv_bfloat162*>(&w);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) w2[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+      for (int e = 0; e < 4; ++e) w2[e] = __floats2bfloat162_rn(acc[j][2 * e], acc[j][2 * e + 1]);
       *reinterpret_cast<uint4*>(a.out + ((long)t * HC + j) * cols + c) = w;
     }
   }
@@ -389,7 +390,13 @@ void ar_add_norm(const ArNormArgs& a, cudaStream_t st) {
 void ar_hc_post(const ArHcArgs& a, cudaStream_t st) {
   BWN_CHECK(a.hc == 4, "ar_hc_post: hc_mult 4 supported");
   BWN_CHECK(a.cols % 8 == 0 && a.cols <= 256 * 8 * 4, "ar_hc_post: dim must be a multiple of 8, at most 8192");
-  launch_k(ar_hc_post_kernel<4>, dim3(a.rows), dim3(256), 0, st, a);
+  // as few register vectors as the row needs (DeepSeek V4 Flash, dim 4096: two)
+  if (a.cols <= 2048)
+    launch_k(ar_hc_post_kernel<4, 1>, dim3(a.rows), dim3(256), 0, st, a);
+  else if (a.cols <= 4096)
+    launch_k(ar_hc_post_kernel<4, 2>, dim3(a.rows), dim3(256), 0, st, a);
+  else
+    launch_k(ar_hc_post_kernel<4, 4>, dim3(a.rows), dim3(256), 0, st, a);
 }
 
 void greedy_allmax(const GreedyArgs& a, cudaStream_t st) {
