@@ -149,6 +149,8 @@ def main(argv=None) -> None:
     ap.add_argument("--checkpoint", "--model-path", default="", help="HF safetensors directory (config.json beside it)")
     ap.add_argument("--layers", "--num-layers", type=int, default=0, help="truncate to this many layers")
     ap.add_argument("--prompt-ids", default="", help="comma-separated prompt token ids (every row)")
+    ap.add_argument("--prompt", default="", help="prompt text, through the tokenizer (every row)")
+    ap.add_argument("--tokenizer", default="", help="HF tokenizer directory (default: the checkpoint's, if any)")
     ap.add_argument("--prompt-len", type=int, default=16, help="uniform-random prompt length without --prompt-ids")
     ap.add_argument("--batch", "--batch-size", type=int, default=1)
     ap.add_argument("--max-new", "--num-tokens", type=int, default=16)
@@ -232,7 +234,15 @@ def main(argv=None) -> None:
         finish()
         return
 
-    if a.prompt_ids:
+    codec = None
+    if a.prompt or a.tokenizer:
+        from ..serve.api import load_tokenizer
+        codec = load_tokenizer(a.tokenizer or a.checkpoint)
+        if codec is None:
+            raise SystemExit("no tokenizer found: give --tokenizer DIR, or a --checkpoint directory with tokenizer files")
+    if a.prompt:
+        prompt = torch.tensor([codec.encode(a.prompt)] * a.batch, dtype=torch.long)
+    elif a.prompt_ids:
         ids = [int(t) for t in a.prompt_ids.split(",") if t.strip()]
         prompt = torch.tensor([ids] * a.batch, dtype=torch.long)
     else:
@@ -301,6 +311,7 @@ def main(argv=None) -> None:
         print(json.dumps({
             "model": cfg.name, "tp": comm.size, "batch": a.batch, "prompt_len": S,
             "generated_row0": gen[0].tolist(), "gen_hash_row0": F.gen_hash(gen[0]),
+            **({"text_row0": codec.decode(gen[0].tolist())} if codec is not None else {}),
             "prefill_fingerprint": F.logits_fingerprint(logits.float().cpu()) if logits is not None else None,
             "ttft_ms": round(ttft, 2), "tpot_ms": round(tpot, 3),
             "occupied_ssm_layers": len(occupancy["ssm"]), "graph": dec.graph is not None,

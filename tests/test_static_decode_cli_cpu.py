@@ -78,3 +78,19 @@ def test_reference_flag_names_and_bench_modes():
                       "--prefill-bench-sweep", "16,48", "--bucket-chunk", "16"])
     assert [ln["prefill_tokens"] for ln in lines] == [32, 16, 48]
     assert all(ln["prefill_tok_s"] > 0 and ln["bucket"] == 16 for ln in lines)
+
+
+def test_text_prompt_through_tokenizer(tmp_path):
+    """--prompt text goes through the tokenizer: the same tokens as the ids it
+    encodes to, and the generated ids decoded as text_row0."""
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+    tk = Tokenizer(models.WordLevel({f"w{i}": i for i in range(512)}, unk_token="w0"))
+    tk.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    tk.decoder = decoders.WordPiece(prefix="##")
+    PreTrainedTokenizerFast(tokenizer_object=tk, unk_token="w0").save_pretrained(str(tmp_path))
+    common = ["-m", "bwn.runtime.static_decode", "--tiny", "--cpu", "--max-new", "4"]
+    by_text = _run(common + ["--tokenizer", str(tmp_path), "--prompt", "w5 w9 w13"])
+    by_ids = _run(common + ["--prompt-ids", "5,9,13"])
+    assert by_text["prompt_len"] == 3 and by_text["gen_hash_row0"] == by_ids["gen_hash_row0"]
+    assert by_text["text_row0"] == " ".join(f"w{i}" for i in by_text["generated_row0"])
