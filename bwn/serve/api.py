@@ -141,6 +141,12 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
     def run(prompt: list[int], body, stream: bool):
         if not prompt:
             raise HTTPException(400, "prompt must hold at least one token id")
+        eng = getattr(worker, "engine", None)
+        eng = getattr(eng, "e", eng)  # a lockstep handle wraps the engine
+        max_seq = getattr(eng, "max_seq", None)
+        if max_seq is not None and len(prompt) + body.max_tokens > max_seq:  # refused before any stream starts
+            raise HTTPException(400, f"prompt ({len(prompt)}) + {body.max_tokens} new tokens exceed "
+                                     f"max_seq {max_seq}")
         q: queue.Queue = queue.Queue()
         req = Request(prompt, body.max_tokens, stop_ids(body), body.temperature,
                       on_token=q.put if stream else None)

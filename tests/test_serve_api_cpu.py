@@ -99,6 +99,9 @@ def test_streaming_continuous(model, tmp_path):
         assert [c["choices"][0]["tokens"] for c in chunks[:-1]] == [[t] for t in want]
         assert "".join(c["choices"][0]["text"] for c in chunks) == " ".join(f"w{t}" for t in want)
         assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+        # a request that cannot fit is refused with a 400 before any event is sent
+        r = client.post("/v1/completions", json={"prompt": [1] * 60, "max_tokens": 10, "stream": True})
+        assert r.status_code == 400 and "max_seq" in r.json()["detail"]
     finally:
         worker.stop()
 
