@@ -6,7 +6,8 @@ its users call (``contrib/qwen3.6-27b/deploy/serve_qwen35.sh``,
 This module gives the same endpoints over the bwn engines:
 
 * ``POST /v1/completions``: ``prompt`` as token ids or text; ``max_tokens``,
-  ``temperature``, ``stop`` (token ids, or strings that are one token each),
+  ``temperature``, ``stop`` (token ids, or strings: generation stops once the
+  output ends with the string's tokens),
   ``stop_token_ids``, ``ignore_eos``, ``stream`` (server-sent events, one
   chunk per token as the continuous engine produces it, then ``[DONE]``);
 * ``POST /v1/chat/completions``: ``messages`` rendered by the tokenizer's chat
@@ -79,11 +80,11 @@ class TextCodec:
             out = out["input_ids"]
         return [int(i) for i in out]
 
-    def stop_id(self, s: str) -> int:
+    def stop_tokens(self, s: str) -> list[int]:
         ids = self.encode(s)
-        if len(ids) != 1:
-            raise ValueError(f"stop string {s!r} is {len(ids)} tokens; only single-token stop strings are supported")
-        return ids[0]
+        if not ids:
+            raise ValueError(f"stop string {s!r} encodes to no tokens")
+        return ids
 
 
 def load_tokenizer(path: str) -> TextCodec | None:
@@ -121,8 +122,10 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
 
     app = FastAPI(title="bwn")
 
-    def stop_ids(body) -> list[int]:
-        out = list(body.stop_token_ids)
+    def stop_ids(body) -> tuple[list[int], list[list[int]]]:
+        """(stop ids, stop sequences): a stop string of one token is a stop
+        id; a longer one stops when the output ends with its encoding."""
+        out, seqs = list(body.stop_token_ids), []
         stops = [body.stop] if isinstance(body.stop, (str, int)) else (body.stop or [])
         for s in stops:
             if isinstance(s, int):
@@ -131,12 +134,13 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
                 raise HTTPException(400, "stop strings need a tokenizer (--tokenizer)")
             else:
                 try:
-                    out.append(codec.stop_id(s))
+                    ids = codec.stop_tokens(s)
                 except ValueError as e:
                     raise HTTPException(400, str(e)) from e
+                (out.append(ids[0]) if len(ids) == 1 else seqs.append(ids))
         if codec is not None and not body.ignore_eos:
             out += [e for e in codec.eos if e not in out]
-        return out
+        return out, seqs
 
     def run(prompt: list[int], body, stream: bool):
         if not prompt:
@@ -148,8 +152,9 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
             raise HTTPException(400, f"prompt ({len(prompt)}) + {body.max_tokens} new tokens exceed "
                                      f"max_seq {max_seq}")
         q: queue.Queue = queue.Queue()
-        req = Request(prompt, body.max_tokens, stop_ids(body), body.temperature,
-                      on_token=q.put if stream else None)
+        stop, seqs = stop_ids(body)
+        req = Request(prompt, body.max_tokens, stop, body.temperature, on_token=q.put if stream else None,
+                      stop_seqs=seqs)
         fut = worker.submit(req)
         if stream:
             return fut, q

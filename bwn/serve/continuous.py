@@ -155,10 +155,10 @@ class ContinuousEngine:
 
     def _maybe_finish(self, r: int, step_ms: float):
         s = self.slots[r]
-        if len(s.tokens) < s.req.max_tokens and s.tokens[-1] not in s.req.stop:
+        if len(s.tokens) < s.req.max_tokens and not s.req.stopped(s.tokens):
             return None
         toks = s.tokens[:s.req.max_tokens]
-        stop = bool(toks) and toks[-1] in s.req.stop
+        stop = s.req.stopped(toks)
         decode_ms = (time.perf_counter() - s.t_admit) * 1e3
         self.slots[r] = None
         self.stats["finished"] += 1

@@ -28,6 +28,16 @@ class Request:
     # called with each new token id as the continuous engine produces it (streaming);
     # engines that finish a request at once leave it to the caller
     on_token: Callable[[int], None] | None = field(default=None, compare=False, repr=False)
+    # multi-token stop sequences: generation stops once the output ends with one of them
+    stop_seqs: list[list[int]] = field(default_factory=list)
+
+    def stopped(self, tokens: list[int]) -> bool:
+        """Whether ``tokens`` (generated so far) end with a stop id or a stop sequence."""
+        if not tokens:
+            return False
+        if tokens[-1] in self.stop:
+            return True
+        return any(q and len(tokens) >= len(q) and tokens[-len(q):] == q for q in self.stop_seqs)
 
 
 @dataclass
@@ -82,18 +92,18 @@ class GenerationEngine:
         self._sync()
         t1 = time.perf_counter()
         gen = [[int(first[i])] for i in range(len(reqs))]
-        done = [r.max_tokens <= 1 or gen[i][-1] in r.stop for i, r in enumerate(reqs)]
+        done = [r.max_tokens <= 1 or r.stopped(gen[i]) for i, r in enumerate(reqs)]
         while not all(done):
             nxt = self.dec.step()
             for i, r in enumerate(reqs):
                 if done[i]:
                     continue
                 gen[i].append(int(nxt[i]))
-                done[i] = len(gen[i]) >= r.max_tokens or gen[i][-1] in r.stop
+                done[i] = len(gen[i]) >= r.max_tokens or r.stopped(gen[i])
         t2 = time.perf_counter()
         res = []
         for i, r in enumerate(reqs):
             toks = gen[i][:r.max_tokens]
-            stop = bool(toks) and toks[-1] in r.stop
+            stop = r.stopped(toks)
             res.append(Result(toks, "stop" if stop else "length", (t1 - t0) * 1e3, (t2 - t1) * 1e3))
         return res

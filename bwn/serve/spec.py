@@ -62,7 +62,7 @@ class SpecEngine:
         first = dec.prefill(torch.tensor([r.prompt for r in reqs], dtype=torch.long)).cpu().tolist()
         t1 = time.perf_counter()
         gen = [[int(x)] for x in first]
-        done = [len(g) >= r.max_tokens or g[-1] in r.stop for g, r in zip(gen, reqs)]
+        done = [len(g) >= r.max_tokens or r.stopped(g) for g, r in zip(gen, reqs)]
         steps = 0
         while not all(done):
             ids, cnt = dec.step()
@@ -72,7 +72,7 @@ class SpecEngine:
                     continue
                 for x in ids[b, :int(cnt[b])].tolist():
                     gen[b].append(int(x))
-                    if len(gen[b]) >= r.max_tokens or gen[b][-1] in r.stop:
+                    if len(gen[b]) >= r.max_tokens or r.stopped(gen[b]):
                         done[b] = True
                         break
         t2 = time.perf_counter()
@@ -82,6 +82,6 @@ class SpecEngine:
         res = []
         for g, r in zip(gen, reqs):
             toks = g[:r.max_tokens]
-            stop = bool(toks) and toks[-1] in r.stop
+            stop = r.stopped(toks)
             res.append(Result(toks, "stop" if stop else "length", (t1 - t0) * 1e3, (t2 - t1) * 1e3))
         return res

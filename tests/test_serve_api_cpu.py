@@ -79,11 +79,16 @@ def test_text_prompt_stop_strings_and_eos(model, tmp_path):
         assert r["usage"] == {"prompt_tokens": 3, "completion_tokens": k, "total_tokens": 3 + k}
         r = client.post("/v1/completions", json={"prompt": _text(prompt), "max_tokens": 6, "ignore_eos": True}).json()
         assert r["choices"][0]["tokens"] == want and r["choices"][0]["finish_reason"] == "length"
-        # a single-token stop string; a multi-token one is refused
+        # a single-token stop string, and a two-token one (stops where the output first ends with it)
         r = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 6, "ignore_eos": True,
                                                  "stop": [f"w{want[1]}"]}).json()
         assert r["choices"][0]["tokens"] == want[:want.index(want[1]) + 1]
-        assert client.post("/v1/completions", json={"prompt": prompt, "stop": "w1 w2"}).status_code == 400
+        seq = want[2:4]
+        end = next(i + 2 for i in range(len(want) - 1) if want[i:i + 2] == seq)
+        r = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 6, "ignore_eos": True,
+                                                 "stop": _text(seq)}).json()
+        assert r["choices"][0]["tokens"] == want[:end] and r["choices"][0]["finish_reason"] == "stop"
+        assert client.post("/v1/completions", json={"prompt": prompt, "stop": " "}).status_code == 400
     finally:
         worker.stop()
 
@@ -158,3 +163,16 @@ def test_metrics_latency_summaries(model):
         assert "bwn_running_requests 0" in text and "bwn_waiting_requests 0" in text
     finally:
         worker.stop()
+
+
+def test_stop_sequences_in_static_engine(model):
+    from bwn.serve.engine import Request
+    r = Request([1], 8, stop=[3], stop_seqs=[[4, 5]])
+    assert not r.stopped([]) and r.stopped([9, 3]) and r.stopped([1, 4, 5]) and not r.stopped([4, 5, 6])
+    want = _greedy(model, [5, 9, 13], 6)
+    seq = want[3:5]
+    end = next(i + 2 for i in range(len(want) - 1) if want[i:i + 2] == seq)
+    eng = GenerationEngine(model, 2, 128, use_graph=False, pad_to=16)
+    res = eng.generate([Request([5, 9, 13], 6, stop_seqs=[seq]), Request([5, 9, 13], 6)])
+    assert res[0].tokens == want[:end] and res[0].finish_reason == "stop"
+    assert res[1].tokens == want and res[1].finish_reason == "length"
