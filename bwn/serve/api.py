@@ -5,7 +5,8 @@ its users call (``contrib/qwen3.6-27b/deploy/serve_qwen35.sh``,
 ``serve_eagle3.sh``; ``contrib/qwen3.6-35b-a3b/VLLM_NEURON_ASSESSMENT.md``).
 This module gives the same endpoints over the bwn engines:
 
-* ``POST /v1/completions``: ``prompt`` as token ids or text; ``max_tokens``,
+* ``POST /v1/completions``: ``prompt`` as token ids or text, or a list of
+  them (one choice each); ``max_tokens``,
   ``temperature``, ``stop`` (token ids, or strings: generation stops once the
   output ends with the string's tokens),
   ``stop_token_ids``, ``ignore_eos``, ``stream`` (server-sent events, one
@@ -34,7 +35,7 @@ _ids = itertools.count()
 
 
 class CompletionIn(BaseModel):
-    prompt: list[int] | str
+    prompt: list[int] | str | list[str] | list[list[int]]
     max_tokens: int = 16
     stop: list[int] | list[str] | str | None = None
     stop_token_ids: list[int] = []
@@ -142,7 +143,8 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
             out += [e for e in codec.eos if e not in out]
         return out, seqs
 
-    def run(prompt: list[int], body, stream: bool):
+    def submit(prompt: list[int], body, stream: bool):
+        """Validate and queue one request; returns (future, token queue)."""
         if not prompt:
             raise HTTPException(400, "prompt must hold at least one token id")
         eng = getattr(worker, "engine", None)
@@ -155,13 +157,24 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
         stop, seqs = stop_ids(body)
         req = Request(prompt, body.max_tokens, stop, body.temperature, on_token=q.put if stream else None,
                       stop_seqs=seqs)
-        fut = worker.submit(req)
-        if stream:
-            return fut, q
+        return worker.submit(req), q
+
+    def wait(fut):
         try:
-            return fut.result(timeout=600), None
+            return fut.result(timeout=600)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
+
+    def run(prompt: list[int], body, stream: bool):
+        fut, q = submit(prompt, body, stream)
+        return (fut, q) if stream else (wait(fut), None)
+
+    def to_ids(p) -> list[int]:
+        if isinstance(p, str):
+            if codec is None:
+                raise HTTPException(400, "text prompts need a tokenizer (--tokenizer); send token ids")
+            return codec.encode(p)
+        return p
 
     def events(fut, q, chunk):
         """SSE body: one chunk per token while the engine produces them, the
@@ -202,25 +215,29 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
 
     @app.post("/v1/completions")
     def completions(body: CompletionIn):
-        if isinstance(body.prompt, str):
-            if codec is None:
-                raise HTTPException(400, "text prompts need a tokenizer (--tokenizer); send token ids")
-            prompt = codec.encode(body.prompt)
-        else:
-            prompt = body.prompt
+        """One prompt (ids or text), or a list of prompts: one choice each,
+        queued together so the engine batches them."""
+        many = isinstance(body.prompt, list) and bool(body.prompt) and not isinstance(body.prompt[0], int)
+        prompts = [to_ids(p) for p in body.prompt] if many else [to_ids(body.prompt)]
         cid, created = f"cmpl-{next(_ids)}", int(time.time())
-        out, q = run(prompt, body, body.stream)
         if body.stream:
+            if many:
+                raise HTTPException(400, "streaming takes a single prompt")
+            fut, q = run(prompts[0], body, True)
+
             def chunk(toks, text, fin):
                 return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
                         "choices": [{"index": 0, "text": text, "tokens": toks, "finish_reason": fin}]}
-            return StreamingResponse(events(out, q, chunk), media_type="text/event-stream")
+            return StreamingResponse(events(fut, q, chunk), media_type="text/event-stream")
+        futs = [submit(p, body, False)[0] for p in prompts]
+        outs = [wait(f) for f in futs]
+        n_in, n_out = sum(map(len, prompts)), sum(len(o.tokens) for o in outs)
         return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "text": codec.decode(out.tokens) if codec else None,
-                             "tokens": out.tokens, "finish_reason": out.finish_reason}],
-                "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out.tokens),
-                          "total_tokens": len(prompt) + len(out.tokens)},
-                "timing_ms": {"prefill": round(out.prefill_ms, 3), "decode": round(out.decode_ms, 3)}}
+                "choices": [{"index": i, "text": codec.decode(o.tokens) if codec else None,
+                             "tokens": o.tokens, "finish_reason": o.finish_reason} for i, o in enumerate(outs)],
+                "usage": {"prompt_tokens": n_in, "completion_tokens": n_out, "total_tokens": n_in + n_out},
+                "timing_ms": {"prefill": round(max(o.prefill_ms for o in outs), 3),
+                              "decode": round(max(o.decode_ms for o in outs), 3)}}
 
     @app.post("/v1/chat/completions")
     def chat(body: ChatIn):

@@ -176,3 +176,19 @@ def test_stop_sequences_in_static_engine(model):
     res = eng.generate([Request([5, 9, 13], 6, stop_seqs=[seq]), Request([5, 9, 13], 6)])
     assert res[0].tokens == want[:end] and res[0].finish_reason == "stop"
     assert res[1].tokens == want and res[1].finish_reason == "length"
+
+
+def test_prompt_lists_give_one_choice_each(model, tmp_path):
+    client, worker = _continuous_client(model, _tokenizer(tmp_path / "tok"))
+    try:
+        ps = [[5, 9, 13], [7, 2]]
+        r = client.post("/v1/completions", json={"prompt": ps, "max_tokens": 3, "ignore_eos": True}).json()
+        assert [c["index"] for c in r["choices"]] == [0, 1]
+        assert [c["tokens"] for c in r["choices"]] == [_greedy(model, p, 3) for p in ps]
+        assert r["usage"]["prompt_tokens"] == 5 and r["usage"]["completion_tokens"] == 6
+        r = client.post("/v1/completions", json={"prompt": ["w5 w9 w13", "w7 w2"], "max_tokens": 3,
+                                                 "ignore_eos": True}).json()
+        assert [c["tokens"] for c in r["choices"]] == [_greedy(model, p, 3) for p in ps]
+        assert client.post("/v1/completions", json={"prompt": ps, "stream": True}).status_code == 400
+    finally:
+        worker.stop()
