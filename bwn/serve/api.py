@@ -6,7 +6,7 @@ its users call (``contrib/qwen3.6-27b/deploy/serve_qwen35.sh``,
 This module gives the same endpoints over the bwn engines:
 
 * ``POST /v1/completions``: ``prompt`` as token ids or text, or a list of
-  them (one choice each); ``max_tokens``,
+  them (``n`` choices each); ``max_tokens``,
   ``temperature``, ``stop`` (token ids, or strings: generation stops once the
   output ends with the string's tokens),
   ``stop_token_ids``, ``ignore_eos``, ``stream`` (server-sent events, one
@@ -37,6 +37,7 @@ _ids = itertools.count()
 class CompletionIn(BaseModel):
     prompt: list[int] | str | list[str] | list[list[int]]
     max_tokens: int = 16
+    n: int = 1  # completions per prompt (distinct only when sampled)
     stop: list[int] | list[str] | str | None = None
     stop_token_ids: list[int] = []
     temperature: float = 0.0
@@ -219,16 +220,19 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
         queued together so the engine batches them."""
         many = isinstance(body.prompt, list) and bool(body.prompt) and not isinstance(body.prompt[0], int)
         prompts = [to_ids(p) for p in body.prompt] if many else [to_ids(body.prompt)]
+        if body.n < 1:
+            raise HTTPException(400, "n must be at least 1")
         cid, created = f"cmpl-{next(_ids)}", int(time.time())
         if body.stream:
-            if many:
-                raise HTTPException(400, "streaming takes a single prompt")
+            if many or body.n > 1:
+                raise HTTPException(400, "streaming takes a single prompt and n = 1")
             fut, q = run(prompts[0], body, True)
 
             def chunk(toks, text, fin):
                 return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
                         "choices": [{"index": 0, "text": text, "tokens": toks, "finish_reason": fin}]}
             return StreamingResponse(events(fut, q, chunk), media_type="text/event-stream")
+        prompts = [p for p in prompts for _ in range(body.n)]  # choice i*n + j: prompt i, sample j
         futs = [submit(p, body, False)[0] for p in prompts]
         outs = [wait(f) for f in futs]
         n_in, n_out = sum(map(len, prompts)), sum(len(o.tokens) for o in outs)

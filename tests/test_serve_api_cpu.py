@@ -190,5 +190,7 @@ def test_prompt_lists_give_one_choice_each(model, tmp_path):
                                                  "ignore_eos": True}).json()
         assert [c["tokens"] for c in r["choices"]] == [_greedy(model, p, 3) for p in ps]
         assert client.post("/v1/completions", json={"prompt": ps, "stream": True}).status_code == 400
+        r = client.post("/v1/completions", json={"prompt": ps, "max_tokens": 2, "n": 2, "ignore_eos": True}).json()
+        assert [c["tokens"] for c in r["choices"]] == [_greedy(model, p, 2) for p in ps for _ in range(2)]
     finally:
         worker.stop()
