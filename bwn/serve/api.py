@@ -54,6 +54,8 @@ class ChatMessage(BaseModel):
 class ChatIn(BaseModel):
     messages: list[ChatMessage]
     max_tokens: int = 16
+    max_completion_tokens: int | None = None  # the newer name of max_tokens; wins when given
+    n: int = 1
     stop: list[int] | list[str] | str | None = None
     stop_token_ids: list[int] = []
     temperature: float = 0.0
@@ -251,9 +253,13 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
             prompt = codec.chat([m.model_dump() for m in body.messages])
         except Exception as e:  # noqa: BLE001 - a template that cannot render these messages
             raise HTTPException(400, f"chat template: {e}") from e
+        if body.max_completion_tokens is not None:
+            body = body.model_copy(update={"max_tokens": body.max_completion_tokens})
+        if body.n < 1 or (body.stream and body.n > 1):
+            raise HTTPException(400, "n must be at least 1, and 1 when streaming")
         cid, created = f"chatcmpl-{next(_ids)}", int(time.time())
-        out, q = run(prompt, body, body.stream)
         if body.stream:
+            out, q = run(prompt, body, True)
             first = [True]
 
             def chunk(toks, text, fin):
@@ -263,11 +269,13 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
                 return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                         "choices": [{"index": 0, "delta": delta, "tokens": toks, "finish_reason": fin}]}
             return StreamingResponse(events(out, q, chunk), media_type="text/event-stream")
+        outs = [wait(f) for f in [submit(prompt, body, False)[0] for _ in range(body.n)]]
+        n_out = sum(len(o.tokens) for o in outs)
         return {"id": cid, "object": "chat.completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "message": {"role": "assistant", "content": codec.decode(out.tokens)},
-                             "tokens": out.tokens, "finish_reason": out.finish_reason}],
-                "usage": {"prompt_tokens": len(prompt), "completion_tokens": len(out.tokens),
-                          "total_tokens": len(prompt) + len(out.tokens)}}
+                "choices": [{"index": i, "message": {"role": "assistant", "content": codec.decode(o.tokens)},
+                             "tokens": o.tokens, "finish_reason": o.finish_reason} for i, o in enumerate(outs)],
+                "usage": {"prompt_tokens": len(prompt), "completion_tokens": n_out,
+                          "total_tokens": len(prompt) + n_out}}
 
     @app.get("/metrics", response_class=PlainTextResponse)
     def metrics():

@@ -147,6 +147,9 @@ def test_chat_completions(model, tmp_path):
         assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
         assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == _text(want)
         assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+        r = client.post("/v1/chat/completions", json={"messages": msgs, "max_completion_tokens": 2, "n": 2}).json()
+        assert [c["message"]["content"] for c in r["choices"]] == [_text(want[:2])] * 2
+        assert r["usage"]["completion_tokens"] == 4
     finally:
         worker.stop()
 
