@@ -43,6 +43,7 @@ class CompletionIn(BaseModel):
     temperature: float = 0.0
     ignore_eos: bool = False
     stream: bool = False
+    stream_options: dict | None = None  # {"include_usage": true}: a last chunk with usage
     model: str | None = None
 
 
@@ -61,6 +62,7 @@ class ChatIn(BaseModel):
     temperature: float = 0.0
     ignore_eos: bool = False
     stream: bool = False
+    stream_options: dict | None = None  # {"include_usage": true}: a last chunk with usage
     model: str | None = None
 
 
@@ -118,6 +120,14 @@ class _Incremental:
             return ""
         delta, self.sent = text[len(self.sent):], text
         return delta
+
+
+def _usage(body, n_prompt: int):
+    """The usage reporter of a streamed request that asked for it, else None."""
+    if not (body.stream_options or {}).get("include_usage"):
+        return None
+    return lambda res: {"prompt_tokens": n_prompt, "completion_tokens": len(res.tokens),
+                        "total_tokens": n_prompt + len(res.tokens)}
 
 
 def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
@@ -179,7 +189,7 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
             return codec.encode(p)
         return p
 
-    def events(fut, q, chunk):
+    def events(fut, q, chunk, usage_of=None):
         """SSE body: one chunk per token while the engine produces them, the
         rest (engines that finish a request at once) after it completes, then
         a final chunk with the finish reason and ``[DONE]``."""
@@ -206,6 +216,10 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
         for tok in rest:
             yield "data: " + json.dumps(chunk([tok], inc.push(tok), None)) + "\n\n"
         yield "data: " + json.dumps(chunk([], "" if codec else None, res.finish_reason)) + "\n\n"
+        if usage_of is not None:  # stream_options.include_usage: usage in a chunk without choices
+            last = chunk([], None, None)
+            last["choices"], last["usage"] = [], usage_of(res)
+            yield "data: " + json.dumps(last) + "\n\n"
         yield "data: [DONE]\n\n"
 
     @app.get("/health")
@@ -233,7 +247,8 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
             def chunk(toks, text, fin):
                 return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
                         "choices": [{"index": 0, "text": text, "tokens": toks, "finish_reason": fin}]}
-            return StreamingResponse(events(fut, q, chunk), media_type="text/event-stream")
+            return StreamingResponse(events(fut, q, chunk, _usage(body, len(prompts[0]))),
+                                     media_type="text/event-stream")
         prompts = [p for p in prompts for _ in range(body.n)]  # choice i*n + j: prompt i, sample j
         futs = [submit(p, body, False)[0] for p in prompts]
         outs = [wait(f) for f in futs]
@@ -268,7 +283,7 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
                     delta["role"], first[0] = "assistant", False
                 return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model_name,
                         "choices": [{"index": 0, "delta": delta, "tokens": toks, "finish_reason": fin}]}
-            return StreamingResponse(events(out, q, chunk), media_type="text/event-stream")
+            return StreamingResponse(events(out, q, chunk, _usage(body, len(prompt))), media_type="text/event-stream")
         outs = [wait(f) for f in [submit(prompt, body, False)[0] for _ in range(body.n)]]
         n_out = sum(len(o.tokens) for o in outs)
         return {"id": cid, "object": "chat.completion", "created": created, "model": model_name,

@@ -104,6 +104,10 @@ def test_streaming_continuous(model, tmp_path):
         assert [c["choices"][0]["tokens"] for c in chunks[:-1]] == [[t] for t in want]
         assert "".join(c["choices"][0]["text"] for c in chunks) == " ".join(f"w{t}" for t in want)
         assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+        chunks = _sse(client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 5, "stream": True,
+                                                           "stream_options": {"include_usage": True}}))
+        assert chunks[-1]["choices"] == [] and chunks[-1]["usage"] == {
+            "prompt_tokens": 5, "completion_tokens": 5, "total_tokens": 10}
         # a request that cannot fit is refused with a 400 before any event is sent
         r = client.post("/v1/completions", json={"prompt": [1] * 60, "max_tokens": 10, "stream": True})
         assert r.status_code == 400 and "max_seq" in r.json()["detail"]
