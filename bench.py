@@ -1,18 +1,22 @@
 #!/usr/bin/env python
-"""Flagship benchmark: Qwen3.6-27B decode on 1-8 B200 (tensor parallel).
+"""Flagship benchmark: Qwen3.6 decode on 1-8 B200 (tensor + expert parallel).
 
     python bench.py --gpus N --steps K --warmup W            (N=1)
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Config: Qwen3.6-27B dense hybrid (64 layers, hidden 5120,
-[DeltaNet x3, GQA x1] x16), bf16, random-init weights from seed 0, TP=N,
+Headline config: Qwen3.6-35B-A3B (40 layers, hidden 2048,
+[DeltaNet x3, GQA x1] x10, 256-expert top-8 MoE on every layer), bf16,
+random-init weights from seed 0, TP=N for attention and EP=N for the experts,
 synthetic uniform-random prompt ids, prefill 2048 then greedy decode at global
-batch 32.  The timed step is one full decode step (all 64 layers, LM head and
-sharded greedy) replayed from a CUDA graph; W untimed warm-up steps, then K
-steps bracketed by barrier + synchronize, CUDA events, max over ranks.  Every
-step streams all weights (54 GB / N per GPU), far more than the 126 MB L2.
+batch 32.  ``--model 27b`` runs Qwen3.6-27B instead.  The timed step is one
+full decode step (all layers, LM head and sharded greedy) replayed from a CUDA
+graph; W untimed warm-up steps, then K steps bracketed by barrier +
+synchronize, timed with two CUDA events around the whole loop, max over ranks.
+Every step streams the layers' weights and the touched experts (GBs per GPU),
+far more than the 126 MB L2.
 
-``--impl reference`` runs the reference's own code path; see the JSON it prints.
+``--impl reference`` runs the reference's own 35B-A3B harness on the same
+config (``bench/reference_arm.py``).
 """
 from __future__ import annotations
 
@@ -25,17 +29,22 @@ import time
 
 import torch
 
-BASELINE_TOK_S = 63.1  # reference Qwen3.6-27B decode, BS=16, trn2.3xl TP=4 (contrib/qwen3.6-27b/README.md:96)
-BASELINE_BS1_TOK_S = 28.2  # reference Qwen3.6-27B decode, BS=1, same box (contrib/qwen3.6-27b/README.md:94)
+# the reference's published decode numbers closest to each config (trn2.3xlarge)
+BASELINE_TOK_S = {
+    "35b": 303.9,  # 35B-A3B decode BS=32, TP=8 LNC=1, full graph (contrib/qwen3.6-35b-a3b/BENCHMARK.md:568)
+    "27b": 63.1,   # 27B decode BS=16, TP=4 (contrib/qwen3.6-27b/README.md:96)
+}
+BASELINE_BS1_TOK_S = {
+    "35b": 48.9,   # 35B-A3B decode BS=1, TP=4 LNC=2 (contrib/qwen3.6-35b-a3b/BENCHMARK.md:515)
+    "27b": 28.2,   # 27B decode BS=1, TP=4 (contrib/qwen3.6-27b/README.md:94)
+}
 METRIC = "decode tok/s/box + p50 TPOT & prefill TTFT, Qwen3.6 TP/EP at 1/2/4/8 B200"
 
 
 def reference_arm(args) -> None:
-    why = ("reference is not pip-installable (no setup.py/pyproject.toml: pip reports 'Directory is not "
-           "installable') and every harness imports torch_neuronx / runs on the 'neuron' device (AWS Trainium), "
-           "which has no CUDA path")
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": why, "metric": METRIC, "n_gpus": args.gpus}))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "bench"))
+    import reference_arm as RA
+    RA.run(args, METRIC, BASELINE_TOK_S.get(args.model))
 
 
 def count_launches(fn) -> int:
@@ -66,13 +75,58 @@ def count_launches(fn) -> int:
     return n[0]
 
 
+def multi_gpu_check(model, dec, comm, dev) -> dict:
+    """One decode step from a copy of the live state through the product path
+    (fused NVLink reductions, NVLink expert all-to-all where enabled) and one
+    through plain NCCL (all-reduce everywhere, the reference's formulation);
+    the final hidden states must agree to bf16 accuracy and the greedy ids
+    must agree wherever the top-2 logit gap exceeds bf16 noise.  Every rank
+    takes the same collective steps."""
+    from bwn.models.qwen36 import Qwen36State
+    st = dec.st
+
+    def clone(s):
+        return Qwen36State(conv=s.conv.clone(), ssm=s.ssm.clone(), k_cache=s.k_cache.clone(),
+                           v_cache=s.v_cache.clone(), positions=s.positions.clone())
+    toks = dec.tokens.clone()
+    s1 = clone(st)
+    h1 = model.decode_hidden(toks, s1)
+    l1 = model.logits(h1)
+    del s1
+    saved = (model.fused_comm, getattr(model, "ep_a2a", None))
+    model.fused_comm = None
+    model.ep_a2a = None
+    try:
+        s2 = clone(st)
+        h2 = model.decode_hidden(toks, s2)
+        l2 = model.logits(h2)
+        del s2
+    finally:
+        model.fused_comm, model.ep_a2a = saved
+    torch.cuda.synchronize()
+    rel = float((h1.float() - h2.float()).norm() / h2.float().norm().clamp_min(1e-12))
+    rel = comm.max_scalar(rel, dev)
+    top = l2.float().topk(2, dim=-1).values
+    gap = top[:, 0] - top[:, 1]
+    diff = l1.argmax(-1) != l2.argmax(-1)
+    noise = 0.05  # logits differ by up to ~0.02 between summation orders of bf16 partials
+    bad = int((diff & (gap > noise)).sum())
+    bad = int(comm.max_scalar(float(bad), dev))
+    out = {"paths": "fused NVLink (+EP all-to-all) vs NCCL all-reduce", "hidden_rel_err": round(rel, 6),
+           "ids_differ": int(diff.sum()), "ids_differ_beyond_noise": bad, "rows": int(diff.numel()),
+           "ok": rel <= 2e-2 and bad == 0}
+    if not out["ok"]:
+        raise RuntimeError(f"multi-GPU check failed: {out}")
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="bwn", choices=["bwn", "reference"])
-    ap.add_argument("--model", default="27b", choices=["27b", "35b"])
+    ap.add_argument("--model", default="35b", choices=["27b", "35b"])
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (result marked invalid)")
@@ -103,7 +157,7 @@ def main() -> None:
     from bwn.parallel.comm import init_distributed
     from bwn.runtime.static_decode import StaticDecoder
     from bwn.utils import fingerprint as F
-    from bwn.utils.clocks import ClockSampler
+    from bwn.utils.clocks import ClockSampler, job_gpu_ids
     from bwn.utils.env import validate
     from bwn.utils.metrics import MetricsLog
 
@@ -117,7 +171,8 @@ def main() -> None:
     base = QWEN36_27B if args.model == "27b" else QWEN36_35B_A3B
     cfg = base if not args.layers else base.scaled(num_layers=args.layers)
     B, S = args.batch, args.prompt_len
-    max_seq = S + args.warmup + args.steps * 2 + 64
+    # warm-up + timed + p50 (<= 32) + end-to-end steps, plus margin
+    max_seq = S + args.warmup + args.steps * 2 + 32 + 64
 
     model = Qwen36Model(cfg, comm, dev, moe_sharding=args.moe_sharding).init_random(seed=0)
     if args.fp8 or args.fp8_experts:
@@ -193,23 +248,42 @@ def main() -> None:
     check_status("prefill")
 
     # ---- device-timed decode ----
+    # One clock sampler per node (local rank 0, every GPU of the job), started
+    # before the barrier so its start-up is outside the timed region; two CUDA
+    # events bracket the whole K-step loop (no event between steps).
     for _ in range(args.warmup):
         dec.step_device()
     torch.cuda.synchronize()
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    clk = ClockSampler(job_gpu_ids(int(os.environ.get("LOCAL_WORLD_SIZE", comm.size)))) if local == 0 else None
+    if clk is not None:
+        clk.__enter__()
     comm.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        evs[0].record()
-        for i in range(args.steps):
-            dec.step_device()
-            evs[i + 1].record()
-        torch.cuda.synchronize()
+    t_ev0, t_ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_ev0.record()
+    for _ in range(args.steps):
+        dec.step_device()
+    t_ev1.record()
+    torch.cuda.synchronize()
+    if clk is not None:
+        clk.__exit__(None, None, None)
     comm.barrier()
-    total_ms = comm.max_scalar(evs[0].elapsed_time(evs[-1]), dev)
-    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
-    p50 = comm.max_scalar(statistics.median(per_step), dev)
+    total_ms = comm.max_scalar(t_ev0.elapsed_time(t_ev1), dev)
     check_status("decode")
+    # per-step TPOT distribution: a separate loop with an event between steps
+    n_p = min(args.steps, 32)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n_p + 1)]
+    comm.barrier()
+    torch.cuda.synchronize()
+    evs[0].record()
+    for i in range(n_p):
+        dec.step_device()
+        evs[i + 1].record()
+    torch.cuda.synchronize()
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(n_p)]
+    p50 = comm.max_scalar(statistics.median(per_step), dev)
+    p_max = comm.max_scalar(max(per_step), dev)
+    check_status("decode p50")
 
     # ---- end to end through the public per-step API (pinned H2D + D2H each step) ----
     host_tok = torch.randint(0, cfg.vocab, (B,), dtype=torch.int32)
@@ -233,6 +307,7 @@ def main() -> None:
     ms_step = total_ms / args.steps
     value = B * args.steps / (total_ms / 1e3)
     e2e_value = B * args.steps / (e_ms / 1e3)
+    mg_check = multi_gpu_check(model, dec, comm, dev) if comm.size > 1 else None
     dec.release()
     del dec
     torch.cuda.empty_cache()
@@ -257,7 +332,7 @@ def main() -> None:
         ms1 = comm.max_scalar(b0.elapsed_time(b1) / n1, dev)
         check_status("batch-1 decode")
         batch1 = {"tpot_ms": round(ms1, 4), "tok_s": round(1e3 / ms1, 1), "steps": n1,
-                  "vs_baseline_bs1": round((1e3 / ms1) / BASELINE_BS1_TOK_S, 2)}
+                  "vs_baseline_bs1": round((1e3 / ms1) / BASELINE_BS1_TOK_S[args.model], 2)}
         d1.release()
         del d1
     if comm.rank == 0:
@@ -271,7 +346,7 @@ def main() -> None:
             "ms_per_step": round(ms_step, 4),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": round(value / BASELINE_TOK_S, 3),
+            "vs_baseline": round(value / BASELINE_TOK_S[args.model], 3),
             "dtype": ("bf16 activations, fp8 e4m3 weights (128x128 block scales)" if args.fp8 else
                       "bf16, fp8 e4m3 routed experts (128x128 block scales)" if args.fp8_experts else "bf16"),
             "data": "synthetic (uniform-random prompt ids, random-init weights seed 0)",
@@ -288,15 +363,17 @@ def main() -> None:
                 "prefill_sequence_parallel": getattr(model, "seq_parallel", None) is not None,
             },
             "tpot_p50_ms": round(p50, 4),
+            "tpot_max_ms": round(p_max, 4),
             "context": context,
             "prefill_ttft_ms": round(prefill_ms, 2) if prefill_ms else None,
             "prefill_tok_s": round(B * S / (prefill_ms / 1e3), 1) if prefill_ms else None,
-            "clocks": clk.summary(),
+            "clocks": clk.summary() if clk is not None else None,
             "e2e": {"value": round(e2e_value, 2), "unit": "decode tokens/s (StaticDecoder.step, host round trip)",
                     "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
             "gpu_launches": launches_per_step * args.steps,
             "gen_hash_row0": F.gen_hash(row0),
             "batch1_decode": batch1,
+            "multi_gpu_check": mg_check,
             "occupancy_min_rows": {k: min(v) for k, v in occupancy.items() if v},
         }
         print(json.dumps(out))

@@ -2,7 +2,7 @@
 """One eager Qwen3.6 decode step, for kernel-level profiling.
 
 The first bwn kernels this script launches are exactly one decode step, so
-``ncu -k regex:'gemm|deltanet|gqa|rms|embedding|argmax' -c <launches>`` captures
+``ncu --clock-control none -k regex:'gemm|deltanet|gqa|rms|embedding|argmax' -c <launches>`` captures
 that step and nothing else.  Example (one GPU):
 
     ncu --metrics gpu__time_duration.sum --clock-control none \

@@ -106,15 +106,25 @@ def synthetic_hf_layer(cfg: Qwen36Config, i: int, seed: int, device) -> dict[str
     return out
 
 
-def synthetic_hf_globals(cfg: Qwen36Config, seed: int, device) -> dict[str, torch.Tensor]:
+def synthetic_hf_global(cfg: Qwen36Config, name: str, seed: int, device) -> torch.Tensor:
+    """One of the non-layer tensors (``embed_tokens.weight``, ``norm.weight``,
+    ``lm_head.weight``) with its random-init values."""
     H, V = cfg.hidden, cfg.vocab
-    out = {
-        "embed_tokens.weight": seeded_tensor("embed", (V, H), seed, device, std=1.0),
-        "norm.weight": seeded_tensor("final_norm", (H,), seed, device, "normal", 0.05, torch.float32),
-    }
-    if not cfg.tie_embeddings:
-        out["lm_head.weight"] = seeded_tensor("lm_head", (V, H), seed, device, std=0.02)
-    return out
+    if name == "embed_tokens.weight":
+        return seeded_tensor("embed", (V, H), seed, device, std=1.0)
+    if name == "norm.weight":
+        return seeded_tensor("final_norm", (H,), seed, device, "normal", 0.05, torch.float32)
+    if name == "lm_head.weight" and not cfg.tie_embeddings:
+        return seeded_tensor("lm_head", (V, H), seed, device, std=0.02)
+    raise KeyError(name)
+
+
+def synthetic_hf_global_names(cfg: Qwen36Config) -> list[str]:
+    return ["embed_tokens.weight", "norm.weight"] + ([] if cfg.tie_embeddings else ["lm_head.weight"])
+
+
+def synthetic_hf_globals(cfg: Qwen36Config, seed: int, device) -> dict[str, torch.Tensor]:
+    return {n: synthetic_hf_global(cfg, n, seed, device) for n in synthetic_hf_global_names(cfg)}
 
 
 # --------------------------------------------------------------------------

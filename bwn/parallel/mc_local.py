@@ -36,13 +36,17 @@ class LocalMulticastBuffer:
         mprop = drv.CUmulticastObjectProp()
         mprop.numDevices = 1
         mprop.size = nbytes
-        mprop.handleTypes = 0
+        # a multicast object needs a shareable handle type even in one process
+        # (zero is rejected as an invalid value); the bound memory requests the same
+        htype = drv.CUmemAllocationHandleType.CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR
+        mprop.handleTypes = htype
         gran = _check(drv.cuMulticastGetGranularity(
             mprop, drv.CUmulticastGranularity_flags.CU_MULTICAST_GRANULARITY_RECOMMENDED))
         aprop = drv.CUmemAllocationProp()
         aprop.type = drv.CUmemAllocationType.CU_MEM_ALLOCATION_TYPE_PINNED
         aprop.location.type = drv.CUmemLocationType.CU_MEM_LOCATION_TYPE_DEVICE
         aprop.location.id = ordinal
+        aprop.requestedHandleTypes = htype
         pgran = _check(drv.cuMemGetAllocationGranularity(
             aprop, drv.CUmemAllocationGranularity_flags.CU_MEM_ALLOC_GRANULARITY_RECOMMENDED))
         g = max(int(gran), int(pgran))

@@ -39,10 +39,10 @@ def allocate(nbytes: int, group, device, name: str = "symm"):
     multicast address from ``hdl`` start at its first byte), followed by the
     guard tail."""
     import torch.distributed._symmetric_memory as symm
-    try:  # older torch releases want symmetric memory enabled per group first
+    # torch releases before 2.9 want symmetric memory enabled per group first;
+    # later ones deprecate the call (it warns on every rank)
+    if tuple(int(x) for x in torch.__version__.split(".")[:2]) < (2, 9):
         symm.enable_symm_mem_for_group(group.group_name)
-    except Exception:  # noqa: BLE001
-        pass
     full = symm.empty(nbytes + CANARY_BYTES, dtype=torch.uint8, device=device)
     full[:nbytes].zero_()
     full[nbytes:].fill_(CANARY)

@@ -130,7 +130,7 @@ def _usage(body, n_prompt: int):
                         "total_tokens": n_prompt + len(res.tokens)}
 
 
-def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
+def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None, max_n: int = 16):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import PlainTextResponse, StreamingResponse
 
@@ -236,8 +236,8 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
         queued together so the engine batches them."""
         many = isinstance(body.prompt, list) and bool(body.prompt) and not isinstance(body.prompt[0], int)
         prompts = [to_ids(p) for p in body.prompt] if many else [to_ids(body.prompt)]
-        if body.n < 1:
-            raise HTTPException(400, "n must be at least 1")
+        if not 1 <= body.n <= max_n:
+            raise HTTPException(400, f"n must be in [1, {max_n}]")
         cid, created = f"cmpl-{next(_ids)}", int(time.time())
         if body.stream:
             if many or body.n > 1:
@@ -249,10 +249,11 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
                         "choices": [{"index": 0, "text": text, "tokens": toks, "finish_reason": fin}]}
             return StreamingResponse(events(fut, q, chunk, _usage(body, len(prompts[0]))),
                                      media_type="text/event-stream")
+        n_in = sum(map(len, prompts))  # each prompt counted once, whatever n (as chat and OpenAI count)
         prompts = [p for p in prompts for _ in range(body.n)]  # choice i*n + j: prompt i, sample j
         futs = [submit(p, body, False)[0] for p in prompts]
         outs = [wait(f) for f in futs]
-        n_in, n_out = sum(map(len, prompts)), sum(len(o.tokens) for o in outs)
+        n_out = sum(len(o.tokens) for o in outs)
         return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
                 "choices": [{"index": i, "text": codec.decode(o.tokens) if codec else None,
                              "tokens": o.tokens, "finish_reason": o.finish_reason} for i, o in enumerate(outs)],
@@ -270,8 +271,8 @@ def build_app(worker, model_name: str = "bwn", codec: TextCodec | None = None):
             raise HTTPException(400, f"chat template: {e}") from e
         if body.max_completion_tokens is not None:
             body = body.model_copy(update={"max_tokens": body.max_completion_tokens})
-        if body.n < 1 or (body.stream and body.n > 1):
-            raise HTTPException(400, "n must be at least 1, and 1 when streaming")
+        if not 1 <= body.n <= max_n or (body.stream and body.n > 1):
+            raise HTTPException(400, f"n must be in [1, {max_n}], and 1 when streaming")
         cid, created = f"chatcmpl-{next(_ids)}", int(time.time())
         if body.stream:
             out, q = run(prompt, body, True)

@@ -2,6 +2,7 @@
 region runs (read-only queries; no GPU setting is changed)."""
 from __future__ import annotations
 
+import os
 import shutil
 import statistics
 import subprocess
@@ -13,9 +14,22 @@ _FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active
 _REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
 
+def job_gpu_ids(local_world: int) -> list[str]:
+    """``nvidia-smi -i`` ids of this node's GPUs 0..local_world-1 of the job
+    (through ``CUDA_VISIBLE_DEVICES`` when it is set)."""
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if cvd:
+        ids = [x.strip() for x in cvd.split(",") if x.strip()]
+        return ids[:local_world]
+    return [str(i) for i in range(local_world)]
+
+
 class ClockSampler:
-    def __init__(self, gpu_index: int = 0, period_ms: int = 50):
-        self.idx = gpu_index
+    """``gpu_index``: one id or a list of ids (one sampler per node covers every
+    GPU of the job, so N ranks do not each start an ``nvidia-smi``)."""
+
+    def __init__(self, gpu_index=0, period_ms: int = 100):
+        self.idx = ",".join(str(i) for i in gpu_index) if isinstance(gpu_index, (list, tuple)) else str(gpu_index)
         self.period = period_ms
         self.proc = None
         self.lines: list[str] = []

@@ -26,6 +26,7 @@
 #include "common/host.h"
 #include "common/sm100.cuh"
 #include "common/launch.cuh"
+#include "kernels/gqa_decode_noalloc.h"
 #include "kernels/launch.h"
 
 namespace bwn {
@@ -71,7 +72,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
   const int sp = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;  // b: query row
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int ntok = p.n_tok > 1 ? p.n_tok : 1;
-  const int pos = p.positions[b];
+  // a position outside [0, s_max) marks an inactive row: nothing is appended
+  // and no key is read (the cache row it names does not exist)
+  const int pos_in = p.positions[b];
+  const int pos = pos_in < p.s_max ? pos_in : -1;
   const int L = pos + 1;  // keys 0..pos
   int chunk = (L + p.splits - 1) / p.splits;
   chunk = (chunk + kGTile - 1) / kGTile * kGTile;
@@ -436,31 +440,16 @@ void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
 
 
 // ===========================================================================
-// Allocation-free entry point (C ABI).  This has no counterpart in the
-// reference; it exists for callers that cannot allocate device memory: host
-// runtimes that reserve all GPU memory for their own pool at start-up
-// (serving engines, embedded runtimes), plugin interfaces whose contract
-// forbids allocation after initialisation, and latency-critical paths that
-// must not risk the implicit device synchronisation of cudaMalloc/cudaFree.
-// Such a caller passes every input and output; the split-KV partials and the
-// merge tickets live in the fixed-size device array below instead.
-//
-// Limits and sharing rules:
-//  * kNoAllocScratchFloats (1 Mi floats = 4 MiB) holds the partials,
-//    batch * q_heads * splits * (4 + 256) floats; kNoAllocTickets (4096)
-//    bounds batch * kv_heads.  The split count is lowered to fit; a problem
-//    that does not fit even with one split is rejected (return code 2).
-//  * The array exists once per GPU that loads this library and is held until
-//    the process exits.  Every call on a device shares it and it keeps the last
-//    call's contents; the tickets that must start at zero are cleared at the
-//    start of every call.  Calls that overlap on the GPU (different streams,
-//    no ordering between them) race on the array and give wrong results.
-//  * The first call on a device, with that device current, resolves the
-//    array's device address with cudaGetSymbolAddress (host code cannot use
-//    the symbol itself as a device pointer).  Make that first call before any
-//    stream capture that includes this entry point.
-// Return codes: 0 ok, 1 bad argument, 2 scratch too small, 3 CUDA error
-// (symbol lookup, memset or launch), 4 internal error.
+// Allocation-free entry point (C ABI, declared in kernels/gqa_decode_noalloc.h).
+// It has no counterpart in the reference: it serves callers that cannot
+// allocate device memory (runtimes that own every byte of GPU memory, plugin
+// hosts that forbid allocation after start-up, paths that must not risk the
+// implicit synchronisation of cudaMalloc).  Its split-KV partials, merge
+// tickets and status word are the file-scope device arrays below: one copy
+// per GPU that loads the library, kept until exit, shared by every call (calls
+// that overlap on the GPU race).  kNoAllocScratchFloats (1 Mi floats = 4 MiB)
+// holds batch * q_heads * splits * (4 + 256) floats; the split count is
+// lowered to fit, and a problem that does not fit with one split is rejected.
 // ===========================================================================
 namespace {
 constexpr long kNoAllocScratchFloats = 1L << 20;
@@ -476,7 +465,38 @@ static float* g_noalloc_partials_ptr[kNoAllocMaxDevices] = {nullptr};
 static int* g_noalloc_tickets_ptr[kNoAllocMaxDevices] = {nullptr};
 static int* g_noalloc_status_ptr[kNoAllocMaxDevices] = {nullptr};
 
+// Resolves the arrays' device addresses once per device, with that device
+// current (host code cannot pass the symbols themselves to a kernel).
+static bool noalloc_setup(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return false;
+  *dev_out = dev;
+  if (g_noalloc_partials_ptr[dev]) return true;
+  void* p0 = nullptr;
+  void* p1 = nullptr;
+  void* p2 = nullptr;
+  if (cudaGetSymbolAddress(&p0, g_noalloc_partials) != cudaSuccess) return false;
+  if (cudaGetSymbolAddress(&p1, g_noalloc_tickets) != cudaSuccess) return false;
+  if (cudaGetSymbolAddress(&p2, g_noalloc_status) != cudaSuccess) return false;
+  g_noalloc_tickets_ptr[dev] = static_cast<int*>(p1);
+  g_noalloc_status_ptr[dev] = static_cast<int*>(p2);
+  g_noalloc_partials_ptr[dev] = static_cast<float*>(p0);
+  return true;
+}
+
 }  // namespace bwn
+
+extern "C" int bwn_gqa_decode_noalloc_status(int* status_out, cudaStream_t stream) {
+  using namespace bwn;
+  if (!status_out) return BWN_NOALLOC_BAD_ARGUMENT;
+  int dev = 0;
+  if (!noalloc_setup(&dev)) return BWN_NOALLOC_CUDA_ERROR;
+  if (cudaMemcpyAsync(status_out, g_noalloc_status_ptr[dev], sizeof(int), cudaMemcpyDeviceToHost, stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return BWN_NOALLOC_CUDA_ERROR;
+  return BWN_NOALLOC_OK;
+}
 
 extern "C" int bwn_gqa_decode_noalloc(const void* qg, long qg_stride, const void* k_new, const void* v_new,
                                       long kv_new_stride, const float* q_norm_w, const float* k_norm_w,
@@ -488,33 +508,24 @@ extern "C" int bwn_gqa_decode_noalloc(const void* qg, long qg_stride, const void
   if (!qg || !k_new || !v_new || !q_norm_w || !k_norm_w || !cos || !sin || !k_cache || !v_cache || !positions ||
       !out || batch <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads != 0 || s_max <= 0 ||
       rope_dim <= 0 || rope_dim > 256 || (rope_dim & 1))
-    return 1;
+    return BWN_NOALLOC_BAD_ARGUMENT;
   const int G = q_heads / kv_heads;
-  if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8)) return 1;
-  if ((long)batch * kv_heads > kNoAllocTickets) return 2;
+  if (!(G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8)) return BWN_NOALLOC_BAD_ARGUMENT;
+  if ((long)batch * kv_heads > kNoAllocTickets) return BWN_NOALLOC_SCRATCH_TOO_SMALL;
   const long per_split = (long)batch * q_heads * (4 + 256);
-  if (per_split > kNoAllocScratchFloats) return 2;
+  if (per_split > kNoAllocScratchFloats) return BWN_NOALLOC_SCRATCH_TOO_SMALL;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return 3;
-  if (!g_noalloc_partials_ptr[dev]) {  // once per device, with that device current
-    void* p0 = nullptr;
-    void* p1 = nullptr;
-    void* p2 = nullptr;
-    if (cudaGetSymbolAddress(&p0, g_noalloc_partials) != cudaSuccess) return 3;
-    if (cudaGetSymbolAddress(&p1, g_noalloc_tickets) != cudaSuccess) return 3;
-    if (cudaGetSymbolAddress(&p2, g_noalloc_status) != cudaSuccess) return 3;
-    g_noalloc_tickets_ptr[dev] = static_cast<int*>(p1);
-    g_noalloc_status_ptr[dev] = static_cast<int*>(p2);
-    g_noalloc_partials_ptr[dev] = static_cast<float*>(p0);
-  }
+  if (!noalloc_setup(&dev)) return BWN_NOALLOC_CUDA_ERROR;
   if (splits <= 0) splits = 8;
   const long max_splits = kNoAllocScratchFloats / per_split;
   if (splits > max_splits) splits = (int)max_splits;
   if (splits > (s_max + 63) / 64) splits = (s_max + 63) / 64;
   if (splits < 1) splits = 1;
-  // tickets must start at zero (a call that gave up a bounded wait may leave them set)
+  // tickets must start at zero (a call that gave up a bounded wait may leave
+  // them set); the status word reports this call only
   if (cudaMemsetAsync(g_noalloc_tickets_ptr[dev], 0, sizeof(int) * (size_t)batch * kv_heads, stream) != cudaSuccess)
-    return 3;
+    return BWN_NOALLOC_CUDA_ERROR;
+  if (cudaMemsetAsync(g_noalloc_status_ptr[dev], 0, sizeof(int), stream) != cudaSuccess) return BWN_NOALLOC_CUDA_ERROR;
   GqaDecodeArgs p{};
   p.qg = static_cast<const __nv_bfloat16*>(qg);
   p.qg_stride = qg_stride;
@@ -543,7 +554,7 @@ extern "C" int bwn_gqa_decode_noalloc(const void* qg, long qg_stride, const void
   try {
     gqa_decode(p, stream);
   } catch (const std::exception&) {
-    return cudaPeekAtLastError() != cudaSuccess ? 3 : 4;
+    return cudaPeekAtLastError() != cudaSuccess ? BWN_NOALLOC_CUDA_ERROR : BWN_NOALLOC_INTERNAL_ERROR;
   }
-  return 0;
+  return BWN_NOALLOC_OK;
 }

@@ -77,7 +77,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
   pdl_wait();
 
   int Lmax = 0;
-  for (int i = 0; i < ntok; ++i) Lmax = max(Lmax, p.positions[cb * ntok + i] + 1);
+  for (int i = 0; i < ntok; ++i) {
+    const int pi = p.positions[cb * ntok + i];
+    if (pi < p.s_max) Lmax = max(Lmax, pi + 1);  // rows at or past s_max are inactive
+  }
   int chunk = (Lmax + p.splits - 1) / p.splits;
   chunk = (chunk + kTN - 1) / kTN * kTN;
   const int k0 = sp * chunk;
@@ -160,11 +163,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const bool real = r < nrows;
     const int i_tok = real ? r / G : 0, g = real ? r % G : 0;
     const int vrow = cb * ntok + i_tok, qh = kvh * G + g;
-    const int pos = real ? p.positions[vrow] : -1;
+    const int pos_in = real ? p.positions[vrow] : -1;
+    const int pos = pos_in < p.s_max ? pos_in : -1;
     const __nv_bfloat16* qrow = p.qg + (long)vrow * p.qg_stride + (long)qh * 512;
     // q row: RMSNorm(1+w), partial RoPE (rotate-half within rope_dim), 1/sqrt(256)
+    const bool act = real && pos >= 0;  // an inactive row's q is zero (no RoPE row to read)
     float ss = 0.f;
-    if (real) {
+    if (act) {
       for (int c = 0; c < 256; c += 8) {
         const uint4 u = *reinterpret_cast<const uint4*>(qrow + c);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -180,7 +185,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const float qscale = rsqrtf(256.f);
     for (int c = 0; c < 256; c += 8) {
       alignas(16) __nv_bfloat16 o8[8];
-      if (real) {
+      if (act) {
         float x[8], y[8];
         const uint4 u = *reinterpret_cast<const uint4*>(qrow + c);
         const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);

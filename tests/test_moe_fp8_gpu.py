@@ -5,9 +5,7 @@ every token-tile width (BN 16..128), DeepSeek's clamped SwiGLU, a K of 64
 (experts sliced across ranks) and an expert-parallel slice.
 
 Each case runs in its own interpreter, so an error in this kernel is reported
-as this test's failure without touching the CUDA context of the other tests.
-The kernel has not had its first GPU run yet; until it has, these cases run
-only when ``FP8_MOE_GPU_TEST=1`` is set."""
+as this test's failure without touching the CUDA context of the other tests."""
 import json
 import os
 import subprocess
@@ -15,9 +13,7 @@ import sys
 
 import pytest
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FP8_MOE_GPU_TEST") != "1",
-                                 reason="fp8 grouped expert GEMM awaiting its first GPU run (FP8_MOE_GPU_TEST=1)")]
+pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 CHILD = r"""

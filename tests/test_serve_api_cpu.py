@@ -199,5 +199,8 @@ def test_prompt_lists_give_one_choice_each(model, tmp_path):
         assert client.post("/v1/completions", json={"prompt": ps, "stream": True}).status_code == 400
         r = client.post("/v1/completions", json={"prompt": ps, "max_tokens": 2, "n": 2, "ignore_eos": True}).json()
         assert [c["tokens"] for c in r["choices"]] == [_greedy(model, p, 2) for p in ps for _ in range(2)]
+        # each prompt counted once in usage whatever n; n is capped
+        assert r["usage"]["prompt_tokens"] == 5 and r["usage"]["completion_tokens"] == 8
+        assert client.post("/v1/completions", json={"prompt": ps, "n": 1000}).status_code == 400
     finally:
         worker.stop()
