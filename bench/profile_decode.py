@@ -50,6 +50,12 @@ def main():
             def all_reduce_max_(self, x):
                 return x
 
+            def all_gather_first(self, x):  # every rank's shard equal to this one's (shapes only)
+                return torch.cat([x] * self.size, 0)
+
+            def all_gather_last(self, x):
+                return torch.cat([x] * self.size, -1)
+
         comm = ShapeOnlyComm(None, 0, args.tp_shapes)
     m = Qwen36Model(cfg, comm, device=dev).init_random(0)
     st = m.new_state(args.batch, args.ctx + 64)

@@ -1,13 +1,15 @@
 #!/usr/bin/env python
 """Single-process instance of every fused compute + collective path, for
 kernel-level profiling: a process group of one rank, so the same kernels run
-(peer stores land in this GPU's own symmetric buffer, multimem operations act
-on a one-GPU multicast object) without other ranks whose flags a profiler's
-kernel replays would stall.  Each path runs ``--iters`` times.
+(peer stores land in this GPU's own symmetric buffer) without other ranks whose
+flags a profiler's kernel replays would stall.  Paths that need an NVLS
+multicast object (the fused all-reduce, the sequence-parallel gather) are
+skipped here: a one-rank group has none, and the driver rejects a multicast
+object over a single device; those kernels are timed with CUDA events at
+N >= 2 (``bench/comm_bench.py``).  Each path runs ``--iters`` times.
 
-    python bench/profile_fused.py --rows 32 --hidden 5120 --k 2176
-    ncu --set full --clock-control none -k regex:ar_add_norm -c 1 python bench/profile_fused.py
-    python bench/profile_fused.py --paths ar --local-mc   # multimem kernels on a one-GPU multicast object
+    python bench/profile_fused.py --paths ep --ep-tokens 512
+    ncu --set full --clock-control none -k regex:ep_ -c 3 python bench/profile_fused.py --paths ep
 """
 import argparse
 import os
@@ -33,9 +35,6 @@ def main():
     ap.add_argument("--ep-tokens", type=int, default=512)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--paths", default="ar,sp,ep,grad")
-    ap.add_argument("--local-mc", action="store_true",
-                    help="fused all-reduce on a one-GPU multicast object built with the driver API, so the "
-                         "multimem kernels run in this single process")
     a = ap.parse_args()
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -69,8 +68,7 @@ def main():
 
     def ar():
         from bwn.parallel.fused import FusedComm
-        fc = (FusedComm.on_local_multicast(H, max_rows=max(R, 32), device=dev) if a.local_mc
-              else FusedComm(comm, H, max_rows=max(R, 32), device=dev))
+        fc = FusedComm(comm, H, max_rows=max(R, 32), device=dev)
         x = torch.randn(R, K, device=dev, generator=g).bfloat16()
         w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
         resid = torch.randn(R, H, device=dev, generator=g).bfloat16()

@@ -115,6 +115,7 @@ class Qwen36Model(nn.Module):
             self.layers.append({k: v.to(self.device) for k, v in t.items()})
         self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, get, self.tp, self.rank, self.dtype).items()}
         self._shard_embed_table()
+        self._prepare_moe_decode()
         return self
 
     def embed(self, tokens: torch.Tensor) -> torch.Tensor:
@@ -138,12 +139,39 @@ class Qwen36Model(nn.Module):
         self.g = {k: v.to(self.device) for k, v in W.fuse_globals(cfg, glob.__getitem__, self.tp, self.rank,
                                                                    self.dtype).items()}
         self._shard_embed_table()
+        self._prepare_moe_decode()
         return self
 
     def _shard_embed_table(self) -> None:
         if self.shard_embed:
             d = self.d
             self.g["embed"] = self.g["embed"][d.vocab_offset:d.vocab_offset + d.vocab].contiguous()
+
+    def _prepare_moe_decode(self) -> None:
+        """Tensors of the decode-sized MoE path (``_moe_decode``): the router with
+        the shared-expert gate as one more row, and the routed experts with the
+        shared expert appended as one more expert (``*_x``; the routed-only
+        tensors become views of them, so nothing is stored twice).  With experts
+        partitioned across ranks each rank appends the whole shared expert and
+        computes it for its own slice of the tokens; with every expert sliced
+        across ranks it appends its slice and computes it for all tokens."""
+        cfg, d = self.cfg, self.d
+        if not cfg.is_moe:
+            return
+        full = d.moe_sharding != "tp" and self.tp > 1
+        for L in self.layers:
+            L["router_x"] = torch.cat([L["router"], L["shared_gate"]], 0).contiguous()
+            gu, dn = L["experts_gate_up"], L["experts_down"]
+            sgu, sdn = L["shared_gate_up"], L["shared_down"]
+            if full:  # every rank's slice, gathered (16-row interleave blocks stay whole)
+                sgu = self.comm.all_gather_first(sgu.contiguous())
+                sdn = self.comm.all_gather_last(sdn.contiguous()).contiguous()
+            if not torch.is_tensor(gu) or sgu.shape[0] != gu.shape[1] or sdn.shape != dn.shape[1:]:
+                continue  # fp8 experts or a shared expert of another width: kept on its own GEMMs
+            gux = torch.cat([gu, sgu[None].to(gu.dtype)], 0)
+            dnx = torch.cat([dn, sdn[None].to(dn.dtype)], 0)
+            L["experts_gate_up_x"], L["experts_down_x"] = gux, dnx
+            L["experts_gate_up"], L["experts_down"] = gux[:-1], dnx[:-1]
 
     FP8_KEYS = ("in_proj", "out_proj", "qkv_proj", "o_proj", "gate_up", "down", "shared_gate_up", "shared_down")
 
@@ -161,6 +189,8 @@ class Qwen36Model(nn.Module):
             if experts and torch.is_tensor(L.get("experts_gate_up")):
                 L["experts_gate_up"] = FP8Experts.from_interleaved(L["experts_gate_up"])
                 L["experts_down"] = FP8Experts.quantize(L["experts_down"])
+                L.pop("experts_gate_up_x", None)  # the shared expert stays bf16, on its own GEMMs
+                L.pop("experts_down_x", None)
         if include_head:
             self.g["lm_head"] = FP8Weight.from_dense(self.g["lm_head"])
         return self
@@ -248,6 +278,8 @@ class Qwen36Model(nn.Module):
         its experts over all tokens and the partials are all-reduced."""
         ep = getattr(self, "ep_a2a", None)
         T = h.shape[0]
+        if self._moe_decode_ok(i, h) and (ep is None or T // self.tp < ep.min_tokens):
+            return self._moe_decode(i, h, x, nxt)
         if ep is not None and T % self.tp == 0 and ep.min_tokens <= T // self.tp <= ep.T_max:
             from .moe import route
             L = self.layers[i]
@@ -259,6 +291,50 @@ class Qwen36Model(nn.Module):
             ys = ep.moe(hs, w, ids, L["experts_gate_up"], L["experts_down"], shared=(sy, sg))
             return O.add_rms_norm(self.comm.all_gather_first(ys), x, nxt, self.cfg.rms_eps)
         return self._reduce_add_norm(self._mlp(i, h), x, nxt)
+
+    def _moe_decode_ok(self, i: int, h: torch.Tensor) -> bool:
+        from ..utils import env
+        cfg = self.cfg
+        return (h.is_cuda and h.shape[0] <= 64 and "router_x" in self.layers[i] and cfg.hidden % 256 == 0
+                and cfg.hidden <= 4096 and cfg.num_experts <= 512 and cfg.top_k <= 16 and not self.moe_shared_only
+                and bool(env.get("BWN_MOE_FUSED")))
+
+    def _moe_decode(self, i: int, h: torch.Tensor, x: torch.Tensor, nxt: torch.Tensor) -> torch.Tensor:
+        """Decode-sized MoE sub-block in four launches (``csrc/kernels/moe_decode.cu``):
+        fused routing + gather, grouped gate/up, grouped down (the shared expert
+        rides along as one more expert), then one combine kernel that also adds
+        the residual and normalises (one GPU) or stores into the symmetric slot
+        for the fused NVLink reduction (several GPUs)."""
+        L, cfg, d = self.layers[i], self.cfg, self.d
+        T = h.shape[0]
+        o = O.ops()
+        if "experts_gate_up_x" in L:
+            if d.moe_sharding == "tp" or self.tp == 1:
+                t_lo, t_hi = 0, T
+            else:
+                per = -(-T // self.tp)
+                t_lo, t_hi = min(T, self.rank * per), min(T, (self.rank + 1) * per)
+            y, w, pos_of, pos_sh, sg = o.moe_decode(h, L["router_x"], L["experts_gate_up_x"], L["experts_down_x"],
+                                                    None, None, d.expert_offset, cfg.num_experts, cfg.top_k,
+                                                    cfg.norm_topk_prob, True, True, t_lo, t_hi, 0.0)
+            shared_y = None
+        else:  # fp8 experts; the bf16 shared expert on its own GEMMs, gated by the fused router's logit
+            gu, dn = L["experts_gate_up"], L["experts_down"]
+            y, w, pos_of, pos_sh, sg = o.moe_decode(h, L["router_x"], gu.w8, dn.w8, gu.scales16, dn.scales16,
+                                                    d.expert_offset, cfg.num_experts, cfg.top_k, cfg.norm_topk_prob,
+                                                    True, False, 0, 0, 0.0)
+            shared_y = O.linear(O.linear_swiglu(h, L["shared_gate_up"]), L["shared_down"])
+        shared_gate = sg if shared_y is not None else None
+        if self.tp == 1:
+            return o.moe_combine_ex(y, w, pos_of, pos_sh, sg, shared_y, shared_gate, 1, x, nxt, cfg.rms_eps)
+        fc = self.fused_comm
+        if fc is not None and fc.fits(T):
+            o.moe_combine_symm(y, w, pos_of, pos_sh, sg, shared_y, shared_gate, fc.local_ar, fc.buf_elems,
+                               fc.peer_flags_ar, fc.state, fc.rank)
+            return fc.reduce_add_norm(x, nxt, cfg.rms_eps)
+        part = o.moe_combine_ex(y, w, pos_of, pos_sh, sg, shared_y, shared_gate, 0, None, None, 0.0)
+        self.comm.all_reduce_(part)
+        return O.add_rms_norm(part, x, nxt, cfg.rms_eps)
 
     def decode_hidden(self, tokens: torch.Tensor, st: Qwen36State) -> torch.Tensor:
         """One decode step for ``tokens [B]`` at ``st.positions``; advances the

@@ -2,12 +2,13 @@
 
 * Row-parallel GEMM -> all-reduce -> residual add -> RMSNorm (the reference's
   ``o_proj/out_proj/down_proj`` + ``functional_all_reduce`` + next norm,
-  ``contrib/qwen3.6-27b/static_decode.py:798-961``): the tcgen05 GEMM epilogue
-  stores its bf16 partial into this rank's slot of a symmetric buffer and the
-  last CTA publishes an epoch flag to every rank; one small kernel per rank
-  waits for the flags, reads the sum of all ranks' slots with
-  ``multimem.ld_reduce`` (the NVSwitch adds them, fp32 accumulation), adds the
-  residual and normalises.
+  ``contrib/qwen3.6-27b/static_decode.py:798-961``), one launch: the tcgen05
+  GEMM epilogue stores its bf16 partial into this rank's slot of a symmetric
+  buffer and the last CTA publishes an epoch flag to every rank; the same CTAs
+  then wait for every rank's flag, read the sum of all ranks' slots with
+  ``multimem.ld_reduce`` (the NVSwitch adds them, fp32 accumulation), add the
+  residual and normalise (``gemm_symm_norm``; ``BWN_F1_ONE_KERNEL=0`` runs the
+  reduction as a second kernel, ``ar_add_norm``).
 * Sharded greedy (``static_decode_35b.py:1534-1564``): packed (logit, id) keys
   exchanged by peer stores, max taken on every rank, one launch.
 
@@ -52,32 +53,11 @@ class FusedComm:
         self.mc_ar = mc + self.ar_off
         self.local_ar = ptrs[self.rank] + self.ar_off
         self.state = torch.zeros(8, dtype=torch.int32, device=dev)
+        from ..utils import env
+        # row-parallel GEMM + reduction + add + RMSNorm as one launch (gemm_symm_norm)
+        self.one_kernel = bool(env.get("BWN_F1_ONE_KERNEL"))
         self.hdl.barrier()
         torch.cuda.synchronize(dev)
-
-    @classmethod
-    def on_local_multicast(cls, hidden: int, max_rows: int = 256, device=None, timeout_s: float = 5.0):
-        """The same buffer layout on a one-GPU multicast object
-        (:class:`~bwn.parallel.mc_local.LocalMulticastBuffer`): a world of one that
-        still runs the ``multimem`` code path, for single-process profiling."""
-        from .comm import Comm
-        from .mc_local import LocalMulticastBuffer
-        self = cls.__new__(cls)
-        self.comm, self.world, self.rank = Comm.single(), 1, 0
-        self.hidden, self.max_rows, self.timeout_s = hidden, max_rows, timeout_s
-        dev = device or torch.device("cuda", torch.cuda.current_device())
-        slots_bytes = 8 * max_rows * 8
-        self.ar_off = ((self.SLOTS + slots_bytes + 255) // 256) * 256
-        self.buf_elems = max_rows * hidden
-        self.mcbuf = LocalMulticastBuffer(self.ar_off + 2 * self.buf_elems * 2, dev)
-        self.buf, self.hdl = self.mcbuf.tensor, None
-        base = self.mcbuf.uc_ptr
-        self.peer_flags_ar, self.peer_flags_g, self.peer_slots = [base + self.FLAGS_AR], [base + self.FLAGS_GREEDY], \
-            [base + self.SLOTS]
-        self.mc_ar = self.mcbuf.mc_ptr + self.ar_off
-        self.local_ar = base + self.ar_off
-        self.state = torch.zeros(8, dtype=torch.int32, device=dev)
-        return self
 
     def fits(self, rows: int) -> bool:
         return rows <= self.max_rows
@@ -89,6 +69,10 @@ class FusedComm:
         if hasattr(w, "w8"):  # FP8 weight: W8A16 GEMM, then the multicast reduction
             from .. import ops as O
             return self.allreduce_add_norm(O.linear(a, w), x, norm_w, eps)
+        if self.one_kernel:
+            return o.gemm_symm_norm(a, w, self.local_ar, self.mc_ar, self.buf_elems, self.peer_flags_ar,
+                                    self.peer_flags_ar[self.rank], self.state, self.rank, x, norm_w, eps,
+                                    self.timeout_s)
         o.gemm_symm(a, w, self.local_ar, self.buf_elems, w.shape[0], self.peer_flags_ar, self.state, self.rank)
         return o.ar_add_norm(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
                              x, norm_w, eps, self.timeout_s)
@@ -100,6 +84,12 @@ class FusedComm:
                           self.rank)
         return o.ar_add_norm(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
                              x, norm_w, eps, self.timeout_s)
+
+    def reduce_add_norm(self, x: torch.Tensor, norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+        """``x += sum over ranks of the partials already stored and signalled in
+        the symmetric slots`` (e.g. by ``moe_combine_symm``); returns ``rmsnorm(x)*(1+norm_w)``."""
+        return ops().ar_add_norm(self.mc_ar, self.buf_elems, self.peer_flags_ar[self.rank], self.world, self.state,
+                                 x, norm_w, eps, self.timeout_s)
 
     def _zero_norm(self, cols: int, dev) -> torch.Tensor:
         w = getattr(self, "_nw0", None)

@@ -40,6 +40,10 @@ FLAGS = {f.name: f for f in (
          "first non-finite layer)", (0, 1, 2)),
     Flag("BWN_SHARD_EMBED", int, 0, "vocab-parallel token embedding (vocab/tp rows per rank, one all-reduce per "
          "lookup) instead of a replicated table", (0, 1)),
+    Flag("BWN_F1_ONE_KERNEL", int, 1, "row-parallel GEMM, NVLS all-reduce, residual add and RMSNorm in one launch "
+         "(0: the reduction as a second kernel)", (0, 1)),
+    Flag("BWN_MOE_FUSED", int, 1, "decode-sized MoE blocks in four launches (fused routing + gather, shared expert "
+         "folded into the grouped GEMMs, combine fused with the add-norm or the NVLink slot store)", (0, 1)),
     Flag("BWN_MOE_SHARED_ONLY", int, 0, "cost probe: skip the routed experts, keep the shared expert (wrong results)",
          (0, 1)),
 )}

@@ -25,6 +25,7 @@
 #include <climits>
 
 #include "comm/fused.h"
+#include "comm/signal.cuh"
 #include "common/host.h"
 #include "common/launch.cuh"
 #include "common/sm100.cuh"
@@ -61,21 +62,6 @@ __device__ __forceinline__ bool wait_flags(const unsigned* flags, int world, uns
     }
   }
   return true;
-}
-
-// Completion of a producer grid: each CTA (one thread, after a CTA barrier)
-// orders its stores before a ticket; the last CTA publishes the new epoch to
-// every rank's flag array (one system fence, then relaxed stores).
-__device__ __forceinline__ void signal_done(const CommSignal& sig) {
-  __threadfence();
-  const int t = atomicAdd(sig.done_ticket, 1);
-  if (t == (int)gridDim.x - 1) {
-    *sig.done_ticket = 0;
-    fence_acq_rel_sys();
-    const unsigned e = (unsigned)(*sig.epoch) + 1u;
-    *sig.epoch = (int)e;
-    for (int r = 0; r < sig.world; ++r) st_relaxed_sys_u32(sig.peer_flags[r] + sig.rank, e);
-  }
 }
 
 __global__ void __launch_bounds__(256) symm_put_signal_kernel(const __nv_bfloat16* __restrict__ x, long ldx, int rows,

@@ -54,6 +54,7 @@ enum GemmEpilogue : int {
   kEpiSwiGLU = 2,  // out = bf16(silu(gate) * up), gate/up interleaved in blocks of 16
   kEpiF32 = 3,     // out = acc (fp32)
   kEpiSymm = 4,    // bf16 partial into this rank's symmetric buffer slot, then signal every peer
+  kEpiSymmNorm = 5,  // kEpiSymm, then (same launch) the NVLS sum over ranks + residual add + RMSNorm (ArTail)
 };
 
 // Completion signalling of a fused compute + collective launch: the last CTA to
@@ -79,6 +80,25 @@ struct AgWait {
   unsigned long long limit_ns = 0;
 };
 
+// The reduction tail of a kEpiSymmNorm GEMM: once every rank's completion flag
+// has arrived, the CTAs read the sum of all ranks' partial rows through the
+// multicast address (multimem.ld_reduce), add it to the residual (bf16, in
+// place) and write RMSNorm(residual) * (1 + w); the last CTA flips the slot
+// selector.
+struct ArTail {
+  const __nv_bfloat16* mc_base = nullptr;  // multicast address of the two partial slots
+  const unsigned* flags = nullptr;         // this rank's flag array (slot r written by rank r)
+  int* sel = nullptr;                      // [2]: slot selector, CTA ticket
+  __nv_bfloat16* resid = nullptr;
+  long ldr = 0;
+  const float* w = nullptr;
+  __nv_bfloat16* out = nullptr;
+  long ldo = 0;
+  int rows = 0, cols = 0;
+  float eps = 1e-6f;
+  unsigned long long limit_ns = 0;
+};
+
 struct GemmProblem {
   // D[M, N] = A[M, K] . B[N, K]^T ; A, B bf16 K-major
   const void* A = nullptr;
@@ -101,8 +121,9 @@ struct GemmProblem {
   int* tickets = nullptr;
   int tickets_len = 0;
   int* status = nullptr;
-  CommSignal sig;  // kEpiSymm only
+  CommSignal sig;  // kEpiSymm / kEpiSymmNorm
   AgWait ag;       // A all-gathered by peers (normal orientation only)
+  ArTail tail;     // kEpiSymmNorm only
 };
 
 void gemm_bf16(const GemmProblem& p, cudaStream_t stream);

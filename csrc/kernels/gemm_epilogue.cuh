@@ -19,8 +19,9 @@ struct GemmArgs {
   float* workspace;            // splits>1: [tiles * splits * BM * BN] fp32
   int* tickets;                // splits>1: [tiles]
   int* status;
-  CommSignal sig;              // kEpiSymm: completion signal to peers
+  CommSignal sig;              // kEpiSymm / kEpiSymmNorm: completion signal to peers
   AgWait ag;                   // A rows all-gathered by peers: wait per owner
+  ArTail tail;                 // kEpiSymmNorm: reduction + residual + RMSNorm after the signal
 };
 
 // Row tile of a work tile; with an all-gathered A this rank's own rows come first.
@@ -33,7 +34,7 @@ __device__ __forceinline__ int gemm_tile_m(const GemmArgs& a, int tile, int bm) 
 template <int BN, int EPI, bool TRANS>
 __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, const float (&v)[32], int ncols, int m, int n0) {
   // m: global row (A row), n0: global column of v[0]; ncols valid in v (16 or 32)
-  if (EPI == kEpiSymm) {
+  if (EPI == kEpiSymm || EPI == kEpiSymmNorm) {
     // out is this rank's bf16 [tokens, ldo] symmetric buffer pair; the slot in
     // use alternates under the device-side selector.  Peers read it through the
     // multicast address once the completion flag is published.

@@ -41,6 +41,98 @@ struct GemmCfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// The reduction tail of kEpiSymmNorm (all 192 threads, after the CTA's tiles
+// and the completion signal): every CTA that owns token rows waits for every
+// rank's flag to reach `epoch`, then for each of its rows reads the sum of the
+// ranks' partials through the switch, adds the residual and normalises.  The
+// grid is at most one CTA per SM and every CTA triggers its dependents only
+// once all of them run, so CTAs waiting here never keep a peer CTA of their own
+// grid from being scheduled; the wait is bounded.
+constexpr int kTailVec = 4;  // 8-column vectors per thread: cols <= 192 * 8 * 4
+__device__ __forceinline__ void gemm_ar_tail(const GemmArgs& args, unsigned epoch) {
+  const ArTail& t = args.tail;
+  __shared__ float red[kGemmThreads / 32];
+  __shared__ int s_ok;
+  const int world = args.sig.world;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if ((int)blockIdx.x < t.rows && (int)threadIdx.x < world) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while ((int)(ld_acquire_sys(t.flags + threadIdx.x) - epoch) < 0) {
+      if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > t.limit_ns) {
+        set_status(args.status, kStatusPeerTimeout);
+        s_ok = 0;  // a peer that never signalled: nothing is read or written
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const int sel = (*t.sel) & 1;
+  for (int row = blockIdx.x; s_ok && row < t.rows; row += gridDim.x) {
+    const __nv_bfloat16* buf = t.mc_base + (long)sel * args.sig.buf_stride + (long)row * t.cols;
+    float v[kTailVec][8];
+#pragma unroll
+    for (int n = 0; n < kTailVec; ++n) {  // every reduction load in flight before use
+      const int c = (threadIdx.x + n * kGemmThreads) * 8;
+      if (c < t.cols) mc_ld_reduce_bf16x8(buf + c, v[n]);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int n = 0; n < kTailVec; ++n) {
+      const int c = (threadIdx.x + n * kGemmThreads) * 8;
+      if (c >= t.cols) continue;
+      const uint4 rr = *reinterpret_cast<const uint4*>(t.resid + (long)row * t.ldr + c);
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {  // the reduced partial is rounded to bf16, as the unfused all-reduce output
+        const float2 rf = __bfloat1622float2(r2[e]);
+        const float p0 = __bfloat162float(__float2bfloat16(v[n][2 * e]));
+        const float p1 = __bfloat162float(__float2bfloat16(v[n][2 * e + 1]));
+        const __nv_bfloat162 nb = __floats2bfloat162_rn(rf.x + p0, rf.y + p1);
+        o2[e] = nb;
+        const float2 nf = __bfloat1622float2(nb);
+        v[n][2 * e] = nf.x;
+        v[n][2 * e + 1] = nf.y;
+        ss += nf.x * nf.x + nf.y * nf.y;
+      }
+      *reinterpret_cast<uint4*>(t.resid + (long)row * t.ldr + c) = o;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGemmThreads / 32; ++i) tot += red[i];
+    const float inv = rsqrtf(tot / t.cols + t.eps);
+#pragma unroll
+    for (int n = 0; n < kTailVec; ++n) {
+      const int c = (threadIdx.x + n * kGemmThreads) * 8;
+      if (c >= t.cols) continue;
+      uint4 o;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o2[e] = __floats2bfloat162_rn(v[n][2 * e] * inv * (1.f + t.w[c + 2 * e]),
+                                      v[n][2 * e + 1] * inv * (1.f + t.w[c + 2 * e + 1]));
+      *reinterpret_cast<uint4*>(t.out + (long)row * t.ldo + c) = o;
+    }
+    __syncthreads();  // red[] is reused by the next row
+  }
+  // flip the slot selector once every CTA has read it: last CTA (ticket)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int tk = atomicAdd(t.sel + 1, 1);
+    if (tk == (int)gridDim.x - 1) {
+      t.sel[1] = 0;
+      t.sel[0] = t.sel[0] + 1;
+    }
+  }
+}
+
 // MAJ bit 0: A is MN-major (stored [K, M]); bit 1: B is MN-major (stored [K, N]).
 template <int BN, int EPI, bool TRANS, int MAJ>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -333,12 +425,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
-  if (EPI == kEpiSymm && warp >= 2) {
+  if ((EPI == kEpiSymm || EPI == kEpiSymmNorm) && warp >= 2) {
     // publish completion: the epilogue warps' stores precede one thread's
     // system-scope fence (named barrier), then the ticket; the last CTA bumps
     // the epoch and release-stores it to all ranks
     asm volatile("bar.sync 1, 128;" ::: "memory");
     if (threadIdx.x == 64) {
+      // the epoch this launch publishes, read before this CTA's ticket (the
+      // last ticket of the grid is what bumps it)
+      *ticket_bcast = *args.sig.epoch + 1;
       __threadfence();
       const int t = atomicAdd(args.sig.done_ticket, 1);
       if (t == (int)gridDim.x - 1) {
@@ -356,6 +451,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
   }
+  if (EPI == kEpiSymmNorm) gemm_ar_tail(args, (unsigned)*ticket_bcast);
 }
 
 // ---------------------------------------------------------------------------
@@ -467,6 +563,7 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   a.tickets = p.tickets;
   a.status = p.status;
   a.sig = p.sig;
+  a.tail = p.tail;
   const int units = tiles * a.splits;
   const int grid = units < sms ? units : sms;
   const bool tr = p.trans_out;
@@ -496,6 +593,15 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
     case kEpiSymm:
       BWN_CHECK(p.sig.epoch && p.sig.done_ticket && p.sig.world >= 1 && p.sig.world <= 8, "gemm: bad comm signal");
       tr ? dispatch_bn<kEpiSymm, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiSymm, false>(bn, ta, tb, a, grid, stream);
+      break;
+    case kEpiSymmNorm:
+      BWN_CHECK(p.sig.epoch && p.sig.done_ticket && p.sig.world >= 1 && p.sig.world <= 8, "gemm: bad comm signal");
+      BWN_CHECK(p.tail.mc_base && p.tail.flags && p.tail.sel && p.tail.resid && p.tail.w && p.tail.out &&
+                    p.tail.cols % 8 == 0 && p.tail.cols <= kGemmThreads * 8 * kTailVec && p.tail.ldr % 8 == 0 &&
+                    p.tail.ldo % 8 == 0,
+                "gemm: bad reduction tail (hidden a multiple of 8, at most %d)", kGemmThreads * 8 * kTailVec);
+      tr ? dispatch_bn<kEpiSymmNorm, true>(bn, ta, tb, a, grid, stream)
+         : dispatch_bn<kEpiSymmNorm, false>(bn, ta, tb, a, grid, stream);
       break;
     default: BWN_FAIL("gemm: bad epilogue %d", p.epi);
   }

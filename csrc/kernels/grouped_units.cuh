@@ -5,7 +5,7 @@
 
 namespace bwn {
 
-constexpr int kGMaxGroups = 256;
+constexpr int kGMaxGroups = kMoeDecodeMaxGroups;  // local experts + a shared-expert group
 
 // Work units are compacted over the groups' actual row counts (cached in
 // shared memory at kernel start): unit u -> group e by binary search over the

@@ -19,6 +19,7 @@
 //  * moe_combine       out[t] = sum_slot w * y[pos(t, slot)] (+ gated shared
 //                      expert), fp32 accumulation, this rank's partial sum.
 #include "common/host.h"
+#include "common/launch.cuh"
 #include "common/sm100.cuh"
 #include "kernels/moe.h"
 #include "kernels/grouped_units.cuh"
@@ -354,6 +355,9 @@ __global__ void __launch_bounds__(kGThreadsG, 1)
     tmem_relinquish();
   }
   __shared__ GUnits gu;
+  // the row counts and packed rows come from the previous kernel (PDL)
+  pdl_trigger();
+  pdl_wait();
   for (int e = threadIdx.x; e < a.groups; e += blockDim.x) {
     const int c = min(a.counts[e], a.max_tiles_n * BN);
     gu.cnt[e] = c;
@@ -502,8 +506,7 @@ static void launch_grouped(const CUtensorMap& tw, const CUtensorMap& tx, const G
   }
   const int units = a.groups * a.tiles_m * a.max_tiles_n;
   const int sms = num_sms();
-  k<<<units < sms ? units : sms, kGThreadsG, C::kSmem, st>>>(tw, tx, a);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(k, dim3(units < sms ? units : sms), dim3(kGThreadsG), C::kSmem, st, tw, tx, a);
 }
 
 void grouped_gemm(const GroupedProblem& p, cudaStream_t st) {

@@ -4,6 +4,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "common/host.h"
+
 namespace bwn {
 
 struct MoeTopkArgs {
@@ -89,5 +91,63 @@ struct GroupedW8Problem {
   float swiglu_limit = 0.f;
 };
 void grouped_gemm_w8(const GroupedW8Problem& p, cudaStream_t st);
+
+// ---- decode-sized MoE block (csrc/kernels/moe_decode.cu) ---------------------
+constexpr int kMoeDecodeMaxGroups = 320;  // local experts + the shared-expert group
+
+// Router GEMV (+ shared-gate row) -> grid barrier -> softmax / top-k /
+// renormalise -> stable expert-major packing (+ the shared expert as group
+// E_local over tokens [t_lo, t_hi)) -> gather of the packed rows, one launch.
+struct MoeRouteFusedArgs {
+  const __nv_bfloat16* x;       // [T, H] normed hidden (row stride ldx)
+  long ldx;
+  const __nv_bfloat16* router;  // [E (+1), H]: routed experts' rows, then the shared gate row when has_sg
+  int T, H, E, k;
+  bool renorm, has_sg;
+  int e0, E_local;              // this rank's experts [e0, e0 + E_local)
+  bool shared_group;            // pack the shared expert as group E_local
+  int t_lo, t_hi;               // tokens whose shared-expert rows this rank computes
+  float* logits;                // [T, E (+1)] scratch
+  unsigned* bar;                // [2] grid barrier (arrivals, generation); zero before first use
+  float* w;                     // [T, k] routing weights
+  int* ids;                     // [T, k] expert ids
+  float* sg;                    // [T] shared-gate logit (0 without has_sg)
+  int* counts;                  // [G] rows per group
+  int* offsets;                 // [G + 1]
+  int* pos_of;                  // [T * k] packed row of each pair, -1 when its expert is not local
+  int* pos_sh;                  // [T] packed row of each token's shared-expert row, -1 if none
+  __nv_bfloat16* x_perm;        // [T * k + T, H] packed rows
+  int* status;
+  unsigned long long limit_ns;
+};
+void moe_route_fused(const MoeRouteFusedArgs& a, cudaStream_t st);
+int moe_route_fused_grid(int T, int E, bool has_sg);
+
+enum { kCombinePartial = 0, kCombineAddNorm = 1, kCombineSymm = 2 };
+// Per token: sum_slot w * y[pos_of] + sigmoid(sg) * y[pos_sh] (+ sigmoid(shared_gate)
+// * shared_y), fp32, rounded to bf16 once; then stored (partial), added to the
+// residual and RMSNorm(1+w)'d (add-norm), or stored into this rank's symmetric
+// slot with the completion flag published (symm).
+struct MoeCombineExArgs {
+  const __nv_bfloat16* y;  // [rows, H] expert outputs, packed
+  const float* w;          // [T, k]
+  const int* pos_of;       // [T, k]
+  int T, k, H;
+  const int* pos_sh;       // [T] or null
+  const float* sg;         // [T] shared-gate logits (with pos_sh)
+  const __nv_bfloat16* shared_y;  // [T, H] separately computed shared expert, or null
+  long ld_shared;
+  const float* shared_gate;       // [T] its gate logits
+  int mode;
+  __nv_bfloat16* out;      // partial / normed output
+  long ldo;
+  __nv_bfloat16* resid;    // add-norm: residual stream (updated)
+  long ldr;
+  const float* norm_w;
+  float eps;
+  __nv_bfloat16* symm_base;  // symm: this rank's slot base
+  CommSignal sig;
+};
+void moe_combine_ex(const MoeCombineExArgs& a, cudaStream_t st);
 
 }  // namespace bwn

@@ -1,0 +1,370 @@
+// Decode-sized MoE block (Qwen3.6-35B-A3B: softmax router, top-k, routed SwiGLU
+// experts, sigmoid-gated shared expert; the reference's moe_forward / _moe,
+// contrib/qwen3.6-35b-a3b/static_decode_35b.py:701-833, 1110-1185) in four
+// launches instead of twelve:
+//
+//  1. moe_route_fused  the router GEMV (and the shared-expert gate row), a
+//                      grid barrier, softmax / top-k / renormalisation, the
+//                      stable expert-major packing of this rank's (token, slot)
+//                      pairs, and the gather of the packed token rows -- one
+//                      launch.  The shared expert is packed as one more group
+//                      (its rows: the tokens this rank owns), so the grouped
+//                      GEMMs run it with the routed experts.
+//  2, 3. grouped tcgen05 GEMMs (gate/up with the SwiGLU epilogue, then down;
+//                      csrc/kernels/moe.cu) over the packed rows.
+//  4. moe_combine_ex   per token: sum of w * expert rows + sigmoid(gate) *
+//                      shared row in fp32, rounded to bf16 once, then either
+//                      stored (the partial), added to the residual and
+//                      RMSNorm(1+w)'d (one GPU), or stored into this rank's
+//                      symmetric slot with the completion flag published to
+//                      every rank (the fused NVLink reduction follows).
+//
+// Every CTA of moe_route_fused computes the (tiny) routing itself from the
+// logits all CTAs produced, so the packing is identical everywhere and no
+// second barrier is needed: each CTA then gathers its share of the rows.  The
+// grid is at most one CTA per SM and each CTA starts its dependents only once
+// all of them run, so the barrier's CTAs are co-resident; its wait is bounded
+// and reports a timeout through the status word.
+#include "comm/signal.cuh"
+#include "common/host.h"
+#include "common/launch.cuh"
+#include "common/sm100.cuh"
+#include "kernels/moe.h"
+
+namespace bwn {
+
+namespace {
+constexpr int kRtThreads = 256;
+constexpr int kRtWarps = kRtThreads / 32;
+constexpr int kRtMaxT = 64;
+constexpr int kRtMaxK = 16;
+constexpr int kRtMaxPairs = kRtMaxT * kRtMaxK;
+constexpr int kRtMaxVec = 16;  // hidden <= 16 * 256
+
+struct RouteSmem {
+  float w[kRtMaxPairs];
+  int ids[kRtMaxPairs];
+  int pos[kRtMaxPairs];
+  int src[kRtMaxPairs + kRtMaxT];  // token of each packed row
+  int cnt[kMoeDecodeMaxGroups];
+  int off[kMoeDecodeMaxGroups + 1];
+  float sg[kRtMaxT];
+  int abort;
+};
+
+__device__ __forceinline__ float dot8_bf16(const uint4& a, const uint4& b) {
+  const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 x = __bfloat1622float2(a2[e]);
+    const float2 y = __bfloat1622float2(b2[e]);
+    s = fmaf(x.x, y.x, s);
+    s = fmaf(x.y, y.y, s);
+  }
+  return s;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFusedArgs a) {
+  __shared__ RouteSmem s;
+  pdl_trigger();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = a.E + (a.has_sg ? 1 : 0);  // router rows (+ shared gate row)
+  const int ntg = (a.T + 7) / 8;
+  const int nvec = a.H / 256;  // 16-byte vectors per lane per row
+  // ---- 1. router logits: one warp per (router row, group of 8 tokens) ----
+  for (int item = blockIdx.x * kRtWarps + warp; item < rows * ntg; item += gridDim.x * kRtWarps) {
+    const int e = item / ntg, tg = item % ntg;
+    const uint4* wr = reinterpret_cast<const uint4*>(a.router + (long)e * a.H);
+    uint4 wv[kRtMaxVec];
+#pragma unroll
+    for (int j = 0; j < kRtMaxVec; ++j)
+      if (j < nvec) wv[j] = wr[lane + 32 * j];
+    const int t1 = min(a.T, tg * 8 + 8);
+    for (int t = tg * 8; t < t1; ++t) {
+      const uint4* xr = reinterpret_cast<const uint4*>(a.x + (long)t * a.ldx);
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < kRtMaxVec; ++j)
+        if (j < nvec) acc += dot8_bf16(wv[j], xr[lane + 32 * j]);
+      acc = warp_sum(acc);
+      if (lane == 0) a.logits[(long)t * rows + e] = acc;
+    }
+  }
+  // ---- 2. grid barrier (count, generation); bounded wait ----
+  if (threadIdx.x == 0) s.abort = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned gen = ld_acquire_gpu_u32(a.bar + 1);
+    __threadfence();
+    const unsigned arrived = atomicAdd(a.bar, 1u);
+    if (arrived == gridDim.x - 1) {
+      atomicExch(a.bar, 0u);
+      __threadfence();
+      atomicAdd(a.bar + 1, 1u);
+    } else {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_gpu_u32(a.bar + 1) == gen) {
+        if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > a.limit_ns) {
+          set_status(a.status, kStatusFlagTimeout);
+          s.abort = 1;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  if (s.abort) return;
+  // ---- 3. routing (every CTA, identically): softmax -> top-k -> renormalise ----
+  const int E = a.E, k = a.k, T = a.T;
+  const int epl = (E + 31) / 32;
+  for (int t = warp; t < T; t += kRtWarps) {
+    const float* l = a.logits + (long)t * rows;
+    float v[16];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = i * 32 + lane;
+      v[i] = (i < epl && e < E) ? __ldcg(l + e) : -INFINITY;
+      mx = fmaxf(mx, v[i]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = (i < epl && i * 32 + lane < E) ? __expf(v[i] - mx) : 0.f;
+      sum += v[i];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+    float picked = 0.f, my_w = 0.f;
+    int my_id = -1;
+    for (int sl = 0; sl < k; ++sl) {
+      float best = -1.f;
+      int bid = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = i * 32 + lane;
+        if (i < epl && e < E && (v[i] > best || (v[i] == best && e < bid))) {
+          best = v[i];
+          bid = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
+        if (ob > best || (ob == best && oi < bid)) {
+          best = ob;
+          bid = oi;
+        }
+      }
+      const float p = best * inv;
+      picked += p;
+      if (lane == sl) {
+        my_w = p;
+        my_id = bid;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i * 32 + lane == bid) v[i] = -2.f;
+    }
+    if (lane < k) {
+      s.w[t * k + lane] = a.renorm ? my_w / picked : my_w;
+      s.ids[t * k + lane] = my_id;
+    }
+    if (lane == 0) s.sg[t] = a.has_sg ? __ldcg(l + E) : 0.f;
+  }
+  // ---- stable expert-major packing of this rank's pairs (+ the shared group) ----
+  const int G = a.E_local + (a.shared_group ? 1 : 0);
+  for (int g = threadIdx.x; g < G; g += blockDim.x) s.cnt[g] = 0;
+  __syncthreads();
+  const int n = T * k;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int el = s.ids[i] - a.e0;
+    if (el >= 0 && el < a.E_local) atomicAdd(&s.cnt[el], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (a.shared_group) s.cnt[a.E_local] = a.t_hi - a.t_lo;
+    int o = 0;
+    for (int g = 0; g < G; ++g) {
+      s.off[g] = o;
+      o += s.cnt[g];
+    }
+    s.off[G] = o;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int id = s.ids[i], el = id - a.e0;
+    int p = -1;
+    if (el >= 0 && el < a.E_local) {
+      int r = 0;  // earlier pairs (token order, then slot) routed to the same expert
+      for (int j = 0; j < i; ++j) r += s.ids[j] == id;
+      p = s.off[el] + r;
+      s.src[p] = i / k;
+    }
+    s.pos[i] = p;
+  }
+  if (a.shared_group)
+    for (int t = a.t_lo + threadIdx.x; t < a.t_hi; t += blockDim.x) s.src[s.off[a.E_local] + t - a.t_lo] = t;
+  __syncthreads();
+  // ---- 4. gather this CTA's share of the packed rows; CTA 0 writes the routing ----
+  const int total = s.off[G];
+  const int hv = a.H / 8;
+  for (int r = blockIdx.x; r < total; r += gridDim.x) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + (long)s.src[r] * a.ldx);
+    uint4* dst = reinterpret_cast<uint4*>(a.x_perm + (long)r * a.H);
+    for (int v = threadIdx.x; v < hv; v += blockDim.x) dst[v] = src[v];
+  }
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      a.w[i] = s.w[i];
+      a.ids[i] = s.ids[i];
+      a.pos_of[i] = s.pos[i];
+    }
+    for (int g = threadIdx.x; g < G; g += blockDim.x) a.counts[g] = s.cnt[g];
+    for (int g = threadIdx.x; g <= G; g += blockDim.x) a.offsets[g] = s.off[g];
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+      a.pos_sh[t] = (a.shared_group && t >= a.t_lo && t < a.t_hi) ? s.off[a.E_local] + t - a.t_lo : -1;
+      a.sg[t] = s.sg[t];
+    }
+  }
+}
+
+// One CTA per token.  VPT: 8-column vectors per thread (H <= 256 * 8 * VPT).
+template <int VPT>
+__global__ void __launch_bounds__(256) moe_combine_ex_kernel(MoeCombineExArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  __shared__ int s_pos[kRtMaxK + 1];
+  __shared__ float s_w[kRtMaxK + 1];
+  __shared__ float red[8];
+  if (threadIdx.x < a.k) {
+    s_pos[threadIdx.x] = a.pos_of[(long)t * a.k + threadIdx.x];
+    s_w[threadIdx.x] = a.w[(long)t * a.k + threadIdx.x];
+  }
+  if (threadIdx.x == 0) {
+    const int ps = a.pos_sh ? a.pos_sh[t] : -1;
+    s_pos[kRtMaxK] = ps;
+    s_w[kRtMaxK] = ps >= 0 ? sigmoid_f(a.sg[t]) : 0.f;
+  }
+  __syncthreads();
+  const float gsep = a.shared_y ? sigmoid_f(a.shared_gate[t]) : 0.f;
+  const int nvec = a.H >> 3;
+  __nv_bfloat16* slot = a.mode == kCombineSymm ? a.symm_base + (long)((*a.sig.sel) & 1) * a.sig.buf_stride : nullptr;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi >= nvec) continue;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    auto add_row = [&](const __nv_bfloat16* rowp, float wt) {
+      const uint4 u = reinterpret_cast<const uint4*>(rowp)[vi];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h2[e]);
+        acc[2 * e] += wt * f.x;
+        acc[2 * e + 1] += wt * f.y;
+      }
+    };
+    for (int sl = 0; sl < a.k; ++sl) {
+      const int r = s_pos[sl];
+      if (r >= 0) add_row(a.y + (long)r * a.H, s_w[sl]);
+    }
+    if (s_pos[kRtMaxK] >= 0) add_row(a.y + (long)s_pos[kRtMaxK] * a.H, s_w[kRtMaxK]);
+    if (a.shared_y) add_row(a.shared_y + (long)t * a.ld_shared, gsep);
+    alignas(16) __nv_bfloat16 pb[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) pb[e] = __float2bfloat16(acc[e]);
+    if (a.mode == kCombinePartial) {
+      reinterpret_cast<uint4*>(a.out + (long)t * a.ldo)[vi] = *reinterpret_cast<uint4*>(pb);
+    } else if (a.mode == kCombineSymm) {
+      reinterpret_cast<uint4*>(slot + (long)t * a.H)[vi] = *reinterpret_cast<uint4*>(pb);
+    } else {  // residual add (bf16, as the unfused add_rms_norm) then RMSNorm(1+w)
+      const uint4 rr = reinterpret_cast<const uint4*>(a.resid + (long)t * a.ldr)[vi];
+      const __nv_bfloat16* rh = reinterpret_cast<const __nv_bfloat16*>(&rr);
+      alignas(16) __nv_bfloat16 nr[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        nr[e] = __float2bfloat16(__bfloat162float(pb[e]) + __bfloat162float(rh[e]));
+        v[i][e] = __bfloat162float(nr[e]);
+        ss += v[i][e] * v[i][e];
+      }
+      reinterpret_cast<uint4*>(a.resid + (long)t * a.ldr)[vi] = *reinterpret_cast<uint4*>(nr);
+    }
+  }
+  if (a.mode == kCombineSymm) {
+    __syncthreads();  // the CTA's slot stores precede thread 0's system-scope fence
+    if (threadIdx.x == 0) signal_done(a.sig);
+    return;
+  }
+  if (a.mode != kCombineAddNorm) return;
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float inv = rsqrtf(tot / a.H + a.eps);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi >= nvec) continue;
+    alignas(16) __nv_bfloat16 o[8];
+    const float4 w0 = reinterpret_cast<const float4*>(a.norm_w)[2 * vi];
+    const float4 w1 = reinterpret_cast<const float4*>(a.norm_w)[2 * vi + 1];
+    const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __float2bfloat16(v[i][e] * inv * (1.f + ww[e]));
+    reinterpret_cast<uint4*>(a.out + (long)t * a.ldo)[vi] = *reinterpret_cast<uint4*>(o);
+  }
+}
+
+int moe_route_fused_grid(int T, int E, bool has_sg) {
+  const int items = (E + (has_sg ? 1 : 0)) * ((T + 7) / 8);
+  int grid = (items + kRtWarps - 1) / kRtWarps;
+  return std::max(1, std::min(grid, num_sms()));
+}
+
+void moe_route_fused(const MoeRouteFusedArgs& a, cudaStream_t st) {
+  BWN_CHECK(a.T >= 1 && a.T <= kRtMaxT, "moe_route_fused: 1..%d tokens", kRtMaxT);
+  BWN_CHECK(a.k >= 1 && a.k <= kRtMaxK && a.k <= a.E && a.E <= 512, "moe_route_fused: k <= 16, E <= 512");
+  BWN_CHECK(a.H % 256 == 0 && a.H / 256 <= kRtMaxVec && a.ldx % 8 == 0, "moe_route_fused: H multiple of 256, <= 4096");
+  BWN_CHECK(a.E_local + (a.shared_group ? 1 : 0) <= kMoeDecodeMaxGroups, "moe_route_fused: too many groups");
+  BWN_CHECK(!a.shared_group || (0 <= a.t_lo && a.t_lo <= a.t_hi && a.t_hi <= a.T), "moe_route_fused: token range");
+  launch_k(moe_route_fused_kernel, dim3(moe_route_fused_grid(a.T, a.E, a.has_sg)), dim3(kRtThreads), 0, st, a);
+}
+
+void moe_combine_ex(const MoeCombineExArgs& a, cudaStream_t st) {
+  if (a.T == 0) return;
+  BWN_CHECK(a.H % 8 == 0 && a.k <= kRtMaxK, "moe_combine_ex: H multiple of 8, k <= 16");
+  BWN_CHECK(a.mode != kCombinePartial || a.ldo % 8 == 0, "moe_combine_ex: 16-byte aligned output rows");
+  BWN_CHECK(a.mode != kCombineAddNorm || (a.ldr % 8 == 0 && a.ldo % 8 == 0), "moe_combine_ex: aligned rows");
+  BWN_CHECK(!a.shared_y || a.ld_shared % 8 == 0, "moe_combine_ex: aligned shared rows");
+  const int vpt = (a.H / 8 + 255) / 256;
+  switch (vpt) {
+    case 1: launch_k(moe_combine_ex_kernel<1>, dim3(a.T), dim3(256), 0, st, a); break;
+    case 2: launch_k(moe_combine_ex_kernel<2>, dim3(a.T), dim3(256), 0, st, a); break;
+    case 3: launch_k(moe_combine_ex_kernel<3>, dim3(a.T), dim3(256), 0, st, a); break;
+    case 4: launch_k(moe_combine_ex_kernel<4>, dim3(a.T), dim3(256), 0, st, a); break;
+    default: BWN_FAIL("moe_combine_ex: hidden %d too wide", a.H);
+  }
+}
+
+}  // namespace bwn

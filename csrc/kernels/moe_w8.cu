@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 
 #include "common/host.h"
+#include "common/launch.cuh"
 #include "common/sm100.cuh"
 #include "kernels/grouped_units.cuh"
 #include "kernels/moe.h"
@@ -121,6 +122,9 @@ __global__ void __launch_bounds__(kXThreads, 1)
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  // the row counts and packed rows come from the previous kernel (PDL)
+  pdl_trigger();
+  pdl_wait();
   gunits_fill(a, gu, BN);
   tc_fence_before();
   __syncthreads();
@@ -327,8 +331,7 @@ void launch_w8g(const CUtensorMap& tw, const CUtensorMap& tx, const GroupedW8Arg
   }
   const int units = a.g.groups * a.g.tiles_m * a.g.max_tiles_n;
   const int sms = num_sms();
-  k<<<units < sms ? units : sms, kXThreads, C::kSmem, st>>>(tw, tx, a);
-  BWN_CUDA_CHECK(cudaGetLastError());
+  launch_k(k, dim3(units < sms ? units : sms), dim3(kXThreads), C::kSmem, st, tw, tx, a);
 }
 
 }  // namespace

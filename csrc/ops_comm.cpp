@@ -10,6 +10,7 @@
 #include "comm/fused.h"
 #include "comm/grad_reduce.h"
 #include "common/host.h"
+#include "kernels/moe.h"
 #include "ops_ext.h"
 
 namespace bwn {
@@ -35,12 +36,12 @@ static CommSignal make_sig(const std::vector<int64_t>& peer_flags, const Tensor&
 
 // Row-parallel GEMM whose epilogue stores the bf16 partial into this rank's
 // symmetric slot and publishes the completion flag to every rank.
-void gemm_symm_op(const Tensor& x, const Tensor& w, int64_t local_base, int64_t buf_stride, int64_t ldo,
-                  std::vector<int64_t> peer_flags, const Tensor& local_state, int64_t rank) {
+static GemmProblem symm_gemm_problem(const Tensor& x, const Tensor& w, int64_t local_base, int64_t buf_stride,
+                                     int64_t ldo, const std::vector<int64_t>& peer_flags, const Tensor& local_state,
+                                     int64_t rank) {
   check_bf16(x, "x");
   check_bf16(w, "w");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && w.dim() == 2 && w.stride(1) == 1, "row-major x, w");
-  const c10::cuda::CUDAGuard guard(x.device());
   const int M = (int)x.size(0), Nw = (int)w.size(0), K = (int)x.size(1);
   GemmProblem p;
   p.epi = kEpiSymm;
@@ -76,7 +77,46 @@ void gemm_symm_op(const Tensor& x, const Tensor& w, int64_t local_base, int64_t 
     p.tickets = s.tickets.data_ptr<int>();
     p.tickets_len = (int)s.tickets.numel();
   }
+  return p;
+}
+
+void gemm_symm_op(const Tensor& x, const Tensor& w, int64_t local_base, int64_t buf_stride, int64_t ldo,
+                  std::vector<int64_t> peer_flags, const Tensor& local_state, int64_t rank) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmProblem p = symm_gemm_problem(x, w, local_base, buf_stride, ldo, peer_flags, local_state, rank);
   gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
+}
+
+// F1 in one launch: the row-parallel GEMM stores its partial into this rank's
+// symmetric slot and signals; the same CTAs then wait for every rank, read the
+// sum through the multicast address, add the residual (in place) and return
+// RMSNorm(residual) * (1 + norm_w).
+Tensor gemm_symm_norm_op(const Tensor& x, const Tensor& w, int64_t local_base, int64_t mc_base, int64_t buf_stride,
+                         std::vector<int64_t> peer_flags, int64_t flags_local, const Tensor& local_state,
+                         int64_t rank, Tensor residual, const Tensor& norm_w, double eps, double timeout_s) {
+  check_bf16(residual, "residual");
+  check_f32(norm_w, "norm_w");
+  TORCH_CHECK(residual.dim() == 2 && residual.stride(1) == 1 && residual.size(0) == x.size(0) &&
+                  residual.size(1) == w.size(0) && norm_w.numel() == w.size(0),
+              "residual [rows, H] with H = w.size(0)");
+  const c10::cuda::CUDAGuard guard(x.device());
+  GemmProblem p = symm_gemm_problem(x, w, local_base, buf_stride, w.size(0), peer_flags, local_state, rank);
+  auto out = at::empty({residual.size(0), residual.size(1)}, residual.options());
+  p.epi = kEpiSymmNorm;
+  p.tail.mc_base = reinterpret_cast<const __nv_bfloat16*>(mc_base);
+  p.tail.flags = reinterpret_cast<const unsigned*>(flags_local);
+  p.tail.sel = local_state.data_ptr<int>() + 2;
+  p.tail.resid = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  p.tail.ldr = residual.stride(0);
+  p.tail.w = norm_w.data_ptr<float>();
+  p.tail.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.tail.ldo = out.stride(0);
+  p.tail.rows = (int)residual.size(0);
+  p.tail.cols = (int)residual.size(1);
+  p.tail.eps = (float)eps;
+  p.tail.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  gemm_bf16(p, at::cuda::getCurrentCUDAStream().stream());
+  return out;
 }
 
 void symm_put_signal_op(const Tensor& x, int64_t local_base, int64_t buf_stride, std::vector<int64_t> peer_flags,
@@ -87,6 +127,21 @@ void symm_put_signal_op(const Tensor& x, int64_t local_base, int64_t buf_stride,
   symm_put_signal(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)x.size(0), (int)x.size(1),
                   reinterpret_cast<__nv_bfloat16*>(local_base), make_sig(peer_flags, local_state, rank, buf_stride),
                   at::cuda::getCurrentCUDAStream().stream());
+}
+
+// MoE combine (routed + shared expert rows, fp32, rounded to bf16 once)
+// straight into this rank's symmetric slot, with the completion flag published:
+// the combine and symm_put_signal in one launch; ar_add_norm follows.
+void moe_combine_symm_op(const Tensor& y, const Tensor& w, const Tensor& pos_of, const c10::optional<Tensor>& pos_sh,
+                         const c10::optional<Tensor>& sg, const c10::optional<Tensor>& shared_y,
+                         const c10::optional<Tensor>& shared_gate, int64_t local_base, int64_t buf_stride,
+                         std::vector<int64_t> peer_flags, const Tensor& local_state, int64_t rank) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  MoeCombineExArgs c = combine_args(y, w, pos_of, pos_sh, sg, shared_y, shared_gate);
+  c.mode = kCombineSymm;
+  c.symm_base = reinterpret_cast<__nv_bfloat16*>(local_base);
+  c.sig = make_sig(peer_flags, local_state, rank, buf_stride);
+  moe_combine_ex(c, at::cuda::getCurrentCUDAStream().stream());
 }
 
 Tensor ar_add_norm_op(int64_t mc_base, int64_t buf_stride, int64_t flags_local, int64_t world,
@@ -414,8 +469,15 @@ void register_comm_defs(torch::Library& m) {
       "gemm_symm(Tensor x, Tensor w, int local_base, int buf_stride, int ldo, int[] peer_flags, "
       "Tensor(a!) local_state, int rank) -> ()");
   m.def(
+      "gemm_symm_norm(Tensor x, Tensor w, int local_base, int mc_base, int buf_stride, int[] peer_flags, "
+      "int flags_local, Tensor(a!) local_state, int rank, Tensor(b!) residual, Tensor norm_w, float eps, "
+      "float timeout_s) -> Tensor");
+  m.def(
       "symm_put_signal(Tensor x, int local_base, int buf_stride, int[] peer_flags, Tensor(a!) local_state, "
       "int rank) -> ()");
+  m.def(
+      "moe_combine_symm(Tensor y, Tensor w, Tensor pos_of, Tensor? pos_sh, Tensor? sg, Tensor? shared_y, "
+      "Tensor? shared_gate, int local_base, int buf_stride, int[] peer_flags, Tensor(a!) local_state, int rank) -> ()");
   m.def(
       "ar_add_norm(int mc_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
       "Tensor(b!) residual, Tensor w, float eps, float timeout_s) -> Tensor");
@@ -438,7 +500,9 @@ void register_comm_impls(torch::Library& m) {
   m.impl("ep_dispatch", &ep_dispatch_op);
   m.impl("ep_return", &ep_return_op);
   m.impl("gemm_symm", &gemm_symm_op);
+  m.impl("gemm_symm_norm", &gemm_symm_norm_op);
   m.impl("symm_put_signal", &symm_put_signal_op);
+  m.impl("moe_combine_symm", &moe_combine_symm_op);
   m.impl("ar_add_norm", &ar_add_norm_op);
   m.impl("ar_hc_post", &ar_hc_post_op);
   m.impl("greedy_allmax", &greedy_allmax_op);

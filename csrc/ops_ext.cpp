@@ -2,6 +2,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <mutex>
 #include <tuple>
 
 #include "common/host.h"
@@ -342,6 +343,214 @@ Tensor moe_experts_w8_op(const Tensor& x, const Tensor& w, const Tensor& ids, co
 }
 
 // ---------------------------------------------------------------------------
+// Decode-sized MoE block (csrc/kernels/moe_decode.cu): fused routing and gather
+// (+ the shared expert as one more group), the two grouped GEMMs (bf16, or fp8
+// E4M3FN experts when gate_up is uint8), then one combine kernel.
+
+// grid-barrier words of moe_route_fused, one pair per device, zeroed once
+static unsigned* moe_barrier_for(const Tensor& like) {
+  static std::mutex mu;
+  static Tensor bars[64];
+  const int dev = like.get_device();
+  std::lock_guard<std::mutex> lk(mu);
+  if (!bars[dev & 63].defined()) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(at::cuda::getCurrentCUDAStream(dev).stream(), &cs);
+    TORCH_CHECK(cs == cudaStreamCaptureStatusNone,
+                "bwn: moe_decode must run once eagerly before CUDA-graph capture");
+    bars[dev & 63] = at::zeros({64}, like.options().dtype(at::kInt));
+  }
+  return reinterpret_cast<unsigned*>(bars[dev & 63].data_ptr<int>());
+}
+
+// Returns (y [rows, H], w [T, k], pos_of [T, k], pos_sh [T], sg [T]); rows
+// T*k + T.  gate_up [G, 2I, H] / down [G, H, I] hold this rank's experts and,
+// with shared_group, the shared expert as group G-1 (its rows: tokens [t_lo, t_hi)).
+std::vector<Tensor> moe_decode_op(const Tensor& x, const Tensor& router, const Tensor& gate_up, const Tensor& down,
+                                  const c10::optional<Tensor>& gate_up_s16, const c10::optional<Tensor>& down_s16,
+                                  int64_t e0, int64_t E, int64_t k, bool renorm, bool has_sg, bool shared_group,
+                                  int64_t t_lo, int64_t t_hi, double swiglu_limit) {
+  check_bf16(x, "x");
+  check_bf16(router, "router");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && router.is_contiguous(), "x [T, H] rows, router contiguous");
+  const bool fp8 = gate_up.scalar_type() == at::kByte;
+  if (!fp8) {
+    check_bf16(gate_up, "gate_up");
+    check_bf16(down, "down");
+  } else {
+    TORCH_CHECK(gate_up_s16.has_value() && down_s16.has_value(), "fp8 experts need their scales");
+    check_f32(*gate_up_s16, "gate_up_scales16");
+    check_f32(*down_s16, "down_scales16");
+  }
+  TORCH_CHECK(gate_up.is_contiguous() && down.is_contiguous() && gate_up.dim() == 3 && down.dim() == 3,
+              "experts [G, 2I, H] / [G, H, I] contiguous");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0), H = (int)x.size(1);
+  const int G = (int)gate_up.size(0), I2 = (int)gate_up.size(1), I = I2 / 2;
+  const int El = G - (shared_group ? 1 : 0);
+  TORCH_CHECK(gate_up.size(2) == H && down.size(0) == G && down.size(1) == H && down.size(2) == I,
+              "expert shapes: gate_up [G, 2I, H], down [G, H, I]");
+  TORCH_CHECK(router.size(0) == E + (has_sg ? 1 : 0) && router.size(1) == H, "router [E (+1), H]");
+  auto opt = x.options();
+  auto iopt = opt.dtype(at::kInt);
+  auto fopt = opt.dtype(at::kFloat);
+  const int rows = T * (int)k + T;
+  auto logits = at::empty({T, router.size(0)}, fopt);
+  auto w = at::empty({T, k}, fopt);
+  auto ids = at::empty({T, k}, iopt);
+  auto sg = at::empty({T}, fopt);
+  auto counts = at::empty({G}, iopt);
+  auto offsets = at::empty({G + 1}, iopt);
+  auto pos_of = at::empty({T, k}, iopt);
+  auto pos_sh = at::empty({T}, iopt);
+  auto xp = at::empty({rows, H}, opt);
+  auto y1 = at::empty({rows, I}, opt);
+  auto y2 = at::empty({rows, H}, opt);
+  auto st = at::cuda::getCurrentCUDAStream().stream();
+  MoeRouteFusedArgs r{};
+  r.x = cbf(x);
+  r.ldx = x.stride(0);
+  r.router = cbf(router);
+  r.T = T;
+  r.H = H;
+  r.E = (int)E;
+  r.k = (int)k;
+  r.renorm = renorm;
+  r.has_sg = has_sg;
+  r.e0 = (int)e0;
+  r.E_local = El;
+  r.shared_group = shared_group;
+  r.t_lo = (int)t_lo;
+  r.t_hi = (int)t_hi;
+  r.logits = logits.data_ptr<float>();
+  r.bar = moe_barrier_for(x);
+  r.w = w.data_ptr<float>();
+  r.ids = ids.data_ptr<int>();
+  r.sg = sg.data_ptr<float>();
+  r.counts = counts.data_ptr<int>();
+  r.offsets = offsets.data_ptr<int>();
+  r.pos_of = pos_of.data_ptr<int>();
+  r.pos_sh = pos_sh.data_ptr<int>();
+  r.x_perm = mbf(xp);
+  r.status = status_dev_ptr();
+  r.limit_ns = 1000000000ull;
+  moe_route_fused(r, st);
+  const int max_rows = std::max(T, 1);
+  if (!fp8) {
+    GroupedProblem g{};
+    g.W = gate_up.data_ptr();
+    g.X = xp.data_ptr();
+    g.rows_total = rows;
+    g.counts = r.counts;
+    g.offsets = r.offsets;
+    g.groups = G;
+    g.N = I2;
+    g.K = H;
+    g.max_rows_per_group = max_rows;
+    g.swiglu = true;
+    g.swiglu_limit = (float)swiglu_limit;
+    g.out = mbf(y1);
+    g.ldo = I;
+    g.status = status_dev_ptr();
+    grouped_gemm(g, st);
+    g.W = down.data_ptr();
+    g.X = y1.data_ptr();
+    g.N = H;
+    g.K = I;
+    g.swiglu = false;
+    g.swiglu_limit = 0.f;
+    g.out = mbf(y2);
+    g.ldo = H;
+    grouped_gemm(g, st);
+  } else {
+    GroupedW8Problem g{};
+    g.W = gate_up.data_ptr<uint8_t>();
+    g.scales16 = gate_up_s16->data_ptr<float>();
+    g.X = xp.data_ptr();
+    g.rows_total = rows;
+    g.counts = r.counts;
+    g.offsets = r.offsets;
+    g.groups = G;
+    g.N = I2;
+    g.K = H;
+    g.max_rows_per_group = max_rows;
+    g.swiglu = true;
+    g.swiglu_limit = (float)swiglu_limit;
+    g.out = mbf(y1);
+    g.ldo = I;
+    g.status = status_dev_ptr();
+    grouped_gemm_w8(g, st);
+    g.W = down.data_ptr<uint8_t>();
+    g.scales16 = down_s16->data_ptr<float>();
+    g.X = y1.data_ptr();
+    g.N = H;
+    g.K = I;
+    g.swiglu = false;
+    g.swiglu_limit = 0.f;
+    g.out = mbf(y2);
+    g.ldo = H;
+    grouped_gemm_w8(g, st);
+  }
+  return {y2, w, pos_of, pos_sh, sg};
+}
+
+MoeCombineExArgs combine_args(const Tensor& y, const Tensor& w, const Tensor& pos_of,
+                              const c10::optional<Tensor>& pos_sh, const c10::optional<Tensor>& sg,
+                              const c10::optional<Tensor>& shared_y, const c10::optional<Tensor>& shared_gate) {
+  check_bf16(y, "y");
+  check_f32(w, "w");
+  TORCH_CHECK(y.is_contiguous() && w.is_contiguous() && pos_of.is_contiguous() && pos_of.scalar_type() == at::kInt,
+              "moe combine: contiguous y, w, int32 pos_of");
+  MoeCombineExArgs c{};
+  c.y = cbf(y);
+  c.w = w.data_ptr<float>();
+  c.pos_of = pos_of.data_ptr<int>();
+  c.T = (int)w.size(0);
+  c.k = (int)w.size(1);
+  c.H = (int)y.size(1);
+  if (pos_sh.has_value()) {
+    TORCH_CHECK(sg.has_value() && pos_sh->scalar_type() == at::kInt && pos_sh->numel() == c.T, "pos_sh [T] int32");
+    c.pos_sh = pos_sh->data_ptr<int>();
+    c.sg = sg->data_ptr<float>();
+  }
+  if (shared_y.has_value()) {
+    check_bf16(*shared_y, "shared_y");
+    TORCH_CHECK(shared_gate.has_value(), "shared_y needs shared_gate");
+    c.shared_y = cbf(*shared_y);
+    c.ld_shared = shared_y->stride(0);
+    c.shared_gate = shared_gate->data_ptr<float>();
+  }
+  return c;
+}
+
+// mode 0: returns the partial [T, H]; mode 1: resid += partial, returns RMSNorm(resid) * (1 + norm_w)
+Tensor moe_combine_ex_op(const Tensor& y, const Tensor& w, const Tensor& pos_of, const c10::optional<Tensor>& pos_sh,
+                         const c10::optional<Tensor>& sg, const c10::optional<Tensor>& shared_y,
+                         const c10::optional<Tensor>& shared_gate, int64_t mode, const c10::optional<Tensor>& resid,
+                         const c10::optional<Tensor>& norm_w, double eps) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  MoeCombineExArgs c = combine_args(y, w, pos_of, pos_sh, sg, shared_y, shared_gate);
+  auto out = at::empty({c.T, c.H}, y.options());
+  c.mode = (int)mode;
+  c.out = mbf(out);
+  c.ldo = out.stride(0);
+  if (mode == kCombineAddNorm) {
+    TORCH_CHECK(resid.has_value() && norm_w.has_value(), "add-norm needs resid and norm_w");
+    check_bf16(*resid, "resid");
+    check_f32(*norm_w, "norm_w");
+    TORCH_CHECK(resid->stride(1) == 1 && resid->size(0) == c.T && resid->size(1) == c.H, "resid [T, H]");
+    c.resid = mbf(*resid);
+    c.ldr = resid->stride(0);
+    c.norm_w = norm_w->data_ptr<float>();
+    c.eps = (float)eps;
+  } else {
+    TORCH_CHECK(mode == kCombinePartial, "moe_combine_ex: mode 0 or 1 (the symmetric-slot mode is moe_combine_symm)");
+  }
+  moe_combine_ex(c, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
+// ---------------------------------------------------------------------------
 // DeepSeek V4
 // ---------------------------------------------------------------------------
 std::tuple<Tensor, Tensor, Tensor> hc_pre_op(const Tensor& x, const Tensor& fn, const Tensor& scale, const Tensor& base,
@@ -643,6 +852,13 @@ void register_ext_defs(torch::Library& m) {
       "hc_pre(Tensor x, Tensor fn, Tensor scale, Tensor base, int sinkhorn_iters, float eps, float norm_eps) "
       "-> (Tensor, Tensor, Tensor)");
   m.def("hc_post(Tensor x, Tensor resid, Tensor post, Tensor comb) -> Tensor");
+  m.def(
+      "moe_decode(Tensor x, Tensor router, Tensor gate_up, Tensor down, Tensor? gate_up_scales16, "
+      "Tensor? down_scales16, int e0, int E, int k, bool renorm, bool has_sg, bool shared_group, int t_lo, int t_hi, "
+      "float swiglu_limit) -> Tensor[]");
+  m.def(
+      "moe_combine_ex(Tensor y, Tensor w, Tensor pos_of, Tensor? pos_sh, Tensor? sg, Tensor? shared_y, "
+      "Tensor? shared_gate, int mode, Tensor(a!)? resid, Tensor? norm_w, float eps) -> Tensor");
   m.def("mqa_attn(Tensor q, Tensor kv, Tensor visible, int q_per_seq, float scale, int splits) -> Tensor");
   m.def(
       "deltanet_prefill(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) conv_ring, Tensor(b!) state, int start, "
@@ -662,6 +878,8 @@ void register_ext_impls(torch::Library& m) {
   m.impl("moe_combine", &moe_combine_op);
   m.impl("hc_pre", &hc_pre_op);
   m.impl("hc_post", &hc_post_op);
+  m.impl("moe_decode", &moe_decode_op);
+  m.impl("moe_combine_ex", &moe_combine_ex_op);
   m.impl("mqa_attn", &mqa_attn_op);
   m.impl("rope_interleaved_", &rope_interleaved_op);
   m.impl("deltanet_prefill", &deltanet_prefill_op);

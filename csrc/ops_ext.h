@@ -20,6 +20,12 @@ struct Scratch {
 };
 Scratch& scratch_for(const at::Tensor& like, long floats, long tickets);
 
+// MoE combine arguments shared by ops_ext.cpp and ops_comm.cpp (ops_ext.cpp)
+struct MoeCombineExArgs;
+MoeCombineExArgs combine_args(const at::Tensor& y, const at::Tensor& w, const at::Tensor& pos_of,
+                              const c10::optional<at::Tensor>& pos_sh, const c10::optional<at::Tensor>& sg,
+                              const c10::optional<at::Tensor>& shared_y, const c10::optional<at::Tensor>& shared_gate);
+
 // shared validation helpers (defined in ops.cpp)
 void check_cuda(const at::Tensor& t, const char* name);
 void check_bf16(const at::Tensor& t, const char* name);
