@@ -7,6 +7,10 @@ MoE blocks (route, gather, two grouped GEMMs, combine: five launches).
     python bench/kernel_case.py --op gqa --B 32 --QH 24 --KVH 4 --ctx 2048
     python bench/kernel_case.py --op deltanet --B 32 --KH 16 --VH 48
     python bench/kernel_case.py --op moe_w8 --T 32 --E 256 --k 8 --H 2048 --I 512
+    # model-level cases (a few full-width layers): pick the kernel with ncu -k
+    python bench/kernel_case.py --op prefill --model 35b --layers 4 --B 2 --ctx 2048   # flash / chunked DeltaNet
+    python bench/kernel_case.py --op decode --model 35b --layers 4 --B 32             # fused MoE decode kernels
+    python bench/kernel_case.py --op deepseek --layers 2 --B 1 --ctx 1024             # HC mixing, MQA attention
 """
 import argparse
 import os
@@ -22,7 +26,11 @@ from bwn.ops import reference as R  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", required=True, choices=["linear", "linear_w8", "swiglu", "gqa", "deltanet", "moe", "moe_w8"])
+    ap.add_argument("--op", required=True, choices=["linear", "linear_w8", "swiglu", "gqa", "deltanet", "moe", "moe_w8",
+                                                    "prefill", "decode", "deepseek"])
+    ap.add_argument("--model", default="35b", choices=["27b", "35b"])
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--fp8-experts", action="store_true")
     ap.add_argument("--M", type=int, default=32)
     ap.add_argument("--N", type=int, default=5120)
     ap.add_argument("--K", type=int, default=6144)
@@ -79,6 +87,44 @@ def main():
         pos = torch.full((a.B,), a.ctx, dtype=torch.int32, device=dev)
         fn = lambda: O.gqa_decode(qg, kv[:, 0], kv[:, 1], qn, qn, cos, sin, kc, vc, pos)  # noqa: E731
         nbytes = a.B * a.KVH * (a.ctx + 1) * D * 2 * 2
+    elif a.op in ("prefill", "decode"):
+        from bwn.config import QWEN36_27B, QWEN36_35B_A3B
+        from bwn.models.qwen36 import Qwen36Model
+        cfg = (QWEN36_27B if a.model == "27b" else QWEN36_35B_A3B).scaled(num_layers=a.layers)
+        m = Qwen36Model(cfg, None, torch.device(dev)).init_random(0)
+        if a.fp8_experts:
+            m.quantize_fp8(include_head=False, experts=True, dense=False)
+        g = torch.Generator().manual_seed(0)
+        if a.op == "prefill":
+            prompt = torch.randint(0, cfg.vocab, (a.B, a.ctx), generator=g).to(dev)
+            st = m.new_state(a.B, a.ctx + 64)
+
+            def fn():
+                st.reset()
+                m.prefill(prompt, st)
+            nbytes = m.weight_bytes()
+        else:
+            st = m.new_state(a.B, a.ctx + 64 + 64)
+            st.k_cache.normal_()
+            st.v_cache.normal_()
+            st.ssm.normal_(0, 0.05)
+            tok = torch.randint(0, cfg.vocab, (a.B,), generator=g).int().to(dev)
+
+            def fn():
+                st.positions.fill_(a.ctx)
+                m.decode_step(tok, st)
+            nbytes = m.weight_bytes()
+    elif a.op == "deepseek":
+        from bwn.config import DeepSeekV4Config
+        from bwn.models.deepseek_v4 import DeepSeekV4Model
+        cfg = DeepSeekV4Config().scaled(num_layers=a.layers, max_seq_len=a.ctx + 64)
+        m = DeepSeekV4Model(cfg, None, torch.device(dev)).init_random_local(0)
+        prompt = torch.randint(0, cfg.vocab, (a.B, a.ctx), generator=torch.Generator().manual_seed(0)).to(dev)
+
+        def fn():
+            st = m.new_state(a.B, a.ctx + 64)
+            m.prefill(prompt, st)
+        nbytes = 1
     else:
         C = 2 * a.KH * 128 + a.VH * 128
         fused = torch.randn(a.B, C + a.VH * 128 + 2 * a.VH, device=dev).bfloat16()

@@ -329,6 +329,10 @@ class Qwen36Model(nn.Module):
             return o.moe_combine_ex(y, w, pos_of, pos_sh, sg, shared_y, shared_gate, 1, x, nxt, cfg.rms_eps)
         fc = self.fused_comm
         if fc is not None and fc.fits(T):
+            if fc.one_kernel:  # combine, NVLS reduction, residual add and RMSNorm in one launch
+                return o.moe_combine_symm_norm(y, w, pos_of, pos_sh, sg, shared_y, shared_gate, fc.local_ar, fc.mc_ar,
+                                               fc.buf_elems, fc.peer_flags_ar, fc.peer_flags_ar[fc.rank], fc.state,
+                                               fc.rank, x, nxt, cfg.rms_eps, fc.timeout_s)
             o.moe_combine_symm(y, w, pos_of, pos_sh, sg, shared_y, shared_gate, fc.local_ar, fc.buf_elems,
                                fc.peer_flags_ar, fc.state, fc.rank)
             return fc.reduce_add_norm(x, nxt, cfg.rms_eps)
@@ -336,14 +340,16 @@ class Qwen36Model(nn.Module):
         self.comm.all_reduce_(part)
         return O.add_rms_norm(part, x, nxt, cfg.rms_eps)
 
-    def decode_hidden(self, tokens: torch.Tensor, st: Qwen36State) -> torch.Tensor:
+    def decode_hidden(self, tokens: torch.Tensor, st: Qwen36State, num_layers: int | None = None) -> torch.Tensor:
         """One decode step for ``tokens [B]`` at ``st.positions``; advances the
-        positions and returns the final-normed hidden ``[B, H]``."""
+        positions and returns the final-normed hidden ``[B, H]``.  ``num_layers``
+        (checks only) stops after that many layers and returns the hidden as
+        normed for the next layer."""
         cfg = self.cfg
         x = self.embed(tokens)  # residual stream [B, H]
         h = O.rms_norm(x, self.layers[0]["in_norm"], cfg.rms_eps)
         di = gi = 0
-        for i in range(cfg.num_layers):
+        for i in range(cfg.num_layers if num_layers is None else num_layers):
             L = self.layers[i]
             if cfg.layer_type(i) == "deltanet":
                 o = self._deltanet_decode(i, h, st, di)

@@ -8,12 +8,14 @@
 // bf16 token rows are "B", the store is transposed.  Per 128-deep K block:
 //   warp 0      TMA: fp8 weight tile [128 x 128 B] (SW128) + bf16 token tile
 //   warps 6-13  converters: the fp8 weight tile to f16 with the hardware
-//               e4m3x2 -> f16x2 conversion (exact for every e4m3 value), and
-//               the bf16 token tile to f16 scaled by this tile's 128x128 block
-//               scale (W x^T = w8 (s x)^T: each CTA owns one scale block row),
-//               both written in the SW128 K-major layout the MMA reads, then
-//               fence.proxy.async
-//   warp 1      tcgen05.mma kind::f16 (f16 x f16 -> fp32 TMEM), 8 per block
+//               e4m3x2 -> f16x2 conversion (exact for every e4m3 value),
+//               stored straight into tensor memory (two warps per TMEM lane
+//               quadrant, one K half each), and the bf16 token tile to f16
+//               scaled by this tile's 128x128 block scale (W x^T = w8 (s x)^T:
+//               each CTA owns one scale block row) in the SW128 K-major layout
+//               the MMA reads from shared memory
+//   warp 1      tcgen05.mma kind::f16 (f16 x f16 -> fp32 TMEM) with A read
+//               from tensor memory, 8 per block
 //   warps 2-5   epilogue (shared with the bf16 GEMM: bf16 / residual /
 //               SwiGLU / fp32 / NVLS multimem reduction)
 // Split-K and the completion signalling are the same as the bf16 GEMM.
@@ -31,20 +33,20 @@ namespace bwn {
 constexpr int kW8BM = 128;
 constexpr int kW8BK = 128;  // fp8 elements (bytes) per row per stage
 constexpr int kW8Threads = 448;
+constexpr int kW8SlotCol0 = 256;  // TMEM columns [0, 256): the two accumulators
 
 template <int BN>
 struct W8Cfg {
   static constexpr int kA8 = kW8BM * kW8BK;        // 16 KB fp8 weight tile
-  static constexpr int kA16 = kW8BM * kW8BK * 2;   // 32 KB f16 weight tile (two SW128 boxes)
   static constexpr int kB = BN * kW8BK * 2;        // token tile (two SW128 boxes), bf16 in / f16 out
   static constexpr int kL = kA8 + kB;              // TMA ring stage
-  static constexpr int kC = kA16 + kB;             // converted ring stage
-  static constexpr int kNC = (BN <= 32) ? 4 : 2;
-  static constexpr int kNLRaw = (216 * 1024 - kNC * kC) / kL;
+  static constexpr int kSlots = BN <= 64 ? 4 : 2;  // converted stages: A in TMEM (64 columns), B in smem
+  static constexpr int kNLRaw = (208 * 1024 - kSlots * kB) / kL;
   static constexpr int kNL = kNLRaw > 8 ? 8 : kNLRaw;
-  static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
   static constexpr int kMaxKb = 512;  // scales staged per unit
-  static constexpr int kSmem = kNL * kL + kNC * kC + 1024 + 512 + kMaxKb * 4;
+  static constexpr int kSmem = kNL * kL + kSlots * kB + 1024 + 512 + kMaxKb * 4;
+  static_assert(kNL >= 2, "gemm_w8: shared memory ring does not fit");
+  static_assert(2 * BN <= kW8SlotCol0, "gemm_w8: accumulators overlap the A slots");
 };
 
 // four e4m3 bytes -> two f16x2 words (bytes 0,1 -> lo; bytes 2,3 -> hi), exactly
@@ -62,20 +64,19 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     gemm_w8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args,
                    const float* __restrict__ scales, int lds) {
   using C = W8Cfg<BN>;
-  constexpr int S = C::kNL;   // TMA ring depth
-  constexpr int SC = C::kNC;  // converted ring depth
+  constexpr int S = C::kNL;      // TMA ring depth
+  constexpr int SL = C::kSlots;  // converted stages
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sA8 = smem;                    // [S][kA8]
   uint8_t* sB = sA8 + S * C::kA8;         // [S][kB]   bf16 tokens
-  uint8_t* sA16 = sB + S * C::kB;         // [SC][kA16] f16 weights
-  uint8_t* sB16 = sA16 + SC * C::kA16;    // [SC][kB]   f16 tokens * scale
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB16 + SC * C::kB);  // [S]  TMA landed
+  uint8_t* sB16 = sB + S * C::kB;         // [SL][kB]  f16 tokens * scale
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB16 + SL * C::kB);  // [S]  TMA landed
   uint64_t* lempty_bar = full_bar + S;    // [S]  converters done reading
-  uint64_t* cvt_bar = lempty_bar + S;     // [SC] converted slot ready
-  uint64_t* empty_bar = cvt_bar + SC;     // [SC] MMA done with the slot
-  uint64_t* tfull_bar = empty_bar + SC;
+  uint64_t* cvt_bar = lempty_bar + S;     // [SL] converted stage ready (A in TMEM, B in smem)
+  uint64_t* empty_bar = cvt_bar + SL;     // [SL] MMA done with the stage
+  uint64_t* tfull_bar = empty_bar + SL;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       mbar_init(&full_bar[i], 1);
       mbar_init(&lempty_bar[i], 256);
     }
-    for (int i = 0; i < SC; ++i) {
+    for (int i = 0; i < SL; ++i) {
       mbar_init(&cvt_bar[i], 256);
       mbar_init(&empty_bar[i], 1);
     }
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   pdl_trigger();
@@ -146,9 +147,15 @@ __global__ void __launch_bounds__(kW8Threads, 1)
     }
   } else if (warp >= 6) {
     // ------------------------------ converters ------------------------------
+    // two warps per TMEM lane quadrant (one K half each): the thread of weight
+    // row r turns its 64 fp8 bytes into f16 (exact) and stores them into its
+    // own TMEM lane of the stage's A slot; all 256 threads scale the token tile
+    // by the block scale into f16 in the SW128 layout the MMA reads as B
     const int c = threadIdx.x - 6 * 32;  // 0..255
-    const int r = c >> 1, half = c & 1;
-    int s = 0, sc2 = 0;
+    const int q = warp & 3, half = (warp - 6) >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    int s = 0, sl = 0;
     uint32_t ph = 0, ph2 = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       // all 256 converter threads leave together after an abort (the named
@@ -162,31 +169,27 @@ __global__ void __launch_bounds__(kW8Threads, 1)
       for (int j = c; j < kb1 - kb0; j += 256) s_scale[j] = scales[(long)tm * lds + kb0 + j];
       asm volatile("bar.sync 2, 256;" ::: "memory");
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (*abort_flag || !mbar_wait(&full_bar[s], ph) || !mbar_wait(&empty_bar[sc2], ph2 ^ 1)) {
+        if (*abort_flag || !mbar_wait(&full_bar[s], ph) || !mbar_wait(&empty_bar[sl], ph2 ^ 1)) {
           set_status(args.status, kStatusMbarTimeout);
           *abort_flag = 1;
           break;
         }
         const float sc = s_scale[kb - kb0];
         const uint8_t* a8 = sA8 + s * C::kA8 + r * 128;
-        uint8_t* a16 = sA16 + sc2 * C::kA16;
+        uint32_t o[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int cc = half * 4 + q;  // 16-byte fp8 chunk = 16 k
+        for (int qq = 0; qq < 4; ++qq) {
+          const int cc = half * 4 + qq;  // 16-byte fp8 chunk = 16 k
           const uint4 raw8 = *reinterpret_cast<const uint4*>(a8 + ((cc ^ (r & 7)) << 4));
           const uint32_t w[4] = {raw8.x, raw8.y, raw8.z, raw8.w};
-          uint32_t o[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) e4m3x4_to_f16x4(w[j], o[2 * j], o[2 * j + 1]);
-          // k = 16*cc .. 16*cc+15 -> f16 box t = cc/4, 16-byte chunks c8 and c8+1
-          const int t = cc >> 2, c8 = (cc & 3) * 2;
-          uint8_t* rowp = a16 + t * (kW8BM * 128) + r * 128;
-          *reinterpret_cast<uint4*>(rowp + ((c8 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(rowp + (((c8 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          for (int j = 0; j < 4; ++j) e4m3x4_to_f16x4(w[j], o[qq * 8 + 2 * j], o[qq * 8 + 2 * j + 1]);
         }
+        // column c of the slot holds k = 2c, 2c+1 of this row
+        tmem_st32u(tmem_base + lane_addr + kW8SlotCol0 + sl * 64 + half * 32, o);
         {  // token tile: bf16 -> f16 * block scale, same swizzled positions
           const uint32_t* b32 = reinterpret_cast<const uint32_t*>(sB + s * C::kB);
-          uint32_t* o32 = reinterpret_cast<uint32_t*>(sB16 + sc2 * C::kB);
+          uint32_t* o32 = reinterpret_cast<uint32_t*>(sB16 + sl * C::kB);
           for (int i = c; i < C::kB / 4; i += 256) {
             const uint32_t v = b32[i];
             const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
@@ -195,21 +198,22 @@ __global__ void __launch_bounds__(kW8Threads, 1)
           }
         }
         fence_async_smem();
-        mbar_arrive(&cvt_bar[sc2]);
+        tc_fence_before();
+        mbar_arrive(&cvt_bar[sl]);
         mbar_arrive(&lempty_bar[s]);
         if (++s == S) {
           s = 0;
           ph ^= 1;
         }
-        if (++sc2 == SC) {
-          sc2 = 0;
+        if (++sl == SL) {
+          sl = 0;
           ph2 ^= 1;
         }
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      // kind::f16 with A = B = f16 (format 0), D = f32
+      // kind::f16 with A = B = f16 (format 0), D = f32; A read from TMEM
       const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kW8BM >> 4) << 24);
       int s = 0, i = 0;
       uint32_t ph = 0;
@@ -231,16 +235,16 @@ __global__ void __launch_bounds__(kW8Threads, 1)
             break;
           }
           tc_fence_after();
+          const uint32_t at = tmem_base + kW8SlotCol0 + s * 64;
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            const uint64_t da = smem_desc_sw128(smem_u32(sA16 + s * C::kA16 + t * (kW8BM * 128)));
             const uint64_t db = smem_desc_sw128(smem_u32(sB16 + s * C::kB + t * (BN * 128)));
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (kb > kb0 || t > 0 || kk > 0) ? 1u : 0u);
+              umma_f16_ts(d, at + t * 32 + kk * 8, db + 2 * kk, idesc, (kb > kb0 || t > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);
-          if (++s == SC) {
+          if (++s == SL) {
             s = 0;
             ph ^= 1;
           }
@@ -345,7 +349,7 @@ __global__ void __launch_bounds__(kW8Threads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    tmem_dealloc(tmem_base, 512);
   }
 }
 

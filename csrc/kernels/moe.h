@@ -123,11 +123,12 @@ struct MoeRouteFusedArgs {
 void moe_route_fused(const MoeRouteFusedArgs& a, cudaStream_t st);
 int moe_route_fused_grid(int T, int E, bool has_sg);
 
-enum { kCombinePartial = 0, kCombineAddNorm = 1, kCombineSymm = 2 };
+enum { kCombinePartial = 0, kCombineAddNorm = 1, kCombineSymm = 2, kCombineSymmNorm = 3 };
 // Per token: sum_slot w * y[pos_of] + sigmoid(sg) * y[pos_sh] (+ sigmoid(shared_gate)
 // * shared_y), fp32, rounded to bf16 once; then stored (partial), added to the
 // residual and RMSNorm(1+w)'d (add-norm), or stored into this rank's symmetric
-// slot with the completion flag published (symm).
+// slot with the completion flag published (symm), or that followed, in the same
+// launch, by the NVLS sum over ranks + residual add + RMSNorm (symm-norm).
 struct MoeCombineExArgs {
   const __nv_bfloat16* y;  // [rows, H] expert outputs, packed
   const float* w;          // [T, k]
@@ -147,6 +148,13 @@ struct MoeCombineExArgs {
   float eps;
   __nv_bfloat16* symm_base;  // symm: this rank's slot base
   CommSignal sig;
+  // symm-norm: the reduction tail (multicast base of the slots, this rank's
+  // flag array, mutable selector [2], status word, wait bound)
+  const __nv_bfloat16* mc_base;
+  const unsigned* flags;
+  int* sel_rw;
+  int* status;
+  unsigned long long limit_ns;
 };
 void moe_combine_ex(const MoeCombineExArgs& a, cudaStream_t st);
 

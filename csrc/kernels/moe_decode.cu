@@ -264,7 +264,9 @@ __global__ void __launch_bounds__(256) moe_combine_ex_kernel(MoeCombineExArgs a)
   __syncthreads();
   const float gsep = a.shared_y ? sigmoid_f(a.shared_gate[t]) : 0.f;
   const int nvec = a.H >> 3;
-  __nv_bfloat16* slot = a.mode == kCombineSymm ? a.symm_base + (long)((*a.sig.sel) & 1) * a.sig.buf_stride : nullptr;
+  const bool to_slot = a.mode == kCombineSymm || a.mode == kCombineSymmNorm;
+  const int sel = to_slot ? ((*a.sig.sel) & 1) : 0;
+  __nv_bfloat16* slot = to_slot ? a.symm_base + (long)sel * a.sig.buf_stride : nullptr;
   float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(256) moe_combine_ex_kernel(MoeCombineExArgs a)
     for (int e = 0; e < 8; ++e) pb[e] = __float2bfloat16(acc[e]);
     if (a.mode == kCombinePartial) {
       reinterpret_cast<uint4*>(a.out + (long)t * a.ldo)[vi] = *reinterpret_cast<uint4*>(pb);
-    } else if (a.mode == kCombineSymm) {
+    } else if (to_slot) {
       reinterpret_cast<uint4*>(slot + (long)t * a.H)[vi] = *reinterpret_cast<uint4*>(pb);
     } else {  // residual add (bf16, as the unfused add_rms_norm) then RMSNorm(1+w)
       const uint4 rr = reinterpret_cast<const uint4*>(a.resid + (long)t * a.ldr)[vi];
@@ -310,12 +312,57 @@ __global__ void __launch_bounds__(256) moe_combine_ex_kernel(MoeCombineExArgs a)
       reinterpret_cast<uint4*>(a.resid + (long)t * a.ldr)[vi] = *reinterpret_cast<uint4*>(nr);
     }
   }
-  if (a.mode == kCombineSymm) {
+  if (to_slot) {
+    __shared__ unsigned s_epoch;
     __syncthreads();  // the CTA's slot stores precede thread 0's system-scope fence
-    if (threadIdx.x == 0) signal_done(a.sig);
+    if (threadIdx.x == 0) {
+      s_epoch = (unsigned)(*a.sig.epoch) + 1u;  // the epoch this launch publishes (read before the ticket)
+      signal_done(a.sig);
+    }
+    if (a.mode == kCombineSymm) return;
+    // ---- symm-norm: wait for every rank, then this token's row of the sum ----
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) s_ok = 1;
+    __syncthreads();
+    if ((int)threadIdx.x < a.sig.world) {
+      const uint64_t t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while ((int)(ld_acquire_sys(a.flags + threadIdx.x) - s_epoch) < 0) {
+        if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > a.limit_ns) {
+          set_status(a.status, kStatusPeerTimeout);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    if (s_ok) {  // a peer that never signalled: nothing is read or written
+      const __nv_bfloat16* buf = a.mc_base + (long)sel * a.sig.buf_stride + (long)t * a.H;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = threadIdx.x + i * blockDim.x;
+        if (vi < nvec) mc_ld_reduce_bf16x8(buf + vi * 8, v[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = threadIdx.x + i * blockDim.x;
+        if (vi >= nvec) continue;
+        const uint4 rr = reinterpret_cast<const uint4*>(a.resid + (long)t * a.ldr)[vi];
+        const __nv_bfloat16* rh = reinterpret_cast<const __nv_bfloat16*>(&rr);
+        alignas(16) __nv_bfloat16 nr[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {  // the reduced partial rounded to bf16, as the unfused all-reduce output
+          const float pr = __bfloat162float(__float2bfloat16(v[i][e]));
+          nr[e] = __float2bfloat16(pr + __bfloat162float(rh[e]));
+          v[i][e] = __bfloat162float(nr[e]);
+          ss += v[i][e] * v[i][e];
+        }
+        reinterpret_cast<uint4*>(a.resid + (long)t * a.ldr)[vi] = *reinterpret_cast<uint4*>(nr);
+      }
+    }
+  } else if (a.mode != kCombineAddNorm) {
     return;
   }
-  if (a.mode != kCombineAddNorm) return;
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -333,6 +380,17 @@ __global__ void __launch_bounds__(256) moe_combine_ex_kernel(MoeCombineExArgs a)
 #pragma unroll
     for (int e = 0; e < 8; ++e) o[e] = __float2bfloat16(v[i][e] * inv * (1.f + ww[e]));
     reinterpret_cast<uint4*>(a.out + (long)t * a.ldo)[vi] = *reinterpret_cast<uint4*>(o);
+  }
+  if (a.mode == kCombineSymmNorm) {  // flip the slot selector once every CTA has read it
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const int tk = atomicAdd(a.sel_rw + 1, 1);
+      if (tk == (int)gridDim.x - 1) {
+        a.sel_rw[1] = 0;
+        a.sel_rw[0] = a.sel_rw[0] + 1;
+      }
+    }
   }
 }
 
@@ -355,7 +413,10 @@ void moe_combine_ex(const MoeCombineExArgs& a, cudaStream_t st) {
   if (a.T == 0) return;
   BWN_CHECK(a.H % 8 == 0 && a.k <= kRtMaxK, "moe_combine_ex: H multiple of 8, k <= 16");
   BWN_CHECK(a.mode != kCombinePartial || a.ldo % 8 == 0, "moe_combine_ex: 16-byte aligned output rows");
-  BWN_CHECK(a.mode != kCombineAddNorm || (a.ldr % 8 == 0 && a.ldo % 8 == 0), "moe_combine_ex: aligned rows");
+  BWN_CHECK((a.mode != kCombineAddNorm && a.mode != kCombineSymmNorm) || (a.ldr % 8 == 0 && a.ldo % 8 == 0),
+            "moe_combine_ex: aligned rows");
+  BWN_CHECK(a.mode != kCombineSymmNorm || (a.mc_base && a.flags && a.sel_rw && a.resid && a.norm_w && a.out),
+            "moe_combine_ex: symm-norm needs the reduction tail");
   BWN_CHECK(!a.shared_y || a.ld_shared % 8 == 0, "moe_combine_ex: aligned shared rows");
   const int vpt = (a.H / 8 + 255) / 256;
   switch (vpt) {

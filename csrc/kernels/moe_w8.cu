@@ -1,23 +1,18 @@
 // Grouped expert GEMM with block-scaled E4M3FN weights for sm_100a: the
 // reference's fused all-expert W8 MoE and FP8 grouped matvec
 // (contrib/qwen3.6-35b-a3b/kernels/moe_fused_w8_35b.py:345-940,
-// kernels/fp8_group_matvec.py:47-105) on the tensor cores.
+// kernels/fp8_group_matvec.py:47-105) on the tensor cores, with bf16
+// activations (W8A16).
 //
 // Same schedule as the bf16 grouped GEMM (csrc/kernels/moe.cu): swap-AB, one
 // work unit = (expert e, 128 weight rows, BN token rows of e), units compacted
 // over the device row counts so one launch shape serves every routing.  The
-// weight stays fp8 in HBM (half the bytes of bf16); per 128-deep K block:
-//   warp 0      TMA: fp8 weight tile [128 rows x 128 B] + bf16 token tile
-//               (two 64-column SW128 boxes)
-//   warps 6-13  converters: fp8 -> bf16 with the hardware e4m3x2 -> f16x2
-//               conversion (exact), times the row group's block scale in fp32,
-//               rounded to bf16 (the same rounding as dequantizing at load),
-//               written in the SW128 K-major layout the MMA reads; the token
-//               tile is copied unchanged; then fence.proxy.async
-//   warp 1      tcgen05.mma kind::f16, bf16 x bf16 -> fp32 TMEM, 8 per block
-//   warps 2-5   epilogue: bf16 rows, or SwiGLU over the 16-row gate/up
-//               interleave (optionally clamped, DeepSeek's swiglu_limit)
-// Scales are kept per 16 weight rows (scales16, see moe.h) so the gate/up
+// weight stays fp8 in HBM (half the bytes of bf16).  Converter warps turn each
+// fp8 tile into bf16 (hardware e4m3x2 -> f16x2, exact; times the row group's
+// block scale in fp32; rounded to bf16, the same rounding as dequantizing at
+// load) and store it straight into tensor memory, where tcgen05.mma reads its
+// A operand; the token tile is the B operand in shared memory as TMA loaded
+// it.  Scales are kept per 16 weight rows (scales16, see moe.h) so the gate/up
 // interleave of a 128-row tile needs no re-quantization.
 #include <cuda_fp16.h>
 
@@ -33,22 +28,22 @@ namespace {
 
 constexpr int kXBM = 128;    // weight rows per tile
 constexpr int kXBK = 128;    // fp8 columns (bytes) per K block
-constexpr int kXThreads = 448;
-constexpr int kXMaxScales = 1024;  // 8 row groups x K blocks staged per unit
+constexpr int kXCvtWarps = 8;                    // two per TMEM lane quadrant
+constexpr int kXThreads = (6 + kXCvtWarps) * 32;
+constexpr int kXSlots = 4;                       // converted A tiles in TMEM, 64 columns each
+constexpr int kXSlotCol0 = 256;                  // TMEM columns [0, 256): the two accumulators
+constexpr int kXMaxScales = 1024;                // 8 row groups x K blocks staged per unit
 
 template <int BN>
 struct XCfg {
   static constexpr int kA8 = kXBM * kXBK;       // 16 KB fp8 weight tile
-  static constexpr int kA16 = kXBM * kXBK * 2;  // 32 KB bf16 weight tile (two SW128 boxes)
   static constexpr int kB = BN * kXBK * 2;      // bf16 token tile (two SW128 boxes)
   static constexpr int kL = kA8 + kB;           // TMA ring stage
-  static constexpr int kC = kA16 + kB;          // converted ring stage
-  static constexpr int kNC = (BN <= 32) ? 4 : 2;
-  static constexpr int kNLRaw = (216 * 1024 - kNC * kC) / kL;
+  static constexpr int kNLRaw = (208 * 1024) / kL;
   static constexpr int kNL = kNLRaw > 8 ? 8 : kNLRaw;
-  static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
-  static constexpr int kSmem = kNL * kL + kNC * kC + 1024 + 512 + kXMaxScales * 4;
-  static_assert(kNL >= 1, "fp8 grouped GEMM: shared memory ring does not fit");
+  static constexpr int kSmem = kNL * kL + 1024 + 512 + kXMaxScales * 4;
+  static_assert(kNL >= 2, "fp8 grouped GEMM: shared memory ring does not fit");
+  static_assert(2 * BN <= kXSlotCol0, "fp8 grouped GEMM: accumulators overlap the A slots");
 };
 
 struct GroupedW8Args {
@@ -74,26 +69,38 @@ __device__ __forceinline__ uint32_t scale_to_bf16x2(uint32_t h2, float s) {
   return *reinterpret_cast<const uint32_t*>(&b);
 }
 
+// Pipeline per 128-deep K block j of a unit (TMA stage s = j mod kNL, TMEM
+// slot t = j mod kXSlots):
+//   warp 0      TMA: fp8 weight tile [128 rows x 128 B] + bf16 token tile into
+//               stage s (full_bar[s]), after the MMAs of the stage's last use
+//               retired (empty_bar[s])
+//   warps 6-13  converters, two per TMEM lane quadrant (one K half each): the
+//               thread of weight row r converts its 64 fp8 bytes to bf16 times
+//               the row group's block scale and stores them into its own TMEM
+//               lane of slot t (tcgen05.st), then arrives on cvt_full[t]
+//   warp 1      tcgen05.mma with A read from TMEM slot t and the token tile from
+//               stage s (8 MMAs of K 16), then commits empty_bar[s] and
+//               cvt_empty[t]; after a unit's last block, the accumulator barrier
+//   warps 2-5   epilogue from the double-buffered TMEM accumulator
+// The converted weights never touch shared memory: per block the SM's shared
+// memory carries the fp8 tile in and out once and the token tile.
 template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(kXThreads, 1)
     grouped_gemm_w8_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                            GroupedW8Args xa) {
   using C = XCfg<BN>;
-  constexpr int S = C::kNL;   // TMA ring depth
-  constexpr int SC = C::kNC;  // converted ring depth
+  constexpr int S = C::kNL;
   const GroupedArgs& a = xa.g;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sA8 = smem;                   // [S][kA8]
   uint8_t* sB = sA8 + S * C::kA8;        // [S][kB]  bf16 tokens as loaded
-  uint8_t* sA16 = sB + S * C::kB;        // [SC][kA16] bf16 weights
-  uint8_t* sB16 = sA16 + SC * C::kA16;   // [SC][kB]   bf16 tokens
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB16 + SC * C::kB);  // [S]  TMA landed
-  uint64_t* lempty_bar = full_bar + S;   // [S]  converters done reading
-  uint64_t* cvt_bar = lempty_bar + S;    // [SC] converted slot ready
-  uint64_t* empty_bar = cvt_bar + SC;    // [SC] MMA done with the slot
-  uint64_t* tfull_bar = empty_bar + SC;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + S * C::kB);  // [S]  TMA landed
+  uint64_t* empty_bar = full_bar + S;    // [S]  MMAs done with the stage
+  uint64_t* cvt_full = empty_bar + S;    // [kXSlots] converted slot written
+  uint64_t* cvt_empty = cvt_full + kXSlots;  // [kXSlots] MMAs done with the slot
+  uint64_t* tfull_bar = cvt_empty + kXSlots;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -103,11 +110,11 @@ __global__ void __launch_bounds__(kXThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&full_bar[i], 1);
-      mbar_init(&lempty_bar[i], 256);
-    }
-    for (int i = 0; i < SC; ++i) {
-      mbar_init(&cvt_bar[i], 256);
       mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < kXSlots; ++i) {
+      mbar_init(&cvt_full[i], kXCvtWarps * 32);
+      mbar_init(&cvt_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
@@ -119,7 +126,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
     tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   // the row counts and packed rows come from the previous kernel (PDL)
@@ -142,7 +149,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
         int e, tm, tn, n0, nr;
         if (!gunit(a, gu, u, e, tm, tn, n0, nr, BN)) continue;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&lempty_bar[s], ph ^ 1)) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1)) {
             set_status(a.status, kStatusMbarTimeout);
             *abort_flag = 1;
             break;
@@ -165,71 +172,64 @@ __global__ void __launch_bounds__(kXThreads, 1)
     }
   } else if (warp >= 6) {
     // ------------------------------ converters ------------------------------
-    const int c = threadIdx.x - 6 * 32;  // 0..255
-    const int r = c >> 1, half = c & 1;  // weight row, which 64-byte half of its 128 bytes
-    int s = 0, sc2 = 0;
-    uint32_t ph = 0, ph2 = 0;
+    const int c = threadIdx.x - 6 * 32;       // 0..255
+    const int q = warp & 3;                   // TMEM lane quadrant this warp may access
+    const int half = (warp - 6) >> 2;         // which 64 of the block's 128 K columns
+    const int r = q * 32 + lane;              // weight row == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    int s = 0, t = 0;
+    uint32_t ph = 0, pht = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      // all 256 converter threads leave together after an abort (the named
+      // all converter threads leave together after an abort (the named
       // barriers below need every one of them)
-      if (bar_any(2, 256, *abort_flag != 0)) break;
+      if (bar_any(2, kXCvtWarps * 32, *abort_flag != 0)) break;
       int e, tm, tn, n0, nr;
       if (!gunit(a, gu, u, e, tm, tn, n0, nr, BN)) continue;
       // this unit's scales: 8 consecutive row groups x nkb blocks, contiguous
       const float* src = xa.scales16 + ((long)e * (a.N >> 4) + (long)tm * 8) * nkb;
-      for (int j = c; j < 8 * nkb; j += 256) s_scale[j] = src[j];
-      asm volatile("bar.sync 2, 256;" ::: "memory");
+      for (int j = c; j < 8 * nkb; j += kXCvtWarps * 32) s_scale[j] = src[j];
+      asm volatile("bar.sync 2, %0;" ::"n"(kXCvtWarps * 32) : "memory");
       for (int kb = 0; kb < nkb; ++kb) {
-        if (*abort_flag || !mbar_wait(&full_bar[s], ph) || !mbar_wait(&empty_bar[sc2], ph2 ^ 1)) {
+        if (*abort_flag || !mbar_wait(&full_bar[s], ph) || !mbar_wait(&cvt_empty[t], pht ^ 1)) {
           set_status(a.status, kStatusMbarTimeout);
           *abort_flag = 1;
           break;
         }
         const float sc = s_scale[(r >> 4) * nkb + kb];
         const uint8_t* a8 = sA8 + s * C::kA8 + r * 128;
-        uint8_t* a16 = sA16 + sc2 * C::kA16;
+        uint32_t o[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int cc = half * 4 + q;  // 16-byte fp8 chunk = 16 k
+        for (int qq = 0; qq < 4; ++qq) {
+          const int cc = half * 4 + qq;  // 16-byte fp8 chunk = 16 k
           const uint4 raw8 = *reinterpret_cast<const uint4*>(a8 + ((cc ^ (r & 7)) << 4));
           const uint32_t w[4] = {raw8.x, raw8.y, raw8.z, raw8.w};
-          uint32_t o[8];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             uint32_t lo, hi;
             e4m3x4_to_f16x4_g(w[j], lo, hi);
-            o[2 * j] = scale_to_bf16x2(lo, sc);
-            o[2 * j + 1] = scale_to_bf16x2(hi, sc);
+            o[qq * 8 + 2 * j] = scale_to_bf16x2(lo, sc);      // k = 16 cc + 4 j, +1
+            o[qq * 8 + 2 * j + 1] = scale_to_bf16x2(hi, sc);  // k = 16 cc + 4 j + 2, +3
           }
-          // k = 16*cc .. 16*cc+15 -> bf16 box t = cc/4, 16-byte chunks c8 and c8+1
-          const int t = cc >> 2, c8 = (cc & 3) * 2;
-          uint8_t* rowp = a16 + t * (kXBM * 128) + r * 128;
-          *reinterpret_cast<uint4*>(rowp + ((c8 ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(rowp + (((c8 + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
-        {  // token tile: already bf16 in the SW128 layout; copy it to the converted slot
-          const uint4* b16 = reinterpret_cast<const uint4*>(sB + s * C::kB);
-          uint4* o16 = reinterpret_cast<uint4*>(sB16 + sc2 * C::kB);
-          for (int i = c; i < C::kB / 16; i += 256) o16[i] = b16[i];
-        }
-        fence_async_smem();
-        mbar_arrive(&cvt_bar[sc2]);
-        mbar_arrive(&lempty_bar[s]);
+        // column c of the slot holds k = 2c, 2c+1 of this row
+        tmem_st32u(tmem_base + lane_addr + kXSlotCol0 + t * 64 + half * 32, o);
+        tc_fence_before();
+        mbar_arrive(&cvt_full[t]);
         if (++s == S) {
           s = 0;
           ph ^= 1;
         }
-        if (++sc2 == SC) {
-          sc2 = 0;
-          ph2 ^= 1;
+        if (++t == kXSlots) {
+          t = 0;
+          pht ^= 1;
         }
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
       const uint32_t idesc = idesc_bf16_f32(kXBM, BN);
-      int s = 0, i = 0;
-      uint32_t ph = 0;
+      int s = 0, t = 0, i = 0;
+      uint32_t ph = 0, pht = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int e, tm, tn, n0, nr;
         if (!gunit(a, gu, u, e, tm, tn, n0, nr, BN)) continue;
@@ -242,24 +242,29 @@ __global__ void __launch_bounds__(kXThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + ab * BN;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&cvt_bar[s], ph)) {
+          if (!mbar_wait(&cvt_full[t], pht) || !mbar_wait(&full_bar[s], ph)) {
             set_status(a.status, kStatusMbarTimeout);
             *abort_flag = 1;
             break;
           }
           tc_fence_after();
+          const uint32_t at = tmem_base + kXSlotCol0 + t * 64;
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const uint64_t da = smem_desc_sw128(smem_u32(sA16 + s * C::kA16 + t * (kXBM * 128)));
-            const uint64_t db = smem_desc_sw128(smem_u32(sB16 + s * C::kB + t * (BN * 128)));
+          for (int box = 0; box < 2; ++box) {
+            const uint64_t db = smem_desc_sw128(smem_u32(sB + s * C::kB + box * (BN * 128)));
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_f16(d, da + 2 * kk, db + 2 * kk, idesc, (kb > 0 || t > 0 || kk > 0) ? 1u : 0u);
+              umma_f16_ts(d, at + box * 32 + kk * 8, db + 2 * kk, idesc, (kb > 0 || box > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);
-          if (++s == SC) {
+          umma_commit(&cvt_empty[t]);
+          if (++s == S) {
             s = 0;
             ph ^= 1;
+          }
+          if (++t == kXSlots) {
+            t = 0;
+            pht ^= 1;
           }
         }
         umma_commit(&tfull_bar[ab]);
@@ -314,7 +319,7 @@ __global__ void __launch_bounds__(kXThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    tmem_dealloc(tmem_base, 512);
   }
 }
 

@@ -21,6 +21,8 @@
 //                       state carried in shared memory, (I - A)^-1 by forward
 //                       substitution (stable, unlike full-width doubling at C >= 32),
 //                       RMSNormGated output fused.
+#include <cstdlib>
+
 #include "common/host.h"
 #include "common/sm100.cuh"
 #include "kernels/prefill.h"
@@ -361,6 +363,20 @@ void gqa_prefill(const GqaPrefillArgs& p, cudaStream_t stream) {
 __global__ void __launch_bounds__(256) dn_prefill_prep_kernel(DnPrefillArgs p) {
   const int t = blockIdx.x, b = blockIdx.y;
   const int KD = p.k_heads * 128, C = 2 * KD + p.v_heads * 128;
+  if (t >= p.S) {  // pad rows of the last chunk: zero, so whole-chunk tiles need no masking
+    for (int i = threadIdx.x; i < p.k_heads * 128; i += blockDim.x) {
+      const long o = (((long)b * p.k_heads + (i >> 7)) * p.S_pad + t) * 128 + (i & 127);
+      p.q_out[o] = __float2bfloat16(0.f);
+      p.k_out[o] = __float2bfloat16(0.f);
+    }
+    for (int i = threadIdx.x; i < p.v_heads * 128; i += blockDim.x)
+      p.v_out[(((long)b * p.v_heads + (i >> 7)) * p.S_pad + t) * 128 + (i & 127)] = __float2bfloat16(0.f);
+    for (int h = threadIdx.x; h < p.v_heads; h += blockDim.x) {
+      p.g_out[((long)b * p.v_heads + h) * p.S_pad + t] = 0.f;
+      p.beta_out[((long)b * p.v_heads + h) * p.S_pad + t] = 0.f;
+    }
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const __nv_bfloat16* row = p.qkv + ((long)b * p.S + t) * p.qkv_row;
   const __nv_bfloat16* ring = p.conv_ring + (long)b * p.ring_slots * C;
@@ -658,10 +674,24 @@ __global__ void __launch_bounds__(256, 1) dn_chunk_kernel(DnPrefillArgs p) {
   for (int i = tid; i < 128 * 128; i += 256) gS[i] = from_f<StateT>(sS[(i >> 7) * kLD + (i & 127)]);
 }
 
+static bool dn_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("BWN_DN_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 void deltanet_prefill(const DnPrefillArgs& p, cudaStream_t stream) {
   BWN_CHECK(p.S_pad >= p.S, "deltanet_prefill: S_pad");
-  dn_prefill_prep_kernel<<<dim3(p.S, p.batch), 256, 0, stream>>>(p);
+  dn_prefill_prep_kernel<<<dim3(p.S_pad, p.batch), 256, 0, stream>>>(p);
   BWN_CUDA_CHECK(cudaGetLastError());
+  if (dn_tc_enabled() && p.status && deltanet_chunk_tc_supported(p)) {
+    deltanet_chunk_tc(p, p.status, stream);
+    dn_ring_update_kernel<<<dim3(8, p.batch), 256, 0, stream>>>(p);
+    BWN_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   static bool set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -53,7 +53,11 @@ struct DnPrefillArgs {
   long out_row;
   int batch, S, S_pad, start, k_heads, v_heads;
   float l2_eps, norm_eps;
+  int* status = nullptr;     // device status word (bounded waits of the tensor-core kernel)
 };
 void deltanet_prefill(const DnPrefillArgs& p, cudaStream_t stream);
+// the chunked recurrence on tcgen05 (csrc/kernels/dn_chunk_tc.cu)
+bool deltanet_chunk_tc_supported(const DnPrefillArgs& p);
+void deltanet_chunk_tc(const DnPrefillArgs& p, int* status, cudaStream_t stream);
 
 }  // namespace bwn

@@ -144,6 +144,40 @@ void moe_combine_symm_op(const Tensor& y, const Tensor& w, const Tensor& pos_of,
   moe_combine_ex(c, at::cuda::getCurrentCUDAStream().stream());
 }
 
+// The same combine, then (same launch) the sum over ranks through the multicast
+// address + residual add (in place) + RMSNorm(1+w): the MoE sub-block's
+// expert-parallel reduction in one kernel.  Returns the normed rows.
+Tensor moe_combine_symm_norm_op(const Tensor& y, const Tensor& w, const Tensor& pos_of,
+                                const c10::optional<Tensor>& pos_sh, const c10::optional<Tensor>& sg,
+                                const c10::optional<Tensor>& shared_y, const c10::optional<Tensor>& shared_gate,
+                                int64_t local_base, int64_t mc_base, int64_t buf_stride, std::vector<int64_t> peer_flags,
+                                int64_t flags_local, const Tensor& local_state, int64_t rank, Tensor residual,
+                                const Tensor& norm_w, double eps, double timeout_s) {
+  check_bf16(residual, "residual");
+  check_f32(norm_w, "norm_w");
+  const c10::cuda::CUDAGuard guard(y.device());
+  MoeCombineExArgs c = combine_args(y, w, pos_of, pos_sh, sg, shared_y, shared_gate);
+  TORCH_CHECK(residual.dim() == 2 && residual.stride(1) == 1 && residual.size(0) == c.T && residual.size(1) == c.H,
+              "residual [T, H]");
+  auto out = at::empty({c.T, c.H}, residual.options());
+  c.mode = kCombineSymmNorm;
+  c.symm_base = reinterpret_cast<__nv_bfloat16*>(local_base);
+  c.sig = make_sig(peer_flags, local_state, rank, buf_stride);
+  c.mc_base = reinterpret_cast<const __nv_bfloat16*>(mc_base);
+  c.flags = reinterpret_cast<const unsigned*>(flags_local);
+  c.sel_rw = local_state.data_ptr<int>() + 2;
+  c.status = status_dev_ptr();
+  c.limit_ns = (unsigned long long)(timeout_s * 1e9);
+  c.resid = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  c.ldr = residual.stride(0);
+  c.norm_w = norm_w.data_ptr<float>();
+  c.eps = (float)eps;
+  c.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  c.ldo = out.stride(0);
+  moe_combine_ex(c, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
 Tensor ar_add_norm_op(int64_t mc_base, int64_t buf_stride, int64_t flags_local, int64_t world,
                       const Tensor& local_state, Tensor residual, const Tensor& w, double eps, double timeout_s) {
   check_bf16(residual, "residual");
@@ -479,6 +513,10 @@ void register_comm_defs(torch::Library& m) {
       "moe_combine_symm(Tensor y, Tensor w, Tensor pos_of, Tensor? pos_sh, Tensor? sg, Tensor? shared_y, "
       "Tensor? shared_gate, int local_base, int buf_stride, int[] peer_flags, Tensor(a!) local_state, int rank) -> ()");
   m.def(
+      "moe_combine_symm_norm(Tensor y, Tensor w, Tensor pos_of, Tensor? pos_sh, Tensor? sg, Tensor? shared_y, "
+      "Tensor? shared_gate, int local_base, int mc_base, int buf_stride, int[] peer_flags, int flags_local, "
+      "Tensor(a!) local_state, int rank, Tensor(b!) residual, Tensor norm_w, float eps, float timeout_s) -> Tensor");
+  m.def(
       "ar_add_norm(int mc_base, int buf_stride, int flags_local, int world, Tensor(a!) local_state, "
       "Tensor(b!) residual, Tensor w, float eps, float timeout_s) -> Tensor");
   m.def(
@@ -503,6 +541,7 @@ void register_comm_impls(torch::Library& m) {
   m.impl("gemm_symm_norm", &gemm_symm_norm_op);
   m.impl("symm_put_signal", &symm_put_signal_op);
   m.impl("moe_combine_symm", &moe_combine_symm_op);
+  m.impl("moe_combine_symm_norm", &moe_combine_symm_norm_op);
   m.impl("ar_add_norm", &ar_add_norm_op);
   m.impl("ar_hc_post", &ar_hc_post_op);
   m.impl("greedy_allmax", &greedy_allmax_op);

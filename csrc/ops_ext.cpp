@@ -77,6 +77,7 @@ Tensor deltanet_prefill_op(const Tensor& qkv, const Tensor& z, const Tensor& a, 
   p.out_row = out.stride(1);
   p.batch = B;
   p.S = S;
+  p.status = status_dev_ptr();
   p.S_pad = S_pad;
   p.start = (int)start;
   p.k_heads = (int)k_heads;

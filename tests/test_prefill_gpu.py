@@ -16,18 +16,37 @@ def _rel(a, b):
     return ((a - b).norm() / (b.norm() + 1e-12)).item()
 
 
-@pytest.mark.parametrize("B,S,KH,VH,start", [(2, 100, 2, 4, 0), (1, 64, 2, 6, 7), (3, 130, 2, 4, 2)])
-def test_deltanet_prefill(B, S, KH, VH, start):
+def _dn_case(B, S, KH, VH, start, near_one=False, seed=0):
+    torch.manual_seed(seed)
     C = 2 * KH * 128 + VH * 128
     W = C + VH * 128 + 2 * VH
     proj = (torch.randn(B, S, W, device=dev) * 0.5).bfloat16()
-    qkv, z = proj[..., :C], proj[..., C:C + VH * 128]
-    b_, a_ = proj[..., C + VH * 128:C + VH * 128 + VH], proj[..., C + VH * 128 + VH:]
     ring = (torch.randn(B, 4, C, device=dev) * 0.5).bfloat16() if start else torch.zeros(B, 4, C, device=dev).bfloat16()
     state = torch.randn(B, VH, 128, 128, device=dev) * 0.05 if start else torch.zeros(B, VH, 128, 128, device=dev)
     vl = torch.tensor([S - 3 * i for i in range(B)], dtype=torch.int32, device=dev)
     conv_w = torch.randn(C, 4, device=dev) * 0.5
-    A_log = torch.rand(VH, device=dev) * 2
+    # near_one: decay exp(g) within 1e-3 of 1 (A_log very negative): the state
+    # keeps almost everything over the whole prompt
+    A_log = (torch.full((VH,), -8.0, device=dev) if near_one else torch.rand(VH, device=dev) * 2)
+    return proj, ring, state, vl, conv_w, A_log
+
+
+@pytest.mark.parametrize("B,S,KH,VH,start", [(2, 100, 2, 4, 0), (1, 64, 2, 6, 7), (3, 130, 2, 4, 2)])
+def test_deltanet_prefill(B, S, KH, VH, start):
+    _check_deltanet_prefill(B, S, KH, VH, start)
+
+
+@pytest.mark.parametrize("near_one", [False, True], ids=["decaying", "near_one_decay"])
+def test_deltanet_prefill_production_shape(near_one):
+    """Qwen3.6-27B's shape at one GPU (16 K-heads, 48 V-heads) over a 2048-token prompt."""
+    _check_deltanet_prefill(2, 2048, 16, 48, 0, near_one=near_one)
+
+
+def _check_deltanet_prefill(B, S, KH, VH, start, near_one=False):
+    C = 2 * KH * 128 + VH * 128
+    proj, ring, state, vl, conv_w, A_log = _dn_case(B, S, KH, VH, start, near_one)
+    qkv, z = proj[..., :C], proj[..., C:C + VH * 128]
+    b_, a_ = proj[..., C + VH * 128:C + VH * 128 + VH], proj[..., C + VH * 128 + VH:]
     dt = torch.randn(VH, device=dev) * 0.1
     nw = torch.randn(128, device=dev) * 0.1 + 1
     ring_r, state_r = ring.cpu().clone(), state.cpu().clone()
