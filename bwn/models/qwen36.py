@@ -186,11 +186,17 @@ class Qwen36Model(nn.Module):
             for k in self.FP8_KEYS if dense else ():
                 if k in L and torch.is_tensor(L[k]) and L[k].dim() == 2 and L[k].shape[1] % 16 == 0:
                     L[k] = FP8Weight.from_dense(L[k])
-            if experts and torch.is_tensor(L.get("experts_gate_up")):
+            if experts and torch.is_tensor(L.get("experts_gate_up_x")):
+                # the shared expert rides along as the last expert, block-scaled like
+                # the routed ones (as the official FP8 checkpoints store it)
+                n = L["experts_gate_up_x"].shape[0] - 1
+                gx = FP8Experts.from_interleaved(L["experts_gate_up_x"])
+                dx = FP8Experts.quantize(L["experts_down_x"])
+                L["experts_gate_up_x"], L["experts_down_x"] = gx, dx
+                L["experts_gate_up"], L["experts_down"] = gx.select(0, n), dx.select(0, n)
+            elif experts and torch.is_tensor(L.get("experts_gate_up")):
                 L["experts_gate_up"] = FP8Experts.from_interleaved(L["experts_gate_up"])
                 L["experts_down"] = FP8Experts.quantize(L["experts_down"])
-                L.pop("experts_gate_up_x", None)  # the shared expert stays bf16, on its own GEMMs
-                L.pop("experts_down_x", None)
         if include_head:
             self.g["lm_head"] = FP8Weight.from_dense(self.g["lm_head"])
         return self
@@ -295,8 +301,9 @@ class Qwen36Model(nn.Module):
     def _moe_decode_ok(self, i: int, h: torch.Tensor) -> bool:
         from ..utils import env
         cfg = self.cfg
-        return (h.is_cuda and h.shape[0] <= 64 and "router_x" in self.layers[i] and cfg.hidden % 256 == 0
-                and cfg.hidden <= 4096 and cfg.num_experts <= 512 and cfg.top_k <= 16 and not self.moe_shared_only
+        return (h.is_cuda and h.shape[0] <= 64 and "router_x" in self.layers[i]
+                and cfg.hidden in (256, 512, 1024, 2048, 4096) and cfg.num_experts <= 512 and cfg.top_k <= 16
+                and not self.moe_shared_only
                 and bool(env.get("BWN_MOE_FUSED")))
 
     def _moe_decode(self, i: int, h: torch.Tensor, x: torch.Tensor, nxt: torch.Tensor) -> torch.Tensor:
@@ -314,9 +321,13 @@ class Qwen36Model(nn.Module):
             else:
                 per = -(-T // self.tp)
                 t_lo, t_hi = min(T, self.rank * per), min(T, (self.rank + 1) * per)
-            y, w, pos_of, pos_sh, sg = o.moe_decode(h, L["router_x"], L["experts_gate_up_x"], L["experts_down_x"],
-                                                    None, None, d.expert_offset, cfg.num_experts, cfg.top_k,
-                                                    cfg.norm_topk_prob, True, True, t_lo, t_hi, 0.0)
+            gx, dx = L["experts_gate_up_x"], L["experts_down_x"]
+            if hasattr(gx, "w8"):  # fp8 experts (shared expert folded in)
+                args = (gx.w8, dx.w8, gx.scales16, dx.scales16)
+            else:
+                args = (gx, dx, None, None)
+            y, w, pos_of, pos_sh, sg = o.moe_decode(h, L["router_x"], *args, d.expert_offset, cfg.num_experts,
+                                                    cfg.top_k, cfg.norm_topk_prob, True, True, t_lo, t_hi, 0.0)
             shared_y = None
         else:  # fp8 experts; the bf16 shared expert on its own GEMMs, gated by the fused router's logit
             gu, dn = L["experts_gate_up"], L["experts_down"]

@@ -33,6 +33,8 @@ FLAGS = {f.name: f for f in (
     Flag("BWN_METRICS", str, "", "path of a JSONL metrics file"),
     Flag("BWN_WAIT_LIMIT_MS", int, 2000, "bound on every device-side wait before it reports a timeout"),
     Flag("BWN_GQA_TC", int, 1, "GQA decode on the tcgen05 kernel (0: CUDA-core kernel)", (0, 1)),
+    Flag("BWN_GEMM_SMALL_RING", int, 1, "decode GEMMs with short K ranges on a 4-stage ring (two CTAs per SM, so the "
+         "next kernel's weight prefetch overlaps)", (0, 1)),
     Flag("BWN_GEMM_MAX_SPLITS", int, 16, "upper bound of the decode GEMMs' split-K factor (1..16)"),
     Flag("BWN_MOE_SHARDING", str, "ep", "MoE expert layout across TP ranks: partition experts (ep) or slice each "
          "expert's intermediate width (tp)", ("ep", "tp")),

@@ -30,13 +30,17 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kGemmThreads = 192;
 
-template <int BN>
+// SMALL: a 4-stage ring (decode GEMMs whose units hold at most 8 K blocks):
+// ~80 KB of shared memory at BN <= 32, so two CTAs fit on an SM and a GEMM
+// launched with PDL can stream its first weight tiles while the previous
+// kernel's CTAs are still resident.
+template <int BN, bool SMALL = false>
 struct GemmCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kStages = SMALL ? 4 : (kStagesRaw > 12 ? 12 : kStagesRaw);
   static constexpr int kTmemCols = (2 * BN) < 32 ? 32 : (2 * BN);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -133,12 +137,13 @@ __device__ __forceinline__ void gemm_ar_tail(const GemmArgs& args, unsigned epoc
   }
 }
 
-// MAJ bit 0: A is MN-major (stored [K, M]); bit 1: B is MN-major (stored [K, N]).
+// MAJ bit 0: A is MN-major (stored [K, M]); bit 1: B is MN-major (stored [K, N]);
+// bit 2: the small (4-stage) ring.
 template <int BN, int EPI, bool TRANS, int MAJ>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         GemmArgs args) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, (MAJ & 4) != 0>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -460,7 +465,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 template <int BN, int EPI, bool TRANS, int MAJ>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
                         cudaStream_t stream) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, (MAJ & 4) != 0>;
   auto k = gemm_bf16_tc_kernel<BN, EPI, TRANS, MAJ>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -474,7 +479,14 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
 
 template <int EPI, bool TRANS>
 static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool small = false) {
+  if (TRANS && small) {  // decode: small ring
+    switch (bn) {
+      case 16: launch_gemm<16, EPI, TRANS, 4>(ta, tb, a, grid, st); return;
+      case 32: launch_gemm<32, EPI, TRANS, 4>(ta, tb, a, grid, st); return;
+      default: break;
+    }
+  }
   switch (bn) {
     case 16: launch_gemm<16, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
     case 32: launch_gemm<32, EPI, TRANS, 0>(ta, tb, a, grid, st); break;
@@ -567,6 +579,11 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   const int units = tiles * a.splits;
   const int grid = units < sms ? units : sms;
   const bool tr = p.trans_out;
+  static const bool small_ok = [] {
+    const char* e = getenv("BWN_GEMM_SMALL_RING");
+    return !(e && e[0] == '0');
+  }();
+  const bool small = small_ok && tr && !maj && bn <= 32 && a.kb_per_split <= 8;
   if (maj) {
     BWN_CHECK(!tr && (p.epi == kEpiBF16 || p.epi == kEpiF32), "gemm: MN-major operands support bf16/f32 epilogues");
     const bool f32 = p.epi == kEpiF32;
@@ -579,20 +596,20 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
   }
   switch (p.epi) {
     case kEpiBF16:
-      tr ? dispatch_bn<kEpiBF16, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiBF16, false>(bn, ta, tb, a, grid, stream);
+      tr ? dispatch_bn<kEpiBF16, true>(bn, ta, tb, a, grid, stream, small) : dispatch_bn<kEpiBF16, false>(bn, ta, tb, a, grid, stream);
       break;
     case kEpiResid:
-      tr ? dispatch_bn<kEpiResid, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiResid, false>(bn, ta, tb, a, grid, stream);
+      tr ? dispatch_bn<kEpiResid, true>(bn, ta, tb, a, grid, stream, small) : dispatch_bn<kEpiResid, false>(bn, ta, tb, a, grid, stream);
       break;
     case kEpiSwiGLU:
-      tr ? dispatch_bn<kEpiSwiGLU, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiSwiGLU, false>(bn, ta, tb, a, grid, stream);
+      tr ? dispatch_bn<kEpiSwiGLU, true>(bn, ta, tb, a, grid, stream, small) : dispatch_bn<kEpiSwiGLU, false>(bn, ta, tb, a, grid, stream);
       break;
     case kEpiF32:
-      tr ? dispatch_bn<kEpiF32, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiF32, false>(bn, ta, tb, a, grid, stream);
+      tr ? dispatch_bn<kEpiF32, true>(bn, ta, tb, a, grid, stream, small) : dispatch_bn<kEpiF32, false>(bn, ta, tb, a, grid, stream);
       break;
     case kEpiSymm:
       BWN_CHECK(p.sig.epoch && p.sig.done_ticket && p.sig.world >= 1 && p.sig.world <= 8, "gemm: bad comm signal");
-      tr ? dispatch_bn<kEpiSymm, true>(bn, ta, tb, a, grid, stream) : dispatch_bn<kEpiSymm, false>(bn, ta, tb, a, grid, stream);
+      tr ? dispatch_bn<kEpiSymm, true>(bn, ta, tb, a, grid, stream, small) : dispatch_bn<kEpiSymm, false>(bn, ta, tb, a, grid, stream);
       break;
     case kEpiSymmNorm:
       BWN_CHECK(p.sig.epoch && p.sig.done_ticket && p.sig.world >= 1 && p.sig.world <= 8, "gemm: bad comm signal");
@@ -600,7 +617,7 @@ void gemm_bf16(const GemmProblem& p, cudaStream_t stream) {
                     p.tail.cols % 8 == 0 && p.tail.cols <= kGemmThreads * 8 * kTailVec && p.tail.ldr % 8 == 0 &&
                     p.tail.ldo % 8 == 0,
                 "gemm: bad reduction tail (hidden a multiple of 8, at most %d)", kGemmThreads * 8 * kTailVec);
-      tr ? dispatch_bn<kEpiSymmNorm, true>(bn, ta, tb, a, grid, stream)
+      tr ? dispatch_bn<kEpiSymmNorm, true>(bn, ta, tb, a, grid, stream, small)
          : dispatch_bn<kEpiSymmNorm, false>(bn, ta, tb, a, grid, stream);
       break;
     default: BWN_FAIL("gemm: bad epilogue %d", p.epi);

@@ -108,7 +108,7 @@ struct MoeRouteFusedArgs {
   bool shared_group;            // pack the shared expert as group E_local
   int t_lo, t_hi;               // tokens whose shared-expert rows this rank computes
   float* logits;                // [T, E (+1)] scratch
-  unsigned* bar;                // [2] grid barrier (arrivals, generation); zero before first use
+  unsigned* bar;                // [64] grid barrier: arrivals at [0], generation at [32]; zero before first use
   float* w;                     // [T, k] routing weights
   int* ids;                     // [T, k] expert ids
   float* sg;                    // [T] shared-gate logit (0 without has_sg)

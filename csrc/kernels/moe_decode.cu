@@ -73,6 +73,7 @@ __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
 }
 }  // namespace
 
+template <int NV>  // 16-byte vectors per lane per hidden row (H = 256 * NV)
 __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFusedArgs a) {
   __shared__ RouteSmem s;
   pdl_trigger();
@@ -80,42 +81,59 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = a.E + (a.has_sg ? 1 : 0);  // router rows (+ shared gate row)
   const int ntg = (a.T + 7) / 8;
-  const int nvec = a.H / 256;  // 16-byte vectors per lane per row
   // ---- 1. router logits: one warp per (router row, group of 8 tokens) ----
   for (int item = blockIdx.x * kRtWarps + warp; item < rows * ntg; item += gridDim.x * kRtWarps) {
     const int e = item / ntg, tg = item % ntg;
     const uint4* wr = reinterpret_cast<const uint4*>(a.router + (long)e * a.H);
-    uint4 wv[kRtMaxVec];
+    uint4 wv[NV];
 #pragma unroll
-    for (int j = 0; j < kRtMaxVec; ++j)
-      if (j < nvec) wv[j] = wr[lane + 32 * j];
+    for (int j = 0; j < NV; ++j) wv[j] = wr[lane + 32 * j];
     const int t1 = min(a.T, tg * 8 + 8);
-    for (int t = tg * 8; t < t1; ++t) {
-      const uint4* xr = reinterpret_cast<const uint4*>(a.x + (long)t * a.ldx);
-      float acc = 0.f;
+    for (int t = tg * 8; t < t1; t += 2) {  // two tokens' rows in flight at once
+      const bool two = t + 1 < t1;
+      const uint4* xr0 = reinterpret_cast<const uint4*>(a.x + (long)t * a.ldx);
+      const uint4* xr1 = reinterpret_cast<const uint4*>(a.x + (long)(two ? t + 1 : t) * a.ldx);
+      uint4 x0[NV], x1[NV];
 #pragma unroll
-      for (int j = 0; j < kRtMaxVec; ++j)
-        if (j < nvec) acc += dot8_bf16(wv[j], xr[lane + 32 * j]);
-      acc = warp_sum(acc);
-      if (lane == 0) a.logits[(long)t * rows + e] = acc;
+      for (int j = 0; j < NV; ++j) {
+        x0[j] = __ldg(xr0 + lane + 32 * j);
+        x1[j] = __ldg(xr1 + lane + 32 * j);
+      }
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        acc0 += dot8_bf16(wv[j], x0[j]);
+        acc1 += dot8_bf16(wv[j], x1[j]);
+      }
+      acc0 = warp_sum(acc0);
+      acc1 = warp_sum(acc1);
+      if (lane == 0) {
+        a.logits[(long)t * rows + e] = acc0;
+        if (two) a.logits[(long)(t + 1) * rows + e] = acc1;
+      }
     }
   }
   // ---- 2. grid barrier (count, generation); bounded wait ----
   if (threadIdx.x == 0) s.abort = 0;
   __syncthreads();
+  // arrival count and generation live on separate 128-byte lines, and the
+  // waiters back off between polls, so polling never starves the arrivals
+  unsigned* const bar_count = a.bar;
+  unsigned* const bar_gen = a.bar + 32;
   if (threadIdx.x == 0) {
-    const unsigned gen = ld_acquire_gpu_u32(a.bar + 1);
+    const unsigned gen = ld_acquire_gpu_u32(bar_gen);
     __threadfence();
-    const unsigned arrived = atomicAdd(a.bar, 1u);
+    const unsigned arrived = atomicAdd(bar_count, 1u);
     if (arrived == gridDim.x - 1) {
-      atomicExch(a.bar, 0u);
+      atomicExch(bar_count, 0u);
       __threadfence();
-      atomicAdd(a.bar + 1, 1u);
+      atomicAdd(bar_gen, 1u);
     } else {
       const uint64_t t0 = globaltimer_ns();
       uint32_t spins = 0;
-      while (ld_acquire_gpu_u32(a.bar + 1) == gen) {
-        if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > a.limit_ns) {
+      while (ld_acquire_gpu_u32(bar_gen) == gen) {
+        __nanosleep(64);
+        if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > a.limit_ns) {
           set_status(a.status, kStatusFlagTimeout);
           s.abort = 1;
           break;
@@ -196,26 +214,66 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
     if (el >= 0 && el < a.E_local) atomicAdd(&s.cnt[el], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    if (a.shared_group) s.cnt[a.E_local] = a.t_hi - a.t_lo;
-    int o = 0;
-    for (int g = 0; g < G; ++g) {
-      s.off[g] = o;
-      o += s.cnt[g];
+  if (threadIdx.x == 0 && a.shared_group) s.cnt[a.E_local] = a.t_hi - a.t_lo;
+  __syncthreads();
+  // exclusive prefix sum of the group counts: each thread scans a run of
+  // consecutive groups, the run totals are scanned by one warp
+  {
+    constexpr int kRun = (kMoeDecodeMaxGroups + kRtThreads - 1) / kRtThreads;
+    const int g0 = threadIdx.x * kRun;
+    int run = 0;
+#pragma unroll
+    for (int u = 0; u < kRun; ++u)
+      if (g0 + u < G) run += s.cnt[g0 + u];
+    // inclusive scan of the 256 run totals: warp scans, then the 8 warp totals
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int nb = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += nb;
     }
-    s.off[G] = o;
+    __shared__ int s_wtot[kRtWarps];
+    if (lane == 31) s_wtot[warp] = incl;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += s_wtot[w];
+    int o = before + incl - run;  // exclusive start of this thread's run
+#pragma unroll
+    for (int u = 0; u < kRun; ++u)
+      if (g0 + u < G) {
+        s.off[g0 + u] = o;
+        o += s.cnt[g0 + u];
+      }
+    if (threadIdx.x == kRtThreads - 1) {
+      int tot = 0;
+      for (int w = 0; w < kRtWarps; ++w) tot += s_wtot[w];
+      s.off[G] = tot;
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int id = s.ids[i], el = id - a.e0;
-    int p = -1;
-    if (el >= 0 && el < a.E_local) {
-      int r = 0;  // earlier pairs (token order, then slot) routed to the same expert
-      for (int j = 0; j < i; ++j) r += s.ids[j] == id;
-      p = s.off[el] + r;
-      s.src[p] = i / k;
+  // stable placement in pair order (token, then slot): warp 0 walks the pairs
+  // 32 at a time; lanes routed to the same expert rank themselves by lane
+  // order (match_any) on top of that expert's running cursor (s.cnt reused)
+  if (warp == 0) {
+    for (int g = lane; g < G; g += 32) s.cnt[g] = 0;
+    __syncwarp();
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + lane;
+      const int id = i < n ? s.ids[i] : -1;
+      const int el = id - a.e0;
+      const bool mine = i < n && el >= 0 && el < a.E_local;
+      const unsigned peers = __match_any_sync(0xffffffffu, mine ? el : -1);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      int p = -1;
+      if (mine) {
+        p = s.off[el] + s.cnt[el] + rank;
+        s.src[p] = i / k;
+      }
+      __syncwarp();
+      if (mine && rank == 0) s.cnt[el] += __popc(peers);
+      if (i < n) s.pos[i] = p;
+      __syncwarp();
     }
-    s.pos[i] = p;
   }
   if (a.shared_group)
     for (int t = a.t_lo + threadIdx.x; t < a.t_hi; t += blockDim.x) s.src[s.off[a.E_local] + t - a.t_lo] = t;
@@ -234,7 +292,7 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
       a.ids[i] = s.ids[i];
       a.pos_of[i] = s.pos[i];
     }
-    for (int g = threadIdx.x; g < G; g += blockDim.x) a.counts[g] = s.cnt[g];
+    for (int g = threadIdx.x; g < G; g += blockDim.x) a.counts[g] = s.off[g + 1] - s.off[g];
     for (int g = threadIdx.x; g <= G; g += blockDim.x) a.offsets[g] = s.off[g];
     for (int t = threadIdx.x; t < T; t += blockDim.x) {
       a.pos_sh[t] = (a.shared_group && t >= a.t_lo && t < a.t_hi) ? s.off[a.E_local] + t - a.t_lo : -1;
@@ -406,7 +464,15 @@ void moe_route_fused(const MoeRouteFusedArgs& a, cudaStream_t st) {
   BWN_CHECK(a.H % 256 == 0 && a.H / 256 <= kRtMaxVec && a.ldx % 8 == 0, "moe_route_fused: H multiple of 256, <= 4096");
   BWN_CHECK(a.E_local + (a.shared_group ? 1 : 0) <= kMoeDecodeMaxGroups, "moe_route_fused: too many groups");
   BWN_CHECK(!a.shared_group || (0 <= a.t_lo && a.t_lo <= a.t_hi && a.t_hi <= a.T), "moe_route_fused: token range");
-  launch_k(moe_route_fused_kernel, dim3(moe_route_fused_grid(a.T, a.E, a.has_sg)), dim3(kRtThreads), 0, st, a);
+  const dim3 grid(moe_route_fused_grid(a.T, a.E, a.has_sg));
+  switch (a.H / 256) {
+    case 1: launch_k(moe_route_fused_kernel<1>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 2: launch_k(moe_route_fused_kernel<2>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 4: launch_k(moe_route_fused_kernel<4>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 8: launch_k(moe_route_fused_kernel<8>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 16: launch_k(moe_route_fused_kernel<16>, grid, dim3(kRtThreads), 0, st, a); break;
+    default: BWN_FAIL("moe_route_fused: hidden %d (256, 512, 1024, 2048 or 4096)", a.H);
+  }
 }
 
 void moe_combine_ex(const MoeCombineExArgs& a, cudaStream_t st) {

@@ -58,7 +58,7 @@ def test_fused_moe_decode_fp8_experts():
     gpu = Qwen36Model(cfg, None, torch.device("cuda")).init_random(0)
     gpu.quantize_fp8(include_head=False, experts=True, dense=False)
     i, T = 0, 24
-    assert "experts_gate_up_x" not in gpu.layers[i]
+    assert hasattr(gpu.layers[i]["experts_gate_up_x"], "w8")  # shared expert folded into the fp8 stack
     h, x = _inputs(cfg, T, seed=3)
     dev = torch.device("cuda")
     x1, x2 = x.to(dev).clone(), x.to(dev).clone()
