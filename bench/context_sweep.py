@@ -5,7 +5,9 @@ and ``BENCHMARK.md:820-835``; its decode batch sweep, ``BENCHMARK.md:543-547``).
 
 For each context S: a fresh state, a bucketed prefill of ``--prefill-batch``
 uniform-random prompts of S tokens (TTFT and aggregate prompt tok/s, CUDA
-events, max over ranks).  Then for each decode batch B: the captured decode
+events, max over ranks); every chunk is a replay of one captured graph per
+bucket whose start position is a device scalar (``--eager-prefill``: plain
+launches).  Then for each decode batch B: the captured decode
 step timed over ``--steps`` steps at the largest context that fits
 (``--decode-context``), tok/s = B / step time.  One JSON line per measurement.
 
@@ -35,6 +37,7 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="debug only: fewer layers (marked in the output)")
     ap.add_argument("--fp8-experts", action="store_true")
     ap.add_argument("--moe-sharding", default="ep", choices=["ep", "tp"])
+    ap.add_argument("--eager-prefill", action="store_true", help="no captured prefill graph")
     a = ap.parse_args()
 
     from bwn.config import QWEN36_27B, QWEN36_35B_A3B
@@ -75,14 +78,18 @@ def main():
     g = torch.Generator().manual_seed(7)
     B = a.prefill_batch
     for S in a.contexts:
-        st = model.new_state(B, S + 8)
         prompt = torch.randint(0, cfg.vocab, (B, S), generator=g).to(dev)
-        model.prefill(prompt[:, :min(S, a.bucket)], model.new_state(B, min(S, a.bucket) + 8), None, a.bucket)  # warm
-        _, ms = timed(lambda: model.prefill(prompt, st, None, a.bucket))
+        cap = -(-S // a.bucket) * a.bucket + 8  # whole buckets
+        pf = StaticDecoder(model, B, cap, use_graph=not a.eager_prefill)
+        pf.capture_prefill(a.bucket)
+        if a.eager_prefill:  # warm the kernels and the allocator on one chunk
+            model.prefill(prompt[:, :min(S, a.bucket)], model.new_state(B, min(S, a.bucket) + 8), None, a.bucket)
+        _, ms = timed(lambda: pf.prefill(prompt, None, a.bucket))
         check_status(f"prefill {S}")
         emit(phase="prefill", context=S, batch=B, bucket=a.bucket, ttft_ms=round(ms, 2),
-             agg_tok_s=round(B * S / (ms / 1e3), 1))
-        del st
+             agg_tok_s=round(B * S / (ms / 1e3), 1), graph=not a.eager_prefill)
+        pf.release()
+        del pf
         torch.cuda.empty_cache()
 
     for Bd in a.decode_batches:

@@ -43,8 +43,12 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
     cfg, d = model.cfg, model.d
     B, S = tokens.shape
     dev = tokens.device
-    start = int(st.positions[0].item())
-    model.ensure_rope(start + S)
+    # the chunk's shared start is the largest row position (rows whose prompt
+    # ended in an earlier chunk sit behind it and have no valid rows here); it
+    # stays on the device and the kernels read it at run time, so a chunk needs
+    # no host sync and one captured graph serves every offset
+    start = st.positions.amax().reshape(1) if dev.type == "cuda" else int(st.positions.max())
+    model.ensure_rope(st.k_cache.shape[3] if dev.type == "cuda" else start + S)
     if valid_len is None:
         valid_len = torch.full((B,), S, dtype=torch.int32, device=dev)
     valid_len = valid_len.to(dev).int()
@@ -86,7 +90,8 @@ def prefill_hidden(model, tokens: torch.Tensor, st, valid_len, chunk: int = 64, 
             captured[i] = x.clone()
         if trace:
             dn = cfg.layer_type(i) == "deltanet"
-            _trace_layer(model, trace, start, i, cfg.layer_type(i), x, st.ssm[di - 1] if dn else st.k_cache[gi - 1])
+            _trace_layer(model, trace, int(st.positions.max()), i, cfg.layer_type(i), x,
+                         st.ssm[di - 1] if dn else st.k_cache[gi - 1])
     if feats_out is not None:
         feats_out.extend(captured[i] for i in feat_layers)
     st.positions.add_(valid_len)
@@ -112,8 +117,8 @@ def prefill_hidden_sp(model, tokens: torch.Tensor, st, sp, chunk: int = 64) -> t
         raise ValueError(f"sequence-parallel prefill needs B*S a multiple of {128 * W} and <= {sp.T_max}")
     Ts = T // W
     dev = tokens.device
-    start = int(st.positions[0].item())
-    model.ensure_rope(start + S)
+    start = st.positions.amax().reshape(1)  # read by the kernels at run time
+    model.ensure_rope(st.k_cache.shape[3])
     valid_len = torch.full((B,), S, dtype=torch.int32, device=dev)
     x_full = model.embed(tokens.reshape(T))
     x = x_full[r * Ts:(r + 1) * Ts].contiguous()  # residual shard

@@ -217,18 +217,23 @@ def gqa_decode(qg, k_new, v_new, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache,
 # --------------------------------------------------------------------------
 # prefill
 # --------------------------------------------------------------------------
-def deltanet_prefill(qkv, z, a, b, conv_ring, state, start_pos: int, valid_len, conv_w, A_log, dt_bias, norm_w,
+def _host_start(start_pos) -> int:
+    return int(start_pos.reshape(-1)[0].item()) if torch.is_tensor(start_pos) else int(start_pos)
+
+
+def deltanet_prefill(qkv, z, a, b, conv_ring, state, start_pos, valid_len, conv_w, A_log, dt_bias, norm_w,
                      k_heads: int, eps: float = 1e-6, chunk: int = 64) -> torch.Tensor:
     """Gated-DeltaNet over a prompt chunk ``qkv [B,S,C]`` (conv ring + recurrent
-    state carried in and out).  Returns ``[B, S, VH*128]``."""
+    state carried in and out).  ``start_pos``: host int, or an int32 device
+    tensor (element 0) read by the kernels at run time.  Returns ``[B, S, VH*128]``."""
     if qkv.is_cuda:
         return _prefill_cuda().deltanet_prefill(qkv, z, a, b, conv_ring, state, start_pos, valid_len, conv_w, A_log,
                                                 dt_bias, norm_w, k_heads, eps)
-    return ref.deltanet_prefill(qkv, a, b, z, conv_ring, state, start_pos, valid_len, conv_w, A_log, dt_bias,
-                                norm_w, k_heads, state.shape[2], state.shape[3], eps, chunk)
+    return ref.deltanet_prefill(qkv, a, b, z, conv_ring, state, _host_start(start_pos), valid_len, conv_w, A_log,
+                                dt_bias, norm_w, k_heads, state.shape[2], state.shape[3], eps, chunk)
 
 
-def gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_pos: int,
+def gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_pos,
                 eps: float = 1e-6) -> torch.Tensor:
     """Gated GQA over a prompt chunk: q/k norm + RoPE at ``start_pos``, K/V
     written to cache rows ``[start, start+S)``, causal attention over the used
@@ -237,6 +242,7 @@ def gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_
         return _prefill_cuda().gqa_prefill(qg, k, v, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, start_pos, eps)
     B, S, QH, D2 = qg.shape
     D = D2 // 2
+    start_pos = _host_start(start_pos)
     q, gate = qg.float().split(D, dim=-1)
     c = cos[start_pos:start_pos + S][None, :, None]
     s = sin[start_pos:start_pos + S][None, :, None]

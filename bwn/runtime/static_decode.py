@@ -11,7 +11,12 @@ decode ``decode_step_stateful``, ``contrib/qwen3.6-35b-a3b/static_decode_35b.py:
   written back into the input buffer inside the graph, so a device-side greedy
   loop needs no host round trip (``run_decode``, ``static_decode_35b.py:3142-3153``);
 * :meth:`StaticDecoder.step` is the host API: pinned H2D of the step's tokens,
-  graph replay, D2H of the next ids.
+  graph replay, D2H of the next ids;
+* :meth:`StaticDecoder.capture_prefill` captures one prefill chunk per bucket
+  size; the chunk's start position is a device scalar, so one graph serves
+  every chunk offset of a bucketed prefill (the reference's per-bucket compiled
+  prefill with runtime ``q_base`` / ``valid_len`` scalars,
+  ``static_decode_35b.py:2646-2653``).
 """
 from __future__ import annotations
 
@@ -44,6 +49,7 @@ class StaticDecoder:
             torch.cuda.manual_seed(seed + getattr(model, "rank", 0))
         self.use_graph = use_graph and dev.type == "cuda"
         self.graph: torch.cuda.CUDAGraph | None = None
+        self._pf: dict[int, tuple] = {}  # bucket -> (graph, ids, valid, hidden out)
         self._host_in = torch.zeros(batch, dtype=torch.int32, pin_memory=dev.type == "cuda")
         self._host_out = torch.zeros(batch, dtype=torch.int32, pin_memory=dev.type == "cuda")
 
@@ -53,10 +59,65 @@ class StaticDecoder:
 
     def prefill(self, prompt: torch.Tensor, valid_len: torch.Tensor | None = None, bucket: int = 0) -> torch.Tensor:
         """Run the prompt ``[B, S]`` through the model; the first generated ids
-        become the next decode input.  Returns the ids ``[B]`` (device)."""
-        ids = self.model.prefill(prompt.to(self.model.device), self.st, valid_len, bucket)
+        become the next decode input.  Returns the ids ``[B]`` (device).  With a
+        graph captured for ``bucket`` (:meth:`capture_prefill`) every chunk is a
+        replay of it."""
+        if bucket in self._pf:
+            ids = self._prefill_graphed(prompt, valid_len, bucket)
+        else:
+            ids = self.model.prefill(prompt.to(self.model.device), self.st, valid_len, bucket)
         self.tokens.copy_(ids)
         return ids
+
+    def capture_prefill(self, bucket: int) -> None:
+        """Capture one prefill chunk of ``bucket`` tokens per row as a CUDA graph.
+        Its start position is read from the state on the device and its per-row
+        valid lengths from a static buffer, so the same graph replays at every
+        chunk offset and pads the last chunk of a prompt to the bucket.  The
+        state's cache must hold whole buckets (``max_seq`` >= the prompt rounded
+        up to ``bucket``).  Warms up eagerly, captures, then resets the state."""
+        if not self.use_graph or bucket in self._pf:
+            return
+        m, B = self.model, self.batch
+        dev = m.device
+        ids = torch.zeros(B, bucket, dtype=torch.long, device=dev)
+        valid = torch.full((B,), bucket, dtype=torch.int32, device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            m.prefill_hidden(ids, self.st, valid)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        check_status("prefill warm-up")
+        self.st.reset()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = m.prefill_hidden(ids, self.st, valid)
+        torch.cuda.synchronize()
+        self.st.reset()
+        self._pf[bucket] = (g, ids, valid, out)
+
+    def _prefill_graphed(self, prompt: torch.Tensor, valid_len: torch.Tensor | None, bucket: int) -> torch.Tensor:
+        g, ids, valid, out = self._pf[bucket]
+        dev = self.model.device
+        prompt = prompt.to(dev)
+        B, S = prompt.shape
+        if B != self.batch:
+            raise ValueError(f"prefill graph was captured for batch {self.batch}, got {B}")
+        if -(-S // bucket) * bucket > self.max_seq:
+            raise ValueError(f"prompt of {S} tokens in {bucket}-token chunks needs max_seq >= "
+                             f"{-(-S // bucket) * bucket} (have {self.max_seq})")
+        vl = (valid_len.to(dev) if valid_len is not None else torch.full((B,), S, device=dev)).int()
+        h = torch.zeros_like(out)
+        for c0 in range(0, S, bucket):
+            n = min(S, c0 + bucket) - c0
+            ids[:, :n].copy_(prompt[:, c0:c0 + n])
+            if n < bucket:
+                ids[:, n:].zero_()
+            torch.clamp(vl - c0, 0, n, out=valid)
+            g.replay()
+            h = torch.where((valid > 0)[:, None], out, h)
+        return self.model.greedy(h)
 
     # ----------------------------------------------------------------- step
     def _step_body(self) -> None:
@@ -88,9 +149,10 @@ class StaticDecoder:
         self.tokens.zero_()
 
     def release(self) -> None:
-        """Drop the graph (must happen before destroying a process group whose
-        collectives it captured)."""
+        """Drop the graphs (must happen before destroying a process group whose
+        collectives they captured)."""
         self.graph = None
+        self._pf.clear()
 
     def step_device(self) -> None:
         """One decode step entirely on the device (input = previous ids)."""

@@ -23,6 +23,7 @@
 #include "common/sm100.cuh"
 #include "kernels/moe.h"
 #include "kernels/grouped_units.cuh"
+#include "kernels/moe_topk.cuh"
 
 namespace bwn {
 
@@ -36,57 +37,9 @@ __global__ void moe_topk_softmax_kernel(const float* __restrict__ logits, int T,
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* l = logits + (long)warp * E;
-  float v[EPL];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = i * 32 + lane;
-    v[i] = e < E ? l[e] : -INFINITY;
-    mx = fmaxf(mx, v[i]);
-  }
-  mx = warp_max(mx);
-  float sum = 0.f;
-#pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    v[i] = (i * 32 + lane) < E ? __expf(v[i] - mx) : 0.f;
-    sum += v[i];
-  }
-  sum = warp_sum(sum);
-  const float inv = 1.f / sum;
-  float picked = 0.f;
-  float my_w = 0.f;
-  int my_id = -1;
-  for (int s = 0; s < k; ++s) {
-    // local best (highest prob, lowest expert id on ties)
-    float best = -1.f;
-    int bid = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < EPL; ++i) {
-      const int e = i * 32 + lane;
-      if (e < E && (v[i] > best || (v[i] == best && e < bid))) {
-        best = v[i];
-        bid = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
-      if (ob > best || (ob == best && oi < bid)) {
-        best = ob;
-        bid = oi;
-      }
-    }
-    const float p = best * inv;
-    picked += p;
-    if (lane == s) {
-      my_w = p;
-      my_id = bid;
-    }
-#pragma unroll
-    for (int i = 0; i < EPL; ++i)
-      if (i * 32 + lane == bid) v[i] = -2.f;  // remove
-  }
+  float my_w;
+  int my_id;
+  const float picked = route_topk<EPL>(l, E, k, lane, my_w, my_id);
   if (lane < k) {
     w_out[(long)warp * k + lane] = renorm ? my_w / picked : my_w;
     id_out[(long)warp * k + lane] = my_id;

@@ -30,6 +30,7 @@
 #include "common/launch.cuh"
 #include "common/sm100.cuh"
 #include "kernels/moe.h"
+#include "kernels/moe_topk.cuh"
 
 namespace bwn {
 
@@ -73,7 +74,7 @@ __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
 }
 }  // namespace
 
-template <int NV>  // 16-byte vectors per lane per hidden row (H = 256 * NV)
+template <int NV, int EPL>  // NV: 16-byte vectors per lane per hidden row (H = 256 * NV); EPL: experts per lane
 __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFusedArgs a) {
   __shared__ RouteSmem s;
   pdl_trigger();
@@ -146,58 +147,11 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
   if (s.abort) return;
   // ---- 3. routing (every CTA, identically): softmax -> top-k -> renormalise ----
   const int E = a.E, k = a.k, T = a.T;
-  const int epl = (E + 31) / 32;
   for (int t = warp; t < T; t += kRtWarps) {
     const float* l = a.logits + (long)t * rows;
-    float v[16];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int e = i * 32 + lane;
-      v[i] = (i < epl && e < E) ? __ldcg(l + e) : -INFINITY;
-      mx = fmaxf(mx, v[i]);
-    }
-    mx = warp_max(mx);
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = (i < epl && i * 32 + lane < E) ? __expf(v[i] - mx) : 0.f;
-      sum += v[i];
-    }
-    sum = warp_sum(sum);
-    const float inv = 1.f / sum;
-    float picked = 0.f, my_w = 0.f;
-    int my_id = -1;
-    for (int sl = 0; sl < k; ++sl) {
-      float best = -1.f;
-      int bid = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int e = i * 32 + lane;
-        if (i < epl && e < E && (v[i] > best || (v[i] == best && e < bid))) {
-          best = v[i];
-          bid = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
-        if (ob > best || (ob == best && oi < bid)) {
-          best = ob;
-          bid = oi;
-        }
-      }
-      const float p = best * inv;
-      picked += p;
-      if (lane == sl) {
-        my_w = p;
-        my_id = bid;
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (i * 32 + lane == bid) v[i] = -2.f;
-    }
+    float my_w;
+    int my_id;
+    const float picked = route_topk<EPL>(l, E, k, lane, my_w, my_id);
     if (lane < k) {
       s.w[t * k + lane] = a.renorm ? my_w / picked : my_w;
       s.ids[t * k + lane] = my_id;
@@ -458,6 +412,18 @@ int moe_route_fused_grid(int T, int E, bool has_sg) {
   return std::max(1, std::min(grid, num_sms()));
 }
 
+template <int EPL>
+static void route_launch(const MoeRouteFusedArgs& a, dim3 grid, cudaStream_t st) {
+  switch (a.H / 256) {
+    case 1: launch_k(moe_route_fused_kernel<1, EPL>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 2: launch_k(moe_route_fused_kernel<2, EPL>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 4: launch_k(moe_route_fused_kernel<4, EPL>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 8: launch_k(moe_route_fused_kernel<8, EPL>, grid, dim3(kRtThreads), 0, st, a); break;
+    case 16: launch_k(moe_route_fused_kernel<16, EPL>, grid, dim3(kRtThreads), 0, st, a); break;
+    default: BWN_FAIL("moe_route_fused: hidden %d (256, 512, 1024, 2048 or 4096)", a.H);
+  }
+}
+
 void moe_route_fused(const MoeRouteFusedArgs& a, cudaStream_t st) {
   BWN_CHECK(a.T >= 1 && a.T <= kRtMaxT, "moe_route_fused: 1..%d tokens", kRtMaxT);
   BWN_CHECK(a.k >= 1 && a.k <= kRtMaxK && a.k <= a.E && a.E <= 512, "moe_route_fused: k <= 16, E <= 512");
@@ -465,13 +431,13 @@ void moe_route_fused(const MoeRouteFusedArgs& a, cudaStream_t st) {
   BWN_CHECK(a.E_local + (a.shared_group ? 1 : 0) <= kMoeDecodeMaxGroups, "moe_route_fused: too many groups");
   BWN_CHECK(!a.shared_group || (0 <= a.t_lo && a.t_lo <= a.t_hi && a.t_hi <= a.T), "moe_route_fused: token range");
   const dim3 grid(moe_route_fused_grid(a.T, a.E, a.has_sg));
-  switch (a.H / 256) {
-    case 1: launch_k(moe_route_fused_kernel<1>, grid, dim3(kRtThreads), 0, st, a); break;
-    case 2: launch_k(moe_route_fused_kernel<2>, grid, dim3(kRtThreads), 0, st, a); break;
-    case 4: launch_k(moe_route_fused_kernel<4>, grid, dim3(kRtThreads), 0, st, a); break;
-    case 8: launch_k(moe_route_fused_kernel<8>, grid, dim3(kRtThreads), 0, st, a); break;
-    case 16: launch_k(moe_route_fused_kernel<16>, grid, dim3(kRtThreads), 0, st, a); break;
-    default: BWN_FAIL("moe_route_fused: hidden %d (256, 512, 1024, 2048 or 4096)", a.H);
+  const int epl = (a.E + 31) / 32;
+  switch (epl <= 1 ? 1 : epl <= 2 ? 2 : epl <= 4 ? 4 : epl <= 8 ? 8 : 16) {
+    case 1: route_launch<1>(a, grid, st); break;
+    case 2: route_launch<2>(a, grid, st); break;
+    case 4: route_launch<4>(a, grid, st); break;
+    case 8: route_launch<8>(a, grid, st); break;
+    default: route_launch<16>(a, grid, st); break;
   }
 }
 

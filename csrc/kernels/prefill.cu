@@ -37,8 +37,12 @@ __global__ void __launch_bounds__(256) gqa_prefill_prep_kernel(GqaPrefillArgs p)
   const int b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = 256;
+  const int pos = prefill_start(p) + t;
+  if (t < p.S && pos >= p.s_max) {  // the chunk runs past the cache: nothing of this row is written
+    if (threadIdx.x == 0) set_status(p.status, kStatusBounds);
+    return;
+  }
   const bool real = t < p.S;
-  const int pos = p.start + t;
   const int R = p.rope_dim, hr = R / 2;
   float c[8], s[8];
 #pragma unroll
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int G = p.q_heads / p.kv_heads;
   const int kvh = h / G;
   const int q0 = qt * kFaM;
-  const int kv_end = p.start + min(q0 + kFaM, p.S);
+  const int kv_end = min(prefill_start(p) + min(q0 + kFaM, p.S), p.s_max);
   const int ntiles = (kv_end + kFaN - 1) / kFaN;
 
   if (threadIdx.x == 0) {
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // ------------------------------ softmax warps ----------------------------
     const int q = warp & 3;
     const int r = q * 32 + lane;  // query row in tile == TMEM lane
-    const int qpos = p.start + q0 + r;
+    const int qpos = prefill_start(p) + q0 + r;
     const bool row_real = (q0 + r) < p.S;
     const float sl2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
@@ -380,10 +384,11 @@ __global__ void __launch_bounds__(256) dn_prefill_prep_kernel(DnPrefillArgs p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const __nv_bfloat16* row = p.qkv + ((long)b * p.S + t) * p.qkv_row;
   const __nv_bfloat16* ring = p.conv_ring + (long)b * p.ring_slots * C;
+  const int start = prefill_start(p);
   auto hist = [&](int ch, int back) -> float {  // x at position start+t-back
     const int tt = t - back;
     if (tt >= 0) return __bfloat162float(row[(long)(-back) * p.qkv_row + ch]);
-    const int pos = p.start + tt;
+    const int pos = start + tt;
     if (pos < 0) return 0.f;
     return __bfloat162float(ring[(pos & (p.ring_slots - 1)) * C + ch]);
   };
@@ -433,11 +438,12 @@ __global__ void dn_ring_update_kernel(DnPrefillArgs p) {
   const int b = blockIdx.y;
   const int KD = p.k_heads * 128, C = 2 * KD + p.v_heads * 128;
   const int vl = p.valid_len[b];
+  const int start = prefill_start(p);
   for (int back = 1; back <= 3; ++back) {
     const int t = vl - back;
     if (t < 0) continue;
     const __nv_bfloat16* row = p.qkv + ((long)b * p.S + t) * p.qkv_row;
-    __nv_bfloat16* dst = p.conv_ring + ((long)b * p.ring_slots + ((p.start + t) & (p.ring_slots - 1))) * C;
+    __nv_bfloat16* dst = p.conv_ring + ((long)b * p.ring_slots + ((start + t) & (p.ring_slots - 1))) * C;
     for (int ch = blockIdx.x * blockDim.x + threadIdx.x; ch < C; ch += gridDim.x * blockDim.x) dst[ch] = row[ch];
   }
 }

@@ -5,6 +5,15 @@
 
 namespace bwn {
 
+#ifdef __CUDACC__
+// The chunk's start position: the device scalar when given (so one captured
+// graph serves every chunk offset of a bucketed prefill), else the host value.
+template <class Args>
+__device__ __forceinline__ int prefill_start(const Args& p) {
+  return p.start_dev ? __ldg(p.start_dev) : p.start;
+}
+#endif
+
 struct GqaPrefillArgs {
   const __nv_bfloat16* qg;   // [B, S, QH, 512] rows of stride qg_row (query || gate per head)
   long qg_row;
@@ -21,6 +30,7 @@ struct GqaPrefillArgs {
   __nv_bfloat16* out;        // [B, S, QH*256] rows of stride out_row
   long out_row;
   int* status;
+  const int* start_dev;      // optional device copy of the start position (read at run time; overrides start)
   int batch, S, S_pad, start, q_heads, kv_heads, s_max, rope_dim;
   float eps, scale;
 };
@@ -51,6 +61,7 @@ struct DnPrefillArgs {
   float* beta_out;
   __nv_bfloat16* out;        // [B, S, VH*128] rows of stride out_row
   long out_row;
+  const int* start_dev;      // optional device copy of the start position (read at run time; overrides start)
   int batch, S, S_pad, start, k_heads, v_heads;
   float l2_eps, norm_eps;
   int* status = nullptr;     // device status word (bounded waits of the tensor-core kernel)

@@ -26,10 +26,18 @@ static long row_stride(const Tensor& t, const char* name) {
   return t.stride(1);
 }
 
+// Optional int32 device tensor holding the chunk's start position in element 0.
+static const int* start_ptr(const c10::optional<Tensor>& start_t, const Tensor& like) {
+  if (!start_t.has_value()) return nullptr;
+  TORCH_CHECK(start_t->scalar_type() == at::kInt && start_t->numel() >= 1 && start_t->device() == like.device(),
+              "bwn: start_t must be an int32 tensor on the activations' device");
+  return start_t->data_ptr<int>();
+}
+
 Tensor deltanet_prefill_op(const Tensor& qkv, const Tensor& z, const Tensor& a, const Tensor& b, Tensor conv_ring,
                            Tensor state, int64_t start, const Tensor& valid_len, const Tensor& conv_w,
                            const Tensor& A_log, const Tensor& dt_bias, const Tensor& norm_w, int64_t k_heads,
-                           double eps) {
+                           double eps, const c10::optional<Tensor>& start_t) {
   check_bf16(qkv, "qkv");
   check_bf16(z, "z");
   check_bf16(a, "a");
@@ -80,6 +88,7 @@ Tensor deltanet_prefill_op(const Tensor& qkv, const Tensor& z, const Tensor& a, 
   p.status = status_dev_ptr();
   p.S_pad = S_pad;
   p.start = (int)start;
+  p.start_dev = start_ptr(start_t, qkv);
   p.k_heads = (int)k_heads;
   p.v_heads = VH;
   p.l2_eps = 1e-6f;
@@ -90,7 +99,7 @@ Tensor deltanet_prefill_op(const Tensor& qkv, const Tensor& z, const Tensor& a, 
 
 Tensor gqa_prefill_op(const Tensor& qg, const Tensor& k, const Tensor& v, const Tensor& q_norm_w,
                       const Tensor& k_norm_w, const Tensor& cos, const Tensor& sin, Tensor k_cache, Tensor v_cache,
-                      int64_t start, double eps) {
+                      int64_t start, double eps, const c10::optional<Tensor>& start_t) {
   check_bf16(qg, "qg");
   check_bf16(k, "k");
   check_bf16(v, "v");
@@ -102,7 +111,8 @@ Tensor gqa_prefill_op(const Tensor& qg, const Tensor& k, const Tensor& v, const 
   const c10::cuda::CUDAGuard guard(qg.device());
   const int B = (int)qg.size(0), S = (int)qg.size(1), QH = (int)qg.size(2), KVH = (int)k.size(2);
   TORCH_CHECK(qg.size(0) == 1 || qg.stride(0) == S * qg.stride(1), "qg rows uniform");
-  TORCH_CHECK(start + S <= k_cache.size(2), "gqa_prefill: chunk exceeds the cache");
+  // with a device start the bound is checked by the kernel (status word)
+  TORCH_CHECK(start_t.has_value() || start + S <= k_cache.size(2), "gqa_prefill: chunk exceeds the cache");
   const int S_pad = ((S + 127) / 128) * 128;
   auto q_rot = at::empty({B, QH, S_pad, 256}, qg.options());
   auto out = at::empty({B, S, QH * 256}, qg.options());
@@ -126,6 +136,7 @@ Tensor gqa_prefill_op(const Tensor& qg, const Tensor& k, const Tensor& v, const 
   p.S = S;
   p.S_pad = S_pad;
   p.start = (int)start;
+  p.start_dev = start_ptr(start_t, qg);
   p.q_heads = QH;
   p.kv_heads = KVH;
   p.s_max = (int)k_cache.size(2);
@@ -863,10 +874,11 @@ void register_ext_defs(torch::Library& m) {
   m.def("mqa_attn(Tensor q, Tensor kv, Tensor visible, int q_per_seq, float scale, int splits) -> Tensor");
   m.def(
       "deltanet_prefill(Tensor qkv, Tensor z, Tensor a, Tensor b, Tensor(a!) conv_ring, Tensor(b!) state, int start, "
-      "Tensor valid_len, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, float eps) -> Tensor");
+      "Tensor valid_len, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, float eps, "
+      "Tensor? start_t=None) -> Tensor");
   m.def(
       "gqa_prefill(Tensor qg, Tensor k, Tensor v, Tensor q_norm_w, Tensor k_norm_w, Tensor cos, Tensor sin, "
-      "Tensor(a!) k_cache, Tensor(b!) v_cache, int start, float eps) -> Tensor");
+      "Tensor(a!) k_cache, Tensor(b!) v_cache, int start, float eps, Tensor? start_t=None) -> Tensor");
 }
 void register_ext_impls(torch::Library& m) {
   register_comm_impls(m);

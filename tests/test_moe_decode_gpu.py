@@ -67,3 +67,27 @@ def test_fused_moe_decode_fp8_experts():
     ref = gpu._reduce_add_norm(gpu._mlp(i, h.to(dev)), x2, nxt)
     torch.cuda.synchronize()
     assert _rel(fused, ref) < 2e-2 and _rel(x1, x2) < 1e-2
+
+
+@pytest.mark.parametrize("moe", ["tiny", "35b"])
+def test_fused_moe_decode_exact_ties_pick_lowest_id(moe):
+    """Duplicated router rows give bit-equal logits: the fused top-k must pick
+    the lower expert id, as the unfused router does, or the expert rows
+    (different weights for the duplicate) change the output."""
+    from bwn.config import QWEN36_35B_A3B, tiny_qwen36
+    cfg = QWEN36_35B_A3B.scaled(num_layers=2) if moe == "35b" else tiny_qwen36(moe=True, layers=4)
+    from bwn.models.qwen36 import Qwen36Model
+    gpu = Qwen36Model(cfg, None, torch.device("cuda")).init_random(0)
+    i, T = 0, 16
+    L = gpu.layers[i]
+    E = cfg.num_experts
+    L["router"][E // 2:].copy_(L["router"][:E // 2])
+    L["router_x"][E // 2:E].copy_(L["router_x"][:E // 2])  # the fused path's copy (+ the shared gate row)
+    h, x = _inputs(cfg, T, seed=5)
+    dev = torch.device("cuda")
+    x1, x2 = x.to(dev).clone(), x.to(dev).clone()
+    nxt = gpu.layers[1]["in_norm"]
+    fused = gpu._moe_decode(i, h.to(dev), x1, nxt)
+    ref = gpu._reduce_add_norm(gpu._mlp(i, h.to(dev)), x2, nxt)
+    torch.cuda.synchronize()
+    assert _rel(fused, ref) < 2e-2 and _rel(x1, x2) < 1e-2

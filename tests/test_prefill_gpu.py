@@ -108,3 +108,33 @@ def test_model_prefill_matches_cpu():
     ids_1 = g.greedy(hg)
     assert torch.equal(ids_b, ids_1)
     assert _rel(sb.ssm, sg.ssm) < 2e-2
+
+
+def test_graph_captured_bucketed_prefill():
+    """One captured prefill chunk replayed at every offset (the start position is
+    a device scalar) equals the eager bucketed prefill, with the short row first
+    and a ragged last chunk padded to the bucket."""
+    from bwn.config import tiny_qwen36
+    from bwn.models.qwen36 import build_qwen36
+    from bwn.runtime.static_decode import StaticDecoder
+
+    cfg = tiny_qwen36()
+    g = build_qwen36(cfg, device="cuda", seed=7)
+    toks = torch.randint(0, cfg.vocab, (2, 150))
+    vl = torch.tensor([111, 150], dtype=torch.int32)
+    eager = g.new_state(2, 256)
+    ids_e = g.prefill(toks.cuda(), eager, vl.cuda(), bucket=64)
+    dec = StaticDecoder(g, 2, 256)
+    dec.capture_prefill(64)
+    ids_g = dec.prefill(toks, vl, bucket=64)
+    torch.cuda.synchronize()
+    from bwn.ops import check_status
+    check_status("graphed prefill")
+    assert torch.equal(ids_g, ids_e)
+    assert dec.st.positions.tolist() == [111, 150]
+    assert _rel(dec.st.ssm, eager.ssm) < 1e-3
+    assert _rel(dec.st.k_cache[:, :, :, :111], eager.k_cache[:, :, :, :111]) < 1e-3
+    # a second prompt through the same graph after a reset
+    dec.reset()
+    ids_g2 = dec.prefill(toks, vl, bucket=64)
+    assert torch.equal(ids_g2, ids_e)

@@ -79,27 +79,32 @@ def test_prefill_and_decode_match_hf(moe):
         assert torch.allclose(got, ref, atol=2e-3, rtol=2e-3), (got - ref).abs().max()
 
 
-def test_bucketed_prefill_equals_whole():
+@pytest.mark.parametrize("lens", [(37, 29), (29, 37)])
+def test_bucketed_prefill_equals_whole(lens):
     """Chunked (bucketed) prefill with state carry == one-shot prefill, including
-    pad rows (valid_len) that must leave the state untouched."""
+    pad rows (valid_len) that must leave the state untouched, whichever row is
+    the short one (a chunk starts at the largest row position)."""
     cfg = tiny_qwen36()
     m = build_qwen36(cfg, seed=3, dtype=torch.float32)
     B, S = 2, 37
     toks = torch.randint(0, cfg.vocab, (B, S))
-    vl = torch.tensor([37, 29], dtype=torch.int32)
+    vl = torch.tensor(lens, dtype=torch.int32)
+    short = lens.index(29)
     st1 = m.new_state(B, 64)
     ids1 = m.prefill(toks, st1, valid_len=vl)
     st2 = m.new_state(B, 64)
     ids2 = m.prefill(toks, st2, valid_len=vl, bucket=16)
     assert torch.equal(ids1, ids2)
-    assert st1.positions.tolist() == [37, 29] and st2.positions.tolist() == [37, 29]
+    assert st1.positions.tolist() == list(lens) and st2.positions.tolist() == list(lens)
     assert torch.allclose(st1.ssm, st2.ssm, atol=1e-4)
-    # the short row equals a standalone run of its 29 real tokens
-    st3 = m.new_state(1, 64)
-    ids3 = m.prefill(toks[1:, :29], st3)
-    assert ids3.item() == ids1[1].item()
-    assert torch.allclose(st3.ssm[:, 0], st1.ssm[:, 1], atol=1e-4)
-    assert torch.equal(st3.conv[:, 0], st1.conv[:, 1])
+    # each row equals a standalone run of its real tokens
+    for r in range(B):
+        st3 = m.new_state(1, 64)
+        ids3 = m.prefill(toks[r:r + 1, :lens[r]], st3)
+        assert ids3.item() == ids2[r].item()
+        assert torch.allclose(st3.ssm[:, 0], st2.ssm[:, r], atol=1e-4)
+        assert torch.allclose(st3.conv[:, 0], st1.conv[:, r], atol=1e-5)  # (the bucketed ring keeps a stale 4th slot)
+    assert short in (0, 1)
 
 
 def test_greedy_decode_consistency():
