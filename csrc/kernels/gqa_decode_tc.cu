@@ -161,59 +161,65 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;  // query row == TMEM lane
     const bool real = r < nrows;
-    const int i_tok = real ? r / G : 0, g = real ? r % G : 0;
-    const int vrow = cb * ntok + i_tok, qh = kvh * G + g;
-    const int pos_in = real ? p.positions[vrow] : -1;
+    const int pos_in = real ? p.positions[cb * ntok + r / G] : -1;
     const int pos = pos_in < p.s_max ? pos_in : -1;
-    const __nv_bfloat16* qrow = p.qg + (long)vrow * p.qg_stride + (long)qh * 512;
-    // q row: RMSNorm(1+w), partial RoPE (rotate-half within rope_dim), 1/sqrt(256)
-    const bool act = real && pos >= 0;  // an inactive row's q is zero (no RoPE row to read)
-    float ss = 0.f;
-    if (act) {
-      for (int c = 0; c < 256; c += 8) {
-        const uint4 u = *reinterpret_cast<const uint4*>(qrow + c);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(h2[e]);
-          ss += f.x * f.x + f.y * f.y;
-        }
+    // Q rows, one warp per row (lane = 8 consecutive dims, one 16-byte load):
+    // RMSNorm(1+w), partial RoPE (rotate-half within rope_dim, the partner
+    // dims fetched from the lane rope_dim/16 away), 1/sqrt(256); an inactive
+    // row's q is zero (no RoPE row to read).  Rows past nrows are zeroed.
+    {
+      const int R = p.rope_dim, hr = R >> 1;
+      const int c = lane * 8;
+      const float qscale = rsqrtf(256.f);
+      float w8[8];
+      {
+        const float4 w0 = *reinterpret_cast<const float4*>(p.q_norm_w + c);
+        const float4 w1 = *reinterpret_cast<const float4*>(p.q_norm_w + c + 4);
+        w8[0] = w0.x; w8[1] = w0.y; w8[2] = w0.z; w8[3] = w0.w;
+        w8[4] = w1.x; w8[5] = w1.y; w8[6] = w1.z; w8[7] = w1.w;
       }
-    }
-    const float inv = rsqrtf(ss / 256.f + p.eps);
-    const int R = p.rope_dim, hr = R >> 1;
-    const float qscale = rsqrtf(256.f);
-    for (int c = 0; c < 256; c += 8) {
-      alignas(16) __nv_bfloat16 o8[8];
-      if (act) {
-        float x[8], y[8];
-        const uint4 u = *reinterpret_cast<const uint4*>(qrow + c);
-        const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(hb[e]) * inv * (1.f + p.q_norm_w[c + e]);
-        if (c < R) {
-          const int pc = c < hr ? c + hr : c - hr;
-          const float sg = c < hr ? -1.f : 1.f;
-          const uint4 up = *reinterpret_cast<const uint4*>(qrow + pc);
-          const __nv_bfloat16* hp = reinterpret_cast<const __nv_bfloat16*>(&up);
+      const int src_lane = c < R ? (c < hr ? lane + (hr >> 3) : lane - (hr >> 3)) : lane;
+      for (int rr = q; rr < kTM; rr += 4) {
+        alignas(16) __nv_bfloat16 o8[8];
+        const int prr = rr < nrows ? __ldg(p.positions + cb * ntok + rr / G) : -1;
+        const bool act = prr >= 0 && prr < p.s_max;  // warp-uniform
+        if (act) {
+          const int vr = cb * ntok + rr / G, qh = kvh * G + rr % G;
+          const uint4 u = *reinterpret_cast<const uint4*>(p.qg + (long)vr * p.qg_stride + (long)qh * 512 + c);
+          const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&u);
+          float x[8];
+          float ss = 0.f;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float xp = __bfloat162float(hp[e]) * inv * (1.f + p.q_norm_w[pc + e]);
-            const float cs = p.cos[(long)pos * R + c + e], sn = p.sin[(long)pos * R + c + e];
-            y[e] = x[e] * cs + sg * xp * sn;
+            x[e] = __bfloat162float(hb[e]);
+            ss += x[e] * x[e];
           }
+          ss = warp_sum(ss);
+          const float inv = rsqrtf(ss / 256.f + p.eps);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] *= inv * (1.f + w8[e]);
+          float y[8], cs[8], sn[8];
+          if (c < R) {
+            const float4* cp = reinterpret_cast<const float4*>(p.cos + (long)prr * R + c);
+            const float4* sp4 = reinterpret_cast<const float4*>(p.sin + (long)prr * R + c);
+            const float4 c0 = cp[0], c1 = cp[1], s0 = sp4[0], s1 = sp4[1];
+            cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+            sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float xp = __shfl_sync(0xffffffffu, x[e], src_lane);
+            y[e] = c < R ? x[e] * cs[e] + (c < hr ? -1.f : 1.f) * xp * sn[e] : x[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16(y[e] * qscale);
         } else {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) y[e] = x[e];
+          for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16(0.f);
         }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16(y[e] * qscale);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o8[e] = __float2bfloat16(0.f);
+        const int box = c >> 6, chk = ((c & 63) >> 3) ^ (rr & 7);
+        *reinterpret_cast<uint4*>(sQ + box * kTBox + rr * 128 + chk * 16) = *reinterpret_cast<uint4*>(o8);
       }
-      const int box = c >> 6, chk = ((c & 63) >> 3) ^ (r & 7);
-      *reinterpret_cast<uint4*>(sQ + box * kTBox + r * 128 + chk * 16) = *reinterpret_cast<uint4*>(o8);
     }
     fence_async_smem();
     mbar_arrive(q_full);

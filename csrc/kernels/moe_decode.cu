@@ -32,6 +32,12 @@
 #include "kernels/moe.h"
 #include "kernels/moe_topk.cuh"
 
+// Phase hook of moe_route_fused (empty in the product build; a timing harness
+// may define it to record a timestamp per CTA and phase).
+#ifndef BWN_ROUTE_PHASE
+#define BWN_ROUTE_PHASE(n)
+#endif
+
 namespace bwn {
 
 namespace {
@@ -47,6 +53,7 @@ struct RouteSmem {
   int ids[kRtMaxPairs];
   int pos[kRtMaxPairs];
   int src[kRtMaxPairs + kRtMaxT];  // token of each packed row
+  unsigned long long msk[kMoeDecodeMaxGroups];  // tokens routed to each local expert (bit t)
   int cnt[kMoeDecodeMaxGroups];
   int off[kMoeDecodeMaxGroups + 1];
   float sg[kRtMaxT];
@@ -82,6 +89,7 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = a.E + (a.has_sg ? 1 : 0);  // router rows (+ shared gate row)
   const int ntg = (a.T + 7) / 8;
+  BWN_ROUTE_PHASE(0);
   // ---- 1. router logits: one warp per (router row, group of 8 tokens) ----
   for (int item = blockIdx.x * kRtWarps + warp; item < rows * ntg; item += gridDim.x * kRtWarps) {
     const int e = item / ntg, tg = item % ntg;
@@ -90,33 +98,34 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
 #pragma unroll
     for (int j = 0; j < NV; ++j) wv[j] = wr[lane + 32 * j];
     const int t1 = min(a.T, tg * 8 + 8);
-    for (int t = tg * 8; t < t1; t += 2) {  // two tokens' rows in flight at once
-      const bool two = t + 1 < t1;
-      const uint4* xr0 = reinterpret_cast<const uint4*>(a.x + (long)t * a.ldx);
-      const uint4* xr1 = reinterpret_cast<const uint4*>(a.x + (long)(two ? t + 1 : t) * a.ldx);
-      uint4 x0[NV], x1[NV];
+    constexpr int TPF = NV <= 8 ? 4 : 2;  // token rows in flight at once (register budget)
+    for (int t = tg * 8; t < t1; t += TPF) {
+      uint4 xv[TPF][NV];
 #pragma unroll
-      for (int j = 0; j < NV; ++j) {
-        x0[j] = __ldg(xr0 + lane + 32 * j);
-        x1[j] = __ldg(xr1 + lane + 32 * j);
-      }
-      float acc0 = 0.f, acc1 = 0.f;
+      for (int u = 0; u < TPF; ++u) {
+        const uint4* xr = reinterpret_cast<const uint4*>(a.x + (long)min(t + u, t1 - 1) * a.ldx);
 #pragma unroll
-      for (int j = 0; j < NV; ++j) {
-        acc0 += dot8_bf16(wv[j], x0[j]);
-        acc1 += dot8_bf16(wv[j], x1[j]);
+        for (int j = 0; j < NV; ++j) xv[u][j] = __ldg(xr + lane + 32 * j);
       }
-      acc0 = warp_sum(acc0);
-      acc1 = warp_sum(acc1);
+      float acc[TPF];
+#pragma unroll
+      for (int u = 0; u < TPF; ++u) {
+        acc[u] = 0.f;
+#pragma unroll
+        for (int j = 0; j < NV; ++j) acc[u] += dot8_bf16(wv[j], xv[u][j]);
+        acc[u] = warp_sum(acc[u]);
+      }
       if (lane == 0) {
-        a.logits[(long)t * rows + e] = acc0;
-        if (two) a.logits[(long)(t + 1) * rows + e] = acc1;
+#pragma unroll
+        for (int u = 0; u < TPF; ++u)
+          if (t + u < t1) a.logits[(long)(t + u) * rows + e] = acc[u];
       }
     }
   }
   // ---- 2. grid barrier (count, generation); bounded wait ----
   if (threadIdx.x == 0) s.abort = 0;
   __syncthreads();
+  BWN_ROUTE_PHASE(1);
   // arrival count and generation live on separate 128-byte lines, and the
   // waiters back off between polls, so polling never starves the arrivals
   unsigned* const bar_count = a.bar;
@@ -144,31 +153,48 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
     __threadfence();
   }
   __syncthreads();
+  BWN_ROUTE_PHASE(2);
   if (s.abort) return;
   // ---- 3. routing (every CTA, identically): softmax -> top-k -> renormalise ----
   const int E = a.E, k = a.k, T = a.T;
-  for (int t = warp; t < T; t += kRtWarps) {
-    const float* l = a.logits + (long)t * rows;
-    float my_w;
-    int my_id;
-    const float picked = route_topk<EPL>(l, E, k, lane, my_w, my_id);
-    if (lane < k) {
-      s.w[t * k + lane] = a.renorm ? my_w / picked : my_w;
-      s.ids[t * k + lane] = my_id;
+  constexpr int NT = EPL <= 8 ? 4 : 2;  // tokens per warp routed together
+  for (int t0 = warp; t0 < T; t0 += kRtWarps * NT) {
+    const float* l[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int t = t0 + j * kRtWarps;
+      l[j] = t < T ? a.logits + (long)t * rows : nullptr;
     }
-    if (lane == 0) s.sg[t] = a.has_sg ? __ldcg(l + E) : 0.f;
+    float my_w[NT], picked[NT];
+    int my_id[NT];
+    route_topk_n<EPL, NT>(l, E, k, lane, my_w, my_id, picked);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int t = t0 + j * kRtWarps;
+      if (t >= T) continue;
+      if (lane < k) {
+        s.w[t * k + lane] = a.renorm ? my_w[j] / picked[j] : my_w[j];
+        s.ids[t * k + lane] = my_id[j];
+      }
+      if (lane == 0) s.sg[t] = a.has_sg ? __ldcg(l[j] + E) : 0.f;
+    }
   }
   // ---- stable expert-major packing of this rank's pairs (+ the shared group) ----
+  // Each token routes to an expert at most once, so a pair's rank inside its
+  // expert's group is the number of earlier tokens routed there: one bit per
+  // token in the expert's mask, set in parallel, counted with popc.
   const int G = a.E_local + (a.shared_group ? 1 : 0);
-  for (int g = threadIdx.x; g < G; g += blockDim.x) s.cnt[g] = 0;
+  for (int g = threadIdx.x; g < G; g += blockDim.x) s.msk[g] = 0ull;
   __syncthreads();
   const int n = T * k;
+  BWN_ROUTE_PHASE(3);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int el = s.ids[i] - a.e0;
-    if (el >= 0 && el < a.E_local) atomicAdd(&s.cnt[el], 1);
+    if (el >= 0 && el < a.E_local) atomicOr(&s.msk[el], 1ull << (i / k));
   }
   __syncthreads();
-  if (threadIdx.x == 0 && a.shared_group) s.cnt[a.E_local] = a.t_hi - a.t_lo;
+  for (int g = threadIdx.x; g < G; g += blockDim.x)
+    s.cnt[g] = g < a.E_local ? __popcll(s.msk[g]) : a.t_hi - a.t_lo;
   __syncthreads();
   // exclusive prefix sum of the group counts: each thread scans a run of
   // consecutive groups, the run totals are scanned by one warp
@@ -205,33 +231,20 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
     }
   }
   __syncthreads();
-  // stable placement in pair order (token, then slot): warp 0 walks the pairs
-  // 32 at a time; lanes routed to the same expert rank themselves by lane
-  // order (match_any) on top of that expert's running cursor (s.cnt reused)
-  if (warp == 0) {
-    for (int g = lane; g < G; g += 32) s.cnt[g] = 0;
-    __syncwarp();
-    for (int i0 = 0; i0 < n; i0 += 32) {
-      const int i = i0 + lane;
-      const int id = i < n ? s.ids[i] : -1;
-      const int el = id - a.e0;
-      const bool mine = i < n && el >= 0 && el < a.E_local;
-      const unsigned peers = __match_any_sync(0xffffffffu, mine ? el : -1);
-      const int rank = __popc(peers & ((1u << lane) - 1u));
-      int p = -1;
-      if (mine) {
-        p = s.off[el] + s.cnt[el] + rank;
-        s.src[p] = i / k;
-      }
-      __syncwarp();
-      if (mine && rank == 0) s.cnt[el] += __popc(peers);
-      if (i < n) s.pos[i] = p;
-      __syncwarp();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int el = s.ids[i] - a.e0;
+    const int t = i / k;
+    int p = -1;
+    if (el >= 0 && el < a.E_local) {
+      p = s.off[el] + __popcll(s.msk[el] & ((1ull << t) - 1ull));
+      s.src[p] = t;
     }
+    s.pos[i] = p;
   }
   if (a.shared_group)
     for (int t = a.t_lo + threadIdx.x; t < a.t_hi; t += blockDim.x) s.src[s.off[a.E_local] + t - a.t_lo] = t;
   __syncthreads();
+  BWN_ROUTE_PHASE(4);
   // ---- 4. gather this CTA's share of the packed rows; CTA 0 writes the routing ----
   const int total = s.off[G];
   const int hv = a.H / 8;
@@ -253,6 +266,8 @@ __global__ void __launch_bounds__(kRtThreads) moe_route_fused_kernel(MoeRouteFus
       a.sg[t] = s.sg[t];
     }
   }
+  __syncthreads();
+  BWN_ROUTE_PHASE(5);
 }
 
 // One CTA per token.  VPT: 8-column vectors per thread (H <= 256 * 8 * VPT).

@@ -5,36 +5,45 @@
 
 namespace bwn {
 
-// Softmax over one token's E logits, then its top-k (largest probability first,
+// Softmax over a token's E logits, then its top-k (largest probability first,
 // the lower expert id on ties, as torch.topk on the fp32 softmax in
 // static_decode_35b.py:723-728).  Lane j holds experts j, 32 + j, ...; each
 // lane sorts its EPL values once (bitonic network in registers), then every
 // round is a warp max of the lanes' heads (redux.sync on the probability bits,
 // which order like the values since they are >= 0), a min over the tied lanes'
-// expert ids, and a pop of the winner's head.  Lane s gets slot s's (p, id);
-// returns the sum of the k probabilities.
-template <int EPL>
-__device__ __forceinline__ float route_topk(const float* l, int E, int k, int lane, float& my_w, int& my_id) {
-  float v[EPL];
-  int id[EPL];
-  float mx = -INFINITY;
+// expert ids, and a pop of the winner's head.  NT tokens (rows l[j], null =
+// none) go through together: their loads share one round trip and their
+// reductions interleave.  Lane s gets slot s's (p, id) of each token; picked[j]
+// is the sum of token j's k probabilities.
+template <int EPL, int NT>
+__device__ __forceinline__ void route_topk_n(const float* const (&l)[NT], int E, int k, int lane,
+                                             float (&my_w)[NT], int (&my_id)[NT], float (&picked)[NT]) {
+  float v[NT][EPL];
+  int id[NT][EPL];
 #pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const int e = i * 32 + lane;
-    v[i] = e < E ? __ldcg(l + e) : -INFINITY;
-    id[i] = e;
-    mx = fmaxf(mx, v[i]);
-  }
-  mx = warp_max(mx);
-  float sum = 0.f;
+  for (int j = 0; j < NT; ++j)
 #pragma unroll
-  for (int i = 0; i < EPL; ++i) {
-    const bool real = i * 32 + lane < E;
-    v[i] = real ? __expf(v[i] - mx) : -1.f;  // absent experts sort last and never win
-    sum += real ? v[i] : 0.f;
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      v[j][i] = (l[j] != nullptr && e < E) ? __ldcg(l[j] + e) : -INFINITY;
+      id[j][i] = e;
+    }
+  float inv[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) mx = fmaxf(mx, v[j][i]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const bool real = i * 32 + lane < E;
+      v[j][i] = real ? __expf(v[j][i] - mx) : -1.f;  // absent experts sort last and never win
+      sum += real ? v[j][i] : 0.f;
+    }
+    inv[j] = 1.f / warp_sum(sum);
   }
-  sum = warp_sum(sum);
-  const float inv = 1.f / sum;
   // bitonic sort: position i before i+1 in (value desc, id asc) order
 #pragma unroll
   for (int size = 2; size <= EPL; size <<= 1) {
@@ -42,47 +51,67 @@ __device__ __forceinline__ float route_topk(const float* l, int E, int k, int la
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
 #pragma unroll
       for (int i = 0; i < EPL; ++i) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool j_first = v[j] > v[i] || (v[j] == v[i] && id[j] < id[i]);
-          const bool up = (i & size) == 0;
-          if (j_first == up) {
-            const float tv = v[i];
-            v[i] = v[j];
-            v[j] = tv;
-            const int ti = id[i];
-            id[i] = id[j];
-            id[j] = ti;
+        const int q = i ^ stride;
+        if (q > i) {
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const bool q_first = v[j][q] > v[j][i] || (v[j][q] == v[j][i] && id[j][q] < id[j][i]);
+            const bool up = (i & size) == 0;
+            if (q_first == up) {
+              const float tv = v[j][i];
+              v[j][i] = v[j][q];
+              v[j][q] = tv;
+              const int ti = id[j][i];
+              id[j][i] = id[j][q];
+              id[j][q] = ti;
+            }
           }
         }
       }
     }
   }
-  float picked = 0.f;
-  my_w = 0.f;
-  my_id = -1;
-  for (int sl = 0; sl < k; ++sl) {
-    // key 0 = nothing left in this lane; a real probability p >= 0 has key bits(p) + 1
-    const unsigned key = v[0] >= 0.f ? __float_as_uint(v[0]) + 1u : 0u;
-    const unsigned m = __reduce_max_sync(0xffffffffu, key);
-    const unsigned win = __reduce_min_sync(0xffffffffu, key == m ? (unsigned)id[0] : 0xffffffffu);
-    const float p = __uint_as_float(m - 1u) * inv;
-    picked += p;
-    if (lane == sl) {
-      my_w = p;
-      my_id = (int)win;
-    }
-    if (lane == (int)(win & 31u)) {  // pop the winner's head
 #pragma unroll
-      for (int i = 0; i + 1 < EPL; ++i) {
-        v[i] = v[i + 1];
-        id[i] = id[i + 1];
+  for (int j = 0; j < NT; ++j) {
+    picked[j] = 0.f;
+    my_w[j] = 0.f;
+    my_id[j] = -1;
+  }
+  for (int sl = 0; sl < k; ++sl) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      // key 0 = nothing left in this lane; a real probability p >= 0 has key bits(p) + 1
+      const unsigned key = v[j][0] >= 0.f ? __float_as_uint(v[j][0]) + 1u : 0u;
+      const unsigned m = __reduce_max_sync(0xffffffffu, key);
+      const unsigned win = __reduce_min_sync(0xffffffffu, key == m ? (unsigned)id[j][0] : 0xffffffffu);
+      const float p = __uint_as_float(m - 1u) * inv[j];
+      picked[j] += p;
+      if (lane == sl) {
+        my_w[j] = p;
+        my_id[j] = (int)win;
       }
-      v[EPL - 1] = -1.f;
-      id[EPL - 1] = 0x7fffffff;
+      if (lane == (int)(win & 31u)) {  // pop the winner's head
+#pragma unroll
+        for (int i = 0; i + 1 < EPL; ++i) {
+          v[j][i] = v[j][i + 1];
+          id[j][i] = id[j][i + 1];
+        }
+        v[j][EPL - 1] = -1.f;
+        id[j][EPL - 1] = 0x7fffffff;
+      }
     }
   }
-  return picked;
+}
+
+// One token (the standalone router).
+template <int EPL>
+__device__ __forceinline__ float route_topk(const float* l, int E, int k, int lane, float& my_w, int& my_id) {
+  const float* ls[1] = {l};
+  float w[1], p[1];
+  int id[1];
+  route_topk_n<EPL, 1>(ls, E, k, lane, w, id, p);
+  my_w = w[0];
+  my_id = id[0];
+  return p[0];
 }
 
 }  // namespace bwn
