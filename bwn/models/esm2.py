@@ -62,7 +62,7 @@ class BwnLinear(nn.Linear):
         if x.is_cuda and _gemm_ok(self.in_features, self.out_features) and x.numel() > 0:
             shp = x.shape
             y = _BwnLinearFn.apply(x.reshape(-1, shp[-1]), self.weight, self.bias)
-            return y.reshape(*shp[:-1], self.out_features).to(x.dtype)
+            return y.reshape(*shp[:-1], self.out_features)  # bf16: consumers read it as is (no widening copy)
         return F.linear(x.to(self.weight.dtype), self.weight, self.bias)
 
 
@@ -78,6 +78,25 @@ def _rotate_half(x):
     return torch.cat((-b, a), dim=-1)
 
 
+class _RopeHeadsFn(torch.autograd.Function):
+    """``x [B*S, H*D]`` (a projection's output) -> rotary-embedded, scaled
+    ``[B, H, S, D]`` in one kernel; its backward is the transposed rotation back
+    into the projection layout (``csrc/kernels/esm.cu``)."""
+
+    @staticmethod
+    def forward(ctx, x2d, cos, sin, B, S, H, scale):
+        ctx.save_for_backward(cos, sin)
+        ctx.dims = (B, S, H, scale)
+        return O.rope_half(x2d, cos, sin, B, S, H, True, 1.0, scale)
+
+    @staticmethod
+    def backward(ctx, g):
+        cos, sin = ctx.saved_tensors
+        B, S, H, scale = ctx.dims
+        gx = O.rope_half(g.contiguous(), cos, sin, B, S, H, False, -1.0, scale)
+        return gx, None, None, None, None, None, None
+
+
 class EsmSelfAttention(nn.Module):
     def __init__(self, cfg: ESM2Config):
         super().__init__()
@@ -90,8 +109,28 @@ class EsmSelfAttention(nn.Module):
         inv = 1.0 / (10000 ** (torch.arange(0, self.hd, 2).float() / self.hd))
         self.register_buffer("inv_freq", inv, persistent=False)
 
+    def _tables(self, S: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp32 ``cos``/``sin`` ``[S, D/2]`` of the rotary angles (cached per length)."""
+        key = (S, str(device))
+        cache = self.__dict__.setdefault("_rope_cache", {})
+        if key not in cache:
+            f = torch.outer(torch.arange(S, device=device, dtype=torch.float32), self.inv_freq.float().to(device))
+            cache.clear()
+            cache[key] = (f.cos().contiguous(), f.sin().contiguous())
+        return cache[key]
+
     def forward(self, x, attn_bias):
         B, S, _ = x.shape
+        if x.is_cuda and self.hd % 4 == 0:
+            # projections stay bf16; RoPE + q scaling + head-major layout in one kernel each
+            ql, kl, vl = self.query(x), self.key(x), self.value(x)
+            H = ql.shape[-1] // self.hd
+            cos, sin = self._tables(S, x.device)
+            q = _RopeHeadsFn.apply(ql.reshape(B * S, -1).to(torch.bfloat16), cos, sin, B, S, H, self.hd ** -0.5)
+            k = _RopeHeadsFn.apply(kl.reshape(B * S, -1).to(torch.bfloat16), cos, sin, B, S, H, 1.0)
+            v = vl.to(torch.bfloat16).view(B, S, H, self.hd).transpose(1, 2)
+            o = F.scaled_dot_product_attention(q, k, v, attn_mask=attn_bias.to(torch.bfloat16), scale=1.0)
+            return o.transpose(1, 2).reshape(B, S, -1)
         q = self.query(x).view(B, S, -1, self.hd).transpose(1, 2)
         k = self.key(x).view(B, S, -1, self.hd).transpose(1, 2)
         v = self.value(x).view(B, S, -1, self.hd).transpose(1, 2)
@@ -194,7 +233,7 @@ class EsmForMaskedLM(nn.Module):
             else:
                 x = layer(x, bias)
         x = self.esm.encoder.emb_layer_norm_after(x)
-        h = self.lm_head.layer_norm(esm_gelu(self.lm_head.dense(x)))
+        h = self.lm_head.layer_norm(esm_gelu(self.lm_head.dense(x)).to(x.dtype))
         w = self.esm.embeddings.word_embeddings.weight
         if h.is_cuda:
             wp = F.pad(w, (0, 0, 0, self.vocab_pad - w.shape[0]))

@@ -336,6 +336,23 @@ def mqa_attn(q, kv, visible, q_per_seq: int, scale: float, splits: int = 0):
     return ref.mqa_attn(q, kv, visible, q_per_seq, scale)
 
 
+def rope_half(x, cos, sin, B: int, S: int, H: int, to_heads: bool, sign: float = 1.0, scale: float = 1.0):
+    """Rotate-half RoPE (ESM-2) fused with ``scale`` and the layout change:
+    ``to_heads``: ``x [B*S, H*D] -> [B, H, S, D]``; otherwise ``x [B, H, S, D] ->
+    [B*S, H*D]``.  ``sign=-1`` rotates by the negative angle (the backward).
+    ``cos``/``sin``: ``[>= S, D/2]`` fp32 tables."""
+    if x.is_cuda:
+        return ops().rope_half(x.contiguous(), cos, sin, B, S, H, to_heads, sign, scale)
+    D = x.numel() // (B * S * H)
+    xs = x.reshape(B, S, H, D) if to_heads else x.reshape(B, H, S, D).transpose(1, 2)
+    x1, x2 = xs.float().split(D // 2, dim=-1)
+    c = cos[:S][None, :, None]
+    s = sin[:S][None, :, None] * sign
+    y = torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1) * scale
+    y = y.to(x.dtype)
+    return y.transpose(1, 2).contiguous() if to_heads else y.reshape(B * S, H * D)
+
+
 def rope_interleaved_(x, cos, sin, pos):
     """In place: interleaved-pair RoPE on the trailing ``2*cos.shape[1]`` dims of
     ``x [rows, H, D]`` at ``pos [rows]``."""

@@ -412,12 +412,12 @@ void gqa_decode(const GqaDecodeArgs& p, cudaStream_t stream) {
     launch_k(gqa_kv_append_kernel, dim3(q.kv_heads, q.batch), dim3(kGD), 0, stream, q);
     const int pairs = (q.batch / ntok) * q.kv_heads;
     int splits = std::max(1, std::min(p.splits, num_sms() / std::max(1, pairs)));
-    splits = std::min(splits, (q.s_max + 127) / 128);
+    splits = std::min(splits, (q.s_max + 63) / 64);
     q.splits = splits;
-    CUtensorMap tk, tv;
+    CUtensorMap tk, tv;  // 64-key x 64-dim boxes (the kernel's K/V tile is four of them)
     const long rows = (long)(q.batch / ntok) * q.kv_heads * q.s_max;
-    make_tmap_2d_bf16(&tk, q.k_cache, rows, kGD, kGD, 128, 64);
-    make_tmap_2d_bf16(&tv, q.v_cache, rows, kGD, kGD, 128, 64);
+    make_tmap_2d_bf16(&tk, q.k_cache, rows, kGD, kGD, 64, 64);
+    make_tmap_2d_bf16(&tv, q.v_cache, rows, kGD, kGD, 64, 64);
     gqa_decode_tc(tk, tv, q, stream);
     return;
   }

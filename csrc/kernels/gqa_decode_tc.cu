@@ -10,7 +10,9 @@
 //   S = Q K^T   (tcgen05, fp32 in TMEM, double-buffered)
 //   P = exp2(S - m)  -> bf16 in shared memory (one thread per query row)
 //   O += P V    (tcgen05, V MN-major, O rescaled lazily in TMEM)
-// with K/V tiles streamed by TMA in the 128-byte swizzle.  The new K/V rows
+// with 64-key K/V tiles streamed by TMA in the 128-byte swizzle through
+// two-stage rings, so the next tile's K and V are in flight while this one
+// is multiplied and soft-maxed.  The new K/V rows
 // are appended by gqa_kv_append_kernel before this kernel runs, so every CTA
 // only reads the cache.  Each split writes (max, sum, O) partials; the last
 // CTA of a (sequence, KV head) merges them and applies the sigmoid gate.
@@ -23,10 +25,13 @@ namespace bwn {
 
 namespace {
 constexpr int kTM = 128;             // query rows per CTA (G * n_tok, padded)
-constexpr int kTN = 128;             // keys per tile
-constexpr int kTBox = 128 * 128;     // [128 rows x 64 dims] SW128 box, 16 KB
+constexpr int kTN = 64;              // keys per tile
+constexpr int kTBox = 128 * 128;     // [128 rows x 64 dims] SW128 box, 16 KB (Q, P)
+constexpr int kKBox = kTN * 128;     // [64 keys x 64 dims] SW128 box, 8 KB (K, V)
+constexpr int kKTile = 4 * kKBox;    // one 64-key x 256-dim tile, 32 KB
+constexpr int kTStages = 2;
 constexpr int kTThreads = 192;
-constexpr int kTSmem = 1024 + 4 * kTBox /*Q*/ + 4 * kTBox /*K*/ + 4 * kTBox /*V*/ + 2 * kTBox /*P*/ + 256;
+constexpr int kTSmem = 1024 + 4 * kTBox /*Q*/ + kTStages * kKTile /*K*/ + kTStages * kKTile /*V*/ + kTBox /*P*/ + 256;
 constexpr int kTW = 4 + 256;         // partial record: max (log2 units), sum, 2 pad, O[256] (16-byte aligned)
 }  // namespace
 
@@ -37,20 +42,20 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint8_t* sQ = sm;
-  uint8_t* sK = sQ + 4 * kTBox;
-  uint8_t* sV = sK + 4 * kTBox;
-  uint8_t* sP = sV + 4 * kTBox;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTBox);
+  uint8_t* sK = sQ + 4 * kTBox;              // [kTStages] tiles
+  uint8_t* sV = sK + kTStages * kKTile;      // [kTStages] tiles (contiguous with sK)
+  uint8_t* sP = sV + kTStages * kKTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTBox);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;
-  uint64_t* v_empty = bars + 4;
-  uint64_t* s_full = bars + 5;   // [2]
-  uint64_t* s_empty = bars + 7;  // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_ready = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_empty = bars + 11; // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_ready = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
 
@@ -61,7 +66,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int nrows = ntok * G;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], (i == 0 || i == 7 || i == 8 || i == 9) ? 128 : 1);
+    for (int i = 0; i < 15; ++i) mbar_init(&bars[i], (i == 0 || i == 11 || i == 12 || i == 13) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -92,21 +97,25 @@ __global__ void __launch_bounds__(kTThreads, 1)
     // ------------------------------ TMA producer ------------------------------
     if (elect_one()) {
       for (int j = 0; j < ntiles && !*abort_flag; ++j) {
-        if (!mbar_wait(k_empty, (j & 1) ^ 1)) {
+        const int st = j & 1;
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u)) {
           set_status(p.status, kStatusMbarTimeout);
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(k_full, 4 * kTBox);
-        for (int bx = 0; bx < 4; ++bx) tma_load_2d(&tmK, k_full, sK + bx * kTBox, bx * 64, (int)(krow0 + j * kTN));
-        if (!mbar_wait(v_empty, (j & 1) ^ 1)) {
+        mbar_arrive_expect_tx(&k_full[st], kKTile);
+        for (int bx = 0; bx < 4; ++bx)
+          tma_load_2d(&tmK, &k_full[st], sK + st * kKTile + bx * kKBox, bx * 64, (int)(krow0 + j * kTN));
+        if (!mbar_wait(&v_empty[st], ph ^ 1u)) {
           set_status(p.status, kStatusMbarTimeout);
           *abort_flag = 1;
-          mbar_wait(k_full, j & 1, 100000000ull);
+          mbar_wait(&k_full[st], ph, 100000000ull);
           break;
         }
-        mbar_arrive_expect_tx(v_full, 4 * kTBox);
-        for (int bx = 0; bx < 4; ++bx) tma_load_2d(&tmV, v_full, sV + bx * kTBox, bx * 64, (int)(krow0 + j * kTN));
+        mbar_arrive_expect_tx(&v_full[st], kKTile);
+        for (int bx = 0; bx < 4; ++bx)
+          tma_load_2d(&tmV, &v_full[st], sV + st * kKTile + bx * kKBox, bx * 64, (int)(krow0 + j * kTN));
       }
     }
   } else if (warp == 1) {
@@ -116,18 +125,20 @@ __global__ void __launch_bounds__(kTThreads, 1)
       const uint32_t id_pv = idesc_bf16_f32_major(kTM, 256, false, true);
       bool ok = ntiles == 0 || mbar_wait(q_full, 0);
       auto issue_qk = [&](int j) -> bool {
-        if (!mbar_wait(k_full, j & 1)) return false;
-        if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1)) return false;
+        const int st = j & 1;
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (!mbar_wait(&k_full[st], ph)) return false;
+        if (!mbar_wait(&s_empty[st], ph ^ 1u)) return false;
         tc_fence_after();
-        const uint32_t d = tmem + (j & 1) * kTN;
+        const uint32_t d = tmem + st * kTN;
         for (int bx = 0; bx < 4; ++bx) {
           const uint64_t da = smem_desc_sw128(smem_u32(sQ + bx * kTBox));
-          const uint64_t db = smem_desc_sw128(smem_u32(sK + bx * kTBox));
+          const uint64_t db = smem_desc_sw128(smem_u32(sK + st * kKTile + bx * kKBox));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_f16(d, da + 2 * kk, db + 2 * kk, id_qk, (bx | kk) ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
-        umma_commit(k_empty);
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
         return true;
       };
       if (ok && ntiles > 0) ok = issue_qk(0);
@@ -136,20 +147,20 @@ __global__ void __launch_bounds__(kTThreads, 1)
           ok = false;
           break;
         }
-        if (!mbar_wait(v_full, j & 1) || !mbar_wait(p_full, j & 1)) {
+        const int st = j & 1;
+        if (!mbar_wait(&v_full[st], (uint32_t)(j >> 1) & 1u) || !mbar_wait(p_full, j & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < 2; ++kb) {
-          const uint64_t da = smem_desc_sw128(smem_u32(sP + kb * kTBox));
-          const uint64_t db = smem_desc_sw128_mn(smem_u32(sV + kb * 8192), kTBox);
+        {
+          const uint64_t da = smem_desc_sw128(smem_u32(sP));
+          const uint64_t db = smem_desc_sw128_mn(smem_u32(sV + st * kKTile), kKBox);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem + 256, da + 2 * kk, db + 128 * kk, id_pv, (j | kb | kk) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) umma_f16(tmem + 256, da + 2 * kk, db + 128 * kk, id_pv, (j | kk) ? 1u : 0u);
         }
         umma_commit(o_ready);
-        umma_commit(v_empty);
+        umma_commit(&v_empty[st]);
       }
       if (!ok) {
         set_status(p.status, kStatusMbarTimeout);
@@ -228,10 +239,22 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    // A warp whose 32 rows are all padding (G * n_tok <= 96) computes nothing:
+    // it only keeps the barrier phases (same waits and arrivals, same order).
+    const bool live = q * 32 < nrows;
     for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
+      if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) {
         ok = false;
         break;
+      }
+      if (!live) {
+        mbar_arrive(&s_empty[j & 1]);
+        if (j > 0 && !mbar_wait(o_ready, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive(p_full);
+        continue;
       }
       tc_fence_after();
       float s[kTN];
@@ -295,7 +318,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
     // ---- this split's partial (max, sum, O) ----
     float* ws = p.workspace + ((((long)cb * p.kv_heads + kvh) * p.splits + sp) * nrows) * kTW;
-    if (ok && ntiles > 0 && mbar_wait(o_ready, (ntiles - 1) & 1)) {
+    if (!live) {
+      if (!ok) {
+        set_status(p.status, kStatusMbarTimeout);
+        *abort_flag = 1;
+      }
+    } else if (ok && ntiles > 0 && mbar_wait(o_ready, (ntiles - 1) & 1)) {
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 256; c += 32) {
@@ -330,24 +358,37 @@ __global__ void __launch_bounds__(kTThreads, 1)
   if (*s_ticket == p.splits - 1) {
     __threadfence();
     const float* wsb = p.workspace + (((long)cb * p.kv_heads + kvh) * p.splits) * nrows * kTW;
-    for (int rr = 0; rr < nrows; ++rr) {
-      float M = -INFINITY;
-      for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, __ldcg(wsb + ((long)s2 * nrows + rr) * kTW));
+    // Stage every split's partial records in the (now idle) K/V buffers with
+    // one coalesced pass, then merge all (row, dim) outputs in parallel.  If a
+    // wait gave up, TMA copies may still target those buffers: merge from
+    // global memory instead.
+    const int nfl = p.splits * nrows * kTW;
+    const bool staged = !*abort_flag && nfl * 4 <= 8 * kTBox;
+    const float* src = wsb;
+    auto ld = [&](const float* q) { return staged ? *q : __ldcg(q); };
+    if (staged) {
+      float* sw = reinterpret_cast<float*>(sK);  // sK and sV are contiguous: 8 boxes
+      for (int i = threadIdx.x * 4; i < nfl; i += blockDim.x * 4)
+        *reinterpret_cast<float4*>(sw + i) = __ldcg(reinterpret_cast<const float4*>(wsb + i));
+      __syncthreads();
+      src = sw;
+    }
+    for (int idx = threadIdx.x; idx < nrows * 256; idx += blockDim.x) {
+      const int rr = idx >> 8, d = idx & 255;
       const int vr = cb * ntok + rr / G, qh2 = kvh * G + rr % G;
-      for (int d = threadIdx.x; d < 256; d += blockDim.x) {
-        float Ls = 0.f, o = 0.f;
-        for (int s2 = 0; s2 < p.splits; ++s2) {
-          const float* e = wsb + ((long)s2 * nrows + rr) * kTW;
-          const float mm = __ldcg(e);
-          if (mm == -INFINITY) continue;
-          const float w = exp2f(mm - M);
-          Ls += __ldcg(e + 1) * w;
-          o += __ldcg(e + 4 + d) * w;
-        }
-        const float gate = __bfloat162float(p.qg[(long)vr * p.qg_stride + (long)qh2 * 512 + 256 + d]);
-        p.out[(long)vr * p.out_stride + (long)qh2 * 256 + d] =
-            __float2bfloat16((Ls > 0.f ? o / Ls : 0.f) * sigmoid_f(gate));
+      const float gate = __bfloat162float(p.qg[(long)vr * p.qg_stride + (long)qh2 * 512 + 256 + d]);
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < p.splits; ++s2) M = fmaxf(M, ld(src + ((long)s2 * nrows + rr) * kTW));
+      float Ls = 0.f, o = 0.f;
+      for (int s2 = 0; s2 < p.splits; ++s2) {
+        const float* e = src + ((long)s2 * nrows + rr) * kTW;
+        const float mm = ld(e);
+        if (mm == -INFINITY) continue;
+        const float w = exp2f(mm - M);
+        Ls += ld(e + 1) * w;
+        o += ld(e + 4 + d) * w;
       }
+      p.out[(long)vr * p.out_stride + (long)qh2 * 256 + d] = __float2bfloat16((Ls > 0.f ? o / Ls : 0.f) * sigmoid_f(gate));
     }
     if (threadIdx.x == 0) p.tickets[cb * p.kv_heads + kvh] = 0;
   }

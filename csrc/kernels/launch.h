@@ -114,4 +114,18 @@ void argmax_packed_bf16(const __nv_bfloat16* logits, long ld, int rows, int cols
                         cudaStream_t stream);
 void unpack_argmax(const int64_t* packed, int rows, int* ids_out, cudaStream_t stream);
 
+
+// ---- ESM-2 rotary embedding + transpose (esm.cu) -----------------------------
+struct RopeHalfArgs {
+  const __nv_bfloat16* in;   // element (b, s, h, d) at b * in_b + s * in_s + h * in_h + d
+  __nv_bfloat16* out;        // element (b, s, h, d) at b * out_b + s * out_s + h * out_h + d
+  long in_b, in_s, in_h, out_b, out_s, out_h;
+  const float* cos;          // [S, D/2]
+  const float* sin;
+  int B, S, H, D;
+  float sign;                // +1 forward rotation, -1 its transpose (backward)
+  float scale;
+};
+void rope_half(const RopeHalfArgs& a, cudaStream_t stream);
+
 }  // namespace bwn

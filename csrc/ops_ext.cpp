@@ -636,6 +636,46 @@ Tensor mqa_attn_op(const Tensor& q, const Tensor& kv, const Tensor& visible, int
   return out;
 }
 
+// ESM-2 rotary embedding fused with the scale and the layout change around
+// attention: to_heads: x [B*S, H*D] (rows b*S+s) -> out [B, H, S, D];
+// otherwise x [B, H, S, D] -> out [B*S, H*D].  sign -1 applies the transposed
+// rotation (the backward of the forward one).
+Tensor rope_half_op(const Tensor& x, const Tensor& cos, const Tensor& sin, int64_t B, int64_t S, int64_t H,
+                    bool to_heads, double sign, double scale) {
+  check_bf16(x, "x");
+  check_f32(cos, "cos");
+  check_f32(sin, "sin");
+  TORCH_CHECK(x.is_contiguous() && cos.is_contiguous() && sin.is_contiguous(), "rope_half: contiguous inputs");
+  TORCH_CHECK(x.numel() % (B * S * H) == 0, "rope_half: shape");
+  const int64_t D = x.numel() / (B * S * H);
+  TORCH_CHECK(D % 4 == 0 && cos.size(0) >= S && cos.size(1) == D / 2 && sin.sizes() == cos.sizes(),
+              "rope_half: tables [>= S, D/2], D multiple of 4");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor out = to_heads ? at::empty({B, H, S, D}, x.options()) : at::empty({B * S, H * D}, x.options());
+  RopeHalfArgs a{};
+  a.in = cbf(x);
+  a.out = mbf(out);
+  const long tok_b = S * H * D, tok_s = H * D, tok_h = D;   // [B, S, H, D]
+  const long hd_b = H * S * D, hd_s = D, hd_h = S * D;      // [B, H, S, D]
+  if (to_heads) {
+    a.in_b = tok_b; a.in_s = tok_s; a.in_h = tok_h;
+    a.out_b = hd_b; a.out_s = hd_s; a.out_h = hd_h;
+  } else {
+    a.in_b = hd_b; a.in_s = hd_s; a.in_h = hd_h;
+    a.out_b = tok_b; a.out_s = tok_s; a.out_h = tok_h;
+  }
+  a.cos = cos.data_ptr<float>();
+  a.sin = sin.data_ptr<float>();
+  a.B = (int)B;
+  a.S = (int)S;
+  a.H = (int)H;
+  a.D = (int)D;
+  a.sign = (float)sign;
+  a.scale = (float)scale;
+  rope_half(a, at::cuda::getCurrentCUDAStream().stream());
+  return out;
+}
+
 void rope_interleaved_op(Tensor x, const Tensor& cos, const Tensor& sin, const Tensor& pos) {
   check_bf16(x, "x");
   TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x [rows, H, D] contiguous");
@@ -849,6 +889,7 @@ void register_ext_defs(torch::Library& m) {
       "Tensor vstep, Tensor(c!) conv_ring, Tensor(d!) state, Tensor positions, Tensor pending, Tensor conv_w, "
       "Tensor A_log, Tensor dt_bias, Tensor norm_w, int k_heads, int n_tok, float eps) -> Tensor");
   m.def("rope_interleaved_(Tensor(a!) x, Tensor cos, Tensor sin, Tensor pos) -> ()");
+  m.def("rope_half(Tensor x, Tensor cos, Tensor sin, int B, int S, int H, bool to_heads, float sign, float scale) -> Tensor");
   register_comm_defs(m);
   m.def("moe_topk(Tensor logits, int k, bool renorm, Tensor? bias, int mode, float route_scale) -> (Tensor, Tensor)");
   m.def(
@@ -895,6 +936,7 @@ void register_ext_impls(torch::Library& m) {
   m.impl("moe_combine_ex", &moe_combine_ex_op);
   m.impl("mqa_attn", &mqa_attn_op);
   m.impl("rope_interleaved_", &rope_interleaved_op);
+  m.impl("rope_half", &rope_half_op);
   m.impl("deltanet_prefill", &deltanet_prefill_op);
   m.impl("gqa_prefill", &gqa_prefill_op);
 }

@@ -96,3 +96,27 @@ def test_infer_command_with_reference_flags(capsys):
     main(["--model-size", "8M", "--max-seq-len", "32", "--sequences", "MKTVRQERLK", "KALTAR"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert [r["position"] for r in res] == [5, 3] and [r["true"] for r in res] == ["Q", "T"]
+
+
+def test_rope_half_layouts_match_rotate_half():
+    """``O.rope_half`` (the CPU twin of the fused kernel) equals HF's
+    ``x*cos + rotate_half(x)*sin`` with the head-major transpose, and its
+    ``sign=-1`` backward layout is the transposed rotation."""
+    import torch
+    from bwn import ops as O
+    from bwn.models.esm2 import _rotate_half
+    B, S, H, D = 2, 7, 3, 8
+    x = torch.randn(B * S, H * D)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2).float() / D))
+    f = torch.outer(torch.arange(S).float(), inv)
+    cos, sin = f.cos(), f.sin()
+    y = O.rope_half(x, cos, sin, B, S, H, True, 1.0, 0.5)
+    xs = x.view(B, S, H, D).transpose(1, 2)
+    emb = torch.cat([f, f], -1)
+    ref = (xs * emb.cos() + _rotate_half(xs) * emb.sin()) * 0.5
+    assert torch.allclose(y, ref, atol=1e-6)
+    g = torch.randn(B, H, S, D)
+    xr = xs.clone().requires_grad_(True)
+    ((xr * emb.cos() + _rotate_half(xr) * emb.sin()) * 0.5).backward(g)
+    gx = O.rope_half(g, cos, sin, B, S, H, False, -1.0, 0.5)
+    assert torch.allclose(gx, xr.grad.transpose(1, 2).reshape(B * S, H * D), atol=1e-6)

@@ -36,3 +36,27 @@ def test_esm_gpu_training_steps():
     losses = [float(tr.step()) for _ in range(12)]
     assert all(l == l for l in losses)
     assert min(losses[-4:]) < losses[0]
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_rope_half_kernel_matches_fp32(D):
+    """The fused rotary + scale + transpose kernel, both directions, against the
+    fp32 PyTorch formula (HF ``x*cos + rotate_half(x)*sin``)."""
+    from bwn import ops as O
+    from bwn.models.esm2 import _rotate_half
+    B, S, H = 2, 300, 5
+    x = torch.randn(B * S, H * D, device="cuda").bfloat16()
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    f = torch.outer(torch.arange(S, device="cuda").float(), inv)
+    cos, sin = f.cos().contiguous(), f.sin().contiguous()
+    y = O.rope_half(x, cos, sin, B, S, H, True, 1.0, D ** -0.5)
+    xs = x.float().view(B, S, H, D).transpose(1, 2)
+    emb = torch.cat([f, f], -1)
+    ref = (xs * emb.cos() + _rotate_half(xs) * emb.sin()) * D ** -0.5
+    assert ((y.float() - ref).norm() / ref.norm()).item() < 1e-2
+    g = torch.randn(B, H, S, D, device="cuda").bfloat16()
+    xr = xs.clone().requires_grad_(True)
+    ((xr * emb.cos() + _rotate_half(xr) * emb.sin()) * D ** -0.5).backward(g.float())
+    gx = O.rope_half(g, cos, sin, B, S, H, False, -1.0, D ** -0.5)
+    gref = xr.grad.transpose(1, 2).reshape(B * S, H * D)
+    assert ((gx.float() - gref).norm() / gref.norm()).item() < 1e-2
