@@ -27,9 +27,10 @@ class _BwnLinearFn(torch.autograd.Function):
     """y = x W^T (+ b) with bf16 tcgen05 GEMMs in both directions."""
 
     @staticmethod
-    def forward(ctx, x2d, w, b):
+    def forward(ctx, x2d, w, b, wb=None):
         xb = x2d.to(torch.bfloat16).contiguous()
-        wb = w.to(torch.bfloat16).contiguous()
+        if wb is None:
+            wb = w.to(torch.bfloat16).contiguous()
         y = O.linear(xb, wb) if b is None else O.linear_bias(xb, wb, b)
         ctx.save_for_backward(xb, wb)
         ctx.has_b = b is not None
@@ -52,16 +53,29 @@ class _BwnLinearFn(torch.autograd.Function):
             gw = O.matmul_tn(gyb, xb, f32_out=True).to(ctx.w_dtype)
         if ctx.has_b and ctx.needs_input_grad[2]:
             gb = gy.float().sum(0).to(ctx.w_dtype)
-        return gx, gw, gb
+        return gx, gw, gb, None
 
 
 class BwnLinear(nn.Linear):
     """``nn.Linear`` whose CUDA forward/backward run on the bwn GEMM kernels."""
 
+    def _bf16_weight(self) -> torch.Tensor:
+        """bf16 copy of the (fp32 master) weight, re-made only when the weight
+        changed (optimizer step, load), so a step's forward and recompute share it."""
+        w = self.weight
+        if w.dtype == torch.bfloat16:
+            return w
+        key = (w.data_ptr(), w._version, w.shape)
+        c = self.__dict__.get("_wb")
+        if c is None or c[0] != key:
+            c = (key, w.detach().to(torch.bfloat16).contiguous())
+            self.__dict__["_wb"] = c
+        return c[1]
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.is_cuda and _gemm_ok(self.in_features, self.out_features) and x.numel() > 0:
             shp = x.shape
-            y = _BwnLinearFn.apply(x.reshape(-1, shp[-1]), self.weight, self.bias)
+            y = _BwnLinearFn.apply(x.reshape(-1, shp[-1]), self.weight, self.bias, self._bf16_weight())
             return y.reshape(*shp[:-1], self.out_features)  # bf16: consumers read it as is (no widening copy)
         return F.linear(x.to(self.weight.dtype), self.weight, self.bias)
 
@@ -167,7 +181,8 @@ class EsmLayer(nn.Module):
 
     def forward(self, x, attn_bias):
         a = self.attention
-        h = a.self(a.LayerNorm(x), attn_bias)
+        hn = a.LayerNorm(x)
+        h = a.self(hn.to(torch.bfloat16) if hn.is_cuda else hn, attn_bias)  # one cast for q, k and v
         x = x + a.output.dense(h)
         h = esm_gelu(self.intermediate.dense(self.LayerNorm(x)))
         return x + self.output.dense(h)
