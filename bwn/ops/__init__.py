@@ -310,13 +310,37 @@ def moe_experts(x, w, ids, gate_up_il, down, expert_offset: int = 0, shared=None
 # --------------------------------------------------------------------------
 # DeepSeek V4: hyper-connections, single-KV-head attention
 # --------------------------------------------------------------------------
+_HC_GEMM_MIN_TOKENS = 64
+_hc_fn_cache: dict = {}
+
+
+def _hc_fn_bf16(fn: torch.Tensor) -> torch.Tensor:
+    key = (fn.data_ptr(), fn._version, tuple(fn.shape))
+    w = _hc_fn_cache.get(key)
+    if w is None:
+        rows = (fn.shape[0] + 7) // 8 * 8
+        w = torch.zeros(rows, fn.shape[1], dtype=torch.bfloat16, device=fn.device)
+        w[:fn.shape[0]] = fn
+        if len(_hc_fn_cache) > 256:
+            _hc_fn_cache.clear()
+        _hc_fn_cache[key] = w
+    return w
+
+
 def hc_pre(x, fn, scale, base, iters: int = 20, eps: float = 1e-6, norm_eps: float = 1e-6):
     """Hyper-Connection pre-mix of ``x [T, hc, dim]``.  With ``fn [(2+hc)*hc, hc*dim]``
     returns ``(y [T,dim], post [T,hc], comb [T,hc,hc])``; with ``fn [hc, hc*dim]``
     (the head) returns ``(y, None, None)``."""
     if x.is_cuda:
-        y, post, comb = ops().hc_pre(x.contiguous(), fn.float().contiguous(), scale.float().contiguous(),
-                                     base.float().contiguous(), iters, eps, norm_eps)
+        x = x.contiguous()
+        T, hc, dim = x.shape
+        mix = None
+        if T >= _HC_GEMM_MIN_TOKENS and (hc * dim) % 64 == 0:
+            # prefill: every token's mix GEMV as one tensor-core GEMM against a
+            # bf16 copy of fn (rows padded to 8), read by the kernel
+            mix = linear_f32(x.view(T, hc * dim), _hc_fn_bf16(fn))
+        y, post, comb = ops().hc_pre(x, fn.float().contiguous(), scale.float().contiguous(),
+                                     base.float().contiguous(), iters, eps, norm_eps, mix)
         return (y, None, None) if fn.shape[0] == x.shape[1] else (y, post, comb)
     return ref.hc_pre(x, fn, scale, base, iters, eps, norm_eps)
 

@@ -1,7 +1,10 @@
 // DeepSeek V4 Flash device kernels.
 //
 //  * hc_pre      Hyper-Connection pre-mix, one CTA per token
-//                (contrib/deepseek-v4-flash/run_deepseek_v4_tp.py:179-256):
+//                (contrib/deepseek-v4-flash/run_deepseek_v4_tp.py:179-256);
+//                for many tokens (prefill) the mix GEMV of every token is one
+//                tensor-core GEMM run before it (mix_in) and the kernel does
+//                the rest:
 //                rms over the hc*dim flattened streams, the (2+hc)*hc mix GEMV,
 //                sigmoid pre/post gates (+eps), the hc x hc Sinkhorn
 //                normalisation of exp(comb) (20 alternating row/column passes),
@@ -35,12 +38,25 @@ __global__ void __launch_bounds__(256) hc_pre_kernel(HcPreArgs a) {
 #pragma unroll
   for (int j = 0; j < MIXMAX; ++j) acc[j] = 0.f;
   float ss = 0.f;
-  for (long c = tid; c < n; c += blockDim.x) {
-    const float v = __bfloat162float(x[c]);
-    ss += v * v;
+  if (a.mix_in) {  // mixes precomputed: only the sum of squares (16-byte loads)
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    for (long c = tid; c < n / 8; c += blockDim.x) {
+      const uint4 u = xv[c];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-    for (int j = 0; j < MIXMAX; ++j)
-      if (j < a.mix_out) acc[j] += v * a.fn[(long)j * n + c];
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h2[e]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+  } else {
+    for (long c = tid; c < n; c += blockDim.x) {
+      const float v = __bfloat162float(x[c]);
+      ss += v * v;
+#pragma unroll
+      for (int j = 0; j < MIXMAX; ++j)
+        if (j < a.mix_out) acc[j] += v * a.fn[(long)j * n + c];
+    }
   }
   ss = warp_sum(ss);
 #pragma unroll
@@ -57,7 +73,11 @@ __global__ void __launch_bounds__(256) hc_pre_kernel(HcPreArgs a) {
     const float rs = rsqrtf(tot / (float)n + a.norm_eps);
     for (int j = 0; j < a.mix_out; ++j) {
       float m = 0.f;
-      for (int w = 0; w < 8; ++w) m += s_red[w][j];
+      if (a.mix_in) {
+        m = a.mix_in[(long)t * a.ld_mix + j];
+      } else {
+        for (int w = 0; w < 8; ++w) m += s_red[w][j];
+      }
       s_mix[j] = m * rs;
     }
     if (a.mix_out == HC) {  // head: pre only, one scale

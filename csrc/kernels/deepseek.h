@@ -15,6 +15,8 @@ struct HcPreArgs {
   __nv_bfloat16* y;        // [T, dim]
   float* post;             // [T, hc]       (mix_out == (2+hc)*hc)
   float* comb;             // [T, hc, hc]
+  const float* mix_in = nullptr;  // optional [T, ld_mix]: x . fn^T already computed (one GEMM over
+  int ld_mix = 0;                 // all tokens); the kernel then only adds the rms scale
 };
 void hc_pre(const HcPreArgs& a, cudaStream_t st);
 void hc_post(const __nv_bfloat16* x, const __nv_bfloat16* resid, const float* post, const float* comb, int tokens,

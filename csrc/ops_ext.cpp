@@ -566,7 +566,8 @@ Tensor moe_combine_ex_op(const Tensor& y, const Tensor& w, const Tensor& pos_of,
 // DeepSeek V4
 // ---------------------------------------------------------------------------
 std::tuple<Tensor, Tensor, Tensor> hc_pre_op(const Tensor& x, const Tensor& fn, const Tensor& scale, const Tensor& base,
-                                             int64_t iters, double eps, double norm_eps) {
+                                             int64_t iters, double eps, double norm_eps,
+                                             const c10::optional<Tensor>& mix_in) {
   check_bf16(x, "x");
   check_f32(fn, "fn");
   TORCH_CHECK(x.dim() == 3 && x.is_contiguous(), "x [T, hc, dim] contiguous");
@@ -590,6 +591,14 @@ std::tuple<Tensor, Tensor, Tensor> hc_pre_op(const Tensor& x, const Tensor& fn, 
   a.y = mbf(y);
   a.post = post.data_ptr<float>();
   a.comb = comb.data_ptr<float>();
+  if (mix_in.has_value()) {
+    check_f32(*mix_in, "mix_in");
+    TORCH_CHECK(mix_in->dim() == 2 && mix_in->size(0) == T && mix_in->size(1) >= mix && mix_in->stride(1) == 1,
+                "hc_pre: mix_in [T, >= mix_out] rows");
+    TORCH_CHECK(((long)hc * dim) % 8 == 0, "hc_pre: hc*dim multiple of 8");
+    a.mix_in = mix_in->data_ptr<float>();
+    a.ld_mix = (int)mix_in->stride(0);
+  }
   hc_pre(a, at::cuda::getCurrentCUDAStream().stream());
   return {y, post, comb};
 }
@@ -902,8 +911,8 @@ void register_ext_defs(torch::Library& m) {
       "moe_experts_w8(Tensor x, Tensor w, Tensor ids, Tensor gate_up8, Tensor gate_up_scales16, Tensor down8, "
       "Tensor down_scales16, int e0, Tensor? shared_y, Tensor? shared_gate, float swiglu_limit) -> Tensor");
   m.def(
-      "hc_pre(Tensor x, Tensor fn, Tensor scale, Tensor base, int sinkhorn_iters, float eps, float norm_eps) "
-      "-> (Tensor, Tensor, Tensor)");
+      "hc_pre(Tensor x, Tensor fn, Tensor scale, Tensor base, int sinkhorn_iters, float eps, float norm_eps, "
+      "Tensor? mix_in=None) -> (Tensor, Tensor, Tensor)");
   m.def("hc_post(Tensor x, Tensor resid, Tensor post, Tensor comb) -> Tensor");
   m.def(
       "moe_decode(Tensor x, Tensor router, Tensor gate_up, Tensor down, Tensor? gate_up_scales16, "

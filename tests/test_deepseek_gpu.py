@@ -15,15 +15,17 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
 
-def test_hc_kernels():
-    T, hc, dim = 5, 4, 256
+@pytest.mark.parametrize("T", [5, 96])  # 96: the mixes come from one bf16 tensor-core GEMM
+def test_hc_kernels(T):
+    hc, dim = 4, 256
     x = torch.randn(T, hc, dim, device="cuda").bfloat16()
     fn = torch.randn(24, hc * dim, device="cuda") * 0.02
     sc = torch.ones(3, device="cuda")
     bs = torch.randn(24, device="cuda") * 0.1
     y, post, comb = O.hc_pre(x, fn, sc, bs)
     yr, pr, cr = R.hc_pre(x.cpu(), fn.cpu(), sc.cpu(), bs.cpu())
-    assert _rel(y.cpu(), yr) < 1e-2 and _rel(post.cpu(), pr) < 1e-4 and _rel(comb.cpu(), cr) < 1e-4
+    tol = 1e-4 if T < 64 else 1e-2  # bf16 copy of fn in the GEMM
+    assert _rel(y.cpu(), yr) < 1e-2 and _rel(post.cpu(), pr) < tol and _rel(comb.cpu(), cr) < tol
     a = torch.randn(T, dim, device="cuda").bfloat16()
     out = O.hc_post(a, x, post, comb)
     assert _rel(out.cpu(), R.hc_post(a.cpu(), x.cpu(), pr, cr)) < 1e-2
@@ -60,3 +62,24 @@ def test_deepseek_gpu_matches_cpu():
     hg = g.forward_tokens(ic.cuda(), sg.positions, bidx.cuda(), sg, 1)
     hc = c.forward_tokens(ic, sc.positions, bidx, sc, 1)
     assert _rel(hg.cpu(), hc) < 6e-2
+
+
+def test_deepseek_fp8_weights_match_bf16():
+    """Block-scaled E4M3 dense projections, LM head and routed experts (the
+    benchmark's fp8 configuration) against the bf16 model on the same weights."""
+    cfg = tiny_deepseek_v4()
+    sd = synthetic_checkpoint(cfg, 5, "cpu")
+    g = DeepSeekV4Model(cfg, device="cuda").load(sd)
+    q = DeepSeekV4Model(cfg, device="cuda").load(sd).quantize_fp8(include_head=True, experts=True)
+    toks = torch.randint(0, cfg.vocab, (2, 24), generator=torch.Generator().manual_seed(1)).cuda()
+    sg, sq = g.new_state(2, 64), q.new_state(2, 64)
+    g.prefill(toks, sg)
+    q.prefill(toks, sq)
+    bidx = torch.arange(2, dtype=torch.int32, device="cuda")
+    nxt = toks[:, -1].int()
+    hg = g.forward_tokens(nxt, sg.positions, bidx, sg, 1)
+    hq = q.forward_tokens(nxt, sq.positions, bidx, sq, 1)
+    torch.cuda.synchronize()
+    O.check_status("deepseek fp8")
+    assert torch.isfinite(hq).all()
+    assert _rel(hq.cpu(), hg.cpu()) < 0.15
