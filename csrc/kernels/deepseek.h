@@ -34,6 +34,10 @@ struct MqaArgs {
   __nv_bfloat16* out;       // [rows, H, D]
 };
 void mqa_attn(const MqaArgs& a, cudaStream_t st);
+// prefill-sized MQA on tcgen05 (csrc/kernels/mqa_tc.cu): head dim 512, 128 % H == 0,
+// (rows * H) % 128 == 0, whole row tiles per sequence, kv rows per sequence % 32 == 0
+bool mqa_prefill_tc_supported(const MqaArgs& a, int kv_rows_per_seq);
+void mqa_prefill_tc(const MqaArgs& a, int kv_rows_per_seq, long kv_total_rows, int* status, cudaStream_t st);
 void rope_interleaved(__nv_bfloat16* x, int rows, int H, int D, int half, const float* cos, const float* sin,
                       const int* pos, cudaStream_t st);
 

@@ -31,7 +31,8 @@ constexpr int kKBox = kTN * 128;     // [64 keys x 64 dims] SW128 box, 8 KB (K, 
 constexpr int kKTile = 4 * kKBox;    // one 64-key x 256-dim tile, 32 KB
 constexpr int kTStages = 2;
 constexpr int kTThreads = 192;
-constexpr int kTSmem = 1024 + 4 * kTBox /*Q*/ + kTStages * kKTile /*K*/ + kTStages * kKTile /*V*/ + kTBox /*P*/ + 256;
+constexpr int kTSmem = 1024 + 4 * kTBox /*Q*/ + kTStages * kKTile /*K*/ + kTStages * kKTile /*V*/ + 2 * kTBox /*P*/ + 256;
+constexpr float kTLazy = 8.f;        // O is rescaled only when a row's max grows by more than 2^8
 constexpr int kTW = 4 + 256;         // partial record: max (log2 units), sum, 2 pad, O[256] (16-byte aligned)
 }  // namespace
 
@@ -45,7 +46,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
   uint8_t* sK = sQ + 4 * kTBox;              // [kTStages] tiles
   uint8_t* sV = sK + kTStages * kKTile;      // [kTStages] tiles (contiguous with sK)
   uint8_t* sP = sV + kTStages * kKTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTBox);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTBox);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -53,9 +54,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
   uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_ready = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* p_full = bars + 13;  // [2] P buffer written (128 arrivals)
+  uint64_t* p_done = bars + 15;  // [2] PV that read the P buffer has completed (commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_ticket = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
 
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
   const int nrows = ntok * G;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 15; ++i) mbar_init(&bars[i], (i == 0 || i == 11 || i == 12 || i == 13) ? 128 : 1);
+    for (int i = 0; i < 17; ++i) mbar_init(&bars[i], (i == 0 || i == 11 || i == 12 || i == 13 || i == 14) ? 128 : 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -148,18 +149,19 @@ __global__ void __launch_bounds__(kTThreads, 1)
           break;
         }
         const int st = j & 1;
-        if (!mbar_wait(&v_full[st], (uint32_t)(j >> 1) & 1u) || !mbar_wait(p_full, j & 1)) {
+        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+        if (!mbar_wait(&v_full[st], ph) || !mbar_wait(&p_full[st], ph)) {
           ok = false;
           break;
         }
         tc_fence_after();
         {
-          const uint64_t da = smem_desc_sw128(smem_u32(sP));
+          const uint64_t da = smem_desc_sw128(smem_u32(sP + st * kTBox));
           const uint64_t db = smem_desc_sw128_mn(smem_u32(sV + st * kKTile), kKBox);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_f16(tmem + 256, da + 2 * kk, db + 128 * kk, id_pv, (j | kk) ? 1u : 0u);
         }
-        umma_commit(o_ready);
+        umma_commit(&p_done[st]);
         umma_commit(&v_empty[st]);
       }
       if (!ok) {
@@ -237,23 +239,32 @@ __global__ void __launch_bounds__(kTThreads, 1)
 
     const float sl2 = 1.4426950408889634f;  // log2(e); 1/sqrt(D) is folded into q
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // m: the reference max the row's P and O are taken against (log2 units).
+    // It is raised (and O rescaled) only when the row's running max exceeds it
+    // by more than kTLazy, so P <= 2^kTLazy and, after the first tiles, the
+    // softmax of tile j+1 overlaps the PV of tile j (P is double-buffered).
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     // A warp whose 32 rows are all padding (G * n_tok <= 96) computes nothing:
     // it only keeps the barrier phases (same waits and arrivals, same order).
     const bool live = q * 32 < nrows;
     for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u)) {
+      const int pb = j & 1;
+      if (!mbar_wait(&s_full[pb], (uint32_t)(j >> 1) & 1u)) {
         ok = false;
         break;
       }
+      // P buffer pb was last read by the PV of tile j - 2
+      auto wait_p_free = [&]() -> bool {
+        return j < 2 || mbar_wait(&p_done[pb], (uint32_t)((j >> 1) & 1) ^ 1u);
+      };
       if (!live) {
-        mbar_arrive(&s_empty[j & 1]);
-        if (j > 0 && !mbar_wait(o_ready, (j - 1) & 1)) {
+        mbar_arrive(&s_empty[pb]);
+        if (!wait_p_free()) {
           ok = false;
           break;
         }
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[pb]);
         continue;
       }
       tc_fence_after();
@@ -261,12 +272,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
       for (int c = 0; c < kTN; c += 32) {
         float v[32];
-        tmem_ld32(tmem + lane_base + (j & 1) * kTN + c, v);
+        tmem_ld32(tmem + lane_base + pb * kTN + c, v);
 #pragma unroll
         for (int e = 0; e < 32; ++e) s[c + e] = v[e];
       }
       tc_fence_before();
-      mbar_arrive(&s_empty[j & 1]);
+      mbar_arrive(&s_empty[pb]);
       const int kbase = k0 + j * kTN;
       float mt = -INFINITY;
 #pragma unroll
@@ -276,27 +287,32 @@ __global__ void __launch_bounds__(kTThreads, 1)
         s[c] = vis ? s[c] * sl2 : -INFINITY;
         mt = fmaxf(mt, s[c]);
       }
-      const float mn = fmaxf(m, mt);
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - mn);
-      if (j > 0) {
-        if (!mbar_wait(o_ready, (j - 1) & 1)) {
+      const bool raise = mt > m + kTLazy;  // (m = -inf: any visible key raises)
+      const float mn = raise ? mt : m;
+      const float alpha = (m == -INFINITY || !raise) ? 1.f : exp2f(m - mn);
+      if (j > 0 && __any_sync(0xffffffffu, raise && m != -INFINITY)) {
+        // rescale O: every PV so far (the last one is tile j - 1) must be done
+        if (!mbar_wait(&p_done[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, mn > m)) {
 #pragma unroll 1
-          for (int c = 0; c < 256; c += 32) {
-            float v[32];
-            tmem_ld32(tmem + lane_base + 256 + c, v);
+        for (int c = 0; c < 256; c += 32) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + 256 + c, v);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= alpha;
-            tmem_st32(tmem + lane_base + 256 + c, v);
-          }
+          for (int e = 0; e < 32; ++e) v[e] *= alpha;
+          tmem_st32(tmem + lane_base + 256 + c, v);
         }
+      }
+      if (!wait_p_free()) {
+        ok = false;
+        break;
       }
       float ls = 0.f;
       const float msafe = mn == -INFINITY ? 0.f : mn;
+      uint8_t* pbuf = sP + pb * kTBox;
 #pragma unroll
       for (int c = 0; c < kTN; c += 8) {
         alignas(16) __nv_bfloat16 pv[8];
@@ -306,15 +322,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
           ls += pe;
           pv[e] = __float2bfloat16(pe);
         }
-        const int box = c >> 6;
-        const int chk = ((c & 63) >> 3) ^ (r & 7);
-        *reinterpret_cast<uint4*>(sP + box * kTBox + r * 128 + chk * 16) = *reinterpret_cast<uint4*>(pv);
+        const int chk = (c >> 3) ^ (r & 7);
+        *reinterpret_cast<uint4*>(pbuf + r * 128 + chk * 16) = *reinterpret_cast<uint4*>(pv);
       }
       l = l * alpha + ls;
       m = mn;
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[pb]);
     }
     // ---- this split's partial (max, sum, O) ----
     float* ws = p.workspace + ((((long)cb * p.kv_heads + kvh) * p.splits + sp) * nrows) * kTW;
@@ -323,7 +338,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         set_status(p.status, kStatusMbarTimeout);
         *abort_flag = 1;
       }
-    } else if (ok && ntiles > 0 && mbar_wait(o_ready, (ntiles - 1) & 1)) {
+    } else if (ok && ntiles > 0 && mbar_wait(&p_done[(ntiles - 1) & 1], (uint32_t)((ntiles - 1) >> 1) & 1u)) {
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 256; c += 32) {

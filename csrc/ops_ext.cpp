@@ -2,6 +2,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <tuple>
 
@@ -614,6 +615,15 @@ Tensor hc_post_op(const Tensor& x, const Tensor& resid, const Tensor& post, cons
   return out;
 }
 
+// BWN_MQA_TC=0 keeps prefill-sized MQA on the CUDA-core kernel (A/B measurement).
+static bool mqa_tc_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("BWN_MQA_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 Tensor mqa_attn_op(const Tensor& q, const Tensor& kv, const Tensor& visible, int64_t q_per_seq, double scale,
                    int64_t splits) {
   check_bf16(q, "q");
@@ -623,6 +633,26 @@ Tensor mqa_attn_op(const Tensor& q, const Tensor& kv, const Tensor& visible, int
   TORCH_CHECK(visible.scalar_type() == at::kInt && visible.is_contiguous(), "visible int32");
   const c10::cuda::CUDAGuard guard(q.device());
   const int rows = (int)q.size(0), H = (int)q.size(1), D = (int)q.size(2);
+  {
+    // prefill-sized: the tcgen05 kernel (no splits, no partials)
+    MqaArgs t{};
+    t.q = cbf(q);
+    t.kv = cbf(kv);
+    t.kv_seq_stride = kv.stride(0);
+    t.visible = visible.data_ptr<int>();
+    t.rows = rows;
+    t.q_per_seq = (int)q_per_seq;
+    t.H = H;
+    t.D = D;
+    t.scale = (float)scale;
+    const int kv_rows = (int)kv.size(1);
+    if (splits <= 0 && (long)rows * H >= 1024 && mqa_tc_enabled() && mqa_prefill_tc_supported(t, kv_rows)) {
+      auto out = at::empty_like(q);
+      t.out = mbf(out);
+      mqa_prefill_tc(t, kv_rows, (long)kv.size(0) * kv_rows, status_dev_ptr(), at::cuda::getCurrentCUDAStream().stream());
+      return out;
+    }
+  }
   if (splits <= 0) splits = std::max<int64_t>(1, std::min<int64_t>(32, (2 * num_sms() + rows - 1) / std::max(rows, 1)));
   auto ws = at::empty({(long)rows * splits * H * (2 + D)}, q.options().dtype(at::kFloat));
   auto tickets = at::zeros({rows}, q.options().dtype(at::kInt));

@@ -45,6 +45,21 @@ def test_mqa_attn(H, D):
     assert _rel(out.cpu(), ref) < 2e-2
 
 
+@pytest.mark.parametrize("H,per,S,start", [(8, 256, 320, 0), (8, 256, 320, 37), (64, 32, 64, 0)])
+def test_mqa_prefill_tensor_core(H, per, S, start):
+    """Prefill-sized MQA (the tcgen05 kernel: rows = token x head, causal per
+    token, a chunk starting at ``start``) against the fp32 reference."""
+    B, D = 2, 512
+    q = torch.randn(B * per, H, D, device="cuda").bfloat16()
+    kv = torch.randn(B, S, D, device="cuda").bfloat16()
+    vis = (start + 1 + torch.arange(per, dtype=torch.int32)).repeat(B).cuda()
+    out = O.mqa_attn(q, kv, vis, per, D ** -0.5)
+    torch.cuda.synchronize()
+    O.check_status("mqa prefill")
+    ref = R.mqa_attn(q.cpu(), kv.cpu(), vis.cpu(), per, D ** -0.5)
+    assert _rel(out.cpu(), ref) < 2e-2
+
+
 def test_deepseek_gpu_matches_cpu():
     cfg = tiny_deepseek_v4()
     sd = synthetic_checkpoint(cfg, 4, "cpu")
