@@ -369,8 +369,8 @@ def main() -> None:
                 "seq_len": S,
                 "parallelism": f"tp{args.gpus}" + (f"+ep{args.gpus}" if cfg.is_moe else ""),
                 "decode": "CUDA-graph replay, on-device greedy",
-                "l2": "inputs larger than L2 (every step streams %.1f GB of weights per GPU)" % (
-                    model.weight_bytes() / 1e9),
+                "l2": "inputs larger than L2 (%.1f GB of weights resident per GPU; every step reads all dense "
+                      "weights and each routed expert the batch picks)" % (model.weight_bytes() / 1e9),
                 "fused_comm": model.fused_comm is not None,
                 "ep_all_to_all": getattr(model, "ep_a2a", None) is not None,
                 "prefill_sequence_parallel": getattr(model, "seq_parallel", None) is not None,

@@ -202,10 +202,25 @@ class Qwen36Model(nn.Module):
         return self
 
     def weight_bytes(self) -> int:
-        def nb(v):
-            return v.nbytes() if hasattr(v, "nbytes") and not torch.is_tensor(v) else v.numel() * v.element_size()
-        n = sum(nb(v) for L in self.layers for v in L.values())
-        return n + sum(nb(v) for v in self.g.values())
+        """Bytes of weights held on this rank, each storage counted once (the
+        routed experts and the router are views of the decode path's stacks)."""
+        seen: dict[int, int] = {}
+
+        def add(t):
+            if torch.is_tensor(t):
+                st = t.untyped_storage()
+                seen[st.data_ptr()] = max(seen.get(st.data_ptr(), 0), st.nbytes())
+            elif t is not None and not isinstance(t, (int, float, str, bool)):
+                for v in vars(t).values() if hasattr(t, "__dict__") else ():
+                    if torch.is_tensor(v):
+                        add(v)
+
+        for L in self.layers:
+            for v in L.values():
+                add(v)
+        for v in self.g.values():
+            add(v)
+        return sum(seen.values())
 
     # ----------------------------------------------------------------- state
     def new_state(self, batch: int, max_seq: int, ssm_dtype=torch.float32, ring_slots: int | None = None) -> Qwen36State:

@@ -18,7 +18,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, moe, q):
+def _worker(rank, world, port, moe, q, sharding=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     try:
@@ -38,8 +38,8 @@ def _worker(rank, world, port, moe, q):
         for i in range(cfg.num_layers):
             hf.update(W.synthetic_hf_layer(cfg, i, 3, "cpu"))
         ref = build_qwen36(cfg, device=dev, hf_state=hf)          # tp=1 replica on every rank
-        tp = build_qwen36(cfg, comm=comm, device=dev, hf_state=hf)  # tp=world
-        tpf = build_qwen36(cfg, comm=comm, device=dev, hf_state=hf)
+        tp = build_qwen36(cfg, comm=comm, device=dev, hf_state=hf, moe_sharding=sharding)  # tp=world
+        tpf = build_qwen36(cfg, comm=comm, device=dev, hf_state=hf, moe_sharding=sharding)
         enable_fused_comm(tpf)
         B = 4
         toks = torch.randint(0, cfg.vocab, (B, 24), generator=torch.Generator().manual_seed(0)).to(dev)
@@ -62,8 +62,10 @@ def _worker(rank, world, port, moe, q):
         q.put((rank, "ERR " + traceback.format_exc()))
 
 
-@pytest.mark.parametrize("moe", [False, True])
-def test_tp_decode_fused_vs_nccl(moe):
+@pytest.mark.parametrize("moe,sharding", [(False, None), (True, None), (True, "ep"), (True, "tp")])
+def test_tp_decode_fused_vs_nccl(moe, sharding):
+    """Dense and MoE; the MoE with experts partitioned across ranks ("ep") and
+    with every expert sliced across ranks ("tp", the batch-1 latency layout)."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs")
@@ -71,7 +73,7 @@ def test_tp_decode_fused_vs_nccl(moe):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, moe, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, moe, q, sharding)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(world))
