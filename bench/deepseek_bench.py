@@ -122,7 +122,10 @@ def main():
         res[f"decode_b{B}"] = {"ms_per_step": round(ms, 3), "tok_s": round(B / ms * 1e3, 1),
                                "graph": graph is not None}
         note(f"decode batch {B} done")
+        # release the captured graph (it holds NCCL calls) before the process group goes
+        run = None
         del graph
+        torch.cuda.synchronize()
     if comm.rank == 0:
         print(json.dumps({"metric": "DeepSeek V4 Flash prefill TTFT + decode tok/s", **res}))
     if comm.size > 1:
