@@ -310,7 +310,6 @@ def moe_experts(x, w, ids, gate_up_il, down, expert_offset: int = 0, shared=None
 # --------------------------------------------------------------------------
 # DeepSeek V4: hyper-connections, single-KV-head attention
 # --------------------------------------------------------------------------
-_HC_GEMM_MIN_TOKENS = 64
 _hc_fn_cache: dict = {}
 
 
@@ -335,9 +334,10 @@ def hc_pre(x, fn, scale, base, iters: int = 20, eps: float = 1e-6, norm_eps: flo
         x = x.contiguous()
         T, hc, dim = x.shape
         mix = None
-        if T >= _HC_GEMM_MIN_TOKENS and (hc * dim) % 64 == 0:
-            # prefill: every token's mix GEMV as one tensor-core GEMM against a
-            # bf16 copy of fn (rows padded to 8), read by the kernel
+        from ..utils import env
+        if env.get("BWN_HC_GEMM") and (hc * dim) % 64 == 0:
+            # every token's mix GEMV as one tensor-core GEMM (split over K at decode
+            # sizes) against a bf16 copy of fn (rows padded to 8), read by the kernel
             mix = linear_f32(x.view(T, hc * dim), _hc_fn_bf16(fn))
         y, post, comb = ops().hc_pre(x, fn.float().contiguous(), scale.float().contiguous(),
                                      base.float().contiguous(), iters, eps, norm_eps, mix)

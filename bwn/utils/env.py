@@ -46,6 +46,7 @@ FLAGS = {f.name: f for f in (
          "(0: the reduction as a second kernel)", (0, 1)),
     Flag("BWN_DN_TC", int, 1, "chunked DeltaNet prefill on the tcgen05 kernel (0: the CUDA-core kernel)", (0, 1)),
     Flag("BWN_MQA_TC", int, 1, "prefill-sized DeepSeek MQA on the tcgen05 kernel (0: the CUDA-core kernel)", (0, 1)),
+    Flag("BWN_HC_GEMM", int, 1, "DeepSeek hc_pre mixes as one tensor-core GEMM (0: the fused per-token GEMV, fp32)", (0, 1)),
     Flag("BWN_MOE_FUSED", int, 1, "decode-sized MoE blocks in four launches (fused routing + gather, shared expert "
          "folded into the grouped GEMMs, combine fused with the add-norm or the NVLink slot store)", (0, 1)),
     Flag("BWN_MOE_SHARED_ONLY", int, 0, "cost probe: skip the routed experts, keep the shared expert (wrong results)",

@@ -187,23 +187,49 @@ __global__ void __launch_bounds__(256) mqa_attn_kernel(MqaArgs a) {
       acc[hh][e] = 0.f;
     }
   }
-  for (int k = k0; k < k1; ++k) {
-    float kvv[DPL];
+  // KU key rows are loaded together (their loads share one round trip), then
+  // folded in one at a time; KU = 1 where the per-head registers leave no room
+  constexpr int KU = HMAX <= 16 ? 4 : 1;
+  for (int kb = k0; kb < k1; kb += KU) {
+    float kvv[KU][DPL];
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) kvv[e] = __bfloat162float(kv[(long)k * D + lane * DPL + e]);
+    for (int u = 0; u < KU; ++u) {
+      const int k = min(kb + u, k1 - 1);
+      const __nv_bfloat16* src = kv + (long)k * D + lane * DPL;
+      if constexpr (DPL % 8 == 0) {
 #pragma unroll
-    for (int hh = 0; hh < HMAX / 8; ++hh) {
-      if (warp + hh * 8 >= a.H) continue;
-      float s = 0.f;
+        for (int e = 0; e < DPL; e += 8) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + e);
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) s += qr[hh][e] * kvv[e];
-      s = warp_sum(s) * a.scale;
-      const float mn = fmaxf(m[hh], s);
-      const float al = __expf(m[hh] - mn), p = __expf(s - mn);
-      l[hh] = l[hh] * al + p;
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(h2[q]);
+            kvv[u][e + 2 * q] = f.x;
+            kvv[u][e + 2 * q + 1] = f.y;
+          }
+        }
+      } else {
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[hh][e] = acc[hh][e] * al + p * kvv[e];
-      m[hh] = mn;
+        for (int e = 0; e < DPL; ++e) kvv[u][e] = __bfloat162float(src[e]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      if (kb + u >= k1) break;
+#pragma unroll
+      for (int hh = 0; hh < HMAX / 8; ++hh) {
+        if (warp + hh * 8 >= a.H) continue;
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) s += qr[hh][e] * kvv[u][e];
+        s = warp_sum(s) * a.scale;
+        const float mn = fmaxf(m[hh], s);
+        const float al = __expf(m[hh] - mn), p = __expf(s - mn);
+        l[hh] = l[hh] * al + p;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[hh][e] = acc[hh][e] * al + p * kvv[u][e];
+        m[hh] = mn;
+      }
     }
   }
   // partials: [rows, splits, H, 2 + D]

@@ -15,16 +15,30 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
 
-@pytest.mark.parametrize("T", [5, 96])  # 96: the mixes come from one bf16 tensor-core GEMM
+@pytest.mark.parametrize("T", [5, 96])  # the mixes come from one bf16 tensor-core GEMM
 def test_hc_kernels(T):
     hc, dim = 4, 256
+    _check_hc(T, hc, dim)
+
+
+def test_hc_pre_fused_gemv_fp32():
+    """The in-kernel fp32 GEMV variant (BWN_HC_GEMM=0), run in a fresh interpreter."""
+    import os
+    import subprocess
+    import sys
+    code = ("import torch, tests.test_deepseek_gpu as t; t._check_hc(5, 4, 256, tol=1e-4)")
+    r = subprocess.run([sys.executable, "-c", code], env={**os.environ, "BWN_HC_GEMM": "0"},
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))), capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+def _check_hc(T, hc, dim, tol=1e-2):  # 1e-2: the GEMM reads a bf16 copy of fn
     x = torch.randn(T, hc, dim, device="cuda").bfloat16()
     fn = torch.randn(24, hc * dim, device="cuda") * 0.02
     sc = torch.ones(3, device="cuda")
     bs = torch.randn(24, device="cuda") * 0.1
     y, post, comb = O.hc_pre(x, fn, sc, bs)
     yr, pr, cr = R.hc_pre(x.cpu(), fn.cpu(), sc.cpu(), bs.cpu())
-    tol = 1e-4 if T < 64 else 1e-2  # bf16 copy of fn in the GEMM
     assert _rel(y.cpu(), yr) < 1e-2 and _rel(post.cpu(), pr) < tol and _rel(comb.cpu(), cr) < tol
     a = torch.randn(T, dim, device="cuda").bfloat16()
     out = O.hc_post(a, x, post, comb)
