@@ -4,7 +4,7 @@
     python bench.py --gpus N --steps K --warmup W            (N=1)
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Headline config: Qwen3.6-35B-A3B (40 layers, hidden 2048,
+Headline config (the reference's headline decode benchmark): Qwen3.6-35B-A3B (40 layers, hidden 2048,
 [DeltaNet x3, GQA x1] x10, 256-expert top-8 MoE on every layer), bf16,
 random-init weights from seed 0, TP=N for attention and EP=N for the experts,
 synthetic uniform-random prompt ids, prefill 2048 then greedy decode at global
