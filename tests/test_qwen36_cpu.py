@@ -123,3 +123,20 @@ def test_greedy_decode_consistency():
     h3 = m.prefill_hidden(torch.cat([toks, nxt[:, None].long()], 1), st3)
     assert torch.allclose(a, m.logits(h3), atol=1e-4)
     assert torch.allclose(st.ssm, st3.ssm, atol=1e-5)
+
+
+def test_weight_bytes_counts_each_storage_once():
+    """The decode path's expert stacks hold the routed experts as views: the
+    weight count must not double them."""
+    from bwn.config import tiny_qwen36
+    from bwn.models.qwen36 import Qwen36Model
+    m = Qwen36Model(tiny_qwen36(moe=True, layers=4), None, "cpu").init_random(0)
+    L = m.layers[0]
+    assert L["experts_gate_up"].untyped_storage().data_ptr() == L["experts_gate_up_x"].untyped_storage().data_ptr()
+    seen = {}
+    for Ld in list(m.layers) + [m.g]:
+        for v in Ld.values():
+            if torch.is_tensor(v):
+                st = v.untyped_storage()
+                seen[st.data_ptr()] = st.nbytes()
+    assert m.weight_bytes() == sum(seen.values())
