@@ -91,6 +91,10 @@ class Qwen36Model(nn.Module):
         # keeps vocab/tp rows, ids outside its range read zeros, one sum all-reduce
         self.shard_embed = bool(env.get("BWN_SHARD_EMBED")) and self.comm.size > 1
         self.d = tp_dims(cfg, self.tp, self.rank, self.moe_sharding)
+        if (cfg.is_moe and self.moe_sharding == "tp" and torch.device(device).type == "cuda"
+                and (2 * cfg.moe_inter // self.tp) % 128):
+            raise ValueError(f"moe_sharding='tp' at TP={self.tp}: each rank's gate/up slice has "
+                             f"{2 * cfg.moe_inter // self.tp} rows; the grouped expert GEMM needs a multiple of 128")
         self.device = torch.device(device)
         self.dtype = dtype
         self.layers: list[dict[str, torch.Tensor]] = []

@@ -34,6 +34,8 @@ def _worker(rank, world, port, moe, q, sharding=None):
         comm = init_distributed("nccl", timeout_s=60)
         dev = torch.device("cuda", rank)
         cfg = tiny_qwen36(moe=moe).scaled(q_heads=8, kv_heads=2, dn_k_heads=2, dn_v_heads=4)
+        if sharding == "tp":  # each rank's slice of an expert: gate/up rows a multiple of 128 (grouped GEMM tiles)
+            cfg = cfg.scaled(moe_inter=64 * world, shared_inter=64 * world)
         hf = dict(W.synthetic_hf_globals(cfg, 3, "cpu"))
         for i in range(cfg.num_layers):
             hf.update(W.synthetic_hf_layer(cfg, i, 3, "cpu"))
